@@ -1,0 +1,481 @@
+"""Benchmark of the HBA attention hot path on B200.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference]
+                    [--config cfg1|cfg3|cfg2] [--no-secondary]
+
+Headline (default): BASELINE config 1 -- one decode step (grouped-query
+scoring of every candidate block summary, flat top-16, gather of the
+selected 64-token blocks, one fused union softmax over sinks + RoPE window +
+routed blocks) for a batch of 64 sequences with 32K cached tokens each
+(14/2 heads, dh 64, bf16).  A step is one CUDA-graph replay of
+hba_b200_decode with the cache resident in HBM; L2 is flushed (a 256 MB
+write) before every timed step, outside the timed events.  `value` is decode
+queries/s over all ranks (each rank decodes its own batch: weak scaling).
+`e2e` is the same step through the C-ABI call with the query copied from
+pinned host memory and the output + LSE copied back, inside the timed region.
+The secondary lines measure config 3 (hierarchical decode at 128K) and
+config 2 (prefill at 32K).  `--impl reference` times the CPU oracle port (the
+reference algorithm restated in numpy) on the host cores instead.
+"""
+
+import argparse
+import ctypes
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, os.path.join(ROOT, "hierarchical-block-attention_b200"))
+sys.path.insert(0, ROOT)
+
+import numpy as np  # noqa: E402
+import torch  # noqa: E402
+
+METRIC = "HBA attn decode queries/s & prefill tok/s at 32K/128K; % HBM/tensor roofline"
+FLUSH_BYTES = 256 << 20
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
+    ap.add_argument("--config", default="cfg1", choices=["cfg1", "cfg2", "cfg3"])
+    ap.add_argument("--no-secondary", action="store_true")
+    return ap.parse_args()
+
+
+def peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        d = json.load(open(p))
+        return dict(hbm=d["hbm_gbs"], bf16=d["bf16_tflops"], bf16_sustained=d.get("bf16_tflops_sustained"),
+                    source="measured")
+    return dict(hbm=6650.0, bf16=1590.0, bf16_sustained=1400.0, source="fallback")
+
+
+def traffic_of(key):
+    """Per-launch DRAM bytes of a kernel from the committed ncu summary, or None."""
+    p = os.path.join(ROOT, "profiles", "ncu_traffic.json")
+    if os.path.exists(p):
+        return json.load(open(p)).get(key)
+    return None
+
+
+class Clocks:
+    """nvidia-smi sampling of SM clocks and throttle reasons during a region."""
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown,"
+         "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+         "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index):
+        self.index = index
+        self.proc = None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.Q}",
+                                          "--format=csv,noheader,nounits", "-lms", "100"],
+                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except Exception:
+            self.proc = None
+        return self
+
+    def __exit__(self, *a):
+        self.rows = []
+        if self.proc is None:
+            return
+        time.sleep(0.25)
+        self.proc.terminate()
+        try:
+            out, _ = self.proc.communicate(timeout=5)
+        except Exception:
+            self.proc.kill()
+            out = ""
+        for line in out.strip().splitlines():
+            f = [x.strip() for x in line.split(",")]
+            if len(f) >= 8:
+                self.rows.append(f)
+
+    def summary(self):
+        if not getattr(self, "rows", None):
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+        sm = [float(r[1]) for r in self.rows if r[1].replace(".", "").isdigit()]
+        mx = [float(r[2]) for r in self.rows if r[2].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in self.rows for i in range(4) if r[4 + i].lower() == "active"})
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": reasons, "samples": len(self.rows)}
+
+
+# ------------------------------------------------------------------ dist ----
+def dist_setup(n_gpus):
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local))
+    return world, rank, local
+
+
+def barrier(world):
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+
+
+def max_over_ranks(x, world, dev):
+    if world == 1:
+        return x
+    import torch.distributed as dist
+    t = torch.tensor([x], dtype=torch.float64, device=dev)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+# ------------------------------------------------------------- b200 arm ----
+def timed_steps(fn, steps, warmup, flush, world, dev, clocks_index):
+    """Per-step device times (ms) of fn(), L2 flushed before each, outside the events."""
+    for _ in range(warmup):
+        fn()
+    torch.cuda.synchronize()
+    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(steps)]
+    barrier(world)
+    torch.cuda.synchronize()
+    with Clocks(clocks_index) as ck:
+        for e0, e1 in evs:
+            flush.zero_()
+            e0.record()
+            fn()
+            e1.record()
+        torch.cuda.synchronize()
+    barrier(world)
+    return [a.elapsed_time(b) for a, b in evs], ck.summary()
+
+
+def kernel_times(call, steps, flush, n_events):
+    """Durations (ms) between consecutive profile marks of the library, per step."""
+    from hba_b200 import _lib
+    L = _lib.load()
+    evs = [torch.cuda.Event(enable_timing=True) for _ in range(n_events)]
+    for e in evs:
+        e.record()
+    torch.cuda.synchronize()
+    arr = (ctypes.c_void_p * n_events)(*[e.cuda_event for e in evs])
+    L.hba_b200_set_profile_events(arr, n_events)
+    per = []
+    try:
+        for _ in range(steps):
+            flush.zero_()
+            call()
+            torch.cuda.synchronize()
+            k = L.hba_b200_profile_events_recorded()
+            per.append([evs[i].elapsed_time(evs[i + 1]) for i in range(k - 1)])
+    finally:
+        L.hba_b200_set_profile_events(None, 0)
+    return [statistics.mean(x) for x in zip(*per)]
+
+
+def decode_bench(name, steps, warmup, world, rank, local, pk):
+    from hba_b200 import HBADecodeCache, baseline_config, synth
+    from hba_b200.attention import stream_of
+    dev = torch.device("cuda", local)
+    cfg, B, n, hier = baseline_config(name)
+    G, dh, Hq, Hkv = cfg.G, cfg.head_dim, cfg.n_heads, cfg.n_kv
+    summ, qkn = synth.make_weights(cfg, dev, seed=0, gains=False)
+    cos, sin = synth.rope_tables(n, dh, 1e6, dev)
+    wl = synth.decode_workload(cfg, B, n, hier=hier, seed=1000 + rank, device=dev, qkn=qkn)
+    cache = HBADecodeCache(cfg, B, n, summ, qkn, cos, sin, device=dev, hier=hier)
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    cache.append(wl["k"], wl["v"])
+    torch.cuda.synchronize()
+    build_s = time.perf_counter() - t0
+    del wl["k"], wl["v"]
+    q = wl["q"].contiguous()
+    out = torch.empty_like(q)
+    lse = torch.empty(B, Hq, dtype=torch.float32, device=dev)
+    flush = torch.empty(FLUSH_BYTES // 4, dtype=torch.float32, device=dev)
+
+    def step_direct():
+        cache.decode_into(q, out, lse, stream=stream_of(dev))
+
+    step_direct()
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        cache.decode_into(q, out, lse, stream=stream_of(dev))
+    times, clocks = timed_steps(graph.replay, steps, warmup, flush, world, dev, local)
+    t_ms = statistics.mean(times)
+    t_ms = max_over_ranks(t_ms, world, dev)
+
+    # dominant kernel (attend) timed live between the library's event marks
+    nmarks = 5 if hier else 4
+    kt = kernel_times(step_direct, max(3, min(steps, 10)), flush, nmarks)
+    attend_ms = kt[-2]
+    keys = cfg.sinks + cfg.window + cfg.k_blocks * cfg.block
+    attend_bytes = B * Hkv * (keys * dh * 2 * 2 + G * dh * 2 * 2)
+    if hier:
+        ns = n // cfg.block // cfg.fanout
+        summ_bytes = B * Hkv * (ns + cfg.beam * cfg.fanout) * cfg.slots * dh * 2
+    else:
+        n_cand = (n - 1 - cfg.window + 1) // cfg.block - 1
+        summ_bytes = B * Hkv * n_cand * cfg.slots * dh * 2
+    step_bytes = attend_bytes + summ_bytes
+    achieved = attend_bytes / (attend_ms * 1e-3) / 1e9
+    tkey = f"attend_{name}"
+    traffic = traffic_of(tkey)
+
+    # e2e: the C-ABI call with the query from pinned host memory and out + lse back
+    q_host = q.cpu().pin_memory()
+    out_host = torch.empty(out.shape, dtype=out.dtype).pin_memory()
+    lse_host = torch.empty(lse.shape, dtype=lse.dtype).pin_memory()
+
+    def step_e2e():
+        q.copy_(q_host, non_blocking=True)
+        cache.decode_into(q, out, lse, stream=stream_of(dev))
+        out_host.copy_(out, non_blocking=True)
+        lse_host.copy_(lse, non_blocking=True)
+
+    e2e_times, _ = timed_steps(step_e2e, steps, warmup, flush, world, dev, local)
+    e2e_ms = max_over_ranks(statistics.mean(e2e_times), world, dev)
+
+    res = dict(
+        metric=METRIC, value=B * world / (t_ms * 1e-3), unit="decode queries/s", n_gpus=world, steps=steps,
+        warmup=warmup, ms_per_step=t_ms, higher_is_better=True, scaling="weak", vs_baseline=None, dtype="bf16",
+        data="synthetic (seeded N(0,1) q/k/v, 8 planted blocks per sequence and kv head)",
+        config=dict(workload=f"{name}: decode, batch {B}/rank, context {n}, {Hq}/{Hkv} heads, dh {dh}, "
+                             f"{'hierarchical beam ' + str(cfg.beam) if hier else 'flat'} top-{cfg.k_blocks}",
+                    batch_per_rank=B, context=n, n_heads=Hq, n_kv=Hkv, head_dim=dh, window=cfg.window,
+                    sinks=cfg.sinks, block=cfg.block, slots=cfg.slots, k_blocks=cfg.k_blocks, hier=hier,
+                    fanout=cfg.fanout if hier else None, beam=cfg.beam if hier else None,
+                    l2="flushed (256 MB write) before every timed step", timing="CUDA graph replay, CUDA events",
+                    parallelism=f"replicas x{world} (batch-sharded, no collective)"),
+        roofline=dict(bound="hbm", kernel="attend_kernel", achieved=achieved, peak=pk["hbm"], unit="GB/s",
+                      frac=achieved / pk["hbm"], peak_source=pk["source"], traffic=traffic,
+                      algorithmic_bytes_per_launch=attend_bytes, kernel_ms=attend_ms),
+        step_effective_gbs=step_bytes / (t_ms * 1e-3) / 1e9,
+        step_algorithmic_bytes=step_bytes,
+        kernel_ms={"select": kt[:-2], "attend": attend_ms, "merge": kt[-1]},
+        cache_build_s=build_s,
+        e2e=dict(value=B * world / (e2e_ms * 1e-3), unit="decode queries/s", ms_per_step=e2e_ms,
+                 h2d_bytes_per_step=q.numel() * q.element_size(),
+                 d2h_bytes_per_step=out.numel() * out.element_size() + lse.numel() * lse.element_size()),
+        gpu_launches=steps * (len(kt) + 0),
+        clocks=clocks,
+    )
+    sample = None
+    if rank == 0:
+        sample = cpu_decode_sample(cache, q, cfg, hier, n)
+    res["cpu_baseline"] = sample
+    del cache
+    torch.cuda.empty_cache()
+    return res
+
+
+def cpu_decode_sample(cache, q, cfg, hier, n, seqs=2):
+    """Oracle (numpy port, one thread) decode of `seqs` sequences of the same
+    workload, copied from the device cache."""
+    from oracle import hba_oracle as orc
+    from hba_b200.ops import qknorm_b200
+    try:
+        from threadpoolctl import threadpool_limits
+    except Exception:  # pragma: no cover
+        threadpool_limits = None
+    qc = qknorm_b200(q[:seqs], cache.q_gain).float().cpu().numpy()
+    nb = n // cfg.block
+    data = []
+    for b in range(seqs):
+        kc = cache.k[b:b + 1, :n].float().cpu().numpy()
+        v = cache.v[b:b + 1, :n].float().cpu().numpy()
+        S0 = cache.summaries[b:b + 1, :, :nb].float().cpu().numpy()
+        S1 = cache.supers[b:b + 1, :, :-(-nb // cfg.fanout)].float().cpu().numpy() if hier else None
+        data.append((kc, v, S0, S1))
+    cos, sin = cache.cos.cpu().numpy(), cache.sin.cpu().numpy()
+    ocfg = dict(block=cfg.block, window=cfg.window, sinks=cfg.sinks, k_blocks=cfg.k_blocks, fanout=cfg.fanout,
+                beam=cfg.beam, qknorm=cfg.qknorm, content_scale_mode=cfg.content_scale_mode, temp_c=cfg.temp_c,
+                n_cal=cfg.n_cal, native_ctx=cfg.native_ctx)
+    scale = orc.union_scale(cfg.qknorm, cfg.content_scale_mode, cfg.temp_c, cfg.n_cal, cfg.native_ctx,
+                            cfg.head_dim, n)
+    ctx = threadpool_limits(limits=1) if threadpool_limits else None
+    if ctx:
+        ctx.__enter__()
+    t0 = time.perf_counter()
+    for b in range(seqs):
+        kc, v, S0, S1 = data[b]
+        orc.decode(qc[b:b + 1], kc, v, cos, sin, S0, S1, ocfg, scale, None, hier=hier, bf16=True, qknorm_q=False)
+    dt = time.perf_counter() - t0
+    if ctx:
+        ctx.__exit__(None, None, None)
+    return dict(value=seqs / dt, unit="decode queries/s", cores=1, kind="port",
+                sample=f"{seqs} sequences of the same workload (one query each, cache contents copied "
+                       f"from the device), numpy oracle, 1 thread")
+
+
+def prefill_bench(name, steps, warmup, world, rank, local, pk):
+    from hba_b200 import baseline_config, synth
+    from hba_b200.attention import (as_f32, c_config, gains, ptr, stream_of, summarizer_weights, union_scale)
+    from hba_b200 import _lib
+    dev = torch.device("cuda", local)
+    cfg, B, n, hier = baseline_config(name)
+    dh, Hq, Hkv = cfg.head_dim, cfg.n_heads, cfg.n_kv
+    summ, qkn = synth.make_weights(cfg, dev, seed=0, gains=False)
+    cos, sin = synth.rope_tables(n, dh, 1e6, dev)
+    wl = synth.prefill_workload(cfg, B, n, seed=2000 + rank, device=dev)
+    q, k, v = wl["q"], wl["k"], wl["v"]
+    out = torch.empty_like(q)
+    lse = torch.empty(B, Hq, n, dtype=torch.float32, device=dev)
+    c = c_config(cfg, hier)
+    L = _lib.load()
+    ws_bytes = L.hba_b200_prefill_workspace_size(ctypes.byref(c), B, n)
+    ws = torch.empty(ws_bytes, dtype=torch.uint8, device=dev)
+    qg, kg = gains(qkn, dev)
+    probes, proj = summarizer_weights(summ, dev)
+    scale = union_scale(cfg, dh, n)
+    flush = torch.empty(FLUSH_BYTES // 4, dtype=torch.float32, device=dev)
+
+    def step():
+        st = L.hba_b200_prefill(ctypes.byref(c), B, n, ctypes.c_float(scale), ptr(q), ptr(k), ptr(v), ptr(cos),
+                                ptr(sin), ptr(qg), ptr(kg), ptr(probes), ptr(proj), ptr(out), ptr(lse), None, None,
+                                ptr(ws), ws_bytes, stream_of(dev))
+        _lib.check(st, "hba_b200_prefill")
+
+    times, clocks = timed_steps(step, steps, warmup, flush, world, dev, local)
+    t_ms = max_over_ranks(statistics.mean(times), world, dev)
+    kt = kernel_times(step, max(2, min(steps, 4)), flush, 5 if not hier else 7)
+    attend_ms = kt[-1]
+    # attended keys per query position i: sinks min(S, i+1), window, routed valid picks
+    i = np.arange(n)
+    win = np.maximum(0, i - np.maximum(cfg.sinks, i - cfg.window + 1) + 1)
+    sink = np.minimum(cfg.sinks, i + 1)
+    lim = i - cfg.window + 1
+    ncand = np.where(lim >= 2 * cfg.block, lim // cfg.block - 1, 0)
+    routed = np.minimum(cfg.k_blocks, ncand) * cfg.block
+    keys = float((win + sink + routed).sum())
+    flops = 4.0 * dh * Hq * B * keys
+    achieved = flops / (attend_ms * 1e-3) / 1e12
+    res = dict(
+        metric=METRIC, value=B * n * world / (t_ms * 1e-3), unit="prefill tokens/s", n_gpus=world, steps=steps,
+        warmup=warmup, ms_per_step=t_ms, higher_is_better=True, scaling="weak", vs_baseline=None, dtype="bf16",
+        data="synthetic (seeded N(0,1) q/k/v; 64-query tiles share a topic with 8 planted blocks)",
+        config=dict(workload=f"{name}: prefill, batch {B}/rank, seq {n}, {Hq}/{Hkv} heads, dh {dh}, flat top-16",
+                    batch_per_rank=B, seq_len=n, n_heads=Hq, n_kv=Hkv, head_dim=dh,
+                    l2="flushed (256 MB write) before every timed step"),
+        roofline=dict(bound="tensor", kernel="attend_kernel", achieved=achieved, peak=pk["bf16"], unit="TFLOP/s",
+                      frac=achieved / pk["bf16"], peak_source=pk["source"], traffic=traffic_of(f"attend_{name}"),
+                      attended_flops=flops, kernel_ms=attend_ms),
+        kernel_ms=kt, clocks=clocks,
+    )
+    del q, k, v, ws, wl
+    torch.cuda.empty_cache()
+    return res
+
+
+# -------------------------------------------------------- reference arm ----
+def _ref_worker(args):
+    """One host process: build one synthetic sequence's cache with the oracle
+    (untimed), run `warmup` decodes, then time `steps` oracle decodes of its query."""
+    name, seed, warmup, steps = args
+    sys.path.insert(0, ROOT)
+    sys.path.insert(0, os.path.join(ROOT, "hierarchical-block-attention_b200"))
+    from hba_b200.config import baseline_config
+    from oracle import hba_oracle as orc
+    cfg, B, n, hier = baseline_config(name)
+    r = np.random.default_rng(seed)
+    dh, Hq, Hkv = cfg.head_dim, cfg.n_heads, cfg.n_kv
+    q = orc.round_bf16(r.standard_normal((1, Hq, dh), dtype=np.float32))
+    k = orc.round_bf16(r.standard_normal((1, n, Hkv, dh), dtype=np.float32))
+    v = orc.round_bf16(r.standard_normal((1, n, Hkv, dh), dtype=np.float32))
+    probes = (r.standard_normal((Hkv, cfg.slots, dh), dtype=np.float32) * dh ** -0.5)
+    proj = np.eye(dh, dtype=np.float32)[None] + r.standard_normal((Hkv, dh, dh), dtype=np.float32) * 0.02
+    ones_q, ones_k = np.ones(Hq, np.float32), np.ones(Hkv, np.float32)
+    kc = orc.head_rmsnorm(k, ones_k, bf16=True)
+    S0 = orc.round_bf16(orc.summarize(kc, probes, proj, cfg.block).astype(np.float32))
+    S1 = orc.round_bf16(orc.build_super(S0, cfg.fanout)[0].astype(np.float32)) if hier else None
+    cos, sin = orc.rope_tables(n, dh, 1e6)
+    ocfg = dict(block=cfg.block, window=cfg.window, sinks=cfg.sinks, k_blocks=cfg.k_blocks, fanout=cfg.fanout,
+                beam=cfg.beam, qknorm=cfg.qknorm, content_scale_mode=cfg.content_scale_mode, temp_c=cfg.temp_c,
+                n_cal=cfg.n_cal, native_ctx=cfg.native_ctx)
+    scale = orc.union_scale(True, "inv_d", cfg.temp_c, cfg.n_cal, cfg.native_ctx, dh, n)
+    for _ in range(warmup):
+        orc.decode(q, kc, v, cos, sin, S0, S1, ocfg, scale, ones_q, hier=hier, bf16=True)
+    t0 = time.perf_counter()
+    for _ in range(steps):
+        orc.decode(q, kc, v, cos, sin, S0, S1, ocfg, scale, ones_q, hier=hier, bf16=True)
+    return time.perf_counter() - t0
+
+
+def reference_arm(args, world, rank):
+    """The reference algorithm's CPU path (the numpy oracle port) on every host
+    core: one process per core, each decoding its own sequence of the workload
+    `steps` times after `warmup`; value = all decodes / the slowest process."""
+    if rank != 0:
+        return None
+    import multiprocessing as mp
+    os.environ.setdefault("OMP_NUM_THREADS", "1")
+    os.environ.setdefault("OPENBLAS_NUM_THREADS", "1")
+    name = args.config if args.config != "cfg2" else "cfg1"
+    procs = max(1, min(os.cpu_count() or 1, 64))
+    with mp.get_context("spawn").Pool(procs) as pool:
+        dts = pool.map(_ref_worker, [(name, 7 + s, args.warmup, args.steps) for s in range(procs)])
+    value = procs * args.steps / max(dts)
+    from hba_b200.config import baseline_config
+    cfg, B, n, hier = baseline_config(name)
+    line = dict(metric=METRIC, value=value, unit="decode queries/s", n_gpus=world, steps=args.steps,
+                warmup=args.warmup, ms_per_step=1e3 * statistics.mean(dts) / args.steps, higher_is_better=True,
+                scaling="weak", vs_baseline=None, dtype="f32 (bf16 inputs)", data="synthetic", impl="reference",
+                config=dict(workload=f"{name}: decode, context {n}, {cfg.n_heads}/{cfg.n_kv} heads, "
+                                     f"dh {cfg.head_dim}, {'hierarchical' if hier else 'flat'} top-{cfg.k_blocks}",
+                            context=n),
+                cpu_baseline=dict(value=value, unit="decode queries/s", cores=procs, kind="port",
+                                  sample=f"{procs} processes x 1 sequence, {args.steps} timed decodes each "
+                                         f"(cache pre-built, untimed), numpy oracle port of the reference eval path"),
+                e2e=dict(value=value, unit="decode queries/s", h2d_bytes_per_step=0, d2h_bytes_per_step=0))
+    return line
+
+
+def main():
+    args = parse()
+    world, rank, local = dist_setup(args.gpus)
+    if args.impl == "reference":
+        line = reference_arm(args, world, rank)
+        if line is not None:
+            print(json.dumps(line))
+        return
+    torch.cuda.set_device(local)
+    sys.path.insert(0, os.path.join(ROOT, "hierarchical-block-attention_b200"))
+    import hba_b200  # noqa: F401  (fails loudly if the CUDA library is missing)
+    hba_b200.load_library()
+    pk = peaks()
+    if args.config in ("cfg1", "cfg3"):
+        res = decode_bench(args.config, args.steps, args.warmup, world, rank, local, pk)
+    else:
+        res = prefill_bench(args.config, args.steps, args.warmup, world, rank, local, pk)
+    if not args.no_secondary and args.config == "cfg1":
+        sec = []
+        for name in ("cfg3", "cfg2"):
+            try:
+                if name == "cfg3":
+                    sec.append(decode_bench(name, min(args.steps, 10), args.warmup, world, rank, local, pk))
+                else:
+                    sec.append(prefill_bench(name, min(args.steps, 3), 3, world, rank, local, pk))
+            except Exception as e:  # report, do not hide, a failing secondary
+                sec.append(dict(config=name, error=repr(e)))
+        res["secondary"] = sec
+    if rank == 0:
+        print(json.dumps(res))
+    if world > 1:
+        import torch.distributed as dist
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

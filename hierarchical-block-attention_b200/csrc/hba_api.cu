@@ -1,0 +1,439 @@
+// C ABI of the HBA B200 library: argument validation, workspace layout and
+// kernel orchestration.  No entry point allocates device memory.
+#include <cmath>
+#include <cstdio>
+
+#include "hba_b200.h"
+#include "hba_internal.h"
+
+using hba::Geom;
+
+namespace {
+
+constexpr size_t kAlign = 256;
+constexpr int kMaxCandPerCta = 2048;  // must match hba_select.cu
+
+size_t align_up(size_t x) { return (x + kAlign - 1) / kAlign * kAlign; }
+
+// Optional event marks at kernel boundaries (hba_b200_set_profile_events).
+struct ProfileHook {
+  cudaEvent_t ev[16];
+  int count = 0;
+  int next = 0;
+};
+ProfileHook g_prof;
+
+void prof_begin(cudaStream_t st) {
+  g_prof.next = 0;
+  if (g_prof.count > 0) cudaEventRecord(g_prof.ev[g_prof.next++], st);
+}
+void prof_mark(cudaStream_t st) {
+  if (g_prof.count > 0 && g_prof.next < g_prof.count) cudaEventRecord(g_prof.ev[g_prof.next++], st);
+}
+
+bool config_ok(const hba_b200_config* c, int* status) {
+  if (c == nullptr) {
+    *status = HBA_B200_ERR_INVALID_ARGUMENT;
+    return false;
+  }
+  if (c->n_heads <= 0 || c->n_kv <= 0 || c->n_heads % c->n_kv != 0 || c->slots <= 0 || c->k_blocks <= 0 ||
+      c->block <= 0 || c->window < 0 || c->sinks < 0 || !(c->eps >= 0.f)) {
+    *status = HBA_B200_ERR_INVALID_ARGUMENT;
+    return false;
+  }
+  const int G = c->n_heads / c->n_kv;
+  if ((c->head_dim != 64 && c->head_dim != 128) || G > 16 || (c->block != 16 && c->block != 32 && c->block != 64) ||
+      c->sinks > c->block || c->k_blocks > 32 || c->slots > 8) {
+    *status = HBA_B200_ERR_UNSUPPORTED;
+    return false;
+  }
+  if (c->hier) {
+    if (c->fanout <= 0 || c->beam <= 0) {
+      *status = HBA_B200_ERR_INVALID_ARGUMENT;
+      return false;
+    }
+    if (c->beam > 32) {
+      *status = HBA_B200_ERR_UNSUPPORTED;
+      return false;
+    }
+  }
+  return true;
+}
+
+Geom make_geom(const hba_b200_config* c, int B, int nq, int n_cap) {
+  Geom g{};
+  g.B = B;
+  g.Hq = c->n_heads;
+  g.Hkv = c->n_kv;
+  g.G = c->n_heads / c->n_kv;
+  g.m = c->slots;
+  g.Bk = c->block;
+  g.W = c->window;
+  g.S = c->sinks;
+  g.K = c->k_blocks;
+  g.F = c->hier ? c->fanout : 1;
+  g.beam = c->hier ? c->beam : 1;
+  g.hier = c->hier ? 1 : 0;
+  g.qknorm = c->qknorm ? 1 : 0;
+  g.eps = c->eps;
+  g.nq = nq;
+  g.n_cap = n_cap;
+  g.nb_cap = n_cap / c->block;
+  g.ns_cap = c->hier ? (g.nb_cap + c->fanout - 1) / c->fanout : 0;
+  return g;
+}
+
+int cuda_status(cudaError_t e) {
+  if (e == cudaSuccess) return HBA_B200_OK;
+  fprintf(stderr, "hba_b200: CUDA error: %s\n", cudaGetErrorString(e));
+  return HBA_B200_ERR_CUDA;
+}
+
+// Split plan shared by the decode and prefill paths.
+struct Plan {
+  int sel_splits;    // flat lists, or super lists (hier)
+  int sel_list_k;    // K, or beam (hier)
+  int child_splits;  // hier only
+  int attn_splits;
+};
+
+int ceil_div(long long a, long long b) { return (int)((a + b - 1) / b); }
+
+Plan make_plan(const hba_b200_config* c, int nb_cap, int bh, bool decode) {
+  Plan p{};
+  const int max_cand = nb_cap;  // blocks 1..nb-2 at most
+  const int per_cta = decode ? 128 : kMaxCandPerCta;
+  if (c->hier) {
+    const int max_sup = (nb_cap + c->fanout - 1) / c->fanout;
+    p.sel_splits = std::max(1, std::max(ceil_div(max_sup, decode ? 64 : kMaxCandPerCta),
+                                        ceil_div(max_sup, kMaxCandPerCta)));
+    p.sel_list_k = c->beam;
+    const int max_child = c->beam * c->fanout;
+    p.child_splits = std::max(1, std::max(ceil_div(max_child, decode ? 64 : kMaxCandPerCta),
+                                          ceil_div(max_child, kMaxCandPerCta)));
+  } else {
+    p.sel_splits = std::max(1, std::max(ceil_div(max_cand, per_cta), ceil_div(max_cand, kMaxCandPerCta)));
+    p.sel_list_k = c->k_blocks;
+    p.child_splits = 0;
+  }
+  if (decode) {
+    const int max_chunks = ceil_div((long long)c->k_blocks * c->block, 64) + ceil_div(c->window, 64) + 1;
+    p.attn_splits = std::max(1, std::min(16, ceil_div(max_chunks, 4)));
+  } else {
+    p.attn_splits = 1;
+  }
+  (void)bh;
+  return p;
+}
+
+struct Lists {
+  float* score;
+  int32_t* idx;
+};
+
+// Carves [score f32 | idx i32] for `entries` list entries from the workspace.
+Lists carve_lists(unsigned char*& ws, size_t entries) {
+  Lists l;
+  l.score = reinterpret_cast<float*>(ws);
+  ws += align_up(entries * sizeof(float));
+  l.idx = reinterpret_cast<int32_t*>(ws);
+  ws += align_up(entries * sizeof(int32_t));
+  return l;
+}
+
+size_t lists_bytes(size_t entries) { return align_up(entries * sizeof(float)) + align_up(entries * sizeof(int32_t)); }
+
+size_t selection_bytes(const hba_b200_config* c, const Plan& p, size_t queries) {
+  size_t b = lists_bytes(queries * p.sel_splits * p.sel_list_k);
+  if (c->hier) b += lists_bytes(queries * p.child_splits * c->k_blocks);
+  return b;
+}
+
+// Runs selection (flat, or super then child) and attention for nq queries per
+// sequence.  Returns an hba_b200_status.
+int run_select_attend(const hba_b200_config* c, const Geom& geo, const hba::QueryPos& qp, const Plan& plan,
+                      const __nv_bfloat16* q, const float* q_gain, const __nv_bfloat16* kc,
+                      const __nv_bfloat16* v, const __nv_bfloat16* summ, const __nv_bfloat16* supers,
+                      const float* cos, const float* sin, __nv_bfloat16* out, float* lse, int32_t* sel_idx,
+                      float* sel_score, unsigned char* ws, cudaStream_t st) {
+  const int dh = c->head_dim;
+  const size_t queries = (size_t)geo.B * geo.Hkv * geo.nq;
+  Lists l1 = carve_lists(ws, queries * plan.sel_splits * plan.sel_list_k);
+  hba::SelParams sp{};
+  sp.geo = geo;
+  sp.qp = qp;
+  sp.q = q;
+  sp.q_gain = q_gain;
+  sp.summ = summ;
+  sp.supers = supers;
+  sp.mode = c->hier ? hba::kSelSuper : hba::kSelFlat;
+  sp.splits = plan.sel_splits;
+  sp.list_k = plan.sel_list_k;
+  sp.out_score = l1.score;
+  sp.out_idx = l1.idx;
+  cudaError_t e = hba::launch_select(sp, dh, st);
+  if (e != cudaSuccess) return cuda_status(e);
+  prof_mark(st);
+  Lists fin = l1;
+  int fin_lists = plan.sel_splits, fin_k = plan.sel_list_k;
+  if (c->hier) {
+    Lists l2 = carve_lists(ws, queries * plan.child_splits * c->k_blocks);
+    sp.mode = hba::kSelChild;
+    sp.in_score = l1.score;
+    sp.in_idx = l1.idx;
+    sp.in_lists = plan.sel_splits;
+    sp.splits = plan.child_splits;
+    sp.list_k = c->k_blocks;
+    sp.out_score = l2.score;
+    sp.out_idx = l2.idx;
+    e = hba::launch_select(sp, dh, st);
+    if (e != cudaSuccess) return cuda_status(e);
+    prof_mark(st);
+    fin = l2;
+    fin_lists = plan.child_splits;
+    fin_k = c->k_blocks;
+  }
+  hba::AttnParams ap{};
+  ap.geo = geo;
+  ap.qp = qp;
+  ap.splits = plan.attn_splits;
+  ap.in_lists = fin_lists;
+  ap.list_k = fin_k;
+  ap.q = q;
+  ap.q_gain = q_gain;
+  ap.k = kc;
+  ap.v = v;
+  ap.cos = cos;
+  ap.sin = sin;
+  ap.in_score = fin.score;
+  ap.in_idx = fin.idx;
+  ap.out = out;
+  ap.lse = lse;
+  ap.sel_idx = sel_idx;
+  ap.sel_score = sel_score;
+  if (plan.attn_splits > 1) ap.part = reinterpret_cast<float*>(ws);
+  e = hba::launch_attend(ap, dh, st);
+  if (e != cudaSuccess) return cuda_status(e);
+  prof_mark(st);
+  if (plan.attn_splits > 1) {
+    hba::MergeParams mp{};
+    mp.B = geo.B;
+    mp.Hq = geo.Hq;
+    mp.Hkv = geo.Hkv;
+    mp.G = geo.G;
+    mp.nq = geo.nq;
+    mp.splits = plan.attn_splits;
+    mp.part = ap.part;
+    mp.out = out;
+    mp.lse = lse;
+    e = hba::launch_merge(mp, dh, st);
+    if (e != cudaSuccess) return cuda_status(e);
+    prof_mark(st);
+  }
+  return HBA_B200_OK;
+}
+
+size_t partial_bytes(const hba_b200_config* c, const Plan& p, size_t queries) {
+  if (p.attn_splits <= 1) return 0;
+  return align_up(queries * p.attn_splits * 16 * (size_t)(c->head_dim + 2) * sizeof(float));
+}
+
+}  // namespace
+
+extern "C" {
+
+const char* hba_b200_status_string(int s) {
+  switch (s) {
+    case HBA_B200_OK: return "ok";
+    case HBA_B200_ERR_INVALID_ARGUMENT: return "invalid argument";
+    case HBA_B200_ERR_NOT_BLOCK_MULTIPLE: return "sequence length is not a multiple of the block size";
+    case HBA_B200_ERR_WORKSPACE: return "workspace too small";
+    case HBA_B200_ERR_UNSUPPORTED: return "configuration outside the compiled kernels' range";
+    case HBA_B200_ERR_CUDA: return "CUDA error";
+    case HBA_B200_ERR_DEVICE_TIMEOUT: return "device-side wait timed out";
+    default: return "unknown status";
+  }
+}
+
+int hba_b200_version(void) { return 100; }
+
+int hba_b200_set_profile_events(void* const* events, int32_t count) {
+  if (count < 0 || count > 16 || (count > 0 && events == nullptr)) return HBA_B200_ERR_INVALID_ARGUMENT;
+  for (int i = 0; i < count; ++i) g_prof.ev[i] = static_cast<cudaEvent_t>(events[i]);
+  g_prof.count = count;
+  g_prof.next = 0;
+  return HBA_B200_OK;
+}
+
+int hba_b200_profile_events_recorded(void) { return g_prof.next; }
+
+int hba_b200_qknorm(const void* x, void* y, const float* gain, int64_t rows, int32_t heads, int32_t head_dim,
+                    float eps, cudaStream_t stream) {
+  if (x == nullptr || y == nullptr || gain == nullptr || rows < 0 || heads <= 0) return HBA_B200_ERR_INVALID_ARGUMENT;
+  if (head_dim != 64 && head_dim != 128) return HBA_B200_ERR_UNSUPPORTED;
+  return cuda_status(hba::launch_qknorm(static_cast<const __nv_bfloat16*>(x), static_cast<__nv_bfloat16*>(y), gain,
+                                        rows, heads, head_dim, eps, stream));
+}
+
+int hba_b200_summarize(const hba_b200_config* cfg, int32_t batch, int32_t n_cap, const void* k_cache,
+                       const float* probes, const float* proj, void* summaries, int32_t blk_begin, int32_t blk_end,
+                       cudaStream_t stream) {
+  int st = HBA_B200_OK;
+  if (!config_ok(cfg, &st)) return st;
+  if (batch <= 0 || n_cap <= 0 || k_cache == nullptr || probes == nullptr || proj == nullptr ||
+      summaries == nullptr || blk_begin < 0 || blk_end < blk_begin || blk_end > n_cap / cfg->block)
+    return HBA_B200_ERR_INVALID_ARGUMENT;
+  Geom geo = make_geom(cfg, batch, 1, n_cap);
+  return cuda_status(hba::launch_summarize(geo, cfg->head_dim, static_cast<const __nv_bfloat16*>(k_cache), probes,
+                                           proj, static_cast<__nv_bfloat16*>(summaries), blk_begin, blk_end,
+                                           nullptr, 0, stream));
+}
+
+int hba_b200_build_supers(const hba_b200_config* cfg, int32_t batch, int32_t nb_cap, int32_t nb,
+                          const void* summaries, void* supers, int32_t s_begin, int32_t s_end, cudaStream_t stream) {
+  int st = HBA_B200_OK;
+  if (!config_ok(cfg, &st)) return st;
+  if (!cfg->hier && cfg->fanout <= 0) return HBA_B200_ERR_INVALID_ARGUMENT;
+  const int F = cfg->fanout;
+  if (batch <= 0 || nb_cap <= 0 || nb < 0 || nb > nb_cap || summaries == nullptr || supers == nullptr ||
+      s_begin < 0 || s_end < s_begin || s_end > (nb_cap + F - 1) / F)
+    return HBA_B200_ERR_INVALID_ARGUMENT;
+  hba_b200_config c2 = *cfg;
+  c2.hier = 1;
+  if (c2.beam <= 0) c2.beam = 1;
+  Geom geo = make_geom(&c2, batch, 1, nb_cap * cfg->block);
+  return cuda_status(hba::launch_supers(geo, cfg->head_dim, nb, static_cast<const __nv_bfloat16*>(summaries),
+                                        static_cast<__nv_bfloat16*>(supers), s_begin, s_end, nullptr, 0, stream));
+}
+
+int hba_b200_append_kv(const hba_b200_config* cfg, int32_t batch, int32_t n_cap, int32_t t, const int32_t* pos,
+                       const void* k_new, const void* v_new, const float* k_gain, const float* probes,
+                       const float* proj, void* k_cache, void* v_cache, void* summaries, void* supers,
+                       cudaStream_t stream) {
+  int st = HBA_B200_OK;
+  if (!config_ok(cfg, &st)) return st;
+  if (batch <= 0 || n_cap <= 0 || t <= 0 || pos == nullptr || k_new == nullptr || v_new == nullptr ||
+      k_cache == nullptr || v_cache == nullptr || (cfg->qknorm && k_gain == nullptr))
+    return HBA_B200_ERR_INVALID_ARGUMENT;
+  if (summaries != nullptr && (probes == nullptr || proj == nullptr)) return HBA_B200_ERR_INVALID_ARGUMENT;
+  Geom geo = make_geom(cfg, batch, 1, n_cap);
+  const int dh = cfg->head_dim;
+  cudaError_t e = hba::launch_append(geo, t, pos, static_cast<const __nv_bfloat16*>(k_new),
+                                     static_cast<const __nv_bfloat16*>(v_new), k_gain,
+                                     static_cast<__nv_bfloat16*>(k_cache), static_cast<__nv_bfloat16*>(v_cache), dh,
+                                     stream);
+  if (e != cudaSuccess) return cuda_status(e);
+  if (summaries != nullptr) {
+    e = hba::launch_summarize(geo, dh, static_cast<const __nv_bfloat16*>(k_cache), probes, proj,
+                              static_cast<__nv_bfloat16*>(summaries), 0, 0, pos, t, stream);
+    if (e != cudaSuccess) return cuda_status(e);
+    if (supers != nullptr && cfg->hier) {
+      e = hba::launch_supers(geo, dh, 0, static_cast<const __nv_bfloat16*>(summaries),
+                             static_cast<__nv_bfloat16*>(supers), 0, 0, pos, t, stream);
+      if (e != cudaSuccess) return cuda_status(e);
+    }
+  }
+  return HBA_B200_OK;
+}
+
+size_t hba_b200_decode_workspace_size(const hba_b200_config* cfg, int32_t batch, int32_t n_cap) {
+  int st = HBA_B200_OK;
+  if (!config_ok(cfg, &st) || batch <= 0 || n_cap <= 0 || n_cap % cfg->block != 0) return 0;
+  const Plan plan = make_plan(cfg, n_cap / cfg->block, batch * cfg->n_kv, true);
+  const size_t queries = (size_t)batch * cfg->n_kv;
+  return selection_bytes(cfg, plan, queries) + partial_bytes(cfg, plan, queries);
+}
+
+int hba_b200_decode(const hba_b200_config* cfg, int32_t batch, int32_t n_cap, const int32_t* seq_lens,
+                    const float* scales, const void* q, const float* q_gain, const void* k_cache,
+                    const void* v_cache, const void* summaries, const void* supers, const float* cos,
+                    const float* sin, void* out, float* lse, int32_t* sel_idx, float* sel_score, void* workspace,
+                    size_t workspace_bytes, cudaStream_t stream) {
+  int st = HBA_B200_OK;
+  if (!config_ok(cfg, &st)) return st;
+  if (batch <= 0 || n_cap <= 0 || seq_lens == nullptr || scales == nullptr || q == nullptr || k_cache == nullptr ||
+      v_cache == nullptr || summaries == nullptr || cos == nullptr || sin == nullptr || out == nullptr ||
+      (cfg->qknorm && q_gain == nullptr) || (cfg->hier && supers == nullptr) ||
+      ((sel_idx == nullptr) != (sel_score == nullptr)))
+    return HBA_B200_ERR_INVALID_ARGUMENT;
+  if (n_cap % cfg->block != 0) return HBA_B200_ERR_NOT_BLOCK_MULTIPLE;
+  Geom geo = make_geom(cfg, batch, 1, n_cap);
+  const Plan plan = make_plan(cfg, geo.nb_cap, batch * cfg->n_kv, true);
+  const size_t need = hba_b200_decode_workspace_size(cfg, batch, n_cap);
+  if (workspace == nullptr || workspace_bytes < need) return HBA_B200_ERR_WORKSPACE;
+  hba::QueryPos qp{seq_lens, scales, 0, 0.f};
+  prof_begin(stream);
+  return run_select_attend(cfg, geo, qp, plan, static_cast<const __nv_bfloat16*>(q), q_gain,
+                           static_cast<const __nv_bfloat16*>(k_cache), static_cast<const __nv_bfloat16*>(v_cache),
+                           static_cast<const __nv_bfloat16*>(summaries), static_cast<const __nv_bfloat16*>(supers),
+                           cos, sin, static_cast<__nv_bfloat16*>(out), lse, sel_idx, sel_score,
+                           static_cast<unsigned char*>(workspace), stream);
+}
+
+size_t hba_b200_prefill_workspace_size(const hba_b200_config* cfg, int32_t batch, int32_t n) {
+  int st = HBA_B200_OK;
+  if (!config_ok(cfg, &st) || batch <= 0 || n <= 0 || n % cfg->block != 0) return 0;
+  const int dh = cfg->head_dim;
+  const size_t nb = (size_t)n / cfg->block;
+  const size_t ns = cfg->hier ? (nb + cfg->fanout - 1) / cfg->fanout : 0;
+  const Plan plan = make_plan(cfg, (int)nb, batch * cfg->n_kv, false);
+  const size_t queries = (size_t)batch * cfg->n_kv * n;
+  size_t b = align_up((size_t)batch * n * cfg->n_kv * dh * 2);            // QKNorm'd keys
+  b += align_up((size_t)batch * cfg->n_kv * nb * cfg->slots * dh * 2);    // summaries
+  b += align_up((size_t)batch * cfg->n_kv * ns * cfg->slots * dh * 2);    // supers
+  b += selection_bytes(cfg, plan, queries) + partial_bytes(cfg, plan, queries);
+  return b;
+}
+
+int hba_b200_prefill(const hba_b200_config* cfg, int32_t batch, int32_t n, float scale, const void* q, const void* k,
+                     const void* v, const float* cos, const float* sin, const float* q_gain, const float* k_gain,
+                     const float* probes, const float* proj, void* out, float* lse, int32_t* sel_idx,
+                     float* sel_score, void* workspace, size_t workspace_bytes, cudaStream_t stream) {
+  int st = HBA_B200_OK;
+  if (!config_ok(cfg, &st)) return st;
+  if (batch <= 0 || n <= 0 || q == nullptr || k == nullptr || v == nullptr || cos == nullptr || sin == nullptr ||
+      probes == nullptr || proj == nullptr || out == nullptr || (cfg->qknorm && (q_gain == nullptr || k_gain == nullptr)) ||
+      ((sel_idx == nullptr) != (sel_score == nullptr)) || !std::isfinite(scale))
+    return HBA_B200_ERR_INVALID_ARGUMENT;
+  if (n % cfg->block != 0) return HBA_B200_ERR_NOT_BLOCK_MULTIPLE;
+  if (n > 65535) return HBA_B200_ERR_UNSUPPORTED;  // query index rides gridDim.y
+  const size_t need = hba_b200_prefill_workspace_size(cfg, batch, n);
+  if (workspace == nullptr || workspace_bytes < need) return HBA_B200_ERR_WORKSPACE;
+  const int dh = cfg->head_dim;
+  const size_t nb = (size_t)n / cfg->block;
+  const size_t ns = cfg->hier ? (nb + cfg->fanout - 1) / cfg->fanout : 0;
+  unsigned char* ws = static_cast<unsigned char*>(workspace);
+  __nv_bfloat16* kc = reinterpret_cast<__nv_bfloat16*>(ws);
+  ws += align_up((size_t)batch * n * cfg->n_kv * dh * 2);
+  __nv_bfloat16* summ = reinterpret_cast<__nv_bfloat16*>(ws);
+  ws += align_up((size_t)batch * cfg->n_kv * nb * cfg->slots * dh * 2);
+  __nv_bfloat16* sup = reinterpret_cast<__nv_bfloat16*>(ws);
+  ws += align_up((size_t)batch * cfg->n_kv * ns * cfg->slots * dh * 2);
+
+  Geom geo = make_geom(cfg, batch, n, n);
+  cudaError_t e;
+  prof_begin(stream);
+  if (cfg->qknorm) {
+    e = hba::launch_qknorm(static_cast<const __nv_bfloat16*>(k), kc, k_gain, (int64_t)batch * n, cfg->n_kv, dh,
+                           cfg->eps, stream);
+    if (e != cudaSuccess) return cuda_status(e);
+  } else {
+    kc = const_cast<__nv_bfloat16*>(static_cast<const __nv_bfloat16*>(k));  // keys are used as given
+  }
+  prof_mark(stream);
+  e = hba::launch_summarize(geo, dh, kc, probes, proj, summ, 0, (int)nb, nullptr, 0, stream);
+  if (e != cudaSuccess) return cuda_status(e);
+  prof_mark(stream);
+  if (cfg->hier) {
+    e = hba::launch_supers(geo, dh, (int)nb, summ, sup, 0, (int)ns, nullptr, 0, stream);
+    if (e != cudaSuccess) return cuda_status(e);
+    prof_mark(stream);
+  }
+  const Plan plan = make_plan(cfg, (int)nb, batch * cfg->n_kv, false);
+  hba::QueryPos qp{nullptr, nullptr, n, scale};
+  return run_select_attend(cfg, geo, qp, plan, static_cast<const __nv_bfloat16*>(q), q_gain, kc,
+                           static_cast<const __nv_bfloat16*>(v), summ, sup, cos, sin, static_cast<__nv_bfloat16*>(out),
+                           lse, sel_idx, sel_score, ws, stream);
+}
+
+}  // extern "C"

@@ -1,0 +1,96 @@
+// Internal parameter blocks and launcher declarations shared by the kernel
+// translation units and the C-ABI layer (hba_api.cu).
+#pragma once
+
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace hba {
+
+// Where a query sits: decode (one query per sequence at seq_lens[b]-1 over a
+// cache of seq_lens[b] tokens, per-sequence scale) or prefill (query t of a
+// length-n sequence at position t, one scale).
+struct QueryPos {
+  const int32_t* seq_lens;  // decode: [B]; prefill: nullptr
+  const float* scales;      // decode: [B]; prefill: nullptr
+  int32_t n_fixed;          // prefill sequence length
+  float scale_fixed;        // prefill scale
+};
+
+// Geometry shared by selection and attention kernels.
+struct Geom {
+  int32_t B, Hq, Hkv, G, m, Bk, W, S, K, F, beam, hier, qknorm;
+  float eps;
+  int32_t nq;      // queries per sequence in this launch (decode 1, prefill n)
+  int32_t n_cap;   // token capacity of the key/value buffers
+  int32_t nb_cap;  // block capacity of the summary buffer
+  int32_t ns_cap;  // super capacity of the super buffer
+};
+
+enum SelMode : int32_t { kSelFlat = 0, kSelSuper = 1, kSelChild = 2 };
+
+struct SelParams {
+  Geom geo;
+  QueryPos qp;
+  int32_t mode;
+  int32_t splits;      // gridDim.x
+  int32_t list_k;      // entries per output list (K, or beam for supers)
+  int32_t in_lists;    // child mode: super lists per query
+  const __nv_bfloat16* q;       // [B, nq, Hq, dh]
+  const float* q_gain;          // [Hq]
+  const __nv_bfloat16* summ;    // [B, Hkv, nb_cap, m, dh]
+  const __nv_bfloat16* supers;  // [B, Hkv, ns_cap, m, dh]
+  const float* in_score;        // child mode: [B*Hkv, nq, in_lists, beam]
+  const int32_t* in_idx;
+  float* out_score;             // [B*Hkv, nq, splits, list_k]
+  int32_t* out_idx;
+};
+
+struct AttnParams {
+  Geom geo;
+  QueryPos qp;
+  int32_t splits;      // gridDim.x (key-range partitions per query)
+  int32_t in_lists;    // selection lists per query to merge
+  int32_t list_k;      // entries per selection list
+  const __nv_bfloat16* q;   // [B, nq, Hq, dh] raw
+  const float* q_gain;
+  const __nv_bfloat16* k;   // [B, n_cap, Hkv, dh] QKNorm'd NoPE keys
+  const __nv_bfloat16* v;   // [B, n_cap, Hkv, dh]
+  const float* cos;         // [n_cap, dh]
+  const float* sin;
+  const float* in_score;    // [B*Hkv, nq, in_lists, list_k]
+  const int32_t* in_idx;
+  __nv_bfloat16* out;       // [B, nq, Hq, dh]      (splits == 1)
+  float* lse;               // [B, Hq, nq] or null  (splits == 1)
+  float* part;              // [B*Hkv, nq, splits, 16, dh + 2] (splits > 1)
+  int32_t* sel_idx;         // [B, Hkv, nq, K] or null
+  float* sel_score;
+};
+
+struct MergeParams {
+  int32_t B, Hq, Hkv, G, nq, splits;
+  const float* part;
+  __nv_bfloat16* out;
+  float* lse;
+};
+
+cudaError_t launch_qknorm(const __nv_bfloat16* x, __nv_bfloat16* y, const float* gain, int64_t rows,
+                          int heads, int dh, float eps, cudaStream_t st);
+cudaError_t launch_append(const Geom& geo, int t, const int32_t* pos, const __nv_bfloat16* k_new,
+                          const __nv_bfloat16* v_new, const float* k_gain, __nv_bfloat16* k_cache,
+                          __nv_bfloat16* v_cache, int dh, cudaStream_t st);
+// Summaries of blocks [blk_begin, blk_end) for every sequence; if pos/t are
+// given (append), only blocks completed by tokens [pos[b], pos[b]+t) of
+// sequence b are rebuilt.
+cudaError_t launch_summarize(const Geom& geo, int dh, const __nv_bfloat16* k_cache, const float* probes,
+                             const float* proj, __nv_bfloat16* summ, int blk_begin, int blk_end,
+                             const int32_t* pos, int t, cudaStream_t st);
+cudaError_t launch_supers(const Geom& geo, int dh, int nb_fixed, const __nv_bfloat16* summ,
+                          __nv_bfloat16* supers, int s_begin, int s_end, const int32_t* pos, int t,
+                          cudaStream_t st);
+cudaError_t launch_select(const SelParams& p, int dh, cudaStream_t st);
+cudaError_t launch_attend(const AttnParams& p, int dh, cudaStream_t st);
+cudaError_t launch_merge(const MergeParams& p, int dh, cudaStream_t st);
+
+}  // namespace hba

@@ -1,0 +1,176 @@
+/*
+ * hba_b200.h -- C ABI of the B200 (sm_100a) implementation of the
+ * Hierarchical Block Attention (HBA) hot path.
+ *
+ * Every entry point takes plain device pointers, sizes and a cudaStream_t,
+ * enqueues its kernels on that stream, and returns an hba_b200_status; none
+ * aborts the process and none allocates device memory (scratch space comes
+ * from the caller's `workspace`).  All tensors are dense, row-major, in the
+ * layouts documented per argument (the reference's token-major
+ * [B, n, H, dh] for q/k/v/out and [B, Hkv, nb, m, dh] for block summaries).
+ *
+ * Reference = nealxpatel/hierarchical-block-attention, file paths relative to
+ * that project.  Each entry point names the reference interface it replaces.
+ */
+#ifndef HBA_B200_H
+#define HBA_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#include <cuda_runtime_api.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef enum hba_b200_status {
+  HBA_B200_OK = 0,
+  HBA_B200_ERR_INVALID_ARGUMENT = 1,   /* null pointer, non-positive size, inconsistent heads */
+  HBA_B200_ERR_NOT_BLOCK_MULTIPLE = 2, /* n % block != 0 (reference: assert n % Bk == 0) */
+  HBA_B200_ERR_WORKSPACE = 3,          /* workspace smaller than the *_workspace_size query */
+  HBA_B200_ERR_UNSUPPORTED = 4,        /* knob outside the compiled kernels' range */
+  HBA_B200_ERR_CUDA = 5,               /* a kernel launch or stream operation failed */
+  HBA_B200_ERR_DEVICE_TIMEOUT = 6      /* a bounded device-side wait expired */
+} hba_b200_status;
+
+/* Architecture knobs, mirroring HBAConfig (src/hba/config.py:105-184). */
+typedef struct hba_b200_config {
+  int32_t n_heads;   /* Hq, query heads                                   */
+  int32_t n_kv;      /* Hkv, KV heads (GQA); G = Hq / Hkv <= 16           */
+  int32_t head_dim;  /* dh: 64 or 128                                     */
+  int32_t block;     /* Bk, routing block size: 16, 32 or 64              */
+  int32_t window;    /* W, RoPE local window (>= 0)                       */
+  int32_t sinks;     /* S, NoPE sink tokens (0 <= S <= Bk)                */
+  int32_t k_blocks;  /* routed top-k budget (1..32)                       */
+  int32_t slots;     /* m, summary slots per block (1..8)                 */
+  int32_t fanout;    /* F, children per super-summary (hier)              */
+  int32_t beam;      /* super-summaries kept by the beam (hier)           */
+  int32_t hier;      /* 0: flat scan; 1: two-level beam descent           */
+  int32_t qknorm;    /* 1: RMS-normalise q and k with per-head gains      */
+  float eps;         /* QKNorm clamp on mean(x^2) (reference: 1e-6)       */
+} hba_b200_config;
+
+/* Human-readable name of a status code (static storage). */
+const char* hba_b200_status_string(int status);
+
+/* Library version, major*10000 + minor*100 + patch. */
+int hba_b200_version(void);
+
+/*
+ * Per-head RMS normalisation with a scalar gain per head:
+ *   y = bf16( x / sqrt(max(mean(x^2), eps)) * gain[h] ), math in fp32.
+ * x, y: [rows, heads, head_dim] bf16 (may alias); gain: [heads] fp32.
+ * Replaces _HeadRMSNorm.forward (src/hba/attention.py:88-94), i.e. the
+ * QKNorm applied by _content_qk (src/hba/attention.py:173-198).
+ */
+int hba_b200_qknorm(const void* x, void* y, const float* gain, int64_t rows, int32_t heads,
+                    int32_t head_dim, float eps, cudaStream_t stream);
+
+/*
+ * Learned slot summaries of complete key blocks [blk_begin, blk_end):
+ *   att = softmax_t(probes[g] . k_t * dh^-1/2); S = (att @ k) @ proj[g]
+ * k_cache:   [batch, n_cap, Hkv, dh] bf16, QKNorm'd NoPE keys
+ * probes:    [Hkv, m, dh] fp32;  proj: [Hkv, dh, dh] fp32
+ * summaries: [batch, Hkv, nb_cap, m, dh] bf16, nb_cap = n_cap / block
+ * Replaces SlotSummarizer.summarize (src/hba/summarizer.py:34-42).
+ */
+int hba_b200_summarize(const hba_b200_config* cfg, int32_t batch, int32_t n_cap, const void* k_cache,
+                       const float* probes, const float* proj, void* summaries, int32_t blk_begin,
+                       int32_t blk_end, cudaStream_t stream);
+
+/*
+ * Super-summaries over the first nb blocks: per-slot mean of `fanout`
+ * children, the last group averaged over the children present.  Writes
+ * supers [s_begin, s_end) of [batch, Hkv, ns_cap, m, dh] bf16,
+ * ns_cap = ceil(nb_cap / fanout).
+ * Replaces build_super (src/hba/attention.py:202-214).
+ */
+int hba_b200_build_supers(const hba_b200_config* cfg, int32_t batch, int32_t nb_cap, int32_t nb,
+                          const void* summaries, void* supers, int32_t s_begin, int32_t s_end,
+                          cudaStream_t stream);
+
+/*
+ * Append `t` new tokens per sequence at positions pos[b] .. pos[b]+t-1 of a
+ * KV/summary cache: k is QKNorm'd (k_gain) and stored, v stored, and the
+ * summaries of blocks completed by the append (plus the super-summaries that
+ * contain them, when `supers` is not NULL) are rebuilt.
+ * k_new, v_new: [batch, t, Hkv, dh] bf16 raw; pos: [batch] int32 device.
+ * Has no single counterpart in the reference, which recomputes QKNorm and
+ * every summary on each call (src/hba/attention.py:631,659); it produces the
+ * same cache contents incrementally.
+ */
+int hba_b200_append_kv(const hba_b200_config* cfg, int32_t batch, int32_t n_cap, int32_t t,
+                       const int32_t* pos, const void* k_new, const void* v_new, const float* k_gain,
+                       const float* probes, const float* proj, void* k_cache, void* v_cache,
+                       void* summaries, void* supers, cudaStream_t stream);
+
+/* Bytes of scratch needed by hba_b200_decode for this batch and cache capacity
+ * (0 when the configuration is rejected). */
+size_t hba_b200_decode_workspace_size(const hba_b200_config* cfg, int32_t batch, int32_t n_cap);
+
+/*
+ * One decode step: the newest token of every sequence (position
+ * seq_lens[b]-1) attends over its cached context with one union softmax over
+ * sinks (NoPE), the RoPE window and the top-k routed blocks (NoPE), routed by
+ * QKNorm'd grouped-query scores against the cached block summaries (flat
+ * scan, or the two-level beam over `supers` when cfg->hier).
+ *   seq_lens:  [batch] int32 device, 1 <= seq_lens[b] <= n_cap
+ *   scales:    [batch] fp32 device, union logit scale (content scale x tau(n))
+ *   q:         [batch, Hq, dh] bf16 raw query;  q_gain: [Hq] fp32
+ *   k_cache, v_cache: [batch, n_cap, Hkv, dh] bf16 (keys QKNorm'd, NoPE)
+ *   summaries: [batch, Hkv, n_cap/block, m, dh] bf16
+ *   supers:    [batch, Hkv, ceil(n_cap/block/F), m, dh] bf16 (hier only)
+ *   cos, sin:  [n_cap, dh] fp32 RoPE tables (rope_tables layout)
+ *   out:       [batch, Hq, dh] bf16;  lse: [batch, Hq] fp32 natural-log or NULL
+ *   sel_idx:   [batch, Hkv, k_blocks] int32 (-1: no pick) or NULL
+ *   sel_score: [batch, Hkv, k_blocks] fp32 or NULL
+ * Replaces the per-query body of hba_attention_eval
+ * (src/hba/attention.py:663-711) at cs = n-1, flat (:694-698) or
+ * hierarchical (:690-693, hier_select :217-246).
+ */
+int hba_b200_decode(const hba_b200_config* cfg, int32_t batch, int32_t n_cap, const int32_t* seq_lens,
+                    const float* scales, const void* q, const float* q_gain, const void* k_cache,
+                    const void* v_cache, const void* summaries, const void* supers, const float* cos,
+                    const float* sin, void* out, float* lse, int32_t* sel_idx, float* sel_score,
+                    void* workspace, size_t workspace_bytes, cudaStream_t stream);
+
+/* Bytes of scratch needed by hba_b200_prefill (0 when rejected). */
+size_t hba_b200_prefill_workspace_size(const hba_b200_config* cfg, int32_t batch, int32_t n);
+
+/*
+ * Full HBA attention forward over n tokens (n % block == 0): QKNorm, block
+ * summaries, (super-summaries), per-query top-k selection and the fused union
+ * softmax with one online log-sum-exp.
+ *   q: [batch, n, Hq, dh], k, v: [batch, n, Hkv, dh] bf16 raw projections
+ *   scale: union logit scale (content_scale x tau(n), or dh^-1/2 without QKNorm)
+ *   cos, sin: [n, dh] fp32; q_gain: [Hq], k_gain: [Hkv] fp32
+ *   probes: [Hkv, m, dh], proj: [Hkv, dh, dh] fp32 (SlotSummarizer weights)
+ *   out: [batch, n, Hq, dh] bf16; lse: [batch, Hq, n] fp32 or NULL
+ *   sel_idx / sel_score: [batch, Hkv, n, k_blocks] or NULL
+ * Replaces hba_attention_eval (src/hba/attention.py:610-713, hier or flat)
+ * and the forward of hba_attention_fused / hba_attention_dense
+ * (src/hba/attention.py:552-607, :306-389), which compute the same union.
+ */
+int hba_b200_prefill(const hba_b200_config* cfg, int32_t batch, int32_t n, float scale, const void* q,
+                     const void* k, const void* v, const float* cos, const float* sin, const float* q_gain,
+                     const float* k_gain, const float* probes, const float* proj, void* out, float* lse,
+                     int32_t* sel_idx, float* sel_score, void* workspace, size_t workspace_bytes,
+                     cudaStream_t stream);
+
+/*
+ * Profiling hook (no counterpart in the reference).  With count > 0, each
+ * later hba_b200_decode / hba_b200_prefill call records events[0] before its
+ * first kernel and events[i] after its i-th kernel, up to `count` events (at
+ * most 16), on the call's stream; hba_b200_profile_events_recorded() returns
+ * how many the last call recorded.  count == 0 turns it off.  Process-global,
+ * not thread-safe; leave it off in production and during graph capture.
+ */
+int hba_b200_set_profile_events(void* const* events, int32_t count);
+int hba_b200_profile_events_recorded(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* HBA_B200_H */

@@ -137,8 +137,11 @@ def grouped_query(qc, Hkv, bf16=False):
     qc = np.asarray(qc, np.float32)
     B, n, Hq, dh = qc.shape
     G = Hq // Hkv
-    s = qc.reshape(B, n, Hkv, G, dh).astype(np.float64).sum(3)
-    s = s.transpose(0, 2, 1, 3).astype(np.float32)
+    q5 = qc.reshape(B, n, Hkv, G, dh)
+    s = q5[:, :, :, 0, :].copy()
+    for h in range(1, G):                     # fp32 adds in head order (the CUDA path's order)
+        s = (s + q5[:, :, :, h, :]).astype(np.float32)
+    s = s.transpose(0, 2, 1, 3)
     return round_bf16(s) if bf16 else s
 
 
@@ -288,7 +291,7 @@ def select_rows(pos, qg_rows, S0, S1, cfg, scale, hier):
 
 
 def eval_forward(q, k, v, cos, sin, cfg, probes, proj, q_gain, k_gain, hier=False,
-                 bf16=False, rows=None, summaries=None, supers=None):
+                 bf16=False, rows=None, summaries=None, supers=None, kc=None, qc=None):
     """`hba_attention_eval` (attention.py:610-713), non-equiv branch, for the
     query positions `rows` (default: all).  q: [B,n,Hq,dh]; k, v: [B,n,Hkv,dh];
     cfg: dict with block, window, sinks, k_blocks, fanout, beam, qknorm,
@@ -303,8 +306,8 @@ def eval_forward(q, k, v, cos, sin, cfg, probes, proj, q_gain, k_gain, hier=Fals
     Bk = cfg["block"]
     assert n % Bk == 0, (n, Bk)
     if cfg["qknorm"]:
-        qc = head_rmsnorm(q, q_gain, bf16=bf16)
-        kc = head_rmsnorm(k, k_gain, bf16=bf16)
+        qc = head_rmsnorm(q, q_gain, bf16=bf16) if qc is None else np.asarray(qc, np.float32)
+        kc = head_rmsnorm(k, k_gain, bf16=bf16) if kc is None else np.asarray(kc, np.float32)
     else:
         qc, kc = q, k
     scale = union_scale(cfg["qknorm"], cfg.get("content_scale_mode", "inv_d"),

@@ -1,0 +1,218 @@
+"""GPU parity: the CUDA path (through the C-ABI) against the oracle on the
+same seeded inputs.  Selection must be index-exact (ties within 1e-6 logit
+excepted), outputs within 2e-2 max-abs (bf16), LSE within 1e-3."""
+
+import numpy as np
+import pytest
+import torch
+
+import gpu_helpers as H
+from hba_b200 import HBADecodeCache, hba_attention_b200, synth
+from hba_b200.ops import build_super_b200, qknorm_b200, summarize_b200
+from oracle import hba_oracle as orc
+
+pytestmark = pytest.mark.gpu
+
+
+# ------------------------------------------------------------ components ----
+@pytest.mark.parametrize("dh", [64, 128])
+def test_qknorm_kernel_matches_oracle(dh):
+    g = torch.Generator(device="cuda").manual_seed(1)
+    x = (torch.randn(37, 5, dh, generator=g, device="cuda") * 3 + 1).to(torch.bfloat16)
+    gain = torch.rand(5, generator=g, device="cuda") + 0.5
+    y = H.np32(qknorm_b200(x, gain))
+    ref = orc.head_rmsnorm(H.np32(x), H.np32(gain), bf16=True)
+    ulp = np.abs(ref) * 2.0 ** -7 + 1e-30
+    assert (np.abs(y - ref) <= ulp).all()
+    assert (y == ref).mean() > 0.99
+    rms = np.sqrt((H.np32(qknorm_b200(x, gain)).astype(np.float64) ** 2).mean(-1))
+    np.testing.assert_allclose(rms, np.broadcast_to(H.np32(gain), rms.shape), rtol=1e-2)
+
+
+@pytest.mark.parametrize("dh,Bk,m", [(64, 64, 4), (128, 64, 4), (64, 32, 2), (128, 16, 8)])
+def test_summaries_and_supers_match_oracle(dh, Bk, m):
+    cfg = H.cfg_of(head_dim=dh, block=Bk, slots=m, n_heads=4, n_kv=2, fanout=4)
+    g = torch.Generator(device="cuda").manual_seed(2)
+    kc = torch.randn(2, 11 * Bk, 2, dh, generator=g, device="cuda").to(torch.bfloat16)
+    summ, _ = synth.make_weights(cfg, "cuda", seed=3)
+    S = summarize_b200(kc, summ.probes, summ.proj, cfg)
+    ref = orc.summarize(H.np32(kc), H.np32(summ.probes), H.np32(summ.proj), Bk)
+    err = np.abs(H.np32(S) - ref)
+    assert (err <= np.abs(ref) * 2.0 ** -7 + 2e-3).all(), err.max()
+    S1, ns = build_super_b200(S, cfg)
+    assert ns == 3                                     # 11 blocks, fanout 4: partial last group
+    ref1, _ = orc.build_super(H.np32(S), 4)
+    err1 = np.abs(H.np32(S1) - ref1)
+    assert (err1 <= np.abs(ref1) * 2.0 ** -7 + 1e-6).all(), err1.max()
+
+
+# ---------------------------------------------------------------- decode ----
+@pytest.mark.parametrize("hier", [False, True])
+def test_decode_small_matches_oracle(hier):
+    cfg = H.cfg_of(n_heads=8, n_kv=2, head_dim=128, fanout=8, beam=3) if hier else H.cfg_of()
+    cache, wl, summ, qkn, cos, sin = H.build_cache(cfg, 3, 4096, hier, seed=11)
+    H.check_decode(cache, wl["q"], cfg, hier, qkn, cos, sin)
+
+
+def test_decode_planted_blocks_are_selected():
+    cfg = H.cfg_of()
+    cache, wl, summ, qkn, cos, sin = H.build_cache(cfg, 4, 8192, False, seed=12, gains=False)
+    _, _, (si, _) = H.check_decode(cache, wl["q"], cfg, False, qkn, cos, sin)
+    sel = si.cpu().numpy()
+    pl = wl["planted"].cpu().numpy()
+    for b in range(4):
+        for g in range(2):
+            assert set(pl[b, g].tolist()) <= set(sel[b, g].tolist())
+
+
+def test_decode_ragged_lengths_and_edges():
+    """Ragged batch: a sequence shorter than the window (no candidates), one
+    with fewer candidates than k, one shorter than the sink count, a full one."""
+    cfg = H.cfg_of()
+    cache, wl, summ, qkn, cos, sin = H.build_cache(cfg, 5, 4096, False, seed=13)
+    lens = np.array([4096, 300, 1024 + 64 * 5 + 7, 2, 1], dtype=np.int64)
+    cache.lens.copy_(torch.tensor(lens, dtype=torch.int32))
+    cache.lens_host = lens.copy()
+    cache._refresh_scales()
+    H.check_decode(cache, wl["q"], cfg, False, qkn, cos, sin)
+
+
+@pytest.mark.parametrize("variant", ["noqk", "inv_sqrt_d", "tau"])
+def test_decode_scale_variants(variant):
+    if variant == "noqk":
+        cfg = H.cfg_of(qknorm=False)
+    elif variant == "inv_sqrt_d":
+        cfg = H.cfg_of(content_scale_mode="inv_sqrt_d")
+    else:
+        cfg = H.cfg_of(native_ctx=1024, n_heads=8, n_kv=2, head_dim=128)      # tau(4096) = 1 + 0.1 ln 4
+    cache, wl, summ, qkn, cos, sin = H.build_cache(cfg, 2, 4096, False, seed=14)
+    H.check_decode(cache, wl["q"], cfg, False, qkn, cos, sin)
+
+
+def test_cache_incremental_append_matches_bulk():
+    cfg = H.cfg_of(n_heads=8, n_kv=2, head_dim=128, fanout=4, beam=2)
+    n = 640
+    summ, qkn = synth.make_weights(cfg, "cuda", seed=5, gains=True)
+    cos, sin = synth.rope_tables(n, 128, 1e6)
+    wl = synth.decode_workload(cfg, 2, n, hier=True, seed=5, qkn=qkn)
+    bulk = HBADecodeCache(cfg, 2, n, summ, qkn, cos, sin, hier=True)
+    bulk.append(wl["k"], wl["v"])
+    inc = HBADecodeCache(cfg, 2, n, summ, qkn, cos, sin, hier=True)
+    for t0 in range(0, n, 37):
+        t1 = min(n, t0 + 37)
+        inc.append(wl["k"][:, t0:t1], wl["v"][:, t0:t1])
+    torch.cuda.synchronize()
+    for name in ("k", "v", "summaries", "supers"):
+        assert torch.equal(getattr(bulk, name), getattr(inc, name)), name
+    a = bulk.attend(wl["q"])
+    b = inc.attend(wl["q"])
+    assert torch.equal(a, b)
+
+
+# --------------------------------------------------------------- prefill ----
+@pytest.mark.parametrize("hier", [False, True])
+def test_prefill_cfg0_shape_matches_oracle(hier):
+    cfg = H.cfg_of(fanout=8, beam=4) if hier else H.cfg_of()
+    rows = H.sample_rows(2048, 48, seed=1)
+    H.check_prefill(cfg, 1, 2048, hier, seed=21, rows=rows)
+
+
+def test_prefill_dh128_gqa4_matches_oracle():
+    cfg = H.cfg_of(n_heads=32, n_kv=8, head_dim=128)
+    rows = H.sample_rows(2048, 24, seed=2)
+    H.check_prefill(cfg, 2, 2048, False, seed=22, rows=rows)
+
+
+def test_prefill_short_sequence_no_candidates():
+    cfg = H.cfg_of()
+    H.check_prefill(cfg, 1, 512, False, seed=23, rows=np.arange(512))
+
+
+def test_prefill_tiny_blocks_and_knobs():
+    """Block 16, window 64, 2 sinks, k 4, 2 slots (the reference's test knobs)."""
+    cfg = H.cfg_of(block=16, window=64, sinks=2, k_blocks=4, slots=2, fanout=4, beam=2, n_heads=4, n_kv=2)
+    for hier in (False, True):
+        H.check_prefill(cfg, 2, 384, hier, seed=24, rows=np.arange(384))
+
+
+def test_prefill_rejects_non_block_multiple():
+    cfg = H.cfg_of()
+    summ, qkn = synth.make_weights(cfg, "cuda")
+    q = torch.zeros(1, 100, 14, 64, device="cuda", dtype=torch.bfloat16)
+    k = torch.zeros(1, 100, 2, 64, device="cuda", dtype=torch.bfloat16)
+    cos, sin = synth.rope_tables(100, 64, 1e6)
+    with pytest.raises(AssertionError):
+        hba_attention_b200(q, k, k, cos, sin, cfg, summ, qkn)
+
+
+def test_prefill_causality():
+    """Outputs at positions <= t must not change when tokens > t change
+    (reference gate_causality, gates.py:101-126), flat selection."""
+    cfg = H.cfg_of()
+    n, t = 2048, 1500
+    summ, qkn = synth.make_weights(cfg, "cuda", seed=7, gains=True)
+    cos, sin = synth.rope_tables(n, 64, 1e6)
+    wl = synth.prefill_workload(cfg, 1, n, seed=7)
+    q, k, v = wl["q"], wl["k"], wl["v"]
+    g = torch.Generator(device="cuda").manual_seed(8)
+    q2, k2, v2 = q.clone(), k.clone(), v.clone()
+    q2[:, t + 1:] = torch.randn(q2[:, t + 1:].shape, generator=g, device="cuda").to(q.dtype)
+    k2[:, t + 1:] = torch.randn(k2[:, t + 1:].shape, generator=g, device="cuda").to(k.dtype)
+    v2[:, t + 1:] = torch.randn(v2[:, t + 1:].shape, generator=g, device="cuda").to(v.dtype)
+    with torch.no_grad():
+        o1 = hba_attention_b200(q, k, v, cos, sin, cfg, summ, qkn)
+        o2 = hba_attention_b200(q2, k2, v2, cos, sin, cfg, summ, qkn)
+    assert torch.equal(o1[:, :t + 1], o2[:, :t + 1])
+    assert not torch.equal(o1[:, t + 1:], o2[:, t + 1:])
+
+
+def test_decode_equals_prefill_last_row():
+    cfg = H.cfg_of(n_heads=8, n_kv=2, head_dim=128)
+    n = 3072
+    summ, qkn = synth.make_weights(cfg, "cuda", seed=9, gains=True)
+    cos, sin = synth.rope_tables(n, 128, 1e6)
+    wl = synth.prefill_workload(cfg, 2, n, seed=9)
+    with torch.no_grad():
+        out, lse, (si, ss) = hba_attention_b200(wl["q"], wl["k"], wl["v"], cos, sin, cfg, summ, qkn,
+                                                return_lse=True, return_selection=True)
+    cache = HBADecodeCache(cfg, 2, n, summ, qkn, cos, sin)
+    cache.append(wl["k"], wl["v"])
+    o2, l2, (si2, ss2) = cache.attend(wl["q"][:, -1], return_lse=True, return_selection=True)
+    assert torch.equal(si[:, :, -1], si2)
+    assert (out[:, -1].float() - o2.float()).abs().max().item() < 1e-2
+    assert (lse[:, :, -1] - l2).abs().max().item() < 1e-4
+
+
+# ------------------------------------------------- BASELINE full sizes ------
+def test_baseline_cfg1_decode_full_size():
+    """B64 x 32K context, 14/2 heads, dh 64, flat top-16: every sequence's 8
+    planted blocks selected; 16 sampled sequences checked against the oracle."""
+    cfg = H.cfg_of()
+    cache, wl, summ, qkn, cos, sin = H.build_cache(cfg, 64, 32768, False, seed=31, gains=False)
+    out, (si, _) = cache.attend(wl["q"], return_selection=True)
+    assert torch.isfinite(out.float()).all()
+    sel = si.cpu().numpy()
+    pl = wl["planted"].cpu().numpy()
+    assert all(set(pl[b, g]) <= set(sel[b, g]) for b in range(64) for g in range(2))
+    H.check_decode(cache, wl["q"], cfg, False, qkn, cos, sin, rows=range(0, 64, 4))
+
+
+def test_baseline_cfg3_hier_decode_full_size():
+    """B32 x 128K context, 32/8 heads, dh 128, beam 8 over 128 supers, tau active."""
+    cfg = H.cfg_of(n_heads=32, n_kv=8, head_dim=128, fanout=16, beam=8)
+    cache, wl, summ, qkn, cos, sin = H.build_cache(cfg, 32, 131072, True, seed=33, gains=False)
+    out, (si, _) = cache.attend(wl["q"], return_selection=True)
+    assert torch.isfinite(out.float()).all()
+    sel = si.cpu().numpy()
+    pl = wl["planted"].cpu().numpy()
+    assert all(set(pl[b, g]) <= set(sel[b, g]) for b in range(32) for g in range(8))
+    H.check_decode(cache, wl["q"], cfg, True, qkn, cos, sin, rows=[0, 13, 31])
+
+
+def test_baseline_cfg2_prefill_full_size_sampled_rows():
+    """B4 x 32K, 32/8 heads, dh 128: 24 sampled query rows per sequence against
+    the oracle; all outputs finite."""
+    cfg = H.cfg_of(n_heads=32, n_kv=8, head_dim=128)
+    rows = H.sample_rows(32768, 16, seed=3)
+    eo, el, out, lse, _ = H.check_prefill(cfg, 4, 32768, False, seed=32, rows=rows, gains=False)
+    assert torch.isfinite(out.float()).all() and torch.isfinite(lse).all()
