@@ -135,6 +135,25 @@ int hba_b200_decode(const hba_b200_config* cfg, int32_t batch, int32_t n_cap, co
                     const float* sin, void* out, float* lse, int32_t* sel_idx, float* sel_score,
                     void* workspace, size_t workspace_bytes, cudaStream_t stream);
 
+/*
+ * hba_b200_decode without a workspace argument, for callers that cannot
+ * allocate device memory when they decode (an engine whose arena owns all of
+ * HBM, a plugin host without an allocator, code where cudaMalloc is not
+ * allowed).  It allocates nothing: its scratch is a fixed 8 MiB __device__
+ * array inside the library, held on every GPU that loads the library until
+ * the process exits.  Requests whose hba_b200_decode_workspace_size exceeds
+ * 8 MiB return HBA_B200_ERR_WORKSPACE (use hba_b200_decode instead).  The
+ * array's device address is looked up on the first call made on each device,
+ * so make that call before any stream capture.  All calls on a device share
+ * the array: calls whose kernels may overlap on the GPU race on it.
+ * No counterpart in the reference.
+ */
+int hba_b200_decode_noalloc(const hba_b200_config* cfg, int32_t batch, int32_t n_cap, const int32_t* seq_lens,
+                            const float* scales, const void* q, const float* q_gain, const void* k_cache,
+                            const void* v_cache, const void* summaries, const void* supers, const float* cos,
+                            const float* sin, void* out, float* lse, int32_t* sel_idx, float* sel_score,
+                            cudaStream_t stream);
+
 /* Bytes of scratch needed by hba_b200_prefill (0 when rejected). */
 size_t hba_b200_prefill_workspace_size(const hba_b200_config* cfg, int32_t batch, int32_t n);
 
