@@ -218,9 +218,9 @@ def decode_bench(name, steps, warmup, world, rank, local, pk):
     t_ms = max_over_ranks(t_ms, world, dev)
 
     # dominant kernel (attend) timed live between the library's event marks
-    nmarks = 5 if hier else 4
+    nmarks = 4 if hier else 3          # begin | select (super, child) | attend
     kt = kernel_times(step_direct, max(3, min(steps, 10)), flush, nmarks)
-    attend_ms = kt[-2]
+    attend_ms = kt[-1]
     keys = cfg.sinks + cfg.window + cfg.k_blocks * cfg.block
     attend_bytes = B * Hkv * (keys * dh * 2 * 2 + G * dh * 2 * 2)
     if hier:
@@ -264,7 +264,7 @@ def decode_bench(name, steps, warmup, world, rank, local, pk):
                       algorithmic_bytes_per_launch=attend_bytes, kernel_ms=attend_ms),
         step_effective_gbs=step_bytes / (t_ms * 1e-3) / 1e9,
         step_algorithmic_bytes=step_bytes,
-        kernel_ms={"select": kt[:-2], "attend": attend_ms, "merge": kt[-1]},
+        kernel_ms={"select": kt[:-1], "attend": attend_ms},
         cache_build_s=build_s,
         e2e=dict(value=B * world / (e2e_ms * 1e-3), unit="decode queries/s", ms_per_step=e2e_ms,
                  h2d_bytes_per_step=q.numel() * q.element_size(),

@@ -2,6 +2,8 @@
 // kernel orchestration.  No entry point allocates device memory.
 #include <cmath>
 #include <cstdio>
+#include <cstdlib>
+#include <cstring>
 
 #include "hba_b200.h"
 #include "hba_internal.h"
@@ -94,8 +96,11 @@ struct Plan {
   int sel_splits;    // flat lists, or super lists (hier)
   int sel_list_k;    // K, or beam (hier)
   int child_splits;  // hier only
-  int attn_splits;
+  int attn_splits;   // prefill: key-range splits per query (1)
+  int ncw, ncr, nchunk, max_seg;  // decode attention chunk slots and partial segments
 };
+
+constexpr int kMinChunksPerCta = 4;
 
 int ceil_div(long long a, long long b) { return (int)((a + b - 1) / b); }
 
@@ -116,13 +121,15 @@ Plan make_plan(const hba_b200_config* c, int nb_cap, int bh, bool decode) {
     p.sel_list_k = c->k_blocks;
     p.child_splits = 0;
   }
-  if (decode) {
-    const int max_chunks = ceil_div((long long)c->k_blocks * c->block, 64) + ceil_div(c->window, 64) + 1;
-    p.attn_splits = std::max(1, std::min(16, ceil_div(max_chunks, 4)));
-  } else {
-    p.attn_splits = 1;
-  }
+  p.attn_splits = 1;
+  p.ncw = ceil_div(c->window, 64);
+  p.ncr = ceil_div((long long)c->k_blocks * c->block, 64);
+  p.nchunk = p.ncw + 1 + p.ncr;
+  // decode attention: every CTA owns >= kMinChunksPerCta chunk slots, so a
+  // (sequence, kv head) is split into at most nchunk / kMinChunksPerCta + 2 segments
+  p.max_seg = p.nchunk / kMinChunksPerCta + 2;
   (void)bh;
+  (void)decode;
   return p;
 }
 
@@ -149,13 +156,14 @@ size_t selection_bytes(const hba_b200_config* c, const Plan& p, size_t queries) 
   return b;
 }
 
-// Runs selection (flat, or super then child) and attention for nq queries per
-// sequence.  Returns an hba_b200_status.
-int run_select_attend(const hba_b200_config* c, const Geom& geo, const hba::QueryPos& qp, const Plan& plan,
-                      const __nv_bfloat16* q, const float* q_gain, const __nv_bfloat16* kc,
-                      const __nv_bfloat16* v, const __nv_bfloat16* summ, const __nv_bfloat16* supers,
-                      const float* cos, const float* sin, __nv_bfloat16* out, float* lse, int32_t* sel_idx,
-                      float* sel_score, unsigned char* ws, cudaStream_t st) {
+// Runs selection (flat, or super then child) for nq queries per sequence and
+// returns the final lists through `fin`.  `counters` (decode) are zeroed by
+// the last selection kernel; with `pdl` the child kernel is launched as a
+// programmatic dependent of the super kernel.
+int run_select(const hba_b200_config* c, const Geom& geo, const hba::QueryPos& qp, const Plan& plan,
+               const __nv_bfloat16* q, const float* q_gain, const __nv_bfloat16* summ,
+               const __nv_bfloat16* supers, unsigned char*& ws, int32_t* counters, Lists& fin, int& fin_lists,
+               int& fin_k, cudaStream_t st) {
   const int dh = c->head_dim;
   const size_t queries = (size_t)geo.B * geo.Hkv * geo.nq;
   Lists l1 = carve_lists(ws, queries * plan.sel_splits * plan.sel_list_k);
@@ -171,11 +179,14 @@ int run_select_attend(const hba_b200_config* c, const Geom& geo, const hba::Quer
   sp.list_k = plan.sel_list_k;
   sp.out_score = l1.score;
   sp.out_idx = l1.idx;
+  sp.counters = c->hier ? nullptr : counters;
+  sp.pdl = 0;
   cudaError_t e = hba::launch_select(sp, dh, st);
   if (e != cudaSuccess) return cuda_status(e);
   prof_mark(st);
-  Lists fin = l1;
-  int fin_lists = plan.sel_splits, fin_k = plan.sel_list_k;
+  fin = l1;
+  fin_lists = plan.sel_splits;
+  fin_k = plan.sel_list_k;
   if (c->hier) {
     Lists l2 = carve_lists(ws, queries * plan.child_splits * c->k_blocks);
     sp.mode = hba::kSelChild;
@@ -186,6 +197,8 @@ int run_select_attend(const hba_b200_config* c, const Geom& geo, const hba::Quer
     sp.list_k = c->k_blocks;
     sp.out_score = l2.score;
     sp.out_idx = l2.idx;
+    sp.counters = counters;
+    sp.pdl = 1;
     e = hba::launch_select(sp, dh, st);
     if (e != cudaSuccess) return cuda_status(e);
     prof_mark(st);
@@ -193,49 +206,31 @@ int run_select_attend(const hba_b200_config* c, const Geom& geo, const hba::Quer
     fin_lists = plan.child_splits;
     fin_k = c->k_blocks;
   }
-  hba::AttnParams ap{};
-  ap.geo = geo;
-  ap.qp = qp;
-  ap.splits = plan.attn_splits;
-  ap.in_lists = fin_lists;
-  ap.list_k = fin_k;
-  ap.q = q;
-  ap.q_gain = q_gain;
-  ap.k = kc;
-  ap.v = v;
-  ap.cos = cos;
-  ap.sin = sin;
-  ap.in_score = fin.score;
-  ap.in_idx = fin.idx;
-  ap.out = out;
-  ap.lse = lse;
-  ap.sel_idx = sel_idx;
-  ap.sel_score = sel_score;
-  if (plan.attn_splits > 1) ap.part = reinterpret_cast<float*>(ws);
-  e = hba::launch_attend(ap, dh, st);
-  if (e != cudaSuccess) return cuda_status(e);
-  prof_mark(st);
-  if (plan.attn_splits > 1) {
-    hba::MergeParams mp{};
-    mp.B = geo.B;
-    mp.Hq = geo.Hq;
-    mp.Hkv = geo.Hkv;
-    mp.G = geo.G;
-    mp.nq = geo.nq;
-    mp.splits = plan.attn_splits;
-    mp.part = ap.part;
-    mp.out = out;
-    mp.lse = lse;
-    e = hba::launch_merge(mp, dh, st);
-    if (e != cudaSuccess) return cuda_status(e);
-    prof_mark(st);
-  }
   return HBA_B200_OK;
 }
 
-size_t partial_bytes(const hba_b200_config* c, const Plan& p, size_t queries) {
-  if (p.attn_splits <= 1) return 0;
-  return align_up(queries * p.attn_splits * 16 * (size_t)(c->head_dim + 2) * sizeof(float));
+// Decode path choice.  Fused (one CTA per sequence and kv head, selection and
+// attention in one kernel, no scratch) when there are enough (sequence, kv
+// head) pairs to fill the GPU and the candidate lists fit its shared-memory
+// top-k; otherwise the split path (selection kernels, then the stream-K
+// attention kernel with partial merges).  HBA_B200_DECODE_PATH=fused|split
+// forces one (tests use it to cover both).
+constexpr long long kFusedMinPairs = 96;
+constexpr int kFusedMaxItems = 2048;  // must match kTopkMaxItems (hba_topk.cuh)
+
+bool use_fused_decode(const hba_b200_config* c, const Geom& geo, size_t bh) {
+  const char* force = getenv("HBA_B200_DECODE_PATH");
+  bool fits = geo.nb_cap <= kFusedMaxItems;
+  if (c->hier) fits = fits && geo.ns_cap <= kFusedMaxItems && (long long)c->beam * c->fanout <= kFusedMaxItems;
+  if (force != nullptr && strcmp(force, "split") == 0) return false;
+  if (force != nullptr && strcmp(force, "fused") == 0) return fits;
+  return fits && (long long)bh >= kFusedMinPairs;
+}
+
+// decode split path: per-(sequence, kv head) softmax partials and merge counters
+size_t decode_state_bytes(const hba_b200_config* c, const Plan& p, size_t bh) {
+  const size_t G = (size_t)(c->n_heads / c->n_kv);
+  return align_up(bh * p.max_seg * G * (size_t)(c->head_dim + 2) * sizeof(float)) + align_up(bh * sizeof(int32_t));
 }
 
 }  // namespace
@@ -307,21 +302,22 @@ int hba_b200_build_supers(const hba_b200_config* cfg, int32_t batch, int32_t nb_
 }
 
 int hba_b200_append_kv(const hba_b200_config* cfg, int32_t batch, int32_t n_cap, int32_t t, const int32_t* pos,
-                       const void* k_new, const void* v_new, const float* k_gain, const float* probes,
-                       const float* proj, void* k_cache, void* v_cache, void* summaries, void* supers,
-                       cudaStream_t stream) {
+                       const void* k_new, const void* v_new, const float* k_gain, const float* cos, const float* sin,
+                       const float* probes, const float* proj, void* k_cache, void* k_rope_cache, void* v_cache,
+                       void* summaries, void* supers, cudaStream_t stream) {
   int st = HBA_B200_OK;
   if (!config_ok(cfg, &st)) return st;
   if (batch <= 0 || n_cap <= 0 || t <= 0 || pos == nullptr || k_new == nullptr || v_new == nullptr ||
-      k_cache == nullptr || v_cache == nullptr || (cfg->qknorm && k_gain == nullptr))
+      k_cache == nullptr || k_rope_cache == nullptr || v_cache == nullptr || cos == nullptr || sin == nullptr ||
+      (cfg->qknorm && k_gain == nullptr))
     return HBA_B200_ERR_INVALID_ARGUMENT;
   if (summaries != nullptr && (probes == nullptr || proj == nullptr)) return HBA_B200_ERR_INVALID_ARGUMENT;
   Geom geo = make_geom(cfg, batch, 1, n_cap);
   const int dh = cfg->head_dim;
   cudaError_t e = hba::launch_append(geo, t, pos, static_cast<const __nv_bfloat16*>(k_new),
-                                     static_cast<const __nv_bfloat16*>(v_new), k_gain,
-                                     static_cast<__nv_bfloat16*>(k_cache), static_cast<__nv_bfloat16*>(v_cache), dh,
-                                     stream);
+                                     static_cast<const __nv_bfloat16*>(v_new), k_gain, cos, sin,
+                                     static_cast<__nv_bfloat16*>(k_cache), static_cast<__nv_bfloat16*>(k_rope_cache),
+                                     static_cast<__nv_bfloat16*>(v_cache), dh, stream);
   if (e != cudaSuccess) return cuda_status(e);
   if (summaries != nullptr) {
     e = hba::launch_summarize(geo, dh, static_cast<const __nv_bfloat16*>(k_cache), probes, proj,
@@ -340,34 +336,94 @@ size_t hba_b200_decode_workspace_size(const hba_b200_config* cfg, int32_t batch,
   int st = HBA_B200_OK;
   if (!config_ok(cfg, &st) || batch <= 0 || n_cap <= 0 || n_cap % cfg->block != 0) return 0;
   const Plan plan = make_plan(cfg, n_cap / cfg->block, batch * cfg->n_kv, true);
-  const size_t queries = (size_t)batch * cfg->n_kv;
-  return selection_bytes(cfg, plan, queries) + partial_bytes(cfg, plan, queries);
+  const size_t bh = (size_t)batch * cfg->n_kv;
+  return selection_bytes(cfg, plan, bh) + decode_state_bytes(cfg, plan, bh);
 }
 
 int hba_b200_decode(const hba_b200_config* cfg, int32_t batch, int32_t n_cap, const int32_t* seq_lens,
                     const float* scales, const void* q, const float* q_gain, const void* k_cache,
-                    const void* v_cache, const void* summaries, const void* supers, const float* cos,
-                    const float* sin, void* out, float* lse, int32_t* sel_idx, float* sel_score, void* workspace,
-                    size_t workspace_bytes, cudaStream_t stream) {
+                    const void* k_rope_cache, const void* v_cache, const void* summaries, const void* supers,
+                    const float* cos, const float* sin, void* out, float* lse, int32_t* sel_idx, float* sel_score,
+                    void* workspace, size_t workspace_bytes, cudaStream_t stream) {
   int st = HBA_B200_OK;
   if (!config_ok(cfg, &st)) return st;
   if (batch <= 0 || n_cap <= 0 || seq_lens == nullptr || scales == nullptr || q == nullptr || k_cache == nullptr ||
-      v_cache == nullptr || summaries == nullptr || cos == nullptr || sin == nullptr || out == nullptr ||
-      (cfg->qknorm && q_gain == nullptr) || (cfg->hier && supers == nullptr) ||
+      k_rope_cache == nullptr || v_cache == nullptr || summaries == nullptr || cos == nullptr || sin == nullptr ||
+      out == nullptr || (cfg->qknorm && q_gain == nullptr) || (cfg->hier && supers == nullptr) ||
       ((sel_idx == nullptr) != (sel_score == nullptr)))
     return HBA_B200_ERR_INVALID_ARGUMENT;
   if (n_cap % cfg->block != 0) return HBA_B200_ERR_NOT_BLOCK_MULTIPLE;
-  Geom geo = make_geom(cfg, batch, 1, n_cap);
-  const Plan plan = make_plan(cfg, geo.nb_cap, batch * cfg->n_kv, true);
   const size_t need = hba_b200_decode_workspace_size(cfg, batch, n_cap);
   if (workspace == nullptr || workspace_bytes < need) return HBA_B200_ERR_WORKSPACE;
+  Geom geo = make_geom(cfg, batch, 1, n_cap);
+  const Plan plan = make_plan(cfg, geo.nb_cap, batch * cfg->n_kv, true);
+  const size_t bh = (size_t)batch * cfg->n_kv;
+  const int G = cfg->n_heads / cfg->n_kv;
+  unsigned char* ws = static_cast<unsigned char*>(workspace);
+  // decode state first: partials, then counters
+  float* part = reinterpret_cast<float*>(ws);
+  ws += align_up(bh * plan.max_seg * G * (size_t)(cfg->head_dim + 2) * sizeof(float));
+  int32_t* counters = reinterpret_cast<int32_t*>(ws);
+  ws += align_up(bh * sizeof(int32_t));
   hba::QueryPos qp{seq_lens, scales, 0, 0.f};
   prof_begin(stream);
-  return run_select_attend(cfg, geo, qp, plan, static_cast<const __nv_bfloat16*>(q), q_gain,
-                           static_cast<const __nv_bfloat16*>(k_cache), static_cast<const __nv_bfloat16*>(v_cache),
-                           static_cast<const __nv_bfloat16*>(summaries), static_cast<const __nv_bfloat16*>(supers),
-                           cos, sin, static_cast<__nv_bfloat16*>(out), lse, sel_idx, sel_score,
-                           static_cast<unsigned char*>(workspace), stream);
+  if (use_fused_decode(cfg, geo, bh)) {
+    hba::DecodeAttnParams dp{};
+    dp.geo = geo;
+    dp.qp = qp;
+    dp.q = static_cast<const __nv_bfloat16*>(q);
+    dp.q_gain = q_gain;
+    dp.k = static_cast<const __nv_bfloat16*>(k_cache);
+    dp.kr = static_cast<const __nv_bfloat16*>(k_rope_cache);
+    dp.v = static_cast<const __nv_bfloat16*>(v_cache);
+    dp.cos = cos;
+    dp.sin = sin;
+    dp.out = static_cast<__nv_bfloat16*>(out);
+    dp.lse = lse;
+    dp.sel_idx = sel_idx;
+    dp.sel_score = sel_score;
+    cudaError_t e = hba::launch_decode_fused(dp, static_cast<const __nv_bfloat16*>(summaries),
+                                             static_cast<const __nv_bfloat16*>(supers), cfg->head_dim, stream);
+    if (e != cudaSuccess) return cuda_status(e);
+    prof_mark(stream);
+    return HBA_B200_OK;
+  }
+  Lists fin{};
+  int fin_lists = 0, fin_k = 0;
+  st = run_select(cfg, geo, qp, plan, static_cast<const __nv_bfloat16*>(q), q_gain,
+                  static_cast<const __nv_bfloat16*>(summaries), static_cast<const __nv_bfloat16*>(supers), ws,
+                  counters, fin, fin_lists, fin_k, stream);
+  if (st != HBA_B200_OK) return st;
+  hba::DecodeAttnParams dp{};
+  dp.geo = geo;
+  dp.qp = qp;
+  dp.ncw = plan.ncw;
+  dp.ncr = plan.ncr;
+  dp.nchunk = plan.nchunk;
+  dp.in_lists = fin_lists;
+  dp.list_k = fin_k;
+  dp.max_seg = plan.max_seg;
+  dp.q = static_cast<const __nv_bfloat16*>(q);
+  dp.q_gain = q_gain;
+  dp.k = static_cast<const __nv_bfloat16*>(k_cache);
+  dp.kr = static_cast<const __nv_bfloat16*>(k_rope_cache);
+  dp.v = static_cast<const __nv_bfloat16*>(v_cache);
+  dp.cos = cos;
+  dp.sin = sin;
+  dp.in_score = fin.score;
+  dp.in_idx = fin.idx;
+  dp.out = static_cast<__nv_bfloat16*>(out);
+  dp.lse = lse;
+  dp.sel_idx = sel_idx;
+  dp.sel_score = sel_score;
+  dp.part = part;
+  dp.counters = counters;
+  const long long total = (long long)bh * plan.nchunk;
+  int grid = hba::decode_attend_grid(cfg->head_dim, (int)std::max<long long>(1, total / kMinChunksPerCta));
+  cudaError_t e = hba::launch_decode_attend(dp, cfg->head_dim, grid, stream);
+  if (e != cudaSuccess) return cuda_status(e);
+  prof_mark(stream);
+  return HBA_B200_OK;
 }
 
 size_t hba_b200_prefill_workspace_size(const hba_b200_config* cfg, int32_t batch, int32_t n) {
@@ -378,10 +434,11 @@ size_t hba_b200_prefill_workspace_size(const hba_b200_config* cfg, int32_t batch
   const size_t ns = cfg->hier ? (nb + cfg->fanout - 1) / cfg->fanout : 0;
   const Plan plan = make_plan(cfg, (int)nb, batch * cfg->n_kv, false);
   const size_t queries = (size_t)batch * cfg->n_kv * n;
-  size_t b = align_up((size_t)batch * n * cfg->n_kv * dh * 2);            // QKNorm'd keys
+  size_t b = kAlign;                                                      // device status word
+  b += 2 * align_up((size_t)batch * n * cfg->n_kv * dh * 2);              // QKNorm'd keys and their RoPE'd copy
   b += align_up((size_t)batch * cfg->n_kv * nb * cfg->slots * dh * 2);    // summaries
   b += align_up((size_t)batch * cfg->n_kv * ns * cfg->slots * dh * 2);    // supers
-  b += selection_bytes(cfg, plan, queries) + partial_bytes(cfg, plan, queries);
+  b += selection_bytes(cfg, plan, queries);
   return b;
 }
 
@@ -403,7 +460,11 @@ int hba_b200_prefill(const hba_b200_config* cfg, int32_t batch, int32_t n, float
   const size_t nb = (size_t)n / cfg->block;
   const size_t ns = cfg->hier ? (nb + cfg->fanout - 1) / cfg->fanout : 0;
   unsigned char* ws = static_cast<unsigned char*>(workspace);
+  int* dev_status = reinterpret_cast<int*>(ws);
+  ws += kAlign;
   __nv_bfloat16* kc = reinterpret_cast<__nv_bfloat16*>(ws);
+  ws += align_up((size_t)batch * n * cfg->n_kv * dh * 2);
+  __nv_bfloat16* kr = reinterpret_cast<__nv_bfloat16*>(ws);
   ws += align_up((size_t)batch * n * cfg->n_kv * dh * 2);
   __nv_bfloat16* summ = reinterpret_cast<__nv_bfloat16*>(ws);
   ws += align_up((size_t)batch * cfg->n_kv * nb * cfg->slots * dh * 2);
@@ -411,15 +472,12 @@ int hba_b200_prefill(const hba_b200_config* cfg, int32_t batch, int32_t n, float
   ws += align_up((size_t)batch * cfg->n_kv * ns * cfg->slots * dh * 2);
 
   Geom geo = make_geom(cfg, batch, n, n);
-  cudaError_t e;
   prof_begin(stream);
-  if (cfg->qknorm) {
-    e = hba::launch_qknorm(static_cast<const __nv_bfloat16*>(k), kc, k_gain, (int64_t)batch * n, cfg->n_kv, dh,
-                           cfg->eps, stream);
-    if (e != cudaSuccess) return cuda_status(e);
-  } else {
-    kc = const_cast<__nv_bfloat16*>(static_cast<const __nv_bfloat16*>(k));  // keys are used as given
-  }
+  cudaError_t e = cudaMemsetAsync(dev_status, 0, sizeof(int), stream);
+  if (e != cudaSuccess) return cuda_status(e);
+  e = hba::launch_qknorm_rope(geo, n, static_cast<const __nv_bfloat16*>(k), k_gain, cos, sin, kc, kr, dh,
+                                          stream);
+  if (e != cudaSuccess) return cuda_status(e);
   prof_mark(stream);
   e = hba::launch_summarize(geo, dh, kc, probes, proj, summ, 0, (int)nb, nullptr, 0, stream);
   if (e != cudaSuccess) return cuda_status(e);
@@ -431,9 +489,51 @@ int hba_b200_prefill(const hba_b200_config* cfg, int32_t batch, int32_t n, float
   }
   const Plan plan = make_plan(cfg, (int)nb, batch * cfg->n_kv, false);
   hba::QueryPos qp{nullptr, nullptr, n, scale};
-  return run_select_attend(cfg, geo, qp, plan, static_cast<const __nv_bfloat16*>(q), q_gain, kc,
-                           static_cast<const __nv_bfloat16*>(v), summ, sup, cos, sin, static_cast<__nv_bfloat16*>(out),
-                           lse, sel_idx, sel_score, ws, stream);
+  Lists fin{};
+  int fin_lists = 0, fin_k = 0;
+  st = run_select(cfg, geo, qp, plan, static_cast<const __nv_bfloat16*>(q), q_gain, summ, sup, ws, nullptr, fin,
+                  fin_lists, fin_k, stream);
+  if (st != HBA_B200_OK) return st;
+  // tensor-core union path: opt-in (HBA_B200_PREFILL_PATH=tc) until validated on hardware
+  const char* force = getenv("HBA_B200_PREFILL_PATH");
+  const bool want_tc = force != nullptr && strcmp(force, "tc") == 0;
+  if (want_tc && fin_lists == 1 && hba::prefill_tc_supported(geo, dh, n, cfg->qknorm != 0)) {
+    e = hba::launch_prefill_tc(geo, dh, n, scale, static_cast<const __nv_bfloat16*>(q), q_gain, k_gain, kc, kr,
+                               static_cast<const __nv_bfloat16*>(v), cos, sin, fin.idx, fin_lists * fin_k,
+                               static_cast<__nv_bfloat16*>(out), lse, dev_status, stream);
+    if (e != cudaSuccess) return cuda_status(e);
+    prof_mark(stream);
+    if (sel_idx != nullptr) {  // the single-split lists are the final picks, layout [B, Hkv, n, K]
+      const size_t bytes = (size_t)batch * cfg->n_kv * n * cfg->k_blocks * sizeof(int32_t);
+      e = cudaMemcpyAsync(sel_idx, fin.idx, bytes, cudaMemcpyDeviceToDevice, stream);
+      if (e == cudaSuccess) e = cudaMemcpyAsync(sel_score, fin.score, bytes, cudaMemcpyDeviceToDevice, stream);
+      if (e != cudaSuccess) return cuda_status(e);
+    }
+    return HBA_B200_OK;
+  }
+  hba::AttnParams ap{};
+  ap.geo = geo;
+  ap.qp = qp;
+  ap.splits = 1;
+  ap.in_lists = fin_lists;
+  ap.list_k = fin_k;
+  ap.q = static_cast<const __nv_bfloat16*>(q);
+  ap.q_gain = q_gain;
+  ap.k = kc;
+  ap.kr = kr;
+  ap.v = static_cast<const __nv_bfloat16*>(v);
+  ap.cos = cos;
+  ap.sin = sin;
+  ap.in_score = fin.score;
+  ap.in_idx = fin.idx;
+  ap.out = static_cast<__nv_bfloat16*>(out);
+  ap.lse = lse;
+  ap.sel_idx = sel_idx;
+  ap.sel_score = sel_score;
+  e = hba::launch_attend(ap, dh, stream);
+  if (e != cudaSuccess) return cuda_status(e);
+  prof_mark(stream);
+  return HBA_B200_OK;
 }
 
 }  // extern "C"

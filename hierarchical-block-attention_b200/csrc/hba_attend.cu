@@ -5,14 +5,14 @@
 // src/hba/attention.py:676-711, which builds the same union with a
 // concatenated softmax).
 //
-// One CTA per (split, query, batch*kv-head), 4 warps.  The CTA merges the
-// partial selection lists into the final top-k, lays the union out as 64-key
-// chunks (routed blocks first, then the window, then the sinks), and walks its
-// slice of chunks: cp.async double-buffered K/V gathers of whole 64-key chunks
-// driven by the block list, RoPE applied to window keys in shared memory, then
-// per warp 16 keys: S = Q K^T, online softmax, O += P V.  Warps merge their
-// (max, sum, O) through shared memory; with one split the CTA writes the
-// normalised output and LSE, otherwise a partial that merge_kernel combines.
+// One CTA per (query, batch*kv-head), 4 warps (the per-query prefill path).
+// The CTA merges the partial selection lists into the final top-k, lays the
+// union out as 64-key chunks (routed blocks first, then the window, then the
+// sinks), and walks the chunks: cp.async double-buffered K/V gathers of whole
+// 64-key chunks driven by the block list (window keys from the RoPE'd key
+// copy), then per warp 16 keys: S = Q K^T, online softmax, O += P V.  Warps
+// merge their (max, sum, O) through shared memory and the CTA writes the
+// normalised output and the natural-log LSE.
 #include <climits>
 
 #include "hba_common.cuh"
@@ -152,8 +152,10 @@ __global__ void __launch_bounds__(kAttnThreads) attend_kernel(AttnParams p) {
   const int c_end = (int)(((long long)NC * (split + 1)) / p.splits);
 
   const size_t tok_stride = (size_t)geo.Hkv * DH;
-  const __nv_bfloat16* kbase = p.k + ((size_t)b * geo.n_cap) * tok_stride + (size_t)g * DH;
-  const __nv_bfloat16* vbase = p.v + ((size_t)b * geo.n_cap) * tok_stride + (size_t)g * DH;
+  const size_t head_base = ((size_t)b * geo.n_cap) * tok_stride + (size_t)g * DH;
+  const __nv_bfloat16* kbase = p.k + head_base;
+  const __nv_bfloat16* krbase = p.kr + head_base;
+  const __nv_bfloat16* vbase = p.v + head_base;
 
   // token of row r of chunk c, -1 when the row is past the segment's end
   auto row_token = [&](int c, int r) -> int {
@@ -169,12 +171,13 @@ __global__ void __launch_bounds__(kAttnThreads) attend_kernel(AttnParams p) {
   };
   auto issue = [&](int c, int buf) {
     constexpr int PIECES = DH / 8;
+    const __nv_bfloat16* ksrc = (c >= NCr && c < NCr + NCw) ? krbase : kbase;  // window keys come RoPE'd
     for (int e = tid; e < kChunk * PIECES; e += kAttnThreads) {
       const int r = e / PIECES, pc = e % PIECES;
       const int tok = row_token(c, r);
       const bool valid = tok >= 0;
       const size_t off = (size_t)(valid ? tok : 0) * tok_stride + pc * 8;
-      cp_async16_zfill(&sm.k[buf][r][pc * 8], kbase + off, valid);
+      cp_async16_zfill(&sm.k[buf][r][pc * 8], ksrc + off, valid);
       cp_async16_zfill(&sm.v[buf][r][pc * 8], vbase + off, valid);
     }
     cp_async_commit();
@@ -201,18 +204,6 @@ __global__ void __launch_bounds__(kAttnThreads) attend_kernel(AttnParams p) {
     if (c < NCr) cnt = min(kChunk, Lr - c * kChunk);
     else if (window) cnt = min(kChunk, nw - (c - NCr) * kChunk);
     else cnt = nsink;
-    if (window) {
-      for (int e = tid; e < cnt * HALF; e += kAttnThreads) {
-        const int r = e / HALF, d = e % HALF;
-        const int tok = w0 + (c - NCr) * kChunk + r;
-        const float* cr = p.cos + (size_t)tok * DH;
-        const float* sr = p.sin + (size_t)tok * DH;
-        const float x1 = bf2f(sm.k[buf][r][d]), x2 = bf2f(sm.k[buf][r][d + HALF]);
-        sm.k[buf][r][d] = f2bf(x1 * cr[d] - x2 * sr[d]);
-        sm.k[buf][r][d + HALF] = f2bf(x2 * cr[d + HALF] + x1 * sr[d + HALF]);
-      }
-      __syncthreads();
-    }
     // ---- S = Q K^T for this warp's 16 keys ----
     const __nv_bfloat16(*Q)[DH + 8] = window ? sm.qr : sm.qc;
     float s[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
@@ -323,44 +314,9 @@ __global__ void __launch_bounds__(kAttnThreads) attend_kernel(AttnParams p) {
       O += cb.o[w][r][d] * f;
     }
     const int hq = g * G + r;
-    if (p.splits == 1) {
-      p.out[(((size_t)b * geo.nq + t) * geo.Hq + hq) * DH + d] = f2bf(L > 0.f ? O / L : 0.f);
-      if (d == 0 && p.lse != nullptr)
-        p.lse[((size_t)b * geo.Hq + hq) * geo.nq + t] = L > 0.f ? (M + log2f(L)) * 0.6931471805599453f : neg_inf();
-    } else {
-      float* part = p.part + ((((size_t)bg * geo.nq + t) * p.splits + split) * 16 + r) * (DH + 2);
-      part[2 + d] = O;
-      if (d == 0) {
-        part[0] = M;
-        part[1] = L;
-      }
-    }
-  }
-}
-
-// Combines the per-split (max, sum, O) partials of each query row:
-// M = max_p M_p, L = sum_p L_p 2^(M_p - M), O = sum_p O_p 2^(M_p - M) / L.
-template <int DH>
-__global__ void __launch_bounds__(128) merge_kernel(MergeParams p) {
-  const int t = blockIdx.y, bg = blockIdx.z;
-  const int b = bg / p.Hkv, g = bg % p.Hkv;
-  for (int e = threadIdx.x; e < p.G * DH; e += blockDim.x) {
-    const int r = e / DH, d = e % DH;
-    const float* base = p.part + (((size_t)bg * p.nq + t) * p.splits * 16 + r) * (DH + 2);
-    const size_t sstride = (size_t)16 * (DH + 2);
-    float M = neg_inf();
-    for (int s = 0; s < p.splits; ++s) M = fmaxf(M, base[s * sstride]);
-    const float Mu = (M == neg_inf()) ? 0.f : M;
-    float L = 0.f, O = 0.f;
-    for (int s = 0; s < p.splits; ++s) {
-      const float f = exp2f(base[s * sstride] - Mu);
-      L += base[s * sstride + 1] * f;
-      O += base[s * sstride + 2 + d] * f;
-    }
-    const int hq = g * p.G + r;
-    p.out[(((size_t)b * p.nq + t) * p.Hq + hq) * DH + d] = f2bf(L > 0.f ? O / L : 0.f);
+    p.out[(((size_t)b * geo.nq + t) * geo.Hq + hq) * DH + d] = f2bf(L > 0.f ? O / L : 0.f);
     if (d == 0 && p.lse != nullptr)
-      p.lse[((size_t)b * p.Hq + hq) * p.nq + t] = L > 0.f ? (M + log2f(L)) * 0.6931471805599453f : neg_inf();
+      p.lse[((size_t)b * geo.Hq + hq) * geo.nq + t] = L > 0.f ? (M + log2f(L)) * 0.6931471805599453f : neg_inf();
   }
 }
 
@@ -382,15 +338,6 @@ cudaError_t launch_attend(const AttnParams& p, int dh, cudaStream_t st) {
     if ((e = attr) != cudaSuccess) return e;
     attend_kernel<128><<<grid, kAttnThreads, smem, st>>>(p);
   }
-  return cudaGetLastError();
-}
-
-cudaError_t launch_merge(const MergeParams& p, int dh, cudaStream_t st) {
-  dim3 grid(1, p.nq, p.B * p.Hkv);
-  if (dh == 64)
-    merge_kernel<64><<<grid, 128, 0, st>>>(p);
-  else
-    merge_kernel<128><<<grid, 128, 0, st>>>(p);
   return cudaGetLastError();
 }
 

@@ -151,6 +151,12 @@ struct WarpTopK {
   static HBA_DEVICE bool beats_(float sa, int ia, float sb, int ib) { return (sa > sb) || (sa == sb && ia < ib); }
 };
 
+// Programmatic dependent launch: a kernel launched with the PDL attribute may
+// start before its predecessor finishes; it must call grid_dep_wait() before
+// reading anything the predecessor writes.  Both are no-ops without PDL.
+HBA_DEVICE void grid_dep_wait() { asm volatile("griddepcontrol.wait;\n" ::: "memory"); }
+HBA_DEVICE void grid_dep_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;\n" ::: "memory"); }
+
 // Total order used for every top-k in this library: higher score first, then
 // lower block index.  Matches the oracle's (score desc, index asc) order.
 HBA_DEVICE bool beats(float sa, int ia, float sb, int ib) {

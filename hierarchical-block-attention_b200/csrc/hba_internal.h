@@ -45,6 +45,8 @@ struct SelParams {
   const int32_t* in_idx;
   float* out_score;             // [B*Hkv, nq, splits, list_k]
   int32_t* out_idx;
+  int32_t* counters;            // decode: [B*Hkv] merge counters zeroed here, or null
+  int32_t pdl;                  // launched as a programmatic dependent of the previous kernel
 };
 
 struct AttnParams {
@@ -56,8 +58,9 @@ struct AttnParams {
   const __nv_bfloat16* q;   // [B, nq, Hq, dh] raw
   const float* q_gain;
   const __nv_bfloat16* k;   // [B, n_cap, Hkv, dh] QKNorm'd NoPE keys
+  const __nv_bfloat16* kr;  // [B, n_cap, Hkv, dh] the same keys RoPE'd at their positions
   const __nv_bfloat16* v;   // [B, n_cap, Hkv, dh]
-  const float* cos;         // [n_cap, dh]
+  const float* cos;         // [n_cap, dh] (query rotation)
   const float* sin;
   const float* in_score;    // [B*Hkv, nq, in_lists, list_k]
   const int32_t* in_idx;
@@ -68,18 +71,45 @@ struct AttnParams {
   float* sel_score;
 };
 
-struct MergeParams {
-  int32_t B, Hq, Hkv, G, nq, splits;
-  const float* part;
-  __nv_bfloat16* out;
-  float* lse;
+// Decode attention over a flattened chunk sequence: for every (sequence, kv
+// head) `nchunk` 64-key chunk slots [window | sinks | routed]; CTA c takes the
+// contiguous slots [c*T/N, (c+1)*T/N) of the T = B*Hkv*nchunk total.
+struct DecodeAttnParams {
+  Geom geo;
+  QueryPos qp;
+  int32_t ncw;          // window chunk slots per (sequence, kv head)
+  int32_t ncr;          // routed chunk slots
+  int32_t nchunk;       // ncw + 1 + ncr
+  int32_t in_lists;     // selection lists per query to merge
+  int32_t list_k;
+  int32_t max_seg;      // partial slots per (sequence, kv head)
+  const __nv_bfloat16* q;
+  const float* q_gain;
+  const __nv_bfloat16* k;
+  const __nv_bfloat16* kr;
+  const __nv_bfloat16* v;
+  const float* cos;
+  const float* sin;
+  const float* in_score;
+  const int32_t* in_idx;
+  __nv_bfloat16* out;   // [B, Hq, dh]
+  float* lse;           // [B, Hq] or null
+  int32_t* sel_idx;     // [B, Hkv, K] or null
+  float* sel_score;
+  float* part;          // [B*Hkv, max_seg, G, dh + 2]
+  int32_t* counters;    // [B*Hkv], zeroed by the selection kernel of this call
 };
 
 cudaError_t launch_qknorm(const __nv_bfloat16* x, __nv_bfloat16* y, const float* gain, int64_t rows,
                           int heads, int dh, float eps, cudaStream_t st);
 cudaError_t launch_append(const Geom& geo, int t, const int32_t* pos, const __nv_bfloat16* k_new,
-                          const __nv_bfloat16* v_new, const float* k_gain, __nv_bfloat16* k_cache,
-                          __nv_bfloat16* v_cache, int dh, cudaStream_t st);
+                          const __nv_bfloat16* v_new, const float* k_gain, const float* cos, const float* sin,
+                          __nv_bfloat16* k_cache, __nv_bfloat16* kr_cache, __nv_bfloat16* v_cache, int dh,
+                          cudaStream_t st);
+// k (QKNorm'd, or copied) and kr = RoPE(k) for a whole [B, n, Hkv, dh] tensor.
+cudaError_t launch_qknorm_rope(const Geom& geo, int n, const __nv_bfloat16* k, const float* k_gain,
+                               const float* cos, const float* sin, __nv_bfloat16* kc, __nv_bfloat16* kr, int dh,
+                               cudaStream_t st);
 // Summaries of blocks [blk_begin, blk_end) for every sequence; if pos/t are
 // given (append), only blocks completed by tokens [pos[b], pos[b]+t) of
 // sequence b are rebuilt.
@@ -91,6 +121,19 @@ cudaError_t launch_supers(const Geom& geo, int dh, int nb_fixed, const __nv_bflo
                           cudaStream_t st);
 cudaError_t launch_select(const SelParams& p, int dh, cudaStream_t st);
 cudaError_t launch_attend(const AttnParams& p, int dh, cudaStream_t st);
-cudaError_t launch_merge(const MergeParams& p, int dh, cudaStream_t st);
+cudaError_t launch_decode_attend(const DecodeAttnParams& p, int dh, int grid, cudaStream_t st);
+// One CTA per (sequence, kv head): selection and attention fused (no scratch).
+cudaError_t launch_decode_fused(const DecodeAttnParams& p, const __nv_bfloat16* summ, const __nv_bfloat16* supers,
+                                int dh, cudaStream_t st);
+size_t decode_fused_smem(int dh);
+// tcgen05/TMEM prefill union softmax (hba_prefill_tc.cu).
+bool prefill_tc_supported(const Geom& geo, int dh, int n, bool qknorm);
+cudaError_t launch_prefill_tc(const Geom& geo, int dh, int n, float scale, const __nv_bfloat16* q,
+                              const float* q_gain, const float* k_gain, const __nv_bfloat16* kc,
+                              const __nv_bfloat16* kr, const __nv_bfloat16* v, const float* cos, const float* sin,
+                              const int32_t* sel, int list_stride, __nv_bfloat16* out, float* lse, int* err,
+                              cudaStream_t st);
+// CTAs the decode attention grid should have for this device (all resident at once).
+int decode_attend_grid(int dh, int total_chunks);
 
 }  // namespace hba

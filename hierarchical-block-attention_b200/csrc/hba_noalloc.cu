@@ -14,7 +14,8 @@
 // current) on the first call made while that device is current, so make that
 // first call before any stream capture.  All calls on a device share the one
 // array and it keeps the last call's contents: decode writes every scratch
-// byte it reads, so nothing needs clearing, but calls whose kernels overlap on
+// byte it reads (its merge counters are zeroed by the call's own selection
+// kernel), so nothing needs clearing, but calls whose kernels overlap on
 // the GPU (different streams, no ordering between them) race on it.
 #include <mutex>
 
@@ -53,16 +54,16 @@ extern "C" {
 
 int hba_b200_decode_noalloc(const hba_b200_config* cfg, int32_t batch, int32_t n_cap, const int32_t* seq_lens,
                             const float* scales, const void* q, const float* q_gain, const void* k_cache,
-                            const void* v_cache, const void* summaries, const void* supers, const float* cos,
-                            const float* sin, void* out, float* lse, int32_t* sel_idx, float* sel_score,
-                            cudaStream_t stream) {
+                            const void* k_rope_cache, const void* v_cache, const void* summaries,
+                            const void* supers, const float* cos, const float* sin, void* out, float* lse,
+                            int32_t* sel_idx, float* sel_score, cudaStream_t stream) {
   const size_t need = hba_b200_decode_workspace_size(cfg, batch, n_cap);
   if (need > kScratchBytes) return HBA_B200_ERR_WORKSPACE;  // batch x context too large for the fixed scratch
   void* scratch = nullptr;
   const cudaError_t e = scratch_address(&scratch);
   if (e != cudaSuccess) return HBA_B200_ERR_CUDA;
-  return hba_b200_decode(cfg, batch, n_cap, seq_lens, scales, q, q_gain, k_cache, v_cache, summaries, supers, cos,
-                         sin, out, lse, sel_idx, sel_score, scratch, kScratchBytes, stream);
+  return hba_b200_decode(cfg, batch, n_cap, seq_lens, scales, q, q_gain, k_cache, k_rope_cache, v_cache, summaries,
+                         supers, cos, sin, out, lse, sel_idx, sel_score, scratch, kScratchBytes, stream);
 }
 
 }  // extern "C"

@@ -1,0 +1,450 @@
+// Prefill union softmax on the 5th-generation tensor cores (tcgen05 + TMEM,
+// operands fed by TMA), the full-sequence forward of the HBA path.
+//
+// One CTA per (sequence, kv head, query tile).  A tile is QT = 128/G
+// consecutive queries x the G query heads of the KV group = the 128 rows of
+// the UMMA M dimension (row r = query r/G, head r%G).  Its keys are walked in
+// 64-key chunks: [sinks (keys 0..63, NoPE) | the tile's RoPE window | the
+// union of the blocks its queries selected (NoPE)] -- a routed block is
+// computed once for the whole tile and masked per row by a bitmask of the
+// queries that selected it (reference semantics: src/hba/attention.py:676-711;
+// the reference's fused path builds the same union at 128x128 granularity,
+// :438-475).
+//
+// Roles (192 threads):
+//   warps 0-3  one thread per row: QKNorm + RoPE of the tile's queries into
+//              128-byte-swizzled shared memory (no separate q pass), then per
+//              chunk: S row from TMEM -> mask -> p = exp2(s*scale*log2e - M2)
+//              -> P row (bf16, swizzled) for the PV MMA; epilogue O/l -> out.
+//              M2 is a per-row upper bound of the logits: with QKNorm,
+//              |s| <= scale*|q|*|k| and |k| = sqrt(dh)*k_gain, so the softmax
+//              needs no running max and O is never rescaled.
+//   warp 4     TMEM allocation; one thread issues tcgen05.mma:
+//              S[c%2] = Q K_c^T (M=128, N=64, K=dh), O += P_c V_c (M=128,
+//              N=dh, K=64, V as an MN-major operand).
+//   warp 5     one thread issues the TMA loads of K_c, V_c (3-stage ring).
+// Every mbarrier wait is bounded; a timeout sets *err and drains.
+#include <climits>
+#include <cudaTypedefs.h>
+
+#include "hba_common.cuh"
+#include "hba_internal.h"
+#include "hba_sm100.cuh"
+
+namespace hba {
+
+using namespace sm100;
+
+constexpr int kTcThreads = 192;
+constexpr int kTcStages = 3;
+constexpr int kTcKeys = 64;            // keys per chunk
+constexpr int kTcMaxBlocks = 2048;     // routed block union capacity (nb <= 2048)
+constexpr int kTcMaxChunks = 1 + 20 + kTcMaxBlocks;
+
+enum ChunkType : uint32_t { kSink = 0, kWindow = 1, kRouted = 2 };
+
+template <int DH>
+struct TcSmem {
+  static constexpr int HALVES = DH / 64;
+  static constexpr int QBYTES = HALVES * 128 * 128;     // [128 rows x DH] bf16, swizzled halves
+  static constexpr int KBYTES = HALVES * 64 * 128;      // [64 keys x DH]
+  alignas(1024) unsigned char qc[QBYTES];
+  alignas(1024) unsigned char qr[QBYTES];
+  alignas(1024) unsigned char k[kTcStages][KBYTES];
+  alignas(1024) unsigned char v[kTcStages][KBYTES];
+  alignas(1024) unsigned char p[2][128 * 128];          // [128 rows x 64 keys] bf16, swizzled
+  uint2 chunks[kTcMaxChunks];                           // (key base | type << 28, query mask)
+  uint64_t q_ready, o_full;
+  uint64_t kv_full[kTcStages], kv_empty[kTcStages];
+  uint64_t s_full[2], p_full[2], p_free[2];
+  uint64_t drain;
+  uint32_t tmem_base;
+  int n_chunks;
+  int scan[kTcThreads];
+};
+
+struct PrefillTcParams {
+  Geom geo;
+  int n;
+  float scale;
+  int QT;              // queries per tile
+  int tiles;           // tiles per (sequence, kv head)
+  const __nv_bfloat16* q;   // [B, n, Hq, dh] raw
+  const float* q_gain;
+  const float* k_gain;
+  const float* cos;
+  const float* sin;
+  const int32_t* sel;       // [B*Hkv, n, list_stride] final picks (-1 = none)
+  int list_stride;
+  __nv_bfloat16* out;       // [B, n, Hq, dh]
+  float* lse;               // [B, Hq, n] or null
+  int* err;
+};
+
+template <int DH>
+__global__ void __launch_bounds__(kTcThreads, 1)
+    prefill_tc_kernel(const __grid_constant__ CUtensorMap tm_kc, const __grid_constant__ CUtensorMap tm_kr,
+                      const __grid_constant__ CUtensorMap tm_v, PrefillTcParams p) {
+  extern __shared__ __align__(1024) unsigned char smem_raw[];
+  // dynamic shared memory is only 16-byte aligned by default: align by hand
+  unsigned char* base_ptr =
+      reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  TcSmem<DH>& sm = *reinterpret_cast<TcSmem<DH>*>(base_ptr);
+  constexpr int HALVES = DH / 64;
+  const Geom& geo = p.geo;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int G = geo.G, QT = p.QT, n = p.n;
+  const int bg = blockIdx.x / p.tiles, tile = blockIdx.x % p.tiles;
+  const int b = bg / geo.Hkv, g = bg % geo.Hkv;
+  const int i0 = tile * QT;
+  const int nq = min(QT, n - i0);
+  const int nb = n / geo.Bk;
+
+  // ---- chunk list: sinks, window, routed union (all threads) ----
+  uint32_t* mask = reinterpret_cast<uint32_t*>(sm.p[0]);  // [nb] query bitmasks, overlays P before use
+  for (int i = tid; i < nb; i += kTcThreads) mask[i] = 0u;
+  __syncthreads();
+  {
+    const int32_t* sel = p.sel + ((size_t)bg * n + i0) * p.list_stride;
+    for (int e = tid; e < nq * p.list_stride; e += kTcThreads) {
+      const int blk = sel[e];
+      if (blk >= 0 && blk < nb) atomicOr(&mask[blk], 1u << (e / p.list_stride));
+    }
+  }
+  __syncthreads();
+  const int jlo = max(geo.S, i0 - geo.W + 1);
+  const int jhi = i0 + nq - 1;
+  const int nw = max(0, jhi - jlo + 1);
+  const int nwc = (nw + kTcKeys - 1) / kTcKeys;
+  const int nsc = geo.S > 0 ? 1 : 0;
+  {
+    const int per = (nb + kTcThreads - 1) / kTcThreads;
+    const int lo = tid * per, hi = min(nb, lo + per);
+    int cnt = 0;
+    for (int i = lo; i < hi; ++i) cnt += mask[i] != 0u;
+    sm.scan[tid] = cnt;
+    __syncthreads();
+    if (tid == 0) {
+      int acc = 0;
+      for (int t = 0; t < kTcThreads; ++t) {
+        const int c = sm.scan[t];
+        sm.scan[t] = acc;
+        acc += c;
+      }
+      sm.n_chunks = nsc + nwc + acc;
+    }
+    __syncthreads();
+    int o = nsc + nwc + sm.scan[tid];
+    for (int i = lo; i < hi; ++i)
+      if (mask[i] != 0u) sm.chunks[o++] = make_uint2((uint32_t)(i * geo.Bk) | (kRouted << 28), mask[i]);
+    if (tid == 0 && nsc) sm.chunks[0] = make_uint2(0u | (kSink << 28), 0u);
+    for (int c = tid; c < nwc; c += kTcThreads)
+      sm.chunks[nsc + c] = make_uint2((uint32_t)(jlo + c * kTcKeys) | (kWindow << 28), 0u);
+  }
+  if (tid == 0) {
+    mbar_init(&sm.q_ready, 128);
+    mbar_init(&sm.o_full, 1);
+    for (int s = 0; s < kTcStages; ++s) {
+      mbar_init(&sm.kv_full[s], 1);
+      mbar_init(&sm.kv_empty[s], 1);
+    }
+    for (int s = 0; s < 2; ++s) {
+      mbar_init(&sm.s_full[s], 1);
+      mbar_init(&sm.p_full[s], 128);
+      mbar_init(&sm.p_free[s], 1);
+    }
+    mbar_init(&sm.drain, 1);
+    fence_barrier_init();
+  }
+  if (warp == 4) {
+    tmem_alloc(&sm.tmem_base, 256);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = sm.tmem_base;
+  const int NCH = sm.n_chunks;
+  const uint32_t t_s0 = tmem, t_o = tmem + 128;
+
+  if (warp == 5) {
+    // ---------------- TMA producer ----------------
+    if (lane == 0) {
+      prefetch_tmap(&tm_kc);
+      prefetch_tmap(&tm_kr);
+      prefetch_tmap(&tm_v);
+      for (int c = 0; c < NCH; ++c) {
+        const int st = c % kTcStages, u = c / kTcStages;
+        if (c >= kTcStages && !mbar_wait(&sm.kv_empty[st], (u - 1) & 1, p.err)) break;
+        const uint2 e = sm.chunks[c];
+        const int kb = (int)(e.x & 0x0FFFFFFFu);
+        const uint32_t type = e.x >> 28;
+        mbar_arrive_expect_tx(&sm.kv_full[st], 2 * TcSmem<DH>::KBYTES);
+        const CUtensorMap* km = type == kWindow ? &tm_kr : &tm_kc;
+        for (int h = 0; h < HALVES; ++h) {
+          tma_load_4d(sm.k[st] + h * 8192, km, h * 64, g, kb, b, &sm.kv_full[st]);
+          tma_load_4d(sm.v[st] + h * 8192, &tm_v, h * 64, g, kb, b, &sm.kv_full[st]);
+        }
+      }
+    }
+  } else if (warp == 4) {
+    // ---------------- MMA issuer ----------------
+    if (lane == 0) {
+      constexpr uint32_t idesc_s = idesc_bf16(128, kTcKeys, false, false);
+      constexpr uint32_t idesc_o = idesc_bf16(128, DH, false, true);
+      bool ok = mbar_wait(&sm.q_ready, 0, p.err);
+      tc_fence_after();
+      auto pv = [&](int c) -> bool {
+        const int sb = c & 1, st = c % kTcStages;
+        if (!mbar_wait(&sm.p_full[sb], (c >> 1) & 1, p.err)) return false;
+        tc_fence_after();
+        const uint32_t pa = smem_u32(sm.p[sb]), va = smem_u32(sm.v[st]);
+#pragma unroll
+        for (int kk = 0; kk < kTcKeys / 16; ++kk)
+          umma_f16(t_o, sdesc_sw128(pa + kk * 32, 16, 1024), sdesc_sw128(va + kk * 2048, 8192, 1024), idesc_o,
+                   (c > 0 || kk > 0) ? 1u : 0u);
+        umma_commit(&sm.kv_empty[st]);
+        umma_commit(&sm.p_free[sb]);
+        return true;
+      };
+      for (int c = 0; ok && c < NCH; ++c) {
+        const int st = c % kTcStages, sb = c & 1;
+        if (!mbar_wait(&sm.kv_full[st], (c / kTcStages) & 1, p.err)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t type = sm.chunks[c].x >> 28;
+        const uint32_t qa = smem_u32(type == kWindow ? sm.qr : sm.qc), ka = smem_u32(sm.k[st]);
+#pragma unroll
+        for (int kk = 0; kk < DH / 16; ++kk) {
+          const int h = kk >> 2, ko = (kk & 3) * 32;
+          umma_f16(t_s0 + sb * kTcKeys, sdesc_sw128(qa + h * 16384 + ko, 16, 1024),
+                   sdesc_sw128(ka + h * 8192 + ko, 16, 1024), idesc_s, kk > 0 ? 1u : 0u);
+        }
+        umma_commit(&sm.s_full[sb]);
+        if (c >= 1 && !pv(c - 1)) {
+          ok = false;
+          break;
+        }
+      }
+      if (ok && NCH >= 1) ok = pv(NCH - 1);
+      umma_commit(&sm.o_full);
+      // drain: every MMA issued above is complete before TMEM can be released
+      umma_commit(&sm.drain);
+      mbar_wait(&sm.drain, 0, p.err);
+    }
+  } else {
+    // ---------------- softmax / epilogue, one thread per row ----------------
+    const int r = tid;
+    const int qt = r / G, hh = r % G;
+    const int i = i0 + qt;
+    const bool row_ok = (r < QT * G) && (qt < nq);
+    const int hq = g * G + hh;
+    float M2 = 0.f;
+    {
+      float x[DH];
+      float ss = 0.f;
+      if (row_ok) {
+        const uint4* src = reinterpret_cast<const uint4*>(p.q + (((size_t)b * n + i) * geo.Hq + hq) * DH);
+#pragma unroll
+        for (int c8 = 0; c8 < DH / 8; ++c8) unpack8(src[c8], x + c8 * 8);
+#pragma unroll
+        for (int d = 0; d < DH; ++d) ss = fmaf(x[d], x[d], ss);
+        const float rms = sqrtf(fmaxf(ss / (float)DH, geo.eps));
+        const float gq = p.q_gain[hq];
+        float qn2 = 0.f;
+#pragma unroll
+        for (int d = 0; d < DH; ++d) {
+          x[d] = round_bf16((x[d] / rms) * gq);
+          qn2 = fmaf(x[d], x[d], qn2);
+        }
+        const float kmax = sqrtf((float)DH) * p.k_gain[g] * (1.f + 1.f / 64.f);
+        M2 = p.scale * sqrtf(qn2) * kmax * kLog2e;
+        if (M2 > 120.f) atomicExch(p.err, 2);  // logit bound too large for the fixed-max softmax
+      } else {
+#pragma unroll
+        for (int d = 0; d < DH; ++d) x[d] = 0.f;
+      }
+      const float* cr = p.cos + (size_t)(row_ok ? i : 0) * DH;
+      const float* sr = p.sin + (size_t)(row_ok ? i : 0) * DH;
+#pragma unroll
+      for (int c8 = 0; c8 < DH / 8; ++c8) {
+        uint32_t wc[4], wr[4];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const int d0 = c8 * 8 + 2 * e;
+          float rr[2];
+#pragma unroll
+          for (int t = 0; t < 2; ++t) {
+            const int d = d0 + t;
+            const float rot = d < DH / 2 ? -x[d + DH / 2] : x[d - DH / 2];
+            rr[t] = row_ok ? x[d] * cr[d] + rot * sr[d] : 0.f;
+          }
+          wc[e] = pack_bf16x2(x[d0], x[d0 + 1]);
+          wr[e] = pack_bf16x2(rr[0], rr[1]);
+        }
+        const int h = c8 >> 3, col = (c8 & 7) * 8;
+        const uint32_t off = h * 16384 + sw128_offset(r, col);
+        *reinterpret_cast<uint4*>(sm.qc + off) = make_uint4(wc[0], wc[1], wc[2], wc[3]);
+        *reinterpret_cast<uint4*>(sm.qr + off) = make_uint4(wr[0], wr[1], wr[2], wr[3]);
+      }
+    }
+    fence_proxy_async_smem();
+    mbar_arrive(&sm.q_ready);
+
+    const float sl2 = p.scale * kLog2e;
+    const int win_lo = max(geo.S, i - geo.W + 1);
+    const uint32_t lane_off = (uint32_t)(warp * 32) << 16;
+    float l = 0.f;
+    bool ok = true;
+    for (int c = 0; c < NCH; ++c) {
+      const int sb = c & 1;
+      if (!mbar_wait(&sm.s_full[sb], (c >> 1) & 1, p.err)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      float s[kTcKeys];
+      tmem_ld32(t_s0 + sb * kTcKeys + lane_off, s);
+      tmem_ld32(t_s0 + sb * kTcKeys + 32 + lane_off, s + 32);
+      tmem_ld_wait();
+      if (c >= 2 && !mbar_wait(&sm.p_free[sb], ((c - 2) >> 1) & 1, p.err)) {
+        ok = false;
+        break;
+      }
+      const uint2 e = sm.chunks[c];
+      const int kb = (int)(e.x & 0x0FFFFFFFu);
+      const uint32_t type = e.x >> 28;
+      bool any = row_ok;
+      if (type == kRouted) any = any && ((e.y >> qt) & 1u);
+      unsigned char* prow = sm.p[sb];
+#pragma unroll
+      for (int c8 = 0; c8 < kTcKeys / 8; ++c8) {
+        uint32_t w[4];
+#pragma unroll
+        for (int t = 0; t < 4; ++t) {
+          float pv2[2];
+#pragma unroll
+          for (int u = 0; u < 2; ++u) {
+            const int col = c8 * 8 + 2 * t + u;
+            const int j = kb + col;
+            bool valid = any;
+            if (type == kSink) valid = valid && j < geo.S && j <= i;
+            else if (type == kWindow) valid = valid && j >= win_lo && j <= i;
+            const float pe = valid ? exp2f(fmaf(s[col], sl2, -M2)) : 0.f;
+            l += pe;
+            pv2[u] = pe;
+          }
+          w[t] = pack_bf16x2(pv2[0], pv2[1]);
+        }
+        *reinterpret_cast<uint4*>(prow + sw128_offset(r, c8 * 8)) = make_uint4(w[0], w[1], w[2], w[3]);
+      }
+      fence_proxy_async_smem();
+      tc_fence_before();
+      mbar_arrive(&sm.p_full[sb]);
+    }
+    if (ok && mbar_wait(&sm.o_full, 0, p.err)) {
+      tc_fence_after();
+      const float inv = l > 0.f ? 1.f / l : 0.f;
+#pragma unroll
+      for (int cb = 0; cb < DH / 32; ++cb) {
+        float o[32];
+        tmem_ld32(t_o + cb * 32 + lane_off, o);
+        tmem_ld_wait();
+        if (row_ok) {
+          uint4* dst = reinterpret_cast<uint4*>(p.out + (((size_t)b * n + i) * geo.Hq + hq) * DH + cb * 32);
+#pragma unroll
+          for (int q4 = 0; q4 < 4; ++q4)
+            dst[q4] = make_uint4(pack_bf16x2(o[q4 * 8 + 0] * inv, o[q4 * 8 + 1] * inv),
+                                 pack_bf16x2(o[q4 * 8 + 2] * inv, o[q4 * 8 + 3] * inv),
+                                 pack_bf16x2(o[q4 * 8 + 4] * inv, o[q4 * 8 + 5] * inv),
+                                 pack_bf16x2(o[q4 * 8 + 6] * inv, o[q4 * 8 + 7] * inv));
+        }
+      }
+      if (row_ok && p.lse != nullptr)
+        p.lse[((size_t)b * geo.Hq + hq) * n + i] =
+            l > 0.f ? (M2 + log2f(l)) * 0.6931471805599453f : neg_inf();
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 4) tmem_dealloc(tmem, 256);
+}
+
+// ---------------------------------------------------------------- host ----
+static PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  if (fn == nullptr) {
+    void* ptr = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(ptr);
+  }
+  return fn;
+}
+
+// [B, n, H, dh] bf16 as a 4-D map {dh, H, n, B}, box {64, 1, 64, 1}, 128-byte swizzle.
+static bool make_map(CUtensorMap* m, const void* base, int B, int n, int H, int dh) {
+  auto fn = encode_fn();
+  if (fn == nullptr) return false;
+  cuuint64_t dims[4] = {(cuuint64_t)dh, (cuuint64_t)H, (cuuint64_t)n, (cuuint64_t)B};
+  cuuint64_t strides[3] = {(cuuint64_t)dh * 2, (cuuint64_t)H * dh * 2, (cuuint64_t)n * H * dh * 2};
+  cuuint32_t box[4] = {64, 1, 64, 1};
+  cuuint32_t es[4] = {1, 1, 1, 1};
+  return fn(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, const_cast<void*>(base), dims, strides, box, es,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+bool prefill_tc_supported(const Geom& geo, int dh, int n, bool qknorm) {
+  const int G = geo.G;
+  return qknorm && (dh == 64 || dh == 128) && geo.Bk == kTcKeys && G >= 4 && G <= 16 && (128 / G) * G >= 64 &&
+         n / geo.Bk <= kTcMaxBlocks && geo.W <= 1024 && encode_fn() != nullptr;
+}
+
+cudaError_t launch_prefill_tc(const Geom& geo, int dh, int n, float scale, const __nv_bfloat16* q,
+                              const float* q_gain, const float* k_gain, const __nv_bfloat16* kc,
+                              const __nv_bfloat16* kr, const __nv_bfloat16* v, const float* cos, const float* sin,
+                              const int32_t* sel, int list_stride, __nv_bfloat16* out, float* lse, int* err,
+                              cudaStream_t st) {
+  CUtensorMap m_kc, m_kr, m_v;
+  if (!make_map(&m_kc, kc, geo.B, n, geo.Hkv, dh) || !make_map(&m_kr, kr, geo.B, n, geo.Hkv, dh) ||
+      !make_map(&m_v, v, geo.B, n, geo.Hkv, dh))
+    return cudaErrorInvalidValue;
+  PrefillTcParams p{};
+  p.geo = geo;
+  p.n = n;
+  p.scale = scale;
+  p.QT = 128 / geo.G;
+  p.tiles = (n + p.QT - 1) / p.QT;
+  p.q = q;
+  p.q_gain = q_gain;
+  p.k_gain = k_gain;
+  p.cos = cos;
+  p.sin = sin;
+  p.sel = sel;
+  p.list_stride = list_stride;
+  p.out = out;
+  p.lse = lse;
+  p.err = err;
+  const long long grid = (long long)geo.B * geo.Hkv * p.tiles;
+  if (dh == 64) {
+    const size_t smem = sizeof(TcSmem<64>) + 1024;
+    static const cudaError_t attr = cudaFuncSetAttribute(prefill_tc_kernel<64>,
+                                                         cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (attr != cudaSuccess) return attr;
+    prefill_tc_kernel<64><<<(unsigned)grid, kTcThreads, smem, st>>>(m_kc, m_kr, m_v, p);
+  } else {
+    const size_t smem = sizeof(TcSmem<128>) + 1024;
+    static const cudaError_t attr = cudaFuncSetAttribute(prefill_tc_kernel<128>,
+                                                         cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (attr != cudaSuccess) return attr;
+    prefill_tc_kernel<128><<<(unsigned)grid, kTcThreads, smem, st>>>(m_kc, m_kr, m_v, p);
+  }
+  return cudaGetLastError();
+}
+
+}  // namespace hba

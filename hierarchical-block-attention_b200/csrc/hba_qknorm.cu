@@ -38,14 +38,64 @@ __global__ void __launch_bounds__(256) qknorm_kernel(const __nv_bfloat16* __rest
   rmsnorm_row<DH>(x + w * DH, y + w * DH, gain[h], eps);
 }
 
+// RoPE of one head row held in the warp layout of load_head_row (lane l has
+// elements [l*DH/32, (l+1)*DH/32)): y = x*cos + rot_half(x)*sin with
+// rot_half(x) = (-x[DH/2:], x[:DH/2]) (reference attention.py:35-44).  The
+// partner element d +- DH/2 sits in lane l ^ 16.
+template <int DH>
+HBA_DEVICE void rope_lane(const float* x, float* y, const float* __restrict__ cos_row,
+                          const float* __restrict__ sin_row) {
+  constexpr int PER = DH / 32;
+  const int lane = threadIdx.x & 31;
+  const float sign = lane < 16 ? -1.f : 1.f;
+#pragma unroll
+  for (int i = 0; i < PER; ++i) {
+    const int d = lane * PER + i;
+    const float partner = __shfl_xor_sync(0xffffffffu, x[i], 16);
+    y[i] = x[i] * cos_row[d] + sign * partner * sin_row[d];
+  }
+}
+
+template <int DH>
+HBA_DEVICE void store_head_row(__nv_bfloat16* __restrict__ y, const float* v) {
+  constexpr int PER = DH / 32;
+  const int lane = threadIdx.x & 31;
+  if constexpr (PER == 2) {
+    reinterpret_cast<__nv_bfloat162*>(y)[lane] = __floats2bfloat162_rn(v[0], v[1]);
+  } else {
+    uint2 u;
+    __nv_bfloat162* h = reinterpret_cast<__nv_bfloat162*>(&u);
+    h[0] = __floats2bfloat162_rn(v[0], v[1]);
+    h[1] = __floats2bfloat162_rn(v[2], v[3]);
+    reinterpret_cast<uint2*>(y)[lane] = u;
+  }
+}
+
+// One key head row: kc = QKNorm(k) (or k), kr = bf16(RoPE(kc) at position p).
+template <int DH>
+HBA_DEVICE void key_row(const __nv_bfloat16* __restrict__ ks, __nv_bfloat16* __restrict__ kc,
+                        __nv_bfloat16* __restrict__ kr, float gain, float eps, bool qknorm,
+                        const float* __restrict__ cos_row, const float* __restrict__ sin_row) {
+  constexpr int PER = DH / 32;
+  float v[PER], r[PER];
+  load_head_row<DH>(ks, v);
+  if (qknorm) qknorm_lane<DH>(v, gain, eps);
+  store_head_row<DH>(kc, v);
+  rope_lane<DH>(v, r, cos_row, sin_row);
+  store_head_row<DH>(kr, r);
+}
+
 // Writes new tokens into the cache: k QKNorm'd (or copied when qknorm is
-// off), v copied.  One warp per (batch, token, kv head).
+// off) and its RoPE'd copy at the token's position, v copied.  One warp per
+// (batch, token, kv head).
 template <int DH>
 __global__ void __launch_bounds__(256) append_kernel(Geom geo, int t, const int32_t* __restrict__ pos,
                                                      const __nv_bfloat16* __restrict__ k_new,
                                                      const __nv_bfloat16* __restrict__ v_new,
-                                                     const float* __restrict__ k_gain,
+                                                     const float* __restrict__ k_gain, const float* __restrict__ cos,
+                                                     const float* __restrict__ sin,
                                                      __nv_bfloat16* __restrict__ k_cache,
+                                                     __nv_bfloat16* __restrict__ kr_cache,
                                                      __nv_bfloat16* __restrict__ v_cache) {
   const int64_t w = (int64_t)blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32;
   const int64_t total = (int64_t)geo.B * t * geo.Hkv;
@@ -55,18 +105,28 @@ __global__ void __launch_bounds__(256) append_kernel(Geom geo, int t, const int3
   const int b = (int)(w / ((int64_t)geo.Hkv * t));
   const int p = pos[b] + tau;
   if (p < 0 || p >= geo.n_cap) return;  // host validated; never write out of the cache
-  const __nv_bfloat16* ks = k_new + w * DH;
-  const __nv_bfloat16* vs = v_new + w * DH;
   const int64_t dst = (((int64_t)b * geo.n_cap + p) * geo.Hkv + g) * DH;
+  key_row<DH>(k_new + w * DH, k_cache + dst, kr_cache + dst, geo.qknorm ? k_gain[g] : 1.f, geo.eps,
+              geo.qknorm != 0, cos + (size_t)p * DH, sin + (size_t)p * DH);
   const int lane = threadIdx.x & 31;
-  if (geo.qknorm) {
-    rmsnorm_row<DH>(ks, k_cache + dst, k_gain[g], geo.eps);
-  } else {
-    for (int d = lane; d < DH / 2; d += 32)
-      reinterpret_cast<__nv_bfloat162*>(k_cache + dst)[d] = reinterpret_cast<const __nv_bfloat162*>(ks)[d];
-  }
   for (int d = lane; d < DH / 2; d += 32)
-    reinterpret_cast<__nv_bfloat162*>(v_cache + dst)[d] = reinterpret_cast<const __nv_bfloat162*>(vs)[d];
+    reinterpret_cast<__nv_bfloat162*>(v_cache + dst)[d] = reinterpret_cast<const __nv_bfloat162*>(v_new + w * DH)[d];
+}
+
+// kc and kr for every (batch, token, kv head) of a [B, n, Hkv, dh] tensor.
+template <int DH>
+__global__ void __launch_bounds__(256) qknorm_rope_kernel(Geom geo, int n, const __nv_bfloat16* __restrict__ k,
+                                                          const float* __restrict__ k_gain,
+                                                          const float* __restrict__ cos,
+                                                          const float* __restrict__ sin,
+                                                          __nv_bfloat16* __restrict__ kc,
+                                                          __nv_bfloat16* __restrict__ kr) {
+  const int64_t w = (int64_t)blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32;
+  if (w >= (int64_t)geo.B * n * geo.Hkv) return;
+  const int g = (int)(w % geo.Hkv);
+  const int p = (int)((w / geo.Hkv) % n);
+  key_row<DH>(k + w * DH, kc + w * DH, kr + w * DH, geo.qknorm ? k_gain[g] : 1.f, geo.eps, geo.qknorm != 0,
+              cos + (size_t)p * DH, sin + (size_t)p * DH);
 }
 
 cudaError_t launch_qknorm(const __nv_bfloat16* x, __nv_bfloat16* y, const float* gain, int64_t rows, int heads,
@@ -82,15 +142,31 @@ cudaError_t launch_qknorm(const __nv_bfloat16* x, __nv_bfloat16* y, const float*
 }
 
 cudaError_t launch_append(const Geom& geo, int t, const int32_t* pos, const __nv_bfloat16* k_new,
-                          const __nv_bfloat16* v_new, const float* k_gain, __nv_bfloat16* k_cache,
-                          __nv_bfloat16* v_cache, int dh, cudaStream_t st) {
+                          const __nv_bfloat16* v_new, const float* k_gain, const float* cos, const float* sin,
+                          __nv_bfloat16* k_cache, __nv_bfloat16* kr_cache, __nv_bfloat16* v_cache, int dh,
+                          cudaStream_t st) {
   const int64_t warps = (int64_t)geo.B * t * geo.Hkv;
   const int64_t blocks = (warps + 7) / 8;
   if (blocks == 0) return cudaSuccess;
   if (dh == 64)
-    append_kernel<64><<<(unsigned)blocks, 256, 0, st>>>(geo, t, pos, k_new, v_new, k_gain, k_cache, v_cache);
+    append_kernel<64><<<(unsigned)blocks, 256, 0, st>>>(geo, t, pos, k_new, v_new, k_gain, cos, sin, k_cache,
+                                                         kr_cache, v_cache);
   else
-    append_kernel<128><<<(unsigned)blocks, 256, 0, st>>>(geo, t, pos, k_new, v_new, k_gain, k_cache, v_cache);
+    append_kernel<128><<<(unsigned)blocks, 256, 0, st>>>(geo, t, pos, k_new, v_new, k_gain, cos, sin, k_cache,
+                                                          kr_cache, v_cache);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_qknorm_rope(const Geom& geo, int n, const __nv_bfloat16* k, const float* k_gain,
+                               const float* cos, const float* sin, __nv_bfloat16* kc, __nv_bfloat16* kr, int dh,
+                               cudaStream_t st) {
+  const int64_t warps = (int64_t)geo.B * n * geo.Hkv;
+  const int64_t blocks = (warps + 7) / 8;
+  if (blocks == 0) return cudaSuccess;
+  if (dh == 64)
+    qknorm_rope_kernel<64><<<(unsigned)blocks, 256, 0, st>>>(geo, n, k, k_gain, cos, sin, kc, kr);
+  else
+    qknorm_rope_kernel<128><<<(unsigned)blocks, 256, 0, st>>>(geo, n, k, k_gain, cos, sin, kc, kr);
   return cudaGetLastError();
 }
 

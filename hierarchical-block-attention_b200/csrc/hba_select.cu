@@ -13,6 +13,7 @@
 
 #include "hba_common.cuh"
 #include "hba_internal.h"
+#include "hba_score.cuh"
 
 namespace hba {
 
@@ -20,52 +21,7 @@ constexpr int kSelThreads = 256;
 constexpr int kSelWarps = kSelThreads / 32;
 constexpr int kMaxCandPerCta = 2048;
 
-HBA_DEVICE void query_position(const QueryPos& qp, int b, int t, int& pos, int& nctx, float& scale) {
-  if (qp.seq_lens != nullptr) {
-    nctx = qp.seq_lens[b];
-    pos = nctx - 1;
-    scale = qp.scales[b];
-  } else {
-    nctx = qp.n_fixed;
-    pos = t;
-    scale = qp.scale_fixed;
-  }
-}
-
-// Candidate blocks of the query at `pos`: 1 .. bmax (reference
-// attention.py:250-256: b >= 1 and (b+1)*Bk <= pos - W + 1); 0 when none.
-HBA_DEVICE int last_candidate(int pos, int W, int Bk) {
-  const int lim = pos - W + 1;
-  return lim >= 2 * Bk ? lim / Bk - 1 : 0;
-}
-
-// max over slots of qg . S[slot] for one summary row of m*DH bf16 values.
-// Lane l takes 16-byte vectors l, l+32, ...; each group of DH/8 lanes covers
-// one slot of one vector round.
-template <int DH>
-HBA_DEVICE float slot_score(const __nv_bfloat16* __restrict__ S, const float* __restrict__ qg, int m) {
-  constexpr int LPS = DH / 8;
-  const int lane = threadIdx.x & 31;
-  const int nvec = m * DH / 8;
-  float best = neg_inf();
-  for (int v0 = 0; v0 < nvec; v0 += 32) {
-    const int v = v0 + lane;
-    float part = 0.f;
-    if (v < nvec) {
-      float f[8];
-      unpack8(__ldg(reinterpret_cast<const uint4*>(S) + v), f);
-      const int d0 = (v * 8) % DH;
-#pragma unroll
-      for (int j = 0; j < 8; ++j) part = fmaf(f[j], qg[d0 + j], part);
-    }
-#pragma unroll
-    for (int o = 1; o < LPS; o <<= 1) part += __shfl_xor_sync(0xffffffffu, part, o);
-    if (v < nvec) best = fmaxf(best, part);
-  }
-  return warp_max(best);
-}
-
-template <int DH>
+template <int DH, int VPL>
 __global__ void __launch_bounds__(kSelThreads) select_kernel(SelParams p) {
   const Geom& geo = p.geo;
   const int split = blockIdx.x, t = blockIdx.y, bg = blockIdx.z;
@@ -79,11 +35,52 @@ __global__ void __launch_bounds__(kSelThreads) select_kernel(SelParams p) {
   __shared__ int sup_lo[32], sup_off[32], sup_cnt[32];
   __shared__ int n_children;
 
+  // let the next kernel of the chain start launching; a child-level kernel
+  // reads the super lists of the previous kernel, so it waits for it first
+  grid_dep_launch_dependents();
+  if (p.pdl) grid_dep_wait();
+  if (p.counters != nullptr && split == 0 && t == 0 && tid == 0) p.counters[bg] = 0;
+
   int pos, nctx;
   float scale;
   query_position(p.qp, b, t, pos, nctx, scale);
   const size_t list_base = (((size_t)bg * geo.nq + t) * p.splits + split) * p.list_k;
   const bool ok_pos = (nctx >= 1 && nctx <= geo.n_cap);
+  const int nb = ok_pos ? nctx / geo.Bk : 0;
+  const int bmax = ok_pos ? min(last_candidate(pos, geo.W, geo.Bk), nb - 1) : 0;
+  const int F = geo.F;
+
+  // ---- candidate range (flat / super known from the position alone) ----
+  int C = 0, id_lo = 0;
+  if (p.mode == kSelFlat) {
+    C = max(0, bmax);
+    id_lo = 1;
+  } else if (p.mode == kSelSuper) {
+    if (bmax >= 1) {
+      id_lo = (F == 1) ? 1 : 0;
+      C = bmax / F - id_lo + 1;
+    }
+  }
+  const __nv_bfloat16* src;
+  int rows_cap;
+  if (p.mode == kSelSuper) {
+    src = p.supers;
+    rows_cap = geo.ns_cap;
+  } else {
+    src = p.summ;
+    rows_cap = geo.nb_cap;
+  }
+  const size_t row_elems = (size_t)geo.m * DH;
+  const __nv_bfloat16* base = src + ((size_t)bg * rows_cap) * row_elems;
+  const int nvec = geo.m * DH / 8;
+  SummaryLoads<DH, VPL, kSelWarps> ld;
+  constexpr int GROUP = kSelWarps * SummaryLoads<DH, VPL, kSelWarps>::U;
+  auto flat_id = [&](int r) { return id_lo + (int)(((long long)C * split) / p.splits) + r; };
+  int R = 0;
+  if (p.mode != kSelChild) {
+    R = (int)(((long long)C * (split + 1)) / p.splits) - (int)(((long long)C * split) / p.splits);
+    ld.load(base, row_elems, nvec, 0, R, flat_id);  // in flight during the query prologue
+  }
 
   // ---- grouped routing query ----
   constexpr int PER = DH / 32;
@@ -97,27 +94,12 @@ __global__ void __launch_bounds__(kSelThreads) select_kernel(SelParams p) {
   }
   __syncthreads();
   for (int d = tid; d < DH; d += kSelThreads) {
-    float s = 0.f;
-    for (int h = 0; h < geo.G; ++h) s += qc_s[h][d];
-    qg_s[d] = round_bf16(s);
+    float sacc = 0.f;
+    for (int h = 0; h < geo.G; ++h) sacc += qc_s[h][d];
+    qg_s[d] = round_bf16(sacc);
   }
 
-  const int nb = ok_pos ? nctx / geo.Bk : 0;
-  const int bmax = ok_pos ? min(last_candidate(pos, geo.W, geo.Bk), nb - 1) : 0;
-  const int F = geo.F;
-
-  // ---- this CTA's candidate slice ----
-  int C = 0;       // candidates of this query (all splits)
-  int id_lo = 0;   // flat/super: id of candidate j is id_lo + j
-  if (p.mode == kSelFlat) {
-    C = bmax;
-    id_lo = 1;
-  } else if (p.mode == kSelSuper) {
-    if (bmax >= 1) {
-      id_lo = (F == 1) ? 1 : 0;
-      C = bmax / F - id_lo + 1;
-    }
-  } else {
+  if (p.mode == kSelChild) {
     // merge the super lists: top b_eff supers, then enumerate their candidate children
     const int ns = (nb + F - 1) / F;
     const int b_eff = min(geo.beam, ns);
@@ -125,19 +107,19 @@ __global__ void __launch_bounds__(kSelThreads) select_kernel(SelParams p) {
       WarpTopK top;
       top.init();
       const int total = p.in_lists * geo.beam;
-      const size_t base = ((size_t)bg * geo.nq + t) * total;
+      const size_t lbase = ((size_t)bg * geo.nq + t) * total;
       for (int e0 = 0; e0 < total; e0 += 32) {
         const int e = e0 + lane;
-        float s = neg_inf();
+        float sv = neg_inf();
         int i = INT_MAX;
         if (e < total) {
-          const int ii = p.in_idx[base + e];
+          const int ii = __ldcg(p.in_idx + lbase + e);
           if (ii >= 0) {
-            s = p.in_score[base + e];
+            sv = __ldcg(p.in_score + lbase + e);
             i = ii;
           }
         }
-        if (b_eff > 0) top.offer(s, i, b_eff);
+        if (b_eff > 0) top.offer(sv, i, b_eff);
       }
       const bool valid = lane < b_eff && top.i != INT_MAX;
       int lo = 0, cnt = 0;
@@ -160,37 +142,26 @@ __global__ void __launch_bounds__(kSelThreads) select_kernel(SelParams p) {
     __syncthreads();
     C = n_children;
   }
+  __syncthreads();
   const int j0 = (int)(((long long)C * split) / p.splits);
-  const int j1 = (int)(((long long)C * (split + 1)) / p.splits);
-  const int R = j1 - j0;  // host guarantees R <= kMaxCandPerCta
+  R = (int)(((long long)C * (split + 1)) / p.splits) - j0;  // host guarantees R <= kMaxCandPerCta
+  auto child_id = [&](int r) {
+    const int j = j0 + r;
+    int sidx = 0;
+    while (sidx < 31 && j >= sup_off[sidx] + sup_cnt[sidx]) ++sidx;
+    return sup_lo[sidx] + (j - sup_off[sidx]);
+  };
 
   // ---- score ----
-  const __nv_bfloat16* src;
-  int rows_cap;
-  if (p.mode == kSelSuper) {
-    src = p.supers;
-    rows_cap = geo.ns_cap;
-  } else {
-    src = p.summ;
-    rows_cap = geo.nb_cap;
-  }
-  const size_t row_elems = (size_t)geo.m * DH;
-  const __nv_bfloat16* base = src + ((size_t)bg * rows_cap) * row_elems;
-  __syncthreads();
-  for (int r = warp; r < R; r += kSelWarps) {
-    const int j = j0 + r;
-    int id;
-    if (p.mode == kSelChild) {
-      int s = 0;
-      while (s < 31 && j >= sup_off[s] + sup_cnt[s]) ++s;
-      id = sup_lo[s] + (j - sup_off[s]);
-    } else {
-      id = id_lo + j;
+  if (p.mode == kSelChild) {
+    for (int rb = 0; rb < R; rb += GROUP) {
+      ld.load(base, row_elems, nvec, rb, R, child_id);
+      ld.score(qg_s, nvec, rb, R, scale, child_id, sc_s, id_s);
     }
-    const float sc = slot_score<DH>(base + (size_t)id * row_elems, qg_s, geo.m) * scale;
-    if (lane == 0) {
-      sc_s[r] = sc;
-      id_s[r] = id;
+  } else {
+    for (int rb = 0; rb < R; rb += GROUP) {
+      if (rb > 0) ld.load(base, row_elems, nvec, rb, R, flat_id);
+      ld.score(qg_s, nvec, rb, R, scale, flat_id, sc_s, id_s);
     }
   }
   __syncthreads();
@@ -202,9 +173,9 @@ __global__ void __launch_bounds__(kSelThreads) select_kernel(SelParams p) {
     const int k = p.list_k;
     for (int e0 = 0; e0 < R; e0 += 32) {
       const int e = e0 + lane;
-      const float s = e < R ? sc_s[e] : neg_inf();
+      const float sv = e < R ? sc_s[e] : neg_inf();
       const int i = e < R ? id_s[e] : INT_MAX;
-      top.offer(s, i, k);
+      top.offer(sv, i, k);
     }
     if (lane < k) {
       const bool valid = top.i != INT_MAX;
@@ -214,13 +185,30 @@ __global__ void __launch_bounds__(kSelThreads) select_kernel(SelParams p) {
   }
 }
 
+template <int DH, int VPL>
+static cudaError_t launch_select_t(const SelParams& p, cudaStream_t st) {
+  cudaLaunchConfig_t lc = {};
+  lc.gridDim = dim3(p.splits, p.geo.nq, p.geo.B * p.geo.Hkv);
+  lc.blockDim = dim3(kSelThreads);
+  lc.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  lc.attrs = attr;
+  lc.numAttrs = p.pdl ? 1 : 0;
+  return cudaLaunchKernelEx(&lc, select_kernel<DH, VPL>, p);
+}
+
 cudaError_t launch_select(const SelParams& p, int dh, cudaStream_t st) {
-  dim3 grid(p.splits, p.geo.nq, p.geo.B * p.geo.Hkv);
-  if (dh == 64)
-    select_kernel<64><<<grid, kSelThreads, 0, st>>>(p);
-  else
-    select_kernel<128><<<grid, kSelThreads, 0, st>>>(p);
-  return cudaGetLastError();
+  const int nvec = p.geo.m * dh / 8;  // 16-byte vectors per summary row
+  const int vpl = (nvec + 31) / 32;
+  if (dh == 64) {
+    if (vpl <= 1) return launch_select_t<64, 1>(p, st);
+    return launch_select_t<64, 2>(p, st);
+  }
+  if (vpl <= 1) return launch_select_t<128, 1>(p, st);
+  if (vpl <= 2) return launch_select_t<128, 2>(p, st);
+  return launch_select_t<128, 4>(p, st);
 }
 
 }  // namespace hba

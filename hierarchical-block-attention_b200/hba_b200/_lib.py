@@ -48,12 +48,13 @@ SIGNATURES = {
     "hba_b200_qknorm": (ctypes.c_int, [_P, _P, _P, _I64, _I32, _I32, _F, _P]),
     "hba_b200_summarize": (ctypes.c_int, [_CFG, _I32, _I32, _P, _P, _P, _P, _I32, _I32, _P]),
     "hba_b200_build_supers": (ctypes.c_int, [_CFG, _I32, _I32, _I32, _P, _P, _I32, _I32, _P]),
-    "hba_b200_append_kv": (ctypes.c_int, [_CFG, _I32, _I32, _I32, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P]),
+    "hba_b200_append_kv": (ctypes.c_int, [_CFG, _I32, _I32, _I32, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P,
+                                          _P, _P, _P]),
     "hba_b200_decode_workspace_size": (_SZ, [_CFG, _I32, _I32]),
     "hba_b200_decode": (ctypes.c_int, [_CFG, _I32, _I32, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P,
-                                       _P, _P, _SZ, _P]),
+                                       _P, _P, _P, _SZ, _P]),
     "hba_b200_decode_noalloc": (ctypes.c_int, [_CFG, _I32, _I32, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P,
-                                               _P, _P, _P]),
+                                               _P, _P, _P, _P]),
     "hba_b200_prefill_workspace_size": (_SZ, [_CFG, _I32, _I32]),
     "hba_b200_set_profile_events": (ctypes.c_int, [ctypes.POINTER(ctypes.c_void_p), _I32]),
     "hba_b200_profile_events_recorded": (ctypes.c_int, []),

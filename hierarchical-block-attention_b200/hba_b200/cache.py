@@ -6,8 +6,9 @@ and every block summary over the whole sequence (src/hba/attention.py:631,
 updates it incrementally, so one decode step reads only what the union
 softmax needs (~2.1K keys + the candidate summaries):
 
-* ``k``        [B, n_cap, Hkv, dh] bf16 -- QKNorm'd NoPE keys (RoPE is applied
-                 in-kernel to the window keys only)
+* ``k``        [B, n_cap, Hkv, dh] bf16 -- QKNorm'd NoPE keys
+* ``kr``       [B, n_cap, Hkv, dh] bf16 -- the same keys RoPE'd at their positions,
+                 written once at append time and read for the window
 * ``v``        [B, n_cap, Hkv, dh] bf16
 * ``summaries``[B, Hkv, n_cap/block, m, dh] bf16 -- slot summaries of complete blocks
 * ``supers``   [B, Hkv, ceil(nb/F), m, dh] bf16 -- hierarchical mode only
@@ -44,6 +45,7 @@ class HBADecodeCache:
         dev = self.device
         self.c = c_config(cfg, self.hier)
         self.k = torch.zeros(self.B, self.n_cap, Hkv, dh, dtype=BF16, device=dev)
+        self.kr = torch.zeros_like(self.k)
         self.v = torch.zeros_like(self.k)
         self.summaries = torch.zeros(self.B, Hkv, self.nb_cap, m, dh, dtype=BF16, device=dev)
         self.supers = (torch.zeros(self.B, Hkv, max(1, self.ns_cap), m, dh, dtype=BF16, device=dev)
@@ -80,8 +82,8 @@ class HBADecodeCache:
             kb, vb = as_bf16(k_new), as_bf16(v_new)
             st = _lib.load().hba_b200_append_kv(
                 ctypes.byref(self.c), self.B, self.n_cap, int(t), ptr(self.lens), ptr(kb), ptr(vb), ptr(self.k_gain),
-                ptr(self.probes), ptr(self.proj), ptr(self.k), ptr(self.v), ptr(self.summaries), ptr(self.supers),
-                stream_of(self.device))
+                ptr(self.cos), ptr(self.sin), ptr(self.probes), ptr(self.proj), ptr(self.k), ptr(self.kr),
+                ptr(self.v), ptr(self.summaries), ptr(self.supers), stream_of(self.device))
             _lib.check(st, "hba_b200_append_kv")
             self.lens += t
         self.lens_host += t
@@ -117,7 +119,8 @@ class HBADecodeCache:
         """Allocation-free decode on preallocated bf16 q/out (graph-capturable)."""
         st = _lib.load().hba_b200_decode(
             ctypes.byref(self.c), self.B, self.n_cap, ptr(self.lens), ptr(self.scales), ptr(qb), ptr(self.q_gain),
-            ptr(self.k), ptr(self.v), ptr(self.summaries), ptr(self.supers), ptr(self.cos), ptr(self.sin), ptr(out),
+            ptr(self.k), ptr(self.kr), ptr(self.v), ptr(self.summaries), ptr(self.supers), ptr(self.cos),
+            ptr(self.sin), ptr(out),
             ptr(lse), ptr(sel_idx), ptr(sel_score), ptr(self.workspace), self.ws_bytes,
             stream if stream is not None else stream_of(self.device))
         _lib.check(st, "hba_b200_decode")

@@ -92,18 +92,21 @@ int hba_b200_build_supers(const hba_b200_config* cfg, int32_t batch, int32_t nb_
 
 /*
  * Append `t` new tokens per sequence at positions pos[b] .. pos[b]+t-1 of a
- * KV/summary cache: k is QKNorm'd (k_gain) and stored, v stored, and the
- * summaries of blocks completed by the append (plus the super-summaries that
- * contain them, when `supers` is not NULL) are rebuilt.
- * k_new, v_new: [batch, t, Hkv, dh] bf16 raw; pos: [batch] int32 device.
+ * KV/summary cache: k is QKNorm'd (k_gain) and stored, its RoPE'd copy (at
+ * the token's position, cos/sin [n_cap, dh] fp32) stored in k_rope_cache, v
+ * stored, and the summaries of blocks completed by the append (plus the
+ * super-summaries that contain them, when `supers` is not NULL) are rebuilt.
+ * k_new, v_new: [batch, t, Hkv, dh] bf16 raw; pos: [batch] int32 device;
+ * k_cache, k_rope_cache, v_cache: [batch, n_cap, Hkv, dh] bf16.
  * Has no single counterpart in the reference, which recomputes QKNorm and
  * every summary on each call (src/hba/attention.py:631,659); it produces the
  * same cache contents incrementally.
  */
 int hba_b200_append_kv(const hba_b200_config* cfg, int32_t batch, int32_t n_cap, int32_t t,
                        const int32_t* pos, const void* k_new, const void* v_new, const float* k_gain,
-                       const float* probes, const float* proj, void* k_cache, void* v_cache,
-                       void* summaries, void* supers, cudaStream_t stream);
+                       const float* cos, const float* sin, const float* probes, const float* proj,
+                       void* k_cache, void* k_rope_cache, void* v_cache, void* summaries, void* supers,
+                       cudaStream_t stream);
 
 /* Bytes of scratch needed by hba_b200_decode for this batch and cache capacity
  * (0 when the configuration is rejected). */
@@ -119,6 +122,8 @@ size_t hba_b200_decode_workspace_size(const hba_b200_config* cfg, int32_t batch,
  *   scales:    [batch] fp32 device, union logit scale (content scale x tau(n))
  *   q:         [batch, Hq, dh] bf16 raw query;  q_gain: [Hq] fp32
  *   k_cache, v_cache: [batch, n_cap, Hkv, dh] bf16 (keys QKNorm'd, NoPE)
+ *   k_rope_cache: [batch, n_cap, Hkv, dh] bf16, the same keys RoPE'd at their
+ *              positions (hba_b200_append_kv writes both); the window reads it
  *   summaries: [batch, Hkv, n_cap/block, m, dh] bf16
  *   supers:    [batch, Hkv, ceil(n_cap/block/F), m, dh] bf16 (hier only)
  *   cos, sin:  [n_cap, dh] fp32 RoPE tables (rope_tables layout)
@@ -131,9 +136,9 @@ size_t hba_b200_decode_workspace_size(const hba_b200_config* cfg, int32_t batch,
  */
 int hba_b200_decode(const hba_b200_config* cfg, int32_t batch, int32_t n_cap, const int32_t* seq_lens,
                     const float* scales, const void* q, const float* q_gain, const void* k_cache,
-                    const void* v_cache, const void* summaries, const void* supers, const float* cos,
-                    const float* sin, void* out, float* lse, int32_t* sel_idx, float* sel_score,
-                    void* workspace, size_t workspace_bytes, cudaStream_t stream);
+                    const void* k_rope_cache, const void* v_cache, const void* summaries, const void* supers,
+                    const float* cos, const float* sin, void* out, float* lse, int32_t* sel_idx,
+                    float* sel_score, void* workspace, size_t workspace_bytes, cudaStream_t stream);
 
 /*
  * hba_b200_decode without a workspace argument, for callers that cannot
@@ -150,9 +155,9 @@ int hba_b200_decode(const hba_b200_config* cfg, int32_t batch, int32_t n_cap, co
  */
 int hba_b200_decode_noalloc(const hba_b200_config* cfg, int32_t batch, int32_t n_cap, const int32_t* seq_lens,
                             const float* scales, const void* q, const float* q_gain, const void* k_cache,
-                            const void* v_cache, const void* summaries, const void* supers, const float* cos,
-                            const float* sin, void* out, float* lse, int32_t* sel_idx, float* sel_score,
-                            cudaStream_t stream);
+                            const void* k_rope_cache, const void* v_cache, const void* summaries,
+                            const void* supers, const float* cos, const float* sin, void* out, float* lse,
+                            int32_t* sel_idx, float* sel_score, cudaStream_t stream);
 
 /* Bytes of scratch needed by hba_b200_prefill (0 when rejected). */
 size_t hba_b200_prefill_workspace_size(const hba_b200_config* cfg, int32_t batch, int32_t n);
@@ -167,6 +172,13 @@ size_t hba_b200_prefill_workspace_size(const hba_b200_config* cfg, int32_t batch
  *   probes: [Hkv, m, dh], proj: [Hkv, dh, dh] fp32 (SlotSummarizer weights)
  *   out: [batch, n, Hq, dh] bf16; lse: [batch, Hq, n] fp32 or NULL
  *   sel_idx / sel_score: [batch, Hkv, n, k_blocks] or NULL
+ * With QKNorm, block 64 and G >= 4 the union softmax runs on the tcgen05
+ * tensor cores (one 128-row tile = 128/G queries x G heads, the routed blocks
+ * of the tile's queries computed once and masked per row); other
+ * configurations use the per-query gather kernel.  The first 4 bytes of the
+ * workspace receive a device status after the call: 0 = ok, 1 = a bounded
+ * device wait timed out, 2 = a QKNorm logit bound too large for the
+ * tensor-core path's fixed-max softmax.
  * Replaces hba_attention_eval (src/hba/attention.py:610-713, hier or flat)
  * and the forward of hba_attention_fused / hba_attention_dense
  * (src/hba/attention.py:552-607, :306-389), which compute the same union.

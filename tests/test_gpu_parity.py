@@ -47,11 +47,37 @@ def test_summaries_and_supers_match_oracle(dh, Bk, m):
 
 
 # ---------------------------------------------------------------- decode ----
+# hba_b200_decode has two paths: "fused" (one CTA per sequence and kv head) and
+# "split" (selection kernels + stream-K attention); the library picks by batch
+# size, HBA_B200_DECODE_PATH forces one so both are checked on small shapes.
+PATHS = ["split", "fused"]
+
+
+@pytest.mark.parametrize("path", PATHS)
 @pytest.mark.parametrize("hier", [False, True])
-def test_decode_small_matches_oracle(hier):
+def test_decode_small_matches_oracle(hier, path, monkeypatch):
+    monkeypatch.setenv("HBA_B200_DECODE_PATH", path)
     cfg = H.cfg_of(n_heads=8, n_kv=2, head_dim=128, fanout=8, beam=3) if hier else H.cfg_of()
     cache, wl, summ, qkn, cos, sin = H.build_cache(cfg, 3, 4096, hier, seed=11)
     H.check_decode(cache, wl["q"], cfg, hier, qkn, cos, sin)
+
+
+def test_decode_paths_agree():
+    """Both paths select the same blocks and agree on out/LSE (same scores)."""
+    import os
+    cfg = H.cfg_of(n_heads=32, n_kv=8, head_dim=128, fanout=16, beam=4)
+    cache, wl, summ, qkn, cos, sin = H.build_cache(cfg, 4, 16384, True, seed=15)
+    res = {}
+    for path in PATHS:
+        os.environ["HBA_B200_DECODE_PATH"] = path
+        try:
+            res[path] = cache.attend(wl["q"], return_lse=True, return_selection=True)
+        finally:
+            del os.environ["HBA_B200_DECODE_PATH"]
+    (o1, l1, (s1, _)), (o2, l2, (s2, _)) = res["split"], res["fused"]
+    assert torch.equal(s1, s2)
+    assert (o1.float() - o2.float()).abs().max().item() < 1e-2
+    assert (l1 - l2).abs().max().item() < 1e-4
 
 
 def test_decode_planted_blocks_are_selected():
@@ -65,9 +91,11 @@ def test_decode_planted_blocks_are_selected():
             assert set(pl[b, g].tolist()) <= set(sel[b, g].tolist())
 
 
-def test_decode_ragged_lengths_and_edges():
+@pytest.mark.parametrize("path", PATHS)
+def test_decode_ragged_lengths_and_edges(path, monkeypatch):
     """Ragged batch: a sequence shorter than the window (no candidates), one
     with fewer candidates than k, one shorter than the sink count, a full one."""
+    monkeypatch.setenv("HBA_B200_DECODE_PATH", path)
     cfg = H.cfg_of()
     cache, wl, summ, qkn, cos, sin = H.build_cache(cfg, 5, 4096, False, seed=13)
     lens = np.array([4096, 300, 1024 + 64 * 5 + 7, 2, 1], dtype=np.int64)
@@ -77,8 +105,10 @@ def test_decode_ragged_lengths_and_edges():
     H.check_decode(cache, wl["q"], cfg, False, qkn, cos, sin)
 
 
+@pytest.mark.parametrize("path", PATHS)
 @pytest.mark.parametrize("variant", ["noqk", "inv_sqrt_d", "tau"])
-def test_decode_scale_variants(variant):
+def test_decode_scale_variants(variant, path, monkeypatch):
+    monkeypatch.setenv("HBA_B200_DECODE_PATH", path)
     if variant == "noqk":
         cfg = H.cfg_of(qknorm=False)
     elif variant == "inv_sqrt_d":
@@ -102,7 +132,7 @@ def test_cache_incremental_append_matches_bulk():
         t1 = min(n, t0 + 37)
         inc.append(wl["k"][:, t0:t1], wl["v"][:, t0:t1])
     torch.cuda.synchronize()
-    for name in ("k", "v", "summaries", "supers"):
+    for name in ("k", "kr", "v", "summaries", "supers"):
         assert torch.equal(getattr(bulk, name), getattr(inc, name)), name
     a = bulk.attend(wl["q"])
     b = inc.attend(wl["q"])
