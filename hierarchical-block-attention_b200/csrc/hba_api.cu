@@ -494,10 +494,11 @@ int hba_b200_prefill(const hba_b200_config* cfg, int32_t batch, int32_t n, float
   st = run_select(cfg, geo, qp, plan, static_cast<const __nv_bfloat16*>(q), q_gain, summ, sup, ws, nullptr, fin,
                   fin_lists, fin_k, stream);
   if (st != HBA_B200_OK) return st;
-  // tensor-core union path: opt-in (HBA_B200_PREFILL_PATH=tc) until validated on hardware
+  // tensor-core union path unless HBA_B200_PREFILL_PATH=gather forces the per-query kernel
   const char* force = getenv("HBA_B200_PREFILL_PATH");
-  const bool want_tc = force != nullptr && strcmp(force, "tc") == 0;
-  if (want_tc && fin_lists == 1 && hba::prefill_tc_supported(geo, dh, n, cfg->qknorm != 0)) {
+  const bool want_tc = !(force != nullptr && strcmp(force, "gather") == 0);
+  const bool v_aligned = (reinterpret_cast<uintptr_t>(v) & 15u) == 0;  // TMA needs 16-byte aligned bases
+  if (want_tc && v_aligned && fin_lists == 1 && hba::prefill_tc_supported(geo, dh, n, cfg->qknorm != 0)) {
     e = hba::launch_prefill_tc(geo, dh, n, scale, static_cast<const __nv_bfloat16*>(q), q_gain, k_gain, kc, kr,
                                static_cast<const __nv_bfloat16*>(v), cos, sin, fin.idx, fin_lists * fin_k,
                                static_cast<__nv_bfloat16*>(out), lse, dev_status, stream);

@@ -140,22 +140,58 @@ def test_cache_incremental_append_matches_bulk():
 
 
 # --------------------------------------------------------------- prefill ----
+# hba_b200_prefill runs the union softmax on the tcgen05 tensor cores ("tc")
+# or with the per-query gather kernel ("gather"); HBA_B200_PREFILL_PATH
+# selects one so both are checked (configurations outside the tensor-core
+# envelope -- no QKNorm, block != 64, G < 4 -- always gather).
+PREFILL_PATHS = ["gather", "tc"]
+
+
+@pytest.mark.parametrize("path", PREFILL_PATHS)
 @pytest.mark.parametrize("hier", [False, True])
-def test_prefill_cfg0_shape_matches_oracle(hier):
+def test_prefill_cfg0_shape_matches_oracle(hier, path, monkeypatch):
+    monkeypatch.setenv("HBA_B200_PREFILL_PATH", path)
     cfg = H.cfg_of(fanout=8, beam=4) if hier else H.cfg_of()
     rows = H.sample_rows(2048, 48, seed=1)
     H.check_prefill(cfg, 1, 2048, hier, seed=21, rows=rows)
 
 
-def test_prefill_dh128_gqa4_matches_oracle():
+@pytest.mark.parametrize("path", PREFILL_PATHS)
+def test_prefill_dh128_gqa4_matches_oracle(path, monkeypatch):
+    monkeypatch.setenv("HBA_B200_PREFILL_PATH", path)
     cfg = H.cfg_of(n_heads=32, n_kv=8, head_dim=128)
     rows = H.sample_rows(2048, 24, seed=2)
     H.check_prefill(cfg, 2, 2048, False, seed=22, rows=rows)
 
 
-def test_prefill_short_sequence_no_candidates():
+@pytest.mark.parametrize("path", PREFILL_PATHS)
+def test_prefill_short_sequence_no_candidates(path, monkeypatch):
+    monkeypatch.setenv("HBA_B200_PREFILL_PATH", path)
     cfg = H.cfg_of()
     H.check_prefill(cfg, 1, 512, False, seed=23, rows=np.arange(512))
+
+
+def test_prefill_paths_agree_on_every_row():
+    """Tensor-core and gather paths: same selection, outputs within bf16 noise, all rows."""
+    import os
+    cfg = H.cfg_of(n_heads=32, n_kv=8, head_dim=128)
+    n = 4096
+    summ, qkn = synth.make_weights(cfg, "cuda", seed=25, gains=True)
+    cos, sin = synth.rope_tables(n, 128, 1e6)
+    wl = synth.prefill_workload(cfg, 2, n, seed=25)
+    res = {}
+    for path in PREFILL_PATHS:
+        os.environ["HBA_B200_PREFILL_PATH"] = path
+        try:
+            with torch.no_grad():
+                res[path] = hba_attention_b200(wl["q"], wl["k"], wl["v"], cos, sin, cfg, summ, qkn,
+                                               return_lse=True, return_selection=True)
+        finally:
+            del os.environ["HBA_B200_PREFILL_PATH"]
+    (o1, l1, (s1, _)), (o2, l2, (s2, _)) = res["gather"], res["tc"]
+    assert torch.equal(s1, s2)
+    assert (o1.float() - o2.float()).abs().max().item() < 2e-2
+    assert (l1 - l2).abs().max().item() < 1e-3
 
 
 def test_prefill_tiny_blocks_and_knobs():
