@@ -24,6 +24,8 @@ struct ProfileHook {
   int next = 0;
 };
 ProfileHook g_prof;
+unsigned long long* g_trace = nullptr;  // hba_b200_set_debug_trace
+long long g_trace_ctas = 0;
 
 void prof_begin(cudaStream_t st) {
   g_prof.next = 0;
@@ -218,13 +220,24 @@ int run_select(const hba_b200_config* c, const Geom& geo, const hba::QueryPos& q
 constexpr long long kFusedMinPairs = 96;
 constexpr int kFusedMaxItems = 2048;  // must match kTopkMaxItems (hba_topk.cuh)
 
-bool use_fused_decode(const hba_b200_config* c, const Geom& geo, size_t bh) {
+enum DecodePath { kDecodeSplit = 0, kDecodeFused = 1, kDecodeTc = 2 };
+
+// Large batches: one CTA per (sequence, kv head) -- on tcgen05 when QKNorm
+// bounds the logits (kDecodeTc), else the mma.sync fused kernel; small
+// batches: the split path.  HBA_B200_DECODE_PATH=tc|fused|split forces one
+// (falling back to split when the forced kernel cannot run the configuration).
+int decode_path(const hba_b200_config* c, const Geom& geo, size_t bh, const void* k, const void* kr, const void* v) {
   const char* force = getenv("HBA_B200_DECODE_PATH");
   bool fits = geo.nb_cap <= kFusedMaxItems;
   if (c->hier) fits = fits && geo.ns_cap <= kFusedMaxItems && (long long)c->beam * c->fanout <= kFusedMaxItems;
-  if (force != nullptr && strcmp(force, "split") == 0) return false;
-  if (force != nullptr && strcmp(force, "fused") == 0) return fits;
-  return fits && (long long)bh >= kFusedMinPairs;
+  const bool tc_ok = fits && hba::decode_tc_supported(geo, c->head_dim, k, kr, v);
+  if (force != nullptr) {
+    if (strcmp(force, "split") == 0) return kDecodeSplit;
+    if (strcmp(force, "fused") == 0) return fits ? kDecodeFused : kDecodeSplit;
+    if (strcmp(force, "tc") == 0) return tc_ok ? kDecodeTc : kDecodeSplit;
+  }
+  if (!fits || (long long)bh < kFusedMinPairs) return kDecodeSplit;
+  return tc_ok ? kDecodeTc : kDecodeFused;
 }
 
 // decode split path: per-(sequence, kv head) softmax partials and merge counters
@@ -261,6 +274,13 @@ int hba_b200_set_profile_events(void* const* events, int32_t count) {
 }
 
 int hba_b200_profile_events_recorded(void) { return g_prof.next; }
+
+int hba_b200_set_debug_trace(void* device_buffer, int64_t bytes) {
+  if (bytes < 0 || (device_buffer == nullptr && bytes != 0)) return HBA_B200_ERR_INVALID_ARGUMENT;
+  g_trace = static_cast<unsigned long long*>(device_buffer);
+  g_trace_ctas = device_buffer == nullptr ? 0 : bytes / 64;
+  return HBA_B200_OK;
+}
 
 int hba_b200_qknorm(const void* x, void* y, const float* gain, int64_t rows, int32_t heads, int32_t head_dim,
                     float eps, cudaStream_t stream) {
@@ -337,11 +357,12 @@ size_t hba_b200_decode_workspace_size(const hba_b200_config* cfg, int32_t batch,
   if (!config_ok(cfg, &st) || batch <= 0 || n_cap <= 0 || n_cap % cfg->block != 0) return 0;
   const Plan plan = make_plan(cfg, n_cap / cfg->block, batch * cfg->n_kv, true);
   const size_t bh = (size_t)batch * cfg->n_kv;
-  return selection_bytes(cfg, plan, bh) + decode_state_bytes(cfg, plan, bh);
+  return kAlign + selection_bytes(cfg, plan, bh) + decode_state_bytes(cfg, plan, bh);  // status word first
 }
 
 int hba_b200_decode(const hba_b200_config* cfg, int32_t batch, int32_t n_cap, const int32_t* seq_lens,
-                    const float* scales, const void* q, const float* q_gain, const void* k_cache,
+                    const float* scales, const void* q, const float* q_gain, const float* k_gain,
+                    const void* k_cache,
                     const void* k_rope_cache, const void* v_cache, const void* summaries, const void* supers,
                     const float* cos, const float* sin, void* out, float* lse, int32_t* sel_idx, float* sel_score,
                     void* workspace, size_t workspace_bytes, cudaStream_t stream) {
@@ -349,7 +370,8 @@ int hba_b200_decode(const hba_b200_config* cfg, int32_t batch, int32_t n_cap, co
   if (!config_ok(cfg, &st)) return st;
   if (batch <= 0 || n_cap <= 0 || seq_lens == nullptr || scales == nullptr || q == nullptr || k_cache == nullptr ||
       k_rope_cache == nullptr || v_cache == nullptr || summaries == nullptr || cos == nullptr || sin == nullptr ||
-      out == nullptr || (cfg->qknorm && q_gain == nullptr) || (cfg->hier && supers == nullptr) ||
+      out == nullptr || (cfg->qknorm && (q_gain == nullptr || k_gain == nullptr)) ||
+      (cfg->hier && supers == nullptr) ||
       ((sel_idx == nullptr) != (sel_score == nullptr)))
     return HBA_B200_ERR_INVALID_ARGUMENT;
   if (n_cap % cfg->block != 0) return HBA_B200_ERR_NOT_BLOCK_MULTIPLE;
@@ -360,16 +382,21 @@ int hba_b200_decode(const hba_b200_config* cfg, int32_t batch, int32_t n_cap, co
   const size_t bh = (size_t)batch * cfg->n_kv;
   const int G = cfg->n_heads / cfg->n_kv;
   unsigned char* ws = static_cast<unsigned char*>(workspace);
-  // decode state first: partials, then counters
+  int* dev_status = reinterpret_cast<int*>(ws);  // device status word (bounded waits, logit bound)
+  ws += kAlign;
+  // split-path state: partials, then counters
   float* part = reinterpret_cast<float*>(ws);
   ws += align_up(bh * plan.max_seg * G * (size_t)(cfg->head_dim + 2) * sizeof(float));
   int32_t* counters = reinterpret_cast<int32_t*>(ws);
   ws += align_up(bh * sizeof(int32_t));
   hba::QueryPos qp{seq_lens, scales, 0, 0.f};
   prof_begin(stream);
-  if (use_fused_decode(cfg, geo, bh)) {
+  const int path = decode_path(cfg, geo, bh, k_cache, k_rope_cache, v_cache);
+  if (path != kDecodeSplit) {
     hba::DecodeAttnParams dp{};
     dp.geo = geo;
+    dp.trace = g_trace;
+    dp.trace_ctas = g_trace_ctas;
     dp.qp = qp;
     dp.q = static_cast<const __nv_bfloat16*>(q);
     dp.q_gain = q_gain;
@@ -382,8 +409,17 @@ int hba_b200_decode(const hba_b200_config* cfg, int32_t batch, int32_t n_cap, co
     dp.lse = lse;
     dp.sel_idx = sel_idx;
     dp.sel_score = sel_score;
-    cudaError_t e = hba::launch_decode_fused(dp, static_cast<const __nv_bfloat16*>(summaries),
-                                             static_cast<const __nv_bfloat16*>(supers), cfg->head_dim, stream);
+    cudaError_t e;
+    if (path == kDecodeTc) {
+      e = cudaMemsetAsync(dev_status, 0, sizeof(int), stream);
+      if (e == cudaSuccess)
+        e = hba::launch_decode_tc(dp, static_cast<const __nv_bfloat16*>(summaries),
+                                  static_cast<const __nv_bfloat16*>(supers), k_gain,
+                                  dev_status, cfg->head_dim, stream);
+    } else {
+      e = hba::launch_decode_fused(dp, static_cast<const __nv_bfloat16*>(summaries),
+                                   static_cast<const __nv_bfloat16*>(supers), cfg->head_dim, stream);
+    }
     if (e != cudaSuccess) return cuda_status(e);
     prof_mark(stream);
     return HBA_B200_OK;

@@ -15,9 +15,13 @@
 //      16-byte loads in flight per lane; scores max_slot(qg . S) * scale;
 //   4. block-wide radix-select top-k (score desc, block index asc);
 //   5. union softmax over 128-key chunks [window | sinks | routed blocks],
-//      3-stage cp.async pipeline into 128-byte-swizzled tiles, each warp 16
-//      keys per chunk on m16n8k16 bf16 tensor-core tiles (the G heads are the
-//      16 rows), online softmax in the log2 domain;
+//      each warp 16 keys per chunk on m16n8k16 bf16 tensor-core tiles (the G
+//      heads are the 16 rows), online softmax in the log2 domain;
+// Steps 3 and 5 share one cp.async ring (5 stages of 32 KB for dh 64, 3 of
+// 64 KB for dh 128): summary pages, window chunks, the beam's child pages,
+// the sink chunk and the routed chunks stream through it in that order, so
+// ~128 KB stay in flight per CTA and the top-k runs while the window loads
+// are already landing.
 //   6. warps merge (max, sum, O); the CTA writes out, the natural-log LSE and
 //      the selected blocks.
 #include <climits>
@@ -31,12 +35,18 @@ namespace hba {
 
 constexpr int kFThreads = 256;
 constexpr int kFWarps = kFThreads / 32;
-constexpr int kFChunk = 128;  // keys per chunk: 8 warps x 16
-constexpr int kFStages = 3;
+constexpr int kFChunk = 128;  // keys per K/V chunk: 8 warps x 16
+
+// One ring stage holds a K/V chunk [2][128 keys][DH] or a page of summary rows.
+template <int DH>
+struct FusedCfg {
+  static constexpr int kStageBytes = 2 * kFChunk * DH * 2;  // 32 KB (dh 64) / 64 KB (dh 128)
+  static constexpr int kStages = DH == 64 ? 5 : 3;
+};
 
 template <int DH>
 struct FusedSmem {
-  __nv_bfloat16 kv[kFStages][2][kFChunk * DH];  // [stage][K|V] swizzled rows of DH bf16
+  alignas(128) unsigned char ring[FusedCfg<DH>::kStages][FusedCfg<DH>::kStageBytes];
   __nv_bfloat16 qc[16][DH + 8];
   __nv_bfloat16 qr[16][DH + 8];
   float qg[DH];
@@ -49,7 +59,7 @@ struct FusedSmem {
 };
 
 template <int DH>
-struct FusedCombine {  // overlays the K/V stages after the chunk loop
+struct FusedCombine {  // overlays the ring after the item loop
   float m[kFWarps][16];
   float l[kFWarps][16];
   float o[kFWarps][16][DH];
@@ -61,9 +71,23 @@ HBA_DEVICE uint32_t swz(int row, int piece) {
   return (uint32_t)(row * DH * 2 + ((piece ^ (row & 7)) << 4));
 }
 
+HBA_DEVICE void cp_async_wait_dyn(int pending) {
+  switch (pending) {
+    case 0: cp_async_wait<0>(); break;
+    case 1: cp_async_wait<1>(); break;
+    case 2: cp_async_wait<2>(); break;
+    case 3: cp_async_wait<3>(); break;
+    default: cp_async_wait<4>(); break;
+  }
+}
+
+enum FusedItem : int { kPageScore = 0, kPageChild = 1, kChunkWindow = 2, kChunkSink = 3, kChunkRouted = 4 };
+
 template <int DH, int VPL>
 __global__ void __launch_bounds__(kFThreads, 1) decode_fused_kernel(DecodeAttnParams p, const __nv_bfloat16* summ,
                                                                     const __nv_bfloat16* supers) {
+  using FC = FusedCfg<DH>;
+  constexpr int NS = FC::kStages;
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   FusedSmem<DH>& sm = *reinterpret_cast<FusedSmem<DH>*>(smem_raw);
   const Geom& geo = p.geo;
@@ -74,6 +98,7 @@ __global__ void __launch_bounds__(kFThreads, 1) decode_fused_kernel(DecodeAttnPa
   const int G = geo.G;
   const int bg = blockIdx.x;
   const int b = bg / geo.Hkv, g = bg % geo.Hkv;
+  const bool hier = geo.hier != 0;
 
   const int nctx = p.qp.seq_lens[b];
   const float scale = p.qp.scales[b];
@@ -83,52 +108,119 @@ __global__ void __launch_bounds__(kFThreads, 1) decode_fused_kernel(DecodeAttnPa
   const int bmax = ok ? min(last_candidate(pos, geo.W, geo.Bk), nb - 1) : 0;
   int kfinal = min(geo.K, nb);
   const int ns = (nb + geo.F - 1) / geo.F;
-  if (geo.hier) kfinal = min(kfinal, min(geo.beam, ns) * geo.F);
+  if (hier) kfinal = min(kfinal, min(geo.beam, ns) * geo.F);
   const int w0 = max(geo.S, pos - geo.W + 1);
   const int nw = ok ? max(0, pos - w0 + 1) : 0;
   const int nsink = ok ? min(geo.S, pos + 1) : 0;
-  const int NCw = (nw + kFChunk - 1) / kFChunk;
-  const int NCs = nsink > 0 ? 1 : 0;
   const size_t tok_stride = (size_t)geo.Hkv * DH;
   const size_t head_base = ((size_t)b * geo.n_cap) * tok_stride + (size_t)g * DH;
   const __nv_bfloat16* kbase = p.k + head_base;
   const __nv_bfloat16* krbase = p.kr + head_base;
   const __nv_bfloat16* vbase = p.v + head_base;
-  int nsel = 0;  // valid routed picks (set after the top-k)
+  const int row_bytes = geo.m * DH * 2;                 // one summary row
+  const int row_pieces = row_bytes / 16;
+  const int PB = FC::kStageBytes / row_bytes;           // summary rows per page
+  const __nv_bfloat16* summ_bg = summ + (size_t)bg * geo.nb_cap * geo.m * DH;
+  const __nv_bfloat16* sup_bg = hier ? supers + (size_t)bg * geo.ns_cap * geo.m * DH : nullptr;
 
-  auto chunk_rows = [&](int c) -> int {
-    if (c < NCw) return min(kFChunk, nw - c * kFChunk);
-    if (c < NCw + NCs) return nsink;
-    return max(0, min(kFChunk, nsel * geo.Bk - (c - NCw - NCs) * kFChunk));
+  // ---- item counts (later ones become known at the top-k points) ----
+  int R1 = 0, id_lo = 1;  // first scoring phase: candidate blocks (flat) or supers (hier)
+  if (!hier) {
+    R1 = max(0, bmax);
+  } else if (bmax >= 1) {
+    id_lo = (geo.F == 1) ? 1 : 0;
+    R1 = bmax / geo.F - id_lo + 1;
+  }
+  const int P1 = (R1 + PB - 1) / PB;
+  const int NCw = (nw + kFChunk - 1) / kFChunk;
+  const int NCs = nsink > 0 ? 1 : 0;
+  int R2 = 0, P2 = 0;    // hier: children of the selected supers
+  int nsel = 0, NCr = 0;
+  bool phase1_done = false, final_done = false;
+
+  // item order: [phase-1 pages | window | child pages | sink | routed]
+  auto kind_of = [&](int it, int& idx) -> int {
+    if (it < P1) { idx = it; return kPageScore; }
+    it -= P1;
+    if (it < NCw) { idx = it; return kChunkWindow; }
+    it -= NCw;
+    if (it < P2) { idx = it; return kPageChild; }
+    it -= P2;
+    if (it < NCs) { idx = it; return kChunkSink; }
+    idx = it - NCs;
+    return kChunkRouted;
   };
-  auto row_token = [&](int c, int r) -> int {
-    if (c < NCw) return w0 + c * kFChunk + r;
-    if (c < NCw + NCs) return r;
-    const int key = (c - NCw - NCs) * kFChunk + r;
-    return sm.blocks[key / geo.Bk] * geo.Bk + key % geo.Bk;
+  auto issuable = [&](int kind) -> bool {
+    if (kind == kPageChild) return phase1_done;
+    if (kind == kChunkSink || kind == kChunkRouted) return final_done;  // item positions need P2 (hier)
+    return true;
   };
-  auto issue = [&](int c, int stage) {
-    const int cnt = chunk_rows(c);
-    if (cnt > 0) {
-      const __nv_bfloat16* ksrc = c < NCw ? krbase : kbase;
-      unsigned char* kt = reinterpret_cast<unsigned char*>(sm.kv[stage][0]);
-      unsigned char* vt = reinterpret_cast<unsigned char*>(sm.kv[stage][1]);
+  auto child_id = [&](int j) -> int {
+    int si = 0;
+    while (si < 31 && j >= sm.sup_off[si] + sm.sup_cnt[si]) ++si;
+    return sm.sup_lo[si] + (j - sm.sup_off[si]);
+  };
+  auto chunk_rows = [&](int kind, int idx) -> int {
+    if (kind == kChunkWindow) return min(kFChunk, nw - idx * kFChunk);
+    if (kind == kChunkSink) return nsink;
+    return max(0, min(kFChunk, nsel * geo.Bk - idx * kFChunk));
+  };
+  auto page_rows = [&](int kind, int idx) -> int {
+    const int R = kind == kPageScore ? R1 : R2;
+    return min(PB, R - idx * PB);
+  };
+  auto issue = [&](int it, int stage) {
+    int idx;
+    const int kind = kind_of(it, idx);
+    unsigned char* st = sm.ring[stage];
+    if (kind == kPageScore || kind == kPageChild) {
+      const int rows = page_rows(kind, idx);
+      for (int e = tid; e < rows * row_pieces; e += kFThreads) {
+        const int r = e / row_pieces, pc = e % row_pieces;
+        const int j = idx * PB + r;
+        const __nv_bfloat16* src;
+        if (kind == kPageScore) src = (hier ? sup_bg : summ_bg) + (size_t)(id_lo + j) * geo.m * DH;
+        else src = summ_bg + (size_t)child_id(j) * geo.m * DH;
+        cp_async16(st + r * row_bytes + pc * 16, src + pc * 8);
+      }
+    } else {
+      const int cnt = chunk_rows(kind, idx);
+      const __nv_bfloat16* ksrc = kind == kChunkWindow ? krbase : kbase;
       for (int e = tid; e < kFChunk * PIECES; e += kFThreads) {
         const int r = e / PIECES, pc = e % PIECES;
         const bool valid = r < cnt;
-        const size_t off = (size_t)(valid ? row_token(c, r) : 0) * tok_stride + pc * 8;
-        cp_async16_zfill(kt + swz<DH>(r, pc), ksrc + off, valid);
-        cp_async16_zfill(vt + swz<DH>(r, pc), vbase + off, valid);
+        int tok = 0;
+        if (valid) {
+          if (kind == kChunkWindow) tok = w0 + idx * kFChunk + r;
+          else if (kind == kChunkSink) tok = r;
+          else {
+            const int key = idx * kFChunk + r;
+            tok = sm.blocks[key / geo.Bk] * geo.Bk + key % geo.Bk;
+          }
+        }
+        const size_t off = (size_t)tok * tok_stride + pc * 8;
+        cp_async16_zfill(st + swz<DH>(r, pc), ksrc + off, valid);
+        cp_async16_zfill(st + kFChunk * DH * 2 + swz<DH>(r, pc), vbase + off, valid);
       }
     }
     cp_async_commit();
   };
 
-  // ---- 1. window / sink chunks first ----
-  const int early = min(kFStages - 1, NCw + NCs);
-  for (int s = 0; s < early; ++s) issue(s, s);
+  int issued = 0;  // items issued (one cp.async group each, in order)
+  auto total_items = [&]() { return P1 + NCw + P2 + NCs + NCr; };
+  auto pump = [&](int upto) {  // issue items < upto that are issuable, in order
+    const int lim = min(upto, final_done ? total_items() : (phase1_done ? P1 + NCw + P2 : P1 + NCw));
+    while (issued < lim) {
+      int idx;
+      if (!issuable(kind_of(issued, idx))) break;
+      issue(issued, issued % NS);
+      ++issued;
+    }
+  };
 
-  // ---- 2. query prologue ----
+  pump(NS - 1);  // summary pages and window chunks first
+
+  // ---- query prologue: qc, qr (RoPE at pos) and the routing query qg ----
   for (int h = warp; h < 16; h += kFWarps) {
     float v[PER], r[PER];
     if (h < G && ok) {
@@ -167,32 +259,22 @@ __global__ void __launch_bounds__(kFThreads, 1) decode_fused_kernel(DecodeAttnPa
   }
   __syncthreads();
 
-  // ---- 3./4. scoring and top-k ----
-  const size_t row_elems = (size_t)geo.m * DH;
-  const int nvec = geo.m * DH / 8;
-  SummaryLoads<DH, VPL, kFWarps> ld;
-  constexpr int GROUP = kFWarps * SummaryLoads<DH, VPL, kFWarps>::U;
-  auto score_range = [&](const __nv_bfloat16* base, int R, auto id_of) {
-    for (int rb = 0; rb < R; rb += GROUP) {
-      ld.load(base, row_elems, nvec, rb, R, id_of);
-      ld.score(sm.qg, nvec, rb, R, scale, id_of, sm.sc, sm.id);
+  // ---- top-k points ----
+  auto final_topk = [&](int R) {
+    nsel = block_topk<kFThreads>(sm.sc, sm.id, R, kfinal, sm.ts);
+    if (tid < 32) {
+      const bool valid = tid < nsel;
+      sm.blocks[tid] = valid ? sm.ts.sel_idx[tid] : -1;
+      if (p.sel_idx != nullptr && tid < geo.K) {
+        p.sel_idx[(size_t)bg * geo.K + tid] = valid ? sm.ts.sel_idx[tid] : -1;
+        p.sel_score[(size_t)bg * geo.K + tid] = valid ? sm.ts.sel_score[tid] : neg_inf();
+      }
     }
     __syncthreads();
+    NCr = (nsel * geo.Bk + kFChunk - 1) / kFChunk;
+    final_done = true;
   };
-  const __nv_bfloat16* summ_bg = summ + (size_t)bg * geo.nb_cap * row_elems;
-  if (!geo.hier) {
-    const int R = max(0, bmax);  // candidates 1..bmax
-    score_range(summ_bg, R, [&](int r) { return 1 + r; });
-    nsel = block_topk<kFThreads>(sm.sc, sm.id, R, kfinal, sm.ts);
-  } else {
-    const int F = geo.F;
-    int R1 = 0, s_lo = 0;
-    if (bmax >= 1) {
-      s_lo = (F == 1) ? 1 : 0;
-      R1 = bmax / F - s_lo + 1;
-    }
-    const __nv_bfloat16* sup_bg = supers + (size_t)bg * geo.ns_cap * row_elems;
-    score_range(sup_bg, R1, [&](int r) { return s_lo + r; });
+  auto super_topk = [&]() {
     const int b_eff = min(geo.beam, ns);
     const int nsup = block_topk<kFThreads>(sm.sc, sm.id, R1, b_eff, sm.ts);
     if (warp == 0) {
@@ -200,8 +282,8 @@ __global__ void __launch_bounds__(kFThreads, 1) decode_fused_kernel(DecodeAttnPa
       int lo = 0, cnt = 0;
       if (valid) {
         const int sidx = sm.ts.sel_idx[lane];
-        lo = max(1, sidx * F);
-        cnt = max(0, min(bmax, sidx * F + F - 1) - lo + 1);
+        lo = max(1, sidx * geo.F);
+        cnt = max(0, min(bmax, sidx * geo.F + geo.F - 1) - lo + 1);
       }
       int incl = cnt;
 #pragma unroll
@@ -215,129 +297,161 @@ __global__ void __launch_bounds__(kFThreads, 1) decode_fused_kernel(DecodeAttnPa
       if (lane == 31) sm.n_children = incl;
     }
     __syncthreads();
-    const int R2 = sm.n_children;
-    score_range(summ_bg, R2, [&](int r) {
-      int si = 0;
-      while (si < 31 && r >= sm.sup_off[si] + sm.sup_cnt[si]) ++si;
-      return sm.sup_lo[si] + (r - sm.sup_off[si]);
-    });
-    nsel = block_topk<kFThreads>(sm.sc, sm.id, R2, kfinal, sm.ts);
-  }
-  if (tid < 32) {
-    const bool valid = tid < nsel;
-    sm.blocks[tid] = valid ? sm.ts.sel_idx[tid] : -1;
-    if (p.sel_idx != nullptr && tid < geo.K) {
-      p.sel_idx[(size_t)bg * geo.K + tid] = valid ? sm.ts.sel_idx[tid] : -1;
-      p.sel_score[(size_t)bg * geo.K + tid] = valid ? sm.ts.sel_score[tid] : neg_inf();
+    R2 = sm.n_children;
+    P2 = (R2 + PB - 1) / PB;
+    phase1_done = true;
+  };
+  if (P1 == 0) {
+    if (!hier) {
+      final_topk(0);
+    } else {
+      super_topk();
+      if (P2 == 0) final_topk(0);
     }
   }
-  __syncthreads();
 
-  // ---- 5. union softmax over the chunks ----
-  const int NCr = (nsel * geo.Bk + kFChunk - 1) / kFChunk;
-  const int NC = NCw + NCs + NCr;
-  for (int s = early; s < kFStages - 1; ++s) {
-    if (s < NC) issue(s, s);
-    else cp_async_commit();
-  }
   float m0 = neg_inf(), m1 = neg_inf(), l0 = 0.f, l1 = 0.f;
   float o[DH / 8][4];
 #pragma unroll
   for (int n = 0; n < DH / 8; ++n) o[n][0] = o[n][1] = o[n][2] = o[n][3] = 0.f;
   const float sl2 = scale * kLog2e;
   const int key0 = warp * 16;
+  const int nvec = row_pieces;
+  constexpr int LPS = DH / 8;
 
-  for (int c = 0; c < NC; ++c) {
-    const int stage = c % kFStages;
-    const int j = c + kFStages - 1;
-    if (j < NC) issue(j, j % kFStages);
-    else cp_async_commit();
-    cp_async_wait<kFStages - 1>();
+  for (int it = 0; it < total_items(); ++it) {
+    pump(it + NS);           // keep NS - 1 items ahead
+    if (issued <= it) pump(it + 1);
+    cp_async_wait_dyn(issued - it - 1);
     __syncthreads();
-    const int cnt = chunk_rows(c);
-    if (key0 < cnt) {
-      const unsigned char* kt = reinterpret_cast<const unsigned char*>(sm.kv[stage][0]);
-      const unsigned char* vt = reinterpret_cast<const unsigned char*>(sm.kv[stage][1]);
-      const __nv_bfloat16(*Q)[DH + 8] = c < NCw ? sm.qr : sm.qc;
-      float s[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+    const int stage = it % NS;
+    int idx;
+    const int kind = kind_of(it, idx);
+    const unsigned char* st = sm.ring[stage];
+    if (kind == kPageScore || kind == kPageChild) {
+      // ---- score a page of summary rows from shared memory ----
+      const int rows = page_rows(kind, idx);
+      for (int r = warp; r < rows; r += kFWarps) {
+        const int j = idx * PB + r;
+        float best = neg_inf();
 #pragma unroll
-      for (int kd = 0; kd < DH; kd += 16) {
-        uint32_t a[4];
-        a[0] = *reinterpret_cast<const uint32_t*>(&Q[gid][kd + tig * 2]);
-        a[1] = *reinterpret_cast<const uint32_t*>(&Q[gid + 8][kd + tig * 2]);
-        a[2] = *reinterpret_cast<const uint32_t*>(&Q[gid][kd + 8 + tig * 2]);
-        a[3] = *reinterpret_cast<const uint32_t*>(&Q[gid + 8][kd + 8 + tig * 2]);
+        for (int v = 0; v < VPL; ++v) {
+          const int vv = lane + 32 * v;
+          float part = 0.f;
+          if (vv < nvec) {
+            float f[8];
+            unpack8(*reinterpret_cast<const uint4*>(st + r * row_bytes + vv * 16), f);
+            const int d0 = (vv * 8) % DH;
+#pragma unroll
+            for (int jj = 0; jj < 8; ++jj) part = fmaf(f[jj], sm.qg[d0 + jj], part);
+          }
+#pragma unroll
+          for (int ox = 1; ox < LPS; ox <<= 1) part += __shfl_xor_sync(0xffffffffu, part, ox);
+          if (vv < nvec) best = fmaxf(best, part);
+        }
+        best = warp_max(best);
+        if (lane == 0) {
+          sm.sc[j] = best * scale;
+          sm.id[j] = kind == kPageScore ? id_lo + j : child_id(j);
+        }
+      }
+    } else {
+      const int cnt = chunk_rows(kind, idx);
+      if (key0 < cnt) {
+        const unsigned char* kt = st;
+        const unsigned char* vt = st + kFChunk * DH * 2;
+        const __nv_bfloat16(*Q)[DH + 8] = kind == kChunkWindow ? sm.qr : sm.qc;
+        float s[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+#pragma unroll
+        for (int kd = 0; kd < DH; kd += 16) {
+          uint32_t a[4];
+          a[0] = *reinterpret_cast<const uint32_t*>(&Q[gid][kd + tig * 2]);
+          a[1] = *reinterpret_cast<const uint32_t*>(&Q[gid + 8][kd + tig * 2]);
+          a[2] = *reinterpret_cast<const uint32_t*>(&Q[gid][kd + 8 + tig * 2]);
+          a[3] = *reinterpret_cast<const uint32_t*>(&Q[gid + 8][kd + 8 + tig * 2]);
+#pragma unroll
+          for (int jj = 0; jj < 2; ++jj) {
+            const int row = key0 + 8 * jj + gid;
+            uint32_t bb[2];
+            bb[0] = *reinterpret_cast<const uint32_t*>(kt + swz<DH>(row, kd / 8) + tig * 4);
+            bb[1] = *reinterpret_cast<const uint32_t*>(kt + swz<DH>(row, kd / 8 + 1) + tig * 4);
+            mma_bf16_16816(s[jj], a, bb);
+          }
+        }
+#pragma unroll
+        for (int jj = 0; jj < 2; ++jj)
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const int key = key0 + 8 * jj + tig * 2 + (e & 1);
+            s[jj][e] = key < cnt ? s[jj][e] * sl2 : neg_inf();
+          }
+        float mx0 = fmaxf(fmaxf(s[0][0], s[0][1]), fmaxf(s[1][0], s[1][1]));
+        float mx1 = fmaxf(fmaxf(s[0][2], s[0][3]), fmaxf(s[1][2], s[1][3]));
+        mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 1));
+        mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 2));
+        mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 1));
+        mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 2));
+        const float mn0 = fmaxf(m0, mx0), mn1 = fmaxf(m1, mx1);
+        const float mu0 = (mn0 == neg_inf()) ? 0.f : mn0;
+        const float mu1 = (mn1 == neg_inf()) ? 0.f : mn1;
+        const float al0 = exp2f(m0 - mu0), al1 = exp2f(m1 - mu1);
+        m0 = mn0;
+        m1 = mn1;
+        float pr[2][4];
 #pragma unroll
         for (int jj = 0; jj < 2; ++jj) {
-          const int row = key0 + 8 * jj + gid;
-          uint32_t bb[2];
-          bb[0] = *reinterpret_cast<const uint32_t*>(kt + swz<DH>(row, kd / 8) + tig * 4);
-          bb[1] = *reinterpret_cast<const uint32_t*>(kt + swz<DH>(row, kd / 8 + 1) + tig * 4);
-          mma_bf16_16816(s[jj], a, bb);
+          pr[jj][0] = exp2f(s[jj][0] - mu0);
+          pr[jj][1] = exp2f(s[jj][1] - mu0);
+          pr[jj][2] = exp2f(s[jj][2] - mu1);
+          pr[jj][3] = exp2f(s[jj][3] - mu1);
         }
-      }
+        l0 = l0 * al0 + pr[0][0] + pr[0][1] + pr[1][0] + pr[1][1];
+        l1 = l1 * al1 + pr[0][2] + pr[0][3] + pr[1][2] + pr[1][3];
 #pragma unroll
-      for (int jj = 0; jj < 2; ++jj)
-#pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          const int key = key0 + 8 * jj + tig * 2 + (e & 1);
-          s[jj][e] = key < cnt ? s[jj][e] * sl2 : neg_inf();
+        for (int n = 0; n < DH / 8; ++n) {
+          o[n][0] *= al0;
+          o[n][1] *= al0;
+          o[n][2] *= al1;
+          o[n][3] *= al1;
         }
-      float mx0 = fmaxf(fmaxf(s[0][0], s[0][1]), fmaxf(s[1][0], s[1][1]));
-      float mx1 = fmaxf(fmaxf(s[0][2], s[0][3]), fmaxf(s[1][2], s[1][3]));
-      mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 1));
-      mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 2));
-      mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 1));
-      mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 2));
-      const float mn0 = fmaxf(m0, mx0), mn1 = fmaxf(m1, mx1);
-      const float mu0 = (mn0 == neg_inf()) ? 0.f : mn0;
-      const float mu1 = (mn1 == neg_inf()) ? 0.f : mn1;
-      const float al0 = exp2f(m0 - mu0), al1 = exp2f(m1 - mu1);
-      m0 = mn0;
-      m1 = mn1;
-      float pr[2][4];
+        uint32_t pa[4];
+        pa[0] = pack_bf16x2(pr[0][0], pr[0][1]);
+        pa[1] = pack_bf16x2(pr[0][2], pr[0][3]);
+        pa[2] = pack_bf16x2(pr[1][0], pr[1][1]);
+        pa[3] = pack_bf16x2(pr[1][2], pr[1][3]);
+        const int vrow = key0 + (lane & 7) + ((lane >> 3) & 1) * 8;
+        const int vpiece = lane >> 4;
 #pragma unroll
-      for (int jj = 0; jj < 2; ++jj) {
-        pr[jj][0] = exp2f(s[jj][0] - mu0);
-        pr[jj][1] = exp2f(s[jj][1] - mu0);
-        pr[jj][2] = exp2f(s[jj][2] - mu1);
-        pr[jj][3] = exp2f(s[jj][3] - mu1);
-      }
-      l0 = l0 * al0 + pr[0][0] + pr[0][1] + pr[1][0] + pr[1][1];
-      l1 = l1 * al1 + pr[0][2] + pr[0][3] + pr[1][2] + pr[1][3];
-#pragma unroll
-      for (int n = 0; n < DH / 8; ++n) {
-        o[n][0] *= al0;
-        o[n][1] *= al0;
-        o[n][2] *= al1;
-        o[n][3] *= al1;
-      }
-      uint32_t pa[4];
-      pa[0] = pack_bf16x2(pr[0][0], pr[0][1]);
-      pa[1] = pack_bf16x2(pr[0][2], pr[0][3]);
-      pa[2] = pack_bf16x2(pr[1][0], pr[1][1]);
-      pa[3] = pack_bf16x2(pr[1][2], pr[1][3]);
-      const int vrow = key0 + (lane & 7) + ((lane >> 3) & 1) * 8;
-      const int vpiece = lane >> 4;
-#pragma unroll
-      for (int nd = 0; nd < DH; nd += 16) {
-        uint32_t bv[4];
-        ldmatrix_x4_trans(bv, vt + swz<DH>(vrow, nd / 8 + vpiece));
-        mma_bf16_16816(o[nd / 8], pa, bv);
-        mma_bf16_16816(o[nd / 8 + 1], pa, bv + 2);
+        for (int nd = 0; nd < DH; nd += 16) {
+          uint32_t bv[4];
+          ldmatrix_x4_trans(bv, vt + swz<DH>(vrow, nd / 8 + vpiece));
+          mma_bf16_16816(o[nd / 8], pa, bv);
+          mma_bf16_16816(o[nd / 8 + 1], pa, bv + 2);
+        }
       }
     }
     __syncthreads();
+    // ---- top-k points (after the page that completes a scoring phase) ----
+    if (kind == kPageScore && idx == P1 - 1) {
+      if (!hier) {
+        final_topk(R1);
+      } else {
+        super_topk();
+        if (P2 == 0) final_topk(0);
+      }
+    } else if (kind == kPageChild && idx == P2 - 1) {
+      final_topk(R2);
+    }
   }
   cp_async_wait<0>();
 
-  // ---- 6. merge the 8 warps, write the output ----
+  // ---- merge the 8 warps, write the output ----
   l0 += __shfl_xor_sync(0xffffffffu, l0, 1);
   l0 += __shfl_xor_sync(0xffffffffu, l0, 2);
   l1 += __shfl_xor_sync(0xffffffffu, l1, 1);
   l1 += __shfl_xor_sync(0xffffffffu, l1, 2);
   __syncthreads();
-  FusedCombine<DH>& cb = *reinterpret_cast<FusedCombine<DH>*>(&sm.kv[0][0][0]);
+  FusedCombine<DH>& cb = *reinterpret_cast<FusedCombine<DH>*>(&sm.ring[0][0]);
   if (tig == 0) {
     cb.m[warp][gid] = m0;
     cb.m[warp][gid + 8] = m1;

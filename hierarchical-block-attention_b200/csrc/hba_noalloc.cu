@@ -53,7 +53,8 @@ cudaError_t scratch_address(void** out) {
 extern "C" {
 
 int hba_b200_decode_noalloc(const hba_b200_config* cfg, int32_t batch, int32_t n_cap, const int32_t* seq_lens,
-                            const float* scales, const void* q, const float* q_gain, const void* k_cache,
+                            const float* scales, const void* q, const float* q_gain, const float* k_gain,
+                            const void* k_cache,
                             const void* k_rope_cache, const void* v_cache, const void* summaries,
                             const void* supers, const float* cos, const float* sin, void* out, float* lse,
                             int32_t* sel_idx, float* sel_score, cudaStream_t stream) {
@@ -62,7 +63,8 @@ int hba_b200_decode_noalloc(const hba_b200_config* cfg, int32_t batch, int32_t n
   void* scratch = nullptr;
   const cudaError_t e = scratch_address(&scratch);
   if (e != cudaSuccess) return HBA_B200_ERR_CUDA;
-  return hba_b200_decode(cfg, batch, n_cap, seq_lens, scales, q, q_gain, k_cache, k_rope_cache, v_cache, summaries,
+  return hba_b200_decode(cfg, batch, n_cap, seq_lens, scales, q, q_gain, k_gain, k_cache, k_rope_cache, v_cache,
+                         summaries,
                          supers, cos, sin, out, lse, sel_idx, sel_score, scratch, kScratchBytes, stream);
 }
 

@@ -1,9 +1,10 @@
 // Block-wide top-k over up to kTopkMaxItems (score, index) pairs held in
 // shared memory, under the library's total order: higher score first, then
-// lower index.  Radix select: 32 bisection steps on the order-preserving
-// integer image of the score find the k-th largest score, ties at that score
-// are taken by ascending index, and the <= k survivors are ranked.  Cost
-// O(R/threads) per step with two barriers per step, independent of k.
+// lower index.  Radix select on the order-preserving 32-bit image of the
+// score: four passes of an 8-bit digit histogram (warp-aggregated shared
+// atomics) find the k-th largest key v; keys > v are taken, and the remaining
+// slots go to keys == v by ascending index (a scan is needed only when there
+// are more such ties than free slots).  The <= 32 survivors are ranked.
 #pragma once
 
 #include <climits>
@@ -21,70 +22,106 @@ HBA_DEVICE uint32_t order_key(float f) {
 }
 
 struct TopkScratch {
-  int warp_cnt[2][32];
+  int hist[256];
+  int digit;
+  int k_rem;
+  int ties;
   int n_sel;
   int sel_idx[32];
   float sel_score[32];
 };
 
 // Every thread of the block must call this (contains barriers).  Writes the
-// selected entries, best first, to out_idx/out_score[0..k) (-1 / -inf padding)
-// of `ts`, and returns the number of valid picks.  NT = blockDim.x.
+// selected entries, best first, to ts.sel_idx / ts.sel_score[0..n) and
+// returns n = min(k, R, 32).  NT = blockDim.x.
 template <int NT>
 HBA_DEVICE int block_topk(const float* __restrict__ sc, const int* __restrict__ id, int R, int k,
                           TopkScratch& ts) {
-  constexpr int NW = NT / 32;
   constexpr int E = (kTopkMaxItems + NT - 1) / NT;
-  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int tid = threadIdx.x, lane = tid & 31;
+  if (k > 32) k = 32;
+  const int take = min(k, R);
+  if (take <= 0) {
+    if (tid == 0) ts.n_sel = 0;
+    __syncthreads();
+    return 0;
+  }
   uint32_t key[E];
 #pragma unroll
   for (int e = 0; e < E; ++e) {
     const int j = tid + e * NT;
     key[e] = j < R ? order_key(sc[j]) : 0u;
   }
-  auto block_count = [&](uint32_t thr, bool strict, int buf) -> int {
-    int c = 0;
+  uint32_t prefix = 0, pmask = 0;
+  int k_rem = take;
+  for (int pass = 0; pass < 4; ++pass) {
+    const int shift = 24 - 8 * pass;
+    for (int i = tid; i < 256; i += NT) ts.hist[i] = 0;
+    __syncthreads();
 #pragma unroll
     for (int e = 0; e < E; ++e) {
       const int j = tid + e * NT;
-      if (j < R) c += strict ? (key[e] > thr) : (key[e] >= thr);
+      const bool in = j < R && (key[e] & pmask) == prefix;
+      const unsigned act = __ballot_sync(0xffffffffu, in);
+      if (in) {
+        const int bin = (key[e] >> shift) & 0xFF;
+        const unsigned peers = __match_any_sync(act, bin);
+        if ((__ffs(peers) - 1) == lane) atomicAdd(&ts.hist[bin], __popc(peers));
+      }
     }
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) c += __shfl_xor_sync(0xffffffffu, c, o);
-    if (lane == 0) ts.warp_cnt[buf][warp] = c;
     __syncthreads();
-    int t = 0;
+    if (tid < 32) {
+      // lane l owns bins [255 - 8l - 7, 255 - 8l], scanned from the top
+      int c[8], tot = 0;
 #pragma unroll
-    for (int w = 0; w < NW; ++w) t += ts.warp_cnt[buf][w];
-    return t;
-  };
-  if (k > 32) k = 32;
-  int take = min(k, R);
+      for (int i = 0; i < 8; ++i) {
+        c[i] = ts.hist[255 - 8 * lane - i];
+        tot += c[i];
+      }
+      int incl = tot;  // inclusive prefix over lanes = elements in bins above and at this lane's range
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const int nv = __shfl_up_sync(0xffffffffu, incl, o);
+        if (lane >= o) incl += nv;
+      }
+      const int before = incl - tot;  // elements in strictly higher bins
+      if (before < k_rem && k_rem <= incl) {
+        int acc = before;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          if (acc < k_rem && k_rem <= acc + c[i]) {
+            ts.digit = 255 - 8 * lane - i;
+            ts.k_rem = k_rem - acc;
+            ts.ties = c[i];
+          }
+          acc += c[i];
+        }
+      }
+    }
+    __syncthreads();
+    prefix |= (uint32_t)ts.digit << shift;
+    pmask |= 0xFFu << shift;
+    k_rem = ts.k_rem;
+  }
+  const uint32_t v = prefix;  // the take-th largest key
+  const int need_ties = k_rem;
+  const bool all_ties = ts.ties == need_ties;
   if (tid == 0) ts.n_sel = 0;
-  if (take <= 0) {
-    __syncthreads();
-    return 0;
-  }
-  // largest threshold v with count(key >= v) >= take  ==  the take-th largest key
-  uint32_t v = 0;
-  for (int bit = 31; bit >= 0; --bit) {
-    const uint32_t cand = v | (1u << bit);
-    if (block_count(cand, false, bit & 1) >= take) v = cand;
-  }
-  const int greater = block_count(v, true, 1);  // the last bisection step used buffer 0
-  const int need_ties = take - greater;  // ties at v taken by ascending index
   __syncthreads();
-  // compact: all keys > v, and ties at v whose index rank among ties < need_ties
 #pragma unroll
   for (int e = 0; e < E; ++e) {
     const int j = tid + e * NT;
     if (j < R) {
       bool pick = key[e] > v;
       if (!pick && key[e] == v) {
-        int before = 0;  // ties at v with a lower index (ties are rare: linear scan)
-        for (int i = 0; i < R; ++i)
-          if (order_key(sc[i]) == v && id[i] < id[j]) ++before;
-        pick = before < need_ties;
+        if (all_ties) {
+          pick = true;
+        } else {  // genuine ties at the boundary: keep the lowest indices
+          int before = 0;
+          for (int i = 0; i < R; ++i)
+            if (order_key(sc[i]) == v && id[i] < id[j]) ++before;
+          pick = before < need_ties;
+        }
       }
       if (pick) {
         const int slot = atomicAdd(&ts.n_sel, 1);
@@ -93,7 +130,6 @@ HBA_DEVICE int block_topk(const float* __restrict__ sc, const int* __restrict__ 
     }
   }
   __syncthreads();
-  // rank the survivors (<= 32) by (score desc, index asc)
   const int n = ts.n_sel;
   int my_pos = -1, my_id = 0;
   float my_s = 0.f;

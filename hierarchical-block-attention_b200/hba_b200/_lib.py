@@ -52,12 +52,13 @@ SIGNATURES = {
                                           _P, _P, _P]),
     "hba_b200_decode_workspace_size": (_SZ, [_CFG, _I32, _I32]),
     "hba_b200_decode": (ctypes.c_int, [_CFG, _I32, _I32, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P,
-                                       _P, _P, _P, _SZ, _P]),
+                                       _P, _P, _P, _P, _SZ, _P]),
     "hba_b200_decode_noalloc": (ctypes.c_int, [_CFG, _I32, _I32, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P,
-                                               _P, _P, _P, _P]),
+                                               _P, _P, _P, _P, _P]),
     "hba_b200_prefill_workspace_size": (_SZ, [_CFG, _I32, _I32]),
     "hba_b200_set_profile_events": (ctypes.c_int, [ctypes.POINTER(ctypes.c_void_p), _I32]),
     "hba_b200_profile_events_recorded": (ctypes.c_int, []),
+    "hba_b200_set_debug_trace": (ctypes.c_int, [_P, _I64]),
     "hba_b200_prefill": (ctypes.c_int, [_CFG, _I32, _I32, _F, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P,
                                         _P, _P, _SZ, _P]),
 }

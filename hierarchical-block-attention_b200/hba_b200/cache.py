@@ -119,7 +119,7 @@ class HBADecodeCache:
         """Allocation-free decode on preallocated bf16 q/out (graph-capturable)."""
         st = _lib.load().hba_b200_decode(
             ctypes.byref(self.c), self.B, self.n_cap, ptr(self.lens), ptr(self.scales), ptr(qb), ptr(self.q_gain),
-            ptr(self.k), ptr(self.kr), ptr(self.v), ptr(self.summaries), ptr(self.supers), ptr(self.cos),
+            ptr(self.k_gain), ptr(self.k), ptr(self.kr), ptr(self.v), ptr(self.summaries), ptr(self.supers), ptr(self.cos),
             ptr(self.sin), ptr(out),
             ptr(lse), ptr(sel_idx), ptr(sel_score), ptr(self.workspace), self.ws_bytes,
             stream if stream is not None else stream_of(self.device))

@@ -120,7 +120,8 @@ size_t hba_b200_decode_workspace_size(const hba_b200_config* cfg, int32_t batch,
  * scan, or the two-level beam over `supers` when cfg->hier).
  *   seq_lens:  [batch] int32 device, 1 <= seq_lens[b] <= n_cap
  *   scales:    [batch] fp32 device, union logit scale (content scale x tau(n))
- *   q:         [batch, Hq, dh] bf16 raw query;  q_gain: [Hq] fp32
+ *   q:         [batch, Hq, dh] bf16 raw query;  q_gain: [Hq], k_gain: [Hkv] fp32
+ *              (the QKNorm gains; k_gain bounds the logits of the tensor-core path)
  *   k_cache, v_cache: [batch, n_cap, Hkv, dh] bf16 (keys QKNorm'd, NoPE)
  *   k_rope_cache: [batch, n_cap, Hkv, dh] bf16, the same keys RoPE'd at their
  *              positions (hba_b200_append_kv writes both); the window reads it
@@ -135,7 +136,8 @@ size_t hba_b200_decode_workspace_size(const hba_b200_config* cfg, int32_t batch,
  * hierarchical (:690-693, hier_select :217-246).
  */
 int hba_b200_decode(const hba_b200_config* cfg, int32_t batch, int32_t n_cap, const int32_t* seq_lens,
-                    const float* scales, const void* q, const float* q_gain, const void* k_cache,
+                    const float* scales, const void* q, const float* q_gain, const float* k_gain,
+                    const void* k_cache,
                     const void* k_rope_cache, const void* v_cache, const void* summaries, const void* supers,
                     const float* cos, const float* sin, void* out, float* lse, int32_t* sel_idx,
                     float* sel_score, void* workspace, size_t workspace_bytes, cudaStream_t stream);
@@ -154,7 +156,8 @@ int hba_b200_decode(const hba_b200_config* cfg, int32_t batch, int32_t n_cap, co
  * No counterpart in the reference.
  */
 int hba_b200_decode_noalloc(const hba_b200_config* cfg, int32_t batch, int32_t n_cap, const int32_t* seq_lens,
-                            const float* scales, const void* q, const float* q_gain, const void* k_cache,
+                            const float* scales, const void* q, const float* q_gain, const float* k_gain,
+                            const void* k_cache,
                             const void* k_rope_cache, const void* v_cache, const void* summaries,
                             const void* supers, const float* cos, const float* sin, void* out, float* lse,
                             int32_t* sel_idx, float* sel_score, cudaStream_t stream);
@@ -199,6 +202,15 @@ int hba_b200_prefill(const hba_b200_config* cfg, int32_t batch, int32_t n, float
  */
 int hba_b200_set_profile_events(void* const* events, int32_t count);
 int hba_b200_profile_events_recorded(void);
+
+/*
+ * Debug hook (no counterpart in the reference): with a non-NULL device
+ * buffer, later one-CTA-per-head decode kernels write 8 uint64 global-timer
+ * stamps per CTA (kernel start, after the query prologue, after selection,
+ * after the union softmax, end, and three spare) to buffer[blockIdx * 8 + i],
+ * for CTAs with blockIdx * 64 < bytes.  NULL turns it off.
+ */
+int hba_b200_set_debug_trace(void* device_buffer, int64_t bytes);
 
 #ifdef __cplusplus
 }

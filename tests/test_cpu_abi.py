@@ -94,13 +94,13 @@ def test_entry_points_reject_bad_arguments_without_a_device(lib):
                               one, one, z, z, z, one, 16, z)
     assert st == _lib.ERR_WORKSPACE
     bad = cfg(head_dim=80)
-    st = lib.hba_b200_decode(ctypes.byref(bad), 1, 128, one, one, one, one, one, one, one, one, z, one, one, one, z,
-                             z, z, one, 1 << 20, z)
-    assert st == _lib.ERR_UNSUPPORTED
-    st = lib.hba_b200_decode(ctypes.byref(cfg(hier=1)), 1, 128, one, one, one, one, one, one, one, one, z, one, one,
+    st = lib.hba_b200_decode(ctypes.byref(bad), 1, 128, one, one, one, one, one, one, one, one, one, z, one, one,
                              one, z, z, z, one, 1 << 20, z)
+    assert st == _lib.ERR_UNSUPPORTED
+    st = lib.hba_b200_decode(ctypes.byref(cfg(hier=1)), 1, 128, one, one, one, one, one, one, one, one, one, z,
+                             one, one, one, z, z, z, one, 1 << 20, z)
     assert st == _lib.ERR_INVALID_ARGUMENT                                             # hier needs supers
-    st = lib.hba_b200_decode(ctypes.byref(c), 1, 128, one, one, one, one, one, z, one, one, z, one, one,
+    st = lib.hba_b200_decode(ctypes.byref(c), 1, 128, one, one, one, one, one, one, z, one, one, z, one, one,
                              one, z, z, z, one, 1 << 20, z)
     assert st == _lib.ERR_INVALID_ARGUMENT                                             # needs the RoPE'd keys
     st = lib.hba_b200_qknorm(z, one, one, 4, 2, 64, ctypes.c_float(1e-6), z)

@@ -47,10 +47,11 @@ def test_summaries_and_supers_match_oracle(dh, Bk, m):
 
 
 # ---------------------------------------------------------------- decode ----
-# hba_b200_decode has two paths: "fused" (one CTA per sequence and kv head) and
+# hba_b200_decode has three paths: "tc" (one CTA per sequence and kv head,
+# attention on tcgen05/TMEM, QKNorm only), "fused" (same shape on mma.sync) and
 # "split" (selection kernels + stream-K attention); the library picks by batch
-# size, HBA_B200_DECODE_PATH forces one so both are checked on small shapes.
-PATHS = ["split", "fused"]
+# size and config, HBA_B200_DECODE_PATH forces one so all are checked.
+PATHS = ["split", "fused", "tc"]
 
 
 @pytest.mark.parametrize("path", PATHS)
@@ -74,10 +75,12 @@ def test_decode_paths_agree():
             res[path] = cache.attend(wl["q"], return_lse=True, return_selection=True)
         finally:
             del os.environ["HBA_B200_DECODE_PATH"]
-    (o1, l1, (s1, _)), (o2, l2, (s2, _)) = res["split"], res["fused"]
-    assert torch.equal(s1, s2)
-    assert (o1.float() - o2.float()).abs().max().item() < 1e-2
-    assert (l1 - l2).abs().max().item() < 1e-4
+    o1, l1, (s1, _) = res["split"]
+    for other in ("fused", "tc"):
+        o2, l2, (s2, _) = res[other]
+        assert torch.equal(s1, s2), other
+        assert (o1.float() - o2.float()).abs().max().item() < 1e-2, other
+        assert (l1 - l2).abs().max().item() < 1e-3, other
 
 
 def test_decode_planted_blocks_are_selected():

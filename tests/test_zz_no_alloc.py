@@ -20,7 +20,7 @@ pytestmark = pytest.mark.gpu
 def _noalloc(cache, q, out, lse, si, ss):
     st = _lib.load().hba_b200_decode_noalloc(
         ctypes.byref(cache.c), cache.B, cache.n_cap, ptr(cache.lens), ptr(cache.scales), ptr(q), ptr(cache.q_gain),
-        ptr(cache.k), ptr(cache.kr), ptr(cache.v), ptr(cache.summaries), ptr(cache.supers), ptr(cache.cos),
+        ptr(cache.k_gain), ptr(cache.k), ptr(cache.kr), ptr(cache.v), ptr(cache.summaries), ptr(cache.supers), ptr(cache.cos),
         ptr(cache.sin),
         ptr(out), ptr(lse), ptr(si), ptr(ss), stream_of(cache.device))
     _lib.check(st, "hba_b200_decode_noalloc")
@@ -53,7 +53,7 @@ def test_noalloc_rejects_requests_beyond_its_scratch():
     big_batch = 4096
     assert L.hba_b200_decode_workspace_size(ctypes.byref(c), big_batch, 131072) > (8 << 20)
     one = ctypes.c_void_p(16)
-    st = L.hba_b200_decode_noalloc(ctypes.byref(c), big_batch, 131072, one, one, one, one, one, one, one, one,
+    st = L.hba_b200_decode_noalloc(ctypes.byref(c), big_batch, 131072, one, one, one, one, one, one, one, one, one,
                                    None, one, one, one, None, None, None, None)
     assert st == _lib.ERR_WORKSPACE
     del cfg
