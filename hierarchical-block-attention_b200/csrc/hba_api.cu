@@ -226,11 +226,12 @@ enum DecodePath { kDecodeSplit = 0, kDecodeFused = 1, kDecodeTc = 2 };
 // bounds the logits (kDecodeTc), else the mma.sync fused kernel; small
 // batches: the split path.  HBA_B200_DECODE_PATH=tc|fused|split forces one
 // (falling back to split when the forced kernel cannot run the configuration).
-int decode_path(const hba_b200_config* c, const Geom& geo, size_t bh, const void* k, const void* kr, const void* v) {
+int decode_path(const hba_b200_config* c, const Geom& geo, size_t bh, const void* k, const void* kr, const void* v,
+                const void* summ, const void* supers) {
   const char* force = getenv("HBA_B200_DECODE_PATH");
   bool fits = geo.nb_cap <= kFusedMaxItems;
   if (c->hier) fits = fits && geo.ns_cap <= kFusedMaxItems && (long long)c->beam * c->fanout <= kFusedMaxItems;
-  const bool tc_ok = fits && hba::decode_tc_supported(geo, c->head_dim, k, kr, v);
+  const bool tc_ok = fits && hba::decode_tc_supported(geo, c->head_dim, k, kr, v, summ, supers);
   if (force != nullptr) {
     if (strcmp(force, "split") == 0) return kDecodeSplit;
     if (strcmp(force, "fused") == 0) return fits ? kDecodeFused : kDecodeSplit;
@@ -278,7 +279,7 @@ int hba_b200_profile_events_recorded(void) { return g_prof.next; }
 int hba_b200_set_debug_trace(void* device_buffer, int64_t bytes) {
   if (bytes < 0 || (device_buffer == nullptr && bytes != 0)) return HBA_B200_ERR_INVALID_ARGUMENT;
   g_trace = static_cast<unsigned long long*>(device_buffer);
-  g_trace_ctas = device_buffer == nullptr ? 0 : bytes / 64;
+  g_trace_ctas = device_buffer == nullptr ? 0 : bytes / 128;
   return HBA_B200_OK;
 }
 
@@ -391,7 +392,7 @@ int hba_b200_decode(const hba_b200_config* cfg, int32_t batch, int32_t n_cap, co
   ws += align_up(bh * sizeof(int32_t));
   hba::QueryPos qp{seq_lens, scales, 0, 0.f};
   prof_begin(stream);
-  const int path = decode_path(cfg, geo, bh, k_cache, k_rope_cache, v_cache);
+  const int path = decode_path(cfg, geo, bh, k_cache, k_rope_cache, v_cache, summaries, supers);
   if (path != kDecodeSplit) {
     hba::DecodeAttnParams dp{};
     dp.geo = geo;

@@ -19,15 +19,17 @@ HBA_DEVICE float bf2f(__nv_bfloat16 x) { return __bfloat162float(x); }
 HBA_DEVICE __nv_bfloat16 f2bf(float x) { return __float2bfloat16_rn(x); }
 HBA_DEVICE float round_bf16(float x) { return __bfloat162float(__float2bfloat16_rn(x)); }
 
-// unpack 8 bf16 held in a uint4 into floats
-HBA_DEVICE void unpack8(const uint4& u, float* f) {
-  const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
-#pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    float2 t = __bfloat1622float2(h[i]);
-    f[2 * i] = t.x;
-    f[2 * i + 1] = t.y;
-  }
+// unpack 8 bf16 held in a uint4 into floats (a bf16 is the upper half of
+// the fp32 with the same value, so the widening is exact bit placement)
+HBA_DEVICE void unpack8(uint4 u, float* f) {
+  f[0] = __uint_as_float(u.x << 16);
+  f[1] = __uint_as_float(u.x & 0xffff0000u);
+  f[2] = __uint_as_float(u.y << 16);
+  f[3] = __uint_as_float(u.y & 0xffff0000u);
+  f[4] = __uint_as_float(u.z << 16);
+  f[5] = __uint_as_float(u.z & 0xffff0000u);
+  f[6] = __uint_as_float(u.w << 16);
+  f[7] = __uint_as_float(u.w & 0xffff0000u);
 }
 
 HBA_DEVICE uint32_t pack_bf16x2(float lo, float hi) {

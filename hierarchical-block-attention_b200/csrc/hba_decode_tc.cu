@@ -14,15 +14,17 @@
 // running max and O^T is never rescaled; l[h] are per-thread partial sums
 // reduced once at the end.
 //
-// Phases:
-//  A (all 8 warps) query prologue; TMA of the first window chunks issued at
-//    once (they need no selection); summary pages stream through a 2-page
-//    cp.async ring and are scored; block-wide radix-select top-k (flat, or
-//    supers then children for the hierarchical beam).
-//  B (roles) warp 0: TMA producer of the K/V ring [window | sinks | routed
-//    block pairs]; warp 1: TMEM owner and single-thread MMA issuer;
-//    warps 4-7: softmax (TMEM lane quarter = warp % 4); warps 2-3 idle.
-//  C warps 4-7 reduce l, read O^T from TMEM, write out, LSE, the picks.
+// Roles and phases:
+//  warp 3 (lane 0) produces from the first instruction on: summary pages by
+//    1-D bulk copies, then the window/sink K/V tiles by TMA (they need no
+//    selection), then the routed tiles once the picks are known.
+//  A (the other 7 warps) query prologue (its loads are issued before any bulk
+//    copy); each warp scores whole pages, 4 rows at a time, keeping a running
+//    top-k; one warp merges the 7 lists (flat, or supers then children of
+//    the beam).
+//  B warp 1: TMEM owner and single-thread MMA issuer; warps 4-7: softmax
+//    (TMEM lane quarter = warp % 4).
+//  C warps 4-7 reduce l, read O^T from TMEM, write out, LSE.
 // Reference semantics: src/hba/attention.py:663-711 at cs = n-1.
 #include <climits>
 #include <cudaTypedefs.h>
@@ -40,33 +42,81 @@ using namespace sm100;
 constexpr int kDtThreads = 256;
 constexpr int kDtWarps = 8;
 constexpr int kDtKeys = 128;  // keys per chunk (UMMA M)
+constexpr int kDtProducer = 3;    // warp that feeds the ring from the first instruction on
+constexpr int kDtScoreWarps = 7;  // every other warp scores summary pages
 
+// barrier of the 7 scoring warps (the producer warp never joins it)
+HBA_DEVICE void score_bar() { asm volatile("bar.sync 2, 224;\n" ::: "memory"); }
+
+// Warp-wide (score, id) compare-exchange with the lane `stride` away under
+// the library order (score desc, id asc); keep_better selects which of the
+// pair this lane keeps.
+HBA_DEVICE void cmpx(float& s, int& i, int stride, bool keep_better) {
+  const float os = __shfl_xor_sync(0xffffffffu, s, stride);
+  const int oi = __shfl_xor_sync(0xffffffffu, i, stride);
+  if (keep_better ? beats(os, oi, s, i) : beats(s, i, os, oi)) {
+    s = os;
+    i = oi;
+  }
+}
+// Bitonic sort of the warp's 32 (score, id) pairs, best in lane 0.
+HBA_DEVICE void warp_sort32(float& s, int& i) {
+  const int lane = threadIdx.x & 31;
+#pragma unroll
+  for (int size = 2; size <= 32; size <<= 1)
+#pragma unroll
+    for (int stride = size >> 1; stride > 0; stride >>= 1)
+      cmpx(s, i, stride, ((lane & stride) == 0) == ((lane & size) == 0));
+}
+// (ls, li) sorted best first <- best 32 of itself and the sorted batch (bs, bi).
+HBA_DEVICE void warp_merge32(float& ls, int& li, float bs, int bi) {
+  const int lane = threadIdx.x & 31;
+  const float rs = __shfl_sync(0xffffffffu, bs, 31 - lane);
+  const int ri = __shfl_sync(0xffffffffu, bi, 31 - lane);
+  if (beats(rs, ri, ls, li)) {  // best 32 of the union, as a bitonic sequence
+    ls = rs;
+    li = ri;
+  }
+#pragma unroll
+  for (int stride = 16; stride > 0; stride >>= 1) cmpx(ls, li, stride, (lane & stride) == 0);
+}
+
+// One ring of NSLOT slots of one K (or V) tile each carries every byte the
+// CTA reads, in this order: summary pages (128/m rows each; the flat scan, or
+// the super rows then the children of the beam), then per 128-key chunk of
+// [window | sinks | routed block pairs] its K tile and its V tile.  Thread 0
+// keeps the ring full from the first instruction on, so the window tiles
+// load while the pages are scored and the top-k runs.  A page slot is freed
+// once all warps have scored it, a K slot when its S MMA completes, a V slot
+// when its PV MMA completes.
 template <int DH>
 struct DtcSmem {
   static constexpr int HALVES = DH / 64;
-  static constexpr int KT = kDtKeys * DH * 2;               // one K or V tile
-  static constexpr int NKV = DH == 64 ? 3 : 2;              // K/V ring stages
-  static constexpr int PAGE = DH == 64 ? 32768 : 16384;     // summary page bytes
-  alignas(1024) unsigned char kv[NKV][2][KT];               // [stage][K|V], halves of [128 x 64] SW128
-  static constexpr int NPG = 3;                             // summary page ring
-  alignas(1024) unsigned char pages[NPG][PAGE];
+  static constexpr int KT = kDtKeys * DH * 2;               // one K or V tile = one slot
+  static constexpr int NSLOT = DH == 64 ? 12 : 6;
+  alignas(1024) unsigned char ring[NSLOT][KT];              // K/V: halves of [128 x 64] SW128
   alignas(1024) unsigned char qc[HALVES][16 * 128];         // Q rows (16 heads) [16 x 64] SW128 per half
   alignas(1024) unsigned char qr[HALVES][16 * 128];
   alignas(1024) unsigned char pt[2][2][16 * 128];           // P^T [buffer][key half][16 heads x 64 keys]
   float qg[DH];
   float m2[16];
   float lsum[4][16];
-  float sc[kTopkMaxItems];
-  int id[kTopkMaxItems];
-  TopkScratch ts;
-  int blocks[32];
+  float wl_s[kDtScoreWarps][32];  // per-warp top-k lists
+  int wl_i[kDtScoreWarps][32];
+  float sel_s[32];                // merged picks, best first
+  int sel_i[32];
+  int nsel;
+  uint32_t thr;
   int sup_lo[32], sup_off[32], sup_cnt[32];
   int n_children;
-  uint64_t kv_full[NKV], kv_empty[NKV];
+  uint64_t full[NSLOT], empty[NSLOT];
   uint64_t s_full[2], p_full[2], p_free[2];
-  uint64_t o_full, drain;
+  uint64_t o_full, drain, child_ready, sel_ready;
   uint32_t tmem_base;
 };
+
+static_assert(sizeof(DtcSmem<64>) + 1024 <= 232448 && sizeof(DtcSmem<128>) + 1024 <= 232448,
+              "decode tile set exceeds the 227 KB of shared memory per CTA");
 
 struct DecodeTcParams {
   DecodeAttnParams a;
@@ -82,7 +132,8 @@ __global__ void __launch_bounds__(kDtThreads, 1)
                      const __grid_constant__ CUtensorMap tm_v, DecodeTcParams P) {
   using SM = DtcSmem<DH>;
   constexpr int HALVES = SM::HALVES;
-  constexpr int NKV = SM::NKV;
+  constexpr int NSLOT = SM::NSLOT;
+  constexpr int NSW = kDtScoreWarps;
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   unsigned char* base_ptr =
       reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -95,13 +146,9 @@ __global__ void __launch_bounds__(kDtThreads, 1)
   const int bg = blockIdx.x;
   const int b = bg / geo.Hkv, g = bg % geo.Hkv;
   const bool hier = geo.hier != 0;
-  unsigned long long* trace = (p.trace != nullptr && bg < p.trace_ctas) ? p.trace + (size_t)bg * 8 : nullptr;
+  unsigned long long* trace = (p.trace != nullptr && bg < p.trace_ctas) ? p.trace + (size_t)bg * 16 : nullptr;
   auto stamp = [&](int i) {
-    if (trace != nullptr && tid == 0) {
-      unsigned long long t;
-      asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
-      trace[i] = t;
-    }
+    if (trace != nullptr && tid == 0) trace[i] = global_ns();
   };
   stamp(0);
 
@@ -119,12 +166,54 @@ __global__ void __launch_bounds__(kDtThreads, 1)
   const int nsink = ok ? min(geo.S, pos + 1) : 0;
   const int NCw = (nw + kDtKeys - 1) / kDtKeys;
   const int NCs = nsink > 0 ? 1 : 0;
+  const bool producer = warp == kDtProducer;
+  const int sw = warp < kDtProducer ? warp : warp - 1;  // scoring-warp index (producer excluded)
+
+  // ---- A.0 query rows, RoPE row and gains: issued before any bulk copy ----
+  uint32_t qraw[3][PER / 2];
+  float cr[PER], sr[PER], qgain[3];
+  float kg = 0.f;
+  if (!producer && ok) {
+#pragma unroll
+    for (int i = 0; i < PER; ++i) {
+      cr[i] = p.cos[(size_t)pos * DH + lane * PER + i];
+      sr[i] = p.sin[(size_t)pos * DH + lane * PER + i];
+    }
+#pragma unroll
+    for (int j = 0; j < 3; ++j) {
+      const int h = sw + NSW * j;
+      if (h < G) {
+        const uint32_t* src =
+            reinterpret_cast<const uint32_t*>(p.q + ((size_t)b * geo.Hq + g * G + h) * DH) + lane * (PER / 2);
+#pragma unroll
+        for (int k = 0; k < PER / 2; ++k) qraw[j][k] = src[k];
+        qgain[j] = p.q_gain[g * G + h];
+      }
+    }
+    kg = P.k_gain[g];
+  }
+
+  // ---- selection geometry (known from the position alone) ----
+  const int row_elems = geo.m * DH;
+  const int row_bytes = row_elems * 2;
+  const int PB = SM::KT / row_bytes;  // summary rows per page
+  const __nv_bfloat16* summ_bg = P.summ + (size_t)bg * geo.nb_cap * row_elems;
+  const __nv_bfloat16* sup_bg = hier ? P.supers + (size_t)bg * geo.ns_cap * row_elems : nullptr;
+  int Ra = 0, ida = 1;  // phase-A candidates: flat blocks 1..bmax, or supers ida..
+  if (!hier) {
+    Ra = max(0, bmax);
+  } else if (bmax >= 1) {
+    ida = (geo.F == 1) ? 1 : 0;
+    Ra = bmax / geo.F - ida + 1;
+  }
+  const __nv_bfloat16* rows_a = hier ? sup_bg : summ_bg;
+  const int NPa = (Ra + PB - 1) / PB;
 
   // ---- barriers, TMEM ----
-  if (tid == 0) {
-    for (int s = 0; s < NKV; ++s) {
-      mbar_init(&sm.kv_full[s], 1);
-      mbar_init(&sm.kv_empty[s], 1);
+  if (producer && lane == 0) {
+    for (int s = 0; s < NSLOT; ++s) {
+      mbar_init(&sm.full[s], 1);
+      mbar_init(&sm.empty[s], 1);
     }
     for (int s = 0; s < 2; ++s) {
       mbar_init(&sm.s_full[s], 1);
@@ -133,6 +222,8 @@ __global__ void __launch_bounds__(kDtThreads, 1)
     }
     mbar_init(&sm.o_full, 1);
     mbar_init(&sm.drain, 1);
+    mbar_init(&sm.child_ready, 1);
+    mbar_init(&sm.sel_ready, 1);
     fence_barrier_init();
   }
   if (warp == 1) {
@@ -144,387 +235,485 @@ __global__ void __launch_bounds__(kDtThreads, 1)
   tc_fence_after();
   const uint32_t tmem = sm.tmem_base;  // cols [0,16) S0, [16,32) S1, [32,48) O^T
 
-  // K/V chunk c -> (kind, token of its first / second 64-row half)
-  int nsel = 0, NCr = 0;
-  auto chunk_src = [&](int c, int& kind, int& t0, int& t1) {
-    if (c < NCw) {
-      kind = 0;
-      t0 = w0 + c * kDtKeys;
-      t1 = t0 + 64;
-    } else if (c < NCw + NCs) {
-      kind = 1;
-      t0 = 0;
-      t1 = 64;
-    } else {
-      kind = 2;
-      const int i = (c - NCw - NCs) * 2;
-      t0 = sm.blocks[i] * 64;
-      t1 = (i + 1 < nsel ? sm.blocks[i + 1] : sm.blocks[i]) * 64;  // odd count: reload a valid block (masked)
-    }
-  };
-  int issued = 0;  // producer thread only
-  auto produce = [&](int upto) {  // issue chunks [issued, upto) into the ring (warp 0, lane 0)
-    for (; issued < upto; ++issued) {
-      const int c = issued, st = c % NKV, u = c / NKV;
-      if (c >= NKV && !mbar_wait(&sm.kv_empty[st], (u - 1) & 1, P.err)) return;
-      int kind, t0, t1;
-      chunk_src(c, kind, t0, t1);
-      mbar_arrive_expect_tx(&sm.kv_full[st], 2 * SM::KT);
-      const CUtensorMap* km = kind == 0 ? &tm_kr : &tm_kc;
-#pragma unroll
-      for (int h = 0; h < HALVES; ++h) {
-        unsigned char* kd = sm.kv[st][0] + h * (kDtKeys * 128);
-        unsigned char* vd = sm.kv[st][1] + h * (kDtKeys * 128);
-        tma_load_4d(kd, km, h * 64, g, t0, b, &sm.kv_full[st]);
-        tma_load_4d(kd + 64 * 128, km, h * 64, g, t1, b, &sm.kv_full[st]);
-        tma_load_4d(vd, &tm_v, h * 64, g, t0, b, &sm.kv_full[st]);
-        tma_load_4d(vd + 64 * 128, &tm_v, h * 64, g, t1, b, &sm.kv_full[st]);
-      }
-    }
-  };
-  if (warp == 0 && lane == 0) {
-    prefetch_tmap(&tm_kc);
-    prefetch_tmap(&tm_kr);
-    prefetch_tmap(&tm_v);
-    produce(min(NKV, NCw + NCs));  // window/sink chunks need no selection
-  }
-
-  // ---- A.1 query prologue: Q rows (SW128), qg, per-head logit bounds ----
-  for (int h = warp; h < 16; h += kDtWarps) {
-    float v[PER], r[PER];
-    float qn2 = 0.f;
-    if (h < G && ok) {
-      const int hq = g * G + h;
-      float cr[PER], sr[PER];  // issued together with the query load
-#pragma unroll
-      for (int i = 0; i < PER; ++i) {
-        cr[i] = p.cos[(size_t)pos * DH + lane * PER + i];
-        sr[i] = p.sin[(size_t)pos * DH + lane * PER + i];
-      }
-      load_head_row<DH>(p.q + ((size_t)b * geo.Hq + hq) * DH, v);
-      qknorm_lane<DH>(v, p.q_gain[hq], geo.eps);
-      const float sign = lane < 16 ? -1.f : 1.f;
-#pragma unroll
-      for (int i = 0; i < PER; ++i) {
-        const float partner = __shfl_xor_sync(0xffffffffu, v[i], 16);
-        r[i] = v[i] * cr[i] + sign * partner * sr[i];
-        qn2 = fmaf(v[i], v[i], qn2);
-      }
-    } else {
-#pragma unroll
-      for (int i = 0; i < PER; ++i) v[i] = r[i] = 0.f;
-    }
-    qn2 = warp_sum(qn2);
-    // element d -> half d/64, column d%64 of row h
-#pragma unroll
-    for (int i = 0; i < PER; i += 2) {
-      const int d = lane * PER + i;
-      const uint32_t off = sw128_offset(h, d % 64);
-      *reinterpret_cast<uint32_t*>(sm.qc[d / 64] + off) = pack_bf16x2(v[i], v[i + 1]);
-      *reinterpret_cast<uint32_t*>(sm.qr[d / 64] + off) = pack_bf16x2(r[i], r[i + 1]);
-    }
+  if (producer) {
+    // ---- ring producer: items [0, NPa) phase-A pages, [NPa, NP) child
+    // pages, then the K and V tiles of chunk c at NP + 2c, NP + 2c + 1 ----
     if (lane == 0) {
-      const float kmax = sqrtf((float)DH) * P.k_gain[g] * (1.f + 1.f / 64.f);
-      const float m2 = scale * sqrtf(qn2) * kmax * kLog2e;
-      sm.m2[h] = (h < G && ok) ? m2 : 0.f;
-      if (m2 > 120.f) atomicExch(P.err, 2);
-    }
-  }
-  __syncthreads();
-  for (int d = tid; d < DH; d += kDtThreads) {
-    float acc = 0.f;
-    for (int h = 0; h < G; ++h) {
-      acc += bf2f(*reinterpret_cast<const __nv_bfloat16*>(sm.qc[d / 64] + sw128_offset(h, d % 64)));
-    }
-    sm.qg[d] = round_bf16(acc);
-  }
-  fence_proxy_async_smem();  // Q tiles are read by the tensor cores
-  __syncthreads();
-  stamp(1);
-
-  // ---- A.2 selection: summary pages through a 2-page cp.async ring ----
-  const int row_bytes = geo.m * DH * 2;
-  const int row_pieces = row_bytes / 16;
-  const int PB = SM::PAGE / row_bytes;
-  const __nv_bfloat16* summ_bg = P.summ + (size_t)bg * geo.nb_cap * geo.m * DH;
-  const __nv_bfloat16* sup_bg = hier ? P.supers + (size_t)bg * geo.ns_cap * geo.m * DH : nullptr;
-  const int nvec = row_pieces;
-  constexpr int LPS = DH / 8;
-  auto child_id = [&](int j) -> int {
-    int si = 0;
-    while (si < 31 && j >= sm.sup_off[si] + sm.sup_cnt[si]) ++si;
-    return sm.sup_lo[si] + (j - sm.sup_off[si]);
-  };
-  // scores candidates [0, R): id_fn(j) is the candidate's row in `rows`.
-  // Each warp scores 4 rows at a time with the per-row arithmetic of
-  // SummaryLoads::score (hba_score.cuh), so every decode path selects from
-  // bit-identical scores.
-  float qgr[VPL][8];
-  auto load_qg = [&]() {
-#pragma unroll
-    for (int v = 0; v < VPL; ++v) {
-      const int d0 = ((lane + 32 * v) * 8) % DH;
-#pragma unroll
-      for (int jj = 0; jj < 8; ++jj) qgr[v][jj] = sm.qg[d0 + jj];
-    }
-  };
-  auto score_phase = [&](const __nv_bfloat16* rows, int R, auto id_fn) {
-    constexpr int NPG = SM::NPG;
-    const int np = (R + PB - 1) / PB;
-    auto issue_page = [&](int pg) {
-      if (pg < np) {
-        const int nr = min(PB, R - pg * PB);
-        unsigned char* dst = sm.pages[pg % NPG];
-        for (int e = tid; e < nr * row_pieces; e += kDtThreads) {
-          const int r = e / row_pieces, pc = e % row_pieces;
-          cp_async16(dst + r * row_bytes + pc * 16, rows + (size_t)id_fn(pg * PB + r) * geo.m * DH + pc * 8);
-        }
-      }
-      cp_async_commit();
-    };
-    for (int pg = 0; pg < NPG - 1; ++pg) issue_page(pg);
-    for (int pg = 0; pg < np; ++pg) {
-      issue_page(pg + NPG - 1);
-      cp_async_wait<NPG - 1>();
-      __syncthreads();
-      const unsigned char* src = sm.pages[pg % NPG];
-      const int nr = min(PB, R - pg * PB);
-      for (int r0 = warp * 4; r0 < nr; r0 += kDtWarps * 4) {
-        float part[4][VPL];
-#pragma unroll
-        for (int u = 0; u < 4; ++u)
-#pragma unroll
-          for (int v = 0; v < VPL; ++v) {
-            const int vv = lane + 32 * v;
-            part[u][v] = 0.f;
-            if (r0 + u < nr && vv < nvec) {
-              float f[8];
-              unpack8(*reinterpret_cast<const uint4*>(src + (r0 + u) * row_bytes + vv * 16), f);
-#pragma unroll
-              for (int jj = 0; jj < 8; ++jj) part[u][v] = fmaf(f[jj], qgr[v][jj], part[u][v]);
-            }
+      prefetch_tmap(&tm_kc);
+      prefetch_tmap(&tm_kr);
+      prefetch_tmap(&tm_v);
+      int NPb = 0, R2 = 0, nsel = 0, issued = 0;
+      auto issue_item = [&](int i) {
+        const int NP = NPa + NPb;
+        unsigned char* dst = sm.ring[i % NSLOT];
+        uint64_t* fb = &sm.full[i % NSLOT];
+        if (i < NPa) {
+          const int j0 = i * PB, nr = min(PB, Ra - j0);
+          mbar_arrive_expect_tx(fb, (uint32_t)(nr * row_bytes));
+          bulk_load(dst, rows_a + (size_t)(ida + j0) * row_elems, (uint32_t)(nr * row_bytes), fb);
+        } else if (i < NP) {  // children of the beam: one bulk copy per contiguous span
+          const int j0 = (i - NPa) * PB, j1 = min(R2, j0 + PB);
+          mbar_arrive_expect_tx(fb, (uint32_t)((j1 - j0) * row_bytes));
+          for (int si = 0; si < 32; ++si) {
+            const int lo = max(j0, sm.sup_off[si]), hi = min(j1, sm.sup_off[si] + sm.sup_cnt[si]);
+            if (lo < hi)
+              bulk_load(dst + (size_t)(lo - j0) * row_bytes,
+                        summ_bg + (size_t)(sm.sup_lo[si] + lo - sm.sup_off[si]) * row_elems,
+                        (uint32_t)((hi - lo) * row_bytes), fb);
           }
+        } else {
+          const int c = (i - NP) >> 1, is_v = (i - NP) & 1;
+          int kind, t0, t1;
+          if (c < NCw) {
+            kind = 0;
+            t0 = w0 + c * kDtKeys;
+            t1 = t0 + 64;
+          } else if (c < NCw + NCs) {
+            kind = 1;
+            t0 = 0;
+            t1 = 64;
+          } else {
+            kind = 2;
+            const int q = (c - NCw - NCs) * 2;
+            t0 = sm.sel_i[q] * 64;
+            t1 = (q + 1 < nsel ? sm.sel_i[q + 1] : sm.sel_i[q]) * 64;  // odd count: a valid block, masked
+          }
+          mbar_arrive_expect_tx(fb, SM::KT);
+          const CUtensorMap* m = is_v ? &tm_v : (kind == 0 ? &tm_kr : &tm_kc);
 #pragma unroll
-        for (int ox = 1; ox < LPS; ox <<= 1)
-#pragma unroll
-          for (int u = 0; u < 4; ++u)
-#pragma unroll
-            for (int v = 0; v < VPL; ++v) part[u][v] += __shfl_xor_sync(0xffffffffu, part[u][v], ox);
-        float best[4];
-#pragma unroll
-        for (int u = 0; u < 4; ++u) {
-          best[u] = neg_inf();
-#pragma unroll
-          for (int v = 0; v < VPL; ++v)
-            if (lane + 32 * v < nvec) best[u] = fmaxf(best[u], part[u][v]);
+          for (int h = 0; h < HALVES; ++h) {
+            tma_load_4d(dst + h * (kDtKeys * 128), m, h * 64, g, t0, b, fb);
+            tma_load_4d(dst + h * (kDtKeys * 128) + 64 * 128, m, h * 64, g, t1, b, fb);
+          }
         }
-#pragma unroll
-        for (int ox = 16; ox > 0; ox >>= 1)
-#pragma unroll
-          for (int u = 0; u < 4; ++u) best[u] = fmaxf(best[u], __shfl_xor_sync(0xffffffffu, best[u], ox));
-        if (lane == 0) {
-#pragma unroll
-          for (int u = 0; u < 4; ++u)
-            if (r0 + u < nr) {
-              const int j = pg * PB + r0 + u;
-              sm.sc[j] = best[u] * scale;
-              sm.id[j] = id_fn(j);
-            }
+      };
+      auto pump_to = [&](int upto) -> bool {
+        for (; issued < upto; ++issued) {
+          if (issued >= NSLOT &&
+              !mbar_wait(&sm.empty[issued % NSLOT], ((issued / NSLOT) - 1) & 1, P.err))
+            return false;
+          issue_item(issued);
         }
-      }
-      __syncthreads();
-    }
-    cp_async_wait<0>();
-  };
-  load_qg();
-  if (!hier) {
-    const int R = max(0, bmax);
-    score_phase(summ_bg, R, [&](int j) { return 1 + j; });
-    stamp(5);
-    nsel = block_topk<kDtThreads>(sm.sc, sm.id, R, kfinal, sm.ts);
-    stamp(6);
-  } else {
-    int R1 = 0, s_lo = 0;
-    if (bmax >= 1) {
-      s_lo = (geo.F == 1) ? 1 : 0;
-      R1 = bmax / geo.F - s_lo + 1;
-    }
-    score_phase(sup_bg, R1, [&](int j) { return s_lo + j; });
-    stamp(5);
-    const int nsup = block_topk<kDtThreads>(sm.sc, sm.id, R1, min(geo.beam, ns), sm.ts);
-    if (warp == 0) {
-      const bool valid = lane < nsup;
-      int lo = 0, cnt = 0;
-      if (valid) {
-        const int sidx = sm.ts.sel_idx[lane];
-        lo = max(1, sidx * geo.F);
-        cnt = max(0, min(bmax, sidx * geo.F + geo.F - 1) - lo + 1);
-      }
-      int incl = cnt;
-#pragma unroll
-      for (int o = 1; o < 32; o <<= 1) {
-        const int nv = __shfl_up_sync(0xffffffffu, incl, o);
-        if (lane >= o) incl += nv;
-      }
-      sm.sup_lo[lane] = lo;
-      sm.sup_cnt[lane] = cnt;
-      sm.sup_off[lane] = incl - cnt;
-      if (lane == 31) sm.n_children = incl;
-    }
-    __syncthreads();
-    const int R2 = sm.n_children;
-    stamp(6);
-    score_phase(summ_bg, R2, [&](int j) { return child_id(j); });
-    stamp(7);
-    nsel = block_topk<kDtThreads>(sm.sc, sm.id, R2, kfinal, sm.ts);
-  }
-  if (tid < 32) {
-    const bool valid = tid < nsel;
-    sm.blocks[tid] = valid ? sm.ts.sel_idx[tid] : 0;
-    if (p.sel_idx != nullptr && tid < geo.K) {
-      p.sel_idx[(size_t)bg * geo.K + tid] = valid ? sm.ts.sel_idx[tid] : -1;
-      p.sel_score[(size_t)bg * geo.K + tid] = valid ? sm.ts.sel_score[tid] : neg_inf();
-    }
-  }
-  __syncthreads();
-  NCr = (nsel * geo.Bk + kDtKeys - 1) / kDtKeys;
-  const int NC = NCw + NCs + NCr;
-  stamp(2);
-
-  // ---- B. union softmax ----
-  if (warp == 0) {
-    if (lane == 0) produce(NC);
-  } else if (warp == 1) {
-    if (lane == 0) {
-      constexpr uint32_t idesc_s = idesc_bf16(128, 16, false, false);
-      constexpr uint32_t idesc_o = idesc_bf16(128, 16, true, false);
-      bool okw = true;
-      auto pv = [&](int c) -> bool {
-        const int sb = c & 1, st = c % NKV;
-        if (!mbar_wait(&sm.p_full[sb], (c >> 1) & 1, P.err)) return false;
-        tc_fence_after();
-        const uint32_t va = smem_u32(sm.kv[st][1]);
-        const uint32_t pa = smem_u32(sm.pt[sb][0]);
-        // dh 64: M = 128 reads a second MN group at LBO 0 (rows 64-127 of O^T duplicate 0-63, unused)
-        const uint32_t lbo = DH == 128 ? kDtKeys * 128 : 0;
-#pragma unroll
-        for (int kk = 0; kk < kDtKeys / 16; ++kk)
-          umma_f16(tmem + 32, sdesc_sw128(va + kk * 2048, lbo, 1024),
-                   sdesc_sw128(pa + (kk >> 2) * 2048 + (kk & 3) * 32, 16, 1024), idesc_o,
-                   (c > 0 || kk > 0) ? 1u : 0u);
-        umma_commit(&sm.kv_empty[st]);
-        umma_commit(&sm.p_free[sb]);
         return true;
       };
-      for (int c = 0; okw && c < NC; ++c) {
-        const int st = c % NKV, sb = c & 1;
-        if (!mbar_wait(&sm.kv_full[st], (c / NKV) & 1, P.err)) {
+      bool okp = pump_to(hier ? NPa : NPa + 2 * (NCw + NCs));  // window/sink tiles need no selection
+      if (hier && okp) {
+        okp = mbar_wait(&sm.child_ready, 0, P.err);
+        R2 = sm.n_children;
+        NPb = (R2 + PB - 1) / PB;
+        okp = okp && pump_to(NPa + NPb + 2 * (NCw + NCs));
+      }
+      if (okp && mbar_wait(&sm.sel_ready, 0, P.err)) {
+        nsel = sm.nsel;
+        pump_to(NPa + NPb + 2 * (NCw + NCs + (nsel * geo.Bk + kDtKeys - 1) / kDtKeys));
+      }
+    }
+  } else {
+    // ---- A.1 QKNorm, RoPE, Q tiles (SW128), per-head logit bounds ----
+#pragma unroll
+    for (int j = 0; j < 3; ++j) {
+      const int h = sw + NSW * j;  // warp-uniform
+      if (h < 16) {
+        float v[PER], r[PER];
+        float qn2 = 0.f;
+        if (h < G && ok) {
+#pragma unroll
+          for (int k = 0; k < PER / 2; ++k) {
+            const float2 t2 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&qraw[j][k]));
+            v[2 * k] = t2.x;
+            v[2 * k + 1] = t2.y;
+          }
+          qknorm_lane<DH>(v, qgain[j], geo.eps);
+          const float sign = lane < 16 ? -1.f : 1.f;
+#pragma unroll
+          for (int i = 0; i < PER; ++i) {
+            const float partner = __shfl_xor_sync(0xffffffffu, v[i], 16);
+            r[i] = v[i] * cr[i] + sign * partner * sr[i];
+            qn2 = fmaf(v[i], v[i], qn2);
+          }
+        } else {
+#pragma unroll
+          for (int i = 0; i < PER; ++i) v[i] = r[i] = 0.f;
+        }
+        qn2 = warp_sum(qn2);
+        // element d -> half d/64, column d%64 of row h
+#pragma unroll
+        for (int i = 0; i < PER; i += 2) {
+          const int d = lane * PER + i;
+          const uint32_t off = sw128_offset(h, d % 64);
+          *reinterpret_cast<uint32_t*>(sm.qc[d / 64] + off) = pack_bf16x2(v[i], v[i + 1]);
+          *reinterpret_cast<uint32_t*>(sm.qr[d / 64] + off) = pack_bf16x2(r[i], r[i + 1]);
+        }
+        if (lane == 0) {
+          const float kmax = sqrtf((float)DH) * kg * (1.f + 1.f / 64.f);
+          const float m2 = scale * sqrtf(qn2) * kmax * kLog2e;
+          sm.m2[h] = (h < G && ok) ? m2 : 0.f;
+          if (m2 > 120.f) atomicExch(P.err, 2);
+        }
+      }
+    }
+    score_bar();
+    // routing query: bf16(fp32 sum of the bf16 QKNorm'd heads, in head order)
+    for (int d = sw * 32 + lane; d < DH; d += NSW * 32) {
+      float acc = 0.f;
+      for (int h = 0; h < G; ++h) acc += bf2f(*reinterpret_cast<const __nv_bfloat16*>(sm.qc[d / 64] + sw128_offset(h, d % 64)));
+      sm.qg[d] = round_bf16(acc);
+    }
+    fence_proxy_async_smem();  // Q tiles are read by the tensor cores
+    score_bar();
+    stamp(1);
+
+    // ---- A.2 selection: each scoring warp owns pages sw, sw + 7, ... ----
+    // One summary row per lane.  A lane reads the LPS 16-byte vectors of a
+    // slot in the order q ^ (lane & 7) -- conflict-free across the 8 lanes of
+    // a shared-memory phase -- and adds the per-vector partials in the
+    // pairwise tree of SummaryLoads::score (hba_score.cuh); XOR relabelling
+    // within aligned groups keeps every pair of that tree, so the scores are
+    // bit-identical to the other decode paths.  Each warp keeps its best 32
+    // (score desc, id asc) in registers: a 32-row batch that beats the k-th
+    // entry is bitonic-sorted and merged in.
+    constexpr int LPS = DH / 8;  // 16-byte vectors per slot
+    constexpr bool kQgRegs = DH == 64;  // this lane's permuted copy of qg in registers
+    const int m_slots = geo.m;
+    const int o = lane & 7;
+    float qgp[kQgRegs ? LPS : 1][8];
+    if constexpr (kQgRegs) {
+#pragma unroll
+      for (int q = 0; q < LPS; ++q)
+#pragma unroll
+        for (int jj = 0; jj < 8; ++jj) qgp[q][jj] = sm.qg[(q ^ o) * 8 + jj];
+    }
+    float ls = neg_inf();
+    int li = INT_MAX;
+    if (tid == 0) sm.thr = 0u;  // order_key of the best k-th score any warp has reached
+    score_bar();
+    auto score_pages = [&](int i0, int np, int R, int k, auto id_of) {
+      for (int pg = sw; pg < np; pg += NSW) {
+        const int i = i0 + pg;
+        mbar_wait(&sm.full[i % NSLOT], (i / NSLOT) & 1, P.err);
+        if (trace != nullptr && lane == 0 && i < 4) trace[8 + 2 * i] = global_ns();
+        const unsigned char* src = sm.ring[i % NSLOT];
+        const int nr = min(PB, R - pg * PB);
+        for (int rg = 0; rg < nr; rg += 32) {
+          const int r = rg + lane;
+          float cs = neg_inf();
+          int ci = INT_MAX;
+          if (r < nr) {
+            const unsigned char* row = src + (size_t)r * row_bytes;
+            float best = neg_inf();
+            for (int sl = 0; sl < m_slots; ++sl) {
+              float pp[LPS];
+#pragma unroll
+              for (int q = 0; q < LPS; ++q) {
+                const int vq = q ^ o;
+                float f[8];
+                unpack8(*reinterpret_cast<const uint4*>(row + (sl * LPS + vq) * 16), f);
+                float qv[8];
+                if constexpr (kQgRegs) {
+#pragma unroll
+                  for (int jj = 0; jj < 8; ++jj) qv[jj] = qgp[q][jj];
+                } else {
+                  const float4 qa = *reinterpret_cast<const float4*>(&sm.qg[vq * 8]);
+                  const float4 qb = *reinterpret_cast<const float4*>(&sm.qg[vq * 8 + 4]);
+                  qv[0] = qa.x, qv[1] = qa.y, qv[2] = qa.z, qv[3] = qa.w;
+                  qv[4] = qb.x, qv[5] = qb.y, qv[6] = qb.z, qv[7] = qb.w;
+                }
+                float part = 0.f;
+#pragma unroll
+                for (int jj = 0; jj < 8; ++jj) part = fmaf(f[jj], qv[jj], part);
+                pp[q] = part;
+              }
+#pragma unroll
+              for (int w = 1; w < LPS; w <<= 1)
+#pragma unroll
+                for (int q = 0; q < LPS; q += 2 * w) pp[q] = pp[q] + pp[q + w];
+              best = fmaxf(best, pp[0]);
+            }
+            cs = best * scale;
+            ci = id_of(pg * PB + r);
+          }
+          // keep the batch entries that can still reach the final top-k
+          const float ts = __shfl_sync(0xffffffffu, ls, k - 1);
+          const int ti = __shfl_sync(0xffffffffu, li, k - 1);
+          const uint32_t thr = *reinterpret_cast<volatile uint32_t*>(&sm.thr);
+          const bool cand = beats(cs, ci, ts, ti) && order_key(cs) >= thr;
+          const unsigned mask = __ballot_sync(0xffffffffu, cand);
+          if (mask == 0u) continue;
+          const bool empty_list = __shfl_sync(0xffffffffu, li, 0) == INT_MAX;  // warp-uniform
+          if (empty_list) {  // the sorted batch is the list
+            warp_sort32(cs, ci);
+            ls = cs;
+            li = ci;
+          } else if (__popc(mask) > 6) {
+            if (!cand) {
+              cs = neg_inf();
+              ci = INT_MAX;
+            }
+            warp_sort32(cs, ci);
+            warp_merge32(ls, li, cs, ci);
+          } else {
+            for (unsigned mm = mask; mm; mm &= mm - 1) {
+              const int srcl = __ffs(mm) - 1;
+              const float xs = __shfl_sync(0xffffffffu, cs, srcl);
+              const int xi = __shfl_sync(0xffffffffu, ci, srcl);
+              const bool better = beats(xs, xi, ls, li);  // lanes above the insertion point
+              const int at = __popc(__ballot_sync(0xffffffffu, !better));
+              const float ps = __shfl_up_sync(0xffffffffu, ls, 1);
+              const int pi = __shfl_up_sync(0xffffffffu, li, 1);
+              if (lane == at) {
+                ls = xs;
+                li = xi;
+              } else if (lane > at) {
+                ls = ps;
+                li = pi;
+              }
+            }
+          }
+          const int kth = __shfl_sync(0xffffffffu, li, k - 1);
+          const float kts = __shfl_sync(0xffffffffu, ls, k - 1);
+          if (lane == 0 && kth != INT_MAX) atomicMax(&sm.thr, order_key(kts));
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&sm.empty[i % NSLOT]);
+        if (trace != nullptr && lane == 0 && i < 4) trace[9 + 2 * i] = global_ns();
+      }
+    };
+    // merges the 7 warp lists in a 3-round tree: best-first picks in
+    // sm.sel_i / sel_s, valid count returned
+    auto merge = [&](int k) -> int {
+      sm.wl_s[sw][lane] = ls;
+      sm.wl_i[sw][lane] = li;
+      score_bar();
+#pragma unroll
+      for (int step = 1; step < NSW; step <<= 1) {
+        if (sw % (2 * step) == 0 && sw + step < NSW) {
+          float a = sm.wl_s[sw][lane];
+          int ai = sm.wl_i[sw][lane];
+          warp_merge32(a, ai, sm.wl_s[sw + step][lane], sm.wl_i[sw + step][lane]);
+          __syncwarp();
+          sm.wl_s[sw][lane] = a;
+          sm.wl_i[sw][lane] = ai;
+        }
+        score_bar();
+      }
+      if (warp == 0) {
+        const float fs = sm.wl_s[0][lane];
+        const int fi = sm.wl_i[0][lane];
+        const int n = __popc(__ballot_sync(0xffffffffu, lane < k && fi != INT_MAX));
+        sm.sel_i[lane] = fi;
+        sm.sel_s[lane] = fs;
+        if (lane == 0) sm.nsel = n;
+      }
+      score_bar();
+      return sm.nsel;
+    };
+    int nsel = 0, NPb = 0;
+    if (!hier) {
+      if (kfinal > 0) score_pages(0, NPa, Ra, kfinal, [&](int j) { return 1 + j; });
+      stamp(5);
+      nsel = merge(max(1, kfinal));
+      stamp(6);
+    } else {
+      const int kb = max(1, min(geo.beam, ns));
+      score_pages(0, NPa, Ra, kb, [&](int j) { return ida + j; });
+      stamp(5);
+      const int nsup = merge(kb);
+      if (warp == 0) {  // the beam's supers in ascending order; their children as contiguous spans
+        const bool valid = lane < nsup;
+        const int sidx = valid ? sm.sel_i[lane] : INT_MAX;
+        int rank = 0;
+        for (int o = 0; o < 32; ++o) rank += __shfl_sync(0xffffffffu, sidx, o) < sidx;
+        __syncwarp();
+        if (valid) sm.sup_lo[rank] = sidx;
+        __syncwarp();
+        const int s = lane < nsup ? sm.sup_lo[lane] : 0;
+        __syncwarp();
+        int lo = 0, cnt = 0;
+        if (lane < nsup) {
+          lo = max(1, s * geo.F);
+          cnt = max(0, min(bmax, s * geo.F + geo.F - 1) - lo + 1);
+        }
+        int incl = cnt;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+          const int nv = __shfl_up_sync(0xffffffffu, incl, o);
+          if (lane >= o) incl += nv;
+        }
+        sm.sup_lo[lane] = lo;
+        sm.sup_cnt[lane] = cnt;
+        sm.sup_off[lane] = incl - cnt;
+        if (lane == 31) sm.n_children = incl;
+        if (lane == 0) sm.thr = 0u;  // child scores start a new threshold
+        __syncwarp();
+        __threadfence_block();
+        if (lane == 0) mbar_arrive(&sm.child_ready);
+      }
+      score_bar();
+      const int R2 = sm.n_children;
+      NPb = (R2 + PB - 1) / PB;
+      stamp(6);
+      auto child_id = [&](int j) -> int {
+        int si = 0;
+        while (si < 31 && j >= sm.sup_off[si] + sm.sup_cnt[si]) ++si;
+        return sm.sup_lo[si] + (j - sm.sup_off[si]);
+      };
+      ls = neg_inf();
+      li = INT_MAX;
+      if (kfinal > 0) score_pages(NPa, NPb, R2, kfinal, child_id);
+      stamp(7);
+      nsel = merge(max(1, kfinal));
+    }
+    if (warp == 0) {
+      const bool valid = lane < nsel;
+      if (p.sel_idx != nullptr && lane < geo.K) {
+        p.sel_idx[(size_t)bg * geo.K + lane] = valid ? sm.sel_i[lane] : -1;
+        p.sel_score[(size_t)bg * geo.K + lane] = valid ? sm.sel_s[lane] : neg_inf();
+      }
+      if (lane == 0) mbar_arrive(&sm.sel_ready);  // picks and count are in shared memory
+    }
+    const int NCr = (nsel * geo.Bk + kDtKeys - 1) / kDtKeys;
+    const int NC = NCw + NCs + NCr;
+    const int NP = NPa + NPb;
+    stamp(2);
+
+    // ---- B. union softmax ----
+    if (warp == 1) {
+      if (lane == 0) {
+        constexpr uint32_t idesc_s = idesc_bf16(128, 16, false, false);
+        constexpr uint32_t idesc_o = idesc_bf16(128, 16, true, false);
+        bool okw = true;
+        auto pv = [&](int c) -> bool {
+          const int sb = c & 1, iv = NP + 2 * c + 1;
+          if (!mbar_wait(&sm.p_full[sb], (c >> 1) & 1, P.err)) return false;
+          if (!mbar_wait(&sm.full[iv % NSLOT], (iv / NSLOT) & 1, P.err)) return false;
+          tc_fence_after();
+          const uint32_t va = smem_u32(sm.ring[iv % NSLOT]);
+          const uint32_t pa = smem_u32(sm.pt[sb][0]);
+          // dh 64: M = 128 reads a second MN group at LBO 0 (rows 64-127 of O^T duplicate 0-63, unused)
+          const uint32_t lbo = DH == 128 ? kDtKeys * 128 : 0;
+  #pragma unroll
+          for (int kk = 0; kk < kDtKeys / 16; ++kk)
+            umma_f16(tmem + 32, sdesc_sw128(va + kk * 2048, lbo, 1024),
+                     sdesc_sw128(pa + (kk >> 2) * 2048 + (kk & 3) * 32, 16, 1024), idesc_o,
+                     (c > 0 || kk > 0) ? 1u : 0u);
+          umma_commit(&sm.empty[iv % NSLOT]);
+          umma_commit(&sm.p_free[sb]);
+          return true;
+        };
+        for (int c = 0; okw && c < NC; ++c) {
+          const int sb = c & 1, ik = NP + 2 * c;
+          if (!mbar_wait(&sm.full[ik % NSLOT], (ik / NSLOT) & 1, P.err)) {
+            okw = false;
+            break;
+          }
+          tc_fence_after();
+          const bool window = c < NCw;
+          const uint32_t ka = smem_u32(sm.ring[ik % NSLOT]);
+  #pragma unroll
+          for (int kk = 0; kk < DH / 16; ++kk) {
+            const int h = kk >> 2, ko = (kk & 3) * 32;
+            const uint32_t qa = smem_u32(window ? sm.qr[h] : sm.qc[h]);
+            umma_f16(tmem + sb * 16, sdesc_sw128(ka + h * (kDtKeys * 128) + ko, 16, 1024),
+                     sdesc_sw128(qa + ko, 16, 1024), idesc_s, kk > 0 ? 1u : 0u);
+          }
+          umma_commit(&sm.s_full[sb]);
+          umma_commit(&sm.empty[ik % NSLOT]);  // K tile free once S is done
+          if (c >= 1 && !pv(c - 1)) {
+            okw = false;
+            break;
+          }
+        }
+        if (okw && NC >= 1) okw = pv(NC - 1);
+        umma_commit(&sm.o_full);
+        umma_commit(&sm.drain);
+        mbar_wait(&sm.drain, 0, P.err);
+      }
+    } else if (warp >= 4) {
+      const int t = tid - 128;  // key row of the chunk / TMEM lane
+      const uint32_t lane_off = (uint32_t)((warp & 3) * 32) << 16;
+      const float sl2 = scale * kLog2e;
+      float lp[16];
+  #pragma unroll
+      for (int h = 0; h < 16; ++h) lp[h] = 0.f;
+      float m2[16];
+  #pragma unroll
+      for (int h = 0; h < 16; ++h) m2[h] = sm.m2[h];
+      bool okw = true;
+      for (int c = 0; c < NC; ++c) {
+        const int sb = c & 1;
+        if (!mbar_wait(&sm.s_full[sb], (c >> 1) & 1, P.err)) {
           okw = false;
           break;
         }
         tc_fence_after();
-        const bool window = c < NCw;
-        const uint32_t ka = smem_u32(sm.kv[st][0]);
-#pragma unroll
-        for (int kk = 0; kk < DH / 16; ++kk) {
-          const int h = kk >> 2, ko = (kk & 3) * 32;
-          const uint32_t qa = smem_u32(window ? sm.qr[h] : sm.qc[h]);
-          umma_f16(tmem + sb * 16, sdesc_sw128(ka + h * (kDtKeys * 128) + ko, 16, 1024),
-                   sdesc_sw128(qa + ko, 16, 1024), idesc_s, kk > 0 ? 1u : 0u);
+        float s[16];
+        {
+          uint32_t r[16];
+          asm volatile(
+              "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, "
+              "[%16];\n"
+              : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+                "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+              : "r"(tmem + sb * 16 + lane_off));
+          tmem_ld_wait();
+  #pragma unroll
+          for (int h = 0; h < 16; ++h) s[h] = __uint_as_float(r[h]);
         }
-        umma_commit(&sm.s_full[sb]);
-        if (c >= 1 && !pv(c - 1)) {
+        if (c >= 2 && !mbar_wait(&sm.p_free[sb], ((c - 2) >> 1) & 1, P.err)) {
           okw = false;
           break;
         }
+        bool valid;
+        if (c < NCw) valid = w0 + c * kDtKeys + t <= pos;
+        else if (c < NCw + NCs) valid = t < nsink;
+        else valid = (c - NCw - NCs) * kDtKeys + t < nsel * geo.Bk;
+        unsigned char* pdst = sm.pt[sb][t >> 6];
+  #pragma unroll
+        for (int h = 0; h < 16; ++h) {
+          const float pe = (valid && h < G) ? exp2f(fmaf(s[h], sl2, -m2[h])) : 0.f;
+          lp[h] += pe;
+          *reinterpret_cast<__nv_bfloat16*>(pdst + sw128_offset(h, t & 63)) = f2bf(pe);
+        }
+        fence_proxy_async_smem();
+        tc_fence_before();
+        mbar_arrive(&sm.p_full[sb]);
       }
-      if (okw && NC >= 1) okw = pv(NC - 1);
-      umma_commit(&sm.o_full);
-      umma_commit(&sm.drain);
-      mbar_wait(&sm.drain, 0, P.err);
-    }
-  } else if (warp >= 4) {
-    const int t = tid - 128;  // key row of the chunk / TMEM lane
-    const uint32_t lane_off = (uint32_t)((warp & 3) * 32) << 16;
-    const float sl2 = scale * kLog2e;
-    float lp[16];
-#pragma unroll
-    for (int h = 0; h < 16; ++h) lp[h] = 0.f;
-    float m2[16];
-#pragma unroll
-    for (int h = 0; h < 16; ++h) m2[h] = sm.m2[h];
-    bool okw = true;
-    for (int c = 0; c < NC; ++c) {
-      const int sb = c & 1;
-      if (!mbar_wait(&sm.s_full[sb], (c >> 1) & 1, P.err)) {
-        okw = false;
-        break;
+      // ---- C. epilogue ----
+      if (trace != nullptr && t == 0) {
+        unsigned long long ts;
+        asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(ts));
+        trace[3] = ts;
       }
-      tc_fence_after();
-      float s[16];
-      {
+  #pragma unroll
+      for (int h = 0; h < 16; ++h) lp[h] = warp_sum(lp[h]);
+      if (lane == 0)
+  #pragma unroll
+        for (int h = 0; h < 16; ++h) sm.lsum[warp & 3][h] = lp[h];
+      asm volatile("bar.sync 1, 128;\n" ::: "memory");  // the 4 softmax warps
+      if (okw && mbar_wait(&sm.o_full, 0, P.err)) {
+        tc_fence_after();
         uint32_t r[16];
         asm volatile(
             "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, "
             "[%16];\n"
             : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
               "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
-            : "r"(tmem + sb * 16 + lane_off));
+            : "r"(tmem + 32 + lane_off));
         tmem_ld_wait();
+        if (t < DH) {
 #pragma unroll
-        for (int h = 0; h < 16; ++h) s[h] = __uint_as_float(r[h]);
-      }
-      if (c >= 2 && !mbar_wait(&sm.p_free[sb], ((c - 2) >> 1) & 1, P.err)) {
-        okw = false;
-        break;
-      }
-      bool valid;
-      if (c < NCw) valid = w0 + c * kDtKeys + t <= pos;
-      else if (c < NCw + NCs) valid = t < nsink;
-      else valid = (c - NCw - NCs) * kDtKeys + t < nsel * geo.Bk;
-      unsigned char* pdst = sm.pt[sb][t >> 6];
-#pragma unroll
-      for (int h = 0; h < 16; ++h) {
-        const float pe = (valid && h < G) ? exp2f(fmaf(s[h], sl2, -m2[h])) : 0.f;
-        lp[h] += pe;
-        *reinterpret_cast<__nv_bfloat16*>(pdst + sw128_offset(h, t & 63)) = f2bf(pe);
-      }
-      fence_proxy_async_smem();
-      tc_fence_before();
-      mbar_arrive(&sm.p_full[sb]);
-    }
-    // ---- C. epilogue ----
-    if (trace != nullptr && t == 0) {
-      unsigned long long ts;
-      asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(ts));
-      trace[3] = ts;
-    }
-#pragma unroll
-    for (int h = 0; h < 16; ++h) lp[h] = warp_sum(lp[h]);
-    if (lane == 0)
-#pragma unroll
-      for (int h = 0; h < 16; ++h) sm.lsum[warp & 3][h] = lp[h];
-    asm volatile("bar.sync 1, 128;\n" ::: "memory");  // the 4 softmax warps
-    if (okw && mbar_wait(&sm.o_full, 0, P.err)) {
-      tc_fence_after();
-      uint32_t r[16];
-      asm volatile(
-          "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, "
-          "[%16];\n"
-          : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
-            "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
-          : "r"(tmem + 32 + lane_off));
-      tmem_ld_wait();
-      if (t < DH) {
-        for (int h = 0; h < G; ++h) {
-          const float L = sm.lsum[0][h] + sm.lsum[1][h] + sm.lsum[2][h] + sm.lsum[3][h];
-          const float O = __uint_as_float(r[h]);
-          p.out[((size_t)b * geo.Hq + g * G + h) * DH + t] = f2bf(L > 0.f ? O / L : 0.f);
+          for (int h = 0; h < 16; ++h) {
+            if (h < G) {
+              const float L = sm.lsum[0][h] + sm.lsum[1][h] + sm.lsum[2][h] + sm.lsum[3][h];
+              const float O = __uint_as_float(r[h]);
+              p.out[((size_t)b * geo.Hq + g * G + h) * DH + t] = f2bf(L > 0.f ? O / L : 0.f);
+            }
+          }
         }
-      }
-      if (t < G && p.lse != nullptr) {
-        const float L = sm.lsum[0][t] + sm.lsum[1][t] + sm.lsum[2][t] + sm.lsum[3][t];
-        p.lse[(size_t)b * geo.Hq + g * G + t] = L > 0.f ? (sm.m2[t] + log2f(L)) * 0.6931471805599453f : neg_inf();
+        if (t < G && p.lse != nullptr) {
+          const float L = sm.lsum[0][t] + sm.lsum[1][t] + sm.lsum[2][t] + sm.lsum[3][t];
+          p.lse[(size_t)b * geo.Hq + g * G + t] = L > 0.f ? (sm.m2[t] + log2f(L)) * 0.6931471805599453f : neg_inf();
+        }
       }
     }
   }
@@ -560,10 +749,13 @@ static bool dtc_map(CUtensorMap* m, const void* base, int B, int n, int H, int d
             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-bool decode_tc_supported(const Geom& geo, int dh, const void* k, const void* kr, const void* v) {
+bool decode_tc_supported(const Geom& geo, int dh, const void* k, const void* kr, const void* v, const void* summ,
+                         const void* supers) {
+  // TMA tiles and 1-D bulk copies start on 16-byte boundaries
   const bool aligned = ((reinterpret_cast<uintptr_t>(k) | reinterpret_cast<uintptr_t>(kr) |
-                         reinterpret_cast<uintptr_t>(v)) & 15u) == 0;
-  return geo.qknorm && (dh == 64 || dh == 128) && geo.Bk == 64 && geo.G <= 16 && geo.nb_cap <= kTopkMaxItems &&
+                         reinterpret_cast<uintptr_t>(v) | reinterpret_cast<uintptr_t>(summ) |
+                         reinterpret_cast<uintptr_t>(geo.hier ? supers : summ)) & 15u) == 0;
+  return geo.qknorm && (dh == 64 || dh == 128) && geo.Bk == 64 && geo.m >= 1 && 128 % geo.m == 0 && geo.G <= 16 && geo.nb_cap <= kTopkMaxItems &&
          (!geo.hier || (geo.ns_cap <= kTopkMaxItems && geo.beam * geo.F <= kTopkMaxItems)) && aligned &&
          dtc_encode_fn() != nullptr;
 }

@@ -76,7 +76,7 @@ struct AttnParams {
 // contiguous slots [c*T/N, (c+1)*T/N) of the T = B*Hkv*nchunk total.
 struct DecodeAttnParams {
   Geom geo;
-  unsigned long long* trace;  // debug: 8 global-timer stamps per CTA, or null
+  unsigned long long* trace;  // debug: 16 global-timer stamps per CTA, or null
   long long trace_ctas;
   QueryPos qp;
   int32_t ncw;          // window chunk slots per (sequence, kv head)
@@ -129,7 +129,8 @@ cudaError_t launch_decode_fused(const DecodeAttnParams& p, const __nv_bfloat16* 
                                 int dh, cudaStream_t st);
 size_t decode_fused_smem(int dh);
 // tcgen05 decode (hba_decode_tc.cu): one CTA per (sequence, kv head), QKNorm only.
-bool decode_tc_supported(const Geom& geo, int dh, const void* k, const void* kr, const void* v);
+bool decode_tc_supported(const Geom& geo, int dh, const void* k, const void* kr, const void* v, const void* summ,
+                         const void* supers);
 cudaError_t launch_decode_tc(const DecodeAttnParams& p, const __nv_bfloat16* summ, const __nv_bfloat16* supers,
                              const float* k_gain, int* err, int dh, cudaStream_t st);
 // tcgen05/TMEM prefill union softmax (hba_prefill_tc.cu).

@@ -1,7 +1,8 @@
 // sm_100a primitives: mbarriers, TMA tile loads, tcgen05 (TMEM allocation,
 // UMMA issue/commit, TMEM loads) and the UMMA shared-memory / instruction
-// descriptors.  Inline PTX, no library code.  Every wait is bounded: after
-// kSpinLimit polls it records an error in *err and returns false.
+// descriptors.  Inline PTX, no library code.  Every wait is bounded in time:
+// after kWaitNs of the global timer it records an error in *err and returns
+// false (a legitimate wait in these kernels lasts microseconds).
 #pragma once
 
 #include <cuda.h>
@@ -12,7 +13,13 @@
 namespace hba {
 namespace sm100 {
 
-constexpr uint32_t kSpinLimit = 1u << 28;
+constexpr unsigned long long kWaitNs = 200ull * 1000 * 1000;  // 200 ms
+
+HBA_DEVICE unsigned long long global_ns() {
+  unsigned long long t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
 
 HBA_DEVICE void mbar_init(uint64_t* bar, uint32_t count) {
   asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;\n" ::"r"(smem_u32(bar)), "r"(count));
@@ -34,10 +41,24 @@ HBA_DEVICE bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
       : "memory");
   return ok != 0;
 }
+// Non-blocking test (try_wait may suspend the thread for a while).
+HBA_DEVICE bool mbar_test_wait(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n .reg .pred p;\n mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
 // Bounded wait for the phase with the given parity; false (and *err set) on timeout.
 HBA_DEVICE bool mbar_wait(uint64_t* bar, uint32_t parity, int* err) {
-  for (uint32_t i = 0; i < kSpinLimit; ++i)
+  if (mbar_try_wait(bar, parity)) return true;
+  const unsigned long long t0 = global_ns();
+  for (uint32_t i = 1;; ++i) {
     if (mbar_try_wait(bar, parity)) return true;
+    if ((i & 63) == 0 && global_ns() - t0 > kWaitNs) break;
+  }
   if (err != nullptr) atomicExch(err, 1);
   return false;
 }
@@ -57,6 +78,15 @@ HBA_DEVICE void tma_load_4d(void* dst, const CUtensorMap* map, int c0, int c1, i
       "[%6];\n" ::"r"(smem_u32(dst)),
       "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(c2), "r"(c3), "r"(smem_u32(bar))
       : "memory");
+}
+
+// 1-D bulk copy global -> shared (16-byte aligned addresses, size a multiple
+// of 16), completion counted on `bar` (bytes).  Never multicast.
+HBA_DEVICE void bulk_load(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];\n" ::"r"(
+                   smem_u32(dst)),
+               "l"(reinterpret_cast<uint64_t>(src)), "r"(bytes), "r"(smem_u32(bar))
+               : "memory");
 }
 
 // ---- tcgen05 ----

@@ -33,7 +33,9 @@ struct TopkScratch {
 
 // Every thread of the block must call this (contains barriers).  Writes the
 // selected entries, best first, to ts.sel_idx / ts.sel_score[0..n) and
-// returns n = min(k, R, 32).  NT = blockDim.x.
+// returns n = min(k, R, 32).  NT = blockDim.x.  id == nullptr means the
+// candidate's id is its position j (callers whose ids grow with j map the
+// returned positions to ids afterwards).
 template <int NT>
 HBA_DEVICE int block_topk(const float* __restrict__ sc, const int* __restrict__ id, int R, int k,
                           TopkScratch& ts) {
@@ -119,7 +121,7 @@ HBA_DEVICE int block_topk(const float* __restrict__ sc, const int* __restrict__ 
         } else {  // genuine ties at the boundary: keep the lowest indices
           int before = 0;
           for (int i = 0; i < R; ++i)
-            if (order_key(sc[i]) == v && id[i] < id[j]) ++before;
+            if (order_key(sc[i]) == v && (id ? id[i] : i) < (id ? id[j] : j)) ++before;
           pick = before < need_ties;
         }
       }
@@ -136,12 +138,12 @@ HBA_DEVICE int block_topk(const float* __restrict__ sc, const int* __restrict__ 
   if (tid < n) {
     const int j = ts.sel_idx[tid];
     my_s = sc[j];
-    my_id = id[j];
+    my_id = id ? id[j] : j;
     int r = 0;
     for (int i = 0; i < n; ++i) {
       const int ji = ts.sel_idx[i];
       const float si = sc[ji];
-      const int ii = id[ji];
+      const int ii = id ? id[ji] : ji;
       r += (si > my_s) || (si == my_s && ii < my_id);
     }
     my_pos = r;

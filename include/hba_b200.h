@@ -205,10 +205,12 @@ int hba_b200_profile_events_recorded(void);
 
 /*
  * Debug hook (no counterpart in the reference): with a non-NULL device
- * buffer, later one-CTA-per-head decode kernels write 8 uint64 global-timer
- * stamps per CTA (kernel start, after the query prologue, after selection,
- * after the union softmax, end, and three spare) to buffer[blockIdx * 8 + i],
- * for CTAs with blockIdx * 64 < bytes.  NULL turns it off.
+ * buffer, later tcgen05 decode kernels write 16 uint64 global-timer stamps
+ * per CTA to buffer[blockIdx * 16 + i], for CTAs with blockIdx * 128 < bytes:
+ * 0 kernel start, 1 after the query prologue, 2 after selection, 3 after the
+ * union softmax, 4 end, 5-7 selection sub-phases, 8-15 arrival at and
+ * release by the scoring warp of the first four summary pages.  NULL turns it
+ * off.
  */
 int hba_b200_set_debug_trace(void* device_buffer, int64_t bytes);
 
