@@ -46,6 +46,8 @@ def parse():
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--config", default="cfg1", choices=["cfg1", "cfg2", "cfg3"])
     ap.add_argument("--no-secondary", action="store_true")
+    ap.add_argument("--ncu-case", default=None, choices=["cfg1", "cfg3"],
+                    help="profiling target: build this decode workload (cfg3 at batch 4), run 3 decodes, exit")
     return ap.parse_args()
 
 
@@ -184,6 +186,29 @@ def kernel_times(call, steps, flush, n_events):
     return [statistics.mean(x) for x in zip(*per)]
 
 
+def ncu_case(name, local):
+    """Profiling target: the decode workload `name` (cfg3 at batch 4, so that
+    the device holds a few GB), decoded 3 times; no timing, no output."""
+    from hba_b200 import HBADecodeCache, baseline_config, synth
+    from hba_b200.attention import stream_of
+    dev = torch.device("cuda", local)
+    cfg, B, n, hier = baseline_config(name)
+    if name == "cfg3":
+        B = 4
+    summ, qkn = synth.make_weights(cfg, dev, seed=0, gains=False)
+    cos, sin = synth.rope_tables(n, cfg.head_dim, 1e6, dev)
+    wl = synth.decode_workload(cfg, B, n, hier=hier, seed=1000, device=dev, qkn=qkn)
+    cache = HBADecodeCache(cfg, B, n, summ, qkn, cos, sin, device=dev, hier=hier)
+    cache.append(wl["k"], wl["v"])
+    del wl["k"], wl["v"]
+    q = wl["q"].contiguous()
+    out = torch.empty_like(q)
+    lse = torch.empty(B, cfg.n_heads, dtype=torch.float32, device=dev)
+    for _ in range(3):
+        cache.decode_into(q, out, lse, stream=stream_of(dev))
+    torch.cuda.synchronize()
+
+
 def decode_bench(name, steps, warmup, world, rank, local, pk):
     from hba_b200 import HBADecodeCache, baseline_config, synth
     from hba_b200.attention import stream_of
@@ -217,9 +242,13 @@ def decode_bench(name, steps, warmup, world, rank, local, pk):
     t_ms = statistics.mean(times)
     t_ms = max_over_ranks(t_ms, world, dev)
 
-    # dominant kernel (attend) timed live between the library's event marks
+    # dominant kernel timed live between the library's event marks: the one
+    # decode kernel (tcgen05 / fused paths) or the attend kernel of the split path
+    from hba_b200 import _lib
     nmarks = 4 if hier else 3          # begin | select (super, child) | attend
     kt = kernel_times(step_direct, max(3, min(steps, 10)), flush, nmarks)
+    kernels = _lib.load().hba_b200_last_decode_kernels().decode()
+    single = "+" not in kernels
     attend_ms = kt[-1]
     keys = cfg.sinks + cfg.window + cfg.k_blocks * cfg.block
     attend_bytes = B * Hkv * (keys * dh * 2 * 2 + G * dh * 2 * 2)
@@ -230,9 +259,10 @@ def decode_bench(name, steps, warmup, world, rank, local, pk):
         n_cand = (n - 1 - cfg.window + 1) // cfg.block - 1
         summ_bytes = B * Hkv * n_cand * cfg.slots * dh * 2
     step_bytes = attend_bytes + summ_bytes
-    achieved = attend_bytes / (attend_ms * 1e-3) / 1e9
-    tkey = f"attend_{name}"
-    traffic = traffic_of(tkey)
+    dom_kernel = kernels if single else "decode_attend_kernel"
+    dom_bytes = step_bytes if single else attend_bytes
+    achieved = dom_bytes / (attend_ms * 1e-3) / 1e9
+    traffic = traffic_of(f"{dom_kernel}_{name}")
 
     # e2e: the C-ABI call with the query from pinned host memory and out + lse back
     q_host = q.cpu().pin_memory()
@@ -259,12 +289,13 @@ def decode_bench(name, steps, warmup, world, rank, local, pk):
                     fanout=cfg.fanout if hier else None, beam=cfg.beam if hier else None,
                     l2="flushed (256 MB write) before every timed step", timing="CUDA graph replay, CUDA events",
                     parallelism=f"replicas x{world} (batch-sharded, no collective)"),
-        roofline=dict(bound="hbm", kernel="attend_kernel", achieved=achieved, peak=pk["hbm"], unit="GB/s",
+        roofline=dict(bound="hbm", kernel=dom_kernel, achieved=achieved, peak=pk["hbm"], unit="GB/s",
                       frac=achieved / pk["hbm"], peak_source=pk["source"], traffic=traffic,
-                      algorithmic_bytes_per_launch=attend_bytes, kernel_ms=attend_ms),
+                      algorithmic_bytes_per_launch=dom_bytes, kernel_ms=attend_ms),
         step_effective_gbs=step_bytes / (t_ms * 1e-3) / 1e9,
         step_algorithmic_bytes=step_bytes,
-        kernel_ms={"select": kt[:-1], "attend": attend_ms},
+        decode_kernels=kernels,
+        kernel_ms={"select": kt[:-1], "attend": attend_ms} if not single else {kernels: attend_ms},
         cache_build_s=build_s,
         e2e=dict(value=B * world / (e2e_ms * 1e-3), unit="decode queries/s", ms_per_step=e2e_ms,
                  h2d_bytes_per_step=q.numel() * q.element_size(),
@@ -454,6 +485,9 @@ def main():
     sys.path.insert(0, os.path.join(ROOT, "hierarchical-block-attention_b200"))
     import hba_b200  # noqa: F401  (fails loudly if the CUDA library is missing)
     hba_b200.load_library()
+    if args.ncu_case is not None:
+        ncu_case(args.ncu_case, local)
+        return
     pk = peaks()
     if args.config in ("cfg1", "cfg3"):
         res = decode_bench(args.config, args.steps, args.warmup, world, rank, local, pk)

@@ -26,6 +26,7 @@ struct ProfileHook {
 ProfileHook g_prof;
 unsigned long long* g_trace = nullptr;  // hba_b200_set_debug_trace
 long long g_trace_ctas = 0;
+const char* g_last_decode = "";  // hba_b200_last_decode_kernels
 
 void prof_begin(cudaStream_t st) {
   g_prof.next = 0;
@@ -276,6 +277,8 @@ int hba_b200_set_profile_events(void* const* events, int32_t count) {
 
 int hba_b200_profile_events_recorded(void) { return g_prof.next; }
 
+const char* hba_b200_last_decode_kernels(void) { return g_last_decode; }
+
 int hba_b200_set_debug_trace(void* device_buffer, int64_t bytes) {
   if (bytes < 0 || (device_buffer == nullptr && bytes != 0)) return HBA_B200_ERR_INVALID_ARGUMENT;
   g_trace = static_cast<unsigned long long*>(device_buffer);
@@ -422,9 +425,11 @@ int hba_b200_decode(const hba_b200_config* cfg, int32_t batch, int32_t n_cap, co
                                    static_cast<const __nv_bfloat16*>(supers), cfg->head_dim, stream);
     }
     if (e != cudaSuccess) return cuda_status(e);
+    g_last_decode = path == kDecodeTc ? "decode_tc_kernel" : "decode_fused_kernel";
     prof_mark(stream);
     return HBA_B200_OK;
   }
+  g_last_decode = "select_kernel+decode_attend_kernel";
   Lists fin{};
   int fin_lists = 0, fin_k = 0;
   st = run_select(cfg, geo, qp, plan, static_cast<const __nv_bfloat16*>(q), q_gain,

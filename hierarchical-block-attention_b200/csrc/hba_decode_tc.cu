@@ -48,6 +48,34 @@ constexpr int kDtScoreWarps = 7;  // every other warp scores summary pages
 // barrier of the 7 scoring warps (the producer warp never joins it)
 HBA_DEVICE void score_bar() { asm volatile("bar.sync 2, 224;\n" ::: "memory"); }
 
+// 2^x by the MUFU instruction (ex2.approx.ftz: relative error ~2^-22, far
+// below the bf16 rounding of the probabilities it feeds)
+HBA_DEVICE float ex2_approx(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+// N fp32 columns of this thread's TMEM lane (32x32b shape), waited.
+template <int N>
+HBA_DEVICE void tmem_ld_row(uint32_t taddr, float* v) {
+  uint32_t r[N];
+  if constexpr (N == 8) {
+    asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];\n"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7])
+                 : "r"(taddr));
+  } else {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];\n"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
+          "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+        : "r"(taddr));
+  }
+  asm volatile("tcgen05.wait::ld.sync.aligned;\n" ::: "memory");
+#pragma unroll
+  for (int i = 0; i < N; ++i) v[i] = __uint_as_float(r[i]);
+}
+
 // Warp-wide (score, id) compare-exchange with the lane `stride` away under
 // the library order (score desc, id asc); keep_better selects which of the
 // pair this lane keeps.
@@ -126,7 +154,7 @@ struct DecodeTcParams {
   int* err;
 };
 
-template <int DH, int VPL>
+template <int DH, int HB>
 __global__ void __launch_bounds__(kDtThreads, 1)
     decode_tc_kernel(const __grid_constant__ CUtensorMap tm_kc, const __grid_constant__ CUtensorMap tm_kr,
                      const __grid_constant__ CUtensorMap tm_v, DecodeTcParams P) {
@@ -359,7 +387,15 @@ __global__ void __launch_bounds__(kDtThreads, 1)
       for (int h = 0; h < G; ++h) acc += bf2f(*reinterpret_cast<const __nv_bfloat16*>(sm.qc[d / 64] + sw128_offset(h, d % 64)));
       sm.qg[d] = round_bf16(acc);
     }
-    fence_proxy_async_smem();  // Q tiles are read by the tensor cores
+    if constexpr (HB < 16) {  // P^T rows of heads >= HB stay zero for the whole kernel
+      // 4 tiles [buffer][key half] of 16 rows x 128 B; rows 8-15 = the second
+      // 1024-byte swizzle atom = 64 chunks of 16 B per tile
+      for (int e = sw * 32 + lane; e < 4 * 64; e += NSW * 32) {
+        const int tile = e >> 6, rem = e & 63;
+        *reinterpret_cast<uint4*>(sm.pt[tile >> 1][tile & 1] + 1024 + rem * 16) = make_uint4(0, 0, 0, 0);
+      }
+    }
+    fence_proxy_async_smem();  // Q and P^T tiles are read by the tensor cores
     score_bar();
     stamp(1);
 
@@ -391,7 +427,6 @@ __global__ void __launch_bounds__(kDtThreads, 1)
       for (int pg = sw; pg < np; pg += NSW) {
         const int i = i0 + pg;
         mbar_wait(&sm.full[i % NSLOT], (i / NSLOT) & 1, P.err);
-        if (trace != nullptr && lane == 0 && i < 4) trace[8 + 2 * i] = global_ns();
         const unsigned char* src = sm.ring[i % NSLOT];
         const int nr = min(PB, R - pg * PB);
         for (int rg = 0; rg < nr; rg += 32) {
@@ -475,7 +510,6 @@ __global__ void __launch_bounds__(kDtThreads, 1)
         }
         __syncwarp();
         if (lane == 0) mbar_arrive(&sm.empty[i % NSLOT]);
-        if (trace != nullptr && lane == 0 && i < 4) trace[9 + 2 * i] = global_ns();
       }
     };
     // merges the 7 warp lists in a 3-round tree: best-first picks in
@@ -591,7 +625,7 @@ __global__ void __launch_bounds__(kDtThreads, 1)
           const uint32_t pa = smem_u32(sm.pt[sb][0]);
           // dh 64: M = 128 reads a second MN group at LBO 0 (rows 64-127 of O^T duplicate 0-63, unused)
           const uint32_t lbo = DH == 128 ? kDtKeys * 128 : 0;
-  #pragma unroll
+#pragma unroll
           for (int kk = 0; kk < kDtKeys / 16; ++kk)
             umma_f16(tmem + 32, sdesc_sw128(va + kk * 2048, lbo, 1024),
                      sdesc_sw128(pa + (kk >> 2) * 2048 + (kk & 3) * 32, 16, 1024), idesc_o,
@@ -609,7 +643,7 @@ __global__ void __launch_bounds__(kDtThreads, 1)
           tc_fence_after();
           const bool window = c < NCw;
           const uint32_t ka = smem_u32(sm.ring[ik % NSLOT]);
-  #pragma unroll
+#pragma unroll
           for (int kk = 0; kk < DH / 16; ++kk) {
             const int h = kk >> 2, ko = (kk & 3) * 32;
             const uint32_t qa = smem_u32(window ? sm.qr[h] : sm.qc[h]);
@@ -632,12 +666,12 @@ __global__ void __launch_bounds__(kDtThreads, 1)
       const int t = tid - 128;  // key row of the chunk / TMEM lane
       const uint32_t lane_off = (uint32_t)((warp & 3) * 32) << 16;
       const float sl2 = scale * kLog2e;
-      float lp[16];
-  #pragma unroll
-      for (int h = 0; h < 16; ++h) lp[h] = 0.f;
-      float m2[16];
-  #pragma unroll
-      for (int h = 0; h < 16; ++h) m2[h] = sm.m2[h];
+      float lp[HB], m2[HB];
+#pragma unroll
+      for (int h = 0; h < HB; ++h) {
+        lp[h] = 0.f;
+        m2[h] = sm.m2[h];
+      }
       bool okw = true;
       for (int c = 0; c < NC; ++c) {
         const int sb = c & 1;
@@ -646,19 +680,8 @@ __global__ void __launch_bounds__(kDtThreads, 1)
           break;
         }
         tc_fence_after();
-        float s[16];
-        {
-          uint32_t r[16];
-          asm volatile(
-              "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, "
-              "[%16];\n"
-              : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
-                "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
-              : "r"(tmem + sb * 16 + lane_off));
-          tmem_ld_wait();
-  #pragma unroll
-          for (int h = 0; h < 16; ++h) s[h] = __uint_as_float(r[h]);
-        }
+        float s[HB];
+        tmem_ld_row<HB>(tmem + sb * 16 + lane_off, s);
         if (c >= 2 && !mbar_wait(&sm.p_free[sb], ((c - 2) >> 1) & 1, P.err)) {
           okw = false;
           break;
@@ -668,9 +691,11 @@ __global__ void __launch_bounds__(kDtThreads, 1)
         else if (c < NCw + NCs) valid = t < nsink;
         else valid = (c - NCw - NCs) * kDtKeys + t < nsel * geo.Bk;
         unsigned char* pdst = sm.pt[sb][t >> 6];
-  #pragma unroll
-        for (int h = 0; h < 16; ++h) {
-          const float pe = (valid && h < G) ? exp2f(fmaf(s[h], sl2, -m2[h])) : 0.f;
+        // branch-free over the HB head rows (rows >= HB were zeroed in the prologue)
+#pragma unroll
+        for (int h = 0; h < HB; ++h) {
+          float pe = ex2_approx(fmaf(s[h], sl2, -m2[h]));
+          pe = (valid && h < G) ? pe : 0.f;
           lp[h] += pe;
           *reinterpret_cast<__nv_bfloat16*>(pdst + sw128_offset(h, t & 63)) = f2bf(pe);
         }
@@ -684,11 +709,11 @@ __global__ void __launch_bounds__(kDtThreads, 1)
         asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(ts));
         trace[3] = ts;
       }
-  #pragma unroll
-      for (int h = 0; h < 16; ++h) lp[h] = warp_sum(lp[h]);
+#pragma unroll
+      for (int h = 0; h < HB; ++h) lp[h] = warp_sum(lp[h]);
       if (lane == 0)
-  #pragma unroll
-        for (int h = 0; h < 16; ++h) sm.lsum[warp & 3][h] = lp[h];
+#pragma unroll
+        for (int h = 0; h < HB; ++h) sm.lsum[warp & 3][h] = lp[h];
       asm volatile("bar.sync 1, 128;\n" ::: "memory");  // the 4 softmax warps
       if (okw && mbar_wait(&sm.o_full, 0, P.err)) {
         tc_fence_after();
@@ -744,8 +769,12 @@ static bool dtc_map(CUtensorMap* m, const void* base, int B, int n, int H, int d
   cuuint64_t strides[3] = {(cuuint64_t)dh * 2, (cuuint64_t)H * dh * 2, (cuuint64_t)n * H * dh * 2};
   cuuint32_t box[4] = {64, 1, 64, 1};
   cuuint32_t es[4] = {1, 1, 1, 1};
+  // a head's slice of a token row is dh*2 bytes: promote L2 fills no wider,
+  // or every routed row would also drag in its neighbour head's slice
+  const CUtensorMapL2promotion promo = dh * 2 >= 256 ? CU_TENSOR_MAP_L2_PROMOTION_L2_256B
+                                                     : CU_TENSOR_MAP_L2_PROMOTION_L2_128B;
   return fn(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, const_cast<void*>(base), dims, strides, box, es,
-            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, promo,
             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
@@ -760,14 +789,14 @@ bool decode_tc_supported(const Geom& geo, int dh, const void* k, const void* kr,
          dtc_encode_fn() != nullptr;
 }
 
-template <int DH, int VPL>
+template <int DH, int HB>
 static cudaError_t launch_dtc_t(const CUtensorMap& a, const CUtensorMap& b, const CUtensorMap& c,
                                 const DecodeTcParams& P, cudaStream_t st) {
   const size_t smem = sizeof(DtcSmem<DH>) + 1024;
   static const cudaError_t attr =
-      cudaFuncSetAttribute(decode_tc_kernel<DH, VPL>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+      cudaFuncSetAttribute(decode_tc_kernel<DH, HB>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (attr != cudaSuccess) return attr;
-  decode_tc_kernel<DH, VPL><<<P.a.geo.B * P.a.geo.Hkv, kDtThreads, smem, st>>>(a, b, c, P);
+  decode_tc_kernel<DH, HB><<<P.a.geo.B * P.a.geo.Hkv, kDtThreads, smem, st>>>(a, b, c, P);
   return cudaGetLastError();
 }
 
@@ -779,14 +808,9 @@ cudaError_t launch_decode_tc(const DecodeAttnParams& p, const __nv_bfloat16* sum
       !dtc_map(&m_v, p.v, geo.B, geo.n_cap, geo.Hkv, dh))
     return cudaErrorInvalidValue;
   DecodeTcParams P{p, summ, supers, k_gain, err};
-  const int vpl = (geo.m * dh / 8 + 31) / 32;
-  if (dh == 64) {
-    if (vpl <= 1) return launch_dtc_t<64, 1>(m_kc, m_kr, m_v, P, st);
-    return launch_dtc_t<64, 2>(m_kc, m_kr, m_v, P, st);
-  }
-  if (vpl <= 1) return launch_dtc_t<128, 1>(m_kc, m_kr, m_v, P, st);
-  if (vpl <= 2) return launch_dtc_t<128, 2>(m_kc, m_kr, m_v, P, st);
-  return launch_dtc_t<128, 4>(m_kc, m_kr, m_v, P, st);
+  // softmax head rows: 8 when the group fits, else all 16 of the MMA's N
+  if (dh == 64) return geo.G <= 8 ? launch_dtc_t<64, 8>(m_kc, m_kr, m_v, P, st) : launch_dtc_t<64, 16>(m_kc, m_kr, m_v, P, st);
+  return geo.G <= 8 ? launch_dtc_t<128, 8>(m_kc, m_kr, m_v, P, st) : launch_dtc_t<128, 16>(m_kc, m_kr, m_v, P, st);
 }
 
 }  // namespace hba

@@ -208,11 +208,18 @@ int hba_b200_profile_events_recorded(void);
  * buffer, later tcgen05 decode kernels write 16 uint64 global-timer stamps
  * per CTA to buffer[blockIdx * 16 + i], for CTAs with blockIdx * 128 < bytes:
  * 0 kernel start, 1 after the query prologue, 2 after selection, 3 after the
- * union softmax, 4 end, 5-7 selection sub-phases, 8-15 arrival at and
- * release by the scoring warp of the first four summary pages.  NULL turns it
- * off.
+ * union softmax, 4 end, 5-7 selection sub-phases, 8-15 softmax of K/V
+ * chunks 0, 2, ..., 14 done.  NULL turns it off.
  */
 int hba_b200_set_debug_trace(void* device_buffer, int64_t bytes);
+
+/*
+ * Introspection (no counterpart in the reference): the kernels the last
+ * hba_b200_decode / hba_b200_decode_noalloc call of this process launched, as
+ * a static string ("decode_tc_kernel", "decode_fused_kernel" or
+ * "select_kernel+decode_attend_kernel"; "" before the first call).
+ */
+const char* hba_b200_last_decode_kernels(void);
 
 #ifdef __cplusplus
 }
