@@ -184,6 +184,9 @@ int run_select(const hba_b200_config* c, const Geom& geo, const hba::QueryPos& q
   sp.out_idx = l1.idx;
   sp.counters = c->hier ? nullptr : counters;
   sp.pdl = 0;
+  sp.own_blo = 0;
+  sp.own_bhi = INT_MAX;
+  sp.n_limit = geo.n_cap;
   cudaError_t e = hba::launch_select(sp, dh, st);
   if (e != cudaSuccess) return cuda_status(e);
   prof_mark(st);
@@ -577,6 +580,101 @@ int hba_b200_prefill(const hba_b200_config* cfg, int32_t batch, int32_t n, float
   if (e != cudaSuccess) return cuda_status(e);
   prof_mark(stream);
   return HBA_B200_OK;
+}
+
+
+// ---- KV-range sharded decode ----
+
+int hba_b200_decode_shard_select(const hba_b200_config* cfg, int32_t batch, int32_t n_cap_local, int32_t tok_lo,
+                                 int32_t level, const int32_t* seq_lens, const float* scales, const void* q,
+                                 const float* q_gain, const void* summaries, const void* supers,
+                                 const int32_t* in_idx, const float* in_score, int32_t n_in_lists, int32_t* out_idx,
+                                 float* out_score, cudaStream_t stream) {
+  int st = HBA_B200_OK;
+  if (!config_ok(cfg, &st)) return st;
+  const int F = cfg->hier ? cfg->fanout : 1;
+  if (batch <= 0 || n_cap_local <= 0 || tok_lo < 0 || seq_lens == nullptr || scales == nullptr || q == nullptr ||
+      (cfg->qknorm && q_gain == nullptr) || out_idx == nullptr || out_score == nullptr || level < 0 || level > 2 ||
+      (level == 0 && cfg->hier) || (level > 0 && !cfg->hier) || (level == 1 && supers == nullptr) ||
+      (level != 1 && summaries == nullptr) || (level == 2 && (in_idx == nullptr || in_score == nullptr || n_in_lists <= 0)))
+    return HBA_B200_ERR_INVALID_ARGUMENT;
+  // shard bounds on block (hier: super) boundaries, so no block or super straddles two shards
+  const long long unit = (long long)cfg->block * F;
+  if (n_cap_local % unit != 0 || tok_lo % unit != 0) return HBA_B200_ERR_NOT_BLOCK_MULTIPLE;
+  const int nb_local = n_cap_local / cfg->block;
+  if (nb_local > 2048 || (long long)cfg->beam * F > 2048 || n_in_lists * cfg->beam > 4096)
+    return HBA_B200_ERR_UNSUPPORTED;  // one CTA per (sequence, kv head) scores at most 2048 rows
+  Geom geo = make_geom(cfg, batch, 1, n_cap_local);
+  hba::SelParams sp{};
+  sp.geo = geo;
+  sp.qp = hba::QueryPos{seq_lens, scales, 0, 0.f};
+  sp.q = static_cast<const __nv_bfloat16*>(q);
+  sp.q_gain = q_gain;
+  sp.summ = static_cast<const __nv_bfloat16*>(summaries);
+  sp.supers = static_cast<const __nv_bfloat16*>(supers);
+  sp.mode = level == 0 ? hba::kSelFlat : (level == 1 ? hba::kSelSuper : hba::kSelChild);
+  sp.splits = 1;
+  sp.list_k = level == 1 ? cfg->beam : cfg->k_blocks;
+  sp.in_lists = level == 2 ? n_in_lists : 0;
+  sp.in_idx = in_idx;
+  sp.in_score = in_score;
+  sp.out_idx = out_idx;
+  sp.out_score = out_score;
+  sp.counters = nullptr;
+  sp.pdl = 0;
+  sp.own_blo = tok_lo / cfg->block;
+  sp.own_bhi = (tok_lo + n_cap_local) / cfg->block;
+  sp.n_limit = INT_MAX;  // contexts run past this shard
+  return cuda_status(hba::launch_select(sp, cfg->head_dim, stream));
+}
+
+int hba_b200_decode_shard_attend(const hba_b200_config* cfg, int32_t batch, int32_t n_cap_local, int32_t tok_lo,
+                                 const int32_t* seq_lens, const float* scales, const void* q, const float* q_gain,
+                                 const float* k_gain, const void* k_cache, const void* k_rope_cache,
+                                 const void* v_cache, const float* cos, const float* sin, const int32_t* in_idx,
+                                 const float* in_score, int32_t n_in, float* part_o, float* part_l, float* part_m2,
+                                 int32_t* sel_idx, float* sel_score, int32_t* dev_status, cudaStream_t stream) {
+  int st = HBA_B200_OK;
+  if (!config_ok(cfg, &st)) return st;
+  if (batch <= 0 || n_cap_local <= 0 || tok_lo < 0 || seq_lens == nullptr || scales == nullptr || q == nullptr ||
+      q_gain == nullptr || k_gain == nullptr || k_cache == nullptr || k_rope_cache == nullptr || v_cache == nullptr ||
+      cos == nullptr || sin == nullptr || in_idx == nullptr || in_score == nullptr || n_in <= 0 ||
+      part_o == nullptr || part_l == nullptr || part_m2 == nullptr || dev_status == nullptr ||
+      ((sel_idx == nullptr) != (sel_score == nullptr)))
+    return HBA_B200_ERR_INVALID_ARGUMENT;
+  if (n_cap_local % cfg->block != 0 || tok_lo % cfg->block != 0) return HBA_B200_ERR_NOT_BLOCK_MULTIPLE;
+  if (tok_lo > 0 && tok_lo < cfg->sinks) return HBA_B200_ERR_UNSUPPORTED;  // the sinks live on one shard
+  Geom geo = make_geom(cfg, batch, 1, n_cap_local);
+  if (!hba::decode_tc_supported(geo, cfg->head_dim, k_cache, k_rope_cache, v_cache, nullptr, nullptr))
+    return HBA_B200_ERR_UNSUPPORTED;  // the shard partials use the tensor-core path's fixed logit bound
+  hba::DecodeAttnParams dp{};
+  dp.geo = geo;
+  dp.qp = hba::QueryPos{seq_lens, scales, 0, 0.f};
+  dp.q = static_cast<const __nv_bfloat16*>(q);
+  dp.q_gain = q_gain;
+  dp.k = static_cast<const __nv_bfloat16*>(k_cache);
+  dp.kr = static_cast<const __nv_bfloat16*>(k_rope_cache);
+  dp.v = static_cast<const __nv_bfloat16*>(v_cache);
+  dp.cos = cos;
+  dp.sin = sin;
+  dp.sel_idx = sel_idx;
+  dp.sel_score = sel_score;
+  cudaError_t e = cudaMemsetAsync(dev_status, 0, sizeof(int32_t), stream);
+  if (e == cudaSuccess)
+    e = hba::launch_decode_tc_shard(dp, k_gain, dev_status, cfg->head_dim, tok_lo, in_idx, in_score, n_in, part_o,
+                                    part_l, part_m2, stream);
+  return cuda_status(e);
+}
+
+int hba_b200_decode_shard_finish(const hba_b200_config* cfg, int32_t batch, const float* part_o,
+                                 const float* part_l, const float* part_m2, void* out, float* lse,
+                                 cudaStream_t stream) {
+  int st = HBA_B200_OK;
+  if (!config_ok(cfg, &st)) return st;
+  if (batch <= 0 || part_o == nullptr || part_l == nullptr || part_m2 == nullptr || out == nullptr)
+    return HBA_B200_ERR_INVALID_ARGUMENT;
+  return cuda_status(hba::launch_shard_finish(batch * cfg->n_heads, cfg->head_dim, part_o, part_l, part_m2,
+                                              static_cast<__nv_bfloat16*>(out), lse, stream));
 }
 
 }  // extern "C"

@@ -152,6 +152,19 @@ struct DecodeTcParams {
   const __nv_bfloat16* supers;
   const float* k_gain;
   int* err;
+  // KV-range shard mode (mode 1): this CTA's caches hold global tokens
+  // [tok_lo, tok_lo + n_cap); the picks are the global top-k of the n_in
+  // candidate entries per (sequence, kv head) in in_idx / in_score (every
+  // shard's local lists); the union over the owned tokens is written as the
+  // unnormalised O, l and the logit bound m2 (identical on every shard).
+  int32_t mode;
+  int32_t tok_lo;
+  int32_t n_in;
+  const int32_t* in_idx;  // [B*Hkv, n_in] global block ids, -1 = none
+  const float* in_score;
+  float* part_o;          // [B, Hq, dh]
+  float* part_l;          // [B, Hq]
+  float* part_m2;         // [B, Hq]
 };
 
 template <int DH, int HB>
@@ -173,7 +186,10 @@ __global__ void __launch_bounds__(kDtThreads, 1)
   const int G = geo.G;
   const int bg = blockIdx.x;
   const int b = bg / geo.Hkv, g = bg % geo.Hkv;
-  const bool hier = geo.hier != 0;
+  const bool shard = P.mode == 1;
+  const bool hier = geo.hier != 0 && !shard;  // a shard gets its picks from the lists
+  const int tok_lo = shard ? P.tok_lo : 0;    // global token of local row 0
+  const int tok_hi = tok_lo + geo.n_cap;      // end of the owned tokens
   unsigned long long* trace = (p.trace != nullptr && bg < p.trace_ctas) ? p.trace + (size_t)bg * 16 : nullptr;
   auto stamp = [&](int i) {
     if (trace != nullptr && tid == 0) trace[i] = global_ns();
@@ -182,16 +198,18 @@ __global__ void __launch_bounds__(kDtThreads, 1)
 
   const int nctx = p.qp.seq_lens[b];
   const float scale = p.qp.scales[b];
-  const bool ok = nctx >= 1 && nctx <= geo.n_cap;
+  const bool ok = nctx >= 1 && (shard || nctx <= geo.n_cap);
   const int pos = ok ? nctx - 1 : -1;
   const int nb = ok ? nctx / geo.Bk : 0;
   const int bmax = ok ? min(last_candidate(pos, geo.W, geo.Bk), nb - 1) : 0;
   int kfinal = min(geo.K, nb);
   const int ns = (nb + geo.F - 1) / geo.F;
-  if (hier) kfinal = min(kfinal, min(geo.beam, ns) * geo.F);
-  const int w0 = max(geo.S, pos - geo.W + 1);
-  const int nw = ok ? max(0, pos - w0 + 1) : 0;
-  const int nsink = ok ? min(geo.S, pos + 1) : 0;
+  if (geo.hier) kfinal = min(kfinal, min(geo.beam, ns) * geo.F);  // shards too: the global k
+  // owned part of the window [wlo, whi] (global tokens) and of the sinks
+  const int wlo = max(max(geo.S, pos - geo.W + 1), tok_lo);
+  const int whi = min(pos, tok_hi - 1);
+  const int nw = ok ? max(0, whi - wlo + 1) : 0;
+  const int nsink = (ok && tok_lo == 0) ? min(geo.S, pos + 1) : 0;
   const int NCw = (nw + kDtKeys - 1) / kDtKeys;
   const int NCs = nsink > 0 ? 1 : 0;
   const bool producer = warp == kDtProducer;
@@ -228,7 +246,9 @@ __global__ void __launch_bounds__(kDtThreads, 1)
   const __nv_bfloat16* summ_bg = P.summ + (size_t)bg * geo.nb_cap * row_elems;
   const __nv_bfloat16* sup_bg = hier ? P.supers + (size_t)bg * geo.ns_cap * row_elems : nullptr;
   int Ra = 0, ida = 1;  // phase-A candidates: flat blocks 1..bmax, or supers ida..
-  if (!hier) {
+  if (shard) {
+    Ra = 0;  // picks come from the lists
+  } else if (!hier) {
     Ra = max(0, bmax);
   } else if (bmax >= 1) {
     ida = (geo.F == 1) ? 1 : 0;
@@ -294,7 +314,7 @@ __global__ void __launch_bounds__(kDtThreads, 1)
           int kind, t0, t1;
           if (c < NCw) {
             kind = 0;
-            t0 = w0 + c * kDtKeys;
+            t0 = wlo - tok_lo + c * kDtKeys;  // local row
             t1 = t0 + 64;
           } else if (c < NCw + NCs) {
             kind = 1;
@@ -542,7 +562,43 @@ __global__ void __launch_bounds__(kDtThreads, 1)
       return sm.nsel;
     };
     int nsel = 0, NPb = 0;
-    if (!hier) {
+    if (shard) {
+      // global top-k of every shard's lists, then the owned picks (local block ids)
+      if (warp == 0) {
+        const int blo = tok_lo / geo.Bk, bhi = tok_hi / geo.Bk;
+        const int kk = max(1, kfinal);
+        for (int e0 = 0; e0 < P.n_in; e0 += 32) {
+          const int e = e0 + lane;
+          float cs = neg_inf();
+          int ci = INT_MAX;
+          if (e < P.n_in) {
+            const int id = P.in_idx[(size_t)bg * P.n_in + e];
+            if (id >= 0) {
+              cs = P.in_score[(size_t)bg * P.n_in + e];
+              ci = id;
+            }
+          }
+          const float ts = __shfl_sync(0xffffffffu, ls, kk - 1);
+          const int ti = __shfl_sync(0xffffffffu, li, kk - 1);
+          if (__any_sync(0xffffffffu, beats(cs, ci, ts, ti))) {
+            warp_sort32(cs, ci);
+            warp_merge32(ls, li, cs, ci);
+          }
+        }
+        const bool valid = lane < kfinal && li != INT_MAX;
+        if (p.sel_idx != nullptr && lane < geo.K) {
+          p.sel_idx[(size_t)bg * geo.K + lane] = valid ? li : -1;
+          p.sel_score[(size_t)bg * geo.K + lane] = valid ? ls : neg_inf();
+        }
+        const bool own = valid && li >= blo && li < bhi;
+        const unsigned om = __ballot_sync(0xffffffffu, own);
+        if (own) sm.sel_i[__popc(om & ((1u << lane) - 1u))] = li - blo;
+        if (lane == 0) sm.nsel = __popc(om);
+      }
+      score_bar();
+      nsel = sm.nsel;
+      stamp(5);
+    } else if (!hier) {
       if (kfinal > 0) score_pages(0, NPa, Ra, kfinal, [&](int j) { return 1 + j; });
       stamp(5);
       nsel = merge(max(1, kfinal));
@@ -599,11 +655,15 @@ __global__ void __launch_bounds__(kDtThreads, 1)
     }
     if (warp == 0) {
       const bool valid = lane < nsel;
-      if (p.sel_idx != nullptr && lane < geo.K) {
+      if (!shard && p.sel_idx != nullptr && lane < geo.K) {
         p.sel_idx[(size_t)bg * geo.K + lane] = valid ? sm.sel_i[lane] : -1;
         p.sel_score[(size_t)bg * geo.K + lane] = valid ? sm.sel_s[lane] : neg_inf();
       }
-      if (lane == 0) mbar_arrive(&sm.sel_ready);  // picks and count are in shared memory
+      __syncwarp();
+      if (lane == 0) {
+        __threadfence_block();
+        mbar_arrive(&sm.sel_ready);  // picks and count are in shared memory
+      }
     }
     const int NCr = (nsel * geo.Bk + kDtKeys - 1) / kDtKeys;
     const int NC = NCw + NCs + NCr;
@@ -687,7 +747,7 @@ __global__ void __launch_bounds__(kDtThreads, 1)
           break;
         }
         bool valid;
-        if (c < NCw) valid = w0 + c * kDtKeys + t <= pos;
+        if (c < NCw) valid = wlo + c * kDtKeys + t <= whi;
         else if (c < NCw + NCs) valid = t < nsink;
         else valid = (c - NCw - NCs) * kDtKeys + t < nsel * geo.Bk;
         unsigned char* pdst = sm.pt[sb][t >> 6];
@@ -725,19 +785,33 @@ __global__ void __launch_bounds__(kDtThreads, 1)
               "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
             : "r"(tmem + 32 + lane_off));
         tmem_ld_wait();
-        if (t < DH) {
+        if (shard) {  // unnormalised partial of the owned tokens, fixed max m2
+          if (t < DH) {
 #pragma unroll
-          for (int h = 0; h < 16; ++h) {
-            if (h < G) {
-              const float L = sm.lsum[0][h] + sm.lsum[1][h] + sm.lsum[2][h] + sm.lsum[3][h];
-              const float O = __uint_as_float(r[h]);
-              p.out[((size_t)b * geo.Hq + g * G + h) * DH + t] = f2bf(L > 0.f ? O / L : 0.f);
+            for (int h = 0; h < 16; ++h)
+              if (h < G)  // no owned keys: O^T was never written
+                P.part_o[((size_t)b * geo.Hq + g * G + h) * DH + t] = NC > 0 ? __uint_as_float(r[h]) : 0.f;
+          }
+          if (t < G) {
+            const float L = sm.lsum[0][t] + sm.lsum[1][t] + sm.lsum[2][t] + sm.lsum[3][t];
+            P.part_l[(size_t)b * geo.Hq + g * G + t] = L;
+            P.part_m2[(size_t)b * geo.Hq + g * G + t] = sm.m2[t];
+          }
+        } else {
+          if (t < DH) {
+#pragma unroll
+            for (int h = 0; h < 16; ++h) {
+              if (h < G) {
+                const float L = sm.lsum[0][h] + sm.lsum[1][h] + sm.lsum[2][h] + sm.lsum[3][h];
+                const float O = __uint_as_float(r[h]);
+                p.out[((size_t)b * geo.Hq + g * G + h) * DH + t] = f2bf(L > 0.f ? O / L : 0.f);
+              }
             }
           }
-        }
-        if (t < G && p.lse != nullptr) {
-          const float L = sm.lsum[0][t] + sm.lsum[1][t] + sm.lsum[2][t] + sm.lsum[3][t];
-          p.lse[(size_t)b * geo.Hq + g * G + t] = L > 0.f ? (sm.m2[t] + log2f(L)) * 0.6931471805599453f : neg_inf();
+          if (t < G && p.lse != nullptr) {
+            const float L = sm.lsum[0][t] + sm.lsum[1][t] + sm.lsum[2][t] + sm.lsum[3][t];
+            p.lse[(size_t)b * geo.Hq + g * G + t] = L > 0.f ? (sm.m2[t] + log2f(L)) * 0.6931471805599453f : neg_inf();
+          }
         }
       }
     }
@@ -800,17 +874,64 @@ static cudaError_t launch_dtc_t(const CUtensorMap& a, const CUtensorMap& b, cons
   return cudaGetLastError();
 }
 
-cudaError_t launch_decode_tc(const DecodeAttnParams& p, const __nv_bfloat16* summ, const __nv_bfloat16* supers,
-                             const float* k_gain, int* err, int dh, cudaStream_t st) {
+static cudaError_t launch_dtc(DecodeTcParams P, int dh, cudaStream_t st) {
+  const DecodeAttnParams& p = P.a;
   CUtensorMap m_kc, m_kr, m_v;
   const Geom& geo = p.geo;
   if (!dtc_map(&m_kc, p.k, geo.B, geo.n_cap, geo.Hkv, dh) || !dtc_map(&m_kr, p.kr, geo.B, geo.n_cap, geo.Hkv, dh) ||
       !dtc_map(&m_v, p.v, geo.B, geo.n_cap, geo.Hkv, dh))
     return cudaErrorInvalidValue;
-  DecodeTcParams P{p, summ, supers, k_gain, err};
   // softmax head rows: 8 when the group fits, else all 16 of the MMA's N
   if (dh == 64) return geo.G <= 8 ? launch_dtc_t<64, 8>(m_kc, m_kr, m_v, P, st) : launch_dtc_t<64, 16>(m_kc, m_kr, m_v, P, st);
   return geo.G <= 8 ? launch_dtc_t<128, 8>(m_kc, m_kr, m_v, P, st) : launch_dtc_t<128, 16>(m_kc, m_kr, m_v, P, st);
+}
+
+
+cudaError_t launch_decode_tc(const DecodeAttnParams& p, const __nv_bfloat16* summ, const __nv_bfloat16* supers,
+                             const float* k_gain, int* err, int dh, cudaStream_t st) {
+  DecodeTcParams P{};
+  P.a = p;
+  P.summ = summ;
+  P.supers = supers;
+  P.k_gain = k_gain;
+  P.err = err;
+  P.mode = 0;
+  return launch_dtc(P, dh, st);
+}
+
+cudaError_t launch_decode_tc_shard(const DecodeAttnParams& p, const float* k_gain, int* err, int dh, int tok_lo,
+                                   const int32_t* in_idx, const float* in_score, int n_in, float* part_o,
+                                   float* part_l, float* part_m2, cudaStream_t st) {
+  DecodeTcParams P{};
+  P.a = p;
+  P.k_gain = k_gain;
+  P.err = err;
+  P.mode = 1;
+  P.tok_lo = tok_lo;
+  P.n_in = n_in;
+  P.in_idx = in_idx;
+  P.in_score = in_score;
+  P.part_o = part_o;
+  P.part_l = part_l;
+  P.part_m2 = part_m2;
+  return launch_dtc(P, dh, st);
+}
+
+// out = O / l (bf16), lse = (m2 + log2 l) * ln 2 from the all-reduced shard partials.
+__global__ void __launch_bounds__(128) shard_finish_kernel(int dh, const float* __restrict__ po,
+                                                           const float* __restrict__ pl,
+                                                           const float* __restrict__ pm2,
+                                                           __nv_bfloat16* __restrict__ out, float* __restrict__ lse) {
+  const size_t row = blockIdx.x;
+  const float L = pl[row];
+  for (int d = threadIdx.x; d < dh; d += blockDim.x) out[row * dh + d] = f2bf(L > 0.f ? po[row * dh + d] / L : 0.f);
+  if (threadIdx.x == 0 && lse != nullptr) lse[row] = L > 0.f ? (pm2[row] + log2f(L)) * 0.6931471805599453f : neg_inf();
+}
+
+cudaError_t launch_shard_finish(int rows, int dh, const float* po, const float* pl, const float* pm2,
+                                __nv_bfloat16* out, float* lse, cudaStream_t st) {
+  shard_finish_kernel<<<rows, 128, 0, st>>>(dh, po, pl, pm2, out, lse);
+  return cudaGetLastError();
 }
 
 }  // namespace hba

@@ -47,6 +47,11 @@ struct SelParams {
   int32_t* out_idx;
   int32_t* counters;            // decode: [B*Hkv] merge counters zeroed here, or null
   int32_t pdl;                  // launched as a programmatic dependent of the previous kernel
+  // KV-range shard: candidate blocks restricted to [own_blo, own_bhi) (supers
+  // to [own_blo/F, own_bhi/F)); summary row r of this shard holds block
+  // own_blo + r (super own_blo/F + r).  One GPU: 0, INT_MAX.
+  int32_t own_blo, own_bhi;
+  int32_t n_limit;  // longest valid context (one GPU: n_cap; a shard: the global capacity)
 };
 
 struct AttnParams {
@@ -129,6 +134,15 @@ cudaError_t launch_decode_fused(const DecodeAttnParams& p, const __nv_bfloat16* 
                                 int dh, cudaStream_t st);
 size_t decode_fused_smem(int dh);
 // tcgen05 decode (hba_decode_tc.cu): one CTA per (sequence, kv head), QKNorm only.
+// KV-range shard: the union over this shard's tokens [tok_lo, tok_lo + n_cap)
+// as unnormalised partials (O, l, m2) after merging n_in candidate picks per
+// (sequence, kv head) into the global top-k; and the final normalisation of
+// the partials' sums.
+cudaError_t launch_decode_tc_shard(const DecodeAttnParams& p, const float* k_gain, int* err, int dh, int tok_lo,
+                                   const int32_t* in_idx, const float* in_score, int n_in, float* part_o,
+                                   float* part_l, float* part_m2, cudaStream_t st);
+cudaError_t launch_shard_finish(int rows, int dh, const float* po, const float* pl, const float* pm2,
+                                __nv_bfloat16* out, float* lse, cudaStream_t st);
 bool decode_tc_supported(const Geom& geo, int dh, const void* k, const void* kr, const void* v, const void* summ,
                          const void* supers);
 cudaError_t launch_decode_tc(const DecodeAttnParams& p, const __nv_bfloat16* summ, const __nv_bfloat16* supers,

@@ -45,33 +45,39 @@ __global__ void __launch_bounds__(kSelThreads) select_kernel(SelParams p) {
   float scale;
   query_position(p.qp, b, t, pos, nctx, scale);
   const size_t list_base = (((size_t)bg * geo.nq + t) * p.splits + split) * p.list_k;
-  const bool ok_pos = (nctx >= 1 && nctx <= geo.n_cap);
+  const bool ok_pos = (nctx >= 1 && nctx <= p.n_limit);
   const int nb = ok_pos ? nctx / geo.Bk : 0;
   const int bmax = ok_pos ? min(last_candidate(pos, geo.W, geo.Bk), nb - 1) : 0;
   const int F = geo.F;
 
-  // ---- candidate range (flat / super known from the position alone) ----
+  // ---- candidate range (flat / super known from the position alone),
+  // intersected with the blocks (supers) this shard owns ----
+  const int own_slo = p.own_blo / F;
+  const int own_shi = p.own_bhi == INT_MAX ? INT_MAX : p.own_bhi / F;
   int C = 0, id_lo = 0;
   if (p.mode == kSelFlat) {
-    C = max(0, bmax);
-    id_lo = 1;
+    id_lo = max(1, p.own_blo);
+    C = max(0, min(bmax, p.own_bhi - 1) - id_lo + 1);
   } else if (p.mode == kSelSuper) {
     if (bmax >= 1) {
-      id_lo = (F == 1) ? 1 : 0;
-      C = bmax / F - id_lo + 1;
+      id_lo = max((F == 1) ? 1 : 0, own_slo);
+      C = max(0, min(bmax / F, own_shi - 1) - id_lo + 1);
     }
   }
   const __nv_bfloat16* src;
-  int rows_cap;
+  int rows_cap, row_base;
   if (p.mode == kSelSuper) {
     src = p.supers;
     rows_cap = geo.ns_cap;
+    row_base = own_slo;
   } else {
     src = p.summ;
     rows_cap = geo.nb_cap;
+    row_base = p.own_blo;
   }
   const size_t row_elems = (size_t)geo.m * DH;
-  const __nv_bfloat16* base = src + ((size_t)bg * rows_cap) * row_elems;
+  // row of candidate id: id - row_base
+  const __nv_bfloat16* base = src + ((ptrdiff_t)bg * rows_cap - row_base) * (ptrdiff_t)row_elems;
   const int nvec = geo.m * DH / 8;
   SummaryLoads<DH, VPL, kSelWarps> ld;
   constexpr int GROUP = kSelWarps * SummaryLoads<DH, VPL, kSelWarps>::U;
@@ -124,8 +130,8 @@ __global__ void __launch_bounds__(kSelThreads) select_kernel(SelParams p) {
       const bool valid = lane < b_eff && top.i != INT_MAX;
       int lo = 0, cnt = 0;
       if (valid) {
-        lo = max(1, top.i * F);
-        const int hi = min(bmax, top.i * F + F - 1);
+        lo = max(max(1, top.i * F), p.own_blo);
+        const int hi = min(min(bmax, top.i * F + F - 1), p.own_bhi - 1);
         cnt = max(0, hi - lo + 1);
       }
       int incl = cnt;

@@ -60,6 +60,15 @@ SIGNATURES = {
     "hba_b200_set_profile_events": (ctypes.c_int, [ctypes.POINTER(ctypes.c_void_p), _I32]),
     "hba_b200_profile_events_recorded": (ctypes.c_int, []),
     "hba_b200_set_debug_trace": (ctypes.c_int, [_P, _I64]),
+    # cfg, batch, n_cap_local, tok_lo, level, seq_lens, scales, q, q_gain, summ, supers, in_idx, in_score,
+    # n_in_lists, out_idx, out_score, stream
+    "hba_b200_decode_shard_select": (ctypes.c_int, [_CFG, _I32, _I32, _I32, _I32, _P, _P, _P, _P, _P, _P, _P, _P,
+                                                    _I32, _P, _P, _P]),
+    # cfg, batch, n_cap_local, tok_lo, seq_lens, scales, q, q_gain, k_gain, k, kr, v, cos, sin, in_idx, in_score,
+    # n_in, part_o, part_l, part_m2, sel_idx, sel_score, dev_status, stream
+    "hba_b200_decode_shard_attend": (ctypes.c_int, [_CFG, _I32, _I32, _I32, _P, _P, _P, _P, _P, _P, _P, _P, _P,
+                                                    _P, _P, _P, _I32, _P, _P, _P, _P, _P, _P, _P]),
+    "hba_b200_decode_shard_finish": (ctypes.c_int, [_CFG, _I32, _P, _P, _P, _P, _P, _P]),
     "hba_b200_prefill": (ctypes.c_int, [_CFG, _I32, _I32, _F, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P,
                                         _P, _P, _SZ, _P]),
 }

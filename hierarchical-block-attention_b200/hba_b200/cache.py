@@ -30,7 +30,11 @@ BF16 = torch.bfloat16
 
 
 class HBADecodeCache:
-    def __init__(self, cfg, batch, max_len, summ, qkn, cos, sin, device="cuda", hier=False):
+    """`pos_offset`: global position of cache row 0 (a KV-range shard holding
+    tokens [pos_offset, pos_offset + max_len) of every sequence; its keys are
+    RoPE'd at their global positions)."""
+
+    def __init__(self, cfg, batch, max_len, summ, qkn, cos, sin, device="cuda", hier=False, pos_offset=0):
         self.cfg = cfg
         self.hier = bool(hier)
         self.B = int(batch)
@@ -40,8 +44,10 @@ class HBADecodeCache:
         self.ns_cap = -(-self.nb_cap // cfg.fanout) if self.hier else 0
         self.device = torch.device(device)
         H, Hkv, dh, m = cfg.n_heads, cfg.n_kv, cfg.head_dim, cfg.slots
-        if cos.shape[0] < self.n_cap:
-            raise ValueError(f"RoPE tables cover {cos.shape[0]} positions < cache capacity {self.n_cap}")
+        self.pos_offset = int(pos_offset)
+        if cos.shape[0] < self.pos_offset + self.n_cap:
+            raise ValueError(f"RoPE tables cover {cos.shape[0]} positions < cache end "
+                             f"{self.pos_offset + self.n_cap}")
         dev = self.device
         self.c = c_config(cfg, self.hier)
         self.k = torch.zeros(self.B, self.n_cap, Hkv, dh, dtype=BF16, device=dev)
@@ -50,8 +56,8 @@ class HBADecodeCache:
         self.summaries = torch.zeros(self.B, Hkv, self.nb_cap, m, dh, dtype=BF16, device=dev)
         self.supers = (torch.zeros(self.B, Hkv, max(1, self.ns_cap), m, dh, dtype=BF16, device=dev)
                        if self.hier else None)
-        self.cos = as_f32(cos[: self.n_cap], dev)
-        self.sin = as_f32(sin[: self.n_cap], dev)
+        self.cos = as_f32(cos[self.pos_offset: self.pos_offset + self.n_cap], dev)
+        self.sin = as_f32(sin[self.pos_offset: self.pos_offset + self.n_cap], dev)
         self.q_gain, self.k_gain = gains(qkn, dev)
         self.probes, self.proj = summarizer_weights(summ, dev)
         self.lens = torch.zeros(self.B, dtype=torch.int32, device=dev)

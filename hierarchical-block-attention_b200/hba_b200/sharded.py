@@ -1,0 +1,199 @@
+"""KV-range sharded decode: one long context split across ranks (one process
+per GPU), for contexts whose caches outgrow one GPU or whose decode should
+use several GPUs' HBM bandwidth at once.
+
+Rank r of P keeps global tokens [r*n_loc, (r+1)*n_loc) of every sequence:
+its K / RoPE'd-K / V caches, the summaries of its blocks and (hierarchical
+mode) the supers of its super-blocks; shard bounds fall on block (super)
+multiples, so no block or super straddles two ranks.  One decode step:
+
+  flat  local top-k over the owned candidate blocks (exact scores)
+        -> all-gather the lists -> every rank merges them into the same
+           global top-k (score desc, block asc) = the one-device picks
+  hier  local top-beam supers -> all-gather -> global beam; each rank scores
+        the children it owns -> local top-k -> all-gather -> global top-k
+  then  each rank runs the union softmax over the tokens it owns (its part of
+        the window, the sinks on rank 0, its picks) with the tensor-core
+        path's fixed per-head logit bound, which is the same on every rank,
+        so the unnormalised partials (O, l) simply add: one all-reduce(sum),
+        then out = O / l, lse = m2 + log2 l.
+
+The reference runs on one device and has no equivalent; the result is its
+decode (src/hba/attention.py:663-711 at cs = n-1) over the whole context.
+The kernels are the library's `hba_b200_decode_shard_*` entry points; the
+collectives go through `TorchComm` (torch.distributed: NCCL on GPUs, gloo in
+the CPU tests, which also swap the kernels for a CPU stand-in via `ops`).
+"""
+
+import ctypes
+
+import numpy as np
+import torch
+import torch.distributed as dist
+
+from . import _lib
+from .attention import as_bf16, as_f32, c_config, gains, ptr, stream_of, union_scale
+from .cache import HBADecodeCache
+
+
+def shard_range(cfg, max_len, rank, world, hier):
+    """(tok_lo, n_loc, n_total): this rank's first global token and token
+    count, and the total capacity (a multiple of world * block * F)."""
+    unit = cfg.block * (cfg.fanout if hier else 1) * world
+    n_total = -(-int(max_len) // unit) * unit
+    n_loc = n_total // world
+    return rank * n_loc, n_loc, n_total
+
+
+class TorchComm:
+    """The two collectives of a step over a torch.distributed process group."""
+
+    def __init__(self, group=None):
+        self.group = group
+        self.world = dist.get_world_size(group)
+        self.rank = dist.get_rank(group)
+
+    def all_gather(self, t):
+        """[*shape] -> [world, *shape] (rank order)."""
+        parts = [torch.empty_like(t) for _ in range(self.world)]
+        dist.all_gather(parts, t.contiguous(), group=self.group)
+        return torch.stack(parts)
+
+    def all_reduce_sum(self, t):
+        dist.all_reduce(t, op=dist.ReduceOp.SUM, group=self.group)
+
+
+class CudaShardOps:
+    """The product path: the library's shard kernels on the rank's GPU."""
+
+    def select(self, sh, level, in_idx, in_score, n_in_lists, out_idx, out_score):
+        st = _lib.load().hba_b200_decode_shard_select(
+            ctypes.byref(sh.c), sh.B, sh.n_loc, sh.tok_lo, level, ptr(sh.glens), ptr(sh.scales), ptr(sh.q),
+            ptr(sh.local.q_gain), ptr(sh.local.summaries), ptr(sh.local.supers), ptr(in_idx), ptr(in_score),
+            n_in_lists, ptr(out_idx), ptr(out_score), stream_of(sh.device))
+        _lib.check(st, "hba_b200_decode_shard_select")
+
+    def attend(self, sh, in_idx, in_score, n_in, part_o, part_l, part_m2, sel_idx, sel_score):
+        st = _lib.load().hba_b200_decode_shard_attend(
+            ctypes.byref(sh.c), sh.B, sh.n_loc, sh.tok_lo, ptr(sh.glens), ptr(sh.scales), ptr(sh.q),
+            ptr(sh.local.q_gain), ptr(sh.local.k_gain), ptr(sh.local.k), ptr(sh.local.kr), ptr(sh.local.v),
+            ptr(sh.cos), ptr(sh.sin), ptr(in_idx), ptr(in_score), n_in, ptr(part_o), ptr(part_l), ptr(part_m2),
+            ptr(sel_idx), ptr(sel_score), ptr(sh.status), stream_of(sh.device))
+        _lib.check(st, "hba_b200_decode_shard_attend")
+
+    def finish(self, sh, part_o, part_l, part_m2, out, lse):
+        st = _lib.load().hba_b200_decode_shard_finish(
+            ctypes.byref(sh.c), sh.B, ptr(part_o), ptr(part_l), ptr(part_m2), ptr(out), ptr(lse),
+            stream_of(sh.device))
+        _lib.check(st, "hba_b200_decode_shard_finish")
+
+
+class HBAShardedDecode:
+    """Decode over a context sharded by token range across the ranks of
+    `comm` (default: the torch.distributed world).  `local` is this rank's
+    cache of tokens [tok_lo, tok_lo + n_loc) (default: an `HBADecodeCache`
+    with pos_offset = tok_lo on `device`); `ops` runs the per-rank pieces
+    (default: the CUDA library)."""
+
+    def __init__(self, cfg, batch, max_len, summ, qkn, cos, sin, device="cuda", hier=False, comm=None,
+                 ops=None, local=None):
+        self.comm = comm if comm is not None else TorchComm()
+        self.ops = ops if ops is not None else CudaShardOps()
+        self.cfg = cfg
+        self.hier = bool(hier)
+        self.B = int(batch)
+        self.rank, self.world = self.comm.rank, self.comm.world
+        self.tok_lo, self.n_loc, self.n_total = shard_range(cfg, max_len, self.rank, self.world, self.hier)
+        if cos.shape[0] < self.n_total:
+            raise ValueError(f"RoPE tables cover {cos.shape[0]} positions < sharded capacity {self.n_total}")
+        self.device = torch.device(device)
+        self.local = local if local is not None else HBADecodeCache(
+            cfg, batch, self.n_loc, summ, qkn, cos, sin, device=device, hier=hier, pos_offset=self.tok_lo)
+        self.c = c_config(cfg, self.hier)
+        dev = self.device
+        self.cos = as_f32(cos[: self.n_total], dev)     # the query is rotated at its global position
+        self.sin = as_f32(sin[: self.n_total], dev)
+        self.glens_host = np.zeros(self.B, dtype=np.int64)
+        self.glens = torch.zeros(self.B, dtype=torch.int32, device=dev)
+        self.scales = torch.zeros(self.B, dtype=torch.float32, device=dev)
+        self.status = torch.zeros(1, dtype=torch.int32, device=dev)
+        BH, K, Hq, dh = self.B * cfg.n_kv, cfg.k_blocks, cfg.n_heads, cfg.head_dim
+        self.l_idx = torch.empty(BH, K, dtype=torch.int32, device=dev)
+        self.l_sc = torch.empty(BH, K, dtype=torch.float32, device=dev)
+        if self.hier:
+            self.s_idx = torch.empty(BH, cfg.beam, dtype=torch.int32, device=dev)
+            self.s_sc = torch.empty(BH, cfg.beam, dtype=torch.float32, device=dev)
+        # O and l in one buffer: one all-reduce per step
+        self.part = torch.empty(self.B * Hq * (dh + 1), dtype=torch.float32, device=dev)
+        self.part_o = self.part[: self.B * Hq * dh].view(self.B, Hq, dh)
+        self.part_l = self.part[self.B * Hq * dh:].view(self.B, Hq)
+        self.part_m2 = torch.empty(self.B, Hq, dtype=torch.float32, device=dev)
+        self.q = None
+
+    # ---------------------------------------------------------------- state --
+    def _set_lengths(self, n):
+        self.glens_host[:] = n
+        self.glens.fill_(int(n))
+        s = union_scale(self.cfg, self.cfg.head_dim, max(1, int(n)))
+        self.scales.fill_(float(s))
+
+    def fill(self, k_full, v_full):
+        """Load a whole context (every sequence n tokens): k_full, v_full
+        [B, n, Hkv, dh] raw projections; this rank keeps its token range."""
+        n = int(k_full.shape[1])
+        if n > self.n_total:
+            raise ValueError(f"context {n} exceeds the sharded capacity {self.n_total}")
+        lo, hi = self.tok_lo, min(self.tok_lo + self.n_loc, n)
+        if hi > lo:
+            self.local.append(k_full[:, lo:hi], v_full[:, lo:hi])
+        self._set_lengths(n)
+
+    def append(self, k_new, v_new):
+        """Append t tokens to every sequence (all sequences hold the same
+        length): each rank keeps the part that falls in its range."""
+        if (self.glens_host != self.glens_host[0]).any():
+            raise ValueError("sharded append needs equal sequence lengths")
+        L, t = int(self.glens_host[0]), int(k_new.shape[1])
+        if L + t > self.n_total:
+            raise ValueError(f"sharded capacity {self.n_total} exceeded")
+        lo, hi = max(L, self.tok_lo), min(L + t, self.tok_lo + self.n_loc)
+        if hi > lo:
+            self.local.append(k_new[:, lo - L: hi - L], v_new[:, lo - L: hi - L])
+        self._set_lengths(L + t)
+
+    # --------------------------------------------------------------- decode --
+    def _gather_lists(self, idx, sc):
+        """[BH, k] local lists of every rank -> [BH, P*k] (rank-major per row)."""
+        BH, k = idx.shape
+        packed = torch.cat([idx.reshape(-1), sc.reshape(-1).view(torch.int32)])
+        g = self.comm.all_gather(packed)                                  # [P, 2*BH*k]
+        gi = g[:, : BH * k].reshape(self.world, BH, k).permute(1, 0, 2).reshape(BH, self.world * k)
+        gs = g[:, BH * k:].reshape(self.world, BH, k).permute(1, 0, 2).reshape(BH, self.world * k)
+        return gi.contiguous(), gs.contiguous().view(torch.float32)
+
+    def decode_into(self, q, out, lse=None, sel_idx=None, sel_score=None):
+        """q [B, Hq, dh] bf16 (the same on every rank) -> out [B, Hq, dh] bf16,
+        lse [B, Hq] natural log, picks [B, Hkv, K] (global block ids)."""
+        if (self.glens_host < 1).any():
+            raise ValueError("every sequence needs at least one cached token")
+        self.q = q
+        if not self.hier:
+            self.ops.select(self, 0, None, None, 0, self.l_idx, self.l_sc)
+        else:
+            self.ops.select(self, 1, None, None, 0, self.s_idx, self.s_sc)
+            si, ss = self._gather_lists(self.s_idx, self.s_sc)           # [BH, P*beam]
+            self.ops.select(self, 2, si, ss, self.world, self.l_idx, self.l_sc)
+        gi, gs = self._gather_lists(self.l_idx, self.l_sc)               # [BH, P*K]
+        self.ops.attend(self, gi, gs, gi.shape[1], self.part_o, self.part_l, self.part_m2, sel_idx, sel_score)
+        self.comm.all_reduce_sum(self.part)
+        self.ops.finish(self, self.part_o, self.part_l, self.part_m2, out, lse)
+
+    def attend(self, q, return_lse=False):
+        """Allocating convenience wrapper of `decode_into`."""
+        if q.dim() == 4:
+            q = q[:, 0]
+        qb = as_bf16(q.to(self.device))
+        out = torch.empty_like(qb)
+        lse = torch.empty(self.B, self.cfg.n_heads, dtype=torch.float32, device=self.device) if return_lse else None
+        self.decode_into(qb, out, lse)
+        return (out, lse) if return_lse else out

@@ -214,6 +214,48 @@ int hba_b200_profile_events_recorded(void);
 int hba_b200_set_debug_trace(void* device_buffer, int64_t bytes);
 
 /*
+ * KV-range sharded decode (no counterpart in the reference, which runs on one
+ * device; the result is the decode of src/hba/attention.py:663-711 at
+ * cs = n-1 over the whole context).  Rank r of P holds global tokens
+ * [tok_lo, tok_lo + n_cap_local) of every sequence -- K/V/RoPE'd-K caches of
+ * that range in local rows 0.., the summaries (and supers) of its blocks --
+ * with bounds on block (hier: super) multiples.  seq_lens are the global
+ * context lengths.  One step, with collectives done by the caller:
+ *   flat: shard_select(level 0) -> all-gather the [B*Hkv, K] lists ->
+ *         shard_attend(every shard's lists) -> all-reduce(sum) part_o,
+ *         part_l -> shard_finish.
+ *   hier: shard_select(level 1, local top-beam supers) -> all-gather ->
+ *         shard_select(level 2, in = every shard's beam lists, children
+ *         this shard owns) -> all-gather -> shard_attend -> ... as flat.
+ * Every rank computes the same global top-k (score desc, block asc) from
+ * exact per-shard scores, so the picks equal the one-device picks.
+ *
+ * shard_select: out_idx/out_score [B*Hkv, K] (level 1: [B*Hkv, beam]) global
+ *   block (super) ids, -1 = none; in lists [B*Hkv, n_in_lists, beam].
+ * shard_attend: in [B*Hkv, n_in] candidate picks; part_o [B, Hq, dh],
+ *   part_l / part_m2 [B, Hq] fp32 -- the union over the owned tokens with the
+ *   tensor-core path's fixed per-head logit bound m2 (the same on every
+ *   shard, so partials add); sel_idx/sel_score (optional) get the global
+ *   picks; dev_status: one device int, 0 = ok (as the prefill status).
+ *   Needs the tensor-core decode path (QKNorm, block 64, head dim 64/128).
+ * shard_finish: out [B, Hq, dh] bf16 = O/l, lse (optional) natural log.
+ */
+int hba_b200_decode_shard_select(const hba_b200_config* cfg, int32_t batch, int32_t n_cap_local, int32_t tok_lo,
+                                 int32_t level, const int32_t* seq_lens, const float* scales, const void* q,
+                                 const float* q_gain, const void* summaries, const void* supers,
+                                 const int32_t* in_idx, const float* in_score, int32_t n_in_lists, int32_t* out_idx,
+                                 float* out_score, cudaStream_t stream);
+int hba_b200_decode_shard_attend(const hba_b200_config* cfg, int32_t batch, int32_t n_cap_local, int32_t tok_lo,
+                                 const int32_t* seq_lens, const float* scales, const void* q, const float* q_gain,
+                                 const float* k_gain, const void* k_cache, const void* k_rope_cache,
+                                 const void* v_cache, const float* cos, const float* sin, const int32_t* in_idx,
+                                 const float* in_score, int32_t n_in, float* part_o, float* part_l, float* part_m2,
+                                 int32_t* sel_idx, float* sel_score, int32_t* dev_status, cudaStream_t stream);
+int hba_b200_decode_shard_finish(const hba_b200_config* cfg, int32_t batch, const float* part_o,
+                                 const float* part_l, const float* part_m2, void* out, float* lse,
+                                 cudaStream_t stream);
+
+/*
  * Introspection (no counterpart in the reference): the kernels the last
  * hba_b200_decode / hba_b200_decode_noalloc call of this process launched, as
  * a static string ("decode_tc_kernel", "decode_fused_kernel" or
