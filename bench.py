@@ -14,7 +14,10 @@ queries/s over all ranks (each rank decodes its own batch: weak scaling).
 `e2e` is the same step through the C-ABI call with the query copied from
 pinned host memory and the output + LSE copied back, inside the timed region.
 The secondary lines measure config 3 (hierarchical decode at 128K) and
-config 2 (prefill at 32K).  `--impl reference` times the CPU oracle port (the
+config 2 (prefill at 32K), and with N > 1 ranks config 3 with every 128K
+context sharded by token range over the N GPUs (one batch of 32 sequences,
+strong scaling; NCCL all-gathers of the per-rank top-k lists and one
+all-reduce of the softmax partials per step).  `--impl reference` times the CPU oracle port (the
 reference algorithm restated in numpy) on the host cores instead.
 """
 
@@ -44,7 +47,7 @@ def parse():
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
-    ap.add_argument("--config", default="cfg1", choices=["cfg1", "cfg2", "cfg3"])
+    ap.add_argument("--config", default="cfg1", choices=["cfg1", "cfg2", "cfg3", "cfg3-shard"])
     ap.add_argument("--no-secondary", action="store_true")
     ap.add_argument("--ncu-case", default=None, choices=["cfg1", "cfg3"],
                     help="profiling target: build this decode workload (cfg3 at batch 4), run 3 decodes, exit")
@@ -184,6 +187,45 @@ def kernel_times(call, steps, flush, n_events):
     finally:
         L.hba_b200_set_profile_events(None, 0)
     return [statistics.mean(x) for x in zip(*per)]
+
+
+def shard_bench(name, steps, warmup, world, rank, local, pk):
+    """KV-range sharded decode: one batch of `name`'s sequences whose contexts
+    are split by token range over the `world` ranks (strong scaling: the
+    batch is the whole job).  Timed with CUDA events, max over ranks."""
+    from hba_b200 import baseline_config, synth
+    from hba_b200.sharded import HBAShardedDecode
+    dev = torch.device("cuda", local)
+    cfg, B, n, hier = baseline_config(name)
+    summ, qkn = synth.make_weights(cfg, dev, seed=0, gains=False)
+    cos, sin = synth.rope_tables(n, cfg.head_dim, 1e6, dev)
+    wl = synth.decode_workload(cfg, B, n, hier=hier, seed=1000, device=dev, qkn=qkn)
+    sh = HBAShardedDecode(cfg, B, n, summ, qkn, cos, sin, device=dev, hier=hier)
+    sh.fill(wl["k"], wl["v"])
+    del wl["k"], wl["v"]
+    torch.cuda.empty_cache()
+    q = wl["q"].contiguous()
+    out = torch.empty_like(q)
+    lse = torch.empty(B, cfg.n_heads, dtype=torch.float32, device=dev)
+    flush = torch.empty(FLUSH_BYTES // 4, dtype=torch.float32, device=dev)
+    times, clocks = timed_steps(lambda: sh.decode_into(q, out, lse), steps, warmup, flush, world, dev, local)
+    t_ms = max_over_ranks(statistics.mean(times), world, dev)
+    res = dict(
+        metric=METRIC, value=B / (t_ms * 1e-3), unit="decode queries/s", n_gpus=world, steps=steps, warmup=warmup,
+        ms_per_step=t_ms, higher_is_better=True, scaling="strong", vs_baseline=None, dtype="bf16",
+        data="synthetic (seeded N(0,1) q/k/v, 8 planted blocks per sequence and kv head)",
+        config=dict(workload=f"{name} sharded: decode, batch {B} (whole job), context {n} split over {world} "
+                             f"ranks by token range ({sh.n_loc} tokens each)", batch=B, context=n,
+                    tokens_per_rank=sh.n_loc, hier=hier,
+                    collectives_per_step=(2 if hier else 1) + 1,
+                    l2="flushed (256 MB write) before every timed step", timing="CUDA events, max over ranks",
+                    parallelism=f"kv-range shards x{world} (NCCL all-gather of top-k lists, all-reduce of partials)"),
+        gpu_launches=steps * ((2 if hier else 1) + 2),
+        clocks=clocks,
+    )
+    del sh
+    torch.cuda.empty_cache()
+    return res
 
 
 def ncu_case(name, local):
@@ -491,14 +533,18 @@ def main():
     pk = peaks()
     if args.config in ("cfg1", "cfg3"):
         res = decode_bench(args.config, args.steps, args.warmup, world, rank, local, pk)
+    elif args.config == "cfg3-shard":
+        res = shard_bench("cfg3", args.steps, args.warmup, world, rank, local, pk)
     else:
         res = prefill_bench(args.config, args.steps, args.warmup, world, rank, local, pk)
     if not args.no_secondary and args.config == "cfg1":
         sec = []
-        for name in ("cfg3", "cfg2"):
+        for name in ("cfg3", "cfg2") + (("cfg3-shard",) if world > 1 else ()):
             try:
                 if name == "cfg3":
                     sec.append(decode_bench(name, min(args.steps, 10), args.warmup, world, rank, local, pk))
+                elif name == "cfg3-shard":
+                    sec.append(shard_bench("cfg3", min(args.steps, 10), args.warmup, world, rank, local, pk))
                 else:
                     sec.append(prefill_bench(name, min(args.steps, 3), 3, world, rank, local, pk))
             except Exception as e:  # report, do not hide, a failing secondary
