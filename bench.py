@@ -237,6 +237,7 @@ def ncu_case(name, local):
     cfg, B, n, hier = baseline_config(name)
     if name == "cfg3":
         B = 4
+        os.environ["HBA_B200_DECODE_PATH"] = "tc"  # the kernel the full-size bench runs (batch 4 alone would split)
     summ, qkn = synth.make_weights(cfg, dev, seed=0, gains=False)
     cos, sin = synth.rope_tables(n, cfg.head_dim, 1e6, dev)
     wl = synth.decode_workload(cfg, B, n, hier=hier, seed=1000, device=dev, qkn=qkn)
@@ -289,7 +290,7 @@ def decode_bench(name, steps, warmup, world, rank, local, pk):
     from hba_b200 import _lib
     nmarks = 4 if hier else 3          # begin | select (super, child) | attend
     kt = kernel_times(step_direct, max(3, min(steps, 10)), flush, nmarks)
-    kernels = _lib.load().hba_b200_last_decode_kernels().decode()
+    kernels = _lib.load().hba_b200_last_kernels().decode()
     single = "+" not in kernels
     attend_ms = kt[-1]
     keys = cfg.sinks + cfg.window + cfg.k_blocks * cfg.block
@@ -424,6 +425,7 @@ def prefill_bench(name, steps, warmup, world, rank, local, pk):
     times, clocks = timed_steps(step, steps, warmup, flush, world, dev, local)
     t_ms = max_over_ranks(statistics.mean(times), world, dev)
     kt = kernel_times(step, max(2, min(steps, 4)), flush, 5 if not hier else 7)
+    kernels = _lib.load().hba_b200_last_kernels().decode().split("+")
     attend_ms = kt[-1]
     # attended keys per query position i: sinks min(S, i+1), window, routed valid picks
     i = np.arange(n)
@@ -442,10 +444,11 @@ def prefill_bench(name, steps, warmup, world, rank, local, pk):
         config=dict(workload=f"{name}: prefill, batch {B}/rank, seq {n}, {Hq}/{Hkv} heads, dh {dh}, flat top-16",
                     batch_per_rank=B, seq_len=n, n_heads=Hq, n_kv=Hkv, head_dim=dh,
                     l2="flushed (256 MB write) before every timed step"),
-        roofline=dict(bound="tensor", kernel="attend_kernel", achieved=achieved, peak=pk["bf16"], unit="TFLOP/s",
-                      frac=achieved / pk["bf16"], peak_source=pk["source"], traffic=traffic_of(f"attend_{name}"),
-                      attended_flops=flops, kernel_ms=attend_ms),
-        kernel_ms=kt, clocks=clocks,
+        roofline=dict(bound="tensor", kernel=kernels[-1], achieved=achieved, peak=pk["bf16"], unit="TFLOP/s",
+                      frac=achieved / pk["bf16"], peak_source=pk["source"],
+                      traffic=traffic_of(f"{kernels[-1]}_{name}"), attended_flops=flops, kernel_ms=attend_ms),
+        kernel_ms={f"{i}:{k}": t for i, (k, t) in enumerate(zip(kernels, kt))},
+        gpu_launches=steps * len(kernels), clocks=clocks,
     )
     del q, k, v, ws, wl
     torch.cuda.empty_cache()

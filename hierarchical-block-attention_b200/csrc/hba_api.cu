@@ -26,7 +26,7 @@ struct ProfileHook {
 ProfileHook g_prof;
 unsigned long long* g_trace = nullptr;  // hba_b200_set_debug_trace
 long long g_trace_ctas = 0;
-const char* g_last_decode = "";  // hba_b200_last_decode_kernels
+const char* g_last_kernels = "";  // hba_b200_last_kernels
 
 void prof_begin(cudaStream_t st) {
   g_prof.next = 0;
@@ -280,7 +280,7 @@ int hba_b200_set_profile_events(void* const* events, int32_t count) {
 
 int hba_b200_profile_events_recorded(void) { return g_prof.next; }
 
-const char* hba_b200_last_decode_kernels(void) { return g_last_decode; }
+const char* hba_b200_last_kernels(void) { return g_last_kernels; }
 
 int hba_b200_set_debug_trace(void* device_buffer, int64_t bytes) {
   if (bytes < 0 || (device_buffer == nullptr && bytes != 0)) return HBA_B200_ERR_INVALID_ARGUMENT;
@@ -428,11 +428,11 @@ int hba_b200_decode(const hba_b200_config* cfg, int32_t batch, int32_t n_cap, co
                                    static_cast<const __nv_bfloat16*>(supers), cfg->head_dim, stream);
     }
     if (e != cudaSuccess) return cuda_status(e);
-    g_last_decode = path == kDecodeTc ? "decode_tc_kernel" : "decode_fused_kernel";
+    g_last_kernels = path == kDecodeTc ? "decode_tc_kernel" : "decode_fused_kernel";
     prof_mark(stream);
     return HBA_B200_OK;
   }
-  g_last_decode = "select_kernel+decode_attend_kernel";
+  g_last_kernels = "select_kernel+decode_attend_kernel";
   Lists fin{};
   int fin_lists = 0, fin_k = 0;
   st = run_select(cfg, geo, qp, plan, static_cast<const __nv_bfloat16*>(q), q_gain,
@@ -549,6 +549,9 @@ int hba_b200_prefill(const hba_b200_config* cfg, int32_t batch, int32_t n, float
                                static_cast<__nv_bfloat16*>(out), lse, dev_status, stream);
     if (e != cudaSuccess) return cuda_status(e);
     prof_mark(stream);
+    g_last_kernels = cfg->hier ? "qknorm_rope_kernel+summarize_kernel+supers_kernel+select_kernel+select_kernel+"
+                                 "prefill_tc_kernel"
+                               : "qknorm_rope_kernel+summarize_kernel+select_kernel+prefill_tc_kernel";
     if (sel_idx != nullptr) {  // the single-split lists are the final picks, layout [B, Hkv, n, K]
       const size_t bytes = (size_t)batch * cfg->n_kv * n * cfg->k_blocks * sizeof(int32_t);
       e = cudaMemcpyAsync(sel_idx, fin.idx, bytes, cudaMemcpyDeviceToDevice, stream);
@@ -579,6 +582,9 @@ int hba_b200_prefill(const hba_b200_config* cfg, int32_t batch, int32_t n, float
   e = hba::launch_attend(ap, dh, stream);
   if (e != cudaSuccess) return cuda_status(e);
   prof_mark(stream);
+  g_last_kernels = cfg->hier ? "qknorm_rope_kernel+summarize_kernel+supers_kernel+select_kernel+select_kernel+"
+                               "attend_kernel"
+                             : "qknorm_rope_kernel+summarize_kernel+select_kernel+attend_kernel";
   return HBA_B200_OK;
 }
 

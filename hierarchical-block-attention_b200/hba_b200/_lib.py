@@ -45,7 +45,7 @@ _CFG = ctypes.POINTER(Config)
 SIGNATURES = {
     "hba_b200_status_string": (ctypes.c_char_p, [ctypes.c_int]),
     "hba_b200_version": (ctypes.c_int, []),
-    "hba_b200_last_decode_kernels": (ctypes.c_char_p, []),
+    "hba_b200_last_kernels": (ctypes.c_char_p, []),
     "hba_b200_qknorm": (ctypes.c_int, [_P, _P, _P, _I64, _I32, _I32, _F, _P]),
     "hba_b200_summarize": (ctypes.c_int, [_CFG, _I32, _I32, _P, _P, _P, _P, _I32, _I32, _P]),
     "hba_b200_build_supers": (ctypes.c_int, [_CFG, _I32, _I32, _I32, _P, _P, _I32, _I32, _P]),

@@ -257,11 +257,11 @@ int hba_b200_decode_shard_finish(const hba_b200_config* cfg, int32_t batch, cons
 
 /*
  * Introspection (no counterpart in the reference): the kernels the last
- * hba_b200_decode / hba_b200_decode_noalloc call of this process launched, as
- * a static string ("decode_tc_kernel", "decode_fused_kernel" or
- * "select_kernel+decode_attend_kernel"; "" before the first call).
+ * hba_b200_decode / _decode_noalloc / _prefill call of this process launched,
+ * in launch order joined by '+', as a static string (e.g. "decode_tc_kernel";
+ * "" before the first call).  The profile marks fall between them.
  */
-const char* hba_b200_last_decode_kernels(void);
+const char* hba_b200_last_kernels(void);
 
 #ifdef __cplusplus
 }
