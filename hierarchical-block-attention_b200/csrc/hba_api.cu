@@ -536,9 +536,36 @@ int hba_b200_prefill(const hba_b200_config* cfg, int32_t batch, int32_t n, float
   hba::QueryPos qp{nullptr, nullptr, n, scale};
   Lists fin{};
   int fin_lists = 0, fin_k = 0;
-  st = run_select(cfg, geo, qp, plan, static_cast<const __nv_bfloat16*>(q), q_gain, summ, sup, ws, nullptr, fin,
-                  fin_lists, fin_k, stream);
-  if (st != HBA_B200_OK) return st;
+  // flat: the query-tiled selection unless HBA_B200_SELECT_PATH=scan forces the per-query kernel
+  const char* force_sel = getenv("HBA_B200_SELECT_PATH");
+  const bool tile_sel = !(force_sel != nullptr && strcmp(force_sel, "scan") == 0) &&
+                        hba::select_tile_supported(geo, dh, summ);
+  if (tile_sel) {
+    fin = carve_lists(ws, (size_t)batch * cfg->n_kv * n * cfg->k_blocks);
+    hba::SelParams sp{};
+    sp.geo = geo;
+    sp.qp = qp;
+    sp.q = static_cast<const __nv_bfloat16*>(q);
+    sp.q_gain = q_gain;
+    sp.summ = summ;
+    sp.mode = hba::kSelFlat;
+    sp.splits = 1;
+    sp.list_k = cfg->k_blocks;
+    sp.out_score = fin.score;
+    sp.out_idx = fin.idx;
+    sp.own_blo = 0;
+    sp.own_bhi = INT_MAX;
+    sp.n_limit = geo.n_cap;
+    e = hba::launch_select_tile(sp, dh, dev_status, stream);
+    if (e != cudaSuccess) return cuda_status(e);
+    prof_mark(stream);
+    fin_lists = 1;
+    fin_k = cfg->k_blocks;
+  } else {
+    st = run_select(cfg, geo, qp, plan, static_cast<const __nv_bfloat16*>(q), q_gain, summ, sup, ws, nullptr, fin,
+                    fin_lists, fin_k, stream);
+    if (st != HBA_B200_OK) return st;
+  }
   // tensor-core union path unless HBA_B200_PREFILL_PATH=gather forces the per-query kernel
   const char* force = getenv("HBA_B200_PREFILL_PATH");
   const bool want_tc = !(force != nullptr && strcmp(force, "gather") == 0);
@@ -551,7 +578,8 @@ int hba_b200_prefill(const hba_b200_config* cfg, int32_t batch, int32_t n, float
     prof_mark(stream);
     g_last_kernels = cfg->hier ? "qknorm_rope_kernel+summarize_kernel+supers_kernel+select_kernel+select_kernel+"
                                  "prefill_tc_kernel"
-                               : "qknorm_rope_kernel+summarize_kernel+select_kernel+prefill_tc_kernel";
+                               : (tile_sel ? "qknorm_rope_kernel+summarize_kernel+select_tile_kernel+prefill_tc_kernel"
+                                           : "qknorm_rope_kernel+summarize_kernel+select_kernel+prefill_tc_kernel");
     if (sel_idx != nullptr) {  // the single-split lists are the final picks, layout [B, Hkv, n, K]
       const size_t bytes = (size_t)batch * cfg->n_kv * n * cfg->k_blocks * sizeof(int32_t);
       e = cudaMemcpyAsync(sel_idx, fin.idx, bytes, cudaMemcpyDeviceToDevice, stream);
@@ -584,7 +612,8 @@ int hba_b200_prefill(const hba_b200_config* cfg, int32_t batch, int32_t n, float
   prof_mark(stream);
   g_last_kernels = cfg->hier ? "qknorm_rope_kernel+summarize_kernel+supers_kernel+select_kernel+select_kernel+"
                                "attend_kernel"
-                             : "qknorm_rope_kernel+summarize_kernel+select_kernel+attend_kernel";
+                             : (tile_sel ? "qknorm_rope_kernel+summarize_kernel+select_tile_kernel+attend_kernel"
+                                         : "qknorm_rope_kernel+summarize_kernel+select_kernel+attend_kernel");
   return HBA_B200_OK;
 }
 

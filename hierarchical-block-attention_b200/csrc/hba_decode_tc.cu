@@ -34,6 +34,7 @@
 #include "hba_score.cuh"
 #include "hba_sm100.cuh"
 #include "hba_topk.cuh"
+#include "hba_warpsort.cuh"
 
 namespace hba {
 
@@ -76,38 +77,6 @@ HBA_DEVICE void tmem_ld_row(uint32_t taddr, float* v) {
   for (int i = 0; i < N; ++i) v[i] = __uint_as_float(r[i]);
 }
 
-// Warp-wide (score, id) compare-exchange with the lane `stride` away under
-// the library order (score desc, id asc); keep_better selects which of the
-// pair this lane keeps.
-HBA_DEVICE void cmpx(float& s, int& i, int stride, bool keep_better) {
-  const float os = __shfl_xor_sync(0xffffffffu, s, stride);
-  const int oi = __shfl_xor_sync(0xffffffffu, i, stride);
-  if (keep_better ? beats(os, oi, s, i) : beats(s, i, os, oi)) {
-    s = os;
-    i = oi;
-  }
-}
-// Bitonic sort of the warp's 32 (score, id) pairs, best in lane 0.
-HBA_DEVICE void warp_sort32(float& s, int& i) {
-  const int lane = threadIdx.x & 31;
-#pragma unroll
-  for (int size = 2; size <= 32; size <<= 1)
-#pragma unroll
-    for (int stride = size >> 1; stride > 0; stride >>= 1)
-      cmpx(s, i, stride, ((lane & stride) == 0) == ((lane & size) == 0));
-}
-// (ls, li) sorted best first <- best 32 of itself and the sorted batch (bs, bi).
-HBA_DEVICE void warp_merge32(float& ls, int& li, float bs, int bi) {
-  const int lane = threadIdx.x & 31;
-  const float rs = __shfl_sync(0xffffffffu, bs, 31 - lane);
-  const int ri = __shfl_sync(0xffffffffu, bi, 31 - lane);
-  if (beats(rs, ri, ls, li)) {  // best 32 of the union, as a bitonic sequence
-    ls = rs;
-    li = ri;
-  }
-#pragma unroll
-  for (int stride = 16; stride > 0; stride >>= 1) cmpx(ls, li, stride, (lane & stride) == 0);
-}
 
 // One ring of NSLOT slots of one K (or V) tile each carries every byte the
 // CTA reads, in this order: summary pages (128/m rows each; the flat scan, or

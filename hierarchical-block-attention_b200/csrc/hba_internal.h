@@ -134,6 +134,10 @@ cudaError_t launch_decode_fused(const DecodeAttnParams& p, const __nv_bfloat16* 
                                 int dh, cudaStream_t st);
 size_t decode_fused_smem(int dh);
 // tcgen05 decode (hba_decode_tc.cu): one CTA per (sequence, kv head), QKNorm only.
+// Prefill flat selection tiled over 64 queries per CTA (scores identical to
+// select_kernel's); writes one list of p.list_k per query.
+bool select_tile_supported(const Geom& geo, int dh, const void* summ);
+cudaError_t launch_select_tile(const SelParams& p, int dh, int* err, cudaStream_t st);
 // KV-range shard: the union over this shard's tokens [tok_lo, tok_lo + n_cap)
 // as unnormalised partials (O, l, m2) after merging n_in candidate picks per
 // (sequence, kv head) into the global top-k; and the final normalisation of

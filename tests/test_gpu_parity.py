@@ -197,6 +197,36 @@ def test_prefill_paths_agree_on_every_row():
     assert (l1 - l2).abs().max().item() < 1e-3
 
 
+@pytest.mark.parametrize("dh,heads,slots,n,block,window", [(128, (32, 8), 4, 4096, 64, 1024),
+                                                             (64, (14, 2), 4, 3072, 64, 1024),
+                                                             (64, (8, 2), 8, 2048, 64, 1024),
+                                                             (128, (16, 4), 2, 1536, 64, 1024),
+                                                             (64, (4, 2), 4, 400, 16, 64)])
+def test_prefill_tiled_selection_is_bit_identical(dh, heads, slots, n, block, window):
+    """Query-tiled selection vs the per-query scan: same picks and the same
+    fp32 scores on every row (the block-16 case leaves a partial last tile
+    of 16 queries)."""
+    import os
+    cfg = H.cfg_of(n_heads=heads[0], n_kv=heads[1], head_dim=dh, slots=slots, block=block, window=window,
+                   sinks=min(4, block))
+    summ, qkn = synth.make_weights(cfg, "cuda", seed=31, gains=True)
+    cos, sin = synth.rope_tables(n, dh, 1e6)
+    wl = synth.prefill_workload(cfg, 2, n, seed=31)
+    res = {}
+    for path in ("scan", "tile"):
+        if path == "scan":
+            os.environ["HBA_B200_SELECT_PATH"] = "scan"
+        try:
+            with torch.no_grad():
+                res[path] = hba_attention_b200(wl["q"], wl["k"], wl["v"], cos, sin, cfg, summ, qkn,
+                                               return_lse=True, return_selection=True)
+        finally:
+            os.environ.pop("HBA_B200_SELECT_PATH", None)
+    (_, _, (i1, s1)), (_, _, (i2, s2)) = res["scan"], res["tile"]
+    assert torch.equal(i1, i2)
+    assert torch.equal(s1, s2)
+
+
 def test_prefill_tiny_blocks_and_knobs():
     """Block 16, window 64, 2 sinks, k 4, 2 slots (the reference's test knobs)."""
     cfg = H.cfg_of(block=16, window=64, sinks=2, k_blocks=4, slots=2, fanout=4, beam=2, n_heads=4, n_kv=2)
