@@ -108,7 +108,7 @@ struct DtcSmem {
   int n_children;
   uint64_t full[NSLOT], empty[NSLOT];
   uint64_t s_full[2], p_full[2], p_free[2];
-  uint64_t o_full, drain, child_ready, sel_ready;
+  uint64_t o_full, drain, child_ready, sel_ready, lists_ready;
   uint32_t tmem_base;
 };
 
@@ -241,6 +241,7 @@ __global__ void __launch_bounds__(kDtThreads, 1)
     mbar_init(&sm.drain, 1);
     mbar_init(&sm.child_ready, 1);
     mbar_init(&sm.sel_ready, 1);
+    mbar_init(&sm.lists_ready, kDtScoreWarps);
     fence_barrier_init();
   }
   if (warp == 1) {
@@ -568,9 +569,25 @@ __global__ void __launch_bounds__(kDtThreads, 1)
       nsel = sm.nsel;
       stamp(5);
     } else if (!hier) {
+      // each warp publishes its list; warp 0 alone merges them, while the MMA
+      // and softmax warps go on to the window and sink chunks
       if (kfinal > 0) score_pages(0, NPa, Ra, kfinal, [&](int j) { return 1 + j; });
       stamp(5);
-      nsel = merge(max(1, kfinal));
+      sm.wl_s[sw][lane] = ls;
+      sm.wl_i[sw][lane] = li;
+      __threadfence_block();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&sm.lists_ready);
+      if (warp == 0) {
+        mbar_wait(&sm.lists_ready, 0, P.err);
+        float fs = sm.wl_s[0][lane];
+        int fi = sm.wl_i[0][lane];
+        for (int w = 1; w < NSW; ++w) warp_merge32(fs, fi, sm.wl_s[w][lane], sm.wl_i[w][lane]);
+        nsel = __popc(__ballot_sync(0xffffffffu, lane < kfinal && fi != INT_MAX));
+        sm.sel_i[lane] = fi;
+        sm.sel_s[lane] = fs;
+        if (lane == 0) sm.nsel = nsel;
+      }
       stamp(6);
     } else {
       const int kb = max(1, min(geo.beam, ns));
@@ -622,7 +639,7 @@ __global__ void __launch_bounds__(kDtThreads, 1)
       stamp(7);
       nsel = merge(max(1, kfinal));
     }
-    if (warp == 0) {
+    if (warp == 0) {  // (flat: only warp 0 knows nsel here; the others read it after sel_ready)
       const bool valid = lane < nsel;
       if (!shard && p.sel_idx != nullptr && lane < geo.K) {
         p.sel_idx[(size_t)bg * geo.K + lane] = valid ? sm.sel_i[lane] : -1;
@@ -634,9 +651,14 @@ __global__ void __launch_bounds__(kDtThreads, 1)
         mbar_arrive(&sm.sel_ready);  // picks and count are in shared memory
       }
     }
-    const int NCr = (nsel * geo.Bk + kDtKeys - 1) / kDtKeys;
-    const int NC = NCw + NCs + NCr;
+    // chunks [window | sinks] are known now; the routed ones once sel_ready completes
+    const int NCk = NCw + NCs;
     const int NP = NPa + NPb;
+    auto routed_chunks = [&]() -> int {  // waits for the picks (a no-op wait once they are in)
+      if (!mbar_wait(&sm.sel_ready, 0, P.err)) return 0;
+      nsel = sm.nsel;
+      return (nsel * geo.Bk + kDtKeys - 1) / kDtKeys;
+    };
     stamp(2);
 
     // ---- B. union softmax ----
@@ -663,7 +685,14 @@ __global__ void __launch_bounds__(kDtThreads, 1)
           umma_commit(&sm.p_free[sb]);
           return true;
         };
-        for (int c = 0; okw && c < NC; ++c) {
+        int NC = NCk;
+        bool picks_in = false;
+        for (int c = 0; okw; ++c) {
+          if (c == NC && !picks_in) {  // window and sinks issued: now the routed chunks
+            NC += routed_chunks();
+            picks_in = true;
+          }
+          if (c >= NC) break;
           const int sb = c & 1, ik = NP + 2 * c;
           if (!mbar_wait(&sm.full[ik % NSLOT], (ik / NSLOT) & 1, P.err)) {
             okw = false;
@@ -702,7 +731,14 @@ __global__ void __launch_bounds__(kDtThreads, 1)
         m2[h] = sm.m2[h];
       }
       bool okw = true;
-      for (int c = 0; c < NC; ++c) {
+      int NC = NCk;
+      bool picks_in = false;
+      for (int c = 0;; ++c) {
+        if (c == NC && !picks_in) {
+          NC += routed_chunks();
+          picks_in = true;
+        }
+        if (c >= NC) break;
         const int sb = c & 1;
         if (!mbar_wait(&sm.s_full[sb], (c >> 1) & 1, P.err)) {
           okw = false;
