@@ -417,12 +417,10 @@ int hba_b200_decode(const hba_b200_config* cfg, int32_t batch, int32_t n_cap, co
     dp.sel_idx = sel_idx;
     dp.sel_score = sel_score;
     cudaError_t e;
-    if (path == kDecodeTc) {
-      e = cudaMemsetAsync(dev_status, 0, sizeof(int), stream);
-      if (e == cudaSuccess)
-        e = hba::launch_decode_tc(dp, static_cast<const __nv_bfloat16*>(summaries),
-                                  static_cast<const __nv_bfloat16*>(supers), k_gain,
-                                  dev_status, cfg->head_dim, stream);
+    if (path == kDecodeTc) {  // the status word is sticky: no per-call reset (one launch per step)
+      e = hba::launch_decode_tc(dp, static_cast<const __nv_bfloat16*>(summaries),
+                                static_cast<const __nv_bfloat16*>(supers), k_gain, dev_status, cfg->head_dim,
+                                stream);
     } else {
       e = hba::launch_decode_fused(dp, static_cast<const __nv_bfloat16*>(summaries),
                                    static_cast<const __nv_bfloat16*>(supers), cfg->head_dim, stream);

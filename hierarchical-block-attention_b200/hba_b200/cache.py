@@ -68,6 +68,7 @@ class HBADecodeCache:
         if self.ws_bytes == 0:
             _lib.check(_lib.ERR_UNSUPPORTED, "hba_b200_decode_workspace_size")
         self.workspace = torch.empty(self.ws_bytes, dtype=torch.uint8, device=dev)
+        self.workspace[:256].zero_()  # sticky device status word (see device_status)
 
     # ---------------------------------------------------------------- state --
     def _refresh_scales(self):
@@ -120,6 +121,15 @@ class HBADecodeCache:
         if return_selection:
             res += ((si, ss),)
         return res[0] if len(res) == 1 else res
+
+    def device_status(self, clear=False):
+        """The decode's sticky device status (0 = ok, 1 = a bounded device wait
+        timed out, 2 = a QKNorm logit bound too large for the tensor-core
+        path); synchronises with the device.  `clear` resets it to 0."""
+        st = int(self.workspace[:4].view(torch.int32).item())
+        if clear:
+            self.workspace[:4].zero_()
+        return st
 
     def decode_into(self, qb, out, lse=None, sel_idx=None, sel_score=None, stream=None):
         """Allocation-free decode on preallocated bf16 q/out (graph-capturable)."""

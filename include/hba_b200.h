@@ -131,6 +131,11 @@ size_t hba_b200_decode_workspace_size(const hba_b200_config* cfg, int32_t batch,
  *   out:       [batch, Hq, dh] bf16;  lse: [batch, Hq] fp32 natural-log or NULL
  *   sel_idx:   [batch, Hkv, k_blocks] int32 (-1: no pick) or NULL
  *   sel_score: [batch, Hkv, k_blocks] fp32 or NULL
+ * The first 4 bytes of the workspace hold a sticky device status: the caller
+ * zeroes them once (and whenever it clears an error); a decode that meets a
+ * device error sets 1 (a bounded wait timed out) or 2 (a QKNorm logit bound
+ * too large for the tensor-core path's fixed-max softmax) and later calls
+ * leave it set.  No per-call reset keeps a decode step at one kernel launch.
  * Replaces the per-query body of hba_attention_eval
  * (src/hba/attention.py:663-711) at cs = n-1, flat (:694-698) or
  * hierarchical (:690-693, hier_select :217-246).

@@ -84,6 +84,7 @@ def check_decode(cache, q, cfg, hier, qkn, cos, sin, rows=None, lens=None):
         worst_l = max(worst_l, float(np.abs(lse_n[b] - res["lse"][0]).max()))
     assert worst_o <= OUT_TOL, worst_o
     assert worst_l <= LSE_TOL, worst_l
+    assert cache.device_status() == 0  # no bounded wait expired, no logit bound overflowed
     return worst_o, worst_l, (si, ss)
 
 
