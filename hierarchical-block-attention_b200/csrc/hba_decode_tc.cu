@@ -41,7 +41,6 @@ namespace hba {
 using namespace sm100;
 
 constexpr int kDtThreads = 256;
-constexpr int kDtWarps = 8;
 constexpr int kDtKeys = 128;  // keys per chunk (UMMA M)
 constexpr int kDtProducer = 3;    // warp that feeds the ring from the first instruction on
 constexpr int kDtScoreWarps = 7;  // every other warp scores summary pages
@@ -225,6 +224,14 @@ __global__ void __launch_bounds__(kDtThreads, 1)
   }
   const __nv_bfloat16* rows_a = hier ? sup_bg : summ_bg;
   const int NPa = (Ra + PB - 1) / PB;
+  // Ring item order: [NPa phase-A pages][K,V of chunks 0 .. WA-1][NPb child
+  // pages][K,V of chunks WA ..].  Flat: WA = all window/sink chunks (no child
+  // pages).  Hier: a few window chunks go ahead of the child pages, so the
+  // attention warps have work (and the memory pipe traffic) while the super
+  // top-k runs.
+  const int NCk = NCw + NCs;  // window + sink chunks: known before any selection
+  const int WA = hier ? min(NCk, SM::NSLOT / 3) : NCk;
+  auto item_of_chunk = [&](int c, int npb) { return c < WA ? NPa + 2 * c : NPa + 2 * WA + npb + 2 * (c - WA); };
 
   // ---- barriers, TMEM ----
   if (producer && lane == 0) {
@@ -254,23 +261,22 @@ __global__ void __launch_bounds__(kDtThreads, 1)
   const uint32_t tmem = sm.tmem_base;  // cols [0,16) S0, [16,32) S1, [32,48) O^T
 
   if (producer) {
-    // ---- ring producer: items [0, NPa) phase-A pages, [NPa, NP) child
-    // pages, then the K and V tiles of chunk c at NP + 2c, NP + 2c + 1 ----
+    // ---- ring producer: the items in the order described at item_of_chunk ----
     if (lane == 0) {
       prefetch_tmap(&tm_kc);
       prefetch_tmap(&tm_kr);
       prefetch_tmap(&tm_v);
       int NPb = 0, R2 = 0, nsel = 0, issued = 0;
       auto issue_item = [&](int i) {
-        const int NP = NPa + NPb;
         unsigned char* dst = sm.ring[i % NSLOT];
         uint64_t* fb = &sm.full[i % NSLOT];
+        const int cp0 = NPa + 2 * WA;  // first child page item
         if (i < NPa) {
           const int j0 = i * PB, nr = min(PB, Ra - j0);
           mbar_arrive_expect_tx(fb, (uint32_t)(nr * row_bytes));
           bulk_load(dst, rows_a + (size_t)(ida + j0) * row_elems, (uint32_t)(nr * row_bytes), fb);
-        } else if (i < NP) {  // children of the beam: one bulk copy per contiguous span
-          const int j0 = (i - NPa) * PB, j1 = min(R2, j0 + PB);
+        } else if (i >= cp0 && i < cp0 + NPb) {  // children of the beam: one bulk copy per contiguous span
+          const int j0 = (i - cp0) * PB, j1 = min(R2, j0 + PB);
           mbar_arrive_expect_tx(fb, (uint32_t)((j1 - j0) * row_bytes));
           for (int si = 0; si < 32; ++si) {
             const int lo = max(j0, sm.sup_off[si]), hi = min(j1, sm.sup_off[si] + sm.sup_cnt[si]);
@@ -280,7 +286,8 @@ __global__ void __launch_bounds__(kDtThreads, 1)
                         (uint32_t)((hi - lo) * row_bytes), fb);
           }
         } else {
-          const int c = (i - NP) >> 1, is_v = (i - NP) & 1;
+          const int e = i < cp0 ? i - NPa : i - NPb - NPa;  // 2 * chunk + (V ? 1 : 0)
+          const int c = e >> 1, is_v = e & 1;
           int kind, t0, t1;
           if (c < NCw) {
             kind = 0;
@@ -314,16 +321,16 @@ __global__ void __launch_bounds__(kDtThreads, 1)
         }
         return true;
       };
-      bool okp = pump_to(hier ? NPa : NPa + 2 * (NCw + NCs));  // window/sink tiles need no selection
+      bool okp = pump_to(NPa + 2 * WA);  // window/sink tiles need no selection
       if (hier && okp) {
         okp = mbar_wait(&sm.child_ready, 0, P.err);
         R2 = sm.n_children;
         NPb = (R2 + PB - 1) / PB;
-        okp = okp && pump_to(NPa + NPb + 2 * (NCw + NCs));
+        okp = okp && pump_to(NPa + NPb + 2 * NCk);
       }
       if (okp && mbar_wait(&sm.sel_ready, 0, P.err)) {
         nsel = sm.nsel;
-        pump_to(NPa + NPb + 2 * (NCw + NCs + (nsel * geo.Bk + kDtKeys - 1) / kDtKeys));
+        pump_to(NPa + NPb + 2 * (NCk + (nsel * geo.Bk + kDtKeys - 1) / kDtKeys));
       }
     }
   } else {
@@ -413,8 +420,9 @@ __global__ void __launch_bounds__(kDtThreads, 1)
     int li = INT_MAX;
     if (tid == 0) sm.thr = 0u;  // order_key of the best k-th score any warp has reached
     score_bar();
+    int pg_first = sw, pg_stride = NSW;  // which pages this warp scores
     auto score_pages = [&](int i0, int np, int R, int k, auto id_of) {
-      for (int pg = sw; pg < np; pg += NSW) {
+      for (int pg = pg_first; pg < np; pg += pg_stride) {
         const int i = i0 + pg;
         mbar_wait(&sm.full[i % NSLOT], (i / NSLOT) & 1, P.err);
         const unsigned char* src = sm.ring[i % NSLOT];
@@ -589,11 +597,33 @@ __global__ void __launch_bounds__(kDtThreads, 1)
         if (lane == 0) sm.nsel = nsel;
       }
       stamp(6);
-    } else {
+    } else if (warp == 0 || warp == 2) {
+      // hierarchical: warps 0 and 2 select (a level has a few pages); warps 1
+      // and 4-7 go on to the window chunks (phase B) at once
+      const int hw = warp >> 1;
+      pg_first = hw;
+      pg_stride = 2;
+      auto pair_bar = []() { asm volatile("bar.sync 3, 64;\n" ::: "memory"); };
+      auto merge2 = [&](int k) -> int {  // the two lists -> best-first picks in sm.sel_i / sel_s
+        sm.wl_s[hw][lane] = ls;
+        sm.wl_i[hw][lane] = li;
+        pair_bar();
+        if (warp == 0) {
+          float fs = sm.wl_s[0][lane];
+          int fi = sm.wl_i[0][lane];
+          warp_merge32(fs, fi, sm.wl_s[1][lane], sm.wl_i[1][lane]);
+          const int n = __popc(__ballot_sync(0xffffffffu, lane < k && fi != INT_MAX));
+          sm.sel_i[lane] = fi;
+          sm.sel_s[lane] = fs;
+          if (lane == 0) sm.nsel = n;
+        }
+        pair_bar();
+        return sm.nsel;
+      };
       const int kb = max(1, min(geo.beam, ns));
       score_pages(0, NPa, Ra, kb, [&](int j) { return ida + j; });
       stamp(5);
-      const int nsup = merge(kb);
+      const int nsup = merge2(kb);
       if (warp == 0) {  // the beam's supers in ascending order; their children as contiguous spans
         const bool valid = lane < nsup;
         const int sidx = valid ? sm.sel_i[lane] : INT_MAX;
@@ -624,7 +654,7 @@ __global__ void __launch_bounds__(kDtThreads, 1)
         __threadfence_block();
         if (lane == 0) mbar_arrive(&sm.child_ready);
       }
-      score_bar();
+      pair_bar();
       const int R2 = sm.n_children;
       NPb = (R2 + PB - 1) / PB;
       stamp(6);
@@ -635,9 +665,9 @@ __global__ void __launch_bounds__(kDtThreads, 1)
       };
       ls = neg_inf();
       li = INT_MAX;
-      if (kfinal > 0) score_pages(NPa, NPb, R2, kfinal, child_id);
+      if (kfinal > 0) score_pages(NPa + 2 * WA, NPb, R2, kfinal, child_id);
       stamp(7);
-      nsel = merge(max(1, kfinal));
+      nsel = merge2(max(1, kfinal));
     }
     if (warp == 0) {  // (flat: only warp 0 knows nsel here; the others read it after sel_ready)
       const bool valid = lane < nsel;
@@ -653,7 +683,6 @@ __global__ void __launch_bounds__(kDtThreads, 1)
     }
     // chunks [window | sinks] are known now; the routed ones once sel_ready completes
     const int NCk = NCw + NCs;
-    const int NP = NPa + NPb;
     auto routed_chunks = [&]() -> int {  // waits for the picks (a no-op wait once they are in)
       if (!mbar_wait(&sm.sel_ready, 0, P.err)) return 0;
       nsel = sm.nsel;
@@ -667,8 +696,9 @@ __global__ void __launch_bounds__(kDtThreads, 1)
         constexpr uint32_t idesc_s = idesc_bf16(128, 16, false, false);
         constexpr uint32_t idesc_o = idesc_bf16(128, 16, true, false);
         bool okw = true;
+        int npb = 0;  // child pages ahead of chunk WA (hier: known at child_ready)
         auto pv = [&](int c) -> bool {
-          const int sb = c & 1, iv = NP + 2 * c + 1;
+          const int sb = c & 1, iv = item_of_chunk(c, npb) + 1;
           if (!mbar_wait(&sm.p_full[sb], (c >> 1) & 1, P.err)) return false;
           if (!mbar_wait(&sm.full[iv % NSLOT], (iv / NSLOT) & 1, P.err)) return false;
           tc_fence_after();
@@ -693,7 +723,14 @@ __global__ void __launch_bounds__(kDtThreads, 1)
             picks_in = true;
           }
           if (c >= NC) break;
-          const int sb = c & 1, ik = NP + 2 * c;
+          if (hier && c == WA) {  // chunks from here on sit behind the child pages in the ring
+            if (!mbar_wait(&sm.child_ready, 0, P.err)) {
+              okw = false;
+              break;
+            }
+            npb = (sm.n_children + PB - 1) / PB;
+          }
+          const int sb = c & 1, ik = item_of_chunk(c, npb);
           if (!mbar_wait(&sm.full[ik % NSLOT], (ik / NSLOT) & 1, P.err)) {
             okw = false;
             break;
