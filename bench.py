@@ -49,8 +49,9 @@ def parse():
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--config", default="cfg1", choices=["cfg1", "cfg2", "cfg3", "cfg3-shard"])
     ap.add_argument("--no-secondary", action="store_true")
-    ap.add_argument("--ncu-case", default=None, choices=["cfg1", "cfg3"],
-                    help="profiling target: build this decode workload (cfg3 at batch 4), run 3 decodes, exit")
+    ap.add_argument("--ncu-case", default=None, choices=["cfg1", "cfg3", "cfg2"],
+                    help="profiling target: build this decode workload (cfg3 at batch 4) and run 3 decodes, "
+                         "or (cfg2) one prefill forward; no timing, no output")
     return ap.parse_args()
 
 
@@ -230,11 +231,21 @@ def shard_bench(name, steps, warmup, world, rank, local, pk):
 
 def ncu_case(name, local):
     """Profiling target: the decode workload `name` (cfg3 at batch 4, so that
-    the device holds a few GB), decoded 3 times; no timing, no output."""
+    the device holds a few GB), decoded 3 times, or (cfg2) one prefill
+    forward at full size (~3 GB on the device); no timing, no output."""
     from hba_b200 import HBADecodeCache, baseline_config, synth
     from hba_b200.attention import stream_of
     dev = torch.device("cuda", local)
     cfg, B, n, hier = baseline_config(name)
+    if name == "cfg2":
+        from hba_b200 import hba_attention_b200
+        summ, qkn = synth.make_weights(cfg, dev, seed=0, gains=False)
+        cos, sin = synth.rope_tables(n, cfg.head_dim, 1e6, dev)
+        wl = synth.prefill_workload(cfg, B, n, seed=0, device=dev)
+        with torch.no_grad():
+            hba_attention_b200(wl["q"], wl["k"], wl["v"], cos, sin, cfg, summ, qkn, hier=hier)
+        torch.cuda.synchronize()
+        return
     if name == "cfg3":
         B = 4
         os.environ["HBA_B200_DECODE_PATH"] = "tc"  # the kernel the full-size bench runs (batch 4 alone would split)

@@ -48,33 +48,6 @@ constexpr int kDtScoreWarps = 7;  // every other warp scores summary pages
 // barrier of the 7 scoring warps (the producer warp never joins it)
 HBA_DEVICE void score_bar() { asm volatile("bar.sync 2, 224;\n" ::: "memory"); }
 
-// 2^x by the MUFU instruction (ex2.approx.ftz: relative error ~2^-22, far
-// below the bf16 rounding of the probabilities it feeds)
-HBA_DEVICE float ex2_approx(float x) {
-  float y;
-  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
-  return y;
-}
-
-// N fp32 columns of this thread's TMEM lane (32x32b shape), waited.
-template <int N>
-HBA_DEVICE void tmem_ld_row(uint32_t taddr, float* v) {
-  uint32_t r[N];
-  if constexpr (N == 8) {
-    asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];\n"
-                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7])
-                 : "r"(taddr));
-  } else {
-    asm volatile(
-        "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];\n"
-        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
-          "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
-        : "r"(taddr));
-  }
-  asm volatile("tcgen05.wait::ld.sync.aligned;\n" ::: "memory");
-#pragma unroll
-  for (int i = 0; i < N; ++i) v[i] = __uint_as_float(r[i]);
-}
 
 
 // One ring of NSLOT slots of one K (or V) tile each carries every byte the
@@ -435,7 +408,7 @@ __global__ void __launch_bounds__(kDtThreads, 1)
             const unsigned char* row = src + (size_t)r * row_bytes;
             float best = neg_inf();
             for (int sl = 0; sl < m_slots; ++sl) {
-              float pp[LPS];
+              float t0 = 0.f, t1 = 0.f, t2 = 0.f, t3 = 0.f;  // pending sums of the pairwise tree
 #pragma unroll
               for (int q = 0; q < LPS; ++q) {
                 const int vq = q ^ o;
@@ -454,13 +427,30 @@ __global__ void __launch_bounds__(kDtThreads, 1)
                 float part = 0.f;
 #pragma unroll
                 for (int jj = 0; jj < 8; ++jj) part = fmaf(f[jj], qv[jj], part);
-                pp[q] = part;
+                // fold into the tree as the vectors arrive: ((p0+p1)+(p2+p3))+...
+                if ((q & 1) == 0) {
+                  t0 = part;
+                } else {
+                  const float l1 = t0 + part;
+                  if ((q & 2) == 0) {
+                    t1 = l1;
+                  } else {
+                    const float l2 = t1 + l1;
+                    if ((q & 4) == 0) {
+                      t2 = l2;
+                    } else {
+                      const float l3 = t2 + l2;
+                      if (LPS == 8) {
+                        best = fmaxf(best, l3);
+                      } else if ((q & 8) == 0) {
+                        t3 = l3;
+                      } else {
+                        best = fmaxf(best, t3 + l3);
+                      }
+                    }
+                  }
+                }
               }
-#pragma unroll
-              for (int w = 1; w < LPS; w <<= 1)
-#pragma unroll
-                for (int q = 0; q < LPS; q += 2 * w) pp[q] = pp[q] + pp[q + w];
-              best = fmaxf(best, pp[0]);
             }
             cs = best * scale;
             ci = id_of(pg * PB + r);

@@ -316,29 +316,42 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       const uint2 e = sm.chunks[c];
       const int kb = (int)(e.x & 0x0FFFFFFFu);
       const uint32_t type = e.x >> 28;
-      bool any = row_ok;
-      if (type == kRouted) any = any && ((e.y >> qt) & 1u);
-      unsigned char* prow = sm.p[sb];
-#pragma unroll
-      for (int c8 = 0; c8 < kTcKeys / 8; ++c8) {
-        uint32_t w[4];
-#pragma unroll
-        for (int t = 0; t < 4; ++t) {
-          float pv2[2];
-#pragma unroll
-          for (int u = 0; u < 2; ++u) {
-            const int col = c8 * 8 + 2 * t + u;
-            const int j = kb + col;
-            bool valid = any;
-            if (type == kSink) valid = valid && j < geo.S && j <= i;
-            else if (type == kWindow) valid = valid && j >= win_lo && j <= i;
-            const float pe = valid ? exp2f(fmaf(s[col], sl2, -M2)) : 0.f;
-            l += pe;
-            pv2[u] = pe;
-          }
-          w[t] = pack_bf16x2(pv2[0], pv2[1]);
+      // this row's valid columns [cl, ch) of the chunk, worked out once
+      int cl = 0, ch = 0;
+      if (row_ok) {
+        if (type == kRouted) {
+          ch = ((e.y >> qt) & 1u) ? kTcKeys : 0;  // a picked block is wholly before i - W + 1
+        } else if (type == kSink) {
+          ch = min(geo.S, i + 1) - kb;
+        } else {
+          cl = max(win_lo - kb, 0);
+          ch = min(i - kb + 1, kTcKeys);
         }
-        *reinterpret_cast<uint4*>(prow + sw128_offset(r, c8 * 8)) = make_uint4(w[0], w[1], w[2], w[3]);
+      }
+      unsigned char* prow = sm.p[sb];
+      if (ch <= cl) {  // nothing of this chunk for this row (most rows of a block few queries picked)
+#pragma unroll
+        for (int c8 = 0; c8 < kTcKeys / 8; ++c8)
+          *reinterpret_cast<uint4*>(prow + sw128_offset(r, c8 * 8)) = make_uint4(0u, 0u, 0u, 0u);
+      } else {
+#pragma unroll
+        for (int c8 = 0; c8 < kTcKeys / 8; ++c8) {
+          uint32_t w[4];
+#pragma unroll
+          for (int t = 0; t < 4; ++t) {
+            float pv2[2];
+#pragma unroll
+            for (int u = 0; u < 2; ++u) {
+              const int col = c8 * 8 + 2 * t + u;
+              float pe = ex2_approx(fmaf(s[col], sl2, -M2));
+              pe = (col >= cl && col < ch) ? pe : 0.f;
+              l += pe;
+              pv2[u] = pe;
+            }
+            w[t] = pack_bf16x2(pv2[0], pv2[1]);
+          }
+          *reinterpret_cast<uint4*>(prow + sw128_offset(r, c8 * 8)) = make_uint4(w[0], w[1], w[2], w[3]);
+        }
       }
       fence_proxy_async_smem();
       tc_fence_before();
