@@ -4,8 +4,8 @@
 // summary rows of the candidate blocks stream through shared memory in
 // stages of 64 blocks (1-D bulk copies, double-buffered), and every staged
 // row is used by all 64 queries of the tile -- instead of every query
-// re-reading every candidate row from L2 (select_kernel).  Each thread
-// scores 4 queries x 4 blocks per stage.
+// re-reading every candidate row from L2 (select_kernel).  Each of the 512
+// threads scores 4 queries x 2 blocks per stage.
 //
 // Scores are bit-identical to select_kernel / SummaryLoads::score
 // (hba_score.cuh): routing query qg = bf16(fp32 sum, in head order, of the
@@ -13,8 +13,8 @@
 // chain from 0; the vectors of a slot added in the pairwise tree ((v0+v1) +
 // (v2+v3)) + ...; max over slots; times the union scale.  Candidates: blocks
 // 1 .. bmax(i), bmax(i) = min((i - W + 1)/Bk - 1, nb - 1) (reference
-// src/hba/attention.py:250-256, :694-698).  Each warp keeps, for 8 of the
-// tile's queries, the best 32 (score desc, block asc) in registers
+// src/hba/attention.py:250-256, :694-698).  Each warp keeps, for 4 of the
+// tile's queries, the best 32 (score desc, block asc) in shared memory
 // (hba_warpsort.cuh) and writes the top k as the query's single list.
 #include <climits>
 
@@ -30,13 +30,15 @@ using namespace sm100;
 
 constexpr int kTsQ = 64;          // queries per CTA
 constexpr int kTsB = 64;          // summary blocks per stage
-constexpr int kTsThreads = 256;
+constexpr int kTsThreads = 512;
+constexpr int kTsWarps = kTsThreads / 32;
+constexpr int kTsQpw = kTsQ / kTsWarps;  // queries per warp in the prologue and the top-k
 constexpr int kTsStageBytes = 65536;  // kTsB rows of m * dh bf16 (m * dh <= 512)
 
 template <int DH>
 struct TsSmem {
   alignas(1024) unsigned char stage[2][kTsStageBytes];
-  alignas(16) uint4 qg[kTsQ][DH / 8];  // bf16 routing queries, vector v of row r at v ^ ((r >> 2) & 7)
+  alignas(16) float4 qg[kTsQ][DH / 4];  // fp32 routing queries; 16-byte chunk c of row r at c ^ ((r >> 2) & 7)
   float sc[kTsQ][kTsB + 1];
   float ls[kTsQ][32];  // per-query running best 32 (score desc, block asc)
   int li[kTsQ][32];
@@ -86,8 +88,8 @@ __global__ void __launch_bounds__(kTsThreads, 1) select_tile_kernel(SelParams p,
     for (int s = 0; s < min(2, nstage); ++s) issue(s);
   }
 
-  // ---- routing queries of the tile (warp w: queries 8w .. 8w+7) ----
-  for (int r = warp * 8; r < warp * 8 + 8; ++r) {
+  // ---- routing queries of the tile (warp w: queries kTsQpw*w ..) ----
+  for (int r = warp * kTsQpw; r < warp * kTsQpw + kTsQpw; ++r) {
     const int i = i0 + r;
     float acc[PER];
 #pragma unroll
@@ -102,23 +104,23 @@ __global__ void __launch_bounds__(kTsThreads, 1) select_tile_kernel(SelParams p,
         for (int e = 0; e < PER; ++e) acc[e] += v[e];
       }
     }
-    // lane holds elements lane*PER .. +PER of the row: write them as bf16 into the swizzled vector
+    // lane holds elements lane*PER .. +PER of the row: qg = bf16(sum), kept as fp32
     const int d0 = lane * PER;
-    const int vec = d0 / 8, sw = vec ^ ((r >> 2) & 7);
-    __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(&sm.qg[r][sw]) + (d0 % 8);
+    float* dst = reinterpret_cast<float*>(&sm.qg[r][(d0 / 4) ^ ((r >> 2) & 7)]) + (d0 % 4);
 #pragma unroll
-    for (int e = 0; e < PER; ++e) dst[e] = __float2bfloat16_rn(acc[e]);
+    for (int e = 0; e < PER; ++e) dst[e] = round_bf16(acc[e]);
   }
   __syncthreads();
 
-  // ---- per-query running lists (shared memory): warp w owns queries 8w .. 8w+7 ----
+  // ---- per-query running lists (shared memory): warp w owns queries kTsQpw*w .. ----
 #pragma unroll
-  for (int u = 0; u < 8; ++u) {
-    sm.ls[warp * 8 + u][lane] = neg_inf();
-    sm.li[warp * 8 + u][lane] = INT_MAX;
+  for (int u = 0; u < kTsQpw; ++u) {
+    sm.ls[warp * kTsQpw + u][lane] = neg_inf();
+    sm.li[warp * kTsQpw + u][lane] = INT_MAX;
   }
   const int k = p.list_k;
-  const int qgrp = tid & 15, bgrp = tid >> 4;  // this thread's 4 queries x 4 blocks
+  const int qgrp = tid & 15, bgrp = tid >> 4;  // this thread's 4 queries x 2 blocks
+  const int qsw = qgrp & 7;                    // swizzle of its qg rows (row >> 2 == qgrp)
   bool ok = true;
 
   for (int s = 0; s < nstage; ++s) {
@@ -126,30 +128,30 @@ __global__ void __launch_bounds__(kTsThreads, 1) select_tile_kernel(SelParams p,
     const int nblk = min(kTsB, bmax_tile + 1 - blo);
     if (!mbar_wait(&sm.full[s & 1], (s >> 1) & 1, err)) ok = false;
     const unsigned char* st = sm.stage[s & 1];
-    float best[4][4];
+    float best[4][2];
 #pragma unroll
     for (int i = 0; i < 4; ++i)
 #pragma unroll
-      for (int j = 0; j < 4; ++j) best[i][j] = neg_inf();
-    int jr[4];  // staged row of each of the thread's blocks (clamped; masked below)
+      for (int j = 0; j < 2; ++j) best[i][j] = neg_inf();
+    int jr[2];  // staged row of each of the thread's blocks (clamped; masked below)
 #pragma unroll
-    for (int j = 0; j < 4; ++j) jr[j] = min(4 * bgrp + j, nblk - 1);
+    for (int j = 0; j < 2; ++j) jr[j] = min(2 * bgrp + j, nblk - 1);
     for (int sl = 0; sl < m; ++sl) {
-      float a[4][4], s1[4][4], s2[4][4], s3[4][4];
+      float a[4][2], s1[4][2], s2[4][2], s3[4][2];
 #pragma unroll 1
       for (int v = 0; v < VPR; ++v) {  // rolled: the tree position is a run-time bit test
-        float sf[4][8];
+        float sf[2][8];
 #pragma unroll
-        for (int j = 0; j < 4; ++j)
+        for (int j = 0; j < 2; ++j)
           unpack8(*reinterpret_cast<const uint4*>(st + (size_t)jr[j] * row_bytes + (sl * VPR + v) * 16), sf[j]);
-        float pv[4][4];
+        float pv[4][2];
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
           const int r = 4 * qgrp + i;
-          float qf[8];
-          unpack8(sm.qg[r][v ^ ((r >> 2) & 7)], qf);
+          const float4 qa = sm.qg[r][(2 * v) ^ qsw], qb = sm.qg[r][(2 * v + 1) ^ qsw];
+          const float qf[8] = {qa.x, qa.y, qa.z, qa.w, qb.x, qb.y, qb.z, qb.w};
 #pragma unroll
-          for (int j = 0; j < 4; ++j) {
+          for (int j = 0; j < 2; ++j) {
             float part = 0.f;
 #pragma unroll
             for (int e = 0; e < 8; ++e) part = fmaf(sf[j][e], qf[e], part);
@@ -160,7 +162,7 @@ __global__ void __launch_bounds__(kTsThreads, 1) select_tile_kernel(SelParams p,
 #pragma unroll
         for (int i = 0; i < 4; ++i)
 #pragma unroll
-          for (int j = 0; j < 4; ++j) {
+          for (int j = 0; j < 2; ++j) {
             if ((v & 1) == 0) {
               a[i][j] = pv[i][j];
             } else {
@@ -191,8 +193,8 @@ __global__ void __launch_bounds__(kTsThreads, 1) select_tile_kernel(SelParams p,
       const int qi = 4 * qgrp + i;
       const int bm = bmax_of(i0 + qi);
 #pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        const int bl = 4 * bgrp + j;
+      for (int j = 0; j < 2; ++j) {
+        const int bl = 2 * bgrp + j;
         sm.sc[qi][bl] = (bl < nblk && blo + bl <= bm) ? best[i][j] * scale : neg_inf();
       }
     }
@@ -200,8 +202,8 @@ __global__ void __launch_bounds__(kTsThreads, 1) select_tile_kernel(SelParams p,
     if (tid == 0 && s + 2 < nstage) issue(s + 2);
     // one rolled copy of the sort network (unrolled copies thrash the instruction cache)
 #pragma unroll 1
-    for (int u = 0; u < 8; ++u) {
-      const int qi = warp * 8 + u;
+    for (int u = 0; u < kTsQpw; ++u) {
+      const int qi = warp * kTsQpw + u;
       float ls = sm.ls[qi][lane];
       int li = sm.li[qi][lane];
 #pragma unroll 1
@@ -219,8 +221,8 @@ __global__ void __launch_bounds__(kTsThreads, 1) select_tile_kernel(SelParams p,
   if (!ok && tid == 0) atomicExch(err, 1);
 
   // ---- lists out: [bg, query, 1, k] ----
-  for (int u = 0; u < 8; ++u) {
-    const int qi = warp * 8 + u, i = i0 + qi;
+  for (int u = 0; u < kTsQpw; ++u) {
+    const int qi = warp * kTsQpw + u, i = i0 + qi;
     if (i < nq && lane < k) {
       const size_t o = ((size_t)bg * nq + i) * k + lane;
       const int id = sm.li[qi][lane];
