@@ -12,7 +12,8 @@ hba_b200_decode with the cache resident in HBM; L2 is flushed (a 256 MB
 write) before every timed step, outside the timed events.  `value` is decode
 queries/s over all ranks (each rank decodes its own batch: weak scaling).
 `e2e` is the same step through the C-ABI call with the query copied from
-pinned host memory and the output + LSE copied back, inside the timed region.
+pinned host memory and the output + LSE copied back, inside the timed region
+(the three captured as one CUDA graph, as a serving loop runs a step).
 The secondary lines measure config 3 (hierarchical decode at 128K) and
 config 2 (prefill at 32K), and with N > 1 ranks config 3 with every 128K
 context sharded by token range over the N GPUs (one batch of 32 sequences,
@@ -209,8 +210,10 @@ def shard_bench(name, steps, warmup, world, rank, local, pk):
     out = torch.empty_like(q)
     lse = torch.empty(B, cfg.n_heads, dtype=torch.float32, device=dev)
     flush = torch.empty(FLUSH_BYTES // 4, dtype=torch.float32, device=dev)
-    times, clocks = timed_steps(lambda: sh.decode_into(q, out, lse), steps, warmup, flush, world, dev, local)
+    sh.capture(q, out, lse)  # the step as one CUDA graph (kernels + NCCL collectives)
+    times, clocks = timed_steps(sh.replay, steps, warmup, flush, world, dev, local)
     t_ms = max_over_ranks(statistics.mean(times), world, dev)
+    sh.release()
     res = dict(
         metric=METRIC, value=B / (t_ms * 1e-3), unit="decode queries/s", n_gpus=world, steps=steps, warmup=warmup,
         ms_per_step=t_ms, higher_is_better=True, scaling="strong", vs_baseline=None, dtype="bf16",
@@ -219,7 +222,8 @@ def shard_bench(name, steps, warmup, world, rank, local, pk):
                              f"ranks by token range ({sh.n_loc} tokens each)", batch=B, context=n,
                     tokens_per_rank=sh.n_loc, hier=hier,
                     collectives_per_step=(2 if hier else 1) + 1,
-                    l2="flushed (256 MB write) before every timed step", timing="CUDA events, max over ranks",
+                    l2="flushed (256 MB write) before every timed step",
+                    timing="CUDA graph replay of the step (kernels + collectives), CUDA events, max over ranks",
                     parallelism=f"kv-range shards x{world} (NCCL all-gather of top-k lists, all-reduce of partials)"),
         gpu_launches=steps * ((2 if hier else 1) + 2),
         clocks=clocks,
@@ -318,19 +322,30 @@ def decode_bench(name, steps, warmup, world, rank, local, pk):
     achieved = dom_bytes / (attend_ms * 1e-3) / 1e9
     traffic = traffic_of(f"{dom_kernel}_{name}")
 
-    # e2e: the C-ABI call with the query from pinned host memory and out + lse back
+    # e2e: the C-ABI call with the query copied from pinned host memory and
+    # out + lse (one device buffer) copied back, captured as one CUDA graph as
+    # a serving loop runs it
     q_host = q.cpu().pin_memory()
-    out_host = torch.empty(out.shape, dtype=out.dtype).pin_memory()
-    lse_host = torch.empty(lse.shape, dtype=lse.dtype).pin_memory()
+    ob, lb = out.numel() * out.element_size(), lse.numel() * lse.element_size()
+    io = torch.empty(ob + lb, dtype=torch.uint8, device=dev)
+    out_e = io[:ob].view(out.dtype).view(out.shape)
+    lse_e = io[ob:].view(lse.dtype).view(lse.shape)
+    io_host = torch.empty(ob + lb, dtype=torch.uint8).pin_memory()
 
-    def step_e2e():
+    def step_e2e_body():
         q.copy_(q_host, non_blocking=True)
-        cache.decode_into(q, out, lse, stream=stream_of(dev))
-        out_host.copy_(out, non_blocking=True)
-        lse_host.copy_(lse, non_blocking=True)
+        cache.decode_into(q, out_e, lse_e, stream=stream_of(dev))
+        io_host.copy_(io, non_blocking=True)
 
-    e2e_times, _ = timed_steps(step_e2e, steps, warmup, flush, world, dev, local)
+    step_e2e_body()
+    torch.cuda.synchronize()
+    g_e2e = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g_e2e):
+        step_e2e_body()
+    e2e_times, _ = timed_steps(g_e2e.replay, steps, warmup, flush, world, dev, local)
     e2e_ms = max_over_ranks(statistics.mean(e2e_times), world, dev)
+    # the copied-back result is the device result
+    assert torch.equal(io_host[:ob].view(out.dtype).view(out.shape), out_e.cpu())
 
     res = dict(
         metric=METRIC, value=B * world / (t_ms * 1e-3), unit="decode queries/s", n_gpus=world, steps=steps,
@@ -352,8 +367,8 @@ def decode_bench(name, steps, warmup, world, rank, local, pk):
         kernel_ms={"select": kt[:-1], "attend": attend_ms} if not single else {kernels: attend_ms},
         cache_build_s=build_s,
         e2e=dict(value=B * world / (e2e_ms * 1e-3), unit="decode queries/s", ms_per_step=e2e_ms,
-                 h2d_bytes_per_step=q.numel() * q.element_size(),
-                 d2h_bytes_per_step=out.numel() * out.element_size() + lse.numel() * lse.element_size()),
+                 h2d_bytes_per_step=q.numel() * q.element_size(), d2h_bytes_per_step=ob + lb,
+                 timing="one CUDA graph per step: pinned H2D of q, hba_b200_decode, D2H of out + lse"),
         gpu_launches=steps * (len(kt) + 0),
         clocks=clocks,
     )

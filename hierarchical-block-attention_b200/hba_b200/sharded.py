@@ -188,6 +188,24 @@ class HBAShardedDecode:
         self.comm.all_reduce_sum(self.part)
         self.ops.finish(self, self.part_o, self.part_l, self.part_m2, out, lse)
 
+    def capture(self, q, out, lse=None, sel_idx=None, sel_score=None):
+        """Capture one step -- kernels, list reshuffles and collectives -- as a
+        CUDA graph on these fixed buffers; `replay()` runs it.  Every rank must
+        capture (the collectives are part of the graph).  Call `release()`
+        before the process group is destroyed."""
+        self.decode_into(q, out, lse, sel_idx, sel_score)  # warm-up outside the capture
+        torch.cuda.synchronize(self.device)
+        self.graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(self.graph):
+            self.decode_into(q, out, lse, sel_idx, sel_score)
+        torch.cuda.synchronize(self.device)
+
+    def replay(self):
+        self.graph.replay()
+
+    def release(self):
+        self.graph = None
+
     def attend(self, q, return_lse=False):
         """Allocating convenience wrapper of `decode_into`."""
         if q.dim() == 4:

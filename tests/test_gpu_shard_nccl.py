@@ -46,6 +46,13 @@ def _rank(rank, world, port, outdir):
         for _ in range(3):  # repeated steps reuse the buffers
             sh.decode_into(q, out, lse, si, ss)
         torch.cuda.synchronize()
+        out_e = out.clone()
+        sh.capture(q, out, lse, si, ss)  # the step as one CUDA graph, collectives included
+        out.zero_()
+        sh.replay()
+        torch.cuda.synchronize()
+        sh.release()
+        assert torch.equal(out, out_e)
         np.savez(os.path.join(outdir, f"r{rank}.npz"), out=out.float().cpu().numpy(), lse=lse.cpu().numpy(),
                  si=si.cpu().numpy(), ss=ss.cpu().numpy(), status=sh.status.cpu().numpy())
     finally:
