@@ -269,7 +269,7 @@ __global__ void __launch_bounds__(kDtThreads, 1)
           } else if (c < NCw + NCs) {
             kind = 1;
             t0 = 0;
-            t1 = 64;
+            t1 = geo.n_cap;  // past the cache: TMA fills the unused half with zeros, no traffic
           } else {
             kind = 2;
             const int q = (c - NCw - NCs) * 2;
