@@ -479,6 +479,7 @@ size_t hba_b200_prefill_workspace_size(const hba_b200_config* cfg, int32_t batch
   const size_t queries = (size_t)batch * cfg->n_kv * n;
   size_t b = kAlign;                                                      // device status word
   b += 2 * align_up((size_t)batch * n * cfg->n_kv * dh * 2);              // QKNorm'd keys and their RoPE'd copy
+  b += 2 * align_up((size_t)batch * n * cfg->n_heads * dh * 2);           // the same for the queries
   b += align_up((size_t)batch * cfg->n_kv * nb * cfg->slots * dh * 2);    // summaries
   b += align_up((size_t)batch * cfg->n_kv * ns * cfg->slots * dh * 2);    // supers
   b += selection_bytes(cfg, plan, queries);
@@ -509,6 +510,10 @@ int hba_b200_prefill(const hba_b200_config* cfg, int32_t batch, int32_t n, float
   ws += align_up((size_t)batch * n * cfg->n_kv * dh * 2);
   __nv_bfloat16* kr = reinterpret_cast<__nv_bfloat16*>(ws);
   ws += align_up((size_t)batch * n * cfg->n_kv * dh * 2);
+  __nv_bfloat16* qcn = reinterpret_cast<__nv_bfloat16*>(ws);  // queries QKNorm'd
+  ws += align_up((size_t)batch * n * cfg->n_heads * dh * 2);
+  __nv_bfloat16* qrn = reinterpret_cast<__nv_bfloat16*>(ws);  // and RoPE'd at their positions
+  ws += align_up((size_t)batch * n * cfg->n_heads * dh * 2);
   __nv_bfloat16* summ = reinterpret_cast<__nv_bfloat16*>(ws);
   ws += align_up((size_t)batch * cfg->n_kv * nb * cfg->slots * dh * 2);
   __nv_bfloat16* sup = reinterpret_cast<__nv_bfloat16*>(ws);
@@ -520,6 +525,11 @@ int hba_b200_prefill(const hba_b200_config* cfg, int32_t batch, int32_t n, float
   if (e != cudaSuccess) return cuda_status(e);
   e = hba::launch_qknorm_rope(geo, n, static_cast<const __nv_bfloat16*>(k), k_gain, cos, sin, kc, kr, dh,
                                           stream);
+  if (e == cudaSuccess) {  // the same pre-pass over the query heads (the gain per query head)
+    Geom gq = geo;
+    gq.Hkv = geo.Hq;
+    e = hba::launch_qknorm_rope(gq, n, static_cast<const __nv_bfloat16*>(q), q_gain, cos, sin, qcn, qrn, dh, stream);
+  }
   if (e != cudaSuccess) return cuda_status(e);
   prof_mark(stream);
   e = hba::launch_summarize(geo, dh, kc, probes, proj, summ, 0, (int)nb, nullptr, 0, stream);
@@ -543,7 +553,8 @@ int hba_b200_prefill(const hba_b200_config* cfg, int32_t batch, int32_t n, float
     hba::SelParams sp{};
     sp.geo = geo;
     sp.qp = qp;
-    sp.q = static_cast<const __nv_bfloat16*>(q);
+    sp.q = qcn;  // already QKNorm'd: the kernel skips its own norm (same arithmetic)
+    sp.q_normed = 1;
     sp.q_gain = q_gain;
     sp.summ = summ;
     sp.mode = hba::kSelFlat;
@@ -569,9 +580,9 @@ int hba_b200_prefill(const hba_b200_config* cfg, int32_t batch, int32_t n, float
   const bool want_tc = !(force != nullptr && strcmp(force, "gather") == 0);
   const bool v_aligned = (reinterpret_cast<uintptr_t>(v) & 15u) == 0;  // TMA needs 16-byte aligned bases
   if (want_tc && v_aligned && fin_lists == 1 && hba::prefill_tc_supported(geo, dh, n, cfg->qknorm != 0)) {
-    e = hba::launch_prefill_tc(geo, dh, n, scale, static_cast<const __nv_bfloat16*>(q), q_gain, k_gain, kc, kr,
-                               static_cast<const __nv_bfloat16*>(v), cos, sin, fin.idx, fin_lists * fin_k,
-                               static_cast<__nv_bfloat16*>(out), lse, dev_status, stream);
+    e = hba::launch_prefill_tc(geo, dh, n, scale, qcn, qrn, k_gain, kc, kr,
+                               static_cast<const __nv_bfloat16*>(v), fin.idx, fin_lists * fin_k,
+                               static_cast<__nv_bfloat16*>(out), lse, dev_status, g_trace, g_trace_ctas, stream);
     if (e != cudaSuccess) return cuda_status(e);
     prof_mark(stream);
     g_last_kernels = cfg->hier ? "qknorm_rope_kernel+summarize_kernel+supers_kernel+select_kernel+select_kernel+"

@@ -500,35 +500,6 @@ __global__ void __launch_bounds__(kDtThreads, 1)
         if (lane == 0) mbar_arrive(&sm.empty[i % NSLOT]);
       }
     };
-    // merges the 7 warp lists in a 3-round tree: best-first picks in
-    // sm.sel_i / sel_s, valid count returned
-    auto merge = [&](int k) -> int {
-      sm.wl_s[sw][lane] = ls;
-      sm.wl_i[sw][lane] = li;
-      score_bar();
-#pragma unroll
-      for (int step = 1; step < NSW; step <<= 1) {
-        if (sw % (2 * step) == 0 && sw + step < NSW) {
-          float a = sm.wl_s[sw][lane];
-          int ai = sm.wl_i[sw][lane];
-          warp_merge32(a, ai, sm.wl_s[sw + step][lane], sm.wl_i[sw + step][lane]);
-          __syncwarp();
-          sm.wl_s[sw][lane] = a;
-          sm.wl_i[sw][lane] = ai;
-        }
-        score_bar();
-      }
-      if (warp == 0) {
-        const float fs = sm.wl_s[0][lane];
-        const int fi = sm.wl_i[0][lane];
-        const int n = __popc(__ballot_sync(0xffffffffu, lane < k && fi != INT_MAX));
-        sm.sel_i[lane] = fi;
-        sm.sel_s[lane] = fs;
-        if (lane == 0) sm.nsel = n;
-      }
-      score_bar();
-      return sm.nsel;
-    };
     int nsel = 0, NPb = 0;
     if (shard) {
       // global top-k of every shard's lists, then the owned picks (local block ids)

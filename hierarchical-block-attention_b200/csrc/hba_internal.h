@@ -52,6 +52,7 @@ struct SelParams {
   // own_blo + r (super own_blo/F + r).  One GPU: 0, INT_MAX.
   int32_t own_blo, own_bhi;
   int32_t n_limit;  // longest valid context (one GPU: n_cap; a shard: the global capacity)
+  int32_t q_normed;  // q is already QKNorm'd (select_tile_kernel only)
 };
 
 struct AttnParams {
@@ -153,11 +154,12 @@ cudaError_t launch_decode_tc(const DecodeAttnParams& p, const __nv_bfloat16* sum
                              const float* k_gain, int* err, int dh, cudaStream_t st);
 // tcgen05/TMEM prefill union softmax (hba_prefill_tc.cu).
 bool prefill_tc_supported(const Geom& geo, int dh, int n, bool qknorm);
-cudaError_t launch_prefill_tc(const Geom& geo, int dh, int n, float scale, const __nv_bfloat16* q,
-                              const float* q_gain, const float* k_gain, const __nv_bfloat16* kc,
-                              const __nv_bfloat16* kr, const __nv_bfloat16* v, const float* cos, const float* sin,
+// qc / qr: the queries QKNorm'd and RoPE'd by the pre-pass, [B, n, Hq, dh] bf16.
+cudaError_t launch_prefill_tc(const Geom& geo, int dh, int n, float scale, const __nv_bfloat16* qc,
+                              const __nv_bfloat16* qr, const float* k_gain, const __nv_bfloat16* kc,
+                              const __nv_bfloat16* kr, const __nv_bfloat16* v,
                               const int32_t* sel, int list_stride, __nv_bfloat16* out, float* lse, int* err,
-                              cudaStream_t st);
+                              unsigned long long* trace, long long trace_rows, cudaStream_t st);
 // CTAs the decode attention grid should have for this device (all resident at once).
 int decode_attend_grid(int dh, int total_chunks);
 

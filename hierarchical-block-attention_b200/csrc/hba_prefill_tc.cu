@@ -36,7 +36,7 @@ namespace hba {
 using namespace sm100;
 
 constexpr int kTcThreads = 192;
-constexpr int kTcStages = 3;
+constexpr int kTcSlots = 6;  // ring of K or V tiles: K(c) = item 2c, V(c) = item 2c + 1
 constexpr int kTcKeys = 64;            // keys per chunk
 constexpr int kTcMaxBlocks = 2048;     // routed block union capacity (nb <= 2048)
 constexpr int kTcMaxChunks = 1 + 20 + kTcMaxBlocks;
@@ -50,12 +50,11 @@ struct TcSmem {
   static constexpr int KBYTES = HALVES * 64 * 128;      // [64 keys x DH]
   alignas(1024) unsigned char qc[QBYTES];
   alignas(1024) unsigned char qr[QBYTES];
-  alignas(1024) unsigned char k[kTcStages][KBYTES];
-  alignas(1024) unsigned char v[kTcStages][KBYTES];
+  alignas(1024) unsigned char ring[kTcSlots][KBYTES];  // a K tile is free once its S MMA is done
   alignas(1024) unsigned char p[2][128 * 128];          // [128 rows x 64 keys] bf16, swizzled
   uint2 chunks[kTcMaxChunks];                           // (key base | type << 28, query mask)
   uint64_t q_ready, o_full;
-  uint64_t kv_full[kTcStages], kv_empty[kTcStages];
+  uint64_t full[kTcSlots], empty[kTcSlots];
   uint64_t s_full[2], p_full[2], p_free[2];
   uint64_t drain;
   uint32_t tmem_base;
@@ -69,22 +68,21 @@ struct PrefillTcParams {
   float scale;
   int QT;              // queries per tile
   int tiles;           // tiles per (sequence, kv head)
-  const __nv_bfloat16* q;   // [B, n, Hq, dh] raw
-  const float* q_gain;
   const float* k_gain;
-  const float* cos;
-  const float* sin;
   const int32_t* sel;       // [B*Hkv, n, list_stride] final picks (-1 = none)
   int list_stride;
   __nv_bfloat16* out;       // [B, n, Hq, dh]
   float* lse;               // [B, Hq, n] or null
   int* err;
+  unsigned long long* trace;  // debug: 16 global-timer stamps for the last tile of (sequence, kv head) < trace_rows
+  long long trace_rows;
 };
 
 template <int DH>
 __global__ void __launch_bounds__(kTcThreads, 1)
     prefill_tc_kernel(const __grid_constant__ CUtensorMap tm_kc, const __grid_constant__ CUtensorMap tm_kr,
-                      const __grid_constant__ CUtensorMap tm_v, PrefillTcParams p) {
+                      const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_qc,
+                      const __grid_constant__ CUtensorMap tm_qr, PrefillTcParams p) {
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   // dynamic shared memory is only 16-byte aligned by default: align by hand
   unsigned char* base_ptr =
@@ -99,6 +97,12 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   const int i0 = tile * QT;
   const int nq = min(QT, n - i0);
   const int nb = n / geo.Bk;
+  unsigned long long* trace =
+      (p.trace != nullptr && tile == p.tiles - 1 && bg < p.trace_rows) ? p.trace + (size_t)bg * 16 : nullptr;
+  auto stamp = [&](int s) {
+    if (trace != nullptr) trace[s] = global_ns();
+  };
+  if (tid == 0) stamp(0);
 
   // ---- chunk list: sinks, window, routed union (all threads) ----
   uint32_t* mask = reinterpret_cast<uint32_t*>(sm.p[0]);  // [nb] query bitmasks, overlays P before use
@@ -122,19 +126,19 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     const int lo = tid * per, hi = min(nb, lo + per);
     int cnt = 0;
     for (int i = lo; i < hi; ++i) cnt += mask[i] != 0u;
-    sm.scan[tid] = cnt;
-    __syncthreads();
-    if (tid == 0) {
-      int acc = 0;
-      for (int t = 0; t < kTcThreads; ++t) {
-        const int c = sm.scan[t];
-        sm.scan[t] = acc;
-        acc += c;
-      }
-      sm.n_chunks = nsc + nwc + acc;
+    // exclusive prefix of the per-thread counts: within each warp, then over the warp totals
+    int incl = cnt;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int nv = __shfl_up_sync(0xffffffffu, incl, o);
+      if (lane >= o) incl += nv;
     }
+    if (lane == 31) sm.scan[warp] = incl;
     __syncthreads();
-    int o = nsc + nwc + sm.scan[tid];
+    int wbase = 0;
+    for (int w = 0; w < warp; ++w) wbase += sm.scan[w];
+    if (tid == kTcThreads - 1) sm.n_chunks = nsc + nwc + wbase + incl;
+    int o = nsc + nwc + wbase + incl - cnt;
     for (int i = lo; i < hi; ++i)
       if (mask[i] != 0u) sm.chunks[o++] = make_uint2((uint32_t)(i * geo.Bk) | (kRouted << 28), mask[i]);
     if (tid == 0 && nsc) sm.chunks[0] = make_uint2(0u | (kSink << 28), 0u);
@@ -142,11 +146,11 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       sm.chunks[nsc + c] = make_uint2((uint32_t)(jlo + c * kTcKeys) | (kWindow << 28), 0u);
   }
   if (tid == 0) {
-    mbar_init(&sm.q_ready, 128);
+    mbar_init(&sm.q_ready, 1);  // the query tile's TMA
     mbar_init(&sm.o_full, 1);
-    for (int s = 0; s < kTcStages; ++s) {
-      mbar_init(&sm.kv_full[s], 1);
-      mbar_init(&sm.kv_empty[s], 1);
+    for (int s = 0; s < kTcSlots; ++s) {
+      mbar_init(&sm.full[s], 1);
+      mbar_init(&sm.empty[s], 1);
     }
     for (int s = 0; s < 2; ++s) {
       mbar_init(&sm.s_full[s], 1);
@@ -165,6 +169,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   tc_fence_after();
   const uint32_t tmem = sm.tmem_base;
   const int NCH = sm.n_chunks;
+  if (tid == 0) stamp(1);
   const uint32_t t_s0 = tmem, t_o = tmem + 128;
 
   if (warp == 5) {
@@ -173,18 +178,22 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       prefetch_tmap(&tm_kc);
       prefetch_tmap(&tm_kr);
       prefetch_tmap(&tm_v);
-      for (int c = 0; c < NCH; ++c) {
-        const int st = c % kTcStages, u = c / kTcStages;
-        if (c >= kTcStages && !mbar_wait(&sm.kv_empty[st], (u - 1) & 1, p.err)) break;
-        const uint2 e = sm.chunks[c];
+      // the query tile: rows r = query * G + head, QKNorm'd (qc) and RoPE'd (qr) by the pre-pass
+      // a box is G heads x QT queries (G * QT <= 128 rows: 126 when G = 7) of 128 bytes, per half
+      mbar_arrive_expect_tx(&sm.q_ready, (uint32_t)(2 * HALVES * G * QT * 128));
+      for (int h = 0; h < HALVES; ++h) {
+        tma_load_4d(sm.qc + h * 16384, &tm_qc, h * 64, g * G, i0, b, &sm.q_ready);
+        tma_load_4d(sm.qr + h * 16384, &tm_qr, h * 64, g * G, i0, b, &sm.q_ready);
+      }
+      for (int it = 0; it < 2 * NCH; ++it) {
+        const int st = it % kTcSlots, u = it / kTcSlots;
+        if (it >= kTcSlots && !mbar_wait(&sm.empty[st], (u - 1) & 1, p.err)) break;
+        const uint2 e = sm.chunks[it >> 1];
         const int kb = (int)(e.x & 0x0FFFFFFFu);
         const uint32_t type = e.x >> 28;
-        mbar_arrive_expect_tx(&sm.kv_full[st], 2 * TcSmem<DH>::KBYTES);
-        const CUtensorMap* km = type == kWindow ? &tm_kr : &tm_kc;
-        for (int h = 0; h < HALVES; ++h) {
-          tma_load_4d(sm.k[st] + h * 8192, km, h * 64, g, kb, b, &sm.kv_full[st]);
-          tma_load_4d(sm.v[st] + h * 8192, &tm_v, h * 64, g, kb, b, &sm.kv_full[st]);
-        }
+        mbar_arrive_expect_tx(&sm.full[st], TcSmem<DH>::KBYTES);
+        const CUtensorMap* m = (it & 1) ? &tm_v : (type == kWindow ? &tm_kr : &tm_kc);
+        for (int h = 0; h < HALVES; ++h) tma_load_4d(sm.ring[st] + h * 8192, m, h * 64, g, kb, b, &sm.full[st]);
       }
     }
   } else if (warp == 4) {
@@ -195,27 +204,29 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       bool ok = mbar_wait(&sm.q_ready, 0, p.err);
       tc_fence_after();
       auto pv = [&](int c) -> bool {
-        const int sb = c & 1, st = c % kTcStages;
+        const int sb = c & 1, iv = 2 * c + 1, st = iv % kTcSlots;
         if (!mbar_wait(&sm.p_full[sb], (c >> 1) & 1, p.err)) return false;
+        if (!mbar_wait(&sm.full[st], (iv / kTcSlots) & 1, p.err)) return false;
         tc_fence_after();
-        const uint32_t pa = smem_u32(sm.p[sb]), va = smem_u32(sm.v[st]);
+        const uint32_t pa = smem_u32(sm.p[sb]), va = smem_u32(sm.ring[st]);
 #pragma unroll
         for (int kk = 0; kk < kTcKeys / 16; ++kk)
           umma_f16(t_o, sdesc_sw128(pa + kk * 32, 16, 1024), sdesc_sw128(va + kk * 2048, 8192, 1024), idesc_o,
                    (c > 0 || kk > 0) ? 1u : 0u);
-        umma_commit(&sm.kv_empty[st]);
+        umma_commit(&sm.empty[st]);
         umma_commit(&sm.p_free[sb]);
         return true;
       };
       for (int c = 0; ok && c < NCH; ++c) {
-        const int st = c % kTcStages, sb = c & 1;
-        if (!mbar_wait(&sm.kv_full[st], (c / kTcStages) & 1, p.err)) {
+        const int sb = c & 1, ik = 2 * c, st = ik % kTcSlots;
+        if (!mbar_wait(&sm.full[st], (ik / kTcSlots) & 1, p.err)) {
           ok = false;
           break;
         }
         tc_fence_after();
         const uint32_t type = sm.chunks[c].x >> 28;
-        const uint32_t qa = smem_u32(type == kWindow ? sm.qr : sm.qc), ka = smem_u32(sm.k[st]);
+        const uint32_t qa = smem_u32(type == kWindow ? sm.qr : sm.qc), ka = smem_u32(sm.ring[st]);
+        if (c == 4) stamp(13);
 #pragma unroll
         for (int kk = 0; kk < DH / 16; ++kk) {
           const int h = kk >> 2, ko = (kk & 3) * 32;
@@ -223,6 +234,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                    sdesc_sw128(ka + h * 8192 + ko, 16, 1024), idesc_s, kk > 0 ? 1u : 0u);
         }
         umma_commit(&sm.s_full[sb]);
+        umma_commit(&sm.empty[st]);  // the K tile is free once S is done
         if (c >= 1 && !pv(c - 1)) {
           ok = false;
           break;
@@ -241,58 +253,23 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     const int i = i0 + qt;
     const bool row_ok = (r < QT * G) && (qt < nq);
     const int hq = g * G + hh;
+    // the query tile arrives by TMA; this row's logit bound from its QKNorm'd values
     float M2 = 0.f;
-    {
-      float x[DH];
-      float ss = 0.f;
-      if (row_ok) {
-        const uint4* src = reinterpret_cast<const uint4*>(p.q + (((size_t)b * n + i) * geo.Hq + hq) * DH);
+    if (!mbar_wait(&sm.q_ready, 0, p.err)) M2 = 0.f;
+    if (row_ok) {
+      float qn2 = 0.f;
 #pragma unroll
-        for (int c8 = 0; c8 < DH / 8; ++c8) unpack8(src[c8], x + c8 * 8);
+      for (int d8 = 0; d8 < DH / 8; ++d8) {
+        float f[8];
+        unpack8(*reinterpret_cast<const uint4*>(sm.qc + (d8 / 8) * 16384 + sw128_offset(r, (d8 % 8) * 8)), f);
 #pragma unroll
-        for (int d = 0; d < DH; ++d) ss = fmaf(x[d], x[d], ss);
-        const float rms = sqrtf(fmaxf(ss / (float)DH, geo.eps));
-        const float gq = p.q_gain[hq];
-        float qn2 = 0.f;
-#pragma unroll
-        for (int d = 0; d < DH; ++d) {
-          x[d] = round_bf16((x[d] / rms) * gq);
-          qn2 = fmaf(x[d], x[d], qn2);
-        }
-        const float kmax = sqrtf((float)DH) * p.k_gain[g] * (1.f + 1.f / 64.f);
-        M2 = p.scale * sqrtf(qn2) * kmax * kLog2e;
-        if (M2 > 120.f) atomicExch(p.err, 2);  // logit bound too large for the fixed-max softmax
-      } else {
-#pragma unroll
-        for (int d = 0; d < DH; ++d) x[d] = 0.f;
+        for (int e = 0; e < 8; ++e) qn2 = fmaf(f[e], f[e], qn2);
       }
-      const float* cr = p.cos + (size_t)(row_ok ? i : 0) * DH;
-      const float* sr = p.sin + (size_t)(row_ok ? i : 0) * DH;
-#pragma unroll
-      for (int c8 = 0; c8 < DH / 8; ++c8) {
-        uint32_t wc[4], wr[4];
-#pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          const int d0 = c8 * 8 + 2 * e;
-          float rr[2];
-#pragma unroll
-          for (int t = 0; t < 2; ++t) {
-            const int d = d0 + t;
-            const float rot = d < DH / 2 ? -x[d + DH / 2] : x[d - DH / 2];
-            rr[t] = row_ok ? x[d] * cr[d] + rot * sr[d] : 0.f;
-          }
-          wc[e] = pack_bf16x2(x[d0], x[d0 + 1]);
-          wr[e] = pack_bf16x2(rr[0], rr[1]);
-        }
-        const int h = c8 >> 3, col = (c8 & 7) * 8;
-        const uint32_t off = h * 16384 + sw128_offset(r, col);
-        *reinterpret_cast<uint4*>(sm.qc + off) = make_uint4(wc[0], wc[1], wc[2], wc[3]);
-        *reinterpret_cast<uint4*>(sm.qr + off) = make_uint4(wr[0], wr[1], wr[2], wr[3]);
-      }
+      const float kmax = sqrtf((float)DH) * p.k_gain[g] * (1.f + 1.f / 64.f);
+      M2 = p.scale * sqrtf(qn2) * kmax * kLog2e;
+      if (M2 > 120.f) atomicExch(p.err, 2);  // logit bound too large for the fixed-max softmax
     }
-    fence_proxy_async_smem();
-    mbar_arrive(&sm.q_ready);
-
+    if (r == 0) stamp(2);
     const float sl2 = p.scale * kLog2e;
     const int win_lo = max(geo.S, i - geo.W + 1);
     const uint32_t lane_off = (uint32_t)(warp * 32) << 16;
@@ -304,15 +281,19 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         ok = false;
         break;
       }
+      const int ts0 = (c == 4) ? 3 : ((c == NCH - 8) ? 8 : -1);  // debug trace slots of two chunks
+      if (r == 0 && ts0 >= 0) stamp(ts0);
       tc_fence_after();
       float s[kTcKeys];
       tmem_ld32(t_s0 + sb * kTcKeys + lane_off, s);
       tmem_ld32(t_s0 + sb * kTcKeys + 32 + lane_off, s + 32);
       tmem_ld_wait();
+      if (r == 0 && ts0 >= 0) stamp(ts0 + 1);
       if (c >= 2 && !mbar_wait(&sm.p_free[sb], ((c - 2) >> 1) & 1, p.err)) {
         ok = false;
         break;
       }
+      if (r == 0 && ts0 >= 0) stamp(ts0 + 2);
       const uint2 e = sm.chunks[c];
       const int kb = (int)(e.x & 0x0FFFFFFFu);
       const uint32_t type = e.x >> 28;
@@ -353,10 +334,13 @@ __global__ void __launch_bounds__(kTcThreads, 1)
           *reinterpret_cast<uint4*>(prow + sw128_offset(r, c8 * 8)) = make_uint4(w[0], w[1], w[2], w[3]);
         }
       }
+      if (r == 0 && ts0 >= 0) stamp(ts0 + 3);
       fence_proxy_async_smem();
       tc_fence_before();
       mbar_arrive(&sm.p_full[sb]);
+      if (r == 0 && ts0 >= 0) stamp(ts0 + 4);
     }
+    if (r == 0) stamp(14);
     if (ok && mbar_wait(&sm.o_full, 0, p.err)) {
       tc_fence_after();
       const float inv = l > 0.f ? 1.f / l : 0.f;
@@ -384,6 +368,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   __syncthreads();
   tc_fence_after();
   if (warp == 4) tmem_dealloc(tmem, 256);
+  if (tid == 0) stamp(15);
 }
 
 // ---------------------------------------------------------------- host ----
@@ -400,15 +385,19 @@ static PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
 }
 
 // [B, n, H, dh] bf16 as a 4-D map {dh, H, n, B}, box {64, 1, 64, 1}, 128-byte swizzle.
-static bool make_map(CUtensorMap* m, const void* base, int B, int n, int H, int dh) {
+// [B, n, H, dh] bf16 tensor; a box is 64 elements of dh x box_h heads x box_n tokens
+static bool make_map(CUtensorMap* m, const void* base, int B, int n, int H, int dh, int box_h = 1, int box_n = 64) {
   auto fn = encode_fn();
   if (fn == nullptr) return false;
   cuuint64_t dims[4] = {(cuuint64_t)dh, (cuuint64_t)H, (cuuint64_t)n, (cuuint64_t)B};
   cuuint64_t strides[3] = {(cuuint64_t)dh * 2, (cuuint64_t)H * dh * 2, (cuuint64_t)n * H * dh * 2};
-  cuuint32_t box[4] = {64, 1, 64, 1};
+  cuuint32_t box[4] = {64, (cuuint32_t)box_h, (cuuint32_t)box_n, 1};
   cuuint32_t es[4] = {1, 1, 1, 1};
+  // L2 fills no wider than a head's slice of a token row (dh * 2 bytes)
+  const CUtensorMapL2promotion promo = dh * 2 >= 256 ? CU_TENSOR_MAP_L2_PROMOTION_L2_256B
+                                                     : CU_TENSOR_MAP_L2_PROMOTION_L2_128B;
   return fn(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, const_cast<void*>(base), dims, strides, box, es,
-            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, promo,
             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
@@ -418,14 +407,16 @@ bool prefill_tc_supported(const Geom& geo, int dh, int n, bool qknorm) {
          n / geo.Bk <= kTcMaxBlocks && geo.W <= 1024 && encode_fn() != nullptr;
 }
 
-cudaError_t launch_prefill_tc(const Geom& geo, int dh, int n, float scale, const __nv_bfloat16* q,
-                              const float* q_gain, const float* k_gain, const __nv_bfloat16* kc,
-                              const __nv_bfloat16* kr, const __nv_bfloat16* v, const float* cos, const float* sin,
+cudaError_t launch_prefill_tc(const Geom& geo, int dh, int n, float scale, const __nv_bfloat16* qc,
+                              const __nv_bfloat16* qr, const float* k_gain, const __nv_bfloat16* kc,
+                              const __nv_bfloat16* kr, const __nv_bfloat16* v,
                               const int32_t* sel, int list_stride, __nv_bfloat16* out, float* lse, int* err,
-                              cudaStream_t st) {
-  CUtensorMap m_kc, m_kr, m_v;
+                              unsigned long long* trace, long long trace_rows, cudaStream_t st) {
+  CUtensorMap m_kc, m_kr, m_v, m_qc, m_qr;
+  const int QT = 128 / geo.G;
   if (!make_map(&m_kc, kc, geo.B, n, geo.Hkv, dh) || !make_map(&m_kr, kr, geo.B, n, geo.Hkv, dh) ||
-      !make_map(&m_v, v, geo.B, n, geo.Hkv, dh))
+      !make_map(&m_v, v, geo.B, n, geo.Hkv, dh) || !make_map(&m_qc, qc, geo.B, n, geo.Hq, dh, geo.G, QT) ||
+      !make_map(&m_qr, qr, geo.B, n, geo.Hq, dh, geo.G, QT))
     return cudaErrorInvalidValue;
   PrefillTcParams p{};
   p.geo = geo;
@@ -433,29 +424,27 @@ cudaError_t launch_prefill_tc(const Geom& geo, int dh, int n, float scale, const
   p.scale = scale;
   p.QT = 128 / geo.G;
   p.tiles = (n + p.QT - 1) / p.QT;
-  p.q = q;
-  p.q_gain = q_gain;
   p.k_gain = k_gain;
-  p.cos = cos;
-  p.sin = sin;
   p.sel = sel;
   p.list_stride = list_stride;
   p.out = out;
   p.lse = lse;
   p.err = err;
+  p.trace = trace;
+  p.trace_rows = trace_rows;
   const long long grid = (long long)geo.B * geo.Hkv * p.tiles;
   if (dh == 64) {
     const size_t smem = sizeof(TcSmem<64>) + 1024;
     static const cudaError_t attr = cudaFuncSetAttribute(prefill_tc_kernel<64>,
                                                          cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (attr != cudaSuccess) return attr;
-    prefill_tc_kernel<64><<<(unsigned)grid, kTcThreads, smem, st>>>(m_kc, m_kr, m_v, p);
+    prefill_tc_kernel<64><<<(unsigned)grid, kTcThreads, smem, st>>>(m_kc, m_kr, m_v, m_qc, m_qr, p);
   } else {
     const size_t smem = sizeof(TcSmem<128>) + 1024;
     static const cudaError_t attr = cudaFuncSetAttribute(prefill_tc_kernel<128>,
                                                          cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (attr != cudaSuccess) return attr;
-    prefill_tc_kernel<128><<<(unsigned)grid, kTcThreads, smem, st>>>(m_kc, m_kr, m_v, p);
+    prefill_tc_kernel<128><<<(unsigned)grid, kTcThreads, smem, st>>>(m_kc, m_kr, m_v, m_qc, m_qr, p);
   }
   return cudaGetLastError();
 }

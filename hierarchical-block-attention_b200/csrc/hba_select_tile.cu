@@ -99,7 +99,7 @@ __global__ void __launch_bounds__(kTsThreads, 1) select_tile_kernel(SelParams p,
         const int hq = g * geo.G + h;
         float v[PER];
         load_head_row<DH>(p.q + (((size_t)b * nq + i) * geo.Hq + hq) * DH, v);
-        if (geo.qknorm) qknorm_lane<DH>(v, p.q_gain[hq], geo.eps);
+        if (geo.qknorm && !p.q_normed) qknorm_lane<DH>(v, p.q_gain[hq], geo.eps);
 #pragma unroll
         for (int e = 0; e < PER; ++e) acc[e] += v[e];
       }

@@ -213,8 +213,12 @@ int hba_b200_profile_events_recorded(void);
  * buffer, later tcgen05 decode kernels write 16 uint64 global-timer stamps
  * per CTA to buffer[blockIdx * 16 + i], for CTAs with blockIdx * 128 < bytes:
  * 0 kernel start, 1 after the query prologue, 2 after selection, 3 after the
- * union softmax, 4 end, 5-7 selection sub-phases, 8-15 softmax of K/V
- * chunks 0, 2, ..., 14 done.  NULL turns it off.
+ * union softmax, 4 end, 5-7 selection sub-phases, 8-15 spare (0).  The
+ * prefill union kernel writes 16 stamps for the last query tile of each
+ * (sequence, kv head) row r < bytes / 128 at buffer[r * 16 + i]: 0 start,
+ * 1 chunk list built, 2 query tile ready, 3-7 and 8-12 the softmax of two
+ * chunks (S ready, S read, P buffer free, P written, P handed over), 13 the
+ * MMA issue of chunk 4's S, 14 softmax done, 15 end.  NULL turns it off.
  */
 int hba_b200_set_debug_trace(void* device_buffer, int64_t bytes);
 
