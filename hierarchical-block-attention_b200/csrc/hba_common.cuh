@@ -32,6 +32,17 @@ HBA_DEVICE void unpack8(uint4 u, float* f) {
   f[7] = __uint_as_float(u.w & 0xffff0000u);
 }
 
+// Two independent IEEE fp32 fmas in one instruction (sm_100 fma.rn.f32x2):
+// (x, y) = (a0 * b0 + x, a1 * b1 + y), each rounded exactly as fmaf.
+HBA_DEVICE void fma2(float& x, float& y, float a0, float a1, float b0, float b1) {
+  unsigned long long a, b, c, d;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(a) : "f"(a0), "f"(a1));
+  asm("mov.b64 %0, {%1, %2};" : "=l"(b) : "f"(b0), "f"(b1));
+  asm("mov.b64 %0, {%1, %2};" : "=l"(c) : "f"(x), "f"(y));
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(x), "=f"(y) : "l"(d));
+}
+
 HBA_DEVICE uint32_t pack_bf16x2(float lo, float hi) {
   __nv_bfloat162 h = __floats2bfloat162_rn(lo, hi);
   return *reinterpret_cast<uint32_t*>(&h);

@@ -82,6 +82,7 @@ struct DtcSmem {
   uint64_t s_full[2], p_full[2], p_free[2];
   uint64_t o_full, drain, child_ready, sel_ready, lists_ready;
   uint32_t tmem_base;
+  int issued;  // ring items the producer has issued (published after each)
 };
 
 static_assert(sizeof(DtcSmem<64>) + 1024 <= 232448 && sizeof(DtcSmem<128>) + 1024 <= 232448,
@@ -134,6 +135,9 @@ __global__ void __launch_bounds__(kDtThreads, 1)
   unsigned long long* trace = (p.trace != nullptr && bg < p.trace_ctas) ? p.trace + (size_t)bg * 16 : nullptr;
   auto stamp = [&](int i) {
     if (trace != nullptr && tid == 0) trace[i] = global_ns();
+  };
+  auto stamp_any = [&](int i) {  // from the calling thread
+    if (trace != nullptr) trace[i] = global_ns();
   };
   stamp(0);
 
@@ -222,6 +226,7 @@ __global__ void __launch_bounds__(kDtThreads, 1)
     mbar_init(&sm.child_ready, 1);
     mbar_init(&sm.sel_ready, 1);
     mbar_init(&sm.lists_ready, kDtScoreWarps);
+    sm.issued = 0;
     fence_barrier_init();
   }
   if (warp == 1) {
@@ -232,6 +237,24 @@ __global__ void __launch_bounds__(kDtThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = sm.tmem_base;  // cols [0,16) S0, [16,32) S1, [32,48) O^T
+  // A consumer of ring item i first sees it issued, then tests full[i % NSLOT]
+  // by parity: a parity test is only unambiguous once the slot's previous
+  // item has landed, which the producer's empty wait before issuing item i
+  // guarantees (that item was consumed).
+  auto issued_past = [&](int i) { return *reinterpret_cast<volatile int*>(&sm.issued) > i; };
+  auto wait_full = [&](int i) -> bool {
+    if (!issued_past(i)) {
+      const unsigned long long t0 = global_ns();
+      for (uint32_t k = 1; !issued_past(i); ++k) {
+        __nanosleep(32);
+        if ((k & 63) == 0 && global_ns() - t0 > kWaitNs) {
+          atomicExch(P.err, 1);
+          return false;
+        }
+      }
+    }
+    return mbar_wait(&sm.full[i % NSLOT], (i / NSLOT) & 1, P.err);
+  };
 
   if (producer) {
     // ---- ring producer: the items in the order described at item_of_chunk ----
@@ -291,6 +314,8 @@ __global__ void __launch_bounds__(kDtThreads, 1)
               !mbar_wait(&sm.empty[issued % NSLOT], ((issued / NSLOT) - 1) & 1, P.err))
             return false;
           issue_item(issued);
+          __threadfence_block();
+          *reinterpret_cast<volatile int*>(&sm.issued) = issued + 1;
         }
         return true;
       };
@@ -302,6 +327,7 @@ __global__ void __launch_bounds__(kDtThreads, 1)
         okp = okp && pump_to(NPa + NPb + 2 * NCk);
       }
       if (okp && mbar_wait(&sm.sel_ready, 0, P.err)) {
+        stamp_any(12);
         nsel = sm.nsel;
         pump_to(NPa + NPb + 2 * (NCk + (nsel * geo.Bk + kDtKeys - 1) / kDtKeys));
       }
@@ -397,7 +423,7 @@ __global__ void __launch_bounds__(kDtThreads, 1)
     auto score_pages = [&](int i0, int np, int R, int k, auto id_of) {
       for (int pg = pg_first; pg < np; pg += pg_stride) {
         const int i = i0 + pg;
-        mbar_wait(&sm.full[i % NSLOT], (i / NSLOT) & 1, P.err);
+        wait_full(i);
         const unsigned char* src = sm.ring[i % NSLOT];
         const int nr = min(PB, R - pg * PB);
         for (int rg = 0; rg < nr; rg += 32) {
@@ -661,7 +687,7 @@ __global__ void __launch_bounds__(kDtThreads, 1)
         auto pv = [&](int c) -> bool {
           const int sb = c & 1, iv = item_of_chunk(c, npb) + 1;
           if (!mbar_wait(&sm.p_full[sb], (c >> 1) & 1, P.err)) return false;
-          if (!mbar_wait(&sm.full[iv % NSLOT], (iv / NSLOT) & 1, P.err)) return false;
+          if (!wait_full(iv)) return false;
           tc_fence_after();
           const uint32_t va = smem_u32(sm.ring[iv % NSLOT]);
           const uint32_t pa = smem_u32(sm.pt[sb][0]);
@@ -692,10 +718,13 @@ __global__ void __launch_bounds__(kDtThreads, 1)
             npb = (sm.n_children + PB - 1) / PB;
           }
           const int sb = c & 1, ik = item_of_chunk(c, npb);
-          if (!mbar_wait(&sm.full[ik % NSLOT], (ik / NSLOT) & 1, P.err)) {
+          if (!wait_full(ik)) {
             okw = false;
             break;
           }
+          if (c == 0) stamp_any(8);
+          if (c == NCk - 1) stamp_any(9);
+          if (c == NCk) stamp_any(10);
           tc_fence_after();
           const bool window = c < NCw;
           const uint32_t ka = smem_u32(sm.ring[ik % NSLOT]);
@@ -714,6 +743,7 @@ __global__ void __launch_bounds__(kDtThreads, 1)
           }
         }
         if (okw && NC >= 1) okw = pv(NC - 1);
+        stamp_any(11);
         umma_commit(&sm.o_full);
         umma_commit(&sm.drain);
         mbar_wait(&sm.drain, 0, P.err);

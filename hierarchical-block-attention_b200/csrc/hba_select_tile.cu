@@ -150,13 +150,12 @@ __global__ void __launch_bounds__(kTsThreads, 1) select_tile_kernel(SelParams p,
           const int r = 4 * qgrp + i;
           const float4 qa = sm.qg[r][(2 * v) ^ qsw], qb = sm.qg[r][(2 * v + 1) ^ qsw];
           const float qf[8] = {qa.x, qa.y, qa.z, qa.w, qb.x, qb.y, qb.z, qb.w};
+          // the two blocks' chains side by side: each half is the fmaf chain
+          float p0 = 0.f, p1 = 0.f;
 #pragma unroll
-          for (int j = 0; j < 2; ++j) {
-            float part = 0.f;
-#pragma unroll
-            for (int e = 0; e < 8; ++e) part = fmaf(sf[j][e], qf[e], part);
-            pv[i][j] = part;
-          }
+          for (int e = 0; e < 8; ++e) fma2(p0, p1, sf[0][e], sf[1][e], qf[e], qf[e]);
+          pv[i][0] = p0;
+          pv[i][1] = p1;
         }
         // pairwise tree over the slot's vectors, built as they arrive
 #pragma unroll

@@ -41,6 +41,19 @@ HBA_DEVICE bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
       : "memory");
   return ok != 0;
 }
+// try_wait that may suspend the thread until the phase completes or hint_ns
+// elapse: a waiting warp sleeps instead of spinning (a spin of mbarrier
+// probes keeps the shared-memory pipe busy, which slows the shuffles and
+// shared loads of the warps doing the work).
+HBA_DEVICE bool mbar_try_wait_sleep(uint64_t* bar, uint32_t parity, uint32_t hint_ns) {
+  uint32_t ok;
+  asm volatile(
+      "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n selp.u32 %0, 1, 0, p;\n}\n"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity), "r"(hint_ns)
+      : "memory");
+  return ok != 0;
+}
 // Non-blocking test (try_wait may suspend the thread for a while).
 HBA_DEVICE bool mbar_test_wait(uint64_t* bar, uint32_t parity) {
   uint32_t ok;
@@ -53,11 +66,11 @@ HBA_DEVICE bool mbar_test_wait(uint64_t* bar, uint32_t parity) {
 }
 // Bounded wait for the phase with the given parity; false (and *err set) on timeout.
 HBA_DEVICE bool mbar_wait(uint64_t* bar, uint32_t parity, int* err) {
-  if (mbar_try_wait(bar, parity)) return true;
+  if (mbar_test_wait(bar, parity)) return true;
   const unsigned long long t0 = global_ns();
-  for (uint32_t i = 1;; ++i) {
-    if (mbar_try_wait(bar, parity)) return true;
-    if ((i & 63) == 0 && global_ns() - t0 > kWaitNs) break;
+  for (;;) {
+    if (mbar_try_wait_sleep(bar, parity, 20000u)) return true;
+    if (global_ns() - t0 > kWaitNs) break;
   }
   if (err != nullptr) atomicExch(err, 1);
   return false;

@@ -213,7 +213,10 @@ int hba_b200_profile_events_recorded(void);
  * buffer, later tcgen05 decode kernels write 16 uint64 global-timer stamps
  * per CTA to buffer[blockIdx * 16 + i], for CTAs with blockIdx * 128 < bytes:
  * 0 kernel start, 1 after the query prologue, 2 after selection, 3 after the
- * union softmax, 4 end, 5-7 selection sub-phases, 8-15 spare (0).  The
+ * union softmax, 4 end, 5-7 selection sub-phases, 8 / 9 / 10 the MMA warp
+ * sees the first window tile / the last window-or-sink tile / the first
+ * routed tile land, 11 last PV issued, 12 the producer sees the picks,
+ * 13-15 spare (0).  The
  * prefill union kernel writes 16 stamps for the last query tile of each
  * (sequence, kv head) row r < bytes / 128 at buffer[r * 16 + i]: 0 start,
  * 1 chunk list built, 2 query tile ready, 3-7 and 8-12 the softmax of two
