@@ -721,4 +721,79 @@ int hba_b200_decode_shard_finish(const hba_b200_config* cfg, int32_t batch, cons
                                               static_cast<__nv_bfloat16*>(out), lse, stream));
 }
 
+int64_t hba_b200_shard_xbuf_bytes(const hba_b200_config* cfg, int32_t batch, int32_t world) {
+  int st = HBA_B200_OK;
+  if (!config_ok(cfg, &st) || batch <= 0 || world < 1 || world > hba::kShardMaxRanks) return -1;
+  return (int64_t)hba::x_layout(batch * cfg->n_kv, world, cfg->head_dim).total;
+}
+
+int hba_b200_peer_alloc(int64_t bytes, void** dptr, void* ipc_handle) {
+  if (bytes <= 0 || dptr == nullptr || ipc_handle == nullptr) return HBA_B200_ERR_INVALID_ARGUMENT;
+  *dptr = nullptr;
+  cudaError_t e = cudaMalloc(dptr, (size_t)bytes);
+  if (e == cudaSuccess) e = cudaMemset(*dptr, 0, (size_t)bytes);  // flags start below every epoch
+  if (e == cudaSuccess) e = cudaIpcGetMemHandle(static_cast<cudaIpcMemHandle_t*>(ipc_handle), *dptr);
+  if (e != cudaSuccess && *dptr != nullptr) {
+    cudaFree(*dptr);
+    *dptr = nullptr;
+  }
+  return cuda_status(e);
+}
+
+int hba_b200_peer_open(const void* ipc_handle, void** dptr) {
+  if (ipc_handle == nullptr || dptr == nullptr) return HBA_B200_ERR_INVALID_ARGUMENT;
+  cudaIpcMemHandle_t h;
+  memcpy(&h, ipc_handle, sizeof(h));
+  return cuda_status(cudaIpcOpenMemHandle(dptr, h, cudaIpcMemLazyEnablePeerAccess));
+}
+
+int hba_b200_peer_close(void* dptr) { return dptr == nullptr ? HBA_B200_OK : cuda_status(cudaIpcCloseMemHandle(dptr)); }
+
+int hba_b200_peer_free(void* dptr) { return dptr == nullptr ? HBA_B200_OK : cuda_status(cudaFree(dptr)); }
+
+int hba_b200_decode_shard_fused(const hba_b200_config* cfg, int32_t batch, int32_t n_cap_local, int32_t tok_lo,
+                                int32_t world, int32_t rank, void* const* xbufs, int32_t* epoch,
+                                const int32_t* seq_lens, const float* scales, const void* q, const float* q_gain,
+                                const float* k_gain, const void* summaries, const void* supers, const void* k_cache,
+                                const void* k_rope_cache, const void* v_cache, const float* cos, const float* sin,
+                                void* out, float* lse, int32_t* sel_idx, float* sel_score, int32_t* dev_status,
+                                cudaStream_t stream) {
+  int st = HBA_B200_OK;
+  if (!config_ok(cfg, &st)) return st;
+  if (batch <= 0 || n_cap_local <= 0 || tok_lo < 0 || world < 1 || world > hba::kShardMaxRanks || rank < 0 ||
+      rank >= world || xbufs == nullptr || epoch == nullptr || seq_lens == nullptr || scales == nullptr ||
+      q == nullptr || q_gain == nullptr || k_gain == nullptr || summaries == nullptr ||
+      (cfg->hier && supers == nullptr) || k_cache == nullptr || k_rope_cache == nullptr || v_cache == nullptr ||
+      cos == nullptr || sin == nullptr || out == nullptr || dev_status == nullptr ||
+      ((sel_idx == nullptr) != (sel_score == nullptr)))
+    return HBA_B200_ERR_INVALID_ARGUMENT;
+  for (int r = 0; r < world; ++r)
+    if (xbufs[r] == nullptr) return HBA_B200_ERR_INVALID_ARGUMENT;
+  const int unit = cfg->block * (cfg->hier ? cfg->fanout : 1);  // no block (super) straddles two ranks
+  if (n_cap_local % unit != 0 || tok_lo % unit != 0) return HBA_B200_ERR_NOT_BLOCK_MULTIPLE;
+  if (tok_lo > 0 && tok_lo < cfg->sinks) return HBA_B200_ERR_UNSUPPORTED;  // the sinks live on one shard
+  Geom geo = make_geom(cfg, batch, 1, n_cap_local);
+  if (!hba::decode_tc_supported(geo, cfg->head_dim, k_cache, k_rope_cache, v_cache, summaries, supers))
+    return HBA_B200_ERR_UNSUPPORTED;
+  hba::DecodeAttnParams dp{};
+  dp.geo = geo;
+  dp.trace = g_trace;
+  dp.trace_ctas = g_trace_ctas;
+  dp.qp = hba::QueryPos{seq_lens, scales, 0, 0.f};
+  dp.q = static_cast<const __nv_bfloat16*>(q);
+  dp.q_gain = q_gain;
+  dp.k = static_cast<const __nv_bfloat16*>(k_cache);
+  dp.kr = static_cast<const __nv_bfloat16*>(k_rope_cache);
+  dp.v = static_cast<const __nv_bfloat16*>(v_cache);
+  dp.cos = cos;
+  dp.sin = sin;
+  dp.out = static_cast<__nv_bfloat16*>(out);
+  dp.lse = lse;
+  dp.sel_idx = sel_idx;
+  dp.sel_score = sel_score;
+  return cuda_status(hba::launch_decode_tc_fused(dp, static_cast<const __nv_bfloat16*>(summaries),
+                                                 static_cast<const __nv_bfloat16*>(supers), k_gain, dev_status,
+                                                 cfg->head_dim, tok_lo, world, rank, epoch, xbufs, stream));
+}
+
 }  // extern "C"

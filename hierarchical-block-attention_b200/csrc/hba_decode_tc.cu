@@ -44,6 +44,7 @@ constexpr int kDtThreads = 256;
 constexpr int kDtKeys = 128;  // keys per chunk (UMMA M)
 constexpr int kDtProducer = 3;    // warp that feeds the ring from the first instruction on
 constexpr int kDtScoreWarps = 7;  // every other warp scores summary pages
+constexpr int kXListW = 32;       // entries per exchanged list slot
 
 // barrier of the 7 scoring warps (the producer warp never joins it)
 HBA_DEVICE void score_bar() { asm volatile("bar.sync 2, 224;\n" ::: "memory"); }
@@ -107,6 +108,16 @@ struct DecodeTcParams {
   float* part_o;          // [B, Hq, dh]
   float* part_l;          // [B, Hq]
   float* part_m2;         // [B, Hq]
+  // Fused shard mode (mode 2): as mode 1 for the owned tokens, but the CTA
+  // selects itself (owned candidates, exact scores) and exchanges with the
+  // same CTA of every other rank over NVLink: it writes its list (and later
+  // its (O, l) partial) into slot [rank] of every rank's exchange buffer
+  // (xpeer[r], IPC-mapped; xpeer[rank] is its own), releases an epoch flag
+  // there, and waits for every rank's flag in its own buffer.  Every rank
+  // merges the same global top-k and sums the same partials in rank order.
+  int32_t world, rank;
+  const int32_t* epoch;   // this step's epoch, bumped on the stream before the launch
+  unsigned char* xpeer[kShardMaxRanks];
 };
 
 template <int DH, int HB>
@@ -128,8 +139,9 @@ __global__ void __launch_bounds__(kDtThreads, 1)
   const int G = geo.G;
   const int bg = blockIdx.x;
   const int b = bg / geo.Hkv, g = bg % geo.Hkv;
-  const bool shard = P.mode == 1;
-  const bool hier = geo.hier != 0 && !shard;  // a shard gets its picks from the lists
+  const bool shard = P.mode >= 1;   // owned tokens [tok_lo, tok_hi) only
+  const bool fused = P.mode == 2;   // ... selecting and exchanging in-kernel
+  const bool hier = geo.hier != 0 && P.mode != 1;  // mode 1 gets its picks from the lists
   const int tok_lo = shard ? P.tok_lo : 0;    // global token of local row 0
   const int tok_hi = tok_lo + geo.n_cap;      // end of the owned tokens
   unsigned long long* trace = (p.trace != nullptr && bg < p.trace_ctas) ? p.trace + (size_t)bg * 16 : nullptr;
@@ -190,16 +202,23 @@ __global__ void __launch_bounds__(kDtThreads, 1)
   const int PB = SM::KT / row_bytes;  // summary rows per page
   const __nv_bfloat16* summ_bg = P.summ + (size_t)bg * geo.nb_cap * row_elems;
   const __nv_bfloat16* sup_bg = hier ? P.supers + (size_t)bg * geo.ns_cap * row_elems : nullptr;
-  int Ra = 0, ida = 1;  // phase-A candidates: flat blocks 1..bmax, or supers ida..
-  if (shard) {
+  // phase-A candidates, ids id0 .. id0 + Ra - 1: flat blocks 1..bmax, or
+  // supers ida..bmax/F, of them the owned ones (blocks [blo, bhi), supers
+  // [blo/F, bhi/F); local row = id - first owned id)
+  const int blo = tok_lo / geo.Bk, bhi = tok_hi / geo.Bk;
+  int Ra = 0, id0 = 1;
+  if (P.mode == 1) {
     Ra = 0;  // picks come from the lists
   } else if (!hier) {
-    Ra = max(0, bmax);
+    id0 = max(1, blo);
+    Ra = max(0, min(bmax, bhi - 1) - id0 + 1);
   } else if (bmax >= 1) {
-    ida = (geo.F == 1) ? 1 : 0;
-    Ra = bmax / geo.F - ida + 1;
+    const int ida = (geo.F == 1) ? 1 : 0;
+    id0 = max(ida, blo / geo.F);
+    Ra = max(0, min(bmax / geo.F, bhi / geo.F - 1) - id0 + 1);
   }
-  const __nv_bfloat16* rows_a = hier ? sup_bg : summ_bg;
+  const __nv_bfloat16* rows_a = hier ? sup_bg + (size_t)(id0 - blo / geo.F) * row_elems
+                                     : summ_bg + (size_t)(id0 - blo) * row_elems;
   const int NPa = (Ra + PB - 1) / PB;
   // Ring item order: [NPa phase-A pages][K,V of chunks 0 .. WA-1][NPb child
   // pages][K,V of chunks WA ..].  Flat: WA = all window/sink chunks (no child
@@ -270,7 +289,7 @@ __global__ void __launch_bounds__(kDtThreads, 1)
         if (i < NPa) {
           const int j0 = i * PB, nr = min(PB, Ra - j0);
           mbar_arrive_expect_tx(fb, (uint32_t)(nr * row_bytes));
-          bulk_load(dst, rows_a + (size_t)(ida + j0) * row_elems, (uint32_t)(nr * row_bytes), fb);
+          bulk_load(dst, rows_a + (size_t)j0 * row_elems, (uint32_t)(nr * row_bytes), fb);
         } else if (i >= cp0 && i < cp0 + NPb) {  // children of the beam: one bulk copy per contiguous span
           const int j0 = (i - cp0) * PB, j1 = min(R2, j0 + PB);
           mbar_arrive_expect_tx(fb, (uint32_t)((j1 - j0) * row_bytes));
@@ -278,7 +297,7 @@ __global__ void __launch_bounds__(kDtThreads, 1)
             const int lo = max(j0, sm.sup_off[si]), hi = min(j1, sm.sup_off[si] + sm.sup_cnt[si]);
             if (lo < hi)
               bulk_load(dst + (size_t)(lo - j0) * row_bytes,
-                        summ_bg + (size_t)(sm.sup_lo[si] + lo - sm.sup_off[si]) * row_elems,
+                        summ_bg + (size_t)(sm.sup_lo[si] + lo - sm.sup_off[si] - blo) * row_elems,
                         (uint32_t)((hi - lo) * row_bytes), fb);
           }
         } else {
@@ -527,10 +546,50 @@ __global__ void __launch_bounds__(kDtThreads, 1)
       }
     };
     int nsel = 0, NPb = 0;
-    if (shard) {
+    // warp 0, from the global top-k (gs, gi) (best first): the picks out,
+    // and the owned ones as local block ids in sm.sel_i, their count nsel
+    auto own_picks = [&](float gs, int gi) {
+      const bool valid = lane < kfinal && gi != INT_MAX;
+      if (p.sel_idx != nullptr && lane < geo.K) {
+        p.sel_idx[(size_t)bg * geo.K + lane] = valid ? gi : -1;
+        p.sel_score[(size_t)bg * geo.K + lane] = valid ? gs : neg_inf();
+      }
+      const bool own = valid && gi >= blo && gi < bhi;
+      const unsigned om = __ballot_sync(0xffffffffu, own);
+      if (own) sm.sel_i[__popc(om & ((1u << lane) - 1u))] = gi - blo;
+      nsel = __popc(om);
+      if (lane == 0) sm.nsel = nsel;
+    };
+    // Fused shard (warp 0): publish lanes [0, kx) of (ls, li) as this rank's
+    // list of exchange x in every rank's buffer, wait for every rank's, and
+    // return in (ls, li) the best 32 of their union, best first.
+    const XLayout xl = x_layout(geo.B * geo.Hkv, fused ? P.world : 1, DH);
+    const uint32_t epoch = fused ? (uint32_t)*P.epoch : 0u;
+    auto xflag = [&](int r, int x, int src) -> uint32_t* {  // rank r's flag of exchange x from rank src
+      return reinterpret_cast<uint32_t*>(P.xpeer[r] + xl.flags) + ((size_t)x * geo.B * geo.Hkv + bg) * P.world + src;
+    };
+    auto exchange_lists = [&](int x, int kx, float& ls_, int& li_) {
+      const uint2 mine = make_uint2(__float_as_uint(lane < kx ? ls_ : neg_inf()), (uint32_t)(lane < kx ? li_ : INT_MAX));
+      for (int r = 0; r < P.world; ++r)
+        reinterpret_cast<uint2*>(P.xpeer[r] + xl.list[x])[((size_t)bg * P.world + P.rank) * kXListW + lane] = mine;
+      __threadfence_system();
+      __syncwarp();
+      if (lane < P.world) st_release_sys(xflag(lane, x, P.rank), epoch);
+      if (lane < P.world) wait_flag(xflag(P.rank, x, lane), epoch, P.err);
+      __syncwarp();
+      const uint2* lists = reinterpret_cast<const uint2*>(P.xpeer[P.rank] + xl.list[x]) + (size_t)bg * P.world * kXListW;
+      float gs = neg_inf();
+      int gi = INT_MAX;
+      for (int r = 0; r < P.world; ++r) {  // each rank's list is sorted: merge them
+        const uint2 e = __ldcg(lists + r * kXListW + lane);
+        warp_merge32(gs, gi, __uint_as_float(e.x), (int)e.y);
+      }
+      ls_ = gs;
+      li_ = gi;
+    };
+    if (P.mode == 1) {
       // global top-k of every shard's lists, then the owned picks (local block ids)
       if (warp == 0) {
-        const int blo = tok_lo / geo.Bk, bhi = tok_hi / geo.Bk;
         const int kk = max(1, kfinal);
         for (int e0 = 0; e0 < P.n_in; e0 += 32) {
           const int e = e0 + lane;
@@ -550,15 +609,7 @@ __global__ void __launch_bounds__(kDtThreads, 1)
             warp_merge32(ls, li, cs, ci);
           }
         }
-        const bool valid = lane < kfinal && li != INT_MAX;
-        if (p.sel_idx != nullptr && lane < geo.K) {
-          p.sel_idx[(size_t)bg * geo.K + lane] = valid ? li : -1;
-          p.sel_score[(size_t)bg * geo.K + lane] = valid ? ls : neg_inf();
-        }
-        const bool own = valid && li >= blo && li < bhi;
-        const unsigned om = __ballot_sync(0xffffffffu, own);
-        if (own) sm.sel_i[__popc(om & ((1u << lane) - 1u))] = li - blo;
-        if (lane == 0) sm.nsel = __popc(om);
+        own_picks(ls, li);
       }
       score_bar();
       nsel = sm.nsel;
@@ -566,7 +617,7 @@ __global__ void __launch_bounds__(kDtThreads, 1)
     } else if (!hier) {
       // each warp publishes its list; warp 0 alone merges them, while the MMA
       // and softmax warps go on to the window and sink chunks
-      if (kfinal > 0) score_pages(0, NPa, Ra, kfinal, [&](int j) { return 1 + j; });
+      if (kfinal > 0) score_pages(0, NPa, Ra, kfinal, [&](int j) { return id0 + j; });
       stamp(5);
       sm.wl_s[sw][lane] = ls;
       sm.wl_i[sw][lane] = li;
@@ -578,10 +629,15 @@ __global__ void __launch_bounds__(kDtThreads, 1)
         float fs = sm.wl_s[0][lane];
         int fi = sm.wl_i[0][lane];
         for (int w = 1; w < NSW; ++w) warp_merge32(fs, fi, sm.wl_s[w][lane], sm.wl_i[w][lane]);
-        nsel = __popc(__ballot_sync(0xffffffffu, lane < kfinal && fi != INT_MAX));
-        sm.sel_i[lane] = fi;
-        sm.sel_s[lane] = fs;
-        if (lane == 0) sm.nsel = nsel;
+        if (fused) {  // this rank's top-k -> every rank -> the global top-k
+          exchange_lists(0, kfinal, fs, fi);
+          own_picks(fs, fi);
+        } else {
+          nsel = __popc(__ballot_sync(0xffffffffu, lane < kfinal && fi != INT_MAX));
+          sm.sel_i[lane] = fi;
+          sm.sel_s[lane] = fs;
+          if (lane == 0) sm.nsel = nsel;
+        }
       }
       stamp(6);
     } else if (warp == 0 || warp == 2) {
@@ -608,10 +664,19 @@ __global__ void __launch_bounds__(kDtThreads, 1)
         return sm.nsel;
       };
       const int kb = max(1, min(geo.beam, ns));
-      score_pages(0, NPa, Ra, kb, [&](int j) { return ida + j; });
+      score_pages(0, NPa, Ra, kb, [&](int j) { return id0 + j; });
       stamp(5);
-      const int nsup = merge2(kb);
+      int nsup = merge2(kb);
       if (warp == 0) {  // the beam's supers in ascending order; their children as contiguous spans
+        if (fused) {  // this rank's top-beam -> every rank -> the global beam
+          float fs = lane < nsup ? sm.sel_s[lane] : neg_inf();
+          int fi = lane < nsup ? sm.sel_i[lane] : INT_MAX;
+          exchange_lists(0, kb, fs, fi);
+          nsup = __popc(__ballot_sync(0xffffffffu, lane < kb && fi != INT_MAX));
+          __syncwarp();
+          sm.sel_i[lane] = fi;
+          __syncwarp();
+        }
         const bool valid = lane < nsup;
         const int sidx = valid ? sm.sel_i[lane] : INT_MAX;
         int rank = 0;
@@ -625,6 +690,7 @@ __global__ void __launch_bounds__(kDtThreads, 1)
         if (lane < nsup) {
           lo = max(1, s * geo.F);
           cnt = max(0, min(bmax, s * geo.F + geo.F - 1) - lo + 1);
+          if (s < blo / geo.F || s >= bhi / geo.F) cnt = 0;  // children on another rank
         }
         int incl = cnt;
 #pragma unroll
@@ -655,6 +721,13 @@ __global__ void __launch_bounds__(kDtThreads, 1)
       if (kfinal > 0) score_pages(NPa + 2 * WA, NPb, R2, kfinal, child_id);
       stamp(7);
       nsel = merge2(max(1, kfinal));
+      if (fused && warp == 0) {  // this rank's top-k of its children -> every rank -> the global top-k
+        float fs = lane < nsel ? sm.sel_s[lane] : neg_inf();
+        int fi = lane < nsel ? sm.sel_i[lane] : INT_MAX;
+        exchange_lists(1, kfinal, fs, fi);
+        __syncwarp();
+        own_picks(fs, fi);
+      }
     }
     if (warp == 0) {  // (flat: only warp 0 knows nsel here; the others read it after sel_ready)
       const bool valid = lane < nsel;
@@ -808,9 +881,12 @@ __global__ void __launch_bounds__(kDtThreads, 1)
 #pragma unroll
         for (int h = 0; h < HB; ++h) sm.lsum[warp & 3][h] = lp[h];
       asm volatile("bar.sync 1, 128;\n" ::: "memory");  // the 4 softmax warps
-      if (okw && mbar_wait(&sm.o_full, 0, P.err)) {
+      const bool have_o = okw && mbar_wait(&sm.o_full, 0, P.err);
+      uint32_t r[16];
+#pragma unroll
+      for (int h = 0; h < 16; ++h) r[h] = 0u;
+      if (have_o) {
         tc_fence_after();
-        uint32_t r[16];
         asm volatile(
             "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, "
             "[%16];\n"
@@ -818,7 +894,47 @@ __global__ void __launch_bounds__(kDtThreads, 1)
               "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
             : "r"(tmem + 32 + lane_off));
         tmem_ld_wait();
-        if (shard) {  // unnormalised partial of the owned tokens, fixed max m2
+      }
+      if (fused) {
+        // (O, l) of the owned tokens -> slot [rank] of every rank's buffer;
+        // then out = sum O / sum l over the ranks' slots, in rank order (the
+        // same on every rank)
+        const size_t xs = 16 * DH + 16;
+        for (int rr = 0; rr < P.world; ++rr) {
+          float* dst = reinterpret_cast<float*>(P.xpeer[rr] + xl.parts) + ((size_t)bg * P.world + P.rank) * xs;
+          if (t < DH) {
+#pragma unroll
+            for (int h = 0; h < 16; ++h)
+              if (h < G) dst[h * DH + t] = NC > 0 ? __uint_as_float(r[h]) : 0.f;  // no owned keys: zero
+          }
+          if (t < G) dst[16 * DH + t] = sm.lsum[0][t] + sm.lsum[1][t] + sm.lsum[2][t] + sm.lsum[3][t];
+        }
+        __threadfence_system();
+        asm volatile("bar.sync 1, 128;\n" ::: "memory");
+        if (t < P.world) st_release_sys(xflag(t, 2, P.rank), epoch);
+        if (t < P.world) wait_flag(xflag(P.rank, 2, t), epoch, P.err);
+        asm volatile("bar.sync 1, 128;\n" ::: "memory");
+        const float* parts = reinterpret_cast<const float*>(P.xpeer[P.rank] + xl.parts) + (size_t)bg * P.world * xs;
+        if (t < DH) {
+#pragma unroll
+          for (int h = 0; h < 16; ++h) {
+            if (h < G) {
+              float O = 0.f, L = 0.f;
+              for (int rr = 0; rr < P.world; ++rr) {
+                O += __ldcg(parts + rr * xs + h * DH + t);
+                L += __ldcg(parts + rr * xs + 16 * DH + h);
+              }
+              p.out[((size_t)b * geo.Hq + g * G + h) * DH + t] = f2bf(L > 0.f ? O / L : 0.f);
+            }
+          }
+        }
+        if (t < G && p.lse != nullptr) {
+          float L = 0.f;
+          for (int rr = 0; rr < P.world; ++rr) L += __ldcg(parts + rr * xs + 16 * DH + t);
+          p.lse[(size_t)b * geo.Hq + g * G + t] = L > 0.f ? (sm.m2[t] + log2f(L)) * 0.6931471805599453f : neg_inf();
+        }
+      } else if (have_o) {
+        if (P.mode == 1) {  // unnormalised partial of the owned tokens, fixed max m2
           if (t < DH) {
 #pragma unroll
             for (int h = 0; h < 16; ++h)
@@ -947,6 +1063,30 @@ cudaError_t launch_decode_tc_shard(const DecodeAttnParams& p, const float* k_gai
   P.part_o = part_o;
   P.part_l = part_l;
   P.part_m2 = part_m2;
+  return launch_dtc(P, dh, st);
+}
+
+__global__ void epoch_bump_kernel(int32_t* epoch) { *epoch += 1; }
+
+cudaError_t launch_decode_tc_fused(const DecodeAttnParams& p, const __nv_bfloat16* summ, const __nv_bfloat16* supers,
+                                   const float* k_gain, int* err, int dh, int tok_lo, int world, int rank,
+                                   int32_t* epoch, void* const* xbufs, cudaStream_t st) {
+  if (world < 1 || world > kShardMaxRanks || rank < 0 || rank >= world) return cudaErrorInvalidValue;
+  epoch_bump_kernel<<<1, 1, 0, st>>>(epoch);  // this step's epoch, the same count on every rank
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return e;
+  DecodeTcParams P{};
+  P.a = p;
+  P.summ = summ;
+  P.supers = supers;
+  P.k_gain = k_gain;
+  P.err = err;
+  P.mode = 2;
+  P.tok_lo = tok_lo;
+  P.world = world;
+  P.rank = rank;
+  P.epoch = epoch;
+  for (int r = 0; r < world; ++r) P.xpeer[r] = static_cast<unsigned char*>(xbufs[r]);
   return launch_dtc(P, dh, st);
 }
 

@@ -8,6 +8,31 @@
 
 namespace hba {
 
+constexpr int kShardMaxRanks = 8;
+
+// Exchange buffer of the fused shard decode (one per rank, IPC-mapped by the
+// others), for BH = B * Hkv (sequence, kv head) rows and `world` ranks:
+// two list regions [BH][world][32] of (score bits, block id), the (O, l)
+// partials [BH][world][16 * dh + 16] fp32, and the epoch flags
+// [3][BH][world] uint32 (exchanges: level-1 list, level-2 list, partials).
+struct XLayout {
+  size_t list[2], parts, flags, total;
+};
+__host__ __device__ inline XLayout x_layout(int BH, int world, int dh) {
+  XLayout l;
+  size_t o = 0;
+  for (int x = 0; x < 2; ++x) {
+    l.list[x] = o;
+    o += (size_t)BH * world * 32 * 8;
+  }
+  l.parts = o;
+  o += (size_t)BH * world * (16 * dh + 16) * 4;
+  l.flags = o;
+  o += (size_t)3 * BH * world * 4;
+  l.total = o;
+  return l;
+}
+
 // Where a query sits: decode (one query per sequence at seq_lens[b]-1 over a
 // cache of seq_lens[b] tokens, per-sequence scale) or prefill (query t of a
 // length-n sequence at position t, one scale).
@@ -146,6 +171,13 @@ cudaError_t launch_select_tile(const SelParams& p, int dh, int* err, cudaStream_
 cudaError_t launch_decode_tc_shard(const DecodeAttnParams& p, const float* k_gain, int* err, int dh, int tok_lo,
                                    const int32_t* in_idx, const float* in_score, int n_in, float* part_o,
                                    float* part_l, float* part_m2, cudaStream_t st);
+// Fused KV-range shard (mode 2): selection of the owned candidates, the list
+// and partial exchanges with the other ranks over their IPC-mapped exchange
+// buffers xbufs[0 .. world) (x_layout), and the union of the owned tokens, in
+// one launch after a one-thread epoch bump.
+cudaError_t launch_decode_tc_fused(const DecodeAttnParams& p, const __nv_bfloat16* summ, const __nv_bfloat16* supers,
+                                   const float* k_gain, int* err, int dh, int tok_lo, int world, int rank,
+                                   int32_t* epoch, void* const* xbufs, cudaStream_t st);
 cudaError_t launch_shard_finish(int rows, int dh, const float* po, const float* pl, const float* pm2,
                                 __nv_bfloat16* out, float* lse, cudaStream_t st);
 bool decode_tc_supported(const Geom& geo, int dh, const void* k, const void* kr, const void* v, const void* summ,

@@ -76,6 +76,29 @@ HBA_DEVICE bool mbar_wait(uint64_t* bar, uint32_t parity, int* err) {
   return false;
 }
 
+// System-scope flag store / load (flags a peer GPU writes or reads over NVLink).
+HBA_DEVICE void st_release_sys(uint32_t* p, uint32_t v) {
+  asm volatile("st.release.sys.global.u32 [%0], %1;\n" ::"l"(p), "r"(v) : "memory");
+}
+HBA_DEVICE uint32_t ld_acquire_sys(const uint32_t* p) {
+  uint32_t v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];\n" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+// Bounded wait until the flag reaches epoch ep (flags only grow); false (and
+// *err set) after kWaitNs.
+HBA_DEVICE bool wait_flag(const uint32_t* p, uint32_t ep, int* err) {
+  if ((int)(ld_acquire_sys(p) - ep) >= 0) return true;
+  const unsigned long long t0 = global_ns();
+  for (uint32_t k = 1;; ++k) {
+    __nanosleep(64);
+    if ((int)(ld_acquire_sys(p) - ep) >= 0) return true;
+    if ((k & 15) == 0 && global_ns() - t0 > kWaitNs) break;
+  }
+  if (err != nullptr) atomicExch(err, 1);
+  return false;
+}
+
 // Shared-memory writes by threads must be made visible to the async proxy
 // (TMA, tensor cores) before the consumer is signalled.
 HBA_DEVICE void fence_proxy_async_smem() { asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory"); }

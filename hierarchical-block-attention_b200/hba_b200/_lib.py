@@ -69,6 +69,15 @@ SIGNATURES = {
     "hba_b200_decode_shard_attend": (ctypes.c_int, [_CFG, _I32, _I32, _I32, _P, _P, _P, _P, _P, _P, _P, _P, _P,
                                                     _P, _P, _P, _I32, _P, _P, _P, _P, _P, _P, _P]),
     "hba_b200_decode_shard_finish": (ctypes.c_int, [_CFG, _I32, _P, _P, _P, _P, _P, _P]),
+    "hba_b200_shard_xbuf_bytes": (_I64, [_CFG, _I32, _I32]),
+    "hba_b200_peer_alloc": (ctypes.c_int, [_I64, ctypes.POINTER(ctypes.c_void_p), _P]),
+    "hba_b200_peer_open": (ctypes.c_int, [_P, ctypes.POINTER(ctypes.c_void_p)]),
+    "hba_b200_peer_close": (ctypes.c_int, [_P]),
+    "hba_b200_peer_free": (ctypes.c_int, [_P]),
+    # cfg, batch, n_cap_local, tok_lo, world, rank, xbufs, epoch, seq_lens, scales, q, q_gain, k_gain, summ,
+    # supers, k, kr, v, cos, sin, out, lse, sel_idx, sel_score, dev_status, stream
+    "hba_b200_decode_shard_fused": (ctypes.c_int, [_CFG, _I32, _I32, _I32, _I32, _I32, _P, _P, _P, _P, _P, _P,
+                                                   _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P]),
     "hba_b200_prefill": (ctypes.c_int, [_CFG, _I32, _I32, _F, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P,
                                         _P, _P, _SZ, _P]),
 }

@@ -20,9 +20,17 @@ multiples, so no block or super straddles two ranks.  One decode step:
 
 The reference runs on one device and has no equivalent; the result is its
 decode (src/hba/attention.py:663-711 at cs = n-1) over the whole context.
-The kernels are the library's `hba_b200_decode_shard_*` entry points; the
-collectives go through `TorchComm` (torch.distributed: NCCL on GPUs, gloo in
-the CPU tests, which also swap the kernels for a CPU stand-in via `ops`).
+
+Two implementations of the step:
+  fused (default on GPUs)  one `hba_b200_decode_shard_fused` launch per step:
+        the kernel's CTA for (sequence, kv head) exchanges its lists and its
+        partial with the same CTA of every other rank through NVLink peer
+        memory (`PeerExchange`: each rank's buffer, IPC-mapped by the others),
+        with epoch flags and bounded waits -- no collective library call.
+  split  the `hba_b200_decode_shard_select / _attend / _finish` kernels with
+        the collectives in between through `TorchComm` (torch.distributed:
+        NCCL on GPUs, gloo in the CPU tests, which also swap the kernels for a
+        CPU stand-in via `ops`).
 """
 
 import ctypes
@@ -63,6 +71,58 @@ class TorchComm:
         dist.all_reduce(t, op=dist.ReduceOp.SUM, group=self.group)
 
 
+class PeerExchange:
+    """The exchange buffers of the fused sharded decode: this rank's (cudaMalloc
+    by the library, zeroed) and every other rank's, mapped into this process
+    through CUDA IPC handles shared over the process group, plus the device
+    epoch counter the fused call bumps each step.  `close()` unmaps and frees
+    (collective: every rank calls it)."""
+
+    def __init__(self, cfg, batch, hier, device, group=None):
+        L = _lib.load()
+        self.group = group
+        self.world = dist.get_world_size(group)
+        self.rank = dist.get_rank(group)
+        self.device = torch.device(device)
+        nbytes = L.hba_b200_shard_xbuf_bytes(ctypes.byref(c_config(cfg, hier)), int(batch), self.world)
+        if nbytes <= 0:
+            raise ValueError(f"fused sharded decode: unsupported world size {self.world}")
+        handle = ctypes.create_string_buffer(64)
+        own = ctypes.c_void_p()
+        with torch.cuda.device(self.device):
+            _lib.check(L.hba_b200_peer_alloc(int(nbytes), ctypes.byref(own), handle), "hba_b200_peer_alloc")
+        self.own = own.value
+        handles = [None] * self.world
+        dist.all_gather_object(handles, bytes(handle.raw), group=group)
+        ptrs, self.mapped = [], []
+        with torch.cuda.device(self.device):
+            for r, h in enumerate(handles):
+                if r == self.rank:
+                    ptrs.append(self.own)
+                    continue
+                pr = ctypes.c_void_p()
+                _lib.check(L.hba_b200_peer_open(ctypes.create_string_buffer(h, 64), ctypes.byref(pr)),
+                           "hba_b200_peer_open")
+                ptrs.append(pr.value)
+                self.mapped.append(pr.value)
+        self.ptrs = (ctypes.c_void_p * self.world)(*ptrs)
+        self.epoch = torch.zeros(1, dtype=torch.int32, device=self.device)
+
+    def close(self):
+        if self.own is None:
+            return
+        L = _lib.load()
+        torch.cuda.synchronize(self.device)
+        with torch.cuda.device(self.device):
+            for pr in self.mapped:
+                L.hba_b200_peer_close(ctypes.c_void_p(pr))
+        self.mapped = []
+        dist.barrier(group=self.group)  # nobody maps our buffer any more
+        with torch.cuda.device(self.device):
+            L.hba_b200_peer_free(ctypes.c_void_p(self.own))
+        self.own = None
+
+
 class CudaShardOps:
     """The product path: the library's shard kernels on the rank's GPU."""
 
@@ -96,7 +156,12 @@ class HBAShardedDecode:
     (default: the CUDA library)."""
 
     def __init__(self, cfg, batch, max_len, summ, qkn, cos, sin, device="cuda", hier=False, comm=None,
-                 ops=None, local=None):
+                 ops=None, local=None, fused=None):
+        # fused: the one-launch NVLink path (default when the collectives and
+        # kernels are the real ones on GPUs); else the split path
+        if fused is None:
+            fused = comm is None and ops is None and torch.device(device).type == "cuda"
+        self.fused = bool(fused)
         self.comm = comm if comm is not None else TorchComm()
         self.ops = ops if ops is not None else CudaShardOps()
         self.cfg = cfg
@@ -129,6 +194,7 @@ class HBAShardedDecode:
         self.part_l = self.part[self.B * Hq * dh:].view(self.B, Hq)
         self.part_m2 = torch.empty(self.B, Hq, dtype=torch.float32, device=dev)
         self.q = None
+        self.x = PeerExchange(cfg, self.B, self.hier, dev, self.comm.group) if self.fused else None
 
     # ---------------------------------------------------------------- state --
     def _set_lengths(self, n):
@@ -177,6 +243,16 @@ class HBAShardedDecode:
         if (self.glens_host < 1).any():
             raise ValueError("every sequence needs at least one cached token")
         self.q = q
+        if self.fused:
+            loc = self.local
+            st = _lib.load().hba_b200_decode_shard_fused(
+                ctypes.byref(self.c), self.B, self.n_loc, self.tok_lo, self.world, self.rank, self.x.ptrs,
+                ptr(self.x.epoch), ptr(self.glens), ptr(self.scales), ptr(q), ptr(loc.q_gain), ptr(loc.k_gain),
+                ptr(loc.summaries), ptr(loc.supers), ptr(loc.k), ptr(loc.kr), ptr(loc.v), ptr(self.cos),
+                ptr(self.sin), ptr(out), ptr(lse), ptr(sel_idx), ptr(sel_score), ptr(self.status),
+                stream_of(self.device))
+            _lib.check(st, "hba_b200_decode_shard_fused")
+            return
         if not self.hier:
             self.ops.select(self, 0, None, None, 0, self.l_idx, self.l_sc)
         else:
@@ -204,7 +280,16 @@ class HBAShardedDecode:
         self.graph.replay()
 
     def release(self):
+        """Drop the captured graph (before the process group is destroyed)."""
         self.graph = None
+
+    def close(self):
+        """Release the graph and, on the fused path, the exchange buffers
+        (collective: every rank calls it)."""
+        self.release()
+        if self.x is not None:
+            self.x.close()
+            self.x = None
 
     def attend(self, q, return_lse=False):
         """Allocating convenience wrapper of `decode_into`."""

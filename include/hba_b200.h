@@ -268,6 +268,42 @@ int hba_b200_decode_shard_finish(const hba_b200_config* cfg, int32_t batch, cons
                                  cudaStream_t stream);
 
 /*
+ * Fused KV-range sharded decode (no counterpart in the reference; same
+ * result as the three calls above): ONE launch per step on each rank does
+ * the owned selection, the list exchanges and the union over the owned
+ * tokens, exchanging with the same (sequence, kv head) CTA of every other
+ * rank over NVLink through the ranks' exchange buffers -- each rank writes
+ * its lists and its (O, l) partial into slot [rank] of every buffer and
+ * releases an epoch flag there -- so there is no collective library call.
+ * Every rank returns the full out / lse / picks.
+ *   xbuf_bytes   size of one rank's exchange buffer (-1 on bad arguments).
+ *   peer_alloc   cudaMalloc + zero a buffer on the current device and write
+ *                its 64-byte CUDA IPC handle to ipc_handle.
+ *   peer_open    map another process's buffer from its handle (same node,
+ *                peer access enabled); peer_close unmaps, peer_free frees.
+ *   decode_shard_fused  xbufs[r] = rank r's buffer as mapped in this process
+ *                (xbufs[rank] = its own); epoch = a device int32, zero at
+ *                start, bumped by the call on `stream` (every rank must make
+ *                the same calls); dev_status is sticky (zero it once; 1 = a
+ *                wait gave up, e.g. a rank that never arrived).  Bounds fall
+ *                on block (hier: block * fanout) multiples; world <= 8.
+ * Every wait is bounded in time; a rank that never arrives turns into a
+ * status, not a hang.
+ */
+int64_t hba_b200_shard_xbuf_bytes(const hba_b200_config* cfg, int32_t batch, int32_t world);
+int hba_b200_peer_alloc(int64_t bytes, void** dptr, void* ipc_handle);
+int hba_b200_peer_open(const void* ipc_handle, void** dptr);
+int hba_b200_peer_close(void* dptr);
+int hba_b200_peer_free(void* dptr);
+int hba_b200_decode_shard_fused(const hba_b200_config* cfg, int32_t batch, int32_t n_cap_local, int32_t tok_lo,
+                                int32_t world, int32_t rank, void* const* xbufs, int32_t* epoch,
+                                const int32_t* seq_lens, const float* scales, const void* q, const float* q_gain,
+                                const float* k_gain, const void* summaries, const void* supers, const void* k_cache,
+                                const void* k_rope_cache, const void* v_cache, const float* cos, const float* sin,
+                                void* out, float* lse, int32_t* sel_idx, float* sel_score, int32_t* dev_status,
+                                cudaStream_t stream);
+
+/*
  * Introspection (no counterpart in the reference): the kernels the last
  * hba_b200_decode / _decode_noalloc / _prefill call of this process launched,
  * in launch order joined by '+', as a static string (e.g. "decode_tc_kernel";

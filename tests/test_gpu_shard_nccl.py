@@ -1,6 +1,7 @@
-"""KV-range sharded decode over NCCL: two processes, one GPU each, run
-`HBAShardedDecode` with torch.distributed collectives; every rank's output
-must match the one-GPU decode of the same context.  Needs 2 GPUs."""
+"""KV-range sharded decode over NCCL (the split path): two processes, one GPU
+each, run `HBAShardedDecode(fused=False)` -- the shard kernels with
+torch.distributed collectives in between; every rank's output must match the
+one-GPU decode of the same context.  Needs 2 GPUs."""
 
 import os
 import socket
@@ -36,7 +37,7 @@ def _rank(rank, world, port, outdir):
         summ, qkn = synth.make_weights(cfg, dev, seed=3, gains=True)
         cos, sin = synth.rope_tables(N, cfg.head_dim, 1e6)
         wl = synth.decode_workload(cfg, B, N, hier=True, seed=3, device=dev, qkn=qkn, planted=8)
-        sh = HBAShardedDecode(cfg, B, N, summ, qkn, cos, sin, device=dev, hier=True)
+        sh = HBAShardedDecode(cfg, B, N, summ, qkn, cos, sin, device=dev, hier=True, fused=False)
         sh.fill(wl["k"], wl["v"])
         q = wl["q"].contiguous()
         out = torch.empty_like(q)
