@@ -772,6 +772,7 @@ int hba_b200_decode_shard_fused(const hba_b200_config* cfg, int32_t batch, int32
   const int unit = cfg->block * (cfg->hier ? cfg->fanout : 1);  // no block (super) straddles two ranks
   if (n_cap_local % unit != 0 || tok_lo % unit != 0) return HBA_B200_ERR_NOT_BLOCK_MULTIPLE;
   if (tok_lo > 0 && tok_lo < cfg->sinks) return HBA_B200_ERR_UNSUPPORTED;  // the sinks live on one shard
+  if ((int64_t)world * n_cap_local / cfg->block >= 0xffff) return HBA_B200_ERR_UNSUPPORTED;  // 16-bit block ids
   Geom geo = make_geom(cfg, batch, 1, n_cap_local);
   if (!hba::decode_tc_supported(geo, cfg->head_dim, k_cache, k_rope_cache, v_cache, summaries, supers))
     return HBA_B200_ERR_UNSUPPORTED;

@@ -71,6 +71,7 @@ struct DtcSmem {
   float qg[DH];
   float m2[16];
   float lsum[4][16];
+  float xl[16];  // fused shard: l of every head summed over the ranks
   float wl_s[kDtScoreWarps][32];  // per-warp top-k lists
   int wl_i[kDtScoreWarps][32];
   float sel_s[32];                // merged picks, best first
@@ -112,9 +113,10 @@ struct DecodeTcParams {
   // selects itself (owned candidates, exact scores) and exchanges with the
   // same CTA of every other rank over NVLink: it writes its list (and later
   // its (O, l) partial) into slot [rank] of every rank's exchange buffer
-  // (xpeer[r], IPC-mapped; xpeer[rank] is its own), releases an epoch flag
-  // there, and waits for every rank's flag in its own buffer.  Every rank
-  // merges the same global top-k and sums the same partials in rank order.
+  // (xpeer[r], IPC-mapped; xpeer[rank] is its own) as epoch-tagged 64-bit
+  // words (x_layout) and waits for this step's tag in every rank's slot of
+  // its own buffer.  Every rank merges the same global top-k and sums the
+  // same partials in rank order.
   int32_t world, rank;
   const int32_t* epoch;   // this step's epoch, bumped on the stream before the launch
   unsigned char* xpeer[kShardMaxRanks];
@@ -565,25 +567,32 @@ __global__ void __launch_bounds__(kDtThreads, 1)
     // return in (ls, li) the best 32 of their union, best first.
     const XLayout xl = x_layout(geo.B * geo.Hkv, fused ? P.world : 1, DH);
     const uint32_t epoch = fused ? (uint32_t)*P.epoch : 0u;
-    auto xflag = [&](int r, int x, int src) -> uint32_t* {  // rank r's flag of exchange x from rank src
-      return reinterpret_cast<uint32_t*>(P.xpeer[r] + xl.flags) + ((size_t)x * geo.B * geo.Hkv + bg) * P.world + src;
-    };
+    // list entry: score bits | block id (0xffff: none) << 32 | epoch (16 bits) << 48
+    const unsigned long long etag = epoch & 0xffffu;
     auto exchange_lists = [&](int x, int kx, float& ls_, int& li_) {
-      const uint2 mine = make_uint2(__float_as_uint(lane < kx ? ls_ : neg_inf()), (uint32_t)(lane < kx ? li_ : INT_MAX));
+      const bool has = lane < kx && li_ != INT_MAX;
+      const unsigned long long mine = (unsigned long long)__float_as_uint(has ? ls_ : neg_inf()) |
+                                      ((unsigned long long)(has ? (uint32_t)li_ & 0xffffu : 0xffffu) << 32) |
+                                      (etag << 48);
       for (int r = 0; r < P.world; ++r)
-        reinterpret_cast<uint2*>(P.xpeer[r] + xl.list[x])[((size_t)bg * P.world + P.rank) * kXListW + lane] = mine;
-      __threadfence_system();
-      __syncwarp();
-      if (lane < P.world) st_release_sys(xflag(lane, x, P.rank), epoch);
-      if (lane < P.world) wait_flag(xflag(P.rank, x, lane), epoch, P.err);
-      __syncwarp();
-      const uint2* lists = reinterpret_cast<const uint2*>(P.xpeer[P.rank] + xl.list[x]) + (size_t)bg * P.world * kXListW;
+        st_relaxed_sys(reinterpret_cast<unsigned long long*>(P.xpeer[r] + xl.list[x]) +
+                           ((size_t)bg * P.world + P.rank) * kXListW + lane,
+                       mine);
+      const unsigned long long* lists =
+          reinterpret_cast<const unsigned long long*>(P.xpeer[P.rank] + xl.list[x]) + (size_t)bg * P.world * kXListW;
+      unsigned long long e[kShardMaxRanks];  // this lane's entry of every rank's list, loaded together
+      wait_tagged_n<kShardMaxRanks>(lists + lane, kXListW, P.world, 48, 0xffffu, etag, e, P.err);
       float gs = neg_inf();
       int gi = INT_MAX;
-      for (int r = 0; r < P.world; ++r) {  // each rank's list is sorted: merge them
-        const uint2 e = __ldcg(lists + r * kXListW + lane);
-        warp_merge32(gs, gi, __uint_as_float(e.x), (int)e.y);
+#pragma unroll
+      for (int r = 0; r < kShardMaxRanks; ++r) {  // each rank's list is sorted: merge them
+        if (r < P.world) {
+          const uint32_t id = (uint32_t)(e[r] >> 32) & 0xffffu;
+          warp_merge32(gs, gi, id == 0xffffu ? neg_inf() : __uint_as_float((uint32_t)e[r]),
+                       id == 0xffffu ? INT_MAX : (int)id);
+        }
       }
+      if (lane == 0) stamp_any(14 + x);
       ls_ = gs;
       li_ = gi;
     };
@@ -899,40 +908,61 @@ __global__ void __launch_bounds__(kDtThreads, 1)
         // (O, l) of the owned tokens -> slot [rank] of every rank's buffer;
         // then out = sum O / sum l over the ranks' slots, in rank order (the
         // same on every rank)
+        // every value tagged with the epoch: (fp32 bits | epoch << 32)
         const size_t xs = 16 * DH + 16;
+        const unsigned long long ptag = (unsigned long long)epoch << 32;
         for (int rr = 0; rr < P.world; ++rr) {
-          float* dst = reinterpret_cast<float*>(P.xpeer[rr] + xl.parts) + ((size_t)bg * P.world + P.rank) * xs;
+          unsigned long long* dst =
+              reinterpret_cast<unsigned long long*>(P.xpeer[rr] + xl.parts) + ((size_t)bg * P.world + P.rank) * xs;
           if (t < DH) {
 #pragma unroll
             for (int h = 0; h < 16; ++h)
-              if (h < G) dst[h * DH + t] = NC > 0 ? __uint_as_float(r[h]) : 0.f;  // no owned keys: zero
+              if (h < G)  // no owned keys: zero
+                st_relaxed_sys(dst + h * DH + t, ptag | __float_as_uint(NC > 0 ? __uint_as_float(r[h]) : 0.f));
           }
-          if (t < G) dst[16 * DH + t] = sm.lsum[0][t] + sm.lsum[1][t] + sm.lsum[2][t] + sm.lsum[3][t];
+          if (t < G)
+            st_relaxed_sys(dst + 16 * DH + t,
+                           ptag | __float_as_uint(sm.lsum[0][t] + sm.lsum[1][t] + sm.lsum[2][t] + sm.lsum[3][t]));
         }
-        __threadfence_system();
+        const unsigned long long* parts =
+            reinterpret_cast<const unsigned long long*>(P.xpeer[P.rank] + xl.parts) + (size_t)bg * P.world * xs;
+        // l: thread t < G sums head t over the ranks (into sm.xl); O: each
+        // thread t < DH its row over the ranks, a rank's G words at a time
+        if (t < G) {
+          unsigned long long w[kShardMaxRanks];
+          wait_tagged_n<kShardMaxRanks>(parts + 16 * DH + t, xs, P.world, 32, 0xffffffffull, epoch, w, P.err);
+          float L = 0.f;
+#pragma unroll
+          for (int rr = 0; rr < kShardMaxRanks; ++rr)
+            if (rr < P.world) L += __uint_as_float((uint32_t)w[rr]);
+          sm.xl[t] = L;
+        }
+        float O[HB];
+#pragma unroll
+        for (int h = 0; h < HB; ++h) O[h] = 0.f;
+        if (t < DH) {
+          for (int rr = 0; rr < P.world; ++rr) {
+            unsigned long long w[HB];
+            wait_tagged_n<HB>(parts + rr * xs + t, DH, G, 32, 0xffffffffull, epoch, w, P.err);
+#pragma unroll
+            for (int h = 0; h < HB; ++h) O[h] += __uint_as_float((uint32_t)w[h]);
+          }
+        }
         asm volatile("bar.sync 1, 128;\n" ::: "memory");
-        if (t < P.world) st_release_sys(xflag(t, 2, P.rank), epoch);
-        if (t < P.world) wait_flag(xflag(P.rank, 2, t), epoch, P.err);
-        asm volatile("bar.sync 1, 128;\n" ::: "memory");
-        const float* parts = reinterpret_cast<const float*>(P.xpeer[P.rank] + xl.parts) + (size_t)bg * P.world * xs;
         if (t < DH) {
 #pragma unroll
-          for (int h = 0; h < 16; ++h) {
+          for (int h = 0; h < HB; ++h) {
             if (h < G) {
-              float O = 0.f, L = 0.f;
-              for (int rr = 0; rr < P.world; ++rr) {
-                O += __ldcg(parts + rr * xs + h * DH + t);
-                L += __ldcg(parts + rr * xs + 16 * DH + h);
-              }
-              p.out[((size_t)b * geo.Hq + g * G + h) * DH + t] = f2bf(L > 0.f ? O / L : 0.f);
+              const float L = sm.xl[h];
+              p.out[((size_t)b * geo.Hq + g * G + h) * DH + t] = f2bf(L > 0.f ? O[h] / L : 0.f);
             }
           }
         }
         if (t < G && p.lse != nullptr) {
-          float L = 0.f;
-          for (int rr = 0; rr < P.world; ++rr) L += __ldcg(parts + rr * xs + 16 * DH + t);
+          const float L = sm.xl[t];
           p.lse[(size_t)b * geo.Hq + g * G + t] = L > 0.f ? (sm.m2[t] + log2f(L)) * 0.6931471805599453f : neg_inf();
         }
+        if (t == 0) stamp_any(13);
       } else if (have_o) {
         if (P.mode == 1) {  // unnormalised partial of the owned tokens, fixed max m2
           if (t < DH) {

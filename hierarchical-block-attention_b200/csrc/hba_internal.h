@@ -12,11 +12,14 @@ constexpr int kShardMaxRanks = 8;
 
 // Exchange buffer of the fused shard decode (one per rank, IPC-mapped by the
 // others), for BH = B * Hkv (sequence, kv head) rows and `world` ranks:
-// two list regions [BH][world][32] of (score bits, block id), the (O, l)
-// partials [BH][world][16 * dh + 16] fp32, and the epoch flags
-// [3][BH][world] uint32 (exchanges: level-1 list, level-2 list, partials).
+// two list regions [BH][world][32] and the (O, l) partials
+// [BH][world][16 * dh + 16], all of self-validating 64-bit words -- a list
+// entry is (score bits | block id (16 bits) << 32 | epoch (16 bits) << 48),
+// a partial value (fp32 bits | epoch << 32) -- written by one aligned 64-bit
+// store each, so a reader that sees this step's epoch in a word has its data
+// (no fence, no flag).
 struct XLayout {
-  size_t list[2], parts, flags, total;
+  size_t list[2], parts, total;
 };
 __host__ __device__ inline XLayout x_layout(int BH, int world, int dh) {
   XLayout l;
@@ -26,9 +29,7 @@ __host__ __device__ inline XLayout x_layout(int BH, int world, int dh) {
     o += (size_t)BH * world * 32 * 8;
   }
   l.parts = o;
-  o += (size_t)BH * world * (16 * dh + 16) * 4;
-  l.flags = o;
-  o += (size_t)3 * BH * world * 4;
+  o += (size_t)BH * world * (16 * dh + 16) * 8;
   l.total = o;
   return l;
 }

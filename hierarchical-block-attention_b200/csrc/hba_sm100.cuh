@@ -76,27 +76,59 @@ HBA_DEVICE bool mbar_wait(uint64_t* bar, uint32_t parity, int* err) {
   return false;
 }
 
-// System-scope flag store / load (flags a peer GPU writes or reads over NVLink).
-HBA_DEVICE void st_release_sys(uint32_t* p, uint32_t v) {
-  asm volatile("st.release.sys.global.u32 [%0], %1;\n" ::"l"(p), "r"(v) : "memory");
+// 64-bit words another GPU writes over NVLink: single-copy-atomic relaxed
+// system-scope store / load (the load bypasses L1, which peers do not update).
+HBA_DEVICE void st_relaxed_sys(unsigned long long* p, unsigned long long v) {
+  asm volatile("st.relaxed.sys.global.u64 [%0], %1;\n" ::"l"(p), "l"(v) : "memory");
 }
-HBA_DEVICE uint32_t ld_acquire_sys(const uint32_t* p) {
-  uint32_t v;
-  asm volatile("ld.acquire.sys.global.u32 %0, [%1];\n" : "=r"(v) : "l"(p) : "memory");
+HBA_DEVICE unsigned long long ld_relaxed_sys(const unsigned long long* p) {
+  unsigned long long v;
+  asm volatile("ld.relaxed.sys.global.u64 %0, [%1];\n" : "=l"(v) : "l"(p) : "memory");
   return v;
 }
-// Bounded wait until the flag reaches epoch ep (flags only grow); false (and
-// *err set) after kWaitNs.
-HBA_DEVICE bool wait_flag(const uint32_t* p, uint32_t ep, int* err) {
-  if ((int)(ld_acquire_sys(p) - ep) >= 0) return true;
+// Bounded wait for N self-validating words p[i * stride] (i < N), loaded
+// together and re-polled while any lacks the tag; w[i] = the words.
+template <int N>
+HBA_DEVICE void wait_tagged_n(const unsigned long long* p, size_t stride, int n, int shift,
+                              unsigned long long mask, unsigned long long tag, unsigned long long (&w)[N], int* err) {
+  bool all = true;
+#pragma unroll
+  for (int i = 0; i < N; ++i) w[i] = i < n ? ld_relaxed_sys(p + i * stride) : 0ull;
+#pragma unroll
+  for (int i = 0; i < N; ++i)
+    if (i < n) all = all && ((w[i] >> shift) & mask) == tag;
+  if (all) return;
   const unsigned long long t0 = global_ns();
   for (uint32_t k = 1;; ++k) {
-    __nanosleep(64);
-    if ((int)(ld_acquire_sys(p) - ep) >= 0) return true;
+    __nanosleep(32);
+    all = true;
+#pragma unroll
+    for (int i = 0; i < N; ++i) {
+      if (i < n && ((w[i] >> shift) & mask) != tag) {
+        w[i] = ld_relaxed_sys(p + i * stride);
+        all = all && ((w[i] >> shift) & mask) == tag;
+      }
+    }
+    if (all) return;
     if ((k & 15) == 0 && global_ns() - t0 > kWaitNs) break;
   }
   if (err != nullptr) atomicExch(err, 1);
-  return false;
+}
+// Bounded wait for a self-validating word: until (word >> shift) & mask == tag;
+// returns the word (*err set after kWaitNs, the stale word returned).
+HBA_DEVICE unsigned long long wait_tagged(const unsigned long long* p, int shift, unsigned long long mask,
+                                          unsigned long long tag, int* err) {
+  unsigned long long v = ld_relaxed_sys(p);
+  if (((v >> shift) & mask) == tag) return v;
+  const unsigned long long t0 = global_ns();
+  for (uint32_t k = 1;; ++k) {
+    __nanosleep(32);
+    v = ld_relaxed_sys(p);
+    if (((v >> shift) & mask) == tag) return v;
+    if ((k & 15) == 0 && global_ns() - t0 > kWaitNs) break;
+  }
+  if (err != nullptr) atomicExch(err, 1);
+  return v;
 }
 
 // Shared-memory writes by threads must be made visible to the async proxy

@@ -215,8 +215,9 @@ int hba_b200_profile_events_recorded(void);
  * 0 kernel start, 1 after the query prologue, 2 after selection, 3 after the
  * union softmax, 4 end, 5-7 selection sub-phases, 8 / 9 / 10 the MMA warp
  * sees the first window tile / the last window-or-sink tile / the first
- * routed tile land, 11 last PV issued, 12 the producer sees the picks,
- * 13-15 spare (0).  The
+ * routed tile land, 11 last PV issued, 12 the producer sees the picks;
+ * fused shard decode: 14 / 15 the first / second list exchange complete,
+ * 13 the partial exchange complete.  The
  * prefill union kernel writes 16 stamps for the last query tile of each
  * (sequence, kv head) row r < bytes / 128 at buffer[r * 16 + i]: 0 start,
  * 1 chunk list built, 2 query tile ready, 3-7 and 8-12 the softmax of two
@@ -273,8 +274,9 @@ int hba_b200_decode_shard_finish(const hba_b200_config* cfg, int32_t batch, cons
  * the owned selection, the list exchanges and the union over the owned
  * tokens, exchanging with the same (sequence, kv head) CTA of every other
  * rank over NVLink through the ranks' exchange buffers -- each rank writes
- * its lists and its (O, l) partial into slot [rank] of every buffer and
- * releases an epoch flag there -- so there is no collective library call.
+ * its lists and its (O, l) partial into slot [rank] of every buffer as
+ * 64-bit words tagged with the step's epoch, and readers wait for the tag
+ * (no fence, no flag) -- so there is no collective library call.
  * Every rank returns the full out / lse / picks.
  *   xbuf_bytes   size of one rank's exchange buffer (-1 on bad arguments).
  *   peer_alloc   cudaMalloc + zero a buffer on the current device and write
@@ -286,7 +288,8 @@ int hba_b200_decode_shard_finish(const hba_b200_config* cfg, int32_t batch, cons
  *                start, bumped by the call on `stream` (every rank must make
  *                the same calls); dev_status is sticky (zero it once; 1 = a
  *                wait gave up, e.g. a rank that never arrived).  Bounds fall
- *                on block (hier: block * fanout) multiples; world <= 8.
+ *                on block (hier: block * fanout) multiples; world <= 8 and
+ *                world * n_cap_local / block < 65535 (16-bit block ids).
  * Every wait is bounded in time; a rank that never arrives turns into a
  * status, not a hang.
  */
