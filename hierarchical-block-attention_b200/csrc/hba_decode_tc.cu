@@ -502,6 +502,10 @@ __global__ void __launch_bounds__(kDtThreads, 1)
             cs = best * scale;
             ci = id_of(pg * PB + r);
           }
+          if (rg + 32 >= nr) {  // the page's last rows are scored: free its slot before the top-k work
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&sm.empty[i % NSLOT]);
+          }
           // keep the batch entries that can still reach the final top-k
           const float ts = __shfl_sync(0xffffffffu, ls, k - 1);
           const int ti = __shfl_sync(0xffffffffu, li, k - 1);
@@ -543,8 +547,6 @@ __global__ void __launch_bounds__(kDtThreads, 1)
           const float kts = __shfl_sync(0xffffffffu, ls, k - 1);
           if (lane == 0 && kth != INT_MAX) atomicMax(&sm.thr, order_key(kts));
         }
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&sm.empty[i % NSLOT]);
       }
     };
     int nsel = 0, NPb = 0;
