@@ -74,6 +74,10 @@ struct DtcSmem {
   float xl[16];  // fused shard: l of every head summed over the ranks
   float wl_s[kDtScoreWarps][32];  // per-warp top-k lists
   int wl_i[kDtScoreWarps][32];
+  float xs[kDtScoreWarps][32];    // a scoring warp's batch candidates and list, for its rank update
+  int xi[kDtScoreWarps][32];
+  float ys[kDtScoreWarps][32];
+  int yi[kDtScoreWarps][32];
   float sel_s[32];                // merged picks, best first
   int sel_i[32];
   int nsel;
@@ -513,36 +517,52 @@ __global__ void __launch_bounds__(kDtThreads, 1)
           const bool cand = beats(cs, ci, ts, ti) && order_key(cs) >= thr;
           const unsigned mask = __ballot_sync(0xffffffffu, cand);
           if (mask == 0u) continue;
-          const bool empty_list = __shfl_sync(0xffffffffu, li, 0) == INT_MAX;  // warp-uniform
-          if (empty_list) {  // the sorted batch is the list
-            warp_sort32(cs, ci);
-            ls = cs;
-            li = ci;
-          } else if (__popc(mask) > 6) {
-            if (!cand) {
-              cs = neg_inf();
-              ci = INT_MAX;
-            }
-            warp_sort32(cs, ci);
-            warp_merge32(ls, li, cs, ci);
-          } else {
-            for (unsigned mm = mask; mm; mm &= mm - 1) {
-              const int srcl = __ffs(mm) - 1;
-              const float xs = __shfl_sync(0xffffffffu, cs, srcl);
-              const int xi = __shfl_sync(0xffffffffu, ci, srcl);
-              const bool better = beats(xs, xi, ls, li);  // lanes above the insertion point
-              const int at = __popc(__ballot_sync(0xffffffffu, !better));
-              const float ps = __shfl_up_sync(0xffffffffu, ls, 1);
-              const int pi = __shfl_up_sync(0xffffffffu, li, 1);
-              if (lane == at) {
-                ls = xs;
-                li = xi;
-              } else if (lane > at) {
-                ls = ps;
-                li = pi;
-              }
-            }
+          // The list keeps its top k (lanes >= k: fillers).  Every entry gets
+          // its exact rank: an old one moves down by the candidates that beat
+          // it, a candidate counts the old entries ahead of it (binary search
+          // of the sorted list; entry k - 1 is behind it) and the candidates
+          // ahead of it.  The top k of list and batch, in a few steps (a
+          // bitonic sort of the batch costs ~2,600 cycles).
+          const int n = __popc(mask);
+          float* xs_ = sm.xs[sw];
+          int* xi_ = sm.xi[sw];
+          float* ys_ = sm.ys[sw];
+          int* yi_ = sm.yi[sw];
+          if (cand) {
+            const int at = __popc(mask & ((1u << lane) - 1u));
+            xs_[at] = cs;
+            xi_[at] = ci;
           }
+          ys_[lane] = ls;
+          yi_[lane] = li;
+          __syncwarp();
+          int opos = lane;
+          for (int j = 0; j < n; ++j) opos += beats(xs_[j], xi_[j], ls, li);
+          int npos = k;
+          float ns = 0.f;
+          int ni = 0;
+          if (lane < n) {
+            ns = xs_[lane];
+            ni = xi_[lane];
+            int lo = 0;
+#pragma unroll
+            for (int step = 16; step > 0; step >>= 1)
+              if (lo + step <= k && beats(ys_[lo + step - 1], yi_[lo + step - 1], ns, ni)) lo += step;
+            for (int j = 0; j < n; ++j) lo += beats(xs_[j], xi_[j], ns, ni);
+            npos = lo;
+          }
+          __syncwarp();
+          if (lane < k && opos < k) {
+            ys_[opos] = ls;
+            yi_[opos] = li;
+          }
+          if (npos < k) {
+            ys_[npos] = ns;
+            yi_[npos] = ni;
+          }
+          __syncwarp();
+          ls = lane < k ? ys_[lane] : neg_inf();
+          li = lane < k ? yi_[lane] : INT_MAX;
           const int kth = __shfl_sync(0xffffffffu, li, k - 1);
           const float kts = __shfl_sync(0xffffffffu, ls, k - 1);
           if (lane == 0 && kth != INT_MAX) atomicMax(&sm.thr, order_key(kts));
