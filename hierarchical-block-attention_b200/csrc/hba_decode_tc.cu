@@ -460,7 +460,7 @@ __global__ void __launch_bounds__(kDtThreads, 1)
             float best = neg_inf();
             for (int sl = 0; sl < m_slots; ++sl) {
               float t0 = 0.f, t1 = 0.f, t2 = 0.f, t3 = 0.f;  // pending sums of the pairwise tree
-#pragma unroll
+#pragma unroll 8  // dh 128: a full unroll of the 16 vectors needs 255 registers and spills
               for (int q = 0; q < LPS; ++q) {
                 const int vq = q ^ o;
                 float f[8];
