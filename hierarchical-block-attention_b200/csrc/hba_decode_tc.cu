@@ -458,50 +458,105 @@ __global__ void __launch_bounds__(kDtThreads, 1)
           if (r < nr) {
             const unsigned char* row = src + (size_t)r * row_bytes;
             float best = neg_inf();
-            for (int sl = 0; sl < m_slots; ++sl) {
-              float t0 = 0.f, t1 = 0.f, t2 = 0.f, t3 = 0.f;  // pending sums of the pairwise tree
-#pragma unroll 8  // dh 128: a full unroll of the 16 vectors needs 255 registers and spills
-              for (int q = 0; q < LPS; ++q) {
-                const int vq = q ^ o;
-                float f[8];
-                unpack8(*reinterpret_cast<const uint4*>(row + (sl * LPS + vq) * 16), f);
-                float qv[8];
-                if constexpr (kQgRegs) {
+            if constexpr (DH == 64) {
+              for (int sl = 0; sl < m_slots; ++sl) {
+                float t0 = 0.f, t1 = 0.f, t2 = 0.f, t3 = 0.f;  // pending sums of the pairwise tree
 #pragma unroll
-                  for (int jj = 0; jj < 8; ++jj) qv[jj] = qgp[q][jj];
-                } else {
-                  const float4 qa = *reinterpret_cast<const float4*>(&sm.qg[vq * 8]);
-                  const float4 qb = *reinterpret_cast<const float4*>(&sm.qg[vq * 8 + 4]);
-                  qv[0] = qa.x, qv[1] = qa.y, qv[2] = qa.z, qv[3] = qa.w;
-                  qv[4] = qb.x, qv[5] = qb.y, qv[6] = qb.z, qv[7] = qb.w;
-                }
-                float part = 0.f;
+                for (int q = 0; q < LPS; q += 2) {
+                  // vectors q, q + 1: two independent chains in packed f32x2 fmas
+                  // (each half is the fmaf chain)
+                  float f0[8], f1[8], qv0[8], qv1[8];
+                  unpack8(*reinterpret_cast<const uint4*>(row + (sl * LPS + (q ^ o)) * 16), f0);
+                  unpack8(*reinterpret_cast<const uint4*>(row + (sl * LPS + ((q + 1) ^ o)) * 16), f1);
+                  if constexpr (kQgRegs) {
 #pragma unroll
-                for (int jj = 0; jj < 8; ++jj) part = fmaf(f[jj], qv[jj], part);
-                // fold into the tree as the vectors arrive: ((p0+p1)+(p2+p3))+...
-                if ((q & 1) == 0) {
-                  t0 = part;
-                } else {
-                  const float l1 = t0 + part;
-                  if ((q & 2) == 0) {
-                    t1 = l1;
+                    for (int jj = 0; jj < 8; ++jj) {
+                      qv0[jj] = qgp[q][jj];
+                      qv1[jj] = qgp[q + 1][jj];
+                    }
                   } else {
-                    const float l2 = t1 + l1;
-                    if ((q & 4) == 0) {
-                      t2 = l2;
+                    const float4 qa = *reinterpret_cast<const float4*>(&sm.qg[(q ^ o) * 8]);
+                    const float4 qb = *reinterpret_cast<const float4*>(&sm.qg[(q ^ o) * 8 + 4]);
+                    const float4 qc2 = *reinterpret_cast<const float4*>(&sm.qg[((q + 1) ^ o) * 8]);
+                    const float4 qd = *reinterpret_cast<const float4*>(&sm.qg[((q + 1) ^ o) * 8 + 4]);
+                    qv0[0] = qa.x, qv0[1] = qa.y, qv0[2] = qa.z, qv0[3] = qa.w;
+                    qv0[4] = qb.x, qv0[5] = qb.y, qv0[6] = qb.z, qv0[7] = qb.w;
+                    qv1[0] = qc2.x, qv1[1] = qc2.y, qv1[2] = qc2.z, qv1[3] = qc2.w;
+                    qv1[4] = qd.x, qv1[5] = qd.y, qv1[6] = qd.z, qv1[7] = qd.w;
+                  }
+                  float p0 = 0.f, p1 = 0.f;
+#pragma unroll
+                  for (int jj = 0; jj < 8; ++jj) fma2(p0, p1, f0[jj], f1[jj], qv0[jj], qv1[jj]);
+                  t0 = p0;
+                  const float part = p1;
+                  {
+                    const float l1 = t0 + part;
+                    if ((q & 2) == 0) {
+                      t1 = l1;
                     } else {
-                      const float l3 = t2 + l2;
-                      if (LPS == 8) {
-                        best = fmaxf(best, l3);
-                      } else if ((q & 8) == 0) {
-                        t3 = l3;
+                      const float l2 = t1 + l1;
+                      if ((q & 4) == 0) {
+                        t2 = l2;
                       } else {
-                        best = fmaxf(best, t3 + l3);
+                        const float l3 = t2 + l2;
+                        if (LPS == 8) {
+                          best = fmaxf(best, l3);
+                        } else if ((q & 8) == 0) {
+                          t3 = l3;
+                        } else {
+                          best = fmaxf(best, t3 + l3);
+                        }
                       }
                     }
                   }
                 }
               }
+            } else {
+              for (int sl = 0; sl < m_slots; ++sl) {
+                float t0 = 0.f, t1 = 0.f, t2 = 0.f, t3 = 0.f;  // pending sums of the pairwise tree
+#pragma unroll 8  // dh 128: a full unroll of the 16 vectors needs 255 registers and spills
+                for (int q = 0; q < LPS; ++q) {
+                  const int vq = q ^ o;
+                  float f[8];
+                  unpack8(*reinterpret_cast<const uint4*>(row + (sl * LPS + vq) * 16), f);
+                  float qv[8];
+                  if constexpr (kQgRegs) {
+#pragma unroll
+                    for (int jj = 0; jj < 8; ++jj) qv[jj] = qgp[q][jj];
+                  } else {
+                    const float4 qa = *reinterpret_cast<const float4*>(&sm.qg[vq * 8]);
+                    const float4 qb = *reinterpret_cast<const float4*>(&sm.qg[vq * 8 + 4]);
+                    qv[0] = qa.x, qv[1] = qa.y, qv[2] = qa.z, qv[3] = qa.w;
+                    qv[4] = qb.x, qv[5] = qb.y, qv[6] = qb.z, qv[7] = qb.w;
+                  }
+                  float part = 0.f;
+#pragma unroll
+                  for (int jj = 0; jj < 8; ++jj) part = fmaf(f[jj], qv[jj], part);
+                  // fold into the tree as the vectors arrive: ((p0+p1)+(p2+p3))+...
+                  if ((q & 1) == 0) {
+                    t0 = part;
+                  } else {
+                    const float l1 = t0 + part;
+                    if ((q & 2) == 0) {
+                      t1 = l1;
+                    } else {
+                      const float l2 = t1 + l1;
+                      if ((q & 4) == 0) {
+                        t2 = l2;
+                      } else {
+                        const float l3 = t2 + l2;
+                        if (LPS == 8) {
+                          best = fmaxf(best, l3);
+                        } else if ((q & 8) == 0) {
+                          t3 = l3;
+                        } else {
+                          best = fmaxf(best, t3 + l3);
+                        }
+                      }
+                    }
+                  }
+                }
+            }
             }
             cs = best * scale;
             ci = id_of(pg * PB + r);
