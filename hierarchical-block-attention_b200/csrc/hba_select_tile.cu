@@ -138,8 +138,8 @@ __global__ void __launch_bounds__(kTsThreads, 1) select_tile_kernel(SelParams p,
     for (int j = 0; j < 2; ++j) jr[j] = min(2 * bgrp + j, nblk - 1);
     for (int sl = 0; sl < m; ++sl) {
       float a[4][2], s1[4][2], s2[4][2], s3[4][2];
-#pragma unroll 4
-      for (int v = 0; v < VPR; ++v) {  // by 4: the low tree-position bits are static
+#pragma unroll 2  // (by 4: 128 registers and a spill)
+      for (int v = 0; v < VPR; ++v) {
         float sf[2][8];
 #pragma unroll
         for (int j = 0; j < 2; ++j)
