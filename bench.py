@@ -11,14 +11,16 @@ routed blocks) for a batch of 64 sequences with 32K cached tokens each
 hba_b200_decode with the cache resident in HBM; L2 is flushed (a 256 MB
 write) before every timed step, outside the timed events.  `value` is decode
 queries/s over all ranks (each rank decodes its own batch: weak scaling).
-`e2e` is the same step through the C-ABI call with the query copied from
-pinned host memory and the output + LSE copied back, inside the timed region
-(the three captured as one CUDA graph, as a serving loop runs a step).
-The secondary lines measure config 3 (hierarchical decode at 128K) and
-config 2 (prefill at 32K), and with N > 1 ranks config 3 with every 128K
-context sharded by token range over the N GPUs (one batch of 32 sequences,
-strong scaling; NCCL all-gathers of the per-rank top-k lists and one
-all-reduce of the softmax partials per step).  `--impl reference` times the CPU oracle port (the
+`e2e` is the same step through the C-ABI call with the query in pinned host
+memory and the output + LSE delivered to pinned host memory inside the timed
+region: the decode kernel reads and writes the mapped host buffers directly
+(zero-copy, one graph node); `e2e.copy_variant` is the same step with an
+explicit H2D copy of q and D2H copy of out + LSE around the kernel (three
+graph nodes).  The secondary lines measure config 3 (hierarchical decode at
+128K) and config 2 (prefill at 32K), and with N > 1 ranks config 3 with every
+128K context sharded by token range over the N GPUs (one batch of 32
+sequences, strong scaling; the fused kernel exchanges the per-rank top-k
+lists and softmax partials over NVLink).  `--impl reference` times the CPU oracle port (the
 reference algorithm restated in numpy) on the host cores instead.
 """
 
@@ -344,9 +346,35 @@ def decode_bench(name, steps, warmup, world, rank, local, pk):
     with torch.cuda.graph(g_e2e):
         step_e2e_body()
     e2e_times, _ = timed_steps(g_e2e.replay, steps, warmup, flush, world, dev, local)
-    e2e_ms = max_over_ranks(statistics.mean(e2e_times), world, dev)
+    e2e_copy_ms = max_over_ranks(statistics.mean(e2e_times), world, dev)
     # the copied-back result is the device result
     assert torch.equal(io_host[:ob].view(out.dtype).view(out.shape), out_e.cpu())
+
+    # e2e, zero-copy (the headline): q sits in mapped pinned host memory and
+    # the decode kernel reads it from there and writes out + lse back into it
+    # -- the step's host -> device and device -> host traffic with no copy
+    # launch around the kernel (hba_b200_host_alloc)
+    from hba_b200.hostio import MappedHostBuffer
+    qbytes = q.numel() * q.element_size()
+    hbuf = MappedHostBuffer(qbytes + ob + lb)
+    hbuf.host_view(q.dtype, q.shape).copy_(q_host)
+    out_z = hbuf.host_view(out.dtype, out.shape, offset=qbytes)
+    q_d, out_d, lse_d = hbuf.device_view(0), hbuf.device_view(qbytes), hbuf.device_view(qbytes + ob)
+
+    def step_zero_copy():
+        cache.decode_into(q_d, out_d, lse_d, stream=stream_of(dev))
+
+    step_zero_copy()
+    torch.cuda.synchronize()
+    g_zc = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g_zc):
+        step_zero_copy()
+    zc_times, _ = timed_steps(g_zc.replay, steps, warmup, flush, world, dev, local)
+    e2e_ms = max_over_ranks(statistics.mean(zc_times), world, dev)
+    torch.cuda.synchronize()
+    assert torch.equal(out_z, out_e.cpu())  # the host-written result is the device result
+    del g_zc
+    hbuf.close()
 
     res = dict(
         metric=METRIC, value=B * world / (t_ms * 1e-3), unit="decode queries/s", n_gpus=world, steps=steps,
@@ -369,7 +397,11 @@ def decode_bench(name, steps, warmup, world, rank, local, pk):
         cache_build_s=build_s,
         e2e=dict(value=B * world / (e2e_ms * 1e-3), unit="decode queries/s", ms_per_step=e2e_ms,
                  h2d_bytes_per_step=q.numel() * q.element_size(), d2h_bytes_per_step=ob + lb,
-                 timing="one CUDA graph per step: pinned H2D of q, hba_b200_decode, D2H of out + lse"),
+                 timing="one CUDA graph per step: hba_b200_decode reading q from and writing out + lse to "
+                        "mapped pinned host memory (zero-copy; hba_b200_host_alloc)",
+                 copy_variant=dict(value=B * world / (e2e_copy_ms * 1e-3), ms_per_step=e2e_copy_ms,
+                                   timing="one CUDA graph per step: pinned H2D of q, hba_b200_decode, "
+                                          "D2H of out + lse")),
         gpu_launches=steps * (len(kt) + 0),
         clocks=clocks,
     )

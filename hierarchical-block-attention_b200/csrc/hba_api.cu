@@ -721,6 +721,22 @@ int hba_b200_decode_shard_finish(const hba_b200_config* cfg, int32_t batch, cons
                                               static_cast<__nv_bfloat16*>(out), lse, stream));
 }
 
+int hba_b200_host_alloc(int64_t bytes, void** host_ptr, void** dev_ptr) {
+  if (bytes <= 0 || host_ptr == nullptr || dev_ptr == nullptr) return HBA_B200_ERR_INVALID_ARGUMENT;
+  *host_ptr = nullptr;
+  *dev_ptr = nullptr;
+  cudaError_t e = cudaHostAlloc(host_ptr, (size_t)bytes, cudaHostAllocMapped);
+  if (e == cudaSuccess) e = cudaHostGetDevicePointer(dev_ptr, *host_ptr, 0);
+  if (e != cudaSuccess && *host_ptr != nullptr) {
+    cudaFreeHost(*host_ptr);
+    *host_ptr = nullptr;
+    *dev_ptr = nullptr;
+  }
+  return cuda_status(e);
+}
+
+int hba_b200_host_free(void* host_ptr) { return host_ptr == nullptr ? HBA_B200_OK : cuda_status(cudaFreeHost(host_ptr)); }
+
 int64_t hba_b200_shard_xbuf_bytes(const hba_b200_config* cfg, int32_t batch, int32_t world) {
   int st = HBA_B200_OK;
   if (!config_ok(cfg, &st) || batch <= 0 || world < 1 || world > hba::kShardMaxRanks) return -1;

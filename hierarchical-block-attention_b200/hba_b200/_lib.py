@@ -70,6 +70,8 @@ SIGNATURES = {
                                                     _P, _P, _P, _I32, _P, _P, _P, _P, _P, _P, _P]),
     "hba_b200_decode_shard_finish": (ctypes.c_int, [_CFG, _I32, _P, _P, _P, _P, _P, _P]),
     "hba_b200_shard_xbuf_bytes": (_I64, [_CFG, _I32, _I32]),
+    "hba_b200_host_alloc": (ctypes.c_int, [_I64, ctypes.POINTER(ctypes.c_void_p), ctypes.POINTER(ctypes.c_void_p)]),
+    "hba_b200_host_free": (ctypes.c_int, [_P]),
     "hba_b200_peer_alloc": (ctypes.c_int, [_I64, ctypes.POINTER(ctypes.c_void_p), _P]),
     "hba_b200_peer_open": (ctypes.c_int, [_P, ctypes.POINTER(ctypes.c_void_p)]),
     "hba_b200_peer_close": (ctypes.c_int, [_P]),

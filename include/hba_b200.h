@@ -294,6 +294,18 @@ int hba_b200_decode_shard_finish(const hba_b200_config* cfg, int32_t batch, cons
  * status, not a hang.
  */
 int64_t hba_b200_shard_xbuf_bytes(const hba_b200_config* cfg, int32_t batch, int32_t world);
+
+/*
+ * Zero-copy host I/O (no counterpart in the reference): pinned host memory
+ * mapped into the device address space (cudaHostAlloc mapped; dev_ptr from
+ * cudaHostGetDevicePointer, so an unmapped pointer is a host-side error).
+ * hba_b200_decode / _decode_noalloc accept dev_ptr for q, out and lse: the
+ * decode kernel then reads the query from and writes the result to host
+ * memory directly, with no copy before or after the launch -- the serving
+ * path for a decode step whose I/O is a few hundred KB.
+ */
+int hba_b200_host_alloc(int64_t bytes, void** host_ptr, void** dev_ptr);
+int hba_b200_host_free(void* host_ptr);
 int hba_b200_peer_alloc(int64_t bytes, void** dptr, void* ipc_handle);
 int hba_b200_peer_open(const void* ipc_handle, void** dptr);
 int hba_b200_peer_close(void* dptr);

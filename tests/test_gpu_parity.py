@@ -315,3 +315,35 @@ def test_baseline_cfg2_prefill_full_size_sampled_rows():
     rows = H.sample_rows(32768, 16, seed=3)
     eo, el, out, lse, _ = H.check_prefill(cfg, 4, 32768, False, seed=32, rows=rows, gains=False)
     assert torch.isfinite(out.float()).all() and torch.isfinite(lse).all()
+
+
+@pytest.mark.parametrize("hier", [False, True])
+def test_decode_zero_copy_host_io(hier):
+    # q read from, out / lse written to mapped pinned host memory by the
+    # decode kernel itself: the same bytes as the device-buffer decode
+    from hba_b200.hostio import MappedHostBuffer
+    cfg = H.cfg_of(n_heads=14, n_kv=2, head_dim=64) if not hier else \
+        H.cfg_of(n_heads=32, n_kv=8, head_dim=128, fanout=16, beam=8)
+    B, n = 8, 4096 + 37
+    summ, qkn = synth.make_weights(cfg, "cuda", seed=11, gains=True)
+    cos, sin = synth.rope_tables(n + cfg.block, cfg.head_dim, 1e6)  # the cache rounds its capacity up to a block
+    wl = synth.decode_workload(cfg, B, n, hier=hier, seed=11, qkn=qkn, planted=8)
+    cache = HBADecodeCache(cfg, B, n, summ, qkn, cos, sin, hier=hier)
+    cache.append(wl["k"], wl["v"])
+    q = wl["q"].contiguous()
+    out_d, lse_d = cache.attend(q, return_lse=True)
+    qb, ob, lb = q.numel() * 2, q.numel() * 2, B * cfg.n_heads * 4
+    buf = MappedHostBuffer(qb + ob + lb)
+    try:
+        buf.host_view(torch.bfloat16, q.shape).copy_(q.cpu())
+        out_h = buf.host_view(torch.bfloat16, q.shape, offset=qb)
+        lse_h = buf.host_view(torch.float32, (B, cfg.n_heads), offset=qb + ob)
+        out_h.zero_()
+        lse_h.zero_()
+        cache.decode_into(buf.device_view(0), buf.device_view(qb), buf.device_view(qb + ob))
+        torch.cuda.synchronize()
+        assert torch.equal(out_h, out_d.cpu())
+        assert torch.equal(lse_h, lse_d.cpu())
+        assert cache.device_status() == 0
+    finally:
+        buf.close()
