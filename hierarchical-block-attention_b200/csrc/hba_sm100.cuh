@@ -114,22 +114,6 @@ HBA_DEVICE void wait_tagged_n(const unsigned long long* p, size_t stride, int n,
   }
   if (err != nullptr) atomicExch(err, 1);
 }
-// Bounded wait for a self-validating word: until (word >> shift) & mask == tag;
-// returns the word (*err set after kWaitNs, the stale word returned).
-HBA_DEVICE unsigned long long wait_tagged(const unsigned long long* p, int shift, unsigned long long mask,
-                                          unsigned long long tag, int* err) {
-  unsigned long long v = ld_relaxed_sys(p);
-  if (((v >> shift) & mask) == tag) return v;
-  const unsigned long long t0 = global_ns();
-  for (uint32_t k = 1;; ++k) {
-    __nanosleep(32);
-    v = ld_relaxed_sys(p);
-    if (((v >> shift) & mask) == tag) return v;
-    if ((k & 15) == 0 && global_ns() - t0 > kWaitNs) break;
-  }
-  if (err != nullptr) atomicExch(err, 1);
-  return v;
-}
 
 // Shared-memory writes by threads must be made visible to the async proxy
 // (TMA, tensor cores) before the consumer is signalled.
