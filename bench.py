@@ -215,6 +215,8 @@ def shard_bench(name, steps, warmup, world, rank, local, pk):
     sh.capture(q, out, lse)  # the step as one CUDA graph: epoch bump + the fused shard kernel
     times, clocks = timed_steps(sh.replay, steps, warmup, flush, world, dev, local)
     t_ms = max_over_ranks(statistics.mean(times), world, dev)
+    torch.cuda.synchronize(dev)
+    status = int(sh.status.item())  # sticky: 1 if any wait of any step gave up
     sh.close()
     res = dict(
         metric=METRIC, value=B / (t_ms * 1e-3), unit="decode queries/s", n_gpus=world, steps=steps, warmup=warmup,
@@ -229,8 +231,11 @@ def shard_bench(name, steps, warmup, world, rank, local, pk):
                     parallelism=f"kv-range shards x{world} (top-k lists and (O, l) partials exchanged inside the "
                                 "decode kernel over NVLink peer memory; no collective library call)"),
         gpu_launches=steps * 2,
+        device_status=status,
         clocks=clocks,
     )
+    if status != 0:
+        res["error"] = f"device status {status} on rank {rank}: a bounded wait gave up"
     del sh
     torch.cuda.empty_cache()
     return res

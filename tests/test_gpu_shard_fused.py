@@ -4,7 +4,7 @@ run `HBAShardedDecode` on its default GPU path -- one
 partials exchanged through the ranks' IPC-mapped buffers inside the kernel.
 Every rank's picks must equal the one-GPU decode's exactly and its output /
 LSE must agree within the parity tolerances, over several steps (eager, then
-as a replayed CUDA graph) and across an append.  Needs 2 GPUs."""
+as a replayed CUDA graph) and across an append.  Needs 2 (and, for the 4-rank cases, 4) GPUs."""
 
 import os
 import socket
@@ -97,12 +97,13 @@ def _one_gpu(cfg, hier, n, wl, summ, qkn, cos, sin):
     return a, b
 
 
-@pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+@pytest.mark.parametrize("world", [2, 4])
 @pytest.mark.parametrize("hier,n", [(False, CAP - 64), (False, CAP // 2 + 512), (True, CAP - 1024),
                                     (True, CAP // 2 + 512)])
-def test_shard_fused_world2(tmp_path, hier, n):
-    # n = CAP // 2 + 512: the 1024-token window straddles the two ranks
-    world = 2
+def test_shard_fused(tmp_path, hier, n, world):
+    # n = CAP // 2 + 512: the 1024-token window straddles two ranks
+    if not torch.cuda.is_available() or torch.cuda.device_count() < world:
+        pytest.skip(f"needs {world} GPUs")
     mp.spawn(_rank, args=(world, _port(), str(tmp_path), hier, n), nprocs=world, join=True)
     cfg = _cfg(hier)
     summ, qkn, cos, sin, wl = _workload(cfg, hier, n, "cuda")
