@@ -38,7 +38,9 @@ constexpr int kTsStageBytes = 65536;  // kTsB rows of m * dh bf16 (m * dh <= 512
 template <int DH>
 struct TsSmem {
   alignas(1024) unsigned char stage[2][kTsStageBytes];
-  alignas(16) float4 qg[kTsQ][DH / 4];  // fp32 routing queries; 16-byte chunk c of row r at c ^ ((r >> 2) & 7)
+  // bf16 routing queries: 16-byte chunk c (elements 8c .. 8c+7) of row r at c ^ ((r >> 2) & 7); one
+  // 128-bit load per query vector (a 128-bit shared load costs a wavefront per quarter-warp)
+  alignas(16) uint4 qg[kTsQ][DH / 8];
   float sc[kTsQ][kTsB + 1];
   float ls[kTsQ][32];  // per-query running best 32 (score desc, block asc)
   int li[kTsQ][32];
@@ -104,11 +106,11 @@ __global__ void __launch_bounds__(kTsThreads, 1) select_tile_kernel(SelParams p,
         for (int e = 0; e < PER; ++e) acc[e] += v[e];
       }
     }
-    // lane holds elements lane*PER .. +PER of the row: qg = bf16(sum), kept as fp32
+    // lane holds elements lane*PER .. +PER of the row: qg = bf16(sum)
     const int d0 = lane * PER;
-    float* dst = reinterpret_cast<float*>(&sm.qg[r][(d0 / 4) ^ ((r >> 2) & 7)]) + (d0 % 4);
+    __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(&sm.qg[r][(d0 / 8) ^ ((r >> 2) & 7)]) + (d0 % 8);
 #pragma unroll
-    for (int e = 0; e < PER; ++e) dst[e] = round_bf16(acc[e]);
+    for (int e = 0; e < PER; ++e) dst[e] = __float2bfloat16_rn(acc[e]);
   }
   __syncthreads();
 
@@ -148,8 +150,8 @@ __global__ void __launch_bounds__(kTsThreads, 1) select_tile_kernel(SelParams p,
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
           const int r = 4 * qgrp + i;
-          const float4 qa = sm.qg[r][(2 * v) ^ qsw], qb = sm.qg[r][(2 * v + 1) ^ qsw];
-          const float qf[8] = {qa.x, qa.y, qa.z, qa.w, qb.x, qb.y, qb.z, qb.w};
+          float qf[8];
+          unpack8(sm.qg[r][v ^ qsw], qf);
           // the two blocks' chains side by side: each half is the fmaf chain
           float p0 = 0.f, p1 = 0.f;
 #pragma unroll
