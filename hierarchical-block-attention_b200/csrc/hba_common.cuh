@@ -43,6 +43,28 @@ HBA_DEVICE void fma2(float& x, float& y, float a0, float a1, float b0, float b1)
   asm("mov.b64 {%0, %1}, %2;" : "=f"(x), "=f"(y) : "l"(d));
 }
 
+// The 8-term fma chain from 0 over two 16-byte vectors of 8 bf16 each, in
+// element order (element 2k is the low half of word k): the same value as
+// unpack8 of both and fmaf(a[e], b[e], acc) for e = 0..7, since sm_100's
+// mixed-precision fma.rn.f32.bf16 widens its bf16 operands exactly and
+// rounds a * b + c once -- without the widening instructions.
+HBA_DEVICE float dot8_bf16(uint4 a, uint4 b) {
+  float d;
+  asm("{\n"
+      " .reg .b16 a0, a1, a2, a3, a4, a5, a6, a7, b0, b1, b2, b3, b4, b5, b6, b7;\n"
+      " mov.b32 {a0, a1}, %1;\n mov.b32 {a2, a3}, %2;\n mov.b32 {a4, a5}, %3;\n mov.b32 {a6, a7}, %4;\n"
+      " mov.b32 {b0, b1}, %5;\n mov.b32 {b2, b3}, %6;\n mov.b32 {b4, b5}, %7;\n mov.b32 {b6, b7}, %8;\n"
+      " mov.b32 %0, 0;\n"
+      " fma.rn.f32.bf16 %0, a0, b0, %0;\n fma.rn.f32.bf16 %0, a1, b1, %0;\n"
+      " fma.rn.f32.bf16 %0, a2, b2, %0;\n fma.rn.f32.bf16 %0, a3, b3, %0;\n"
+      " fma.rn.f32.bf16 %0, a4, b4, %0;\n fma.rn.f32.bf16 %0, a5, b5, %0;\n"
+      " fma.rn.f32.bf16 %0, a6, b6, %0;\n fma.rn.f32.bf16 %0, a7, b7, %0;\n"
+      "}\n"
+      : "=f"(d)
+      : "r"(a.x), "r"(a.y), "r"(a.z), "r"(a.w), "r"(b.x), "r"(b.y), "r"(b.z), "r"(b.w));
+  return d;
+}
+
 HBA_DEVICE uint32_t pack_bf16x2(float lo, float hi) {
   __nv_bfloat162 h = __floats2bfloat162_rn(lo, hi);
   return *reinterpret_cast<uint32_t*>(&h);

@@ -142,22 +142,16 @@ __global__ void __launch_bounds__(kTsThreads, 1) select_tile_kernel(SelParams p,
       float a[4][2], s1[4][2], s2[4][2], s3[4][2];
 #pragma unroll 2  // (by 4: 128 registers and a spill)
       for (int v = 0; v < VPR; ++v) {
-        float sf[2][8];
+        uint4 sw[2];
 #pragma unroll
         for (int j = 0; j < 2; ++j)
-          unpack8(*reinterpret_cast<const uint4*>(st + (size_t)jr[j] * row_bytes + (sl * VPR + v) * 16), sf[j]);
+          sw[j] = *reinterpret_cast<const uint4*>(st + (size_t)jr[j] * row_bytes + (sl * VPR + v) * 16);
         float pv[4][2];
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
-          const int r = 4 * qgrp + i;
-          float qf[8];
-          unpack8(sm.qg[r][v ^ qsw], qf);
-          // the two blocks' chains side by side: each half is the fmaf chain
-          float p0 = 0.f, p1 = 0.f;
+          const uint4 qw = sm.qg[4 * qgrp + i][v ^ qsw];
 #pragma unroll
-          for (int e = 0; e < 8; ++e) fma2(p0, p1, sf[0][e], sf[1][e], qf[e], qf[e]);
-          pv[i][0] = p0;
-          pv[i][1] = p1;
+          for (int j = 0; j < 2; ++j) pv[i][j] = dot8_bf16(sw[j], qw);  // the 8-term fmaf chain
         }
         // pairwise tree over the slot's vectors, built as they arrive
 #pragma unroll
