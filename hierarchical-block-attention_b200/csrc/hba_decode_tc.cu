@@ -68,7 +68,7 @@ struct DtcSmem {
   alignas(1024) unsigned char qc[HALVES][16 * 128];         // Q rows (16 heads) [16 x 64] SW128 per half
   alignas(1024) unsigned char qr[HALVES][16 * 128];
   alignas(1024) unsigned char pt[2][2][16 * 128];           // P^T [buffer][key half][16 heads x 64 keys]
-  float qg[DH];
+  alignas(16) __nv_bfloat16 qg[DH];  // routing query (bf16 values), read as packed 16-byte vectors
   float m2[16];
   float lsum[4][16];
   float xl[16];  // fused shard: l of every head summed over the ranks
@@ -406,7 +406,7 @@ __global__ void __launch_bounds__(kDtThreads, 1)
     for (int d = sw * 32 + lane; d < DH; d += NSW * 32) {
       float acc = 0.f;
       for (int h = 0; h < G; ++h) acc += bf2f(*reinterpret_cast<const __nv_bfloat16*>(sm.qc[d / 64] + sw128_offset(h, d % 64)));
-      sm.qg[d] = round_bf16(acc);
+      sm.qg[d] = __float2bfloat16_rn(acc);
     }
     if constexpr (HB < 16) {  // P^T rows of heads >= HB stay zero for the whole kernel
       // 4 tiles [buffer][key half] of 16 rows x 128 B; rows 8-15 = the second
@@ -430,15 +430,18 @@ __global__ void __launch_bounds__(kDtThreads, 1)
     // (score desc, id asc) in registers: a 32-row batch that beats the k-th
     // entry is bitonic-sorted and merged in.
     constexpr int LPS = DH / 8;  // 16-byte vectors per slot
+    // dh 64: the query in fp32 registers and two vectors' chains in packed
+    // f32x2 fmas.  dh 128: each 8-term chain is dot8_bf16 (mixed-precision
+    // fmas on the packed bf16 halves, the same value as the fp32 fmaf chain
+    // over the widened vectors); measured, each form is the faster one for
+    // its head size.
     constexpr bool kQgRegs = DH == 64;  // this lane's permuted copy of qg in registers
     const int m_slots = geo.m;
     const int o = lane & 7;
     float qgp[kQgRegs ? LPS : 1][8];
     if constexpr (kQgRegs) {
 #pragma unroll
-      for (int q = 0; q < LPS; ++q)
-#pragma unroll
-        for (int jj = 0; jj < 8; ++jj) qgp[q][jj] = sm.qg[(q ^ o) * 8 + jj];
+      for (int q = 0; q < LPS; ++q) unpack8(*reinterpret_cast<const uint4*>(&sm.qg[(q ^ o) * 8]), qgp[q]);
     }
     float ls = neg_inf();
     int li = INT_MAX;
@@ -465,28 +468,12 @@ __global__ void __launch_bounds__(kDtThreads, 1)
                 for (int q = 0; q < LPS; q += 2) {
                   // vectors q, q + 1: two independent chains in packed f32x2 fmas
                   // (each half is the fmaf chain)
-                  float f0[8], f1[8], qv0[8], qv1[8];
+                  float f0[8], f1[8];
                   unpack8(*reinterpret_cast<const uint4*>(row + (sl * LPS + (q ^ o)) * 16), f0);
                   unpack8(*reinterpret_cast<const uint4*>(row + (sl * LPS + ((q + 1) ^ o)) * 16), f1);
-                  if constexpr (kQgRegs) {
-#pragma unroll
-                    for (int jj = 0; jj < 8; ++jj) {
-                      qv0[jj] = qgp[q][jj];
-                      qv1[jj] = qgp[q + 1][jj];
-                    }
-                  } else {
-                    const float4 qa = *reinterpret_cast<const float4*>(&sm.qg[(q ^ o) * 8]);
-                    const float4 qb = *reinterpret_cast<const float4*>(&sm.qg[(q ^ o) * 8 + 4]);
-                    const float4 qc2 = *reinterpret_cast<const float4*>(&sm.qg[((q + 1) ^ o) * 8]);
-                    const float4 qd = *reinterpret_cast<const float4*>(&sm.qg[((q + 1) ^ o) * 8 + 4]);
-                    qv0[0] = qa.x, qv0[1] = qa.y, qv0[2] = qa.z, qv0[3] = qa.w;
-                    qv0[4] = qb.x, qv0[5] = qb.y, qv0[6] = qb.z, qv0[7] = qb.w;
-                    qv1[0] = qc2.x, qv1[1] = qc2.y, qv1[2] = qc2.z, qv1[3] = qc2.w;
-                    qv1[4] = qd.x, qv1[5] = qd.y, qv1[6] = qd.z, qv1[7] = qd.w;
-                  }
                   float p0 = 0.f, p1 = 0.f;
 #pragma unroll
-                  for (int jj = 0; jj < 8; ++jj) fma2(p0, p1, f0[jj], f1[jj], qv0[jj], qv1[jj]);
+                  for (int jj = 0; jj < 8; ++jj) fma2(p0, p1, f0[jj], f1[jj], qgp[q][jj], qgp[q + 1][jj]);
                   t0 = p0;
                   const float part = p1;
                   {
@@ -514,24 +501,11 @@ __global__ void __launch_bounds__(kDtThreads, 1)
             } else {
               for (int sl = 0; sl < m_slots; ++sl) {
                 float t0 = 0.f, t1 = 0.f, t2 = 0.f, t3 = 0.f;  // pending sums of the pairwise tree
-#pragma unroll 8  // dh 128: a full unroll of the 16 vectors needs 255 registers and spills
+#pragma unroll
                 for (int q = 0; q < LPS; ++q) {
                   const int vq = q ^ o;
-                  float f[8];
-                  unpack8(*reinterpret_cast<const uint4*>(row + (sl * LPS + vq) * 16), f);
-                  float qv[8];
-                  if constexpr (kQgRegs) {
-#pragma unroll
-                    for (int jj = 0; jj < 8; ++jj) qv[jj] = qgp[q][jj];
-                  } else {
-                    const float4 qa = *reinterpret_cast<const float4*>(&sm.qg[vq * 8]);
-                    const float4 qb = *reinterpret_cast<const float4*>(&sm.qg[vq * 8 + 4]);
-                    qv[0] = qa.x, qv[1] = qa.y, qv[2] = qa.z, qv[3] = qa.w;
-                    qv[4] = qb.x, qv[5] = qb.y, qv[6] = qb.z, qv[7] = qb.w;
-                  }
-                  float part = 0.f;
-#pragma unroll
-                  for (int jj = 0; jj < 8; ++jj) part = fmaf(f[jj], qv[jj], part);
+                  const float part = dot8_bf16(*reinterpret_cast<const uint4*>(row + (sl * LPS + vq) * 16),
+                                               *reinterpret_cast<const uint4*>(&sm.qg[vq * 8]));
                   // fold into the tree as the vectors arrive: ((p0+p1)+(p2+p3))+...
                   if ((q & 1) == 0) {
                     t0 = part;
