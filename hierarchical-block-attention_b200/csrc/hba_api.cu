@@ -268,7 +268,21 @@ const char* hba_b200_status_string(int s) {
   }
 }
 
-int hba_b200_version(void) { return 100; }
+int hba_b200_version(void) { return 200; }
+
+int hba_b200_device_status(void* status_word, int32_t clear, cudaStream_t stream) {
+  if (status_word == nullptr) return HBA_B200_ERR_INVALID_ARGUMENT;
+  int32_t word = 0;
+  cudaError_t e = cudaMemcpyAsync(&word, status_word, sizeof(word), cudaMemcpyDeviceToHost, stream);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(stream);
+  if (e == cudaSuccess && clear) {
+    e = cudaMemsetAsync(status_word, 0, sizeof(word), stream);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(stream);
+  }
+  if (e != cudaSuccess) return cuda_status(e);
+  if (word == 0) return HBA_B200_OK;
+  return word == 1 ? HBA_B200_ERR_DEVICE_TIMEOUT : HBA_B200_ERR_CUDA;
+}
 
 int hba_b200_set_profile_events(void* const* events, int32_t count) {
   if (count < 0 || count > 16 || (count > 0 && events == nullptr)) return HBA_B200_ERR_INVALID_ARGUMENT;
@@ -389,7 +403,7 @@ int hba_b200_decode(const hba_b200_config* cfg, int32_t batch, int32_t n_cap, co
   const size_t bh = (size_t)batch * cfg->n_kv;
   const int G = cfg->n_heads / cfg->n_kv;
   unsigned char* ws = static_cast<unsigned char*>(workspace);
-  int* dev_status = reinterpret_cast<int*>(ws);  // device status word (bounded waits, logit bound)
+  int* dev_status = reinterpret_cast<int*>(ws);  // sticky device status word (bounded waits)
   ws += kAlign;
   // split-path state: partials, then counters
   float* part = reinterpret_cast<float*>(ws);
@@ -690,7 +704,7 @@ int hba_b200_decode_shard_attend(const hba_b200_config* cfg, int32_t batch, int3
   if (tok_lo > 0 && tok_lo < cfg->sinks) return HBA_B200_ERR_UNSUPPORTED;  // the sinks live on one shard
   Geom geo = make_geom(cfg, batch, 1, n_cap_local);
   if (!hba::decode_tc_supported(geo, cfg->head_dim, k_cache, k_rope_cache, v_cache, nullptr, nullptr))
-    return HBA_B200_ERR_UNSUPPORTED;  // the shard partials use the tensor-core path's fixed logit bound
+    return HBA_B200_ERR_UNSUPPORTED;  // the shard partials come from the tensor-core kernel
   hba::DecodeAttnParams dp{};
   dp.geo = geo;
   dp.qp = hba::QueryPos{seq_lens, scales, 0, 0.f};
@@ -710,14 +724,12 @@ int hba_b200_decode_shard_attend(const hba_b200_config* cfg, int32_t batch, int3
   return cuda_status(e);
 }
 
-int hba_b200_decode_shard_finish(const hba_b200_config* cfg, int32_t batch, const float* part_o,
-                                 const float* part_l, const float* part_m2, void* out, float* lse,
-                                 cudaStream_t stream) {
+int hba_b200_decode_shard_finish(const hba_b200_config* cfg, int32_t batch, int32_t world, const float* parts,
+                                 void* out, float* lse, cudaStream_t stream) {
   int st = HBA_B200_OK;
   if (!config_ok(cfg, &st)) return st;
-  if (batch <= 0 || part_o == nullptr || part_l == nullptr || part_m2 == nullptr || out == nullptr)
-    return HBA_B200_ERR_INVALID_ARGUMENT;
-  return cuda_status(hba::launch_shard_finish(batch * cfg->n_heads, cfg->head_dim, part_o, part_l, part_m2,
+  if (batch <= 0 || world < 1 || parts == nullptr || out == nullptr) return HBA_B200_ERR_INVALID_ARGUMENT;
+  return cuda_status(hba::launch_shard_finish(batch * cfg->n_heads, cfg->head_dim, world, parts,
                                               static_cast<__nv_bfloat16*>(out), lse, stream));
 }
 

@@ -131,8 +131,8 @@ __global__ void __launch_bounds__(kAttnThreads) attend_kernel(AttnParams p) {
       const float x1 = bf2f(sm.qc[h][d]), x2 = bf2f(sm.qc[h][d + HALF]);
       const float* cr = p.cos + (size_t)pos * DH;
       const float* sr = p.sin + (size_t)pos * DH;
-      y1 = x1 * cr[d] - x2 * sr[d];
-      y2 = x2 * cr[d + HALF] + x1 * sr[d + HALF];
+      y1 = rope_elem(x1, -x2, cr[d], sr[d]);
+      y2 = rope_elem(x2, x1, cr[d + HALF], sr[d + HALF]);
     }
     sm.qr[h][d] = f2bf(y1);
     sm.qr[h][d + HALF] = f2bf(y2);

@@ -19,6 +19,13 @@ HBA_DEVICE float bf2f(__nv_bfloat16 x) { return __bfloat162float(x); }
 HBA_DEVICE __nv_bfloat16 f2bf(float x) { return __float2bfloat16_rn(x); }
 HBA_DEVICE float round_bf16(float x) { return __bfloat162float(__float2bfloat16_rn(x)); }
 
+// One element of RoPE, y = x*cos + rot*sin (rot = the rot_half partner, sign
+// included), with every rounding fixed: rn(rn(x*cos) + rn(rot*sin)), no fused
+// multiply-add.  x and rot are bf16 values and every caller rounds y to bf16
+// once, so the window operands are bit-reproducible (the test oracle computes
+// the same float32 expression).
+HBA_DEVICE float rope_elem(float x, float rot, float c, float s) { return __fadd_rn(__fmul_rn(x, c), __fmul_rn(rot, s)); }
+
 // unpack 8 bf16 held in a uint4 into floats (a bf16 is the upper half of
 // the fp32 with the same value, so the widening is exact bit placement)
 HBA_DEVICE void unpack8(uint4 u, float* f) {

@@ -239,7 +239,7 @@ __global__ void __launch_bounds__(kFThreads, 1) decode_fused_kernel(DecodeAttnPa
       for (int i = 0; i < PER; ++i) {
         const int d = lane * PER + i;
         const float partner = __shfl_xor_sync(0xffffffffu, v[i], 16);
-        r[i] = v[i] * cr[d] + sign * partner * sr[d];
+        r[i] = rope_elem(v[i], sign * partner, cr[d], sr[d]);
       }
     } else {
 #pragma unroll

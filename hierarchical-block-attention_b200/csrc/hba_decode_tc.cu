@@ -9,10 +9,14 @@
 //     S^T[128 keys x 16] = K[128 x dh] . Q^T          (A = K, B = Q, K-major)
 //     O^T[dh x 16]      += V^T[dh x 128] . P^T         (A = V^T MN-major, B = P^T)
 // One softmax thread per key reads its 16 head scores from TMEM and writes
-// p = exp2(s*scale*log2e - M2[h]) into P^T.  M2[h] is a per-head upper bound
-// of the logits (QKNorm: |s| <= scale*|q_h|*sqrt(dh)*k_gain), so there is no
-// running max and O^T is never rescaled; l[h] are per-thread partial sums
-// reduced once at the end.
+// p = exp2(s*scale*log2e - M[h]) into P^T; l[h] are per-thread partial sums
+// reduced once at the end.  M[h] is the per-head QKNorm bound of the logits
+// (|s| <= scale*|q_h|*sqrt(dh)*k_gain) when every head's bound is small
+// enough that no p can flush to zero (kBoundedLog2): then there is no max
+// and O^T is never rescaled.  With larger bounds (trained QKNorm gains) M[h]
+// is a lazily raised running max: the 4 softmax warps exchange their chunk
+// maxima, and when one passes M[h] by more than kRescaleLog2 the warps wait
+// for the previous PV, rescale their O^T rows in TMEM and l, and go on.
 //
 // Roles and phases:
 //  warp 3 (lane 0) produces from the first instruction on: summary pages by
@@ -69,9 +73,13 @@ struct DtcSmem {
   alignas(1024) unsigned char qr[HALVES][16 * 128];
   alignas(1024) unsigned char pt[2][2][16 * 128];           // P^T [buffer][key half][16 heads x 64 keys]
   alignas(16) __nv_bfloat16 qg[DH];  // routing query (bf16 values), read as packed 16-byte vectors
-  float m2[16];
+  float m2[16];      // per-head QKNorm logit bound (log2 units)
+  float mfin[16];    // per-head softmax reference maximum at the end of the union
+  float cmax[2][4][16];  // per-chunk maxima of the 4 softmax warps (running-max mode)
   float lsum[4][16];
-  float xl[16];  // fused shard: l of every head summed over the ranks
+  float xl[16];  // fused shard: l of every head merged over the ranks
+  float xm[16];  // fused shard: the ranks' largest reference maximum per head
+  float xw[kShardMaxRanks][16];  // fused shard: weight 2^(m_rank - xm) of each rank's partial
   float wl_s[kDtScoreWarps][32];  // per-warp top-k lists
   int wl_i[kDtScoreWarps][32];
   float xs[kDtScoreWarps][32];    // a scoring warp's batch candidates and list, for its rank update
@@ -85,7 +93,7 @@ struct DtcSmem {
   int sup_lo[32], sup_off[32], sup_cnt[32];
   int n_children;
   uint64_t full[NSLOT], empty[NSLOT];
-  uint64_t s_full[2], p_full[2], p_free[2];
+  uint64_t s_full[2], p_full[2], p_free[2], cm_full[2];
   uint64_t o_full, drain, child_ready, sel_ready, lists_ready;
   uint32_t tmem_base;
   int issued;  // ring items the producer has issued (published after each)
@@ -245,6 +253,7 @@ __global__ void __launch_bounds__(kDtThreads, 1)
       mbar_init(&sm.s_full[s], 1);
       mbar_init(&sm.p_full[s], 128);
       mbar_init(&sm.p_free[s], 1);
+      mbar_init(&sm.cm_full[s], 4);  // one arrival per softmax warp
     }
     mbar_init(&sm.o_full, 1);
     mbar_init(&sm.drain, 1);
@@ -377,7 +386,7 @@ __global__ void __launch_bounds__(kDtThreads, 1)
 #pragma unroll
           for (int i = 0; i < PER; ++i) {
             const float partner = __shfl_xor_sync(0xffffffffu, v[i], 16);
-            r[i] = v[i] * cr[i] + sign * partner * sr[i];
+            r[i] = rope_elem(v[i], sign * partner, cr[i], sr[i]);
             qn2 = fmaf(v[i], v[i], qn2);
           }
         } else {
@@ -397,7 +406,6 @@ __global__ void __launch_bounds__(kDtThreads, 1)
           const float kmax = sqrtf((float)DH) * kg * (1.f + 1.f / 64.f);
           const float m2 = scale * sqrtf(qn2) * kmax * kLog2e;
           sm.m2[h] = (h < G && ok) ? m2 : 0.f;
-          if (m2 > 120.f) atomicExch(P.err, 2);
         }
       }
     }
@@ -885,11 +893,20 @@ __global__ void __launch_bounds__(kDtThreads, 1)
       const int t = tid - 128;  // key row of the chunk / TMEM lane
       const uint32_t lane_off = (uint32_t)((warp & 3) * 32) << 16;
       const float sl2 = scale * kLog2e;
-      float lp[HB], m2[HB];
+      // mr[h]: the reference maximum of head h (log2 units), uniform over the
+      // 128 softmax threads.  bounded: the QKNorm bounds, fixed; otherwise a
+      // running max that starts empty.
+      float lp[HB], mr[HB];
+      bool bounded = true;
 #pragma unroll
       for (int h = 0; h < HB; ++h) {
         lp[h] = 0.f;
-        m2[h] = sm.m2[h];
+        mr[h] = sm.m2[h];
+        bounded = bounded && mr[h] <= kBoundedLog2;
+      }
+      if (!bounded) {
+#pragma unroll
+        for (int h = 0; h < HB; ++h) mr[h] = neg_inf();
       }
       bool okw = true;
       int NC = NCk;
@@ -901,14 +918,15 @@ __global__ void __launch_bounds__(kDtThreads, 1)
         }
         if (c >= NC) break;
         const int sb = c & 1;
-        if (!mbar_wait(&sm.s_full[sb], (c >> 1) & 1, P.err)) {
+        // a failed wait leaves the whole warp together (the TMEM accesses below are warp-collective)
+        if (!__all_sync(0xffffffffu, mbar_wait(&sm.s_full[sb], (c >> 1) & 1, P.err))) {
           okw = false;
           break;
         }
         tc_fence_after();
         float s[HB];
         tmem_ld_row<HB>(tmem + sb * 16 + lane_off, s);
-        if (c >= 2 && !mbar_wait(&sm.p_free[sb], ((c - 2) >> 1) & 1, P.err)) {
+        if (c >= 2 && !__all_sync(0xffffffffu, mbar_wait(&sm.p_free[sb], ((c - 2) >> 1) & 1, P.err))) {
           okw = false;
           break;
         }
@@ -916,11 +934,62 @@ __global__ void __launch_bounds__(kDtThreads, 1)
         if (c < NCw) valid = wlo + c * kDtKeys + t <= whi;
         else if (c < NCw + NCs) valid = t < nsink;
         else valid = (c - NCw - NCs) * kDtKeys + t < nsel * geo.Bk;
+        if (!bounded) {
+          // chunk maxima: warp max, then the 4 warps' through shared memory
+          // (an mbarrier of 4 arrivals per buffer; a warp writes buffer c & 1
+          // again at chunk c + 2 only after every warp arrived for c + 1,
+          // i.e. read chunk c's values)
+          float cm[HB];
+#pragma unroll
+          for (int h = 0; h < HB; ++h) cm[h] = warp_max_f32((valid && h < G) ? s[h] * sl2 : neg_inf());
+          __syncwarp();
+          if (lane == 0) {
+#pragma unroll
+            for (int h = 0; h < HB; ++h) sm.cmax[sb][warp & 3][h] = cm[h];
+            mbar_arrive(&sm.cm_full[sb]);
+          }
+          if (!__all_sync(0xffffffffu, mbar_wait(&sm.cm_full[sb], (c >> 1) & 1, P.err))) {
+            okw = false;
+            break;
+          }
+          float mn[HB];
+          bool need = false;
+#pragma unroll
+          for (int h = 0; h < HB; ++h) {
+            const float x = fmaxf(fmaxf(sm.cmax[sb][0][h], sm.cmax[sb][1][h]),
+                                  fmaxf(sm.cmax[sb][2][h], sm.cmax[sb][3][h]));
+            mn[h] = fmaxf(mr[h], x);
+            need = need || mn[h] > mr[h] + kRescaleLog2;  // -inf + 8 = -inf: the first valid value
+          }
+          if (need) {  // uniform: every softmax thread computed it from the same values
+            float al[HB];
+#pragma unroll
+            for (int h = 0; h < HB; ++h) al[h] = mr[h] == neg_inf() ? 0.f : ex2_approx(mr[h] - mn[h]);
+            if (c >= 1) {
+              // O^T holds PV(0 .. c-1): wait for the last one, rescale this lane's row
+              if (!__all_sync(0xffffffffu, mbar_wait(&sm.p_free[(c - 1) & 1], ((c - 1) >> 1) & 1, P.err))) {
+                okw = false;
+                break;
+              }
+              tc_fence_after();
+              float o[HB];
+              tmem_ld_row<HB>(tmem + 32 + lane_off, o);
+#pragma unroll
+              for (int h = 0; h < HB; ++h) o[h] *= al[h];
+              tmem_st_row<HB>(tmem + 32 + lane_off, o);
+            }
+#pragma unroll
+            for (int h = 0; h < HB; ++h) {
+              lp[h] *= al[h];
+              mr[h] = mn[h];
+            }
+          }
+        }
         unsigned char* pdst = sm.pt[sb][t >> 6];
         // branch-free over the HB head rows (rows >= HB were zeroed in the prologue)
 #pragma unroll
         for (int h = 0; h < HB; ++h) {
-          float pe = ex2_approx(fmaf(s[h], sl2, -m2[h]));
+          float pe = ex2_approx(fmaf(s[h], sl2, -mr[h]));
           pe = (valid && h < G) ? pe : 0.f;
           lp[h] += pe;
           *reinterpret_cast<__nv_bfloat16*>(pdst + sw128_offset(h, t & 63)) = f2bf(pe);
@@ -928,6 +997,10 @@ __global__ void __launch_bounds__(kDtThreads, 1)
         fence_proxy_async_smem();
         tc_fence_before();
         mbar_arrive(&sm.p_full[sb]);
+      }
+      if (t == 0) {
+#pragma unroll
+        for (int h = 0; h < HB; ++h) sm.mfin[h] = mr[h];
       }
       // ---- C. epilogue ----
       if (trace != nullptr && t == 0) {
@@ -941,7 +1014,7 @@ __global__ void __launch_bounds__(kDtThreads, 1)
 #pragma unroll
         for (int h = 0; h < HB; ++h) sm.lsum[warp & 3][h] = lp[h];
       asm volatile("bar.sync 1, 128;\n" ::: "memory");  // the 4 softmax warps
-      const bool have_o = okw && mbar_wait(&sm.o_full, 0, P.err);
+      const bool have_o = __all_sync(0xffffffffu, okw && mbar_wait(&sm.o_full, 0, P.err));
       uint32_t r[16];
 #pragma unroll
       for (int h = 0; h < 16; ++h) r[h] = 0u;
@@ -956,11 +1029,12 @@ __global__ void __launch_bounds__(kDtThreads, 1)
         tmem_ld_wait();
       }
       if (fused) {
-        // (O, l) of the owned tokens -> slot [rank] of every rank's buffer;
-        // then out = sum O / sum l over the ranks' slots, in rank order (the
-        // same on every rank)
-        // every value tagged with the epoch: (fp32 bits | epoch << 32)
-        const size_t xs = 16 * DH + 16;
+        // (O, l, M) of the owned tokens -> slot [rank] of every rank's
+        // buffer; then the max-rescaled merge over the ranks' slots in rank
+        // order (the same on every rank): M* = max_r M_r, w_r = 2^(M_r - M*),
+        // out = sum w_r O_r / sum w_r l_r, lse = (M* + log2 sum w_r l_r) ln 2.
+        // Every value is tagged with the epoch: (fp32 bits | epoch << 32).
+        const size_t xs = 16 * DH + 32;
         const unsigned long long ptag = (unsigned long long)epoch << 32;
         for (int rr = 0; rr < P.world; ++rr) {
           unsigned long long* dst =
@@ -971,23 +1045,39 @@ __global__ void __launch_bounds__(kDtThreads, 1)
               if (h < G)  // no owned keys: zero
                 st_relaxed_sys(dst + h * DH + t, ptag | __float_as_uint(NC > 0 ? __uint_as_float(r[h]) : 0.f));
           }
-          if (t < G)
+          if (t < G) {
             st_relaxed_sys(dst + 16 * DH + t,
                            ptag | __float_as_uint(sm.lsum[0][t] + sm.lsum[1][t] + sm.lsum[2][t] + sm.lsum[3][t]));
+            st_relaxed_sys(dst + 16 * DH + 16 + t, ptag | __float_as_uint(sm.mfin[t]));
+          }
         }
         const unsigned long long* parts =
             reinterpret_cast<const unsigned long long*>(P.xpeer[P.rank] + xl.parts) + (size_t)bg * P.world * xs;
-        // l: thread t < G sums head t over the ranks (into sm.xl); O: each
-        // thread t < DH its row over the ranks, a rank's G words at a time
+        // thread t < G: head t's (l, M) of every rank -> M*, the weights, the
+        // merged l; then each thread t < DH merges its O^T row over the ranks,
+        // a rank's G words at a time
         if (t < G) {
-          unsigned long long w[kShardMaxRanks];
-          wait_tagged_n<kShardMaxRanks>(parts + 16 * DH + t, xs, P.world, 32, 0xffffffffull, epoch, w, P.err);
-          float L = 0.f;
+          unsigned long long wl[kShardMaxRanks], wm[kShardMaxRanks];
+          wait_tagged_n<kShardMaxRanks>(parts + 16 * DH + t, xs, P.world, 32, 0xffffffffull, epoch, wl, P.err);
+          wait_tagged_n<kShardMaxRanks>(parts + 16 * DH + 16 + t, xs, P.world, 32, 0xffffffffull, epoch, wm, P.err);
+          float M = neg_inf();
 #pragma unroll
           for (int rr = 0; rr < kShardMaxRanks; ++rr)
-            if (rr < P.world) L += __uint_as_float((uint32_t)w[rr]);
+            if (rr < P.world) M = fmaxf(M, __uint_as_float((uint32_t)wm[rr]));
+          float L = 0.f;
+#pragma unroll
+          for (int rr = 0; rr < kShardMaxRanks; ++rr) {
+            if (rr < P.world) {
+              const float mr_ = __uint_as_float((uint32_t)wm[rr]);
+              const float w = (mr_ == neg_inf()) ? 0.f : ex2_approx(mr_ - M);
+              sm.xw[rr][t] = w;
+              L += w * __uint_as_float((uint32_t)wl[rr]);
+            }
+          }
           sm.xl[t] = L;
+          sm.xm[t] = M;
         }
+        asm volatile("bar.sync 1, 128;\n" ::: "memory");
         float O[HB];
 #pragma unroll
         for (int h = 0; h < HB; ++h) O[h] = 0.f;
@@ -996,11 +1086,9 @@ __global__ void __launch_bounds__(kDtThreads, 1)
             unsigned long long w[HB];
             wait_tagged_n<HB>(parts + rr * xs + t, DH, G, 32, 0xffffffffull, epoch, w, P.err);
 #pragma unroll
-            for (int h = 0; h < HB; ++h) O[h] += __uint_as_float((uint32_t)w[h]);
+            for (int h = 0; h < HB; ++h)
+              if (h < G) O[h] += sm.xw[rr][h] * __uint_as_float((uint32_t)w[h]);
           }
-        }
-        asm volatile("bar.sync 1, 128;\n" ::: "memory");
-        if (t < DH) {
 #pragma unroll
           for (int h = 0; h < HB; ++h) {
             if (h < G) {
@@ -1011,11 +1099,11 @@ __global__ void __launch_bounds__(kDtThreads, 1)
         }
         if (t < G && p.lse != nullptr) {
           const float L = sm.xl[t];
-          p.lse[(size_t)b * geo.Hq + g * G + t] = L > 0.f ? (sm.m2[t] + log2f(L)) * 0.6931471805599453f : neg_inf();
+          p.lse[(size_t)b * geo.Hq + g * G + t] = L > 0.f ? (sm.xm[t] + log2f(L)) * 0.6931471805599453f : neg_inf();
         }
         if (t == 0) stamp_any(13);
       } else if (have_o) {
-        if (P.mode == 1) {  // unnormalised partial of the owned tokens, fixed max m2
+        if (P.mode == 1) {  // unnormalised partial of the owned tokens and its reference max
           if (t < DH) {
 #pragma unroll
             for (int h = 0; h < 16; ++h)
@@ -1025,7 +1113,7 @@ __global__ void __launch_bounds__(kDtThreads, 1)
           if (t < G) {
             const float L = sm.lsum[0][t] + sm.lsum[1][t] + sm.lsum[2][t] + sm.lsum[3][t];
             P.part_l[(size_t)b * geo.Hq + g * G + t] = L;
-            P.part_m2[(size_t)b * geo.Hq + g * G + t] = sm.m2[t];
+            P.part_m2[(size_t)b * geo.Hq + g * G + t] = sm.mfin[t];
           }
         } else {
           if (t < DH) {
@@ -1040,7 +1128,7 @@ __global__ void __launch_bounds__(kDtThreads, 1)
           }
           if (t < G && p.lse != nullptr) {
             const float L = sm.lsum[0][t] + sm.lsum[1][t] + sm.lsum[2][t] + sm.lsum[3][t];
-            p.lse[(size_t)b * geo.Hq + g * G + t] = L > 0.f ? (sm.m2[t] + log2f(L)) * 0.6931471805599453f : neg_inf();
+            p.lse[(size_t)b * geo.Hq + g * G + t] = L > 0.f ? (sm.mfin[t] + log2f(L)) * 0.6931471805599453f : neg_inf();
           }
         }
       }
@@ -1171,20 +1259,36 @@ cudaError_t launch_decode_tc_fused(const DecodeAttnParams& p, const __nv_bfloat1
   return launch_dtc(P, dh, st);
 }
 
-// out = O / l (bf16), lse = (m2 + log2 l) * ln 2 from the all-reduced shard partials.
-__global__ void __launch_bounds__(128) shard_finish_kernel(int dh, const float* __restrict__ po,
-                                                           const float* __restrict__ pl,
-                                                           const float* __restrict__ pm2,
+// The max-rescaled merge of the ranks' partials (gathered rank-major, per
+// rank [m | l | O] over `rows` = B * Hq rows): M = max_r m_r,
+// w_r = 2^(m_r - M), out = sum_r w_r O_r / sum_r w_r l_r (bf16),
+// lse = (M + log2 sum_r w_r l_r) ln 2, summed in rank order.
+__global__ void __launch_bounds__(128) shard_finish_kernel(int rows, int dh, int world,
+                                                           const float* __restrict__ parts,
                                                            __nv_bfloat16* __restrict__ out, float* __restrict__ lse) {
   const size_t row = blockIdx.x;
-  const float L = pl[row];
-  for (int d = threadIdx.x; d < dh; d += blockDim.x) out[row * dh + d] = f2bf(L > 0.f ? po[row * dh + d] / L : 0.f);
-  if (threadIdx.x == 0 && lse != nullptr) lse[row] = L > 0.f ? (pm2[row] + log2f(L)) * 0.6931471805599453f : neg_inf();
+  const size_t stride = (size_t)rows * (dh + 2);  // one rank's partials
+  float M = neg_inf();
+  for (int r = 0; r < world; ++r) M = fmaxf(M, parts[r * stride + row]);
+  float L = 0.f;
+  for (int r = 0; r < world; ++r) {
+    const float m = parts[r * stride + row];
+    if (m != neg_inf()) L += ex2_approx(m - M) * parts[r * stride + rows + row];
+  }
+  for (int d = threadIdx.x; d < dh; d += blockDim.x) {
+    float o = 0.f;
+    for (int r = 0; r < world; ++r) {
+      const float m = parts[r * stride + row];
+      if (m != neg_inf()) o += ex2_approx(m - M) * parts[r * stride + 2 * (size_t)rows + row * dh + d];
+    }
+    out[row * dh + d] = f2bf(L > 0.f ? o / L : 0.f);
+  }
+  if (threadIdx.x == 0 && lse != nullptr) lse[row] = L > 0.f ? (M + log2f(L)) * 0.6931471805599453f : neg_inf();
 }
 
-cudaError_t launch_shard_finish(int rows, int dh, const float* po, const float* pl, const float* pm2,
-                                __nv_bfloat16* out, float* lse, cudaStream_t st) {
-  shard_finish_kernel<<<rows, 128, 0, st>>>(dh, po, pl, pm2, out, lse);
+cudaError_t launch_shard_finish(int rows, int dh, int world, const float* parts, __nv_bfloat16* out, float* lse,
+                                cudaStream_t st) {
+  shard_finish_kernel<<<rows, 128, 0, st>>>(rows, dh, world, parts, out, lse);
   return cudaGetLastError();
 }
 

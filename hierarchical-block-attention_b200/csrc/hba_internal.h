@@ -12,8 +12,9 @@ constexpr int kShardMaxRanks = 8;
 
 // Exchange buffer of the fused shard decode (one per rank, IPC-mapped by the
 // others), for BH = B * Hkv (sequence, kv head) rows and `world` ranks:
-// two list regions [BH][world][32] and the (O, l) partials
-// [BH][world][16 * dh + 16], all of self-validating 64-bit words -- a list
+// two list regions [BH][world][32] and the (O, l, M) partials
+// [BH][world][16 * dh + 32] (O^T [16 heads][dh], l [16], the reference
+// maximum M [16]), all of self-validating 64-bit words -- a list
 // entry is (score bits | block id (16 bits) << 32 | epoch (16 bits) << 48),
 // a partial value (fp32 bits | epoch << 32) -- written by one aligned 64-bit
 // store each, so a reader that sees this step's epoch in a word has its data
@@ -29,7 +30,7 @@ __host__ __device__ inline XLayout x_layout(int BH, int world, int dh) {
     o += (size_t)BH * world * 32 * 8;
   }
   l.parts = o;
-  o += (size_t)BH * world * (16 * dh + 16) * 8;
+  o += (size_t)BH * world * (16 * dh + 32) * 8;
   l.total = o;
   return l;
 }
@@ -166,9 +167,9 @@ size_t decode_fused_smem(int dh);
 bool select_tile_supported(const Geom& geo, int dh, const void* summ);
 cudaError_t launch_select_tile(const SelParams& p, int dh, int* err, cudaStream_t st);
 // KV-range shard: the union over this shard's tokens [tok_lo, tok_lo + n_cap)
-// as unnormalised partials (O, l, m2) after merging n_in candidate picks per
-// (sequence, kv head) into the global top-k; and the final normalisation of
-// the partials' sums.
+// as unnormalised partials (O, l, m) -- m the softmax reference maximum in
+// log2 units -- after merging n_in candidate picks per (sequence, kv head)
+// into the global top-k; and the max-rescaled merge of every rank's partials.
 cudaError_t launch_decode_tc_shard(const DecodeAttnParams& p, const float* k_gain, int* err, int dh, int tok_lo,
                                    const int32_t* in_idx, const float* in_score, int n_in, float* part_o,
                                    float* part_l, float* part_m2, cudaStream_t st);
@@ -179,8 +180,9 @@ cudaError_t launch_decode_tc_shard(const DecodeAttnParams& p, const float* k_gai
 cudaError_t launch_decode_tc_fused(const DecodeAttnParams& p, const __nv_bfloat16* summ, const __nv_bfloat16* supers,
                                    const float* k_gain, int* err, int dh, int tok_lo, int world, int rank,
                                    int32_t* epoch, void* const* xbufs, cudaStream_t st);
-cudaError_t launch_shard_finish(int rows, int dh, const float* po, const float* pl, const float* pm2,
-                                __nv_bfloat16* out, float* lse, cudaStream_t st);
+// parts: [world][rows * (dh + 2)] fp32, per rank [m (rows) | l (rows) | O (rows x dh)].
+cudaError_t launch_shard_finish(int rows, int dh, int world, const float* parts, __nv_bfloat16* out, float* lse,
+                                cudaStream_t st);
 bool decode_tc_supported(const Geom& geo, int dh, const void* k, const void* kr, const void* v, const void* summ,
                          const void* supers);
 cudaError_t launch_decode_tc(const DecodeAttnParams& p, const __nv_bfloat16* summ, const __nv_bfloat16* supers,

@@ -68,4 +68,13 @@ int hba_b200_decode_noalloc(const hba_b200_config* cfg, int32_t batch, int32_t n
                          supers, cos, sin, out, lse, sel_idx, sel_score, scratch, kScratchBytes, stream);
 }
 
+int hba_b200_decode_noalloc_status(int32_t clear, cudaStream_t stream) {
+  // the decode's sticky status word is the first 4 bytes of its workspace,
+  // here the scratch array
+  void* scratch = nullptr;
+  const cudaError_t e = scratch_address(&scratch);
+  if (e != cudaSuccess) return HBA_B200_ERR_CUDA;
+  return hba_b200_device_status(scratch, clear, stream);
+}
+
 }  // extern "C"

@@ -14,11 +14,15 @@
 // Roles (192 threads):
 //   warps 0-3  one thread per row: QKNorm + RoPE of the tile's queries into
 //              128-byte-swizzled shared memory (no separate q pass), then per
-//              chunk: S row from TMEM -> mask -> p = exp2(s*scale*log2e - M2)
+//              chunk: S row from TMEM -> mask -> p = exp2(s*scale*log2e - M)
 //              -> P row (bf16, swizzled) for the PV MMA; epilogue O/l -> out.
-//              M2 is a per-row upper bound of the logits: with QKNorm,
-//              |s| <= scale*|q|*|k| and |k| = sqrt(dh)*k_gain, so the softmax
-//              needs no running max and O is never rescaled.
+//              M is the row's QKNorm bound of the logits (|s| <=
+//              scale*|q|*|k|, |k| = sqrt(dh)*k_gain) when that bound is small
+//              enough that no p can flush to zero (kBoundedLog2): no running
+//              max, O never rescaled.  Otherwise M is the row's running max,
+//              raised lazily: when a chunk's max passes it by more than
+//              kRescaleLog2, the warp waits for the previous PV and rescales
+//              its rows of O in TMEM (and l) before writing P.
 //   warp 4     TMEM allocation; one thread issues tcgen05.mma:
 //              S[c%2] = Q K_c^T (M=128, N=64, K=dh), O += P_c V_c (M=128,
 //              N=dh, K=64, V as an MN-major operand).
@@ -255,7 +259,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     const int hq = g * G + hh;
     // the query tile arrives by TMA; this row's logit bound from its QKNorm'd values
     float M2 = 0.f;
-    if (!mbar_wait(&sm.q_ready, 0, p.err)) M2 = 0.f;
+    bool ok = __all_sync(0xffffffffu, mbar_wait(&sm.q_ready, 0, p.err));
     if (row_ok) {
       float qn2 = 0.f;
 #pragma unroll
@@ -267,17 +271,19 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       }
       const float kmax = sqrtf((float)DH) * p.k_gain[g] * (1.f + 1.f / 64.f);
       M2 = p.scale * sqrtf(qn2) * kmax * kLog2e;
-      if (M2 > 120.f) atomicExch(p.err, 2);  // logit bound too large for the fixed-max softmax
     }
+    // the row's reference maximum: its bound (fixed), or a running max that starts empty
+    const bool bounded = M2 <= kBoundedLog2;
+    float M = bounded ? M2 : neg_inf();
     if (r == 0) stamp(2);
     const float sl2 = p.scale * kLog2e;
     const int win_lo = max(geo.S, i - geo.W + 1);
     const uint32_t lane_off = (uint32_t)(warp * 32) << 16;
     float l = 0.f;
-    bool ok = true;
-    for (int c = 0; c < NCH; ++c) {
+    for (int c = 0; ok && c < NCH; ++c) {
       const int sb = c & 1;
-      if (!mbar_wait(&sm.s_full[sb], (c >> 1) & 1, p.err)) {
+      // a failed wait leaves the whole warp together (the TMEM accesses are warp-collective)
+      if (!__all_sync(0xffffffffu, mbar_wait(&sm.s_full[sb], (c >> 1) & 1, p.err))) {
         ok = false;
         break;
       }
@@ -289,7 +295,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       tmem_ld32(t_s0 + sb * kTcKeys + 32 + lane_off, s + 32);
       tmem_ld_wait();
       if (r == 0 && ts0 >= 0) stamp(ts0 + 1);
-      if (c >= 2 && !mbar_wait(&sm.p_free[sb], ((c - 2) >> 1) & 1, p.err)) {
+      if (c >= 2 && !__all_sync(0xffffffffu, mbar_wait(&sm.p_free[sb], ((c - 2) >> 1) & 1, p.err))) {
         ok = false;
         break;
       }
@@ -309,6 +315,40 @@ __global__ void __launch_bounds__(kTcThreads, 1)
           ch = min(i - kb + 1, kTcKeys);
         }
       }
+      if (!__all_sync(0xffffffffu, bounded)) {
+        // running max: this row's chunk max over its valid columns
+        float mx = neg_inf();
+        if (ch > cl) {
+#pragma unroll
+          for (int col = 0; col < kTcKeys; ++col) mx = fmaxf(mx, (col >= cl && col < ch) ? s[col] : neg_inf());
+        }
+        const float mn = bounded ? M : fmaxf(M, mx * sl2);
+        const bool need = mn > M + kRescaleLog2;  // -inf + 8 = -inf: the first valid value
+        if (__any_sync(0xffffffffu, need)) {
+          const float al = need ? (M == neg_inf() ? 0.f : ex2_approx(M - mn)) : 1.f;
+          if (c >= 1) {
+            // O holds PV(0 .. c-1): wait for the last one, rescale the warp's 32 rows
+            if (!__all_sync(0xffffffffu, mbar_wait(&sm.p_free[(c - 1) & 1], ((c - 1) >> 1) & 1, p.err))) {
+              ok = false;
+              break;
+            }
+            tc_fence_after();
+#pragma unroll
+            for (int cb = 0; cb < DH / 32; ++cb) {
+              float o[32];
+              tmem_ld32(t_o + cb * 32 + lane_off, o);
+              tmem_ld_wait();
+#pragma unroll
+              for (int j = 0; j < 32; ++j) o[j] *= al;
+              tmem_st_row<32>(t_o + cb * 32 + lane_off, o);
+            }
+          }
+          if (need) {
+            l *= al;
+            M = mn;
+          }
+        }
+      }
       unsigned char* prow = sm.p[sb];
       if (ch <= cl) {  // nothing of this chunk for this row (most rows of a block few queries picked)
 #pragma unroll
@@ -324,7 +364,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
 #pragma unroll
             for (int u = 0; u < 2; ++u) {
               const int col = c8 * 8 + 2 * t + u;
-              float pe = ex2_approx(fmaf(s[col], sl2, -M2));
+              float pe = ex2_approx(fmaf(s[col], sl2, -M));
               pe = (col >= cl && col < ch) ? pe : 0.f;
               l += pe;
               pv2[u] = pe;
@@ -341,7 +381,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       if (r == 0 && ts0 >= 0) stamp(ts0 + 4);
     }
     if (r == 0) stamp(14);
-    if (ok && mbar_wait(&sm.o_full, 0, p.err)) {
+    if (__all_sync(0xffffffffu, ok && mbar_wait(&sm.o_full, 0, p.err))) {
       tc_fence_after();
       const float inv = l > 0.f ? 1.f / l : 0.f;
 #pragma unroll
@@ -361,7 +401,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       }
       if (row_ok && p.lse != nullptr)
         p.lse[((size_t)b * geo.Hq + hq) * n + i] =
-            l > 0.f ? (M2 + log2f(l)) * 0.6931471805599453f : neg_inf();
+            l > 0.f ? (M + log2f(l)) * 0.6931471805599453f : neg_inf();
     }
   }
   tc_fence_before();

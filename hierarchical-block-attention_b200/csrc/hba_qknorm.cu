@@ -52,7 +52,7 @@ HBA_DEVICE void rope_lane(const float* x, float* y, const float* __restrict__ co
   for (int i = 0; i < PER; ++i) {
     const int d = lane * PER + i;
     const float partner = __shfl_xor_sync(0xffffffffu, x[i], 16);
-    y[i] = x[i] * cos_row[d] + sign * partner * sin_row[d];
+    y[i] = rope_elem(x[i], sign * partner, cos_row[d], sin_row[d]);
   }
 }
 

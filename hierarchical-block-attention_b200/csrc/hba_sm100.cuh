@@ -213,6 +213,52 @@ HBA_DEVICE void tmem_ld_row(uint32_t taddr, float* v) {
   for (int i = 0; i < N; ++i) v[i] = __uint_as_float(r[i]);
 }
 
+// N fp32 columns written to this thread's TMEM lane (32x32b shape), waited:
+// the values are in TMEM before the caller's tcgen05 fence + thread sync.
+template <int N>
+HBA_DEVICE void tmem_st_row(uint32_t taddr, const float* v) {
+  static_assert(N == 8 || N == 16 || N == 32, "tmem_st_row: 8, 16 or 32 columns");
+  if constexpr (N == 8) {
+    asm volatile("tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8};\n" ::"r"(taddr),
+                 "f"(v[0]), "f"(v[1]), "f"(v[2]), "f"(v[3]), "f"(v[4]), "f"(v[5]), "f"(v[6]), "f"(v[7])
+                 : "memory");
+  } else if constexpr (N == 16) {
+    asm volatile(
+        "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};\n" ::
+            "r"(taddr),
+        "f"(v[0]), "f"(v[1]), "f"(v[2]), "f"(v[3]), "f"(v[4]), "f"(v[5]), "f"(v[6]), "f"(v[7]), "f"(v[8]),
+        "f"(v[9]), "f"(v[10]), "f"(v[11]), "f"(v[12]), "f"(v[13]), "f"(v[14]), "f"(v[15])
+        : "memory");
+  } else {
+    asm volatile(
+        "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,"
+        "%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};\n" ::"r"(taddr),
+        "f"(v[0]), "f"(v[1]), "f"(v[2]), "f"(v[3]), "f"(v[4]), "f"(v[5]), "f"(v[6]), "f"(v[7]), "f"(v[8]),
+        "f"(v[9]), "f"(v[10]), "f"(v[11]), "f"(v[12]), "f"(v[13]), "f"(v[14]), "f"(v[15]), "f"(v[16]),
+        "f"(v[17]), "f"(v[18]), "f"(v[19]), "f"(v[20]), "f"(v[21]), "f"(v[22]), "f"(v[23]), "f"(v[24]),
+        "f"(v[25]), "f"(v[26]), "f"(v[27]), "f"(v[28]), "f"(v[29]), "f"(v[30]), "f"(v[31])
+        : "memory");
+  }
+  asm volatile("tcgen05.wait::st.sync.aligned;\n" ::: "memory");
+}
+
+// Maximum of x over the full warp in one instruction (sm_100a redux.sync
+// .f32; -inf is the identity, a NaN input is ignored).
+HBA_DEVICE float warp_max_f32(float x) {
+  float y;
+  asm volatile("redux.sync.max.f32 %0, %1, 0xffffffff;\n" : "=f"(y) : "f"(x));
+  return y;
+}
+
+// Softmax reference maxima of the tensor-core kernels, in log2 units.  A
+// QKNorm bound m2 <= kBoundedLog2 serves as a fixed maximum for the whole
+// union: no logit exceeds it and none lies below -m2, so p = 2^(s - m2) >=
+// 2^-120 never flushes to zero.  Above it the kernels keep a running maximum,
+// raised (with O and l rescaled) only when a chunk's maximum passes it by
+// more than kRescaleLog2, so every p <= 2^kRescaleLog2.
+constexpr float kBoundedLog2 = 60.f;
+constexpr float kRescaleLog2 = 8.f;
+
 // UMMA instruction descriptor, kind::f16: D fp32, A and B bf16, M x N tile,
 // A/B K-major unless the *_mn flag selects MN-major.
 __host__ __device__ constexpr uint32_t idesc_bf16(int M, int N, bool a_mn, bool b_mn) {

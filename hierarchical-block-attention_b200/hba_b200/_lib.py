@@ -56,6 +56,8 @@ SIGNATURES = {
                                        _P, _P, _P, _P, _SZ, _P]),
     "hba_b200_decode_noalloc": (ctypes.c_int, [_CFG, _I32, _I32, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P,
                                                _P, _P, _P, _P, _P]),
+    "hba_b200_decode_noalloc_status": (ctypes.c_int, [_I32, _P]),
+    "hba_b200_device_status": (ctypes.c_int, [_P, _I32, _P]),
     "hba_b200_prefill_workspace_size": (_SZ, [_CFG, _I32, _I32]),
     "hba_b200_set_profile_events": (ctypes.c_int, [ctypes.POINTER(ctypes.c_void_p), _I32]),
     "hba_b200_profile_events_recorded": (ctypes.c_int, []),
@@ -68,7 +70,8 @@ SIGNATURES = {
     # n_in, part_o, part_l, part_m2, sel_idx, sel_score, dev_status, stream
     "hba_b200_decode_shard_attend": (ctypes.c_int, [_CFG, _I32, _I32, _I32, _P, _P, _P, _P, _P, _P, _P, _P, _P,
                                                     _P, _P, _P, _I32, _P, _P, _P, _P, _P, _P, _P]),
-    "hba_b200_decode_shard_finish": (ctypes.c_int, [_CFG, _I32, _P, _P, _P, _P, _P, _P]),
+    # cfg, batch, world, parts, out, lse, stream
+    "hba_b200_decode_shard_finish": (ctypes.c_int, [_CFG, _I32, _I32, _P, _P, _P, _P]),
     "hba_b200_shard_xbuf_bytes": (_I64, [_CFG, _I32, _I32]),
     "hba_b200_host_alloc": (ctypes.c_int, [_I64, ctypes.POINTER(ctypes.c_void_p), ctypes.POINTER(ctypes.c_void_p)]),
     "hba_b200_host_free": (ctypes.c_int, [_P]),
@@ -109,6 +112,13 @@ def status_string(status):
         return load().hba_b200_status_string(int(status)).decode()
     except Exception:
         return "unknown"
+
+
+def check_device(status_word_ptr, stream, what, clear=False):
+    """Wait for `stream`, read a kernel status word (a workspace's first 4
+    bytes, or a shard call's dev_status) and raise HBAError
+    (ERR_DEVICE_TIMEOUT: a bounded device-side wait expired) unless it is 0."""
+    check(load().hba_b200_device_status(status_word_ptr, 1 if clear else 0, stream), what)
 
 
 def check(status, what):

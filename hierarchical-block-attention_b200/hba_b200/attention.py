@@ -105,7 +105,7 @@ def _no_grad_guard(*ts):
 
 # ------------------------------------------------------------- forwards ------
 def hba_attention_b200(q, k, v, cos, sin, cfg, summ, qkn, cap=None, hier=False, equiv=False, return_lse=False,
-                       return_selection=False):
+                       return_selection=False, check_status=True):
     """HBA attention forward on the B200 library; drop-in for
     ``hba_attention_eval`` (reference attention.py:610).
 
@@ -114,7 +114,9 @@ def hba_attention_b200(q, k, v, cos, sin, cfg, summ, qkn, cap=None, hier=False, 
     materialise per-chunk score tensors.  Returns out [B, n, Hq, dh] in q's
     dtype; with ``return_lse`` also lse [B, Hq, n] (fp32, natural log); with
     ``return_selection`` also (idx, score) [B, Hkv, n, k_blocks] (-1 = no pick).
-    Raises AssertionError when n % cfg.block != 0, as the reference does."""
+    Raises AssertionError when n % cfg.block != 0, as the reference does, and
+    HBAError when a bounded device-side wait expired (``check_status``, on by
+    default, waits for the call's stream to read the kernels' status word)."""
     if equiv:
         raise NotImplementedError("equiv=True (dense uniform-RoPE attention) is not part of the HBA hot path")
     _need_cuda(q, k, v)
@@ -148,6 +150,8 @@ def hba_attention_b200(q, k, v, cos, sin, cfg, summ, qkn, cap=None, hier=False, 
                                 ptr(sn), ptr(qg), ptr(kg), ptr(probes), ptr(proj), ptr(out), ptr(lse), ptr(sel_i),
                                 ptr(sel_s), ptr(ws), ws_bytes, stream_of(dev))
         _lib.check(st, "hba_b200_prefill")
+        if check_status:  # a bounded device wait that expired raises here instead of returning garbage
+            _lib.check_device(ptr(ws), stream_of(dev), "hba_b200_prefill (device status)")
     res = (out.to(q.dtype),)
     if return_lse:
         res += (lse,)

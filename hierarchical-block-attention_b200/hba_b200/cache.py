@@ -96,10 +96,13 @@ class HBADecodeCache:
         self.lens_host += t
         self._refresh_scales()
 
-    def attend(self, q, return_lse=False, return_selection=False):
+    def attend(self, q, return_lse=False, return_selection=False, check_status=True):
         """Decode attention for the newest token of every sequence.
         q: [B, Hq, dh] (or [B, 1, Hq, dh]) raw query.  Returns out [B, Hq, dh]
-        (q's dtype), plus lse [B, Hq] and (idx, score) [B, Hkv, k] on request."""
+        (q's dtype), plus lse [B, Hq] and (idx, score) [B, Hkv, k] on request.
+        With ``check_status`` (default) it waits for the step and raises
+        HBAError if a bounded device wait expired; ``decode_into`` (the
+        graph-capturable path) leaves that to ``check_status()``."""
         if q.dim() == 4:
             q = q[:, 0]
         if (self.lens_host < 1).any():
@@ -115,6 +118,8 @@ class HBADecodeCache:
                 si = torch.empty(self.B, cfg.n_kv, cfg.k_blocks, dtype=torch.int32, device=dev)
                 ss = torch.empty(self.B, cfg.n_kv, cfg.k_blocks, dtype=torch.float32, device=dev)
             self.decode_into(qb, out, lse, si, ss)
+            if check_status:
+                self.check_status()
         res = (out.to(q.dtype),)
         if return_lse:
             res += (lse,)
@@ -123,13 +128,17 @@ class HBADecodeCache:
         return res[0] if len(res) == 1 else res
 
     def device_status(self, clear=False):
-        """The decode's sticky device status (0 = ok, 1 = a bounded device wait
-        timed out, 2 = a QKNorm logit bound too large for the tensor-core
-        path); synchronises with the device.  `clear` resets it to 0."""
+        """The decode's sticky device status word (0 = ok, 1 = a bounded device
+        wait timed out); synchronises with the device.  `clear` resets it to 0."""
         st = int(self.workspace[:4].view(torch.int32).item())
         if clear:
             self.workspace[:4].zero_()
         return st
+
+    def check_status(self, clear=False):
+        """Raise HBAError (ERR_DEVICE_TIMEOUT) if a decode since the last clear
+        met an expired bounded device wait; waits for the current stream."""
+        _lib.check_device(ptr(self.workspace), stream_of(self.device), "hba_b200_decode (device status)", clear)
 
     def decode_into(self, qb, out, lse=None, sel_idx=None, sel_score=None, stream=None):
         """Allocation-free decode on preallocated bf16 q/out (graph-capturable)."""

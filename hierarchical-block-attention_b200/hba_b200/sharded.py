@@ -13,10 +13,13 @@ multiples, so no block or super straddles two ranks.  One decode step:
   hier  local top-beam supers -> all-gather -> global beam; each rank scores
         the children it owns -> local top-k -> all-gather -> global top-k
   then  each rank runs the union softmax over the tokens it owns (its part of
-        the window, the sinks on rank 0, its picks) with the tensor-core
-        path's fixed per-head logit bound, which is the same on every rank,
-        so the unnormalised partials (O, l) simply add: one all-reduce(sum),
-        then out = O / l, lse = m2 + log2 l.
+        the window, the sinks on rank 0, its picks) and keeps it as an
+        unnormalised partial (O, l) scaled by its own reference maximum m2
+        (log2 units: the QKNorm logit bound while it is small, else the
+        running maximum of the owned logits); one all-gather of the
+        (m2, l, O) triples, then the max-rescaled merge: M = max m2_r,
+        w_r = 2^(m2_r - M), out = sum w_r O_r / sum w_r l_r,
+        lse = (M + log2 sum w_r l_r) ln 2.
 
 The reference runs on one device and has no equivalent; the result is its
 decode (src/hba/attention.py:663-711 at cs = n-1) over the whole context.
@@ -54,7 +57,7 @@ def shard_range(cfg, max_len, rank, world, hier):
 
 
 class TorchComm:
-    """The two collectives of a step over a torch.distributed process group."""
+    """The collective of a step (an all-gather) over a torch.distributed process group."""
 
     def __init__(self, group=None):
         self.group = group
@@ -66,9 +69,6 @@ class TorchComm:
         parts = [torch.empty_like(t) for _ in range(self.world)]
         dist.all_gather(parts, t.contiguous(), group=self.group)
         return torch.stack(parts)
-
-    def all_reduce_sum(self, t):
-        dist.all_reduce(t, op=dist.ReduceOp.SUM, group=self.group)
 
 
 class PeerExchange:
@@ -141,10 +141,9 @@ class CudaShardOps:
             ptr(sel_idx), ptr(sel_score), ptr(sh.status), stream_of(sh.device))
         _lib.check(st, "hba_b200_decode_shard_attend")
 
-    def finish(self, sh, part_o, part_l, part_m2, out, lse):
+    def finish(self, sh, parts, out, lse):
         st = _lib.load().hba_b200_decode_shard_finish(
-            ctypes.byref(sh.c), sh.B, ptr(part_o), ptr(part_l), ptr(part_m2), ptr(out), ptr(lse),
-            stream_of(sh.device))
+            ctypes.byref(sh.c), sh.B, int(parts.shape[0]), ptr(parts), ptr(out), ptr(lse), stream_of(sh.device))
         _lib.check(st, "hba_b200_decode_shard_finish")
 
 
@@ -188,11 +187,12 @@ class HBAShardedDecode:
         if self.hier:
             self.s_idx = torch.empty(BH, cfg.beam, dtype=torch.int32, device=dev)
             self.s_sc = torch.empty(BH, cfg.beam, dtype=torch.float32, device=dev)
-        # O and l in one buffer: one all-reduce per step
-        self.part = torch.empty(self.B * Hq * (dh + 1), dtype=torch.float32, device=dev)
-        self.part_o = self.part[: self.B * Hq * dh].view(self.B, Hq, dh)
-        self.part_l = self.part[self.B * Hq * dh:].view(self.B, Hq)
-        self.part_m2 = torch.empty(self.B, Hq, dtype=torch.float32, device=dev)
+        # this rank's partial [m2 | l | O] in one buffer: one all-gather per step
+        BHq = self.B * Hq
+        self.part = torch.empty(BHq * (dh + 2), dtype=torch.float32, device=dev)
+        self.part_m2 = self.part[:BHq].view(self.B, Hq)
+        self.part_l = self.part[BHq: 2 * BHq].view(self.B, Hq)
+        self.part_o = self.part[2 * BHq:].view(self.B, Hq, dh)
         self.q = None
         self.x = PeerExchange(cfg, self.B, self.hier, dev, self.comm.group) if self.fused else None
 
@@ -261,8 +261,8 @@ class HBAShardedDecode:
             self.ops.select(self, 2, si, ss, self.world, self.l_idx, self.l_sc)
         gi, gs = self._gather_lists(self.l_idx, self.l_sc)               # [BH, P*K]
         self.ops.attend(self, gi, gs, gi.shape[1], self.part_o, self.part_l, self.part_m2, sel_idx, sel_score)
-        self.comm.all_reduce_sum(self.part)
-        self.ops.finish(self, self.part_o, self.part_l, self.part_m2, out, lse)
+        parts = self.comm.all_gather(self.part)                          # [P, B*Hq*(dh+2)]
+        self.ops.finish(self, parts, out, lse)
 
     def capture(self, q, out, lse=None, sel_idx=None, sel_score=None):
         """Capture one step -- kernels, list reshuffles and collectives -- as a
@@ -299,4 +299,12 @@ class HBAShardedDecode:
         out = torch.empty_like(qb)
         lse = torch.empty(self.B, self.cfg.n_heads, dtype=torch.float32, device=self.device) if return_lse else None
         self.decode_into(qb, out, lse)
+        if self.device.type == "cuda":
+            self.check_status()
         return (out, lse) if return_lse else out
+
+    def check_status(self, clear=False):
+        """Raise HBAError (ERR_DEVICE_TIMEOUT) if a step since the last clear
+        met an expired bounded device wait (e.g. a rank that never arrived at
+        an exchange); waits for the current stream."""
+        _lib.check_device(ptr(self.status), stream_of(self.device), "sharded decode (device status)", clear)

@@ -5,7 +5,12 @@ answer).
 
 * q/k/v ~ N(0, 1) (raw projections; the cache / forward applies QKNorm).
 * Summarizer probes ~ N(0, 1/dh), proj = I + 0.02 N(0, 1) (the reference
-  init, src/hba/summarizer.py:25,31-32); QKNorm gains 1 unless `gains` is set.
+  init, src/hba/summarizer.py:25,31-32); QKNorm gains 1 unless `gains` is set:
+  True draws them from U[0.6, 1.6]; "trained" from U[7, 17], so that
+  gain_q * gain_k spans ~50-290 -- the magnitude the reference's
+  data-dependent init gives a trained donor (gain_q * gain_k =
+  sqrt(dh) * rms_q * rms_k, src/hba/model.py:197-253), where the logits
+  reach the hundreds.
 * Decode planting: per (sequence, kv head), 8 distinct candidate blocks of
   the query at n-1 (hierarchical: in 8 distinct super-nodes) get keys
   sqrt(dh) * (0.8 q^ + 0.6 w_t), w_t a random unit vector orthogonal to the
@@ -60,7 +65,10 @@ def make_weights(cfg, device="cuda", seed=0, gains=False):
     Hkv, m, dh = cfg.n_kv, cfg.slots, cfg.head_dim
     probes = torch.randn(Hkv, m, dh, generator=g) * dh ** -0.5
     proj = torch.eye(dh).unsqueeze(0).repeat(Hkv, 1, 1) + torch.randn(Hkv, dh, dh, generator=g) * 0.02
-    if gains:
+    if gains == "trained":
+        qg = torch.rand(cfg.n_heads, generator=g) * 10.0 + 7.0
+        kg = torch.rand(Hkv, generator=g) * 10.0 + 7.0
+    elif gains:
         qg = torch.rand(cfg.n_heads, generator=g) * 1.0 + 0.6
         kg = torch.rand(Hkv, generator=g) * 1.0 + 0.6
     else:

@@ -132,10 +132,11 @@ size_t hba_b200_decode_workspace_size(const hba_b200_config* cfg, int32_t batch,
  *   sel_idx:   [batch, Hkv, k_blocks] int32 (-1: no pick) or NULL
  *   sel_score: [batch, Hkv, k_blocks] fp32 or NULL
  * The first 4 bytes of the workspace hold a sticky device status: the caller
- * zeroes them once (and whenever it clears an error); a decode that meets a
- * device error sets 1 (a bounded wait timed out) or 2 (a QKNorm logit bound
- * too large for the tensor-core path's fixed-max softmax) and later calls
- * leave it set.  No per-call reset keeps a decode step at one kernel launch.
+ * zeroes them once (and whenever it clears an error); a decode whose bounded
+ * device wait times out sets 1 and later calls leave it set.  No per-call
+ * reset keeps a decode step at one kernel launch.  Read it with
+ * hba_b200_device_status(workspace, ...) after the step: this call returns
+ * when the work is enqueued, before the device could report.
  * Replaces the per-query body of hba_attention_eval
  * (src/hba/attention.py:663-711) at cs = n-1, flat (:694-698) or
  * hierarchical (:690-693, hier_select :217-246).
@@ -157,7 +158,9 @@ int hba_b200_decode(const hba_b200_config* cfg, int32_t batch, int32_t n_cap, co
  * 8 MiB return HBA_B200_ERR_WORKSPACE (use hba_b200_decode instead).  The
  * array's device address is looked up on the first call made on each device,
  * so make that call before any stream capture.  All calls on a device share
- * the array: calls whose kernels may overlap on the GPU race on it.
+ * the array: calls whose kernels may overlap on the GPU race on it.  The
+ * request size counts the split path's partials whatever path runs, so the
+ * limit is about batch x context <= 8 MiB of hba_b200_decode_workspace_size.
  * No counterpart in the reference.
  */
 int hba_b200_decode_noalloc(const hba_b200_config* cfg, int32_t batch, int32_t n_cap, const int32_t* seq_lens,
@@ -166,6 +169,15 @@ int hba_b200_decode_noalloc(const hba_b200_config* cfg, int32_t batch, int32_t n
                             const void* k_rope_cache, const void* v_cache, const void* summaries,
                             const void* supers, const float* cos, const float* sin, void* out, float* lse,
                             int32_t* sel_idx, float* sel_score, cudaStream_t stream);
+
+/*
+ * The sticky device status of hba_b200_decode_noalloc on the current device
+ * (the word sits in the library's scratch array, out of the caller's reach):
+ * waits for `stream`, reads it, zeroes it when `clear` is non-zero, and
+ * returns what hba_b200_device_status returns for it.  The word starts at
+ * zero when the library loads.  No counterpart in the reference.
+ */
+int hba_b200_decode_noalloc_status(int32_t clear, cudaStream_t stream);
 
 /* Bytes of scratch needed by hba_b200_prefill (0 when rejected). */
 size_t hba_b200_prefill_workspace_size(const hba_b200_config* cfg, int32_t batch, int32_t n);
@@ -184,9 +196,8 @@ size_t hba_b200_prefill_workspace_size(const hba_b200_config* cfg, int32_t batch
  * tensor cores (one 128-row tile = 128/G queries x G heads, the routed blocks
  * of the tile's queries computed once and masked per row); other
  * configurations use the per-query gather kernel.  The first 4 bytes of the
- * workspace receive a device status after the call: 0 = ok, 1 = a bounded
- * device wait timed out, 2 = a QKNorm logit bound too large for the
- * tensor-core path's fixed-max softmax.
+ * workspace receive a device status (zeroed by the call; 1 = a bounded device
+ * wait timed out), read by hba_b200_device_status(workspace, ...).
  * Replaces hba_attention_eval (src/hba/attention.py:610-713, hier or flat)
  * and the forward of hba_attention_fused / hba_attention_dense
  * (src/hba/attention.py:552-607, :306-389), which compute the same union.
@@ -196,6 +207,17 @@ int hba_b200_prefill(const hba_b200_config* cfg, int32_t batch, int32_t n, float
                      const float* k_gain, const float* probes, const float* proj, void* out, float* lse,
                      int32_t* sel_idx, float* sel_score, void* workspace, size_t workspace_bytes,
                      cudaStream_t stream);
+
+/*
+ * Device status readout (no counterpart in the reference, whose torch calls
+ * are synchronous).  The kernels report a failed bounded device-side wait by
+ * writing 1 into a status word instead of hanging or trapping: the first 4
+ * bytes of the decode / prefill workspace, or a shard call's dev_status.
+ * This waits for `stream`, reads the word, zeroes it when `clear` is
+ * non-zero, and returns HBA_B200_OK (word 0), HBA_B200_ERR_DEVICE_TIMEOUT
+ * (word 1) or HBA_B200_ERR_CUDA (any other value, or a failed copy).
+ */
+int hba_b200_device_status(void* status_word, int32_t clear, cudaStream_t stream);
 
 /*
  * Profiling hook (no counterpart in the reference).  With count > 0, each
@@ -235,8 +257,8 @@ int hba_b200_set_debug_trace(void* device_buffer, int64_t bytes);
  * with bounds on block (hier: super) multiples.  seq_lens are the global
  * context lengths.  One step, with collectives done by the caller:
  *   flat: shard_select(level 0) -> all-gather the [B*Hkv, K] lists ->
- *         shard_attend(every shard's lists) -> all-reduce(sum) part_o,
- *         part_l -> shard_finish.
+ *         shard_attend(every shard's lists) -> all-gather the (m2, l, O)
+ *         partials -> shard_finish.
  *   hier: shard_select(level 1, local top-beam supers) -> all-gather ->
  *         shard_select(level 2, in = every shard's beam lists, children
  *         this shard owns) -> all-gather -> shard_attend -> ... as flat.
@@ -245,13 +267,19 @@ int hba_b200_set_debug_trace(void* device_buffer, int64_t bytes);
  *
  * shard_select: out_idx/out_score [B*Hkv, K] (level 1: [B*Hkv, beam]) global
  *   block (super) ids, -1 = none; in lists [B*Hkv, n_in_lists, beam].
- * shard_attend: in [B*Hkv, n_in] candidate picks; part_o [B, Hq, dh],
- *   part_l / part_m2 [B, Hq] fp32 -- the union over the owned tokens with the
- *   tensor-core path's fixed per-head logit bound m2 (the same on every
- *   shard, so partials add); sel_idx/sel_score (optional) get the global
- *   picks; dev_status: one device int, 0 = ok (as the prefill status).
+ * shard_attend: in [B*Hkv, n_in] candidate picks; the union over the owned
+ *   tokens as an unnormalised partial: part_o [B, Hq, dh], part_l [B, Hq] and
+ *   part_m2 [B, Hq] fp32, the softmax reference maximum (log2 units) the
+ *   partial is scaled by -- the QKNorm logit bound while it is small, else a
+ *   running maximum of the owned logits, so it differs between shards;
+ *   sel_idx/sel_score (optional) get the global picks; dev_status: one device
+ *   int, zeroed by the call, 1 = a bounded wait timed out.
  *   Needs the tensor-core decode path (QKNorm, block 64, head dim 64/128).
- * shard_finish: out [B, Hq, dh] bf16 = O/l, lse (optional) natural log.
+ * shard_finish: the max-rescaled merge of every rank's partial.  parts
+ *   [world][B*Hq*(dh+2)] fp32, rank-major (an all-gather of each rank's
+ *   contiguous [m2 | l | O] = [B*Hq | B*Hq | B*Hq*dh]); out [B, Hq, dh] bf16
+ *   = sum_r w_r O_r / sum_r w_r l_r with w_r = 2^(m2_r - max m2), lse
+ *   (optional) natural log.
  */
 int hba_b200_decode_shard_select(const hba_b200_config* cfg, int32_t batch, int32_t n_cap_local, int32_t tok_lo,
                                  int32_t level, const int32_t* seq_lens, const float* scales, const void* q,
@@ -264,9 +292,8 @@ int hba_b200_decode_shard_attend(const hba_b200_config* cfg, int32_t batch, int3
                                  const void* v_cache, const float* cos, const float* sin, const int32_t* in_idx,
                                  const float* in_score, int32_t n_in, float* part_o, float* part_l, float* part_m2,
                                  int32_t* sel_idx, float* sel_score, int32_t* dev_status, cudaStream_t stream);
-int hba_b200_decode_shard_finish(const hba_b200_config* cfg, int32_t batch, const float* part_o,
-                                 const float* part_l, const float* part_m2, void* out, float* lse,
-                                 cudaStream_t stream);
+int hba_b200_decode_shard_finish(const hba_b200_config* cfg, int32_t batch, int32_t world, const float* parts,
+                                 void* out, float* lse, cudaStream_t stream);
 
 /*
  * Fused KV-range sharded decode (no counterpart in the reference; same

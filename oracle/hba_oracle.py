@@ -17,7 +17,8 @@ float32 arrays that hold exact bf16 values) and evaluates everything after
 them in float64, so the CUDA path is compared against the exact math on the
 exact bytes it consumed.  Where the reference materialises a tensor in the
 input dtype *and* the CUDA path does the same (QKNorm output, grouped routing
-query), ``bf16=True`` applies the same round-to-nearest-even to bf16.
+query, the RoPE'd window q and k of the tensor-core tiles), ``bf16=True``
+applies the same round-to-nearest-even to bf16.
 
 Selection order: ``torch.topk`` leaves tie order unspecified; the oracle
 orders picks by (score descending, block index ascending).  Parity tests
@@ -110,6 +111,21 @@ def apply_rope(x, cos_rows, sin_rows):
     must broadcast against x (rows already gathered at x's positions)."""
     x = np.asarray(x, np.float64)
     return x * cos_rows + rot_half(x) * sin_rows
+
+
+def apply_rope_bf16(x, cos_rows, sin_rows):
+    """The RoPE'd tensor-core operand of the bf16 path: the same rotation of
+    the stored bf16 values (x), evaluated in float32 as rn(rn(x*cos) +
+    rn(rot_half(x)*sin)) -- numpy float32 ops round each product and the sum,
+    with no fused multiply-add -- then rounded once to bf16.  The reference's
+    bf16 path (attention.py:40-44 on bf16 tensors) rounds the same tensor to
+    bf16; the CUDA kernels compute exactly this, so kernel and oracle hold
+    bit-identical window operands."""
+    x = np.asarray(x, np.float32)
+    c = np.asarray(cos_rows, np.float32)
+    s_ = np.asarray(sin_rows, np.float32)
+    y = (x * c) + (rot_half(x) * s_)
+    return round_bf16(y.astype(np.float32)).astype(np.float64)
 
 
 # ------------------------------------------------------- slot summaries -------
@@ -232,13 +248,16 @@ def hier_select(qg, S0, S1, fanout, beam, k, cand, scale):
 
 
 # ------------------------------------------------------ union softmax ---------
-def union_attention_rows(pos, qc_rows, kc_g, v_g, cos, sin, sel_idx, sel_ok, S, W, Bk, scale):
+def union_attention_rows(pos, qc_rows, kc_g, v_g, cos, sin, sel_idx, sel_ok, S, W, Bk, scale, bf16=False):
     """The eval path's inner body for one (batch, KV head), attention.py:676-711:
     one softmax over [sinks (NoPE, j < S, j <= i) | window (RoPE, S <= j <= i,
     j > i - W) | routed blocks (NoPE, the valid picks)].
     pos: [c] query positions; qc_rows: [c, G, dh] QKNorm'd queries;
     kc_g, v_g: [n, dh]; cos/sin: [n_tab, dh]; sel_idx/sel_ok: [c, kk].
-    Returns (out [c, G, dh], lse [c, G]) in float64 (natural-log LSE)."""
+    ``bf16``: the RoPE'd window q and k are the bf16 path's rounded operands
+    (``apply_rope_bf16``).  Returns (out [c, G, dh], lse [c, G]) in float64
+    (natural-log LSE)."""
+    rope = apply_rope_bf16 if bf16 else apply_rope
     kc_g = np.asarray(kc_g, np.float64)
     v_g = np.asarray(v_g, np.float64)
     cos = np.asarray(cos, np.float64)
@@ -249,7 +268,7 @@ def union_attention_rows(pos, qc_rows, kc_g, v_g, cos, sin, sel_idx, sel_ok, S, 
     for r in range(c):
         i = int(pos[r])
         q = np.asarray(qc_rows[r], np.float64)                      # [G, dh]
-        qr = apply_rope(q, cos[i][None], sin[i][None])
+        qr = rope(q, cos[i][None], sin[i][None])
         keys, vals, logits = [], [], []
         ns_ = min(S, i + 1)
         if ns_ > 0:
@@ -257,7 +276,7 @@ def union_attention_rows(pos, qc_rows, kc_g, v_g, cos, sin, sel_idx, sel_ok, S, 
             vals.append(v_g[:ns_])
         w0 = max(S, i - W + 1)
         if w0 <= i:
-            kw = apply_rope(kc_g[w0:i + 1], cos[w0:i + 1], sin[w0:i + 1])
+            kw = rope(kc_g[w0:i + 1], cos[w0:i + 1], sin[w0:i + 1])
             logits.append(qr @ kw.T)
             vals.append(v_g[w0:i + 1])
         for b, ok in zip(sel_idx[r], sel_ok[r]):
@@ -332,7 +351,7 @@ def eval_forward(q, k, v, cos, sin, cfg, probes, proj, q_gain, k_gain, hier=Fals
             idx, val, ok = select_rows(rows, qg[b, g, rows], Sh, S1h, cfg, scale, hier)
             idx_all[b, g], val_all[b, g], ok_all[b, g] = idx, val, ok
             o, ls = union_attention_rows(rows, qc[b, rows, g * G:(g + 1) * G], kc[b, :, g], v[b, :, g],
-                                         cos, sin, idx, ok, cfg["sinks"], cfg["window"], Bk, scale)
+                                         cos, sin, idx, ok, cfg["sinks"], cfg["window"], Bk, scale, bf16=bf16)
             out[b, :, g * G:(g + 1) * G] = o
             lse[b, g * G:(g + 1) * G] = ls.T
     return dict(out=out, lse=lse, idx=idx_all, val=val_all, ok=ok_all, scale=scale)
@@ -368,17 +387,19 @@ def decode(q_rows, kc, v, cos, sin, S0, S1, cfg, scale, q_gain, hier=False, bf16
             idx, val, ok = select_rows(pos, qg[b, g][None], S0[b, g, :nb], S1h, cfg, scale, hier)
             idx_all[b, g], val_all[b, g], ok_all[b, g] = idx[0], val[0], ok[0]
             o, ls = union_attention_rows(pos, qc[b, g * G:(g + 1) * G][None], kc[b, :, g], v[b, :, g],
-                                         cos, sin, idx, ok, cfg["sinks"], cfg["window"], cfg["block"], scale)
+                                         cos, sin, idx, ok, cfg["sinks"], cfg["window"], cfg["block"], scale,
+                                         bf16=bf16)
             out[b, g * G:(g + 1) * G] = o[0]
             lse[b, g * G:(g + 1) * G] = ls[0]
     return dict(out=out, lse=lse, idx=idx_all, val=val_all, ok=ok_all, qc=qc)
 
 
-def selection_parity(idx_a, val_a, ok_a, idx_b, val_b, ok_b, tie=1e-6):
+def selection_parity(idx_a, val_a, ok_a, idx_b, val_b, ok_b, tie=1e-6, tie_rel=0.0):
     """Compare two pick lists of one query (any order).  Picks must agree as
     sets of valid block indices, except that a pick present in only one list
-    is excused when its score lies within `tie` of the other list's boundary
-    (the smallest valid score), i.e. a top-k tie.  Returns (ok, detail)."""
+    is excused when its score lies within `tie` (plus `tie_rel` times the
+    boundary's magnitude) of the other list's boundary (the smallest valid
+    score), i.e. a top-k tie.  Returns (ok, detail)."""
     A = {int(i): float(v) for i, v, o in zip(idx_a, val_a, ok_a) if o}
     Bs = {int(i): float(v) for i, v, o in zip(idx_b, val_b, ok_b) if o}
     if len(A) != len(Bs):
@@ -390,9 +411,9 @@ def selection_parity(idx_a, val_a, ok_a, idx_b, val_b, ok_b, tie=1e-6):
     ba = min(A.values())
     bb = min(Bs.values())
     for i in only_a:
-        if abs(A[i] - bb) > tie:
+        if abs(A[i] - bb) > tie + tie_rel * abs(bb):
             return False, f"block {i} score {A[i]!r} only in first list (boundary {bb!r})"
     for i in only_b:
-        if abs(Bs[i] - ba) > tie:
+        if abs(Bs[i] - ba) > tie + tie_rel * abs(ba):
             return False, f"block {i} score {Bs[i]!r} only in second list (boundary {ba!r})"
     return True, "tie"

@@ -14,6 +14,11 @@ from oracle import hba_oracle as orc
 OUT_TOL = 2e-2    # max |out - oracle| in bf16
 LSE_TOL = 1e-3    # max |lse - oracle| (natural log)
 TIE = 1e-6        # selection picks may differ only inside a 1e-6-logit tie
+# With trained QKNorm gains the routing scores reach the hundreds, where one
+# float32 ulp is ~1e-5: the kernels' fp32 sums (exact bf16 products) and the
+# oracle's float64 sums then resolve near-ties differently below ~1e-6
+# relative, so those tests widen the tie by 1e-6 of the score's magnitude.
+TIE_REL_TRAINED = 1e-6
 
 
 def np32(t):
@@ -37,8 +42,8 @@ def scale_of(cfg, n):
     return orc.union_scale(cfg.qknorm, cfg.content_scale_mode, cfg.temp_c, cfg.n_cal, cfg.native_ctx, cfg.head_dim, n)
 
 
-def compare_selection(k_idx, k_sc, o_idx, o_val, o_ok, where):
-    ok, why = orc.selection_parity(k_idx, k_sc, k_idx >= 0, o_idx, o_val, o_ok, tie=TIE)
+def compare_selection(k_idx, k_sc, o_idx, o_val, o_ok, where, tie_rel=0.0):
+    ok, why = orc.selection_parity(k_idx, k_sc, k_idx >= 0, o_idx, o_val, o_ok, tie=TIE, tie_rel=tie_rel)
     assert ok, f"{where}: {why}; kernel {list(k_idx)} oracle {list(o_idx[o_ok])}"
     common = [i for i in k_idx if i >= 0 and i in set(o_idx[o_ok].tolist())]
     kd = {int(i): float(s) for i, s in zip(k_idx, k_sc) if i >= 0}
@@ -57,7 +62,7 @@ def build_cache(cfg, B, n, hier, seed, gains=True, planted=8):
     return cache, wl, summ, qkn, cos, sin
 
 
-def check_decode(cache, q, cfg, hier, qkn, cos, sin, rows=None, lens=None):
+def check_decode(cache, q, cfg, hier, qkn, cos, sin, rows=None, lens=None, tie_rel=0.0):
     """Decode through the C-ABI and compare every sequence in `rows` with the
     oracle on the cache's stored values.  Returns (max out err, max lse err)."""
     out, lse, (si, ss) = cache.attend(q, return_lse=True, return_selection=True)
@@ -79,16 +84,17 @@ def check_decode(cache, q, cfg, hier, qkn, cos, sin, rows=None, lens=None):
                          hier=hier, bf16=True, qknorm_q=False)
         for g in range(cfg.n_kv):
             compare_selection(si_n[b, g], ss_n[b, g], res["idx"][0, g], res["val"][0, g], res["ok"][0, g],
-                              f"b={b} g={g} n={n_b}")
+                              f"b={b} g={g} n={n_b}", tie_rel=tie_rel)
         worst_o = max(worst_o, float(np.abs(out_n[b] - res["out"][0]).max()))
         worst_l = max(worst_l, float(np.abs(lse_n[b] - res["lse"][0]).max()))
     assert worst_o <= OUT_TOL, worst_o
     assert worst_l <= LSE_TOL, worst_l
-    assert cache.device_status() == 0  # no bounded wait expired, no logit bound overflowed
+    assert cache.device_status() == 0  # no bounded wait expired
+    assert np.isfinite(out_n).all() and np.isfinite(lse_n).all()
     return worst_o, worst_l, (si, ss)
 
 
-def check_prefill(cfg, B, n, hier, seed, rows, gains=True, qkv=None):
+def check_prefill(cfg, B, n, hier, seed, rows, gains=True, qkv=None, tie_rel=0.0):
     summ, qkn = synth.make_weights(cfg, "cuda", seed=seed, gains=gains)
     cos, sin = synth.rope_tables(n, cfg.head_dim, 1e6)
     if qkv is None:
@@ -115,7 +121,8 @@ def check_prefill(cfg, B, n, hier, seed, rows, gains=True, qkv=None):
         for g in range(cfg.n_kv):
             for r, row in enumerate(rows):
                 compare_selection(si_n[b, g, row], ss_n[b, g, row], res["idx"][b, g, r], res["val"][b, g, r],
-                                  res["ok"][b, g, r], f"b={b} g={g} row={row}")
+                                  res["ok"][b, g, r], f"b={b} g={g} row={row}", tie_rel=tie_rel)
+    assert np.isfinite(np32(out)).all() and np.isfinite(np32(lse)[:, :, rows]).all()
     eo = float(np.abs(np32(out)[:, rows] - res["out"]).max())
     el = float(np.abs(np32(lse)[:, :, rows] - res["lse"]).max())
     assert eo <= OUT_TOL, eo

@@ -125,7 +125,7 @@ class CpuShardOps:
                 picks, _ = self._merge(in_idx[r], in_score[r], kk)
                 picks = [int(p) for p in picks if p >= 0]
                 q = qc[b, g * G:(g + 1) * G].astype(np.float64)                    # [G, dh]
-                qr = orc.apply_rope(q, self.cos[pos][None], self.sin[pos][None])
+                qr = orc.apply_rope_bf16(q, self.cos[pos][None], self.sin[pos][None])
                 kcg, vg = loc.kc[b, :, g].astype(np.float64), loc.v[b, :, g].astype(np.float64)
                 lg, vals = [], []
                 for j in range(0, min(c.sinks, pos + 1)):                      # sinks (NoPE)
@@ -134,7 +134,7 @@ class CpuShardOps:
                         vals.append(vg[j - lo])
                 for j in range(max(c.sinks, pos - c.window + 1), pos + 1):      # window (RoPE)
                     if lo <= j < hi:
-                        kr = orc.apply_rope(kcg[j - lo][None], self.cos[j][None], self.sin[j][None])[0]
+                        kr = orc.apply_rope_bf16(kcg[j - lo][None], self.cos[j][None], self.sin[j][None])[0]
                         lg.append(qr @ kr)
                         vals.append(vg[j - lo])
                 for p in picks:                                                 # routed (NoPE)
@@ -142,13 +142,16 @@ class CpuShardOps:
                         if lo <= j < hi:
                             lg.append(q @ kcg[j - lo])
                             vals.append(vg[j - lo])
-                # the same per-head bound on every rank: |q_h| |k|max, |k| <= sqrt(dh) * k_gain
-                M = scale * np.linalg.norm(q, axis=1) * math.sqrt(dh) * float(loc.k_gain[g]) * (1 + 1 / 64)
+                # this rank's own reference maximum per head (a running max of
+                # the owned logits: it differs between ranks, so the finish
+                # merge has to rescale)
                 if lg:
                     L = np.stack(lg, 1) * scale                                  # [G, keys]
+                    M = L.max(1)
                     e = np.exp(L - M[:, None])
                     O, l = e @ np.stack(vals), e.sum(1)
                 else:
+                    M = np.full(G, NEG_INF)
                     O, l = np.zeros((G, dh)), np.zeros(G)
                 part_o[b, g * G:(g + 1) * G] = torch.as_tensor(O, dtype=torch.float32)
                 part_l[b, g * G:(g + 1) * G] = torch.as_tensor(l, dtype=torch.float32)
@@ -158,8 +161,19 @@ class CpuShardOps:
                     ids[: len(picks)] = picks[: sel_idx.shape[-1]]
                     sel_idx[b, g] = torch.as_tensor(ids, dtype=torch.int32)
 
-    def finish(self, sh, part_o, part_l, part_m2, out, lse):
-        l = part_l.double()
-        out.copy_((part_o.double() / l[..., None].clamp_min(1e-300)).to(out.dtype))
+    def finish(self, sh, parts, out, lse):
+        """Max-rescaled merge of the gathered [world, B*Hq*(dh+2)] partials
+        (per rank [m2 | l | O], m2 in log2 units)."""
+        P = parts.shape[0]
+        B, Hq, dh = out.shape
+        BHq = B * Hq
+        p = parts.double()
+        m = p[:, :BHq].view(P, B, Hq)
+        l = p[:, BHq: 2 * BHq].view(P, B, Hq)
+        O = p[:, 2 * BHq:].view(P, B, Hq, dh)
+        M = m.max(0).values
+        w = torch.where(torch.isinf(m) & (m < 0), torch.zeros_like(m), torch.exp2(m - M))
+        Ls = (w * l).sum(0)
+        out.copy_(((w[..., None] * O).sum(0) / Ls[..., None].clamp_min(1e-300)).to(out.dtype))
         if lse is not None:
-            lse.copy_(((part_m2.double() + torch.log2(l)) * math.log(2)).to(lse.dtype))
+            lse.copy_(((M + torch.log2(Ls)) * math.log(2)).to(lse.dtype))

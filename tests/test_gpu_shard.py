@@ -25,7 +25,7 @@ class _Shared:
 
 
 class ThreadComm:
-    """all_gather / all_reduce among the threads of one process."""
+    """all_gather among the threads of one process."""
 
     def __init__(self, rank, world, shared):
         self.rank, self.world, self.s = rank, world, shared
@@ -38,19 +38,11 @@ class ThreadComm:
         self.s.bar.wait()
         return out
 
-    def all_reduce_sum(self, t):
-        self.s.bar.wait()
-        self.s.slots[self.rank] = t.clone()
-        self.s.bar.wait()
-        tot = torch.stack(self.s.slots).sum(0)
-        self.s.bar.wait()
-        t.copy_(tot)
 
-
-def _run(cfg, B, n, hier, world, seed=5, cap=None):
+def _run(cfg, B, n, hier, world, seed=5, cap=None, gains=True):
     """n context tokens in a sharded capacity of `cap` (default n)."""
     cap = cap or n
-    summ, qkn = synth.make_weights(cfg, "cuda", seed=seed, gains=True)
+    summ, qkn = synth.make_weights(cfg, "cuda", seed=seed, gains=gains)
     cos, sin = synth.rope_tables(cap, cfg.head_dim, 1e6)
     wl = synth.decode_workload(cfg, B, n, hier=hier, seed=seed, qkn=qkn, planted=8)
     q = wl["q"].contiguous()
@@ -112,3 +104,17 @@ def test_shard_window_straddles_ranks():
     tok_lo, n_loc, n_total = shard_range(cfg, 8192, 3, 4, False)
     assert n_total == 8192 and tok_lo == 6144
     _run(cfg, B=2, n=tok_lo + 64 * 3, hier=False, world=4, cap=8192)
+
+
+@pytest.mark.parametrize("world", [2, 4])
+@pytest.mark.parametrize("hier", [False, True])
+def test_shard_trained_gains(world, hier):
+    # trained QKNorm gains: every rank keeps a running maximum of its own
+    # logits, so the partials carry different maxima and the finish merge
+    # has to rescale them (the max-rescaled merge, not a plain sum)
+    if hier:
+        cfg = cfg_of(n_heads=32, n_kv=8, head_dim=128, fanout=16, beam=8, k_blocks=16)
+        _run(cfg, B=2, n=16384, hier=True, world=world, seed=6, gains="trained")
+    else:
+        cfg = cfg_of(n_heads=14, n_kv=2, head_dim=64, k_blocks=16)
+        _run(cfg, B=4, n=8192, hier=False, world=world, seed=6, gains="trained")

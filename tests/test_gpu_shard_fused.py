@@ -28,15 +28,15 @@ def _cfg(hier):
     return cfg_of(n_heads=14, n_kv=2, head_dim=64, k_blocks=16)
 
 
-def _workload(cfg, hier, n, dev):
+def _workload(cfg, hier, n, dev, gains=True):
     from hba_b200 import synth
-    summ, qkn = synth.make_weights(cfg, dev, seed=7, gains=True)
+    summ, qkn = synth.make_weights(cfg, dev, seed=7, gains=gains)
     cos, sin = synth.rope_tables(CAP, cfg.head_dim, 1e6)
     wl = synth.decode_workload(cfg, B, n + 1, hier=hier, seed=7, device=dev, qkn=qkn, planted=8)
     return summ, qkn, cos, sin, wl
 
 
-def _rank(rank, world, port, outdir, hier, n):
+def _rank(rank, world, port, outdir, hier, n, gains=True):
     import datetime
     from hba_b200.sharded import HBAShardedDecode
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
@@ -47,7 +47,7 @@ def _rank(rank, world, port, outdir, hier, n):
     try:
         cfg = _cfg(hier)
         dev = torch.device("cuda", rank)
-        summ, qkn, cos, sin, wl = _workload(cfg, hier, n, dev)
+        summ, qkn, cos, sin, wl = _workload(cfg, hier, n, dev, gains)
         sh = HBAShardedDecode(cfg, B, CAP, summ, qkn, cos, sin, device=dev, hier=hier)
         assert sh.fused
         sh.fill(wl["k"][:, :n], wl["v"][:, :n])
@@ -102,11 +102,23 @@ def _one_gpu(cfg, hier, n, wl, summ, qkn, cos, sin):
                                     (True, CAP // 2 + 512)])
 def test_shard_fused(tmp_path, hier, n, world):
     # n = CAP // 2 + 512: the 1024-token window straddles two ranks
+    _check(tmp_path, hier, n, world, True)
+
+
+@pytest.mark.parametrize("world", [2, 4])
+@pytest.mark.parametrize("hier,n", [(False, CAP // 2 + 512), (True, CAP - 1024)])
+def test_shard_fused_trained_gains(tmp_path, hier, n, world):
+    # trained QKNorm gains: each rank's partial carries its own running
+    # maximum and the in-kernel merge rescales them
+    _check(tmp_path, hier, n, world, "trained")
+
+
+def _check(tmp_path, hier, n, world, gains):
     if not torch.cuda.is_available() or torch.cuda.device_count() < world:
         pytest.skip(f"needs {world} GPUs")
-    mp.spawn(_rank, args=(world, _port(), str(tmp_path), hier, n), nprocs=world, join=True)
+    mp.spawn(_rank, args=(world, _port(), str(tmp_path), hier, n, gains), nprocs=world, join=True)
     cfg = _cfg(hier)
-    summ, qkn, cos, sin, wl = _workload(cfg, hier, n, "cuda")
+    summ, qkn, cos, sin, wl = _workload(cfg, hier, n, "cuda", gains)
     (o1, l1, (si1, ss1)), (o2, l2, (si2, _)) = _one_gpu(cfg, hier, n, wl, summ, qkn, cos, sin)
     for r in range(world):
         res = np.load(tmp_path / f"r{r}.npz")

@@ -1,0 +1,115 @@
+"""GPU parity at trained QKNorm gains.
+
+The reference's data-dependent init sets gain_q * gain_k = sqrt(dh) * rms_q *
+rms_k (src/hba/model.py:197-253); for a trained donor that product is in the
+tens to hundreds, so the union's logits reach the hundreds.  The tensor-core
+kernels then cannot use the QKNorm bound as a fixed softmax maximum (far
+below the bound every probability would flush to zero): they switch to a
+lazily rescaled running maximum.  These tests drive every decode and prefill
+path, and the sharded merge, at gains drawn from U[7, 17] against the oracle
+on the same seeded inputs, with the parity tolerances (selection ties widened
+by 1e-6 of the score magnitude, see gpu_helpers.TIE_REL_TRAINED)."""
+
+import numpy as np
+import pytest
+import torch
+
+import gpu_helpers as H
+from hba_b200 import synth
+
+pytestmark = pytest.mark.gpu
+
+TR = H.TIE_REL_TRAINED
+
+
+def _bound_nat(cfg, qkn, n):
+    """Largest QKNorm logit bound over the heads, natural-log units."""
+    qg, kg = qkn.q.gain.float().cpu().numpy(), qkn.k.gain.float().cpu().numpy()
+    G = cfg.n_heads // cfg.n_kv
+    prod = max(float(qg[h]) * float(kg[h // G]) for h in range(cfg.n_heads))
+    return H.scale_of(cfg, n) * cfg.head_dim * prod
+
+
+@pytest.mark.parametrize("path", ["split", "fused", "tc"])
+@pytest.mark.parametrize("hier", [False, True])
+def test_decode_trained_gains_matches_oracle(hier, path, monkeypatch):
+    monkeypatch.setenv("HBA_B200_DECODE_PATH", path)
+    cfg = H.cfg_of(n_heads=8, n_kv=2, head_dim=128, fanout=8, beam=3) if hier else H.cfg_of()
+    cache, wl, summ, qkn, cos, sin = H.build_cache(cfg, 3, 4096, hier, seed=61, gains="trained")
+    # the regime the fixed-maximum softmax could not hold: bounds far above 2^60
+    assert _bound_nat(cfg, qkn, 4096) / np.log(2) > 60
+    H.check_decode(cache, wl["q"], cfg, hier, qkn, cos, sin, tie_rel=TR)
+
+
+def test_decode_trained_gains_ragged():
+    cfg = H.cfg_of()
+    cache, wl, summ, qkn, cos, sin = H.build_cache(cfg, 5, 4096, False, seed=62, gains="trained")
+    lens = np.array([4096, 300, 1024 + 64 * 5 + 7, 2, 1], dtype=np.int64)
+    cache.lens.copy_(torch.tensor(lens, dtype=torch.int32))
+    cache.lens_host = lens.copy()
+    cache._refresh_scales()
+    H.check_decode(cache, wl["q"], cfg, False, qkn, cos, sin, tie_rel=TR)
+
+
+def test_decode_trained_gains_cfg1_full_size():
+    """BASELINE config 1 shape (B64 x 32K, 14/2, dh 64) at trained gains."""
+    cfg = H.cfg_of()
+    cache, wl, summ, qkn, cos, sin = H.build_cache(cfg, 64, 32768, False, seed=63, gains="trained")
+    out, (si, _) = cache.attend(wl["q"], return_selection=True)
+    assert torch.isfinite(out.float()).all()
+    sel = si.cpu().numpy()
+    pl = wl["planted"].cpu().numpy()
+    assert all(set(pl[b, g]) <= set(sel[b, g]) for b in range(64) for g in range(2))
+    H.check_decode(cache, wl["q"], cfg, False, qkn, cos, sin, rows=range(0, 64, 8), tie_rel=TR)
+
+
+def test_decode_trained_gains_cfg3_full_size():
+    """BASELINE config 3 shape (B32 x 128K, 32/8, dh 128, beam 8, tau active) at trained gains."""
+    cfg = H.cfg_of(n_heads=32, n_kv=8, head_dim=128, fanout=16, beam=8)
+    cache, wl, summ, qkn, cos, sin = H.build_cache(cfg, 32, 131072, True, seed=64, gains="trained")
+    out = cache.attend(wl["q"])
+    assert torch.isfinite(out.float()).all()
+    H.check_decode(cache, wl["q"], cfg, True, qkn, cos, sin, rows=[0, 17, 31], tie_rel=TR)
+
+
+@pytest.mark.parametrize("path", ["gather", "tc"])
+@pytest.mark.parametrize("hier", [False, True])
+def test_prefill_trained_gains_matches_oracle(hier, path, monkeypatch):
+    monkeypatch.setenv("HBA_B200_PREFILL_PATH", path)
+    cfg = H.cfg_of(fanout=8, beam=4) if hier else H.cfg_of()
+    rows = H.sample_rows(2048, 48, seed=5)
+    H.check_prefill(cfg, 1, 2048, hier, seed=65, rows=rows, gains="trained", tie_rel=TR)
+
+
+@pytest.mark.parametrize("path", ["gather", "tc"])
+def test_prefill_trained_gains_dh128(path, monkeypatch):
+    monkeypatch.setenv("HBA_B200_PREFILL_PATH", path)
+    cfg = H.cfg_of(n_heads=32, n_kv=8, head_dim=128)
+    rows = H.sample_rows(4096, 32, seed=6)
+    H.check_prefill(cfg, 2, 4096, False, seed=66, rows=rows, gains="trained", tie_rel=TR)
+
+
+def test_prefill_trained_gains_cfg2_full_size_sampled_rows():
+    """BASELINE config 2 shape (B4 x 32K, 32/8, dh 128) at trained gains, sampled rows."""
+    cfg = H.cfg_of(n_heads=32, n_kv=8, head_dim=128)
+    rows = H.sample_rows(32768, 12, seed=7)
+    _, _, out, lse, _ = H.check_prefill(cfg, 4, 32768, False, seed=67, rows=rows, gains="trained", tie_rel=TR)
+    assert torch.isfinite(out.float()).all() and torch.isfinite(lse).all()
+
+
+def test_decode_and_prefill_last_row_agree_at_trained_gains():
+    from hba_b200 import HBADecodeCache, hba_attention_b200
+    cfg = H.cfg_of(n_heads=8, n_kv=2, head_dim=128)
+    n = 3072
+    summ, qkn = synth.make_weights(cfg, "cuda", seed=68, gains="trained")
+    cos, sin = synth.rope_tables(n, 128, 1e6)
+    wl = synth.prefill_workload(cfg, 2, n, seed=68)
+    with torch.no_grad():
+        out, lse, (si, _) = hba_attention_b200(wl["q"], wl["k"], wl["v"], cos, sin, cfg, summ, qkn,
+                                               return_lse=True, return_selection=True)
+    cache = HBADecodeCache(cfg, 2, n, summ, qkn, cos, sin)
+    cache.append(wl["k"], wl["v"])
+    o2, l2, (si2, _) = cache.attend(wl["q"][:, -1], return_lse=True, return_selection=True)
+    assert torch.equal(si[:, :, -1], si2)
+    assert (out[:, -1].float() - o2.float()).abs().max().item() < 2e-2
+    assert (lse[:, :, -1] - l2).abs().max().item() < 1e-3

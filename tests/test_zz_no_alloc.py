@@ -26,8 +26,12 @@ def _noalloc(cache, q, out, lse, si, ss):
     _lib.check(st, "hba_b200_decode_noalloc")
 
 
+@pytest.mark.parametrize("path", ["split", "fused", "tc"])
 @pytest.mark.parametrize("hier", [False, True])
-def test_noalloc_decode_matches_workspace_decode_on_two_calls(hier):
+def test_noalloc_decode_matches_workspace_decode_on_two_calls(hier, path, monkeypatch):
+    # every decode path, forced (the library reads the variable on each call):
+    # the small batch here would otherwise always take the split path
+    monkeypatch.setenv("HBA_B200_DECODE_PATH", path)
     cfg = H.cfg_of(n_heads=8, n_kv=2, head_dim=128, fanout=8, beam=4) if hier else H.cfg_of()
     cache, wl, summ, qkn, cos, sin = H.build_cache(cfg, 4, 4096, hier, seed=41)
     ref_out, ref_lse, (ref_si, ref_ss) = cache.attend(wl["q"], return_lse=True, return_selection=True)
@@ -43,6 +47,9 @@ def test_noalloc_decode_matches_workspace_decode_on_two_calls(hier):
         assert torch.equal(si, rsi)
         assert (out.float() - ro.float()).abs().max().item() <= H.OUT_TOL
         assert (lse - rl).abs().max().item() <= H.LSE_TOL
+    # the status word inside the scratch array, read through its own entry point
+    L = _lib.load()
+    assert L.hba_b200_decode_noalloc_status(0, stream_of(cache.device)) == _lib.OK
 
 
 def test_noalloc_rejects_requests_beyond_its_scratch():
