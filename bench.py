@@ -151,23 +151,43 @@ def max_over_ranks(x, world, dev):
 
 
 # ------------------------------------------------------------- b200 arm ----
-def timed_steps(fn, steps, warmup, flush, world, dev, clocks_index):
-    """Per-step device times (ms) of fn(), L2 flushed before each, outside the events."""
+def timed_steps(fn, steps, warmup, flush, world, dev, clocks_index, marks=0):
+    """Per-step device times (ms) of fn(), L2 flushed before each, outside the
+    events.  With marks > 0 the library also records CUDA events at its kernel
+    boundaries inside the same timed steps (hba_b200_set_profile_events, a
+    fresh set per step): returns (times, clocks, per-kernel mean ms)."""
+    from hba_b200 import _lib
+    L = _lib.load()
     for _ in range(warmup):
         fn()
     torch.cuda.synchronize()
     evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(steps)]
+    kev = [[torch.cuda.Event(enable_timing=True) for _ in range(marks)] for _ in range(steps)]
+    karr = [(ctypes.c_void_p * marks)(*[e.cuda_event for e in ks]) if marks else None for ks in kev]
+    recorded = []
     barrier(world)
     torch.cuda.synchronize()
-    with Clocks(clocks_index) as ck:
-        for e0, e1 in evs:
-            flush.zero_()
-            e0.record()
-            fn()
-            e1.record()
-        torch.cuda.synchronize()
+    try:
+        with Clocks(clocks_index) as ck:
+            for (e0, e1), arr in zip(evs, karr):
+                if marks:
+                    L.hba_b200_set_profile_events(arr, marks)
+                flush.zero_()
+                e0.record()
+                fn()
+                e1.record()
+                if marks:
+                    recorded.append(L.hba_b200_profile_events_recorded())
+            torch.cuda.synchronize()
+    finally:
+        if marks:
+            L.hba_b200_set_profile_events(None, 0)
     barrier(world)
-    return [a.elapsed_time(b) for a, b in evs], ck.summary()
+    times = [a.elapsed_time(b) for a, b in evs]
+    if not marks:
+        return times, ck.summary()
+    per = [[ks[i].elapsed_time(ks[i + 1]) for i in range(k - 1)] for ks, k in zip(kev, recorded)]
+    return times, ck.summary(), [statistics.mean(x) for x in zip(*per)]
 
 
 def kernel_times(call, steps, flush, n_events):
@@ -275,6 +295,23 @@ def ncu_case(name, local):
     torch.cuda.synchronize()
 
 
+DECODE_DATA = "synthetic (seeded N(0,1) q/k/v, 8 planted blocks per sequence and kv head)"
+
+
+def decode_config(name, world):
+    """The `config` of a decode line; the reference arm prints the same one."""
+    from hba_b200.config import baseline_config
+    cfg, B, n, hier = baseline_config(name)
+    return dict(workload=f"{name}: decode, batch {B}/rank, context {n}, {cfg.n_heads}/{cfg.n_kv} heads, "
+                         f"dh {cfg.head_dim}, {'hierarchical beam ' + str(cfg.beam) if hier else 'flat'} "
+                         f"top-{cfg.k_blocks}",
+                batch_per_rank=B, context=n, n_heads=cfg.n_heads, n_kv=cfg.n_kv, head_dim=cfg.head_dim,
+                window=cfg.window, sinks=cfg.sinks, block=cfg.block, slots=cfg.slots, k_blocks=cfg.k_blocks,
+                hier=hier, fanout=cfg.fanout if hier else None, beam=cfg.beam if hier else None,
+                l2="flushed (256 MB write) before every timed step", timing="CUDA graph replay, CUDA events",
+                parallelism=f"replicas x{world} (batch-sharded, no collective)")
+
+
 def decode_bench(name, steps, warmup, world, rank, local, pk):
     from hba_b200 import HBADecodeCache, baseline_config, synth
     from hba_b200.attention import stream_of
@@ -308,14 +345,16 @@ def decode_bench(name, steps, warmup, world, rank, local, pk):
     t_ms = statistics.mean(times)
     t_ms = max_over_ranks(t_ms, world, dev)
 
-    # dominant kernel timed live between the library's event marks: the one
-    # decode kernel (tcgen05 / fused paths) or the attend kernel of the split path
+    # dominant kernel: the tcgen05 / fused paths' step IS one kernel launch,
+    # so its time is the graph-replayed step measured above (the same timed
+    # region as ms_per_step); the split path's attend kernel is timed between
+    # the library's event marks.  The eager per-launch time is kept beside it.
     from hba_b200 import _lib
     nmarks = 4 if hier else 3          # begin | select (super, child) | attend
     kt = kernel_times(step_direct, max(3, min(steps, 10)), flush, nmarks)
     kernels = _lib.load().hba_b200_last_kernels().decode()
     single = "+" not in kernels
-    attend_ms = kt[-1]
+    attend_ms = t_ms if single else kt[-1]
     keys = cfg.sinks + cfg.window + cfg.k_blocks * cfg.block
     attend_bytes = B * Hkv * (keys * dh * 2 * 2 + G * dh * 2 * 2)
     if hier:
@@ -384,17 +423,15 @@ def decode_bench(name, steps, warmup, world, rank, local, pk):
     res = dict(
         metric=METRIC, value=B * world / (t_ms * 1e-3), unit="decode queries/s", n_gpus=world, steps=steps,
         warmup=warmup, ms_per_step=t_ms, higher_is_better=True, scaling="weak", vs_baseline=None, dtype="bf16",
-        data="synthetic (seeded N(0,1) q/k/v, 8 planted blocks per sequence and kv head)",
-        config=dict(workload=f"{name}: decode, batch {B}/rank, context {n}, {Hq}/{Hkv} heads, dh {dh}, "
-                             f"{'hierarchical beam ' + str(cfg.beam) if hier else 'flat'} top-{cfg.k_blocks}",
-                    batch_per_rank=B, context=n, n_heads=Hq, n_kv=Hkv, head_dim=dh, window=cfg.window,
-                    sinks=cfg.sinks, block=cfg.block, slots=cfg.slots, k_blocks=cfg.k_blocks, hier=hier,
-                    fanout=cfg.fanout if hier else None, beam=cfg.beam if hier else None,
-                    l2="flushed (256 MB write) before every timed step", timing="CUDA graph replay, CUDA events",
-                    parallelism=f"replicas x{world} (batch-sharded, no collective)"),
+        data=DECODE_DATA,
+        config=decode_config(name, world),
         roofline=dict(bound="hbm", kernel=dom_kernel, achieved=achieved, peak=pk["hbm"], unit="GB/s",
                       frac=achieved / pk["hbm"], peak_source=pk["source"], traffic=traffic,
-                      algorithmic_bytes_per_launch=dom_bytes, kernel_ms=attend_ms),
+                      algorithmic_bytes_per_launch=dom_bytes, kernel_ms=attend_ms,
+                      kernel_timing=("the step's single kernel launch, graph-replayed in the timed steps "
+                                     "(= ms_per_step)") if single else
+                                    "eager launches between the library's event marks",
+                      kernel_ms_eager=kt[-1]),
         step_effective_gbs=step_bytes / (t_ms * 1e-3) / 1e9,
         step_algorithmic_bytes=step_bytes,
         decode_kernels=kernels,
@@ -458,6 +495,70 @@ def cpu_decode_sample(cache, q, cfg, hier, n, seqs=2):
                        f"from the device), numpy oracle, 1 thread")
 
 
+def prefill_attended_keys(cfg, n):
+    """Sum over query positions i < n of the union's keys: sinks min(S, i+1),
+    window, routed valid picks (min(k, candidates) blocks)."""
+    i = np.arange(n)
+    win = np.maximum(0, i - np.maximum(cfg.sinks, i - cfg.window + 1) + 1)
+    sink = np.minimum(cfg.sinks, i + 1)
+    lim = i - cfg.window + 1
+    ncand = np.where(lim >= 2 * cfg.block, lim // cfg.block - 1, 0)
+    routed = np.minimum(cfg.k_blocks, ncand) * cfg.block
+    return float((win + sink + routed).sum())
+
+
+def cpu_prefill_sample(q, k, v, cos, sin, cfg, summ, qkn, n, B, rows=32):
+    """The oracle (numpy port, one thread) on a bounded sample of the same
+    prefill workload: the summaries of one whole sequence (every kv head),
+    then the selection and union of `rows` query positions of it (all heads),
+    spread over the sequence.  Projected to the whole batch: B x (summary time
+    + n x the mean per-row time); the value is tokens/s of that projection."""
+    from oracle import hba_oracle as orc
+    try:
+        from threadpoolctl import threadpool_limits
+    except Exception:  # pragma: no cover
+        threadpool_limits = None
+    r = np.random.default_rng(0)
+    rws = np.sort(r.choice(np.arange(cfg.window, n), size=rows, replace=False))
+    qs = q[0, torch.as_tensor(rws, device=q.device)].float().cpu().numpy()[None]   # [1, rows, Hq, dh]
+    ks, vs = k[:1].float().cpu().numpy(), v[:1].float().cpu().numpy()
+    cosn, sinn = cos.float().cpu().numpy(), sin.float().cpu().numpy()
+    probes, proj = summ.probes.float().cpu().numpy(), summ.proj.float().cpu().numpy()
+    qg, kg = qkn.q.gain.float().cpu().numpy(), qkn.k.gain.float().cpu().numpy()
+    ocfg = dict(block=cfg.block, window=cfg.window, sinks=cfg.sinks, k_blocks=cfg.k_blocks, fanout=cfg.fanout,
+                beam=cfg.beam, qknorm=cfg.qknorm, content_scale_mode=cfg.content_scale_mode, temp_c=cfg.temp_c,
+                n_cal=cfg.n_cal, native_ctx=cfg.native_ctx)
+    scale = orc.union_scale(cfg.qknorm, cfg.content_scale_mode, cfg.temp_c, cfg.n_cal, cfg.native_ctx,
+                            cfg.head_dim, n)
+    Hkv, G = cfg.n_kv, cfg.n_heads // cfg.n_kv
+    ctx = threadpool_limits(limits=1) if threadpool_limits else None
+    if ctx:
+        ctx.__enter__()
+    try:
+        t0 = time.perf_counter()
+        kc = orc.head_rmsnorm(ks, kg, bf16=True)
+        S0 = orc.summarize(kc, probes, proj, cfg.block)
+        t_summ = time.perf_counter() - t0
+        qc = orc.head_rmsnorm(qs, qg, bf16=True)
+        qgr = orc.grouped_query(qc, Hkv, bf16=True)                                   # [1, Hkv, rows, dh]
+        t1 = time.perf_counter()
+        for g in range(Hkv):
+            idx, val, ok = orc.select_rows(rws, qgr[0, g], S0[0, g], None, ocfg, scale, False)
+            orc.union_attention_rows(rws, qc[0, :, g * G:(g + 1) * G], kc[0, :, g], vs[0, :, g], cosn, sinn, idx,
+                                     ok, cfg.sinks, cfg.window, cfg.block, scale, bf16=True)
+        t_rows = time.perf_counter() - t1
+    finally:
+        if ctx:
+            ctx.__exit__(None, None, None)
+    t_full = B * (t_summ + n * t_rows / rows)
+    return dict(value=B * n / t_full, unit="prefill tokens/s", cores=1, kind="port",
+                sample=f"numpy oracle, 1 thread: summaries of 1 whole sequence ({t_summ:.2f} s) + selection and "
+                       f"union of {rows} query rows of it, all {cfg.n_heads} heads ({t_rows:.2f} s); projected "
+                       f"linearly to {B} x {n} tokens (rows spread over positions >= the window, where each "
+                       f"row attends its full ~2.1K keys)",
+                measured_s=t_summ + t_rows, projected_s=t_full)
+
+
 def prefill_bench(name, steps, warmup, world, rank, local, pk):
     from hba_b200 import baseline_config, synth
     from hba_b200.attention import (as_f32, c_config, gains, ptr, stream_of, summarizer_weights, union_scale)
@@ -480,64 +581,92 @@ def prefill_bench(name, steps, warmup, world, rank, local, pk):
     scale = union_scale(cfg, dh, n)
     flush = torch.empty(FLUSH_BYTES // 4, dtype=torch.float32, device=dev)
 
-    def step():
-        st = L.hba_b200_prefill(ctypes.byref(c), B, n, ctypes.c_float(scale), ptr(q), ptr(k), ptr(v), ptr(cos),
-                                ptr(sin), ptr(qg), ptr(kg), ptr(probes), ptr(proj), ptr(out), ptr(lse), None, None,
+    def call(qq, kk, vv, oo):
+        st = L.hba_b200_prefill(ctypes.byref(c), B, n, ctypes.c_float(scale), ptr(qq), ptr(kk), ptr(vv), ptr(cos),
+                                ptr(sin), ptr(qg), ptr(kg), ptr(probes), ptr(proj), ptr(oo), ptr(lse), None, None,
                                 ptr(ws), ws_bytes, stream_of(dev))
         _lib.check(st, "hba_b200_prefill")
 
-    times, clocks = timed_steps(step, steps, warmup, flush, world, dev, local)
+    def step():
+        call(q, k, v, out)
+
+    # the step's kernels are timed between the library's marks inside the same timed steps
+    nmarks = 5 if not hier else 7
+    times, clocks, kt = timed_steps(step, steps, warmup, flush, world, dev, local, marks=nmarks)
     t_ms = max_over_ranks(statistics.mean(times), world, dev)
-    kt = kernel_times(step, max(2, min(steps, 4)), flush, 5 if not hier else 7)
     kernels = _lib.load().hba_b200_last_kernels().decode().split("+")
     attend_ms = kt[-1]
-    # attended keys per query position i: sinks min(S, i+1), window, routed valid picks
-    i = np.arange(n)
-    win = np.maximum(0, i - np.maximum(cfg.sinks, i - cfg.window + 1) + 1)
-    sink = np.minimum(cfg.sinks, i + 1)
-    lim = i - cfg.window + 1
-    ncand = np.where(lim >= 2 * cfg.block, lim // cfg.block - 1, 0)
-    routed = np.minimum(cfg.k_blocks, ncand) * cfg.block
-    keys = float((win + sink + routed).sum())
+    keys = prefill_attended_keys(cfg, n)
     flops = 4.0 * dh * Hq * B * keys
     achieved = flops / (attend_ms * 1e-3) / 1e12
+    status = L.hba_b200_device_status(ptr(ws), 0, stream_of(dev))
+
+    # e2e: the C-ABI call with q/k/v copied in from pinned host memory and the
+    # output copied back to pinned host memory, every step, inside the timed
+    # region (one stream: H2D, the prefill kernels, D2H)
+    qh, kh, vh = (t.cpu().pin_memory() for t in (q, k, v))
+    oh = torch.empty(out.shape, dtype=out.dtype).pin_memory()
+
+    def step_e2e():
+        q.copy_(qh, non_blocking=True)
+        k.copy_(kh, non_blocking=True)
+        v.copy_(vh, non_blocking=True)
+        call(q, k, v, out)
+        oh.copy_(out, non_blocking=True)
+
+    e2e_times, _ = timed_steps(step_e2e, max(2, min(steps, 3)), 1, flush, world, dev, local)
+    e2e_ms = max_over_ranks(statistics.mean(e2e_times), world, dev)
+    torch.cuda.synchronize()
+    assert torch.equal(oh, out.cpu())  # the copied-back result is the device result
+    h2d = sum(t.numel() * t.element_size() for t in (q, k, v))
+    d2h = out.numel() * out.element_size()
     res = dict(
         metric=METRIC, value=B * n * world / (t_ms * 1e-3), unit="prefill tokens/s", n_gpus=world, steps=steps,
         warmup=warmup, ms_per_step=t_ms, higher_is_better=True, scaling="weak", vs_baseline=None, dtype="bf16",
         data="synthetic (seeded N(0,1) q/k/v; 64-query tiles share a topic with 8 planted blocks)",
         config=dict(workload=f"{name}: prefill, batch {B}/rank, seq {n}, {Hq}/{Hkv} heads, dh {dh}, flat top-16",
                     batch_per_rank=B, seq_len=n, n_heads=Hq, n_kv=Hkv, head_dim=dh,
-                    l2="flushed (256 MB write) before every timed step"),
+                    l2="flushed (256 MB write) before every timed step",
+                    timing="eager C-ABI call per step, CUDA events; kernel times between the library's event "
+                           "marks in the same steps"),
         roofline=dict(bound="tensor", kernel=kernels[-1], achieved=achieved, peak=pk["bf16"], unit="TFLOP/s",
                       frac=achieved / pk["bf16"], peak_source=pk["source"],
                       traffic=traffic_of(f"{kernels[-1]}_{name}"), attended_flops=flops, kernel_ms=attend_ms),
-        kernel_ms={f"{i}:{k}": t for i, (k, t) in enumerate(zip(kernels, kt))},
-        gpu_launches=steps * len(kernels), clocks=clocks,
+        kernel_ms={f"{i}:{k_}": t for i, (k_, t) in enumerate(zip(kernels, kt))},
+        e2e=dict(value=B * n * world / (e2e_ms * 1e-3), unit="prefill tokens/s", ms_per_step=e2e_ms,
+                 h2d_bytes_per_step=h2d, d2h_bytes_per_step=d2h,
+                 timing="per step: pinned H2D of q, k, v, hba_b200_prefill, pinned D2H of out, one stream"),
+        gpu_launches=steps * len(kernels), device_status=status, clocks=clocks,
     )
-    del q, k, v, ws, wl
+    if rank == 0:
+        res["cpu_baseline"] = cpu_prefill_sample(q, k, v, cos, sin, cfg, summ, qkn, n, B)
+    del q, k, v, ws, wl, qh, kh, vh, oh
     torch.cuda.empty_cache()
     return res
 
 
 # -------------------------------------------------------- reference arm ----
 def _ref_worker(args):
-    """One host process: build one synthetic sequence's cache with the oracle
-    (untimed), run `warmup` decodes, then time `steps` oracle decodes of its query."""
+    """One host process: one sequence of the GPU arm's workload (the same
+    seeded generator with its planted blocks, built on the host), its cache
+    built with the oracle (untimed), `warmup` decodes, then `steps` timed
+    oracle decodes of its query."""
     name, seed, warmup, steps = args
     sys.path.insert(0, ROOT)
     sys.path.insert(0, os.path.join(ROOT, "hierarchical-block-attention_b200"))
+    torch.set_num_threads(1)
+    from hba_b200 import synth
     from hba_b200.config import baseline_config
     from oracle import hba_oracle as orc
     cfg, B, n, hier = baseline_config(name)
-    r = np.random.default_rng(seed)
-    dh, Hq, Hkv = cfg.head_dim, cfg.n_heads, cfg.n_kv
-    q = orc.round_bf16(r.standard_normal((1, Hq, dh), dtype=np.float32))
-    k = orc.round_bf16(r.standard_normal((1, n, Hkv, dh), dtype=np.float32))
-    v = orc.round_bf16(r.standard_normal((1, n, Hkv, dh), dtype=np.float32))
-    probes = (r.standard_normal((Hkv, cfg.slots, dh), dtype=np.float32) * dh ** -0.5)
-    proj = np.eye(dh, dtype=np.float32)[None] + r.standard_normal((Hkv, dh, dh), dtype=np.float32) * 0.02
-    ones_q, ones_k = np.ones(Hq, np.float32), np.ones(Hkv, np.float32)
-    kc = orc.head_rmsnorm(k, ones_k, bf16=True)
+    dh = cfg.head_dim
+    summ, qkn = synth.make_weights(cfg, "cpu", seed=0, gains=False)
+    wl = synth.decode_workload(cfg, 1, n, hier=hier, seed=seed, device="cpu", qkn=qkn)
+    q = wl["q"].float().numpy()
+    k, v = wl["k"].float().numpy(), wl["v"].float().numpy()
+    probes, proj = summ.probes.numpy(), summ.proj.numpy()
+    qg, kg = qkn.q.gain.numpy(), qkn.k.gain.numpy()
+    kc = orc.head_rmsnorm(k, kg, bf16=True)
     S0 = orc.round_bf16(orc.summarize(kc, probes, proj, cfg.block).astype(np.float32))
     S1 = orc.round_bf16(orc.build_super(S0, cfg.fanout)[0].astype(np.float32)) if hier else None
     cos, sin = orc.rope_tables(n, dh, 1e6)
@@ -546,38 +675,36 @@ def _ref_worker(args):
                 n_cal=cfg.n_cal, native_ctx=cfg.native_ctx)
     scale = orc.union_scale(True, "inv_d", cfg.temp_c, cfg.n_cal, cfg.native_ctx, dh, n)
     for _ in range(warmup):
-        orc.decode(q, kc, v, cos, sin, S0, S1, ocfg, scale, ones_q, hier=hier, bf16=True)
+        orc.decode(q, kc, v, cos, sin, S0, S1, ocfg, scale, qg, hier=hier, bf16=True)
     t0 = time.perf_counter()
     for _ in range(steps):
-        orc.decode(q, kc, v, cos, sin, S0, S1, ocfg, scale, ones_q, hier=hier, bf16=True)
+        orc.decode(q, kc, v, cos, sin, S0, S1, ocfg, scale, qg, hier=hier, bf16=True)
     return time.perf_counter() - t0
 
 
 def reference_arm(args, world, rank):
     """The reference algorithm's CPU path (the numpy oracle port) on every host
-    core: one process per core, each decoding its own sequence of the workload
-    `steps` times after `warmup`; value = all decodes / the slowest process."""
+    core: one process per core, each decoding its own sequence of the GPU
+    arm's workload `steps` times after `warmup`; value = all decodes / the
+    slowest process.  Prints the GPU arm's `config` and `data`."""
     if rank != 0:
         return None
     import multiprocessing as mp
     os.environ.setdefault("OMP_NUM_THREADS", "1")
     os.environ.setdefault("OPENBLAS_NUM_THREADS", "1")
-    name = args.config if args.config != "cfg2" else "cfg1"
+    name = args.config if args.config in ("cfg1", "cfg3") else "cfg1"
     procs = max(1, min(os.cpu_count() or 1, 64))
     with mp.get_context("spawn").Pool(procs) as pool:
-        dts = pool.map(_ref_worker, [(name, 7 + s, args.warmup, args.steps) for s in range(procs)])
+        dts = pool.map(_ref_worker, [(name, 1000 + s, args.warmup, args.steps) for s in range(procs)])
     value = procs * args.steps / max(dts)
-    from hba_b200.config import baseline_config
-    cfg, B, n, hier = baseline_config(name)
     line = dict(metric=METRIC, value=value, unit="decode queries/s", n_gpus=world, steps=args.steps,
                 warmup=args.warmup, ms_per_step=1e3 * statistics.mean(dts) / args.steps, higher_is_better=True,
-                scaling="weak", vs_baseline=None, dtype="f32 (bf16 inputs)", data="synthetic", impl="reference",
-                config=dict(workload=f"{name}: decode, context {n}, {cfg.n_heads}/{cfg.n_kv} heads, "
-                                     f"dh {cfg.head_dim}, {'hierarchical' if hier else 'flat'} top-{cfg.k_blocks}",
-                            context=n),
+                scaling="weak", vs_baseline=None, dtype="f64 (bf16 inputs)", data=DECODE_DATA, impl="reference",
+                config=decode_config(name, world),
                 cpu_baseline=dict(value=value, unit="decode queries/s", cores=procs, kind="port",
-                                  sample=f"{procs} processes x 1 sequence, {args.steps} timed decodes each "
-                                         f"(cache pre-built, untimed), numpy oracle port of the reference eval path"),
+                                  sample=f"{procs} processes x 1 sequence of the workload (planted, the GPU arm's "
+                                         f"generator), {args.steps} timed decodes each (cache pre-built, untimed), "
+                                         f"numpy oracle port of the reference eval path"),
                 e2e=dict(value=value, unit="decode queries/s", h2d_bytes_per_step=0, d2h_bytes_per_step=0))
     return line
 

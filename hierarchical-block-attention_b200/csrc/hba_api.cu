@@ -558,11 +558,14 @@ int hba_b200_prefill(const hba_b200_config* cfg, int32_t batch, int32_t n, float
   hba::QueryPos qp{nullptr, nullptr, n, scale};
   Lists fin{};
   int fin_lists = 0, fin_k = 0;
-  // flat: the query-tiled selection unless HBA_B200_SELECT_PATH=scan forces the per-query kernel
+  // flat: the tcgen05 selection GEMM; HBA_B200_SELECT_PATH=tile forces the
+  // query-tiled CUDA-core kernel, =scan the per-query kernel
   const char* force_sel = getenv("HBA_B200_SELECT_PATH");
-  const bool tile_sel = !(force_sel != nullptr && strcmp(force_sel, "scan") == 0) &&
+  const bool no_tc = force_sel != nullptr && (strcmp(force_sel, "scan") == 0 || strcmp(force_sel, "tile") == 0);
+  const bool tc_sel = !no_tc && hba::select_tc_supported(geo, dh, summ, qcn);
+  const bool tile_sel = !tc_sel && !(force_sel != nullptr && strcmp(force_sel, "scan") == 0) &&
                         hba::select_tile_supported(geo, dh, summ);
-  if (tile_sel) {
+  if (tc_sel || tile_sel) {
     fin = carve_lists(ws, (size_t)batch * cfg->n_kv * n * cfg->k_blocks);
     hba::SelParams sp{};
     sp.geo = geo;
@@ -579,7 +582,7 @@ int hba_b200_prefill(const hba_b200_config* cfg, int32_t batch, int32_t n, float
     sp.own_blo = 0;
     sp.own_bhi = INT_MAX;
     sp.n_limit = geo.n_cap;
-    e = hba::launch_select_tile(sp, dh, dev_status, stream);
+    e = tc_sel ? hba::launch_select_tc(sp, dh, dev_status, stream) : hba::launch_select_tile(sp, dh, dev_status, stream);
     if (e != cudaSuccess) return cuda_status(e);
     prof_mark(stream);
     fin_lists = 1;
@@ -601,8 +604,11 @@ int hba_b200_prefill(const hba_b200_config* cfg, int32_t batch, int32_t n, float
     prof_mark(stream);
     g_last_kernels = cfg->hier ? "qknorm_rope_kernel+summarize_kernel+supers_kernel+select_kernel+select_kernel+"
                                  "prefill_tc_kernel"
-                               : (tile_sel ? "qknorm_rope_kernel+summarize_kernel+select_tile_kernel+prefill_tc_kernel"
-                                           : "qknorm_rope_kernel+summarize_kernel+select_kernel+prefill_tc_kernel");
+                               : (tc_sel ? "qknorm_rope_kernel+summarize_kernel+select_tc_kernel+prefill_tc_kernel"
+                                         : (tile_sel ? "qknorm_rope_kernel+summarize_kernel+select_tile_kernel+"
+                                                       "prefill_tc_kernel"
+                                                     : "qknorm_rope_kernel+summarize_kernel+select_kernel+"
+                                                       "prefill_tc_kernel"));
     if (sel_idx != nullptr) {  // the single-split lists are the final picks, layout [B, Hkv, n, K]
       const size_t bytes = (size_t)batch * cfg->n_kv * n * cfg->k_blocks * sizeof(int32_t);
       e = cudaMemcpyAsync(sel_idx, fin.idx, bytes, cudaMemcpyDeviceToDevice, stream);
@@ -635,8 +641,10 @@ int hba_b200_prefill(const hba_b200_config* cfg, int32_t batch, int32_t n, float
   prof_mark(stream);
   g_last_kernels = cfg->hier ? "qknorm_rope_kernel+summarize_kernel+supers_kernel+select_kernel+select_kernel+"
                                "attend_kernel"
-                             : (tile_sel ? "qknorm_rope_kernel+summarize_kernel+select_tile_kernel+attend_kernel"
-                                         : "qknorm_rope_kernel+summarize_kernel+select_kernel+attend_kernel");
+                             : (tc_sel ? "qknorm_rope_kernel+summarize_kernel+select_tc_kernel+attend_kernel"
+                                       : (tile_sel ? "qknorm_rope_kernel+summarize_kernel+select_tile_kernel+"
+                                                     "attend_kernel"
+                                                   : "qknorm_rope_kernel+summarize_kernel+select_kernel+attend_kernel"));
   return HBA_B200_OK;
 }
 

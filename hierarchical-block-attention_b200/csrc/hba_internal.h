@@ -166,6 +166,11 @@ size_t decode_fused_smem(int dh);
 // select_kernel's); writes one list of p.list_k per query.
 bool select_tile_supported(const Geom& geo, int dh, const void* summ);
 cudaError_t launch_select_tile(const SelParams& p, int dh, int* err, cudaStream_t st);
+// Prefill flat selection on tcgen05 (hba_select_tc.cu): 128 queries per CTA,
+// scores as a UMMA GEMM per stage of summaries, top-k from TMEM; p.q holds the
+// QKNorm'd queries.  Writes one list of p.list_k per query.
+bool select_tc_supported(const Geom& geo, int dh, const void* summ, const void* q);
+cudaError_t launch_select_tc(const SelParams& p, int dh, int* err, cudaStream_t st);
 // KV-range shard: the union over this shard's tokens [tok_lo, tok_lo + n_cap)
 // as unnormalised partials (O, l, m) -- m the softmax reference maximum in
 // log2 units -- after merging n_in candidate picks per (sequence, kv head)

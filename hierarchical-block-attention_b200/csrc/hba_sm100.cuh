@@ -132,6 +132,15 @@ HBA_DEVICE void tma_load_4d(void* dst, const CUtensorMap* map, int c0, int c1, i
       : "memory");
 }
 
+// 3-D tiled TMA load into shared memory, completion counted on `bar` (bytes).
+HBA_DEVICE void tma_load_3d(void* dst, const CUtensorMap* map, int c0, int c1, int c2, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4}], "
+      "[%5];\n" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(c2), "r"(smem_u32(bar))
+      : "memory");
+}
+
 // 1-D bulk copy global -> shared (16-byte aligned addresses, size a multiple
 // of 16), completion counted on `bar` (bytes).  Never multicast.
 HBA_DEVICE void bulk_load(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {

@@ -52,6 +52,22 @@ def compare_selection(k_idx, k_sc, o_idx, o_val, o_ok, where, tie_rel=0.0):
         assert abs(kd[i] - od[i]) <= 1e-5 * max(1.0, abs(od[i])), (where, i, kd[i], od[i])
 
 
+def assert_picks_agree(si_a, ss_a, si_b, ss_b, tie=TIE, tie_rel=1e-6, score_rel=1e-5):
+    """Two kernels' pick lists [..., k] (e.g. the tensor-core selection GEMM
+    against the CUDA-core scan, whose fp32 summation orders differ): the same
+    sets except inside a tie, and the common picks' scores within score_rel."""
+    a_i, a_s = si_a.reshape(-1, si_a.shape[-1]).cpu().numpy(), np32(ss_a).reshape(-1, ss_a.shape[-1])
+    b_i, b_s = si_b.reshape(-1, si_b.shape[-1]).cpu().numpy(), np32(ss_b).reshape(-1, ss_b.shape[-1])
+    for r in range(a_i.shape[0]):
+        ok, why = orc.selection_parity(a_i[r], a_s[r], a_i[r] >= 0, b_i[r], b_s[r], b_i[r] >= 0, tie=tie,
+                                       tie_rel=tie_rel)
+        assert ok, f"row {r}: {why}"
+        da = {int(i): float(x) for i, x in zip(a_i[r], a_s[r]) if i >= 0}
+        for i, x in zip(b_i[r], b_s[r]):
+            if i >= 0 and int(i) in da:
+                assert abs(da[int(i)] - float(x)) <= score_rel * max(1.0, abs(float(x))), (r, i, da[int(i)], x)
+
+
 def build_cache(cfg, B, n, hier, seed, gains=True, planted=8):
     summ, qkn = synth.make_weights(cfg, "cuda", seed=seed, gains=gains)
     n_cap = -(-n // cfg.block) * cfg.block

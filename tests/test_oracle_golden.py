@@ -127,3 +127,21 @@ def test_round_bf16_matches_torch():
                                                                      1e-40], np.float32)])
     ref = torch.from_numpy(x).to(torch.bfloat16).float().numpy()
     np.testing.assert_array_equal(orc.round_bf16(x), ref)
+
+
+@pytest.mark.parametrize("hier", [False, True])
+def test_oracle_matches_reference_model_layer(hier):
+    """The oracle (fp32 mode) against layer 0 of the reference's own HBAModel
+    at trained-donor QKNorm gains (gain_q * gain_k ~ 81, logits in the tens):
+    the reference's hba_attention_eval outputs on the same bf16 q/k/v."""
+    import model_fixture as MF
+    f = MF.load()
+    cfg = f["cfg"]
+    n = f["q"].shape[1]
+    cos, sin = orc.rope_tables(n, cfg["head_dim"], cfg["rope_theta"])
+    res = orc.eval_forward(f["q"], f["k"], f["v"], cos, sin, MF.oracle_cfg(cfg), f["probes"], f["proj"],
+                           f["q_gain"], f["k_gain"], hier=hier, rows=f["rows"])
+    ref = f["out_eval_hier"] if hier else f["out_eval"]
+    assert np.abs(res["out"] - ref).max() < 1e-4
+    # the gains are in the regime the fixed-maximum softmax could not hold
+    assert float(np.outer(f["q_gain"], f["k_gain"]).min()) > 50
