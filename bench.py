@@ -163,6 +163,10 @@ def timed_steps(fn, steps, warmup, flush, world, dev, clocks_index, marks=0):
     torch.cuda.synchronize()
     evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(steps)]
     kev = [[torch.cuda.Event(enable_timing=True) for _ in range(marks)] for _ in range(steps)]
+    for ks in kev:  # torch creates an event's CUDA handle at its first record
+        for e in ks:
+            e.record()
+    torch.cuda.synchronize()
     karr = [(ctypes.c_void_p * marks)(*[e.cuda_event for e in ks]) if marks else None for ks in kev]
     recorded = []
     barrier(world)

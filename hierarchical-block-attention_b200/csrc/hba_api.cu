@@ -251,6 +251,12 @@ size_t decode_state_bytes(const hba_b200_config* c, const Plan& p, size_t bh) {
   return align_up(bh * p.max_seg * G * (size_t)(c->head_dim + 2) * sizeof(float)) + align_up(bh * sizeof(int32_t));
 }
 
+// The tensor-core union runs for this configuration (before the pointer checks).
+bool prefill_tc_config(const hba_b200_config* cfg, int32_t batch, int32_t n) {
+  const Geom geo = make_geom(cfg, batch, n, n);
+  return hba::prefill_tc_supported(geo, cfg->head_dim, n, cfg->qknorm != 0);
+}
+
 }  // namespace
 
 extern "C" {
@@ -496,6 +502,8 @@ size_t hba_b200_prefill_workspace_size(const hba_b200_config* cfg, int32_t batch
   b += 2 * align_up((size_t)batch * n * cfg->n_heads * dh * 2);           // the same for the queries
   b += align_up((size_t)batch * cfg->n_kv * nb * cfg->slots * dh * 2);    // summaries
   b += align_up((size_t)batch * cfg->n_kv * ns * cfg->slots * dh * 2);    // supers
+  if (prefill_tc_config(cfg, batch, n))                                    // chunk-tiled K, RoPE'd K, V
+    b += 3 * align_up((size_t)batch * n * cfg->n_kv * dh * 2);
   b += selection_bytes(cfg, plan, queries);
   return b;
 }
@@ -532,13 +540,37 @@ int hba_b200_prefill(const hba_b200_config* cfg, int32_t batch, int32_t n, float
   ws += align_up((size_t)batch * cfg->n_kv * nb * cfg->slots * dh * 2);
   __nv_bfloat16* sup = reinterpret_cast<__nv_bfloat16*>(ws);
   ws += align_up((size_t)batch * cfg->n_kv * ns * cfg->slots * dh * 2);
+  __nv_bfloat16 *kc_sw = nullptr, *kr_sw = nullptr, *v_sw = nullptr;  // chunk-tiled copies (tensor-core union)
+  if (prefill_tc_config(cfg, batch, n)) {
+    const size_t kv_bytes = align_up((size_t)batch * n * cfg->n_kv * dh * 2);
+    kc_sw = reinterpret_cast<__nv_bfloat16*>(ws);
+    kr_sw = reinterpret_cast<__nv_bfloat16*>(ws + kv_bytes);
+    v_sw = reinterpret_cast<__nv_bfloat16*>(ws + 2 * kv_bytes);
+    ws += 3 * kv_bytes;
+  }
 
   Geom geo = make_geom(cfg, batch, n, n);
+  const Plan plan = make_plan(cfg, (int)nb, batch * cfg->n_kv, false);
+  // selection: the tcgen05 selection GEMM; HBA_B200_SELECT_PATH=tile forces the
+  // query-tiled CUDA-core kernel, =scan the per-query kernel
+  const char* force_sel = getenv("HBA_B200_SELECT_PATH");
+  const bool no_tc = force_sel != nullptr && (strcmp(force_sel, "scan") == 0 || strcmp(force_sel, "tile") == 0);
+  const bool tc_sel = !no_tc && hba::select_tc_supported(geo, dh, summ, qcn);
+  const bool tile_sel = !tc_sel && !(force_sel != nullptr && strcmp(force_sel, "scan") == 0) &&
+                        hba::select_tile_supported(geo, dh, summ);
+  const int n_lists = (tc_sel || tile_sel) ? 1 : (cfg->hier ? plan.child_splits : plan.sel_splits);
+  // union: the tensor-core kernel unless HBA_B200_PREFILL_PATH=gather forces the per-query kernel
+  const char* force = getenv("HBA_B200_PREFILL_PATH");
+  const bool want_tc = !(force != nullptr && strcmp(force, "gather") == 0);
+  const bool v_aligned = (reinterpret_cast<uintptr_t>(v) & 15u) == 0;
+  const bool use_tc = want_tc && v_aligned && kc_sw != nullptr && n_lists == 1;
+
   prof_begin(stream);
   cudaError_t e = cudaMemsetAsync(dev_status, 0, sizeof(int), stream);
   if (e != cudaSuccess) return cuda_status(e);
-  e = hba::launch_qknorm_rope(geo, n, static_cast<const __nv_bfloat16*>(k), k_gain, cos, sin, kc, kr, dh,
-                                          stream);
+  e = hba::launch_qknorm_rope(geo, n, static_cast<const __nv_bfloat16*>(k), k_gain, cos, sin, kc, kr, dh, stream,
+                              use_tc ? static_cast<const __nv_bfloat16*>(v) : nullptr, use_tc ? kc_sw : nullptr,
+                              kr_sw, v_sw);
   if (e == cudaSuccess) {  // the same pre-pass over the query heads (the gain per query head)
     Geom gq = geo;
     gq.Hkv = geo.Hq;
@@ -554,17 +586,9 @@ int hba_b200_prefill(const hba_b200_config* cfg, int32_t batch, int32_t n, float
     if (e != cudaSuccess) return cuda_status(e);
     prof_mark(stream);
   }
-  const Plan plan = make_plan(cfg, (int)nb, batch * cfg->n_kv, false);
   hba::QueryPos qp{nullptr, nullptr, n, scale};
   Lists fin{};
   int fin_lists = 0, fin_k = 0;
-  // flat: the tcgen05 selection GEMM; HBA_B200_SELECT_PATH=tile forces the
-  // query-tiled CUDA-core kernel, =scan the per-query kernel
-  const char* force_sel = getenv("HBA_B200_SELECT_PATH");
-  const bool no_tc = force_sel != nullptr && (strcmp(force_sel, "scan") == 0 || strcmp(force_sel, "tile") == 0);
-  const bool tc_sel = !no_tc && hba::select_tc_supported(geo, dh, summ, qcn);
-  const bool tile_sel = !tc_sel && !(force_sel != nullptr && strcmp(force_sel, "scan") == 0) &&
-                        hba::select_tile_supported(geo, dh, summ);
   if (tc_sel || tile_sel) {
     fin = carve_lists(ws, (size_t)batch * cfg->n_kv * n * cfg->k_blocks);
     hba::SelParams sp{};
@@ -592,13 +616,9 @@ int hba_b200_prefill(const hba_b200_config* cfg, int32_t batch, int32_t n, float
                     fin_lists, fin_k, stream);
     if (st != HBA_B200_OK) return st;
   }
-  // tensor-core union path unless HBA_B200_PREFILL_PATH=gather forces the per-query kernel
-  const char* force = getenv("HBA_B200_PREFILL_PATH");
-  const bool want_tc = !(force != nullptr && strcmp(force, "gather") == 0);
-  const bool v_aligned = (reinterpret_cast<uintptr_t>(v) & 15u) == 0;  // TMA needs 16-byte aligned bases
-  if (want_tc && v_aligned && fin_lists == 1 && hba::prefill_tc_supported(geo, dh, n, cfg->qknorm != 0)) {
-    e = hba::launch_prefill_tc(geo, dh, n, scale, qcn, qrn, k_gain, kc, kr,
-                               static_cast<const __nv_bfloat16*>(v), fin.idx, fin_lists * fin_k,
+  if (use_tc) {
+    if (fin_lists != 1) return HBA_B200_ERR_UNSUPPORTED;  // (n_lists predicted it: never taken)
+    e = hba::launch_prefill_tc(geo, dh, n, scale, qcn, qrn, k_gain, kc_sw, kr_sw, v_sw, fin.idx, fin_lists * fin_k,
                                static_cast<__nv_bfloat16*>(out), lse, dev_status, g_trace, g_trace_ctas, stream);
     if (e != cudaSuccess) return cuda_status(e);
     prof_mark(stream);

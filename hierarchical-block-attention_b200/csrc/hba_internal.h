@@ -142,9 +142,13 @@ cudaError_t launch_append(const Geom& geo, int t, const int32_t* pos, const __nv
                           __nv_bfloat16* k_cache, __nv_bfloat16* kr_cache, __nv_bfloat16* v_cache, int dh,
                           cudaStream_t st);
 // k (QKNorm'd, or copied) and kr = RoPE(k) for a whole [B, n, Hkv, dh] tensor.
+// With kc_sw: kc, plus kc, RoPE(kc) and v (when given) in the chunk-tiled
+// layout of the tensor-core prefill ([B, Hkv, n/64, dh/64] tiles of the
+// 8 KB 128-byte-swizzled [64 tokens x 64 dims] image; n % 64 == 0), kr unused.
 cudaError_t launch_qknorm_rope(const Geom& geo, int n, const __nv_bfloat16* k, const float* k_gain,
                                const float* cos, const float* sin, __nv_bfloat16* kc, __nv_bfloat16* kr, int dh,
-                               cudaStream_t st);
+                               cudaStream_t st, const __nv_bfloat16* v = nullptr, __nv_bfloat16* kc_sw = nullptr,
+                               __nv_bfloat16* kr_sw = nullptr, __nv_bfloat16* v_sw = nullptr);
 // Summaries of blocks [blk_begin, blk_end) for every sequence; if pos/t are
 // given (append), only blocks completed by tokens [pos[b], pos[b]+t) of
 // sequence b are rebuilt.
@@ -194,10 +198,12 @@ cudaError_t launch_decode_tc(const DecodeAttnParams& p, const __nv_bfloat16* sum
                              const float* k_gain, int* err, int dh, cudaStream_t st);
 // tcgen05/TMEM prefill union softmax (hba_prefill_tc.cu).
 bool prefill_tc_supported(const Geom& geo, int dh, int n, bool qknorm);
-// qc / qr: the queries QKNorm'd and RoPE'd by the pre-pass, [B, n, Hq, dh] bf16.
+// qc / qr: the queries QKNorm'd and RoPE'd by the pre-pass, [B, n, Hq, dh] bf16;
+// kc_sw / kr_sw / v_sw: the keys QKNorm'd, RoPE'd, and the values, in the
+// pre-pass's chunk-tiled layout.
 cudaError_t launch_prefill_tc(const Geom& geo, int dh, int n, float scale, const __nv_bfloat16* qc,
-                              const __nv_bfloat16* qr, const float* k_gain, const __nv_bfloat16* kc,
-                              const __nv_bfloat16* kr, const __nv_bfloat16* v,
+                              const __nv_bfloat16* qr, const float* k_gain, const __nv_bfloat16* kc_sw,
+                              const __nv_bfloat16* kr_sw, const __nv_bfloat16* v_sw,
                               const int32_t* sel, int list_stride, __nv_bfloat16* out, float* lse, int* err,
                               unsigned long long* trace, long long trace_rows, cudaStream_t st);
 // CTAs the decode attention grid should have for this device (all resident at once).

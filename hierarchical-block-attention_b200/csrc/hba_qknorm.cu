@@ -113,20 +113,77 @@ __global__ void __launch_bounds__(256) append_kernel(Geom geo, int t, const int3
     reinterpret_cast<__nv_bfloat162*>(v_cache + dst)[d] = reinterpret_cast<const __nv_bfloat162*>(v_new + w * DH)[d];
 }
 
+// Element offset of (token t, dim d) of one (sequence, head) in the
+// chunk-tiled layout: per 64-token chunk, per 64-dim half, the 8 KB image a
+// 128-byte-swizzled TMA box [64 tokens x 64 dims] leaves in shared memory
+// (sw128_offset), so that one 1-D bulk copy of a chunk fills a K or V ring
+// slot in the UMMA operand layout.  row_base = first element of the
+// (sequence, head)'s chunk 0.
+template <int DH>
+HBA_DEVICE size_t chunked_offset(size_t row_base, int t, int d) {
+  constexpr int HALVES = DH / 64;
+  const int r = t & 63;
+  const int c = d & 63;
+  const uint32_t off = (uint32_t)(r * 128 + ((((c >> 3) ^ (r & 7))) << 4) + (c & 7) * 2) / 2;
+  return row_base + ((size_t)(t >> 6) * HALVES + (d >> 6)) * 4096 + off;
+}
+
+// A lane's PER consecutive elements (d = lane * PER ...) stored at their
+// chunk-tiled positions (contiguous: they sit in one 16-byte group).
+template <int DH>
+HBA_DEVICE void store_chunked(__nv_bfloat16* __restrict__ y, size_t row_base, int t, const float* v) {
+  constexpr int PER = DH / 32;
+  const int lane = threadIdx.x & 31;
+  __nv_bfloat16* dst = y + chunked_offset<DH>(row_base, t, lane * PER);
+  if constexpr (PER == 2) {
+    *reinterpret_cast<__nv_bfloat162*>(dst) = __floats2bfloat162_rn(v[0], v[1]);
+  } else {
+    uint2 u;
+    __nv_bfloat162* h = reinterpret_cast<__nv_bfloat162*>(&u);
+    h[0] = __floats2bfloat162_rn(v[0], v[1]);
+    h[1] = __floats2bfloat162_rn(v[2], v[3]);
+    *reinterpret_cast<uint2*>(dst) = u;
+  }
+}
+
 // kc and kr for every (batch, token, kv head) of a [B, n, Hkv, dh] tensor.
+// With kc_sw != nullptr (the tensor-core prefill): kc as above, and kc, its
+// RoPE'd copy and v (when given) also in the chunk-tiled layout [B, Hkv,
+// n/64, dh/64, 64 x 64] (kr itself is then not written).
 template <int DH>
 __global__ void __launch_bounds__(256) qknorm_rope_kernel(Geom geo, int n, const __nv_bfloat16* __restrict__ k,
                                                           const float* __restrict__ k_gain,
                                                           const float* __restrict__ cos,
                                                           const float* __restrict__ sin,
                                                           __nv_bfloat16* __restrict__ kc,
-                                                          __nv_bfloat16* __restrict__ kr) {
+                                                          __nv_bfloat16* __restrict__ kr,
+                                                          const __nv_bfloat16* __restrict__ v,
+                                                          __nv_bfloat16* __restrict__ kc_sw,
+                                                          __nv_bfloat16* __restrict__ kr_sw,
+                                                          __nv_bfloat16* __restrict__ v_sw) {
   const int64_t w = (int64_t)blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32;
   if (w >= (int64_t)geo.B * n * geo.Hkv) return;
   const int g = (int)(w % geo.Hkv);
   const int p = (int)((w / geo.Hkv) % n);
-  key_row<DH>(k + w * DH, kc + w * DH, kr + w * DH, geo.qknorm ? k_gain[g] : 1.f, geo.eps, geo.qknorm != 0,
-              cos + (size_t)p * DH, sin + (size_t)p * DH);
+  if (kc_sw == nullptr) {
+    key_row<DH>(k + w * DH, kc + w * DH, kr + w * DH, geo.qknorm ? k_gain[g] : 1.f, geo.eps, geo.qknorm != 0,
+                cos + (size_t)p * DH, sin + (size_t)p * DH);
+    return;
+  }
+  constexpr int PER = DH / 32;
+  const int b = (int)(w / ((int64_t)geo.Hkv * n));
+  const size_t row_base = ((size_t)b * geo.Hkv + g) * (size_t)n * DH;  // n % 64 == 0
+  float x[PER], r[PER];
+  load_head_row<DH>(k + w * DH, x);
+  if (geo.qknorm) qknorm_lane<DH>(x, k_gain[g], geo.eps);
+  store_head_row<DH>(kc + w * DH, x);
+  store_chunked<DH>(kc_sw, row_base, p, x);
+  rope_lane<DH>(x, r, cos + (size_t)p * DH, sin + (size_t)p * DH);
+  store_chunked<DH>(kr_sw, row_base, p, r);
+  if (v != nullptr) {
+    load_head_row<DH>(v + w * DH, x);
+    store_chunked<DH>(v_sw, row_base, p, x);
+  }
 }
 
 cudaError_t launch_qknorm(const __nv_bfloat16* x, __nv_bfloat16* y, const float* gain, int64_t rows, int heads,
@@ -159,14 +216,19 @@ cudaError_t launch_append(const Geom& geo, int t, const int32_t* pos, const __nv
 
 cudaError_t launch_qknorm_rope(const Geom& geo, int n, const __nv_bfloat16* k, const float* k_gain,
                                const float* cos, const float* sin, __nv_bfloat16* kc, __nv_bfloat16* kr, int dh,
-                               cudaStream_t st) {
+                               cudaStream_t st, const __nv_bfloat16* v, __nv_bfloat16* kc_sw,
+                               __nv_bfloat16* kr_sw, __nv_bfloat16* v_sw) {
   const int64_t warps = (int64_t)geo.B * n * geo.Hkv;
   const int64_t blocks = (warps + 7) / 8;
   if (blocks == 0) return cudaSuccess;
+  if (kc_sw != nullptr && (n % 64 != 0 || kr_sw == nullptr || (v != nullptr && v_sw == nullptr)))
+    return cudaErrorInvalidValue;
   if (dh == 64)
-    qknorm_rope_kernel<64><<<(unsigned)blocks, 256, 0, st>>>(geo, n, k, k_gain, cos, sin, kc, kr);
+    qknorm_rope_kernel<64><<<(unsigned)blocks, 256, 0, st>>>(geo, n, k, k_gain, cos, sin, kc, kr, v, kc_sw, kr_sw,
+                                                              v_sw);
   else
-    qknorm_rope_kernel<128><<<(unsigned)blocks, 256, 0, st>>>(geo, n, k, k_gain, cos, sin, kc, kr);
+    qknorm_rope_kernel<128><<<(unsigned)blocks, 256, 0, st>>>(geo, n, k, k_gain, cos, sin, kc, kr, v, kc_sw, kr_sw,
+                                                               v_sw);
   return cudaGetLastError();
 }
 

@@ -192,10 +192,12 @@ size_t hba_b200_prefill_workspace_size(const hba_b200_config* cfg, int32_t batch
  *   probes: [Hkv, m, dh], proj: [Hkv, dh, dh] fp32 (SlotSummarizer weights)
  *   out: [batch, n, Hq, dh] bf16; lse: [batch, Hq, n] fp32 or NULL
  *   sel_idx / sel_score: [batch, Hkv, n, k_blocks] or NULL
- * With QKNorm, block 64 and G >= 4 the union softmax runs on the tcgen05
- * tensor cores (one 128-row tile = 128/G queries x G heads, the routed blocks
- * of the tile's queries computed once and masked per row); other
- * configurations use the per-query gather kernel.  The first 4 bytes of the
+ * The flat selection runs as a tcgen05 GEMM of 128 routing queries against
+ * 128 summary rows per stage.  With QKNorm, block 64 and G >= 4 the union
+ * softmax runs on the tcgen05 tensor cores (two 128-row tiles of 128/G
+ * queries x G heads per CTA sharing one K/V stream, the routed blocks of
+ * their queries computed once and masked per row); other configurations use
+ * the per-query gather kernel.  The first 4 bytes of the
  * workspace receive a device status (zeroed by the call; 1 = a bounded device
  * wait timed out), read by hba_b200_device_status(workspace, ...).
  * Replaces hba_attention_eval (src/hba/attention.py:610-713, hier or flat)
@@ -240,11 +242,10 @@ int hba_b200_profile_events_recorded(void);
  * routed tile land, 11 last PV issued, 12 the producer sees the picks;
  * fused shard decode: 14 / 15 the first / second list exchange complete,
  * 13 the partial exchange complete.  The
- * prefill union kernel writes 16 stamps for the last query tile of each
+ * prefill union kernel writes stamps for the last pair of query tiles of each
  * (sequence, kv head) row r < bytes / 128 at buffer[r * 16 + i]: 0 start,
- * 1 chunk list built, 2 query tile ready, 3-7 and 8-12 the softmax of two
- * chunks (S ready, S read, P buffer free, P written, P handed over), 13 the
- * MMA issue of chunk 4's S, 14 softmax done, 15 end.  NULL turns it off.
+ * 1 chunk list built, 2 query tiles ready, 14 the first tile's softmax done,
+ * 15 end.  NULL turns it off.
  */
 int hba_b200_set_debug_trace(void* device_buffer, int64_t bytes);
 
