@@ -22,7 +22,7 @@
 // tile's MMAs (and the next chunk's S), so the tensor pipe and the two
 // softmax groups overlap.
 //
-// Roles (320 threads):
+// Roles (352 threads):
 //   warps 4T .. 4T+3  softmax / epilogue of tile T, one thread per row (TMEM
 //              lane): S row -> mask -> p = exp2(s*scale*log2e - M) -> P row
 //              (bf16, tcgen05.st) for the PV MMA; epilogue O/l -> out.  M is
@@ -32,7 +32,8 @@
 //              rescaled.  Otherwise M is the row's running max, raised lazily:
 //              when a chunk's max passes it by more than kRescaleLog2, the warp
 //              rescales its rows of O in TMEM (and l) before writing P.
-//   warp 8     TMEM allocation; one thread issues tcgen05.mma.
+//   warps 8, 10  one thread each issues tile 0's / tile 1's tcgen05.mma
+//              (warp 8 also owns the TMEM allocation).
 //   warp 9     one thread issues the loads: the query tiles (TMA), then K_c
 //              and V_c through a 5-slot ring, each one 1-D bulk copy of a
 //              contiguous chunk of the pre-pass's chunk-tiled K / RoPE'd K /
@@ -53,7 +54,7 @@ namespace hba {
 
 using namespace sm100;
 
-constexpr int kTcThreads = 320;
+constexpr int kTcThreads = 352;
 // ring of K or V tiles: K(c) = item 2c, V(c) = item 2c + 1 in slot item % 5.
 // With an odd slot count, V(c + 2) reuses K(c)'s slot (free once S(c) is
 // done) and K(c + 3) reuses V(c)'s (free once PV(c) is done): the load that
@@ -61,7 +62,8 @@ constexpr int kTcThreads = 320;
 constexpr int kTcSlots = 5;
 constexpr int kTcKeys = 64;            // keys per chunk
 constexpr int kTcMaxRouted = 1024;     // routed union capacity of a tile pair
-constexpr int kTcMma = 8;              // MMA warp
+constexpr int kTcMma = 8;              // MMA warp of tile 0 (and TMEM owner)
+constexpr int kTcMma2 = 10;            // MMA warp of tile 1
 constexpr int kTcTma = 9;              // TMA warp
 
 enum ChunkType : uint32_t { kSink = 0, kWindow = 1, kRouted = 2 };
@@ -77,7 +79,7 @@ struct TcSmem {
   // the routed union: block ids and the pair's query masks (bit q: query i0 + q picked it)
   unsigned long long rmask[kTcMaxRouted];
   uint16_t rblk[kTcMaxRouted];
-  uint64_t q_ready, drain;
+  uint64_t q_ready, drain[2];
   uint64_t full[kTcSlots], empty[kTcSlots];
   uint64_t s_full[2], s_free[2], o_full[2];
   uint64_t p_full[2][2], p_free[2][2];  // [tile][P buffer]
@@ -190,10 +192,11 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   }
   if (tid == 0) {
     mbar_init(&sm.q_ready, 1);  // the query tiles' TMA
-    mbar_init(&sm.drain, 1);
+    mbar_init(&sm.drain[0], 1);
+    mbar_init(&sm.drain[1], 1);
     for (int s = 0; s < kTcSlots; ++s) {
       mbar_init(&sm.full[s], 1);
-      mbar_init(&sm.empty[s], 1);
+      mbar_init(&sm.empty[s], 2);  // one commit per MMA issuer
     }
     for (int t = 0; t < 2; ++t) {
       mbar_init(&sm.s_full[t], 1);
@@ -278,33 +281,38 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         bulk_load(sm.ring[st], src + (size_t)(ck.kb / kTcKeys) * (KB / 2), KB, &sm.full[st]);
       }
     }
-  } else if (warp == kTcMma) {
-    // ---------------- MMA issuer ----------------
+  } else if (warp == kTcMma || warp == kTcMma2) {
+    // ---------------- MMA issuers: one thread per tile ----------------
+    // Each tile's S and PV MMAs are issued by its own thread, so a tile whose
+    // softmax is ready is never held behind the other tile's issue; a K or V
+    // slot is released once both issuers have committed it.  An issuer waits
+    // for every item to land, also one its tile skips, before committing it:
+    // so neither can commit a slot's next use before the other's arrival
+    // for the current one (the empty barriers count two arrivals a phase).
     if (lane == 0) {
+      const int t = warp == kTcMma ? 0 : 1;
       constexpr uint32_t idesc_s = idesc_bf16(128, kTcKeys, false, false);
       constexpr uint32_t idesc_o = idesc_bf16(128, DH, false, true);
+      const uint32_t tt = tmem + (uint32_t)(t * 256);
       bool ok = mbar_wait(&sm.q_ready, 0, p.err);
       tc_fence_after();
-      int ns[2] = {0, 0}, np[2] = {0, 0};  // S and PV MMAs issued per tile
+      int ns = 0, np = 0;  // S and PV MMAs this tile has issued
       auto pv = [&](int c) -> bool {
         const int iv = 2 * c + 1, st = iv % kTcSlots;
-        const uint32_t need = chunk(c).need;
         if (!mbar_wait(&sm.full[st], (iv / kTcSlots) & 1, p.err)) return false;
-        const uint32_t va = smem_u32(sm.ring[st]);
-        for (int t = 0; t < 2; ++t) {
-          if (!((need >> t) & 1u)) continue;
-          const int pb = np[t] & 1;  // P buffer of this tile's np[t]-th chunk
-          if (!mbar_wait(&sm.p_full[t][pb], (np[t] >> 1) & 1, p.err)) return false;
+        if ((chunk(c).need >> t) & 1u) {
+          const int pb = np & 1;  // P buffer of this tile's np-th chunk
+          if (!mbar_wait(&sm.p_full[t][pb], (np >> 1) & 1, p.err)) return false;
           tc_fence_after();
-          const uint32_t tt = tmem + (uint32_t)(t * 256);
+          const uint32_t va = smem_u32(sm.ring[st]);
 #pragma unroll
           for (int kk = 0; kk < kTcKeys / 16; ++kk)  // K = 16 keys = 8 packed columns of P per MMA
             umma_f16_ts(tt + 128, tt + 64 + pb * 32 + kk * 8, sdesc_sw128(va + kk * 2048, 8192, 1024), idesc_o,
-                        (np[t] > 0 || kk > 0) ? 1u : 0u);
+                        (np > 0 || kk > 0) ? 1u : 0u);
           umma_commit(&sm.p_free[t][pb]);
-          ++np[t];
+          ++np;
         }
-        umma_commit(&sm.empty[st]);
+        umma_commit(&sm.empty[st]);  // this issuer is done with the V tile
         return true;
       };
       for (int c = 0; ok && c < NCH; ++c) {
@@ -314,34 +322,32 @@ __global__ void __launch_bounds__(kTcThreads, 1)
           ok = false;
           break;
         }
-        const uint32_t type = ck.type;
-        const uint32_t ka = smem_u32(sm.ring[st]);
-        for (int t = 0; t < 2 && ok; ++t) {
-          if (!((ck.need >> t) & 1u)) continue;
+        if ((ck.need >> t) & 1u) {
           // the tile's S buffer is free once its softmax has read the previous S
-          if (ns[t] > 0 && !mbar_wait(&sm.s_free[t], (ns[t] - 1) & 1, p.err)) {
+          if (ns > 0 && !mbar_wait(&sm.s_free[t], (ns - 1) & 1, p.err)) {
             ok = false;
             break;
           }
           tc_fence_after();
-          const uint32_t qa = smem_u32(type == kWindow ? sm.qr[t] : sm.qc[t]);
+          const uint32_t qa = smem_u32(ck.type == kWindow ? sm.qr[t] : sm.qc[t]);
+          const uint32_t ka = smem_u32(sm.ring[st]);
 #pragma unroll
           for (int kk = 0; kk < DH / 16; ++kk) {
             const int h = kk >> 2, ko = (kk & 3) * 32;
-            umma_f16(tmem + (uint32_t)(t * 256), sdesc_sw128(qa + h * 16384 + ko, 16, 1024),
-                     sdesc_sw128(ka + h * 8192 + ko, 16, 1024), idesc_s, kk > 0 ? 1u : 0u);
+            umma_f16(tt, sdesc_sw128(qa + h * 16384 + ko, 16, 1024), sdesc_sw128(ka + h * 8192 + ko, 16, 1024),
+                     idesc_s, kk > 0 ? 1u : 0u);
           }
           umma_commit(&sm.s_full[t]);
-          ++ns[t];
+          ++ns;
         }
-        umma_commit(&sm.empty[st]);  // the K tile is free once its S MMAs are done
-        if (ok && c >= 1 && !pv(c - 1)) ok = false;
+        umma_commit(&sm.empty[st]);  // this issuer is done with the K tile
+        if (c >= 1 && !pv(c - 1)) ok = false;
       }
       if (ok && NCH >= 1) ok = pv(NCH - 1);
-      for (int t = 0; t < 2; ++t) umma_commit(&sm.o_full[t]);
-      // drain: every MMA issued above is complete before TMEM can be released
-      umma_commit(&sm.drain);
-      mbar_wait(&sm.drain, 0, p.err);
+      umma_commit(&sm.o_full[t]);
+      // drain: every MMA this thread issued is complete before TMEM can be released
+      umma_commit(&sm.drain[t]);
+      mbar_wait(&sm.drain[t], 0, p.err);
     }
   } else {
     // ---------------- softmax / epilogue of tile t, one thread per row ----------------
