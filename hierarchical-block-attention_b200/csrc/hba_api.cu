@@ -519,7 +519,6 @@ int hba_b200_prefill(const hba_b200_config* cfg, int32_t batch, int32_t n, float
       ((sel_idx == nullptr) != (sel_score == nullptr)) || !std::isfinite(scale))
     return HBA_B200_ERR_INVALID_ARGUMENT;
   if (n % cfg->block != 0) return HBA_B200_ERR_NOT_BLOCK_MULTIPLE;
-  if (n > 65535) return HBA_B200_ERR_UNSUPPORTED;  // query index rides gridDim.y
   const size_t need = hba_b200_prefill_workspace_size(cfg, batch, n);
   if (workspace == nullptr || workspace_bytes < need) return HBA_B200_ERR_WORKSPACE;
   const int dh = cfg->head_dim;
@@ -564,6 +563,8 @@ int hba_b200_prefill(const hba_b200_config* cfg, int32_t batch, int32_t n, float
   const bool want_tc = !(force != nullptr && strcmp(force, "gather") == 0);
   const bool v_aligned = (reinterpret_cast<uintptr_t>(v) & 15u) == 0;
   const bool use_tc = want_tc && v_aligned && kc_sw != nullptr && n_lists == 1;
+  // the per-query selection and gather kernels put the query index in gridDim.y
+  if (n > 65535 && !((tc_sel || tile_sel) && use_tc)) return HBA_B200_ERR_UNSUPPORTED;
 
   prof_begin(stream);
   cudaError_t e = cudaMemsetAsync(dev_status, 0, sizeof(int), stream);

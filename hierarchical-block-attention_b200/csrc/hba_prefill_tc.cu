@@ -137,6 +137,37 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   };
   if (tid == 0) stamp(0);
 
+  // ---- barriers, then the query tiles' TMA, which needs no chunk list and
+  // lands while the list is built ----
+  if (tid == kTcTma * 32) {
+    mbar_init(&sm.q_ready, 1);
+    mbar_init(&sm.drain[0], 1);
+    mbar_init(&sm.drain[1], 1);
+    for (int s = 0; s < kTcSlots; ++s) {
+      mbar_init(&sm.full[s], 1);
+      mbar_init(&sm.empty[s], 2);  // one commit per MMA issuer
+    }
+    for (int t = 0; t < 2; ++t) {
+      mbar_init(&sm.s_full[t], 1);
+      mbar_init(&sm.s_free[t], 128);
+      mbar_init(&sm.o_full[t], 1);
+      for (int u = 0; u < 2; ++u) {
+        mbar_init(&sm.p_full[t][u], 128);
+        mbar_init(&sm.p_free[t][u], 1);
+      }
+    }
+    fence_barrier_init();
+    // rows r = query * G + head, QKNorm'd (qc) and RoPE'd (qr) by the pre-pass;
+    // a box is G heads x QT queries (G * QT <= 128 rows: 126 when G = 7) of 128 bytes, per half
+    const int ntile = nq1 > 0 ? 2 : 1;
+    mbar_arrive_expect_tx(&sm.q_ready, (uint32_t)(ntile * 2 * HALVES * G * QT * 128));
+    for (int t = 0; t < ntile; ++t)
+      for (int h = 0; h < HALVES; ++h) {
+        tma_load_4d(sm.qc[t] + h * 16384, &tm_qc, h * 64, g * G, i0 + t * QT, b, &sm.q_ready);
+        tma_load_4d(sm.qr[t] + h * 16384, &tm_qr, h * 64, g * G, i0 + t * QT, b, &sm.q_ready);
+      }
+  }
+
   // ---- chunk list: sinks, window, routed union (all threads) ----
   // [nb] 64-bit query masks of the pair, overlaying the ring before its first use
   unsigned long long* mask = reinterpret_cast<unsigned long long*>(sm.ring[0]);
@@ -189,25 +220,6 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         ++o;
       }
     }
-  }
-  if (tid == 0) {
-    mbar_init(&sm.q_ready, 1);  // the query tiles' TMA
-    mbar_init(&sm.drain[0], 1);
-    mbar_init(&sm.drain[1], 1);
-    for (int s = 0; s < kTcSlots; ++s) {
-      mbar_init(&sm.full[s], 1);
-      mbar_init(&sm.empty[s], 2);  // one commit per MMA issuer
-    }
-    for (int t = 0; t < 2; ++t) {
-      mbar_init(&sm.s_full[t], 1);
-      mbar_init(&sm.s_free[t], 128);
-      mbar_init(&sm.o_full[t], 1);
-      for (int u = 0; u < 2; ++u) {
-        mbar_init(&sm.p_full[t][u], 128);
-        mbar_init(&sm.p_free[t][u], 1);
-      }
-    }
-    fence_barrier_init();
   }
   if (warp == kTcMma) {
     tmem_alloc(&sm.tmem_base, 512);
@@ -263,15 +275,6 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   if (warp == kTcTma) {
     // ---------------- TMA producer ----------------
     if (lane == 0) {
-      // the query tiles: rows r = query * G + head, QKNorm'd (qc) and RoPE'd (qr) by the pre-pass;
-      // a box is G heads x QT queries (G * QT <= 128 rows: 126 when G = 7) of 128 bytes, per half
-      const int ntile = nq1 > 0 ? 2 : 1;
-      mbar_arrive_expect_tx(&sm.q_ready, (uint32_t)(ntile * 2 * HALVES * G * QT * 128));
-      for (int t = 0; t < ntile; ++t)
-        for (int h = 0; h < HALVES; ++h) {
-          tma_load_4d(sm.qc[t] + h * 16384, &tm_qc, h * 64, g * G, i0 + t * QT, b, &sm.q_ready);
-          tma_load_4d(sm.qr[t] + h * 16384, &tm_qr, h * 64, g * G, i0 + t * QT, b, &sm.q_ready);
-        }
       for (int it = 0; it < 2 * NCH; ++it) {
         const int st = it % kTcSlots, u = it / kTcSlots;
         if (it >= kTcSlots && !mbar_wait(&sm.empty[st], (u - 1) & 1, p.err)) break;
