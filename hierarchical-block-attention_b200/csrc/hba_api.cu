@@ -489,17 +489,17 @@ int hba_b200_decode(const hba_b200_config* cfg, int32_t batch, int32_t n_cap, co
   return HBA_B200_OK;
 }
 
-size_t hba_b200_prefill_workspace_size(const hba_b200_config* cfg, int32_t batch, int32_t n) {
+size_t hba_b200_prefill_range_workspace_size(const hba_b200_config* cfg, int32_t batch, int32_t n, int32_t n_q) {
   int st = HBA_B200_OK;
-  if (!config_ok(cfg, &st) || batch <= 0 || n <= 0 || n % cfg->block != 0) return 0;
+  if (!config_ok(cfg, &st) || batch <= 0 || n <= 0 || n % cfg->block != 0 || n_q <= 0 || n_q > n) return 0;
   const int dh = cfg->head_dim;
   const size_t nb = (size_t)n / cfg->block;
   const size_t ns = cfg->hier ? (nb + cfg->fanout - 1) / cfg->fanout : 0;
   const Plan plan = make_plan(cfg, (int)nb, batch * cfg->n_kv, false);
-  const size_t queries = (size_t)batch * cfg->n_kv * n;
+  const size_t queries = (size_t)batch * cfg->n_kv * n_q;
   size_t b = kAlign;                                                      // device status word
   b += 2 * align_up((size_t)batch * n * cfg->n_kv * dh * 2);              // QKNorm'd keys and their RoPE'd copy
-  b += 2 * align_up((size_t)batch * n * cfg->n_heads * dh * 2);           // the same for the queries
+  b += 2 * align_up((size_t)batch * n_q * cfg->n_heads * dh * 2);         // the same for the queries
   b += align_up((size_t)batch * cfg->n_kv * nb * cfg->slots * dh * 2);    // summaries
   b += align_up((size_t)batch * cfg->n_kv * ns * cfg->slots * dh * 2);    // supers
   if (prefill_tc_config(cfg, batch, n))                                    // chunk-tiled K, RoPE'd K, V
@@ -508,18 +508,33 @@ size_t hba_b200_prefill_workspace_size(const hba_b200_config* cfg, int32_t batch
   return b;
 }
 
+size_t hba_b200_prefill_workspace_size(const hba_b200_config* cfg, int32_t batch, int32_t n) {
+  return hba_b200_prefill_range_workspace_size(cfg, batch, n, n);
+}
+
 int hba_b200_prefill(const hba_b200_config* cfg, int32_t batch, int32_t n, float scale, const void* q, const void* k,
                      const void* v, const float* cos, const float* sin, const float* q_gain, const float* k_gain,
                      const float* probes, const float* proj, void* out, float* lse, int32_t* sel_idx,
                      float* sel_score, void* workspace, size_t workspace_bytes, cudaStream_t stream) {
+  return hba_b200_prefill_range(cfg, batch, n, 0, n, scale, q, k, v, cos, sin, q_gain, k_gain, probes, proj, out, lse,
+                                sel_idx, sel_score, workspace, workspace_bytes, stream);
+}
+
+int hba_b200_prefill_range(const hba_b200_config* cfg, int32_t batch, int32_t n, int32_t q_lo, int32_t n_q,
+                           float scale, const void* q, const void* k, const void* v, const float* cos,
+                           const float* sin, const float* q_gain, const float* k_gain, const float* probes,
+                           const float* proj, void* out, float* lse, int32_t* sel_idx, float* sel_score,
+                           void* workspace, size_t workspace_bytes, cudaStream_t stream) {
   int st = HBA_B200_OK;
   if (!config_ok(cfg, &st)) return st;
   if (batch <= 0 || n <= 0 || q == nullptr || k == nullptr || v == nullptr || cos == nullptr || sin == nullptr ||
       probes == nullptr || proj == nullptr || out == nullptr || (cfg->qknorm && (q_gain == nullptr || k_gain == nullptr)) ||
-      ((sel_idx == nullptr) != (sel_score == nullptr)) || !std::isfinite(scale))
+      ((sel_idx == nullptr) != (sel_score == nullptr)) || !std::isfinite(scale) || q_lo < 0 || n_q <= 0 ||
+      q_lo > n - n_q)
     return HBA_B200_ERR_INVALID_ARGUMENT;
   if (n % cfg->block != 0) return HBA_B200_ERR_NOT_BLOCK_MULTIPLE;
-  const size_t need = hba_b200_prefill_workspace_size(cfg, batch, n);
+  const bool ranged = q_lo != 0 || n_q != n;
+  const size_t need = hba_b200_prefill_range_workspace_size(cfg, batch, n, n_q);
   if (workspace == nullptr || workspace_bytes < need) return HBA_B200_ERR_WORKSPACE;
   const int dh = cfg->head_dim;
   const size_t nb = (size_t)n / cfg->block;
@@ -532,9 +547,9 @@ int hba_b200_prefill(const hba_b200_config* cfg, int32_t batch, int32_t n, float
   __nv_bfloat16* kr = reinterpret_cast<__nv_bfloat16*>(ws);
   ws += align_up((size_t)batch * n * cfg->n_kv * dh * 2);
   __nv_bfloat16* qcn = reinterpret_cast<__nv_bfloat16*>(ws);  // queries QKNorm'd
-  ws += align_up((size_t)batch * n * cfg->n_heads * dh * 2);
+  ws += align_up((size_t)batch * n_q * cfg->n_heads * dh * 2);
   __nv_bfloat16* qrn = reinterpret_cast<__nv_bfloat16*>(ws);  // and RoPE'd at their positions
-  ws += align_up((size_t)batch * n * cfg->n_heads * dh * 2);
+  ws += align_up((size_t)batch * n_q * cfg->n_heads * dh * 2);
   __nv_bfloat16* summ = reinterpret_cast<__nv_bfloat16*>(ws);
   ws += align_up((size_t)batch * cfg->n_kv * nb * cfg->slots * dh * 2);
   __nv_bfloat16* sup = reinterpret_cast<__nv_bfloat16*>(ws);
@@ -548,7 +563,7 @@ int hba_b200_prefill(const hba_b200_config* cfg, int32_t batch, int32_t n, float
     ws += 3 * kv_bytes;
   }
 
-  Geom geo = make_geom(cfg, batch, n, n);
+  Geom geo = make_geom(cfg, batch, n_q, n);  // n_q queries per sequence over n keys
   const Plan plan = make_plan(cfg, (int)nb, batch * cfg->n_kv, false);
   // selection: the tcgen05 selection GEMM; HBA_B200_SELECT_PATH=tile forces the
   // query-tiled CUDA-core kernel, =scan the per-query kernel
@@ -563,8 +578,9 @@ int hba_b200_prefill(const hba_b200_config* cfg, int32_t batch, int32_t n, float
   const bool want_tc = !(force != nullptr && strcmp(force, "gather") == 0);
   const bool v_aligned = (reinterpret_cast<uintptr_t>(v) & 15u) == 0;
   const bool use_tc = want_tc && v_aligned && kc_sw != nullptr && n_lists == 1;
-  // the per-query selection and gather kernels put the query index in gridDim.y
-  if (n > 65535 && !((tc_sel || tile_sel) && use_tc)) return HBA_B200_ERR_UNSUPPORTED;
+  // the per-query selection and gather kernels put the query index in gridDim.y;
+  // a query range runs on the tensor-core selection and union only
+  if ((n > 65535 || ranged) && !(tc_sel && use_tc)) return HBA_B200_ERR_UNSUPPORTED;
 
   prof_begin(stream);
   cudaError_t e = cudaMemsetAsync(dev_status, 0, sizeof(int), stream);
@@ -572,10 +588,11 @@ int hba_b200_prefill(const hba_b200_config* cfg, int32_t batch, int32_t n, float
   e = hba::launch_qknorm_rope(geo, n, static_cast<const __nv_bfloat16*>(k), k_gain, cos, sin, kc, kr, dh, stream,
                               use_tc ? static_cast<const __nv_bfloat16*>(v) : nullptr, use_tc ? kc_sw : nullptr,
                               kr_sw, v_sw);
-  if (e == cudaSuccess) {  // the same pre-pass over the query heads (the gain per query head)
+  if (e == cudaSuccess) {  // the same pre-pass over the query heads (the gain per query head), at positions q_lo..
     Geom gq = geo;
     gq.Hkv = geo.Hq;
-    e = hba::launch_qknorm_rope(gq, n, static_cast<const __nv_bfloat16*>(q), q_gain, cos, sin, qcn, qrn, dh, stream);
+    e = hba::launch_qknorm_rope(gq, n_q, static_cast<const __nv_bfloat16*>(q), q_gain, cos, sin, qcn, qrn, dh, stream,
+                                nullptr, nullptr, nullptr, nullptr, q_lo);
   }
   if (e != cudaSuccess) return cuda_status(e);
   prof_mark(stream);
@@ -587,11 +604,11 @@ int hba_b200_prefill(const hba_b200_config* cfg, int32_t batch, int32_t n, float
     if (e != cudaSuccess) return cuda_status(e);
     prof_mark(stream);
   }
-  hba::QueryPos qp{nullptr, nullptr, n, scale};
+  hba::QueryPos qp{nullptr, nullptr, n, scale};  // n keys; local query t sits at position q_lo + t
   Lists fin{};
   int fin_lists = 0, fin_k = 0;
   if (tc_sel || tile_sel) {
-    fin = carve_lists(ws, (size_t)batch * cfg->n_kv * n * cfg->k_blocks);
+    fin = carve_lists(ws, (size_t)batch * cfg->n_kv * n_q * cfg->k_blocks);
     hba::SelParams sp{};
     sp.geo = geo;
     sp.qp = qp;
@@ -607,6 +624,7 @@ int hba_b200_prefill(const hba_b200_config* cfg, int32_t batch, int32_t n, float
     sp.own_blo = 0;
     sp.own_bhi = INT_MAX;
     sp.n_limit = geo.n_cap;
+    sp.q_off = q_lo;
     e = tc_sel ? hba::launch_select_tc(sp, dh, dev_status, stream) : hba::launch_select_tile(sp, dh, dev_status, stream);
     if (e != cudaSuccess) return cuda_status(e);
     prof_mark(stream);
@@ -619,8 +637,9 @@ int hba_b200_prefill(const hba_b200_config* cfg, int32_t batch, int32_t n, float
   }
   if (use_tc) {
     if (fin_lists != 1) return HBA_B200_ERR_UNSUPPORTED;  // (n_lists predicted it: never taken)
-    e = hba::launch_prefill_tc(geo, dh, n, scale, qcn, qrn, k_gain, kc_sw, kr_sw, v_sw, fin.idx, fin_lists * fin_k,
-                               static_cast<__nv_bfloat16*>(out), lse, dev_status, g_trace, g_trace_ctas, stream);
+    e = hba::launch_prefill_tc(geo, dh, n, q_lo, scale, qcn, qrn, k_gain, kc_sw, kr_sw, v_sw, fin.idx,
+                               fin_lists * fin_k, static_cast<__nv_bfloat16*>(out), lse, dev_status, g_trace,
+                               g_trace_ctas, stream);
     if (e != cudaSuccess) return cuda_status(e);
     prof_mark(stream);
     g_last_kernels = cfg->hier ? "qknorm_rope_kernel+summarize_kernel+supers_kernel+select_kernel+select_kernel+"
@@ -630,8 +649,8 @@ int hba_b200_prefill(const hba_b200_config* cfg, int32_t batch, int32_t n, float
                                                        "prefill_tc_kernel"
                                                      : "qknorm_rope_kernel+summarize_kernel+select_kernel+"
                                                        "prefill_tc_kernel"));
-    if (sel_idx != nullptr) {  // the single-split lists are the final picks, layout [B, Hkv, n, K]
-      const size_t bytes = (size_t)batch * cfg->n_kv * n * cfg->k_blocks * sizeof(int32_t);
+    if (sel_idx != nullptr) {  // the single-split lists are the final picks, layout [B, Hkv, n_q, K]
+      const size_t bytes = (size_t)batch * cfg->n_kv * n_q * cfg->k_blocks * sizeof(int32_t);
       e = cudaMemcpyAsync(sel_idx, fin.idx, bytes, cudaMemcpyDeviceToDevice, stream);
       if (e == cudaSuccess) e = cudaMemcpyAsync(sel_score, fin.score, bytes, cudaMemcpyDeviceToDevice, stream);
       if (e != cudaSuccess) return cuda_status(e);

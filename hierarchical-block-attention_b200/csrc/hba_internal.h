@@ -80,6 +80,7 @@ struct SelParams {
   int32_t own_blo, own_bhi;
   int32_t n_limit;  // longest valid context (one GPU: n_cap; a shard: the global capacity)
   int32_t q_normed;  // q is already QKNorm'd (select_tile_kernel only)
+  int32_t q_off;     // position of local query 0 (select_tc_kernel: a query range of the sequence)
 };
 
 struct AttnParams {
@@ -148,7 +149,7 @@ cudaError_t launch_append(const Geom& geo, int t, const int32_t* pos, const __nv
 cudaError_t launch_qknorm_rope(const Geom& geo, int n, const __nv_bfloat16* k, const float* k_gain,
                                const float* cos, const float* sin, __nv_bfloat16* kc, __nv_bfloat16* kr, int dh,
                                cudaStream_t st, const __nv_bfloat16* v = nullptr, __nv_bfloat16* kc_sw = nullptr,
-                               __nv_bfloat16* kr_sw = nullptr, __nv_bfloat16* v_sw = nullptr);
+                               __nv_bfloat16* kr_sw = nullptr, __nv_bfloat16* v_sw = nullptr, int pos0 = 0);
 // Summaries of blocks [blk_begin, blk_end) for every sequence; if pos/t are
 // given (append), only blocks completed by tokens [pos[b], pos[b]+t) of
 // sequence b are rebuilt.
@@ -201,7 +202,8 @@ bool prefill_tc_supported(const Geom& geo, int dh, int n, bool qknorm);
 // qc / qr: the queries QKNorm'd and RoPE'd by the pre-pass, [B, n, Hq, dh] bf16;
 // kc_sw / kr_sw / v_sw: the keys QKNorm'd, RoPE'd, and the values, in the
 // pre-pass's chunk-tiled layout.
-cudaError_t launch_prefill_tc(const Geom& geo, int dh, int n, float scale, const __nv_bfloat16* qc,
+// geo.nq local queries at positions q_off .. over n keys.
+cudaError_t launch_prefill_tc(const Geom& geo, int dh, int n, int q_off, float scale, const __nv_bfloat16* qc,
                               const __nv_bfloat16* qr, const float* k_gain, const __nv_bfloat16* kc_sw,
                               const __nv_bfloat16* kr_sw, const __nv_bfloat16* v_sw,
                               const int32_t* sel, int list_stride, __nv_bfloat16* out, float* lse, int* err,

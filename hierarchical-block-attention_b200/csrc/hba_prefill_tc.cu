@@ -91,8 +91,9 @@ struct TcSmem {
 static_assert(sizeof(TcSmem<128>) + 1024 <= 232448, "prefill tile set exceeds the 227 KB of shared memory");
 
 struct PrefillTcParams {
-  Geom geo;
+  Geom geo;            // geo.nq local queries (positions q_off ..) over n keys
   int n;
+  int q_off;
   float scale;
   int QT;              // queries per tile
   int pairs;           // tile pairs per (sequence, kv head)
@@ -125,8 +126,10 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   const int pair = p.pairs - 1 - (int)(blockIdx.x % p.pairs);  // the latest (longest) pairs first
   const int bg = blockIdx.x / p.pairs;
   const int b = bg / geo.Hkv, g = bg % geo.Hkv;
-  const int i0 = pair * 2 * QT;
-  const int nq2 = min(2 * QT, n - i0);         // queries of the pair
+  const int nql = geo.nq;                      // local queries; local query t sits at position q_off + t
+  const int li0 = pair * 2 * QT;               // the pair's first local query
+  const int i0 = p.q_off + li0;                // ... and its position
+  const int nq2 = min(2 * QT, nql - li0);      // queries of the pair
   const int nq0 = min(QT, nq2), nq1 = max(0, nq2 - QT);  // queries of tile 0, tile 1
   auto nqt = [&](int t) { return t == 0 ? nq0 : nq1; };
   const int nb = n / geo.Bk;
@@ -163,8 +166,8 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     mbar_arrive_expect_tx(&sm.q_ready, (uint32_t)(ntile * 2 * HALVES * G * QT * 128));
     for (int t = 0; t < ntile; ++t)
       for (int h = 0; h < HALVES; ++h) {
-        tma_load_4d(sm.qc[t] + h * 16384, &tm_qc, h * 64, g * G, i0 + t * QT, b, &sm.q_ready);
-        tma_load_4d(sm.qr[t] + h * 16384, &tm_qr, h * 64, g * G, i0 + t * QT, b, &sm.q_ready);
+        tma_load_4d(sm.qc[t] + h * 16384, &tm_qc, h * 64, g * G, li0 + t * QT, b, &sm.q_ready);
+        tma_load_4d(sm.qr[t] + h * 16384, &tm_qr, h * 64, g * G, li0 + t * QT, b, &sm.q_ready);
       }
   }
 
@@ -174,7 +177,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   for (int i = tid; i < nb; i += kTcThreads) mask[i] = 0ull;
   __syncthreads();
   {
-    const int32_t* sel = p.sel + ((size_t)bg * n + i0) * p.list_stride;
+    const int32_t* sel = p.sel + ((size_t)bg * nql + li0) * p.list_stride;
     for (int e = tid; e < nq2 * p.list_stride; e += kTcThreads) {
       const int blk = sel[e];
       if (blk >= 0 && blk < nb) atomicOr(&mask[blk], 1ull << (e / p.list_stride));
@@ -357,7 +360,8 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     const int t = warp >> 2;
     const int r = tid - 128 * t;
     const int qt = r / G, hh = r % G;
-    const int i = i0 + t * QT + qt;
+    const int i = i0 + t * QT + qt;          // position
+    const int li = li0 + t * QT + qt;        // local query
     const bool row_ok = (r < QT * G) && (qt < nqt(t));
     const int hq = g * G + hh;
     const uint32_t lane_off = (uint32_t)((warp & 3) * 32) << 16;
@@ -495,7 +499,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
           for (int q = 0; q < 32; ++q) o[q] = 0.f;
         }
         if (row_ok) {
-          uint4* dst = reinterpret_cast<uint4*>(p.out + (((size_t)b * n + i) * geo.Hq + hq) * DH + cb * 32);
+          uint4* dst = reinterpret_cast<uint4*>(p.out + (((size_t)b * nql + li) * geo.Hq + hq) * DH + cb * 32);
 #pragma unroll
           for (int q4 = 0; q4 < 4; ++q4)
             dst[q4] = make_uint4(pack_bf16x2(o[q4 * 8 + 0] * inv, o[q4 * 8 + 1] * inv),
@@ -505,7 +509,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         }
       }
       if (row_ok && p.lse != nullptr)
-        p.lse[((size_t)b * geo.Hq + hq) * n + i] = l > 0.f ? (M + log2f(l)) * 0.6931471805599453f : neg_inf();
+        p.lse[((size_t)b * geo.Hq + hq) * nql + li] = l > 0.f ? (M + log2f(l)) * 0.6931471805599453f : neg_inf();
     }
   }
   tc_fence_before();
@@ -552,7 +556,7 @@ bool prefill_tc_supported(const Geom& geo, int dh, int n, bool qknorm) {
          geo.W <= 1024 && encode_fn() != nullptr;
 }
 
-cudaError_t launch_prefill_tc(const Geom& geo, int dh, int n, float scale, const __nv_bfloat16* qc,
+cudaError_t launch_prefill_tc(const Geom& geo, int dh, int n, int q_off, float scale, const __nv_bfloat16* qc,
                               const __nv_bfloat16* qr, const float* k_gain, const __nv_bfloat16* kc_sw,
                               const __nv_bfloat16* kr_sw, const __nv_bfloat16* v_sw,
                               const int32_t* sel, int list_stride, __nv_bfloat16* out, float* lse, int* err,
@@ -561,7 +565,8 @@ cudaError_t launch_prefill_tc(const Geom& geo, int dh, int n, float scale, const
   const int QT = 128 / geo.G;
   if (n % kTcKeys != 0 || ((reinterpret_cast<uintptr_t>(kc_sw) | reinterpret_cast<uintptr_t>(kr_sw) |
                             reinterpret_cast<uintptr_t>(v_sw)) & 15u) != 0 ||
-      !make_map(&m_qc, qc, geo.B, n, geo.Hq, dh, geo.G, QT) || !make_map(&m_qr, qr, geo.B, n, geo.Hq, dh, geo.G, QT))
+      !make_map(&m_qc, qc, geo.B, geo.nq, geo.Hq, dh, geo.G, QT) ||
+      !make_map(&m_qr, qr, geo.B, geo.nq, geo.Hq, dh, geo.G, QT))
     return cudaErrorInvalidValue;
   PrefillTcParams p{};
   p.kc = kc_sw;
@@ -569,9 +574,10 @@ cudaError_t launch_prefill_tc(const Geom& geo, int dh, int n, float scale, const
   p.v = v_sw;
   p.geo = geo;
   p.n = n;
+  p.q_off = q_off;
   p.scale = scale;
   p.QT = 128 / geo.G;
-  p.pairs = (n + 2 * p.QT - 1) / (2 * p.QT);
+  p.pairs = (geo.nq + 2 * p.QT - 1) / (2 * p.QT);
   p.k_gain = k_gain;
   p.sel = sel;
   p.list_stride = list_stride;

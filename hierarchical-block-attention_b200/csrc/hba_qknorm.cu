@@ -160,11 +160,11 @@ __global__ void __launch_bounds__(256) qknorm_rope_kernel(Geom geo, int n, const
                                                           const __nv_bfloat16* __restrict__ v,
                                                           __nv_bfloat16* __restrict__ kc_sw,
                                                           __nv_bfloat16* __restrict__ kr_sw,
-                                                          __nv_bfloat16* __restrict__ v_sw) {
+                                                          __nv_bfloat16* __restrict__ v_sw, int pos0) {
   const int64_t w = (int64_t)blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32;
   if (w >= (int64_t)geo.B * n * geo.Hkv) return;
   const int g = (int)(w % geo.Hkv);
-  const int p = (int)((w / geo.Hkv) % n);
+  const int p = pos0 + (int)((w / geo.Hkv) % n);  // the row's position (RoPE tables row)
   if (kc_sw == nullptr) {
     key_row<DH>(k + w * DH, kc + w * DH, kr + w * DH, geo.qknorm ? k_gain[g] : 1.f, geo.eps, geo.qknorm != 0,
                 cos + (size_t)p * DH, sin + (size_t)p * DH);
@@ -172,7 +172,7 @@ __global__ void __launch_bounds__(256) qknorm_rope_kernel(Geom geo, int n, const
   }
   constexpr int PER = DH / 32;
   const int b = (int)(w / ((int64_t)geo.Hkv * n));
-  const size_t row_base = ((size_t)b * geo.Hkv + g) * (size_t)n * DH;  // n % 64 == 0
+  const size_t row_base = ((size_t)b * geo.Hkv + g) * (size_t)n * DH;  // n % 64 == 0, pos0 == 0
   float x[PER], r[PER];
   load_head_row<DH>(k + w * DH, x);
   if (geo.qknorm) qknorm_lane<DH>(x, k_gain[g], geo.eps);
@@ -217,18 +217,18 @@ cudaError_t launch_append(const Geom& geo, int t, const int32_t* pos, const __nv
 cudaError_t launch_qknorm_rope(const Geom& geo, int n, const __nv_bfloat16* k, const float* k_gain,
                                const float* cos, const float* sin, __nv_bfloat16* kc, __nv_bfloat16* kr, int dh,
                                cudaStream_t st, const __nv_bfloat16* v, __nv_bfloat16* kc_sw,
-                               __nv_bfloat16* kr_sw, __nv_bfloat16* v_sw) {
+                               __nv_bfloat16* kr_sw, __nv_bfloat16* v_sw, int pos0) {
   const int64_t warps = (int64_t)geo.B * n * geo.Hkv;
   const int64_t blocks = (warps + 7) / 8;
   if (blocks == 0) return cudaSuccess;
-  if (kc_sw != nullptr && (n % 64 != 0 || kr_sw == nullptr || (v != nullptr && v_sw == nullptr)))
+  if (kc_sw != nullptr && (n % 64 != 0 || pos0 != 0 || kr_sw == nullptr || (v != nullptr && v_sw == nullptr)))
     return cudaErrorInvalidValue;
   if (dh == 64)
     qknorm_rope_kernel<64><<<(unsigned)blocks, 256, 0, st>>>(geo, n, k, k_gain, cos, sin, kc, kr, v, kc_sw, kr_sw,
-                                                              v_sw);
+                                                              v_sw, pos0);
   else
     qknorm_rope_kernel<128><<<(unsigned)blocks, 256, 0, st>>>(geo, n, k, k_gain, cos, sin, kc, kr, v, kc_sw, kr_sw,
-                                                               v_sw);
+                                                               v_sw, pos0);
   return cudaGetLastError();
 }
 

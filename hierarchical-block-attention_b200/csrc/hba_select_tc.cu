@@ -71,7 +71,8 @@ __global__ void __launch_bounds__(kStThreads, 2)
   constexpr int BPS = kStN / MS;  // blocks per stage
   const float scale = p.qp.scale_fixed;
   const int nb = p.qp.n_fixed / geo.Bk;
-  auto bmax_of = [&](int i) { return i < nq ? min(last_candidate(i, geo.W, geo.Bk), nb - 1) : 0; };
+  // local query i sits at position q_off + i (a query range of the sequence)
+  auto bmax_of = [&](int i) { return i < nq ? min(last_candidate(p.q_off + i, geo.W, geo.Bk), nb - 1) : 0; };
   const int bmax_tile = bmax_of(min(i0 + kStQ, nq) - 1);  // grows with i: the tile's largest
   const int NS = bmax_tile >= 1 ? (bmax_tile + BPS - 1) / BPS : 0;
   const int k = geo.K;

@@ -11,8 +11,8 @@ All compute runs in libhba_b200.so (CUDA); nothing falls back to the CPU.
 """
 
 from ._lib import HBAError, load as load_library
-from .attention import (content_scale, hba_attention_b200, hba_attention_b200_fused, log_len_tau,
-                        union_scale)
+from .attention import (content_scale, hba_attention_b200, hba_attention_b200_fused, hba_attention_b200_range,
+                        log_len_tau, union_scale)
 from .cache import HBADecodeCache
 from .config import BASELINE, HBAConfig, baseline_config
 from .decoder import HBAModelDecoder
@@ -20,5 +20,5 @@ from .ops import build_super_b200, qknorm_b200, summarize_b200
 from .patch import install
 
 __all__ = ["HBAError", "load_library", "content_scale", "log_len_tau", "union_scale", "hba_attention_b200",
-           "hba_attention_b200_fused", "HBADecodeCache", "HBAModelDecoder", "HBAConfig", "BASELINE", "baseline_config", "install",
+           "hba_attention_b200_fused", "hba_attention_b200_range", "HBADecodeCache", "HBAModelDecoder", "HBAConfig", "BASELINE", "baseline_config", "install",
            "qknorm_b200", "summarize_b200", "build_super_b200"]

@@ -85,6 +85,11 @@ SIGNATURES = {
                                                    _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P]),
     "hba_b200_prefill": (ctypes.c_int, [_CFG, _I32, _I32, _F, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P,
                                         _P, _P, _SZ, _P]),
+    "hba_b200_prefill_range_workspace_size": (_SZ, [_CFG, _I32, _I32, _I32]),
+    # cfg, batch, n, q_lo, n_q, scale, q, k, v, cos, sin, q_gain, k_gain, probes, proj, out, lse, sel_idx,
+    # sel_score, workspace, workspace_bytes, stream
+    "hba_b200_prefill_range": (ctypes.c_int, [_CFG, _I32, _I32, _I32, _I32, _F, _P, _P, _P, _P, _P, _P, _P, _P, _P,
+                                              _P, _P, _P, _P, _P, _SZ, _P]),
 }
 
 _lib = None

@@ -119,36 +119,57 @@ def hba_attention_b200(q, k, v, cos, sin, cfg, summ, qkn, cap=None, hier=False, 
     default, waits for the call's stream to read the kernels' status word)."""
     if equiv:
         raise NotImplementedError("equiv=True (dense uniform-RoPE attention) is not part of the HBA hot path")
+    return _forward(q, k, v, cos, sin, cfg, summ, qkn, hier, 0, None, return_lse, return_selection, check_status)
+
+
+def hba_attention_b200_range(q, k, v, cos, sin, cfg, summ, qkn, q_lo, n_total=None, return_lse=False,
+                             return_selection=False, check_status=True):
+    """Rows q_lo .. q_lo + n_q - 1 of ``hba_attention_b200`` for queries q
+    [B, n_q, Hq, dh] at those positions over keys / values k, v [B, n, Hkv,
+    dh] of tokens 0 .. n - 1 (n >= q_lo + n_q, a multiple of the block).
+    The logit scale uses the temperature of ``n_total`` (default n): the
+    length of the whole sequence whose rows these are, as the reference's
+    forward applies one tau(n) to every row.  The piece a rank computes in a
+    prefill split by token range.  Tensor-core path only (flat selection,
+    QKNorm, block 64, G >= 4)."""
+    return _forward(q, k, v, cos, sin, cfg, summ, qkn, False, int(q_lo), n_total, return_lse, return_selection,
+                    check_status)
+
+
+def _forward(q, k, v, cos, sin, cfg, summ, qkn, hier, q_lo, n_total, return_lse, return_selection, check_status):
     _need_cuda(q, k, v)
     _no_grad_guard(q, k, v)
-    B, n, Hq, dh = q.shape
+    B, n_q, Hq, dh = q.shape
+    n = k.shape[1]
     Hkv = k.shape[2]
     if Hq != cfg.n_heads or Hkv != cfg.n_kv or dh != cfg.head_dim:
         raise ValueError(f"shape {tuple(q.shape)}/{tuple(k.shape)} does not match the config heads")
     assert n % cfg.block == 0, (n, cfg.block)
+    if q_lo < 0 or q_lo + n_q > n:
+        raise ValueError(f"query rows [{q_lo}, {q_lo + n_q}) outside the {n} keys")
     dev = q.device
     with torch.cuda.device(dev):
         qb, kb, vb = as_bf16(q), as_bf16(k), as_bf16(v)
         cs, sn = as_f32(cos[:n], dev), as_f32(sin[:n], dev)
         qg, kg = gains(qkn, dev)
         probes, proj = summarizer_weights(summ, dev)
-        scale = union_scale(cfg, dh, n)
+        scale = union_scale(cfg, dh, n if n_total is None else int(n_total))
         c = c_config(cfg, hier)
         L = _lib.load()
-        ws_bytes = L.hba_b200_prefill_workspace_size(ctypes.byref(c), B, n)
+        ws_bytes = L.hba_b200_prefill_range_workspace_size(ctypes.byref(c), B, n, n_q)
         if ws_bytes == 0:
             _lib.check(_lib.ERR_UNSUPPORTED if n % cfg.block == 0 else _lib.ERR_NOT_BLOCK_MULTIPLE,
                        "hba_b200_prefill_workspace_size")
         ws = torch.empty(ws_bytes, dtype=torch.uint8, device=dev)
         out = torch.empty_like(qb)
-        lse = torch.empty(B, Hq, n, dtype=torch.float32, device=dev) if return_lse else None
+        lse = torch.empty(B, Hq, n_q, dtype=torch.float32, device=dev) if return_lse else None
         sel_i = sel_s = None
         if return_selection:
-            sel_i = torch.empty(B, Hkv, n, cfg.k_blocks, dtype=torch.int32, device=dev)
-            sel_s = torch.empty(B, Hkv, n, cfg.k_blocks, dtype=torch.float32, device=dev)
-        st = L.hba_b200_prefill(ctypes.byref(c), B, n, ctypes.c_float(scale), ptr(qb), ptr(kb), ptr(vb), ptr(cs),
-                                ptr(sn), ptr(qg), ptr(kg), ptr(probes), ptr(proj), ptr(out), ptr(lse), ptr(sel_i),
-                                ptr(sel_s), ptr(ws), ws_bytes, stream_of(dev))
+            sel_i = torch.empty(B, Hkv, n_q, cfg.k_blocks, dtype=torch.int32, device=dev)
+            sel_s = torch.empty(B, Hkv, n_q, cfg.k_blocks, dtype=torch.float32, device=dev)
+        st = L.hba_b200_prefill_range(ctypes.byref(c), B, n, q_lo, n_q, ctypes.c_float(scale), ptr(qb), ptr(kb),
+                                      ptr(vb), ptr(cs), ptr(sn), ptr(qg), ptr(kg), ptr(probes), ptr(proj), ptr(out),
+                                      ptr(lse), ptr(sel_i), ptr(sel_s), ptr(ws), ws_bytes, stream_of(dev))
         _lib.check(st, "hba_b200_prefill")
         if check_status:  # a bounded device wait that expired raises here instead of returning garbage
             _lib.check_device(ptr(ws), stream_of(dev), "hba_b200_prefill (device status)")

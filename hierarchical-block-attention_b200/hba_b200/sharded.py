@@ -214,6 +214,21 @@ class HBAShardedDecode:
             self.local.append(k_full[:, lo:hi], v_full[:, lo:hi])
         self._set_lengths(n)
 
+    def fill_local(self, k_loc, v_loc, n):
+        """Load this rank's part of a context of n tokens (every sequence):
+        k_loc, v_loc [B, t, Hkv, dh] raw projections of tokens [tok_lo,
+        tok_lo + t) -- the rows a prefill split by token range computed on
+        this rank (t = 0 when the context ends before the range)."""
+        if n > self.n_total:
+            raise ValueError(f"context {n} exceeds the sharded capacity {self.n_total}")
+        t = int(k_loc.shape[1])
+        if t != max(0, min(self.tok_lo + self.n_loc, n) - self.tok_lo):
+            raise ValueError(f"rank {self.rank} holds tokens [{self.tok_lo}, {self.tok_lo + self.n_loc}) of {n}: "
+                             f"got {t}")
+        if t > 0:
+            self.local.append(k_loc, v_loc)
+        self._set_lengths(n)
+
     def append(self, k_new, v_new):
         """Append t tokens to every sequence (all sequences hold the same
         length): each rank keeps the part that falls in its range."""

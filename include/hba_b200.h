@@ -211,6 +211,27 @@ int hba_b200_prefill(const hba_b200_config* cfg, int32_t batch, int32_t n, float
                      cudaStream_t stream);
 
 /*
+ * The forward for a range of query positions [q_lo, q_lo + n_q) of
+ * sequences whose keys and values [0, n) are given: the rows q_lo .. of
+ * hba_b200_prefill over the n tokens (same summaries, same selection, same
+ * union; `scale` is the caller's -- content scale x tau of the whole
+ * sequence's length, as every row of the reference's forward uses).  For a
+ * prefill split by token range over ranks: rank r passes its queries and
+ * the keys / values of tokens [0, its last position].
+ *   q: [batch, n_q, Hq, dh]; k, v: [batch, n, Hkv, dh]; cos, sin: [n, dh]
+ *   out: [batch, n_q, Hq, dh]; lse: [batch, Hq, n_q]; sel: [batch, Hkv, n_q, k]
+ * Runs on the tensor-core selection and union (flat selection, QKNorm, block
+ * 64, G >= 4); HBA_B200_ERR_UNSUPPORTED otherwise.  No counterpart in the
+ * reference, which runs one device.
+ */
+size_t hba_b200_prefill_range_workspace_size(const hba_b200_config* cfg, int32_t batch, int32_t n, int32_t n_q);
+int hba_b200_prefill_range(const hba_b200_config* cfg, int32_t batch, int32_t n, int32_t q_lo, int32_t n_q,
+                           float scale, const void* q, const void* k, const void* v, const float* cos,
+                           const float* sin, const float* q_gain, const float* k_gain, const float* probes,
+                           const float* proj, void* out, float* lse, int32_t* sel_idx, float* sel_score,
+                           void* workspace, size_t workspace_bytes, cudaStream_t stream);
+
+/*
  * Device status readout (no counterpart in the reference, whose torch calls
  * are synchronous).  The kernels report a failed bounded device-side wait by
  * writing 1 into a status word instead of hanging or trapping: the first 4
