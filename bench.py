@@ -50,7 +50,7 @@ def parse():
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
-    ap.add_argument("--config", default="cfg1", choices=["cfg1", "cfg2", "cfg3", "cfg3-shard"])
+    ap.add_argument("--config", default="cfg1", choices=["cfg1", "cfg2", "cfg3", "cfg3-shard", "cfg4"])
     ap.add_argument("--no-secondary", action="store_true")
     ap.add_argument("--ncu-case", default=None, choices=["cfg1", "cfg3", "cfg2"],
                     help="profiling target: build this decode workload (cfg3 at batch 4) and run 3 decodes, "
@@ -649,6 +649,138 @@ def prefill_bench(name, steps, warmup, world, rank, local, pk):
     return res
 
 
+class _AttnTimer:
+    """CUDA events around every call of the wrapped function (the HBA
+    attention of a layer); .ms() sums the closed intervals."""
+
+    def __init__(self, fn):
+        self.fn, self.ev = fn, []
+
+    def __call__(self, *a, **kw):
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        r = self.fn(*a, **kw)
+        e1.record()
+        self.ev.append((e0, e1))
+        return r
+
+    def ms(self):
+        torch.cuda.synchronize()
+        t = sum(a.elapsed_time(b) for a, b in self.ev)
+        self.ev = []
+        return t
+
+
+def cfg4_bench(steps, warmup, world, rank, local, pk):
+    """a random-init 24-layer decoder (hidden 896, 14 / 2
+    heads, dh 64, SwiGLU 4864, vocab 151936, every layer HBA: window 1024,
+    block 64, top-16, 4 sinks, 4 slots) over batch 8 x 131072 uniform random
+    token ids, the KV range split evenly over the world's GPUs: one prefill
+    of the whole prompt, then `steps` decode steps (one token per sequence).
+    value = prefill tokens/s; decode queries/s and the attention share of
+    each phase beside it."""
+    import types
+    from transformers import Qwen2Config, Qwen2ForCausalLM
+    import hba_b200.decoder as decmod
+    import hba_b200.sharded_model as shmod
+    from hba_b200 import HBAConfig, synth
+    dev = torch.device("cuda", local)
+    B, N, L = 8, 131072, 24
+    cfg = HBAConfig(n_layers=L, n_heads=14, n_kv=2, head_dim=64, hidden=896, rope_theta=1e6, native_ctx=32768,
+                    vocab_size=151936, block=64, window=1024, sinks=4, k_blocks=16, slots=4)
+    qcfg = Qwen2Config(vocab_size=cfg.vocab_size, hidden_size=cfg.hidden, intermediate_size=4864, num_hidden_layers=L,
+                       num_attention_heads=cfg.n_heads, num_key_value_heads=cfg.n_kv, max_position_embeddings=N + 64,
+                       rope_theta=cfg.rope_theta, tie_word_embeddings=True)
+    torch.manual_seed(0)
+    with torch.device(dev):
+        donor = Qwen2ForCausalLM(qcfg).to(torch.bfloat16).eval()
+    summ, qkn = zip(*[synth.make_weights(cfg, dev, seed=100 + i, gains=False) for i in range(L)])
+    model = types.SimpleNamespace(cfg=cfg, core=donor.model, lm_head=donor.lm_head, summarizers=list(summ),
+                                  qknorms=list(qkn))
+    g = torch.Generator().manual_seed(4)
+    ids = torch.randint(0, cfg.vocab_size, (B, N + max(1, steps + warmup)), generator=g).to(dev)
+    cap = N + steps + warmup + 64
+    sharded = world > 1
+    # time the HBA attention inside the model's layer loop: prefill (range) calls and decode cache steps
+    if sharded:
+        at = _AttnTimer(shmod.hba_attention_b200_range)
+        shmod.hba_attention_b200_range = at
+    else:
+        at = _AttnTimer(decmod.hba_attention_b200)
+        decmod.hba_attention_b200 = at
+    try:
+        # warm-up: a short prompt through a small decoder (kernels loaded, tensor maps cached)
+        small = (shmod.HBAShardedModelDecoder(model, B, 4096, dev) if sharded else decmod.HBAModelDecoder(model, B, 4096))
+        small.prefill(ids[:, :2048])
+        small.step(ids[:, 2048])
+        if sharded:
+            small.close()
+        del small
+        torch.cuda.empty_cache()
+        at.ms()
+        dec = shmod.HBAShardedModelDecoder(model, B, cap, dev) if sharded else decmod.HBAModelDecoder(model, B, cap)
+        barrier(world)
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        dec.prefill(ids[:, :N])
+        e1.record()
+        torch.cuda.synchronize()
+        prefill_ms = max_over_ranks(e0.elapsed_time(e1), world, dev)
+        prefill_attn_ms = max_over_ranks(at.ms(), world, dev)
+        # decode steps: every layer's cache step is the HBA attention of the step
+        for j in range(warmup):
+            dec.step(ids[:, N + j])
+        torch.cuda.synchronize()
+        cstep = [None]
+        for cache_obj in (dec.shards if sharded else dec.caches):
+            orig = cache_obj.attend if sharded else cache_obj.step
+            t = _AttnTimer(orig)
+            if sharded:
+                cache_obj.attend = t
+            else:
+                cache_obj.step = t
+            cstep.append(t)
+        barrier(world)
+        torch.cuda.synchronize()
+        d0, d1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        with Clocks(local) as ck:
+            d0.record()
+            for j in range(steps):
+                dec.step(ids[:, N + warmup + j])
+            d1.record()
+            torch.cuda.synchronize()
+        step_ms = max_over_ranks(d0.elapsed_time(d1) / steps, world, dev)
+        step_attn_ms = max_over_ranks(sum(t.ms() for t in cstep[1:]) / steps, world, dev)
+        if sharded:
+            dec.close()
+    finally:
+        if sharded:
+            shmod.hba_attention_b200_range = at.fn
+        else:
+            decmod.hba_attention_b200 = at.fn
+    res = dict(
+        metric=METRIC, value=B * N / (prefill_ms * 1e-3), unit="prefill tokens/s", n_gpus=world, steps=steps,
+        warmup=warmup, ms_per_step=step_ms, higher_is_better=True, scaling="strong", vs_baseline=None, dtype="bf16",
+        data="synthetic (uniform random token ids from seed; random-init weights of the config-4 architecture)",
+        config=dict(workload=f"cfg4: {L}-layer decoder (hidden 896, 14/2 heads, dh 64, SwiGLU 4864, vocab 151936, "
+                             f"every layer HBA flat top-16), batch {B} x {N} tokens, KV range split over {world} "
+                             f"GPU(s)", batch=B, seq_len=N, layers=L,
+                    parallelism=(f"sequence shards x{world}: per-layer NCCL all-gather of the new K/V in the "
+                                 f"prefill, the fused NVLink sharded decode per layer") if sharded else "one GPU"),
+        prefill=dict(ms=prefill_ms, tokens_per_s=B * N / (prefill_ms * 1e-3), attention_ms=prefill_attn_ms,
+                     attention_fraction=prefill_attn_ms / prefill_ms),
+        decode=dict(ms_per_step=step_ms, queries_per_s=B / (step_ms * 1e-3), attention_ms_per_step=step_attn_ms,
+                    attention_fraction=step_attn_ms / step_ms,
+                    timing="eager per-layer calls (projections, cache append + HBA decode attention, MLP), "
+                           "the status of every layer's attention checked"),
+        clocks=ck.summary(),
+    )
+    del dec, donor, model
+    torch.cuda.empty_cache()
+    return res
+
+
 # -------------------------------------------------------- reference arm ----
 def _ref_worker(args):
     """One host process: one sequence of the GPU arm's workload (the same
@@ -733,6 +865,8 @@ def main():
         res = decode_bench(args.config, args.steps, args.warmup, world, rank, local, pk)
     elif args.config == "cfg3-shard":
         res = shard_bench("cfg3", args.steps, args.warmup, world, rank, local, pk)
+    elif args.config == "cfg4":
+        res = cfg4_bench(args.steps, args.warmup, world, rank, local, pk)
     else:
         res = prefill_bench(args.config, args.steps, args.warmup, world, rank, local, pk)
     if not args.no_secondary and args.config == "cfg1":
