@@ -41,8 +41,8 @@ class HBAShardedModelDecoder:
         self.group = None  # the default torch.distributed group (the shards' exchange buffers live there)
         self.B = int(batch)
         self.device = torch.device(device)
-        self.world = dist.get_world_size(group)
-        self.rank = dist.get_rank(group)
+        self.world = dist.get_world_size(self.group)
+        self.rank = dist.get_rank(self.group)
         cfg = self.cfg
         n_layers = len(model.core.layers)
         # one layer's shard fixes the token ranges (the same for every layer)
