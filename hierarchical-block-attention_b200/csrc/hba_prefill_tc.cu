@@ -1,47 +1,60 @@
 // Prefill union softmax on the 5th-generation tensor cores (tcgen05 + TMEM,
-// operands fed by TMA), the full-sequence forward of the HBA path.
+// operands fed by TMA and bulk copies), the full-sequence forward of the HBA
+// path.
 //
 // One CTA per (sequence, kv head, pair of query tiles).  A tile is QT = 128/G
 // consecutive queries x the G query heads of the KV group = the 128 rows of
 // the UMMA M dimension (row r = query r/G, head r%G); the CTA's two tiles (T =
-// 0, 1: queries [i0, i0+QT) and [i0+QT, i0+2QT)) share one stream of 64-key
-// chunks: [sinks (keys 0..63, NoPE) | the pair's RoPE window | the union of
-// the blocks their queries selected (NoPE)] -- a routed block is loaded once
-// for both tiles and masked per row by a bitmask of the queries that selected
-// it; a chunk that no query of a tile needs is skipped for that tile
-// (reference semantics: src/hba/attention.py:676-711; the reference's fused
-// path builds the same union at 128x128 granularity, :438-475).
+// 0, 1: queries [i0, i0+QT) and [i0+QT, i0+2QT)) share one stream of 128-key
+// chunks, each two 64-key halves:
+//   [the pair's RoPE window, 64-aligned, two consecutive blocks per chunk |
+//    NoPE blocks in pairs: the sink block, then the union of the blocks the
+//    pair's queries selected, those both tiles need first, then tile 0's,
+//    then tile 1's]
+// A routed block is loaded once for both tiles and masked per row by a
+// bitmask of the queries that selected it; a chunk that no query of a tile
+// needs is skipped for that tile (reference semantics:
+// src/hba/attention.py:676-711; the reference's fused path builds the same
+// union at 128x128 granularity, :438-475).
 //
-// Per tile T, TMEM columns [256T, 256T + 256): S [0, 64) fp32, two P buffers
-// [64, 96) and [96, 128) (64 bf16 probabilities per row, two per column), O
-// [128, 128 + dh) fp32.  With two P buffers a row's softmax of chunk j waits
-// only for PV(j - 2) before storing P.
-//   S_T = Q_T K_c^T   (M 128, N 64, K dh; A = the swizzled query tile)
-//   O_T += P_T V_c    (M 128, N dh, K 64; A = P_T from TMEM, V MN-major)
-// While one tile's softmax warps turn S into P, the tensor cores run the other
-// tile's MMAs (and the next chunk's S), so the tensor pipe and the two
-// softmax groups overlap.
+// Per tile T, TMEM columns [256T, 256T + 256): S [0, 128) fp32, P (128 bf16
+// probabilities per row, two per column) written over S's first 64 columns,
+// O [128, 128 + dh) fp32.
+//   S_T = Q_T K_c^T   (M 128, N 128, K dh; A = the swizzled query tile)
+//   O_T += P_T V_c    (M 128, N dh, K 128; A = P_T from TMEM, V MN-major)
+// One thread issues all MMAs, per chunk c in the order PV_0(c-1), S_0(c),
+// PV_1(c-1), S_1(c): S_t(c) may overwrite P_t(c-1) because tcgen05.mma
+// operations of one thread execute in issue order, and the commit of S_t(c)
+// also tells tile t's softmax that PV_t(c-1) is complete (so O may be
+// rescaled then).  S_0(c) completes half a step before S_1(c), so each
+// tile's softmax runs while the tensor cores run the other tile's PV and S.
 //
-// Roles (352 threads):
+// The query tile holds the RoPE'd queries for the window chunks and is
+// reloaded with the QKNorm'd ones before the tile's first NoPE chunk (issued
+// once its last window S is complete, so the load overlaps that chunk's
+// softmax).
+//
+// Roles (320 threads):
 //   warps 4T .. 4T+3  softmax / epilogue of tile T, one thread per row (TMEM
 //              lane): S row -> mask -> p = exp2(s*scale*log2e - M) -> P row
-//              (bf16, tcgen05.st) for the PV MMA; epilogue O/l -> out.  M is
-//              the row's QKNorm bound of the logits (|s| <= scale*|q|*|k|,
-//              |k| = sqrt(dh)*k_gain) when that bound is small enough that no
-//              p can flush to zero (kBoundedLog2): no running max, O never
-//              rescaled.  Otherwise M is the row's running max, raised lazily:
-//              when a chunk's max passes it by more than kRescaleLog2, the warp
-//              rescales its rows of O in TMEM (and l) before writing P.
-//   warps 8, 10  one thread each issues tile 0's / tile 1's tcgen05.mma
-//              (warp 8 also owns the TMEM allocation).
-//   warp 9     one thread issues the loads: the query tiles (TMA), then K_c
-//              and V_c through a 5-slot ring, each one 1-D bulk copy of a
-//              contiguous chunk of the pre-pass's chunk-tiled K / RoPE'd K /
-//              V copies (the 128-byte-swizzled image of a [64 keys x 64
-//              dims] box per half, so the ring holds UMMA operands as a
-//              tiled TMA load would leave them, at the bulk engine's higher
-//              per-SM rate).  Window chunks are 64-key aligned (the row masks
-//              cut the window's ragged first chunk).
+//              (bf16, tcgen05.st) for the PV MMA, in four quarters of 32
+//              columns with the next quarter's TMEM load in flight;
+//              epilogue O/l -> out.  M is the row's QKNorm bound of the logits
+//              (|s| <= scale*|q|*|k|, |k| = sqrt(dh)*k_gain) when that bound
+//              is small enough that no p can flush to zero (kBoundedLog2): no
+//              running max, O never rescaled.  Otherwise M is the row's
+//              running max, raised lazily: when a chunk's max passes it by
+//              more than kRescaleLog2, the warp rescales its rows of O in
+//              TMEM (and l) before writing P.
+//   warp 8     one thread issues every tcgen05.mma (and the query reloads);
+//              the warp owns the TMEM allocation.
+//   warp 9     one thread issues the loads: the RoPE'd query tiles (TMA),
+//              then K_c and V_c through a ring of 128-key slots, each half of
+//              a slot one 1-D bulk copy per 64-dim group from the pre-pass's
+//              chunk-tiled K / RoPE'd K / V copies (the 128-byte-swizzled
+//              image of a [64 keys x 64 dims] box), so the ring holds UMMA
+//              operands as a tiled TMA load would leave them, at the bulk
+//              engine's higher per-SM rate.
 // Every mbarrier wait is bounded; a timeout sets *err and drains.
 #include <climits>
 #include <cudaTypedefs.h>
@@ -54,41 +67,41 @@ namespace hba {
 
 using namespace sm100;
 
-constexpr int kTcThreads = 352;
-// ring of K or V tiles: K(c) = item 2c, V(c) = item 2c + 1 in slot item % 5.
-// With an odd slot count, V(c + 2) reuses K(c)'s slot (free once S(c) is
-// done) and K(c + 3) reuses V(c)'s (free once PV(c) is done): the load that
-// waits for a PV has three chunk periods to land.
-constexpr int kTcSlots = 5;
-constexpr int kTcKeys = 64;            // keys per chunk
-constexpr int kTcMaxRouted = 1024;     // routed union capacity of a tile pair
-constexpr int kTcMma = 8;              // MMA warp of tile 0 (and TMEM owner)
-constexpr int kTcMma2 = 10;            // MMA warp of tile 1
-constexpr int kTcTma = 9;              // TMA warp
+constexpr int kTcThreads = 320;
+constexpr int kTcBlock = 64;           // keys per routed block = per half chunk
+constexpr int kTcKeys = 128;           // keys per chunk (UMMA N of S, K of PV)
+constexpr int kTcMaxEntries = 1040;    // NoPE list capacity: the sink block + the routed union of a tile pair
+constexpr int kTcMaxChunks = 544;      // window chunks (<= 9 for W <= 1024) + NoPE chunks (<= 520)
+constexpr int kTcMma = 8;              // MMA warp (and TMEM owner)
+constexpr int kTcTma = 9;              // load warp
 
-enum ChunkType : uint32_t { kSink = 0, kWindow = 1, kRouted = 2 };
+enum HalfType : uint32_t { kSink = 0, kWindow = 1, kRouted = 2, kPad = 3 };
 
 template <int DH>
 struct TcSmem {
-  static constexpr int HALVES = DH / 64;
-  static constexpr int QBYTES = HALVES * 128 * 128;     // [128 rows x DH] bf16, swizzled halves
-  static constexpr int KBYTES = HALVES * 64 * 128;      // [64 keys x DH]
-  alignas(1024) unsigned char qc[2][QBYTES];            // per tile: QKNorm'd queries (NoPE chunks)
-  alignas(1024) unsigned char qr[2][QBYTES];            // per tile: the same RoPE'd (window chunks)
-  alignas(1024) unsigned char ring[kTcSlots][KBYTES];   // a K tile is free once its S MMAs are done
-  // the routed union: block ids and the pair's query masks (bit q: query i0 + q picked it)
-  unsigned long long rmask[kTcMaxRouted];
-  uint16_t rblk[kTcMaxRouted];
-  uint64_t q_ready, drain[2];
-  uint64_t full[kTcSlots], empty[kTcSlots];
-  uint64_t s_full[2], s_free[2], o_full[2];
-  uint64_t p_full[2][2], p_free[2][2];  // [tile][P buffer]
+  static constexpr int HALVES = DH / 64;                // 64-dim groups
+  static constexpr int QBYTES = HALVES * 128 * 128;     // [128 rows x DH] bf16, swizzled per dim group
+  static constexpr int GBYTES = kTcKeys * 128;          // one dim group of a K or V chunk: 128 rows of 128 B
+  static constexpr int KT = HALVES * GBYTES;            // [128 keys x DH]
+  // K(c) is ring item 2c, V(c) item 2c + 1, slot item % NSLOT: a K slot is
+  // free once both tiles' S(c) are done, a V slot once both PV(c) are
+  static constexpr int NSLOT = DH == 64 ? 8 : 4;
+  alignas(1024) unsigned char q[2][QBYTES];             // per tile: RoPE'd, then QKNorm'd queries
+  alignas(1024) unsigned char ring[NSLOT][KT];
+  // NoPE blocks: ids and the pair's query masks (bit q: query i0 + q picked it)
+  unsigned long long emask[kTcMaxEntries];
+  uint16_t eblk[kTcMaxEntries];
+  uint64_t q_ready, qn_read[2], qc_ready[2], drain[2];
+  uint64_t full[NSLOT], empty[NSLOT];
+  uint64_t s_full[2], p_full[2], o_full[2];
   uint32_t tmem_base;
-  int n_chunks;
-  int scan[kTcThreads / 32];
+  int n_entries;
+  int scan[3][kTcThreads / 32];
+  alignas(4) uint8_t cneed[kTcMaxChunks];  // per chunk: the tiles (bit t) with a query that needs it
 };
 
-static_assert(sizeof(TcSmem<128>) + 1024 <= 232448, "prefill tile set exceeds the 227 KB of shared memory");
+static_assert(sizeof(TcSmem<128>) + 1024 <= 232448 && sizeof(TcSmem<64>) + 1024 <= 232448,
+              "prefill tile set exceeds the 227 KB of shared memory");
 
 struct PrefillTcParams {
   Geom geo;            // geo.nq local queries (positions q_off ..) over n keys
@@ -114,12 +127,14 @@ template <int DH>
 __global__ void __launch_bounds__(kTcThreads, 1)
     prefill_tc_kernel(const __grid_constant__ CUtensorMap tm_qc, const __grid_constant__ CUtensorMap tm_qr,
                       PrefillTcParams p) {
+  using SM = TcSmem<DH>;
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   // dynamic shared memory is only 16-byte aligned by default: align by hand
   unsigned char* base_ptr =
       reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  TcSmem<DH>& sm = *reinterpret_cast<TcSmem<DH>*>(base_ptr);
-  constexpr int HALVES = DH / 64;
+  SM& sm = *reinterpret_cast<SM*>(base_ptr);
+  constexpr int HALVES = SM::HALVES;
+  constexpr int NSLOT = SM::NSLOT;
   const Geom& geo = p.geo;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int G = geo.G, QT = p.QT, n = p.n;
@@ -132,7 +147,8 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   const int nq2 = min(2 * QT, nql - li0);      // queries of the pair
   const int nq0 = min(QT, nq2), nq1 = max(0, nq2 - QT);  // queries of tile 0, tile 1
   auto nqt = [&](int t) { return t == 0 ? nq0 : nq1; };
-  const int nb = n / geo.Bk;
+  const int nb = n / kTcBlock;
+  const uint32_t qbox_bytes = (uint32_t)(HALVES * G * QT * 128);  // a tile's query box (G*QT <= 128 rows)
   unsigned long long* trace =
       (p.trace != nullptr && pair == p.pairs - 1 && bg < p.trace_rows) ? p.trace + (size_t)bg * 16 : nullptr;
   auto stamp = [&](int s) {
@@ -140,38 +156,33 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   };
   if (tid == 0) stamp(0);
 
-  // ---- barriers, then the query tiles' TMA, which needs no chunk list and
-  // lands while the list is built ----
+  // ---- barriers, then the RoPE'd query tiles' TMA, which needs no chunk list
+  // and lands while the list is built ----
   if (tid == kTcTma * 32) {
     mbar_init(&sm.q_ready, 1);
-    mbar_init(&sm.drain[0], 1);
-    mbar_init(&sm.drain[1], 1);
-    for (int s = 0; s < kTcSlots; ++s) {
-      mbar_init(&sm.full[s], 1);
-      mbar_init(&sm.empty[s], 2);  // one commit per MMA issuer
-    }
     for (int t = 0; t < 2; ++t) {
+      mbar_init(&sm.qn_read[t], 128);
+      mbar_init(&sm.qc_ready[t], 1);
+      mbar_init(&sm.drain[t], 1);
       mbar_init(&sm.s_full[t], 1);
-      mbar_init(&sm.s_free[t], 128);
+      mbar_init(&sm.p_full[t], 128);
       mbar_init(&sm.o_full[t], 1);
-      for (int u = 0; u < 2; ++u) {
-        mbar_init(&sm.p_full[t][u], 128);
-        mbar_init(&sm.p_free[t][u], 1);
-      }
+    }
+    for (int s = 0; s < NSLOT; ++s) {
+      mbar_init(&sm.full[s], 1);
+      mbar_init(&sm.empty[s], 1);
     }
     fence_barrier_init();
-    // rows r = query * G + head, QKNorm'd (qc) and RoPE'd (qr) by the pre-pass;
-    // a box is G heads x QT queries (G * QT <= 128 rows: 126 when G = 7) of 128 bytes, per half
+    // rows r = query * G + head, RoPE'd by the pre-pass; a box is G heads x QT
+    // queries (G * QT <= 128 rows: 126 when G = 7) of 128 bytes, per dim group
     const int ntile = nq1 > 0 ? 2 : 1;
-    mbar_arrive_expect_tx(&sm.q_ready, (uint32_t)(ntile * 2 * HALVES * G * QT * 128));
+    mbar_arrive_expect_tx(&sm.q_ready, (uint32_t)ntile * qbox_bytes);
     for (int t = 0; t < ntile; ++t)
-      for (int h = 0; h < HALVES; ++h) {
-        tma_load_4d(sm.qc[t] + h * 16384, &tm_qc, h * 64, g * G, li0 + t * QT, b, &sm.q_ready);
-        tma_load_4d(sm.qr[t] + h * 16384, &tm_qr, h * 64, g * G, li0 + t * QT, b, &sm.q_ready);
-      }
+      for (int h = 0; h < HALVES; ++h)
+        tma_load_4d(sm.q[t] + h * 16384, &tm_qr, h * 64, g * G, li0 + t * QT, b, &sm.q_ready);
   }
 
-  // ---- chunk list: sinks, window, routed union (all threads) ----
+  // ---- NoPE list: the sink block, then the routed union by class (all threads) ----
   // [nb] 64-bit query masks of the pair, overlaying the ring before its first use
   unsigned long long* mask = reinterpret_cast<unsigned long long*>(sm.ring[0]);
   for (int i = tid; i < nb; i += kTcThreads) mask[i] = 0ull;
@@ -180,47 +191,73 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     const int32_t* sel = p.sel + ((size_t)bg * nql + li0) * p.list_stride;
     for (int e = tid; e < nq2 * p.list_stride; e += kTcThreads) {
       const int blk = sel[e];
-      if (blk >= 0 && blk < nb) atomicOr(&mask[blk], 1ull << (e / p.list_stride));
+      if (blk >= 1 && blk < nb) atomicOr(&mask[blk], 1ull << (e / p.list_stride));
     }
   }
   __syncthreads();
-  // the pair's window keys [jlo, jhi], walked in 64-key aligned chunks from jla
-  const int jlo = max(geo.S, i0 - geo.W + 1);
-  const int jhi = i0 + nq2 - 1;
-  const int jla = jlo & ~(kTcKeys - 1);
-  const int nwc = jhi >= jlo ? (jhi - jla) / kTcKeys + 1 : 0;
-  const int nsc = geo.S > 0 ? 1 : 0;
   const uint32_t qmask_t = QT >= 32 ? 0xffffffffu : ((1u << QT) - 1u);
+  const int nsk = geo.S > 0 ? 1 : 0;  // the sink block heads the NoPE list
   {
+    // class of a routed block: 0 = both tiles need it, 1 = tile 0 only, 2 = tile 1 only
+    auto cls_of = [&](unsigned long long mk) {
+      const bool a = ((uint32_t)mk & qmask_t) != 0u, c = ((uint32_t)(mk >> QT) & qmask_t) != 0u;
+      return a && c ? 0 : (a ? 1 : 2);
+    };
     const int per = (nb + kTcThreads - 1) / kTcThreads;
     const int lo = tid * per, hi = min(nb, lo + per);
-    int cnt = 0;
-    for (int i = lo; i < hi; ++i) cnt += mask[i] != 0ull;
-    // exclusive prefix of the per-thread counts: within each warp, then over the warp totals
-    int incl = cnt;
-#pragma unroll
-    for (int o = 1; o < 32; o <<= 1) {
-      const int nv = __shfl_up_sync(0xffffffffu, incl, o);
-      if (lane >= o) incl += nv;
-    }
-    if (lane == 31) sm.scan[warp] = incl;
-    __syncthreads();
-    int wbase = 0, total_routed = 0;
-    for (int w = 0; w < kTcThreads / 32; ++w) {
-      if (w < warp) wbase += sm.scan[w];
-      total_routed += sm.scan[w];
-    }
-    // the host admits only 2 * QT * k <= kTcMaxRouted, so the union always fits
-    if (tid == 0) sm.n_chunks = nsc + nwc + min(total_routed, kTcMaxRouted);
-    int o = wbase + incl - cnt;
+    int cnt[3] = {0, 0, 0};
     for (int i = lo; i < hi; ++i) {
       const unsigned long long mk = mask[i];
       if (mk != 0ull) {
-        if (o < kTcMaxRouted) {
-          sm.rblk[o] = (uint16_t)i;
-          sm.rmask[o] = mk;
+        const int k = cls_of(mk);
+        cnt[0] += k == 0;
+        cnt[1] += k == 1;
+        cnt[2] += k == 2;
+      }
+    }
+    // exclusive prefix of the per-thread counts of each class: within each warp, then over the warp totals
+    int incl[3] = {cnt[0], cnt[1], cnt[2]};
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+#pragma unroll
+      for (int k = 0; k < 3; ++k) {
+        const int nv = __shfl_up_sync(0xffffffffu, incl[k], o);
+        if (lane >= o) incl[k] += nv;
+      }
+    }
+    if (lane == 31) {
+#pragma unroll
+      for (int k = 0; k < 3; ++k) sm.scan[k][warp] = incl[k];
+    }
+    __syncthreads();
+    int wbase[3] = {0, 0, 0}, total[3] = {0, 0, 0};
+    for (int w = 0; w < kTcThreads / 32; ++w)
+#pragma unroll
+      for (int k = 0; k < 3; ++k) {
+        if (w < warp) wbase[k] += sm.scan[k][w];
+        total[k] += sm.scan[k][w];
+      }
+    // the host admits only 1 + 2 * QT * k <= kTcMaxEntries, so the list always fits
+    if (tid == 0) {
+      sm.n_entries = min(nsk + total[0] + total[1] + total[2], kTcMaxEntries);
+      if (nsk) {
+        sm.eblk[0] = 0;
+        sm.emask[0] = 0ull;
+      }
+    }
+    int o[3];
+    o[0] = nsk + wbase[0] + incl[0] - cnt[0];
+    o[1] = nsk + total[0] + wbase[1] + incl[1] - cnt[1];
+    o[2] = nsk + total[0] + total[1] + wbase[2] + incl[2] - cnt[2];
+    for (int i = lo; i < hi; ++i) {
+      const unsigned long long mk = mask[i];
+      if (mk != 0ull) {
+        const int k = cls_of(mk);
+        const int e = k == 0 ? o[0]++ : (k == 1 ? o[1]++ : o[2]++);
+        if (e < kTcMaxEntries) {
+          sm.eblk[e] = (uint16_t)i;
+          sm.emask[e] = mk;
         }
-        ++o;
       }
     }
   }
@@ -232,130 +269,214 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   __syncthreads();  // the chunk list is complete (and the mask overlay dead) from here on
   tc_fence_after();
   const uint32_t tmem = sm.tmem_base;
-  const int NCH = sm.n_chunks;
+  const int NE = sm.n_entries;
+  // the pair's window keys [jlo, jhi], in 64-key blocks from jla, two per chunk
+  const int jlo = max(geo.S, i0 - geo.W + 1);
+  const int jhi = i0 + nq2 - 1;
+  const int jla = jlo & ~(kTcBlock - 1);
+  const int nwb = jhi >= jlo ? (jhi - jla) / kTcBlock + 1 : 0;
+  const int nwc = (nwb + 1) / 2;
+  const int NCH = min(nwc + (NE + 1) / 2, kTcMaxChunks);  // the host's limits keep it below the cap
   if (tid == 0) stamp(1);
-  // chunk c: [sinks | window (aligned) | routed union]: first key, type, the
-  // query masks of the two tiles (routed) and the tiles that need it
-  struct Chunk {
+
+  // half h of chunk c: its type, first key and the query masks of the two tiles (routed)
+  struct Half {
     int kb;
-    uint32_t type, m0, m1, need;
+    uint32_t type, m0, m1;
   };
-  auto chunk = [&](int c) -> Chunk {
-    Chunk ch;
-    ch.m0 = ch.m1 = 0u;
-    if (c < nsc) {
-      ch.kb = 0;
-      ch.type = kSink;
-      ch.need = 1u | (nq1 > 0 ? 2u : 0u);
-    } else if (c < nsc + nwc) {
-      ch.kb = jla + (c - nsc) * kTcKeys;
-      ch.type = kWindow;
-      ch.need = 0u;
-      // tile t needs it if it meets the tile's window keys [max(S, first - W + 1), last]
-      for (int t = 0; t < 2; ++t) {
-        if (nqt(t) == 0) continue;
+  auto half_of = [&](int c, int h) -> Half {
+    Half x;
+    x.m0 = x.m1 = 0u;
+    if (c < nwc) {
+      const int w = 2 * c + h;
+      x.kb = jla + w * kTcBlock;
+      x.type = w < nwb ? kWindow : kPad;
+    } else {
+      const int e = 2 * (c - nwc) + h;
+      if (e >= NE) {
+        x.kb = 0;
+        x.type = kPad;
+      } else {
+        x.kb = (int)sm.eblk[e] * kTcBlock;
+        if (nsk && e == 0) {
+          x.type = kSink;
+        } else {
+          const unsigned long long mk = sm.emask[e];
+          x.type = kRouted;
+          x.m0 = (uint32_t)mk & qmask_t;
+          x.m1 = (uint32_t)(mk >> QT) & qmask_t;
+        }
+      }
+    }
+    return x;
+  };
+  // the tiles (bit t) with a query that needs a half / a chunk
+  auto half_need = [&](const Half& x) -> uint32_t {
+    uint32_t nd = 0u;
+    for (int t = 0; t < 2; ++t) {
+      if (nqt(t) == 0) continue;
+      bool need = false;
+      if (x.type == kWindow) {
         const int first = i0 + t * QT, last = first + nqt(t) - 1;
         const int lo_t = max(geo.S, first - geo.W + 1);
-        if (ch.kb + kTcKeys - 1 >= lo_t && ch.kb <= last) ch.need |= 1u << t;
+        need = x.kb + kTcBlock - 1 >= lo_t && x.kb <= last;
+      } else if (x.type == kSink) {
+        need = true;
+      } else if (x.type == kRouted) {
+        need = (t == 0 ? x.m0 : x.m1) != 0u;
       }
-    } else {
-      const int r = c - nsc - nwc;
-      const unsigned long long mk = sm.rmask[r];
-      ch.kb = (int)sm.rblk[r] * geo.Bk;
-      ch.type = kRouted;
-      ch.m0 = (uint32_t)mk & qmask_t;
-      ch.m1 = (uint32_t)(mk >> QT) & qmask_t;
-      ch.need = (ch.m0 != 0u ? 1u : 0u) | (ch.m1 != 0u ? 2u : 0u);
+      if (need) nd |= 1u << t;
     }
-    return ch;
+    return nd;
   };
-  constexpr int KB = TcSmem<DH>::KBYTES;
+  auto chunk_need = [&](int c) { return half_need(half_of(c, 0)) | half_need(half_of(c, 1)); };
+  // once per CTA, so the issuer and the softmax warps skip chunks by one shared-memory byte
+  for (int c = tid; c < NCH; c += kTcThreads) sm.cneed[c] = (uint8_t)chunk_need(c);
+  __syncthreads();
   const size_t head_elems = (size_t)n * DH;  // one (sequence, head) of the chunk-tiled copies
   const __nv_bfloat16* kc_bg = p.kc + (size_t)bg * head_elems;
   const __nv_bfloat16* kr_bg = p.kr + (size_t)bg * head_elems;
   const __nv_bfloat16* v_bg = p.v + (size_t)bg * head_elems;
 
   if (warp == kTcTma) {
-    // ---------------- TMA producer ----------------
+    // ---------------- load producer ----------------
     if (lane == 0) {
       for (int it = 0; it < 2 * NCH; ++it) {
-        const int st = it % kTcSlots, u = it / kTcSlots;
-        if (it >= kTcSlots && !mbar_wait(&sm.empty[st], (u - 1) & 1, p.err)) break;
-        const Chunk ck = chunk(it >> 1);
-        const __nv_bfloat16* src = (it & 1) ? v_bg : (ck.type == kWindow ? kr_bg : kc_bg);
-        mbar_arrive_expect_tx(&sm.full[st], KB);
-        bulk_load(sm.ring[st], src + (size_t)(ck.kb / kTcKeys) * (KB / 2), KB, &sm.full[st]);
+        const int st = it % NSLOT, u = it / NSLOT;
+        if (it >= NSLOT && !mbar_wait(&sm.empty[st], (u - 1) & 1, p.err)) break;
+        const int c = it >> 1;
+        const __nv_bfloat16* src = (it & 1) ? v_bg : (c < nwc ? kr_bg : kc_bg);
+        const Half x0 = half_of(c, 0), x1 = half_of(c, 1);
+        // a padding half loads the chunk's other block again (finite values, masked to p = 0)
+        const int blk0 = x0.kb / kTcBlock, blk1 = x1.type == kPad ? blk0 : x1.kb / kTcBlock;
+        mbar_arrive_expect_tx(&sm.full[st], SM::KT);
+#pragma unroll
+        for (int dg = 0; dg < HALVES; ++dg) {
+          unsigned char* dst = sm.ring[st] + dg * SM::GBYTES;
+          bulk_load(dst, src + ((size_t)blk0 * HALVES + dg) * 4096, 8192, &sm.full[st]);
+          bulk_load(dst + 8192, src + ((size_t)blk1 * HALVES + dg) * 4096, 8192, &sm.full[st]);
+        }
       }
     }
-  } else if (warp == kTcMma || warp == kTcMma2) {
-    // ---------------- MMA issuers: one thread per tile ----------------
-    // Each tile's S and PV MMAs are issued by its own thread, so a tile whose
-    // softmax is ready is never held behind the other tile's issue; a K or V
-    // slot is released once both issuers have committed it.  An issuer waits
-    // for every item to land, also one its tile skips, before committing it:
-    // so neither can commit a slot's next use before the other's arrival
-    // for the current one (the empty barriers count two arrivals a phase).
-    if (lane == 0) {
-      const int t = warp == kTcMma ? 0 : 1;
+  } else if (warp == kTcMma) {
+    // ---------------- MMA issuer: one thread for both tiles ----------------
+    // Step c issues, per tile t: the PV of t's pending chunk (once t's
+    // softmax has written its P), then S_t(c) if t needs chunk c.  The
+    // tensor pipe so runs PV_0, S_0, PV_1, S_1 per chunk: S_0(c) completes
+    // half a step before S_1(c), and each tile's softmax overlaps the other
+    // tile's MMAs.  K(c) is released after step c (both S(c) issued), V(c)
+    // after step c + 1 (both PV(c) issued); an extra step NCH issues the
+    // last PVs.  A tile's first NoPE chunk reloads its query tile: the TMA is
+    // issued once its last window S is complete, before waiting for that
+    // chunk's P, so the load overlaps the softmax.
+    // The whole warp runs the loop, so every operand (descriptors, TMEM
+    // addresses) is warp-uniform; one elected lane issues each tcgen05 op.
+    {
       constexpr uint32_t idesc_s = idesc_bf16(128, kTcKeys, false, false);
       constexpr uint32_t idesc_o = idesc_bf16(128, DH, false, true);
-      const uint32_t tt = tmem + (uint32_t)(t * 256);
-      bool ok = mbar_wait(&sm.q_ready, 0, p.err);
-      tc_fence_after();
-      int ns = 0, np = 0;  // S and PV MMAs this tile has issued
-      auto pv = [&](int c) -> bool {
-        const int iv = 2 * c + 1, st = iv % kTcSlots;
-        if (!mbar_wait(&sm.full[st], (iv / kTcSlots) & 1, p.err)) return false;
-        if ((chunk(c).need >> t) & 1u) {
-          const int pb = np & 1;  // P buffer of this tile's np-th chunk
-          if (!mbar_wait(&sm.p_full[t][pb], (np >> 1) & 1, p.err)) return false;
-          tc_fence_after();
-          const uint32_t va = smem_u32(sm.ring[st]);
-#pragma unroll
-          for (int kk = 0; kk < kTcKeys / 16; ++kk)  // K = 16 keys = 8 packed columns of P per MMA
-            umma_f16_ts(tt + 128, tt + 64 + pb * 32 + kk * 8, sdesc_sw128(va + kk * 2048, 8192, 1024), idesc_o,
-                        (np > 0 || kk > 0) ? 1u : 0u);
-          umma_commit(&sm.p_free[t][pb]);
-          ++np;
-        }
-        umma_commit(&sm.empty[st]);  // this issuer is done with the V tile
-        return true;
+      auto wwait = [&](uint64_t* bar, uint32_t parity) {
+        return __all_sync(0xffffffffu, mbar_wait(bar, parity, p.err));
       };
-      for (int c = 0; ok && c < NCH; ++c) {
-        const int ik = 2 * c, st = ik % kTcSlots;
-        const Chunk ck = chunk(c);
-        if (!mbar_wait(&sm.full[st], (ik / kTcSlots) & 1, p.err)) {
-          ok = false;
-          break;
-        }
-        if ((ck.need >> t) & 1u) {
-          // the tile's S buffer is free once its softmax has read the previous S
-          if (ns > 0 && !mbar_wait(&sm.s_free[t], (ns - 1) & 1, p.err)) {
-            ok = false;
-            break;
-          }
-          tc_fence_after();
-          const uint32_t qa = smem_u32(ck.type == kWindow ? sm.qr[t] : sm.qc[t]);
-          const uint32_t ka = smem_u32(sm.ring[st]);
+      bool ok = wwait(&sm.q_ready, 0);
+      tc_fence_after();
+      int pend[2] = {-1, -1};  // chunk whose PV is still to issue, per tile
+      int np[2] = {0, 0}, ns[2] = {0, 0};
+      bool nope[2] = {false, false};  // the query tile holds the QKNorm'd queries
+      auto wait_item = [&](int it) { return wwait(&sm.full[it % NSLOT], (it / NSLOT) & 1); };
+      // the need bits are read four chunks at a time; items a tile has waited for are not tested again
+      uint32_t needw = 0u, prev_need = 0u;
+      for (int c = 0; ok && c <= NCH; ++c) {
+        if ((c & 3) == 0 && c < NCH) needw = *reinterpret_cast<const uint32_t*>(&sm.cneed[c]);
+        const uint32_t need = c < NCH ? (needw >> (8 * (c & 3))) & 3u : 0u;
 #pragma unroll
-          for (int kk = 0; kk < DH / 16; ++kk) {
-            const int h = kk >> 2, ko = (kk & 3) * 32;
-            umma_f16(tt, sdesc_sw128(qa + h * 16384 + ko, 16, 1024), sdesc_sw128(ka + h * 8192 + ko, 16, 1024),
-                     idesc_s, kk > 0 ? 1u : 0u);
+        for (int t = 0; t < 2; ++t) {
+          const uint32_t tt = tmem + (uint32_t)(t * 256);
+          const bool s_t = ok && ((need >> t) & 1u);
+          const bool reload = s_t && c >= nwc && !nope[t];
+          if (reload) {
+            // Q is free once the tile's last S is complete and the softmax has read it for its bound
+            if ((ns[t] > 0 && !wwait(&sm.s_full[t], (ns[t] - 1) & 1)) || !wwait(&sm.qn_read[t], 0)) {
+              ok = false;
+              break;
+            }
+            if (elect_one_sync()) {
+              mbar_arrive_expect_tx(&sm.qc_ready[t], qbox_bytes);
+              for (int h = 0; h < HALVES; ++h)
+                tma_load_4d(sm.q[t] + h * 16384, &tm_qc, h * 64, g * G, li0 + t * QT, b, &sm.qc_ready[t]);
+            }
+            __syncwarp();
           }
-          umma_commit(&sm.s_full[t]);
-          ++ns;
+          if (ok && pend[t] >= 0) {
+            const int iv = 2 * pend[t] + 1;
+            if (!wait_item(iv) || !wwait(&sm.p_full[t], np[t] & 1)) {
+              ok = false;
+              break;
+            }
+            tc_fence_after();
+            const uint64_t vdesc = sdesc_sw128(smem_u32(sm.ring[iv % NSLOT]), SM::GBYTES, 1024);
+            if (elect_one_sync()) {
+#pragma unroll
+              for (int kk = 0; kk < kTcKeys / 16; ++kk)  // K = 16 keys = 8 packed columns of P per MMA
+                umma_f16_ts(tt + 128, tt + kk * 8, vdesc + (uint64_t)(kk * 2048 >> 4), idesc_o,
+                            (np[t] > 0 || kk > 0) ? 1u : 0u);
+            }
+            __syncwarp();
+            ++np[t];
+            pend[t] = -1;
+          }
+          if (s_t) {
+            if (reload) {
+              if (!wwait(&sm.qc_ready[t], 0)) {
+                ok = false;
+                break;
+              }
+              nope[t] = true;
+            }
+            if (!wait_item(2 * c)) {
+              ok = false;
+              break;
+            }
+            tc_fence_after();
+            const uint64_t qdesc = sdesc_sw128(smem_u32(sm.q[t]), 16, 1024);
+            const uint64_t kdesc = sdesc_sw128(smem_u32(sm.ring[(2 * c) % NSLOT]), 16, 1024);
+            if (elect_one_sync()) {
+#pragma unroll
+              for (int kk = 0; kk < DH / 16; ++kk) {
+                const int h = kk >> 2, ko = (kk & 3) * 32;
+                umma_f16(tt, qdesc + (uint64_t)((h * 16384 + ko) >> 4), kdesc + (uint64_t)((h * SM::GBYTES + ko) >> 4),
+                         idesc_s, kk > 0 ? 1u : 0u);
+              }
+              umma_commit(&sm.s_full[t]);
+            }
+            __syncwarp();
+            ++ns[t];
+            pend[t] = c;
+          }
         }
-        umma_commit(&sm.empty[st]);  // this issuer is done with the K tile
-        if (c >= 1 && !pv(c - 1)) ok = false;
+        if (!ok) break;
+        // release K(c) and V(c - 1) once landed (a tile that used one has waited for it)
+        if (c < NCH) {
+          if (need == 0u && !wait_item(2 * c)) break;
+          if (elect_one_sync()) umma_commit(&sm.empty[(2 * c) % NSLOT]);
+          __syncwarp();
+        }
+        if (c >= 1) {
+          if (prev_need == 0u && !wait_item(2 * c - 1)) break;
+          if (elect_one_sync()) umma_commit(&sm.empty[(2 * c - 1) % NSLOT]);
+          __syncwarp();
+        }
+        prev_need = need;
       }
-      if (ok && NCH >= 1) ok = pv(NCH - 1);
-      umma_commit(&sm.o_full[t]);
-      // drain: every MMA this thread issued is complete before TMEM can be released
-      umma_commit(&sm.drain[t]);
-      mbar_wait(&sm.drain[t], 0, p.err);
+      if (elect_one_sync()) {
+        umma_commit(&sm.o_full[0]);
+        umma_commit(&sm.o_full[1]);
+        // drain: every MMA is complete before TMEM can be released
+        umma_commit(&sm.drain[0]);
+      }
+      __syncwarp();
+      wwait(&sm.drain[0], 0);
     }
-  } else {
+  } else if (warp < 8) {
     // ---------------- softmax / epilogue of tile t, one thread per row ----------------
     const int t = warp >> 2;
     const int r = tid - 128 * t;
@@ -365,8 +486,9 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     const bool row_ok = (r < QT * G) && (qt < nqt(t));
     const int hq = g * G + hh;
     const uint32_t lane_off = (uint32_t)((warp & 3) * 32) << 16;
-    const uint32_t t_s = tmem + (uint32_t)(t * 256), t_p = t_s + 64, t_o = t_s + 128;  // S, P buffer 0, O
-    // the query tiles arrive by TMA; this row's logit bound from its QKNorm'd values
+    const uint32_t t_s = tmem + (uint32_t)(t * 256), t_o = t_s + 128;  // S (P over its first 64 columns), O
+    // the query tiles arrive by TMA; this row's logit bound from its (RoPE'd:
+    // a rotation, same norm up to rounding) values
     float M2 = 0.f;
     bool ok = __all_sync(0xffffffffu, mbar_wait(&sm.q_ready, 0, p.err));
     if (row_ok) {
@@ -374,13 +496,14 @@ __global__ void __launch_bounds__(kTcThreads, 1)
 #pragma unroll
       for (int d8 = 0; d8 < DH / 8; ++d8) {
         float f[8];
-        unpack8(*reinterpret_cast<const uint4*>(sm.qc[t] + (d8 / 8) * 16384 + sw128_offset(r, (d8 % 8) * 8)), f);
+        unpack8(*reinterpret_cast<const uint4*>(sm.q[t] + (d8 / 8) * 16384 + sw128_offset(r, (d8 % 8) * 8)), f);
 #pragma unroll
         for (int e = 0; e < 8; ++e) qn2 = fmaf(f[e], f[e], qn2);
       }
       const float kmax = sqrtf((float)DH) * p.k_gain[g] * (1.f + 1.f / 64.f);
       M2 = p.scale * sqrtf(qn2) * kmax * kLog2e;
     }
+    mbar_arrive(&sm.qn_read[t]);  // the tile may be reloaded from here on
     // the row's reference maximum: its bound (fixed), or a running max that starts empty
     const bool bounded = M2 <= kBoundedLog2;
     const bool warp_bounded = __all_sync(0xffffffffu, bounded);
@@ -388,56 +511,90 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     if (r == 0 && t == 0) stamp(2);
     const float sl2 = p.scale * kLog2e;
     const int win_lo = max(geo.S, i - geo.W + 1);
-    float l = 0.f;
+    // this row's valid columns [lo, hi) of a half (hi <= lo: none)
+    auto row_range = [&](const Half& x, int& lo, int& hi) {
+      lo = 0;
+      hi = 0;
+      if (!row_ok) return;
+      if (x.type == kWindow) {
+        lo = max(win_lo - x.kb, 0);
+        hi = min(i - x.kb + 1, kTcBlock);
+      } else if (x.type == kSink) {
+        hi = min(geo.S, i + 1);
+      } else if (x.type == kRouted) {
+        hi = ((((t == 0 ? x.m0 : x.m1)) >> qt) & 1u) ? kTcBlock : 0;  // a picked block is wholly before i - W + 1
+      }
+    };
+    // the row's sum of p over even and odd columns, one packed pair (the
+    // softmax is issue-bound, not MUFU-bound: sm_100's paired fp32 fma / add
+    // halve the instructions around the exponentials)
+    unsigned long long lsum = f2pack(0.f, 0.f);
+    // P of quarter qq (32 columns of S) -> TMEM columns [16 qq, 16 qq + 16), valid columns [lo, hi) of the quarter
+    auto quarter = [&](const float* s, int qq, int lo, int hi) {
+      uint32_t pk[16];
+      const unsigned long long sl2x2 = f2pack(sl2, sl2), nm2 = f2pack(-M, -M);
+      if (hi - lo == 32) {
+#pragma unroll
+        for (int q = 0; q < 16; ++q) {
+          float x0, x1;
+          f2unpack(ffma2(f2pack(s[2 * q], s[2 * q + 1]), sl2x2, nm2), x0, x1);
+          const float p0 = ex2_approx(x0), p1 = ex2_approx(x1);
+          lsum = fadd2(lsum, f2pack(p0, p1));
+          pk[q] = pack_bf16x2(p0, p1);
+        }
+      } else if (hi > lo) {
+#pragma unroll
+        for (int q = 0; q < 16; ++q) {
+          float x0, x1;
+          f2unpack(ffma2(f2pack(s[2 * q], s[2 * q + 1]), sl2x2, nm2), x0, x1);
+          float p0 = ex2_approx(x0), p1 = ex2_approx(x1);
+          p0 = (2 * q >= lo && 2 * q < hi) ? p0 : 0.f;
+          p1 = (2 * q + 1 >= lo && 2 * q + 1 < hi) ? p1 : 0.f;
+          lsum = fadd2(lsum, f2pack(p0, p1));
+          pk[q] = pack_bf16x2(p0, p1);
+        }
+      } else {
+#pragma unroll
+        for (int q = 0; q < 16; ++q) pk[q] = 0u;
+      }
+      tmem_st16_nowait(t_s + (uint32_t)(16 * qq) + lane_off, pk);
+    };
     int j = 0;  // chunks this tile has processed
+    uint32_t needw = 0u;
     for (int c = 0; ok && c < NCH; ++c) {
-      const Chunk ck = chunk(c);
-      if (!((ck.need >> t) & 1u)) continue;
+      if ((c & 3) == 0) needw = *reinterpret_cast<const uint32_t*>(&sm.cneed[c]);
+      if (!((needw >> (8 * (c & 3) + t)) & 1u)) continue;
+      const Half x0 = half_of(c, 0), x1 = half_of(c, 1);
       // a failed wait leaves the whole warp together (the TMEM accesses are warp-collective)
       if (!__all_sync(0xffffffffu, mbar_wait(&sm.s_full[t], j & 1, p.err))) {
         ok = false;
         break;
       }
       tc_fence_after();
-      float s[kTcKeys];
-      tmem_ld32(t_s + lane_off, s);
-      tmem_ld32(t_s + 32 + lane_off, s + 32);
-      tmem_ld_wait();
-      tc_fence_before();
-      mbar_arrive(&sm.s_free[t]);  // the next S MMA of this tile may overwrite S
-      const int kb = ck.kb;
-      const uint32_t type = ck.type;
-      // this row's valid columns [cl, ch) of the chunk, worked out once
-      int cl = 0, ch = 0;
-      if (row_ok) {
-        if (type == kRouted) {
-          const uint32_t qm = t == 0 ? ck.m0 : ck.m1;
-          ch = ((qm >> qt) & 1u) ? kTcKeys : 0;  // a picked block is wholly before i - W + 1
-        } else if (type == kSink) {
-          ch = min(geo.S, i + 1) - kb;
-        } else {
-          cl = max(win_lo - kb, 0);
-          ch = min(i - kb + 1, kTcKeys);
-        }
-      }
+      int lo0, hi0, lo1, hi1;
+      row_range(x0, lo0, hi0);
+      row_range(x1, lo1, hi1);
       if (!warp_bounded) {
         // running max: this row's chunk max over its valid columns
         float mx = neg_inf();
-        if (ch > cl) {
 #pragma unroll
-          for (int col = 0; col < kTcKeys; ++col) mx = fmaxf(mx, (col >= cl && col < ch) ? s[col] : neg_inf());
+        for (int h = 0; h < 2; ++h) {
+          const int lo = h == 0 ? lo0 : lo1, hi = h == 0 ? hi0 : hi1;
+          if (__any_sync(0xffffffffu, hi > lo)) {
+            float s[kTcBlock];
+            tmem_ld32(t_s + h * 64 + lane_off, s);
+            tmem_ld32(t_s + h * 64 + 32 + lane_off, s + 32);
+            tmem_ld_wait();
+#pragma unroll
+            for (int col = 0; col < kTcBlock; ++col) mx = fmaxf(mx, (col >= lo && col < hi) ? s[col] : neg_inf());
+          }
         }
         const float mn = bounded ? M : fmaxf(M, mx * sl2);
         const bool need = mn > M + kRescaleLog2;  // -inf + 8 = -inf: the first valid value
         if (__any_sync(0xffffffffu, need)) {
           const float al = need ? (M == neg_inf() ? 0.f : ex2_approx(M - mn)) : 1.f;
           if (j >= 1) {
-            // O holds PV(0 .. j-1): wait for the last one, rescale the warp's rows
-            if (!__all_sync(0xffffffffu, mbar_wait(&sm.p_free[t][(j - 1) & 1], ((j - 1) >> 1) & 1, p.err))) {
-              ok = false;
-              break;
-            }
-            tc_fence_after();
+            // O holds PV(0 .. j-1), complete: S(j) was issued after PV(j-1)
 #pragma unroll
             for (int cb = 0; cb < DH / 32; ++cb) {
               float o[32];
@@ -449,41 +606,37 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             }
           }
           if (need) {
-            l *= al;
+            lsum = ffma2(lsum, f2pack(al, al), f2pack(0.f, 0.f));
             M = mn;
           }
         }
       }
-      uint32_t pk[kTcKeys / 2];
-      if (ch <= cl) {  // nothing of this chunk for this row (most rows of a block few queries picked)
-#pragma unroll
-        for (int q = 0; q < kTcKeys / 2; ++q) pk[q] = 0u;
-      } else {
-#pragma unroll
-        for (int q = 0; q < kTcKeys / 2; ++q) {
-          float pv2[2];
-#pragma unroll
-          for (int u = 0; u < 2; ++u) {
-            const int col = 2 * q + u;
-            float pe = ex2_approx(fmaf(s[col], sl2, -M));
-            pe = (col >= cl && col < ch) ? pe : 0.f;
-            l += pe;
-            pv2[u] = pe;
-          }
-          pk[q] = pack_bf16x2(pv2[0], pv2[1]);
-        }
+      // four quarters of 32 columns, the next one's TMEM load in flight while
+      // one is turned into P; P of quarter qq overwrites S columns [16qq,
+      // 16qq + 16), read by then
+      {
+        float sa[32], sb[32];
+        tmem_ld32(t_s + lane_off, sa);
+        tmem_ld_wait();
+        tmem_ld32(t_s + 32 + lane_off, sb);
+        quarter(sa, 0, lo0, min(hi0, 32));
+        tmem_ld_wait();
+        tmem_ld32(t_s + 64 + lane_off, sa);
+        quarter(sb, 1, max(lo0 - 32, 0), hi0 - 32);
+        tmem_ld_wait();
+        tmem_ld32(t_s + 96 + lane_off, sb);
+        quarter(sa, 2, lo1, min(hi1, 32));
+        tmem_ld_wait();
+        quarter(sb, 3, max(lo1 - 32, 0), hi1 - 32);
       }
-      // P buffer j & 1 is free once PV(j - 2) of this tile has completed
-      const int pb = j & 1;
-      if (j >= 2 && !__all_sync(0xffffffffu, mbar_wait(&sm.p_free[t][pb], ((j - 2) >> 1) & 1, p.err))) {
-        ok = false;
-        break;
-      }
-      tmem_st_u32<32>(t_p + pb * 32 + lane_off, pk);
+      tmem_st_wait();
       tc_fence_before();
-      mbar_arrive(&sm.p_full[t][pb]);
+      mbar_arrive(&sm.p_full[t]);
       ++j;
     }
+    float l0, l1;
+    f2unpack(lsum, l0, l1);
+    const float l = l0 + l1;
     if (r == 0 && t == 0) stamp(14);
     if (__all_sync(0xffffffffu, ok && (j == 0 || mbar_wait(&sm.o_full[t], 0, p.err)))) {
       tc_fence_after();
@@ -549,11 +702,11 @@ static bool make_map(CUtensorMap* m, const void* base, int B, int n, int H, int 
 bool prefill_tc_supported(const Geom& geo, int dh, int n, bool qknorm) {
   const int G = geo.G;
   const int QT = 128 / G;
-  // the routed union of a tile pair (2 QT queries x k picks) fits the chunk list; its
-  // block masks (nb x 8 bytes) fit the K/V ring they overlay while the list is built
-  return qknorm && (dh == 64 || dh == 128) && geo.Bk == kTcKeys && G >= 4 && G <= 16 && QT * G >= 64 &&
-         2 * QT * geo.K <= kTcMaxRouted && (size_t)(n / geo.Bk) * 8 <= sizeof(TcSmem<64>::ring) &&
-         geo.W <= 1024 && encode_fn() != nullptr;
+  // the sink block and the routed union of a tile pair (2 QT queries x k picks) fit the
+  // NoPE list; its block masks (nb x 8 bytes) fit the K/V ring they overlay while the list is built
+  return qknorm && (dh == 64 || dh == 128) && geo.Bk == kTcBlock && G >= 4 && G <= 16 && QT * G >= 64 &&
+         1 + 2 * QT * geo.K <= kTcMaxEntries && (size_t)(n / geo.Bk) * 8 <= sizeof(TcSmem<64>::ring) &&
+         (size_t)(n / geo.Bk) * 8 <= sizeof(TcSmem<128>::ring) && geo.W <= 1024 && encode_fn() != nullptr;
 }
 
 cudaError_t launch_prefill_tc(const Geom& geo, int dh, int n, int q_off, float scale, const __nv_bfloat16* qc,
@@ -563,7 +716,7 @@ cudaError_t launch_prefill_tc(const Geom& geo, int dh, int n, int q_off, float s
                               unsigned long long* trace, long long trace_rows, cudaStream_t st) {
   CUtensorMap m_qc, m_qr;
   const int QT = 128 / geo.G;
-  if (n % kTcKeys != 0 || ((reinterpret_cast<uintptr_t>(kc_sw) | reinterpret_cast<uintptr_t>(kr_sw) |
+  if (n % kTcBlock != 0 || ((reinterpret_cast<uintptr_t>(kc_sw) | reinterpret_cast<uintptr_t>(kr_sw) |
                             reinterpret_cast<uintptr_t>(v_sw)) & 15u) != 0 ||
       !make_map(&m_qc, qc, geo.B, geo.nq, geo.Hq, dh, geo.G, QT) ||
       !make_map(&m_qr, qr, geo.B, geo.nq, geo.Hq, dh, geo.G, QT))

@@ -149,7 +149,11 @@ HBA_DEVICE void store_chunked(__nv_bfloat16* __restrict__ y, size_t row_base, in
 // kc and kr for every (batch, token, kv head) of a [B, n, Hkv, dh] tensor.
 // With kc_sw != nullptr (the tensor-core prefill): kc as above, and kc, its
 // RoPE'd copy and v (when given) also in the chunk-tiled layout [B, Hkv,
-// n/64, dh/64, 64 x 64] (kr itself is then not written).
+// n/64, dh/64, 64 x 64] (kr itself is then not written).  A warp handles
+// kQkRows consecutive rows and issues all their loads before any math, so
+// enough bytes are in flight per SM for this pure streaming pass.
+constexpr int kQkRows = 4;
+
 template <int DH>
 __global__ void __launch_bounds__(256) qknorm_rope_kernel(Geom geo, int n, const __nv_bfloat16* __restrict__ k,
                                                           const float* __restrict__ k_gain,
@@ -161,28 +165,39 @@ __global__ void __launch_bounds__(256) qknorm_rope_kernel(Geom geo, int n, const
                                                           __nv_bfloat16* __restrict__ kc_sw,
                                                           __nv_bfloat16* __restrict__ kr_sw,
                                                           __nv_bfloat16* __restrict__ v_sw, int pos0) {
-  const int64_t w = (int64_t)blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32;
-  if (w >= (int64_t)geo.B * n * geo.Hkv) return;
-  const int g = (int)(w % geo.Hkv);
-  const int p = pos0 + (int)((w / geo.Hkv) % n);  // the row's position (RoPE tables row)
-  if (kc_sw == nullptr) {
-    key_row<DH>(k + w * DH, kc + w * DH, kr + w * DH, geo.qknorm ? k_gain[g] : 1.f, geo.eps, geo.qknorm != 0,
-                cos + (size_t)p * DH, sin + (size_t)p * DH);
-    return;
-  }
   constexpr int PER = DH / 32;
-  const int b = (int)(w / ((int64_t)geo.Hkv * n));
-  const size_t row_base = ((size_t)b * geo.Hkv + g) * (size_t)n * DH;  // n % 64 == 0, pos0 == 0
-  float x[PER], r[PER];
-  load_head_row<DH>(k + w * DH, x);
-  if (geo.qknorm) qknorm_lane<DH>(x, k_gain[g], geo.eps);
-  store_head_row<DH>(kc + w * DH, x);
-  store_chunked<DH>(kc_sw, row_base, p, x);
-  rope_lane<DH>(x, r, cos + (size_t)p * DH, sin + (size_t)p * DH);
-  store_chunked<DH>(kr_sw, row_base, p, r);
-  if (v != nullptr) {
-    load_head_row<DH>(v + w * DH, x);
-    store_chunked<DH>(v_sw, row_base, p, x);
+  const int64_t total = (int64_t)geo.B * n * geo.Hkv;
+  const int64_t w0 = ((int64_t)blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32) * kQkRows;
+  if (w0 >= total) return;
+  float x[kQkRows][PER], vv[kQkRows][PER];
+#pragma unroll
+  for (int r = 0; r < kQkRows; ++r)
+    if (w0 + r < total) load_head_row<DH>(k + (w0 + r) * DH, x[r]);
+  const bool tiled = kc_sw != nullptr;
+  if (tiled && v != nullptr) {
+#pragma unroll
+    for (int r = 0; r < kQkRows; ++r)
+      if (w0 + r < total) load_head_row<DH>(v + (w0 + r) * DH, vv[r]);
+  }
+#pragma unroll
+  for (int r = 0; r < kQkRows; ++r) {
+    const int64_t w = w0 + r;
+    if (w >= total) break;  // warp-uniform
+    const int g = (int)(w % geo.Hkv);
+    const int p = pos0 + (int)((w / geo.Hkv) % n);  // the row's position (RoPE tables row)
+    float rr[PER];
+    if (geo.qknorm) qknorm_lane<DH>(x[r], k_gain[g], geo.eps);
+    store_head_row<DH>(kc + w * DH, x[r]);
+    rope_lane<DH>(x[r], rr, cos + (size_t)p * DH, sin + (size_t)p * DH);
+    if (!tiled) {
+      store_head_row<DH>(kr + w * DH, rr);
+      continue;
+    }
+    const int b = (int)(w / ((int64_t)geo.Hkv * n));
+    const size_t row_base = ((size_t)b * geo.Hkv + g) * (size_t)n * DH;  // n % 64 == 0, pos0 == 0
+    store_chunked<DH>(kc_sw, row_base, p, x[r]);
+    store_chunked<DH>(kr_sw, row_base, p, rr);
+    if (v != nullptr) store_chunked<DH>(v_sw, row_base, p, vv[r]);
   }
 }
 
@@ -218,7 +233,7 @@ cudaError_t launch_qknorm_rope(const Geom& geo, int n, const __nv_bfloat16* k, c
                                const float* cos, const float* sin, __nv_bfloat16* kc, __nv_bfloat16* kr, int dh,
                                cudaStream_t st, const __nv_bfloat16* v, __nv_bfloat16* kc_sw,
                                __nv_bfloat16* kr_sw, __nv_bfloat16* v_sw, int pos0) {
-  const int64_t warps = (int64_t)geo.B * n * geo.Hkv;
+  const int64_t warps = ((int64_t)geo.B * n * geo.Hkv + kQkRows - 1) / kQkRows;
   const int64_t blocks = (warps + 7) / 8;
   if (blocks == 0) return cudaSuccess;
   if (kc_sw != nullptr && (n % 64 != 0 || pos0 != 0 || kr_sw == nullptr || (v != nullptr && v_sw == nullptr)))

@@ -180,6 +180,18 @@ HBA_DEVICE void umma_f16_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc, u
       "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate)
       : "memory");
 }
+// One lane of the (converged) warp is elected: true there, false elsewhere.
+// Code that runs on the whole warp keeps its operands warp-uniform and
+// issues a single-thread instruction (tcgen05.mma, a TMA copy) from the
+// elected lane.
+HBA_DEVICE bool elect_one_sync() {
+  uint32_t pred = 0;
+  asm volatile(
+      "{\n .reg .b32 r;\n .reg .pred p;\n elect.sync r|p, 0xffffffff;\n selp.u32 %0, 1, 0, p;\n}\n"
+      : "=r"(pred));
+  return pred != 0;
+}
+
 // Arrives on `bar` once every tcgen05.mma issued so far by this thread is complete.
 HBA_DEVICE void umma_commit(uint64_t* bar) {
   asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];\n" ::"r"(
@@ -209,6 +221,27 @@ HBA_DEVICE float ex2_approx(float x) {
   float y;
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
   return y;
+}
+
+// Two fp32 lanes in one 64-bit register pair, and sm_100's packed fp32 ops
+// on them (each lane rounded exactly as the scalar fmaf / add).
+HBA_DEVICE unsigned long long f2pack(float lo, float hi) {
+  unsigned long long r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
+  return r;
+}
+HBA_DEVICE void f2unpack(unsigned long long v, float& lo, float& hi) {
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(v));
+}
+HBA_DEVICE unsigned long long ffma2(unsigned long long a, unsigned long long b, unsigned long long c) {
+  unsigned long long d;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+  return d;
+}
+HBA_DEVICE unsigned long long fadd2(unsigned long long a, unsigned long long b) {
+  unsigned long long d;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
 }
 
 // N fp32 columns of this thread's TMEM lane (32x32b shape), waited.
@@ -274,6 +307,18 @@ HBA_DEVICE void tmem_st_u32(uint32_t taddr, const uint32_t* v) {
       : "memory");
   asm volatile("tcgen05.wait::st.sync.aligned;\n" ::: "memory");
 }
+
+// 16 raw 32-bit columns written to this thread's TMEM lane (32x32b shape),
+// not waited: the caller issues tmem_st_wait() before its tcgen05 fence.
+HBA_DEVICE void tmem_st16_nowait(uint32_t taddr, const uint32_t* v) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};\n" ::"r"(
+          taddr),
+      "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]), "r"(v[8]), "r"(v[9]),
+      "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]), "r"(v[15])
+      : "memory");
+}
+HBA_DEVICE void tmem_st_wait() { asm volatile("tcgen05.wait::st.sync.aligned;\n" ::: "memory"); }
 
 // Maximum of x over the full warp in one instruction (sm_100a redux.sync
 // .f32; -inf is the identity, a NaN input is ignored).

@@ -12,8 +12,9 @@
 
 namespace hba {
 
-constexpr int kSumThreads = 128;
-constexpr int kBlocksPerCta = 8;
+constexpr int kSumThreads = 256;
+constexpr int kSumRound = 4;       // blocks whose pooled rows are projected together
+constexpr int kBlocksPerCta = 16;  // blocks per CTA (the projection is staged once per CTA)
 
 // First/last block completed by appending tokens [p, p+t) (inclusive range,
 // empty when lo > hi).
@@ -22,20 +23,30 @@ HBA_DEVICE void completed_blocks(int p, int t, int Bk, int& lo, int& hi) {
   hi = (p + t) / Bk - 1;
 }
 
+// Per block, in shared memory: the keys (fp32 rows of DH + 4 floats, so a
+// row is 16-byte aligned and 8 lanes' float4 reads of 8 rows hit distinct
+// banks), the slot logits, the pooled rows of a round of kSumRound blocks
+// (transposed: [DH][rows]).  The projection then runs once per round, each
+// thread 2 rows x DH/32 columns (one float2 of pooled values and one vector
+// of projection columns per d).  Every sum runs in the same order as the
+// reference formula's loops (d, then tokens, then d), in fp32.
 template <int DH>
-__global__ void __launch_bounds__(kSumThreads) summarize_kernel(Geom geo, const __nv_bfloat16* __restrict__ kc,
-                                                                const float* __restrict__ probes,
-                                                                const float* __restrict__ proj,
-                                                                __nv_bfloat16* __restrict__ summ, int blk_begin,
-                                                                int blk_end, const int32_t* __restrict__ pos,
-                                                                int t, float rsd) {
-  extern __shared__ float smem[];
+__global__ void __launch_bounds__(kSumThreads, 2) summarize_kernel(Geom geo, const __nv_bfloat16* __restrict__ kc,
+                                                                   const float* __restrict__ probes,
+                                                                   const float* __restrict__ proj,
+                                                                   __nv_bfloat16* __restrict__ summ, int blk_begin,
+                                                                   int blk_end, const int32_t* __restrict__ pos,
+                                                                   int t, float rsd) {
+  extern __shared__ __align__(16) float smem[];
+  constexpr int KS = DH + 4;
+  constexpr int CP = DH / 32;  // projection columns per thread
   const int m = geo.m, Bk = geo.Bk;
+  const int R = kSumRound * m;             // pooled rows of a round
   float* proj_s = smem;                    // [DH][DH]
   float* probe_s = proj_s + DH * DH;       // [m][DH]
-  float* k_s = probe_s + m * DH;           // [Bk][DH+1]
-  float* att_s = k_s + Bk * (DH + 1);      // [m][Bk]
-  float* pool_s = att_s + m * Bk;          // [m][DH]
+  float* k_s = probe_s + m * DH;           // [Bk][KS]
+  float* att_s = k_s + Bk * KS;            // [m][Bk]
+  float* pool_s = att_s + m * Bk;          // [DH][R]
   const int g = blockIdx.y, b = blockIdx.z, tid = threadIdx.x;
 
   int lo = blk_begin, hi = blk_end - 1;
@@ -51,63 +62,102 @@ __global__ void __launch_bounds__(kSumThreads) summarize_kernel(Geom geo, const 
   const int last = min(hi, first + kBlocksPerCta - 1);
   if (first > last) return;
 
-  for (int e = tid; e < DH * DH; e += kSumThreads) proj_s[e] = proj[(size_t)g * DH * DH + e];
+  for (int e = tid; e < DH * DH / 4; e += kSumThreads)
+    reinterpret_cast<float4*>(proj_s)[e] = reinterpret_cast<const float4*>(proj + (size_t)g * DH * DH)[e];
   for (int e = tid; e < m * DH; e += kSumThreads) probe_s[e] = probes[(size_t)g * m * DH + e];
+  __nv_bfloat16* summ_bg = summ + (((size_t)b * geo.Hkv + g) * geo.nb_cap) * (size_t)m * DH;
 
-  for (int blk = first; blk <= last; ++blk) {
-    __syncthreads();
-    // keys of the block -> fp32 smem (row stride DH+1: conflict-free column reads)
-    for (int e = tid; e < Bk * (DH / 8); e += kSumThreads) {
-      const int row = e / (DH / 8), c8 = e % (DH / 8);
-      const size_t off = (((size_t)b * geo.n_cap + (size_t)blk * Bk + row) * geo.Hkv + g) * DH + c8 * 8;
-      float f[8];
-      unpack8(*reinterpret_cast<const uint4*>(kc + off), f);
-#pragma unroll
-      for (int j = 0; j < 8; ++j) k_s[row * (DH + 1) + c8 * 8 + j] = f[j];
-    }
-    __syncthreads();
-    for (int e = tid; e < m * Bk; e += kSumThreads) {
-      const int mi = e / Bk, tok = e % Bk;
-      const float* pr = probe_s + mi * DH;
-      const float* kr = k_s + tok * (DH + 1);
-      float acc = 0.f;
-#pragma unroll 8
-      for (int d = 0; d < DH; ++d) acc = fmaf(pr[d], kr[d], acc);
-      att_s[e] = acc * rsd;
-    }
-    __syncthreads();
-    // softmax over the block's tokens, one warp per slot
-    for (int mi = tid / 32; mi < m; mi += kSumThreads / 32) {
-      const int lane = tid & 31;
-      float mx = neg_inf();
-      for (int j = lane; j < Bk; j += 32) mx = fmaxf(mx, att_s[mi * Bk + j]);
-      mx = warp_max(mx);
-      float sum = 0.f;
-      for (int j = lane; j < Bk; j += 32) {
-        const float e = expf(att_s[mi * Bk + j] - mx);
-        att_s[mi * Bk + j] = e;
-        sum += e;
+  for (int b0 = first; b0 <= last; b0 += kSumRound) {
+    const int nr = min(kSumRound, last - b0 + 1);
+    for (int jb = 0; jb < nr; ++jb) {
+      const int blk = b0 + jb;
+      __syncthreads();  // k_s / att_s free (and, first time, proj_s / probe_s written)
+      for (int e = tid; e < Bk * (DH / 8); e += kSumThreads) {
+        const int row = e / (DH / 8), c8 = e % (DH / 8);
+        const size_t off = (((size_t)b * geo.n_cap + (size_t)blk * Bk + row) * geo.Hkv + g) * DH + c8 * 8;
+        float f[8];
+        unpack8(*reinterpret_cast<const uint4*>(kc + off), f);
+        float4* dst = reinterpret_cast<float4*>(k_s + row * KS + c8 * 8);
+        dst[0] = make_float4(f[0], f[1], f[2], f[3]);
+        dst[1] = make_float4(f[4], f[5], f[6], f[7]);
       }
-      sum = warp_sum(sum);
-      for (int j = lane; j < Bk; j += 32) att_s[mi * Bk + j] /= sum;
-    }
-    __syncthreads();
-    for (int e = tid; e < m * DH; e += kSumThreads) {
-      const int mi = e / DH, d = e % DH;
-      const float* a = att_s + mi * Bk;
-      float acc = 0.f;
-      for (int tok = 0; tok < Bk; ++tok) acc = fmaf(a[tok], k_s[tok * (DH + 1) + d], acc);
-      pool_s[e] = acc;
-    }
-    __syncthreads();
-    __nv_bfloat16* dst = summ + ((((size_t)b * geo.Hkv + g) * geo.nb_cap + blk) * m) * DH;
-    for (int e = tid; e < m * DH; e += kSumThreads) {
-      const int mi = e / DH, col = e % DH;
-      const float* pl = pool_s + mi * DH;
-      float acc = 0.f;
+      __syncthreads();
+      // att[mi][tok] = probes[mi] . k[tok] * dh^-1/2 (an fma chain over d)
+      for (int e = tid; e < m * Bk; e += kSumThreads) {
+        const int mi = e / Bk, tok = e % Bk;
+        const float4* pr = reinterpret_cast<const float4*>(probe_s + mi * DH);
+        const float4* kr = reinterpret_cast<const float4*>(k_s + tok * KS);
+        float acc = 0.f;
 #pragma unroll 8
-      for (int d = 0; d < DH; ++d) acc = fmaf(pl[d], proj_s[d * DH + col], acc);
-      dst[e] = f2bf(acc);
+        for (int d4 = 0; d4 < DH / 4; ++d4) {
+          const float4 a = pr[d4], k4 = kr[d4];
+          acc = fmaf(a.x, k4.x, acc);
+          acc = fmaf(a.y, k4.y, acc);
+          acc = fmaf(a.z, k4.z, acc);
+          acc = fmaf(a.w, k4.w, acc);
+        }
+        att_s[e] = acc * rsd;
+      }
+      __syncthreads();
+      // softmax over the block's tokens, one warp per slot
+      for (int mi = tid / 32; mi < m; mi += kSumThreads / 32) {
+        const int lane = tid & 31;
+        float mx = neg_inf();
+        for (int j = lane; j < Bk; j += 32) mx = fmaxf(mx, att_s[mi * Bk + j]);
+        mx = warp_max(mx);
+        float sum = 0.f;
+        for (int j = lane; j < Bk; j += 32) {
+          const float e = expf(att_s[mi * Bk + j] - mx);
+          att_s[mi * Bk + j] = e;
+          sum += e;
+        }
+        sum = warp_sum(sum);
+        for (int j = lane; j < Bk; j += 32) att_s[mi * Bk + j] /= sum;
+      }
+      __syncthreads();
+      // pooled[mi][d] = sum_tok att[mi][tok] k[tok][d] -> pool_s[d][jb * m + mi]
+      for (int e = tid; e < m * DH; e += kSumThreads) {
+        const int mi = e / DH, d = e % DH;
+        const float* a = att_s + mi * Bk;
+        float acc = 0.f;
+        for (int tok = 0; tok < Bk; ++tok) acc = fmaf(a[tok], k_s[tok * KS + d], acc);
+        pool_s[d * R + jb * m + mi] = acc;
+      }
+    }
+    __syncthreads();
+    // S[row][col] = pooled[row] @ proj, rows = the round's (block, slot) pairs
+    const int rows = nr * m;
+    const int cg = tid & 31, rg = tid >> 5;
+    for (int r0 = 2 * rg; r0 < rows; r0 += 2 * (kSumThreads / 32)) {
+      const bool two = r0 + 1 < rows;
+      float acc0[CP], acc1[CP];
+#pragma unroll
+      for (int c = 0; c < CP; ++c) acc0[c] = acc1[c] = 0.f;
+#pragma unroll 4
+      for (int d = 0; d < DH; ++d) {
+        const float p0 = pool_s[d * R + r0], p1 = two ? pool_s[d * R + r0 + 1] : 0.f;
+        float w[CP];
+        if constexpr (CP == 4) {
+          const float4 v = reinterpret_cast<const float4*>(proj_s + d * DH)[cg];
+          w[0] = v.x; w[1] = v.y; w[2] = v.z; w[3] = v.w;
+        } else {
+          const float2 v = reinterpret_cast<const float2*>(proj_s + d * DH)[cg];
+          w[0] = v.x; w[1] = v.y;
+        }
+#pragma unroll
+        for (int c = 0; c < CP; ++c) {
+          acc0[c] = fmaf(p0, w[c], acc0[c]);
+          acc1[c] = fmaf(p1, w[c], acc1[c]);
+        }
+      }
+      // row r = block b0 + r / m, slot r % m: rows of consecutive blocks are consecutive in summ
+      __nv_bfloat16* d0 = summ_bg + ((size_t)b0 * m + r0) * DH + cg * CP;
+#pragma unroll
+      for (int c = 0; c < CP; ++c) d0[c] = f2bf(acc0[c]);
+      if (two) {
+#pragma unroll
+        for (int c = 0; c < CP; ++c) d0[DH + c] = f2bf(acc1[c]);
+      }
     }
   }
 }
@@ -147,7 +197,8 @@ __global__ void __launch_bounds__(128) supers_kernel(Geom geo, int nb_fixed, con
 }
 
 static size_t summarize_smem(int dh, int m, int Bk) {
-  return sizeof(float) * ((size_t)dh * dh + (size_t)m * dh + (size_t)Bk * (dh + 1) + (size_t)m * Bk + (size_t)m * dh);
+  return sizeof(float) * ((size_t)dh * dh + (size_t)m * dh + (size_t)Bk * (dh + 4) + (size_t)m * Bk +
+                          (size_t)dh * kSumRound * m);
 }
 
 cudaError_t launch_summarize(const Geom& geo, int dh, const __nv_bfloat16* k_cache, const float* probes,
