@@ -18,43 +18,48 @@
 // union at 128x128 granularity, :438-475).
 //
 // Per tile T, TMEM columns [256T, 256T + 256): S [0, 128) fp32, P (128 bf16
-// probabilities per row, two per column) written over S's first 64 columns,
-// O [128, 128 + dh) fp32.
+// probabilities per row, two per column: keys [64h, 64h + 64) in columns
+// [64h, 64h + 32)) written over S, O [128, 128 + dh) fp32.
 //   S_T = Q_T K_c^T   (M 128, N 128, K dh; A = the swizzled query tile)
 //   O_T += P_T V_c    (M 128, N dh, K 128; A = P_T from TMEM, V MN-major)
-// One thread issues all MMAs, per chunk c in the order PV_0(c-1), S_0(c),
+// One warp issues all MMAs, per chunk c in the order PV_0(c-1), S_0(c),
 // PV_1(c-1), S_1(c): S_t(c) may overwrite P_t(c-1) because tcgen05.mma
 // operations of one thread execute in issue order, and the commit of S_t(c)
 // also tells tile t's softmax that PV_t(c-1) is complete (so O may be
-// rescaled then).  S_0(c) completes half a step before S_1(c), so each
-// tile's softmax runs while the tensor cores run the other tile's PV and S.
+// rescaled then).  S_0(c) completes half a step before S_1(c), so each tile's
+// softmax runs while the tensor cores run the other tile's PV and S.
 //
 // The query tile holds the RoPE'd queries for the window chunks and is
 // reloaded with the QKNorm'd ones before the tile's first NoPE chunk (issued
 // once its last window S is complete, so the load overlaps that chunk's
 // softmax).
 //
-// Roles (320 threads):
-//   warps 4T .. 4T+3  softmax / epilogue of tile T, one thread per row (TMEM
-//              lane): S row -> mask -> p = exp2(s*scale*log2e - M) -> P row
-//              (bf16, tcgen05.st) for the PV MMA, in four quarters of 32
-//              columns with the next quarter's TMEM load in flight;
-//              epilogue O/l -> out.  M is the row's QKNorm bound of the logits
-//              (|s| <= scale*|q|*|k|, |k| = sqrt(dh)*k_gain) when that bound
-//              is small enough that no p can flush to zero (kBoundedLog2): no
-//              running max, O never rescaled.  Otherwise M is the row's
-//              running max, raised lazily: when a chunk's max passes it by
-//              more than kRescaleLog2, the warp rescales its rows of O in
-//              TMEM (and l) before writing P.
-//   warp 8     one thread issues every tcgen05.mma (and the query reloads);
-//              the warp owns the TMEM allocation.
-//   warp 9     one thread issues the loads: the RoPE'd query tiles (TMA),
+// Roles (576 threads):
+//   warps 8T .. 8T+7  softmax / epilogue of tile T: row = TMEM lane, warps
+//              8T + 4h + q take lane quarter q and the chunk's 64-column half
+//              h: S -> mask -> p = exp2(s*scale*log2e - M) -> P (bf16,
+//              tcgen05.st) for the PV MMA, in pieces of 16 columns with the
+//              next piece's TMEM load in flight; epilogue O/l -> out, each
+//              warp its half of O's columns.  M is the row's QKNorm bound of
+//              the logits (|s| <= scale*|q|*|k|, |k| = sqrt(dh)*k_gain) when
+//              that bound is small enough that no p can flush to zero
+//              (kBoundedLog2): no running max, O never rescaled.  Otherwise M
+//              is the row's running max, raised lazily: when a chunk's max
+//              (over both halves, exchanged through shared memory) passes it
+//              by more than kRescaleLog2, the warps rescale their parts of O
+//              in TMEM (and l) before writing P.  Two warps per row group
+//              keep the MUFU units busy: one warp's exponentials alone are
+//              latency-bound.
+//   warp 16    one thread issues the loads: the RoPE'd query tiles (TMA),
 //              then K_c and V_c through a ring of 128-key slots, each half of
 //              a slot one 1-D bulk copy per 64-dim group from the pre-pass's
 //              chunk-tiled K / RoPE'd K / V copies (the 128-byte-swizzled
 //              image of a [64 keys x 64 dims] box), so the ring holds UMMA
 //              operands as a tiled TMA load would leave them, at the bulk
 //              engine's higher per-SM rate.
+//   warp 17    issues every tcgen05.mma (one elected lane; the loop runs on
+//              the whole warp so its operands stay warp-uniform) and the
+//              query reloads; it owns the TMEM allocation.
 // Every mbarrier wait is bounded; a timeout sets *err and drains.
 #include <climits>
 #include <cudaTypedefs.h>
@@ -67,13 +72,14 @@ namespace hba {
 
 using namespace sm100;
 
-constexpr int kTcThreads = 320;
+constexpr int kTcThreads = 576;
 constexpr int kTcBlock = 64;           // keys per routed block = per half chunk
 constexpr int kTcKeys = 128;           // keys per chunk (UMMA N of S, K of PV)
 constexpr int kTcMaxEntries = 1040;    // NoPE list capacity: the sink block + the routed union of a tile pair
 constexpr int kTcMaxChunks = 544;      // window chunks (<= 9 for W <= 1024) + NoPE chunks (<= 520)
-constexpr int kTcMma = 8;              // MMA warp (and TMEM owner)
-constexpr int kTcTma = 9;              // load warp
+constexpr int kTcSoftmaxWarps = 16;    // two warps per row group of a tile (one per 64-column half)
+constexpr int kTcTma = 16;             // load warp
+constexpr int kTcMma = 17;             // MMA warp (and TMEM owner)
 
 enum HalfType : uint32_t { kSink = 0, kWindow = 1, kRouted = 2, kPad = 3 };
 
@@ -94,6 +100,11 @@ struct TcSmem {
   uint64_t q_ready, qn_read[2], qc_ready[2], drain[2];
   uint64_t full[NSLOT], empty[NSLOT];
   uint64_t s_full[2], p_full[2], o_full[2];
+  // the two softmax warps of a row group (tile t, lane quarter): chunk maxima
+  // exchanged in the running-max mode (by chunk parity), and the row sums
+  uint64_t mx_bar[2][4][2], l_bar[2][4];
+  float mx_x[2][2][2][128];  // [tile][column half][chunk parity][row]
+  float l_x[2][2][128];      // [tile][column half][row]
   uint32_t tmem_base;
   int n_entries;
   int scan[3][kTcThreads / 32];
@@ -161,11 +172,16 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   if (tid == kTcTma * 32) {
     mbar_init(&sm.q_ready, 1);
     for (int t = 0; t < 2; ++t) {
-      mbar_init(&sm.qn_read[t], 128);
+      mbar_init(&sm.qn_read[t], 256);
+      for (int q = 0; q < 4; ++q) {
+        mbar_init(&sm.mx_bar[t][q][0], 64);
+        mbar_init(&sm.mx_bar[t][q][1], 64);
+        mbar_init(&sm.l_bar[t][q], 64);
+      }
       mbar_init(&sm.qc_ready[t], 1);
       mbar_init(&sm.drain[t], 1);
       mbar_init(&sm.s_full[t], 1);
-      mbar_init(&sm.p_full[t], 128);
+      mbar_init(&sm.p_full[t], 256);
       mbar_init(&sm.o_full[t], 1);
     }
     for (int s = 0; s < NSLOT; ++s) {
@@ -416,8 +432,9 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             const uint64_t vdesc = sdesc_sw128(smem_u32(sm.ring[iv % NSLOT]), SM::GBYTES, 1024);
             if (elect_one_sync()) {
 #pragma unroll
-              for (int kk = 0; kk < kTcKeys / 16; ++kk)  // K = 16 keys = 8 packed columns of P per MMA
-                umma_f16_ts(tt + 128, tt + kk * 8, vdesc + (uint64_t)(kk * 2048 >> 4), idesc_o,
+              // K = 16 keys = 8 packed columns of P per MMA; P of keys [64h, 64h + 64) in columns [64h, 64h + 32)
+              for (int kk = 0; kk < kTcKeys / 16; ++kk)
+                umma_f16_ts(tt + 128, tt + (kk >> 2) * 64 + (kk & 3) * 8, vdesc + (uint64_t)(kk * 2048 >> 4), idesc_o,
                             (np[t] > 0 || kk > 0) ? 1u : 0u);
             }
             __syncwarp();
@@ -476,17 +493,25 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       __syncwarp();
       wwait(&sm.drain[0], 0);
     }
-  } else if (warp < 8) {
-    // ---------------- softmax / epilogue of tile t, one thread per row ----------------
-    const int t = warp >> 2;
-    const int r = tid - 128 * t;
+  } else if (warp < kTcSoftmaxWarps) {
+    // ---------------- softmax / epilogue: tile t, row = TMEM lane, one 64-column half ----------------
+    // Two warps share each row group (the same TMEM lane quarter): warp
+    // half hc turns S columns [64hc, 64hc + 64) (the chunk's half hc) into P
+    // columns [64hc, 64hc + 32), which only it has read, and owns O columns
+    // [hc dh/2, (hc + 1) dh/2) in the epilogue.  The row's maximum (running-max
+    // mode) and its sum are combined through shared memory and an mbarrier of
+    // the pair (bounded waits, like every other).
+    const int t = warp >> 3;
+    const int hc = (warp >> 2) & 1;
+    const int lq = warp & 3;
+    const int r = lq * 32 + lane;
     const int qt = r / G, hh = r % G;
     const int i = i0 + t * QT + qt;          // position
     const int li = li0 + t * QT + qt;        // local query
     const bool row_ok = (r < QT * G) && (qt < nqt(t));
     const int hq = g * G + hh;
-    const uint32_t lane_off = (uint32_t)((warp & 3) * 32) << 16;
-    const uint32_t t_s = tmem + (uint32_t)(t * 256), t_o = t_s + 128;  // S (P over its first 64 columns), O
+    const uint32_t lane_off = (uint32_t)(lq * 32) << 16;
+    const uint32_t t_s = tmem + (uint32_t)(t * 256), t_o = t_s + 128;  // S (P in its columns [0,32) and [64,96)), O
     // the query tiles arrive by TMA; this row's logit bound from its (RoPE'd:
     // a rotation, same norm up to rounding) values
     float M2 = 0.f;
@@ -506,9 +531,9 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     mbar_arrive(&sm.qn_read[t]);  // the tile may be reloaded from here on
     // the row's reference maximum: its bound (fixed), or a running max that starts empty
     const bool bounded = M2 <= kBoundedLog2;
-    const bool warp_bounded = __all_sync(0xffffffffu, bounded);
+    const bool warp_bounded = __all_sync(0xffffffffu, bounded);  // the same in both warps of the pair
     float M = bounded ? M2 : neg_inf();
-    if (r == 0 && t == 0) stamp(2);
+    if (r == 0 && t == 0 && hc == 0) stamp(2);
     const float sl2 = p.scale * kLog2e;
     const int win_lo = max(geo.S, i - geo.W + 1);
     // this row's valid columns [lo, hi) of a half (hi <= lo: none)
@@ -525,17 +550,16 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         hi = ((((t == 0 ? x.m0 : x.m1)) >> qt) & 1u) ? kTcBlock : 0;  // a picked block is wholly before i - W + 1
       }
     };
-    // the row's sum of p over even and odd columns, one packed pair (the
-    // softmax is issue-bound, not MUFU-bound: sm_100's paired fp32 fma / add
-    // halve the instructions around the exponentials)
+    // this thread's sum of p over even and odd columns, one packed pair (sm_100's
+    // paired fp32 fma / add keep the instructions around the exponentials few)
     unsigned long long lsum = f2pack(0.f, 0.f);
-    // P of quarter qq (32 columns of S) -> TMEM columns [16 qq, 16 qq + 16), valid columns [lo, hi) of the quarter
-    auto quarter = [&](const float* s, int qq, int lo, int hi) {
-      uint32_t pk[16];
+    // P of piece pc of this half (16 columns of S) -> TMEM columns [64hc + 8pc, +8); valid columns [lo, hi)
+    auto piece = [&](const float* s, int pc, int lo, int hi) {
+      uint32_t pk[8];
       const unsigned long long sl2x2 = f2pack(sl2, sl2), nm2 = f2pack(-M, -M);
-      if (hi - lo == 32) {
+      if (hi - lo == 16) {
 #pragma unroll
-        for (int q = 0; q < 16; ++q) {
+        for (int q = 0; q < 8; ++q) {
           float x0, x1;
           f2unpack(ffma2(f2pack(s[2 * q], s[2 * q + 1]), sl2x2, nm2), x0, x1);
           const float p0 = ex2_approx(x0), p1 = ex2_approx(x1);
@@ -544,7 +568,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         }
       } else if (hi > lo) {
 #pragma unroll
-        for (int q = 0; q < 16; ++q) {
+        for (int q = 0; q < 8; ++q) {
           float x0, x1;
           f2unpack(ffma2(f2pack(s[2 * q], s[2 * q + 1]), sl2x2, nm2), x0, x1);
           float p0 = ex2_approx(x0), p1 = ex2_approx(x1);
@@ -555,54 +579,57 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         }
       } else {
 #pragma unroll
-        for (int q = 0; q < 16; ++q) pk[q] = 0u;
+        for (int q = 0; q < 8; ++q) pk[q] = 0u;
       }
-      tmem_st16_nowait(t_s + (uint32_t)(16 * qq) + lane_off, pk);
+      tmem_st8_nowait(t_s + (uint32_t)(64 * hc + 8 * pc) + lane_off, pk);
     };
     int j = 0;  // chunks this tile has processed
     uint32_t needw = 0u;
     for (int c = 0; ok && c < NCH; ++c) {
       if ((c & 3) == 0) needw = *reinterpret_cast<const uint32_t*>(&sm.cneed[c]);
       if (!((needw >> (8 * (c & 3) + t)) & 1u)) continue;
-      const Half x0 = half_of(c, 0), x1 = half_of(c, 1);
+      const Half x = half_of(c, hc);
       // a failed wait leaves the whole warp together (the TMEM accesses are warp-collective)
       if (!__all_sync(0xffffffffu, mbar_wait(&sm.s_full[t], j & 1, p.err))) {
         ok = false;
         break;
       }
       tc_fence_after();
-      int lo0, hi0, lo1, hi1;
-      row_range(x0, lo0, hi0);
-      row_range(x1, lo1, hi1);
+      int lo, hi;
+      row_range(x, lo, hi);
       if (!warp_bounded) {
-        // running max: this row's chunk max over its valid columns
+        // running max: the chunk max of the row's valid columns of this half, then of both halves
         float mx = neg_inf();
+        if (__any_sync(0xffffffffu, hi > lo)) {
+          float s[kTcBlock];
+          tmem_ld32(t_s + hc * 64 + lane_off, s);
+          tmem_ld32(t_s + hc * 64 + 32 + lane_off, s + 32);
+          tmem_ld_wait();
 #pragma unroll
-        for (int h = 0; h < 2; ++h) {
-          const int lo = h == 0 ? lo0 : lo1, hi = h == 0 ? hi0 : hi1;
-          if (__any_sync(0xffffffffu, hi > lo)) {
-            float s[kTcBlock];
-            tmem_ld32(t_s + h * 64 + lane_off, s);
-            tmem_ld32(t_s + h * 64 + 32 + lane_off, s + 32);
-            tmem_ld_wait();
-#pragma unroll
-            for (int col = 0; col < kTcBlock; ++col) mx = fmaxf(mx, (col >= lo && col < hi) ? s[col] : neg_inf());
-          }
+          for (int col = 0; col < kTcBlock; ++col) mx = fmaxf(mx, (col >= lo && col < hi) ? s[col] : neg_inf());
         }
+        sm.mx_x[t][hc][j & 1][r] = mx;
+        mbar_arrive(&sm.mx_bar[t][lq][j & 1]);
+        if (!__all_sync(0xffffffffu, mbar_wait(&sm.mx_bar[t][lq][j & 1], (j >> 1) & 1, p.err))) {
+          ok = false;
+          break;
+        }
+        mx = fmaxf(sm.mx_x[t][0][j & 1][r], sm.mx_x[t][1][j & 1][r]);
         const float mn = bounded ? M : fmaxf(M, mx * sl2);
         const bool need = mn > M + kRescaleLog2;  // -inf + 8 = -inf: the first valid value
         if (__any_sync(0xffffffffu, need)) {
           const float al = need ? (M == neg_inf() ? 0.f : ex2_approx(M - mn)) : 1.f;
           if (j >= 1) {
-            // O holds PV(0 .. j-1), complete: S(j) was issued after PV(j-1)
+            // O holds PV(0 .. j-1), complete: S(j) was issued after PV(j-1); this warp's half of O
 #pragma unroll
-            for (int cb = 0; cb < DH / 32; ++cb) {
+            for (int cb = 0; cb < DH / 64; ++cb) {
+              const uint32_t oc = t_o + (uint32_t)(hc * (DH / 2) + cb * 32) + lane_off;
               float o[32];
-              tmem_ld32(t_o + cb * 32 + lane_off, o);
+              tmem_ld32(oc, o);
               tmem_ld_wait();
 #pragma unroll
               for (int q = 0; q < 32; ++q) o[q] *= al;
-              tmem_st_row<32>(t_o + cb * 32 + lane_off, o);
+              tmem_st_row<32>(oc, o);
             }
           }
           if (need) {
@@ -611,48 +638,54 @@ __global__ void __launch_bounds__(kTcThreads, 1)
           }
         }
       }
-      // four quarters of 32 columns, the next one's TMEM load in flight while
-      // one is turned into P; P of quarter qq overwrites S columns [16qq,
-      // 16qq + 16), read by then
+      // four pieces of 16 columns, the next one's TMEM load in flight while one is turned into P
       {
-        float sa[32], sb[32];
-        tmem_ld32(t_s + lane_off, sa);
+        const uint32_t sc = t_s + (uint32_t)(hc * 64) + lane_off;
+        float sa[16], sb[16];
+        tmem_ld16(sc, sa);
         tmem_ld_wait();
-        tmem_ld32(t_s + 32 + lane_off, sb);
-        quarter(sa, 0, lo0, min(hi0, 32));
+        tmem_ld16(sc + 16, sb);
+        piece(sa, 0, lo, min(hi, 16));
         tmem_ld_wait();
-        tmem_ld32(t_s + 64 + lane_off, sa);
-        quarter(sb, 1, max(lo0 - 32, 0), hi0 - 32);
+        tmem_ld16(sc + 32, sa);
+        piece(sb, 1, max(lo - 16, 0), min(hi, 32) - 16);
         tmem_ld_wait();
-        tmem_ld32(t_s + 96 + lane_off, sb);
-        quarter(sa, 2, lo1, min(hi1, 32));
+        tmem_ld16(sc + 48, sb);
+        piece(sa, 2, max(lo - 32, 0), min(hi, 48) - 32);
         tmem_ld_wait();
-        quarter(sb, 3, max(lo1 - 32, 0), hi1 - 32);
+        piece(sb, 3, max(lo - 48, 0), hi - 48);
       }
       tmem_st_wait();
       tc_fence_before();
       mbar_arrive(&sm.p_full[t]);
       ++j;
     }
-    float l0, l1;
-    f2unpack(lsum, l0, l1);
-    const float l = l0 + l1;
-    if (r == 0 && t == 0) stamp(14);
+    if (r == 0 && t == 0 && hc == 0) stamp(14);
+    // the row's sum over both halves (in the same order in both warps)
+    {
+      float a0, a1;
+      f2unpack(lsum, a0, a1);
+      sm.l_x[t][hc][r] = a0 + a1;
+      mbar_arrive(&sm.l_bar[t][lq]);
+      ok = __all_sync(0xffffffffu, mbar_wait(&sm.l_bar[t][lq], 0, p.err)) && ok;
+    }
+    const float l = sm.l_x[t][0][r] + sm.l_x[t][1][r];
     if (__all_sync(0xffffffffu, ok && (j == 0 || mbar_wait(&sm.o_full[t], 0, p.err)))) {
       tc_fence_after();
       const float inv = l > 0.f ? 1.f / l : 0.f;
 #pragma unroll
-      for (int cb = 0; cb < DH / 32; ++cb) {
+      for (int cb = 0; cb < DH / 64; ++cb) {
+        const int col0 = hc * (DH / 2) + cb * 32;
         float o[32];
         if (j > 0) {
-          tmem_ld32(t_o + cb * 32 + lane_off, o);
+          tmem_ld32(t_o + (uint32_t)col0 + lane_off, o);
           tmem_ld_wait();
         } else {
 #pragma unroll
           for (int q = 0; q < 32; ++q) o[q] = 0.f;
         }
         if (row_ok) {
-          uint4* dst = reinterpret_cast<uint4*>(p.out + (((size_t)b * nql + li) * geo.Hq + hq) * DH + cb * 32);
+          uint4* dst = reinterpret_cast<uint4*>(p.out + (((size_t)b * nql + li) * geo.Hq + hq) * DH + col0);
 #pragma unroll
           for (int q4 = 0; q4 < 4; ++q4)
             dst[q4] = make_uint4(pack_bf16x2(o[q4 * 8 + 0] * inv, o[q4 * 8 + 1] * inv),
@@ -661,7 +694,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                                  pack_bf16x2(o[q4 * 8 + 6] * inv, o[q4 * 8 + 7] * inv));
         }
       }
-      if (row_ok && p.lse != nullptr)
+      if (row_ok && hc == 0 && p.lse != nullptr)
         p.lse[((size_t)b * geo.Hq + hq) * nql + li] = l > 0.f ? (M + log2f(l)) * 0.6931471805599453f : neg_inf();
     }
   }
