@@ -86,8 +86,14 @@ HBA_DEVICE unsigned long long ld_relaxed_sys(const unsigned long long* p) {
   asm volatile("ld.relaxed.sys.global.u64 %0, [%1];\n" : "=l"(v) : "l"(p) : "memory");
   return v;
 }
+// Limit of a wait on another rank's words: ranks may arrive at a step apart
+// by host-side work (a first launch that loads its module, the interpreter),
+// so this limit is longer than the in-CTA one; still bounded.
+constexpr unsigned long long kPeerWaitNs = 2000ull * 1000 * 1000;  // 2 s
+
 // Bounded wait for N self-validating words p[i * stride] (i < N), loaded
-// together and re-polled while any lacks the tag; w[i] = the words.
+// together and re-polled while any lacks the tag; w[i] = the words.  Once
+// *err is set (an earlier wait of this launch expired) it does not wait again.
 template <int N>
 HBA_DEVICE void wait_tagged_n(const unsigned long long* p, size_t stride, int n, int shift,
                               unsigned long long mask, unsigned long long tag, unsigned long long (&w)[N], int* err) {
@@ -98,6 +104,7 @@ HBA_DEVICE void wait_tagged_n(const unsigned long long* p, size_t stride, int n,
   for (int i = 0; i < N; ++i)
     if (i < n) all = all && ((w[i] >> shift) & mask) == tag;
   if (all) return;
+  if (err != nullptr && *reinterpret_cast<volatile int*>(err) != 0) return;
   const unsigned long long t0 = global_ns();
   for (uint32_t k = 1;; ++k) {
     __nanosleep(32);
@@ -110,7 +117,10 @@ HBA_DEVICE void wait_tagged_n(const unsigned long long* p, size_t stride, int n,
       }
     }
     if (all) return;
-    if ((k & 15) == 0 && global_ns() - t0 > kWaitNs) break;
+    if ((k & 15) == 0) {
+      if (global_ns() - t0 > kPeerWaitNs) break;
+      if (err != nullptr && *reinterpret_cast<volatile int*>(err) != 0) return;
+    }
   }
   if (err != nullptr) atomicExch(err, 1);
 }

@@ -113,6 +113,15 @@ def test_shard_fused_trained_gains(tmp_path, hier, n, world):
     _check(tmp_path, hier, n, world, "trained")
 
 
+@pytest.mark.parametrize("world", [2, 4])
+@pytest.mark.parametrize("hier", [False, True])
+def test_shard_fused_empty_ranks(tmp_path, hier, world):
+    # the context ends where a rank's range begins: the later ranks own no
+    # token (no window, no candidate) until the append gives the first of
+    # them one; they still take part in every exchange
+    _check(tmp_path, hier, CAP // 2, world, True)
+
+
 def _check(tmp_path, hier, n, world, gains):
     if not torch.cuda.is_available() or torch.cuda.device_count() < world:
         pytest.skip(f"needs {world} GPUs")

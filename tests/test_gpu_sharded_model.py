@@ -70,8 +70,8 @@ def _port():
         return s.getsockname()[1]
 
 
-def test_sharded_model_matches_one_gpu(tmp_path):
-    world = 2
+@pytest.mark.parametrize("world", [2, 4])
+def test_sharded_model_matches_one_gpu(tmp_path, world):
     if not torch.cuda.is_available() or torch.cuda.device_count() < world:
         pytest.skip(f"needs {world} GPUs")
     mp.spawn(_rank, args=(world, _port(), str(tmp_path)), nprocs=world, join=True)

@@ -2,9 +2,9 @@
 
 One GPU runs the fused sharded decode kernel as rank 0 of a world of 2 whose
 rank 1 never launches: rank 1's slots in rank 0's exchange buffer stay zero,
-so every wait on them (the list exchange, the partial exchange) gives up
-after the kernels' limit (200 ms of the global timer each), sets the status
-word to 1, and the kernel returns.  The host reads HBA_B200_ERR_DEVICE_TIMEOUT
+so the first wait on them (the list exchange) gives up after the kernels'
+limit for waits on another rank (2 s of the global timer), sets the status
+word to 1, and the launch waits no more: the kernel returns.  The host reads HBA_B200_ERR_DEVICE_TIMEOUT
 through hba_b200_device_status, and the context stays usable: a normal decode
 afterwards gives the oracle's result.  No kernel waits on another launch: the
 flag the wait polls is simply never written."""
@@ -56,7 +56,7 @@ def test_missing_peer_expires_into_device_timeout_status():
     elapsed = time.time() - t0
     assert dst == _lib.ERR_DEVICE_TIMEOUT, _lib.status_string(dst)
     assert int(status.item()) == 1
-    assert elapsed < 60, elapsed              # bounded: a few 200 ms waits per CTA, not a hang
+    assert elapsed < 30, elapsed              # bounded: one expired 2 s wait, not a hang
     # the clear flag zeroes the word; the context is still usable
     assert L.hba_b200_device_status(ptr(status), 1, stream_of(loc.device)) == _lib.ERR_DEVICE_TIMEOUT
     assert L.hba_b200_device_status(ptr(status), 0, stream_of(loc.device)) == _lib.OK
