@@ -1,6 +1,8 @@
 // QKNorm (per-head RMS normalisation with a scalar gain) and the KV-cache
 // append.  Both are memory-bound elementwise passes: one warp per (row, head),
 // 16-byte vector loads, fp32 math.
+#include <cstdint>
+
 #include "hba_common.cuh"
 #include "hba_internal.h"
 
@@ -169,6 +171,11 @@ __global__ void __launch_bounds__(256) qknorm_rope_kernel(Geom geo, int n, const
   const int64_t total = (int64_t)geo.B * n * geo.Hkv;
   const int64_t w0 = ((int64_t)blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32) * kQkRows;
   if (w0 >= total) return;
+  // row w = (b * n + token) * Hkv + head: one division per warp (the host
+  // keeps B * n * Hkv below 2^31), then the kQkRows rows by increments
+  const int H = geo.Hkv;
+  int bt = (int)w0 / H;      // b * n + token of the first row
+  int g0 = (int)w0 - bt * H;  // its head
   float x[kQkRows][PER], vv[kQkRows][PER];
 #pragma unroll
   for (int r = 0; r < kQkRows; ++r)
@@ -179,12 +186,20 @@ __global__ void __launch_bounds__(256) qknorm_rope_kernel(Geom geo, int n, const
     for (int r = 0; r < kQkRows; ++r)
       if (w0 + r < total) load_head_row<DH>(v + (w0 + r) * DH, vv[r]);
   }
+  int b_ = bt / n, tok = bt - b_ * n;
 #pragma unroll
   for (int r = 0; r < kQkRows; ++r) {
     const int64_t w = w0 + r;
     if (w >= total) break;  // warp-uniform
-    const int g = (int)(w % geo.Hkv);
-    const int p = pos0 + (int)((w / geo.Hkv) % n);  // the row's position (RoPE tables row)
+    if (r > 0 && ++g0 == H) {  // next row: next head, or the next token's head 0
+      g0 = 0;
+      if (++tok == n) {
+        tok = 0;
+        ++b_;
+      }
+    }
+    const int g = g0;
+    const int p = pos0 + tok;  // the row's position (RoPE tables row)
     float rr[PER];
     if (geo.qknorm) qknorm_lane<DH>(x[r], k_gain[g], geo.eps);
     store_head_row<DH>(kc + w * DH, x[r]);
@@ -193,8 +208,7 @@ __global__ void __launch_bounds__(256) qknorm_rope_kernel(Geom geo, int n, const
       store_head_row<DH>(kr + w * DH, rr);
       continue;
     }
-    const int b = (int)(w / ((int64_t)geo.Hkv * n));
-    const size_t row_base = ((size_t)b * geo.Hkv + g) * (size_t)n * DH;  // n % 64 == 0, pos0 == 0
+    const size_t row_base = ((size_t)b_ * geo.Hkv + g) * (size_t)n * DH;  // n % 64 == 0, pos0 == 0
     store_chunked<DH>(kc_sw, row_base, p, x[r]);
     store_chunked<DH>(kr_sw, row_base, p, rr);
     if (v != nullptr) store_chunked<DH>(v_sw, row_base, p, vv[r]);
@@ -238,6 +252,7 @@ cudaError_t launch_qknorm_rope(const Geom& geo, int n, const __nv_bfloat16* k, c
   if (blocks == 0) return cudaSuccess;
   if (kc_sw != nullptr && (n % 64 != 0 || pos0 != 0 || kr_sw == nullptr || (v != nullptr && v_sw == nullptr)))
     return cudaErrorInvalidValue;
+  if ((int64_t)geo.B * n * geo.Hkv + kQkRows >= (int64_t)INT32_MAX) return cudaErrorInvalidValue;  // 32-bit row math
   if (dh == 64)
     qknorm_rope_kernel<64><<<(unsigned)blocks, 256, 0, st>>>(geo, n, k, k_gain, cos, sin, kc, kr, v, kc_sw, kr_sw,
                                                               v_sw, pos0);
