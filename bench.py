@@ -473,8 +473,8 @@ def cpu_decode_sample(cache, q, cfg, hier, n, seqs=2):
     nb = n // cfg.block
     data = []
     for b in range(seqs):
-        kc = cache.k[b:b + 1, :n].float().cpu().numpy()
-        v = cache.v[b:b + 1, :n].float().cpu().numpy()
+        kc = cache.tokens("k")[b:b + 1, :n].float().cpu().numpy()
+        v = cache.tokens("v")[b:b + 1, :n].float().cpu().numpy()
         S0 = cache.summaries[b:b + 1, :, :nb].float().cpu().numpy()
         S1 = cache.supers[b:b + 1, :, :-(-nb // cfg.fanout)].float().cpu().numpy() if hier else None
         data.append((kc, v, S0, S1))

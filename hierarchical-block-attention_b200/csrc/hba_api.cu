@@ -354,10 +354,10 @@ int hba_b200_append_kv(const hba_b200_config* cfg, int32_t batch, int32_t n_cap,
                        void* summaries, void* supers, cudaStream_t stream) {
   int st = HBA_B200_OK;
   if (!config_ok(cfg, &st)) return st;
-  if (batch <= 0 || n_cap <= 0 || t <= 0 || pos == nullptr || k_new == nullptr || v_new == nullptr ||
-      k_cache == nullptr || k_rope_cache == nullptr || v_cache == nullptr || cos == nullptr || sin == nullptr ||
-      (cfg->qknorm && k_gain == nullptr))
-    return HBA_B200_ERR_INVALID_ARGUMENT;
+  if (batch <= 0 || n_cap <= 0 || n_cap % 64 != 0 || t <= 0 || pos == nullptr || k_new == nullptr ||
+      v_new == nullptr || k_cache == nullptr || k_rope_cache == nullptr || v_cache == nullptr || cos == nullptr ||
+      sin == nullptr || (cfg->qknorm && k_gain == nullptr))
+    return HBA_B200_ERR_INVALID_ARGUMENT;  // the chunk-tiled cache holds whole 64-token blocks
   if (summaries != nullptr && (probes == nullptr || proj == nullptr)) return HBA_B200_ERR_INVALID_ARGUMENT;
   Geom geo = make_geom(cfg, batch, 1, n_cap);
   const int dh = cfg->head_dim;
@@ -368,7 +368,7 @@ int hba_b200_append_kv(const hba_b200_config* cfg, int32_t batch, int32_t n_cap,
   if (e != cudaSuccess) return cuda_status(e);
   if (summaries != nullptr) {
     e = hba::launch_summarize(geo, dh, static_cast<const __nv_bfloat16*>(k_cache), probes, proj,
-                              static_cast<__nv_bfloat16*>(summaries), 0, 0, pos, t, stream);
+                              static_cast<__nv_bfloat16*>(summaries), 0, 0, pos, t, stream, /*tiled=*/true);
     if (e != cudaSuccess) return cuda_status(e);
     if (supers != nullptr && cfg->hier) {
       e = hba::launch_supers(geo, dh, 0, static_cast<const __nv_bfloat16*>(summaries),
@@ -401,7 +401,7 @@ int hba_b200_decode(const hba_b200_config* cfg, int32_t batch, int32_t n_cap, co
       (cfg->hier && supers == nullptr) ||
       ((sel_idx == nullptr) != (sel_score == nullptr)))
     return HBA_B200_ERR_INVALID_ARGUMENT;
-  if (n_cap % cfg->block != 0) return HBA_B200_ERR_NOT_BLOCK_MULTIPLE;
+  if (n_cap % cfg->block != 0 || n_cap % 64 != 0) return HBA_B200_ERR_NOT_BLOCK_MULTIPLE;  // whole cache tiles
   const size_t need = hba_b200_decode_workspace_size(cfg, batch, n_cap);
   if (workspace == nullptr || workspace_bytes < need) return HBA_B200_ERR_WORKSPACE;
   Geom geo = make_geom(cfg, batch, 1, n_cap);
@@ -748,7 +748,8 @@ int hba_b200_decode_shard_attend(const hba_b200_config* cfg, int32_t batch, int3
       part_o == nullptr || part_l == nullptr || part_m2 == nullptr || dev_status == nullptr ||
       ((sel_idx == nullptr) != (sel_score == nullptr)))
     return HBA_B200_ERR_INVALID_ARGUMENT;
-  if (n_cap_local % cfg->block != 0 || tok_lo % cfg->block != 0) return HBA_B200_ERR_NOT_BLOCK_MULTIPLE;
+  if (n_cap_local % cfg->block != 0 || tok_lo % cfg->block != 0 || n_cap_local % 64 != 0 || tok_lo % 64 != 0)
+    return HBA_B200_ERR_NOT_BLOCK_MULTIPLE;
   if (tok_lo > 0 && tok_lo < cfg->sinks) return HBA_B200_ERR_UNSUPPORTED;  // the sinks live on one shard
   Geom geo = make_geom(cfg, batch, 1, n_cap_local);
   if (!hba::decode_tc_supported(geo, cfg->head_dim, k_cache, k_rope_cache, v_cache, nullptr, nullptr))
@@ -846,7 +847,8 @@ int hba_b200_decode_shard_fused(const hba_b200_config* cfg, int32_t batch, int32
   for (int r = 0; r < world; ++r)
     if (xbufs[r] == nullptr) return HBA_B200_ERR_INVALID_ARGUMENT;
   const int unit = cfg->block * (cfg->hier ? cfg->fanout : 1);  // no block (super) straddles two ranks
-  if (n_cap_local % unit != 0 || tok_lo % unit != 0) return HBA_B200_ERR_NOT_BLOCK_MULTIPLE;
+  if (n_cap_local % unit != 0 || tok_lo % unit != 0 || n_cap_local % 64 != 0 || tok_lo % 64 != 0)
+    return HBA_B200_ERR_NOT_BLOCK_MULTIPLE;
   if (tok_lo > 0 && tok_lo < cfg->sinks) return HBA_B200_ERR_UNSUPPORTED;  // the sinks live on one shard
   if ((int64_t)world * n_cap_local / cfg->block >= 0xffff) return HBA_B200_ERR_UNSUPPORTED;  // 16-bit block ids
   Geom geo = make_geom(cfg, batch, 1, n_cap_local);

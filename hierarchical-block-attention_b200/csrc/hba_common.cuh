@@ -19,6 +19,23 @@ HBA_DEVICE float bf2f(__nv_bfloat16 x) { return __bfloat162float(x); }
 HBA_DEVICE __nv_bfloat16 f2bf(float x) { return __float2bfloat16_rn(x); }
 HBA_DEVICE float round_bf16(float x) { return __bfloat162float(__float2bfloat16_rn(x)); }
 
+// Element offset of (token t, dim d) of one (sequence, kv head) in the
+// chunk-tiled layout [n/64][dh/64][64 tokens x 64 dims]: per 64-token block
+// and 64-dim group the 8 KB image a 128-byte-swizzled TMA box leaves in
+// shared memory (the 16-byte unit u of row r sits at unit u ^ (r & 7)), so
+// one 1-D bulk copy of a block's group lands as a UMMA operand.  head_base =
+// the (sequence, head)'s first element; the 8 elements of a 16-byte unit
+// (d % 8 == 0 .. 7) stay contiguous.  The KV cache (K, RoPE'd K, V) and the
+// prefill's chunk-tiled copies use it.
+template <int DH>
+HBA_DEVICE size_t tiled_offset(size_t head_base, int t, int d) {
+  constexpr int GROUPS = DH / 64;
+  const int r = t & 63;
+  const int c = d & 63;
+  const uint32_t off = (uint32_t)(r * 64 + ((((c >> 3) ^ (r & 7))) << 3) + (c & 7));
+  return head_base + ((size_t)(t >> 6) * GROUPS + (d >> 6)) * 4096 + off;
+}
+
 // One element of RoPE, y = x*cos + rot*sin (rot = the rot_half partner, sign
 // included), with every rounding fixed: rn(rn(x*cos) + rn(rot*sin)), no fused
 // multiply-add.  x and rot are bf16 values and every caller rounds y to bf16

@@ -72,7 +72,6 @@ __global__ void __launch_bounds__(kDThreads) decode_attend_kernel(DecodeAttnPara
   const long long T = (long long)geo.B * geo.Hkv * p.nchunk;
   const long long g0 = T * blockIdx.x / N, g1 = T * (blockIdx.x + 1) / N;
   bool waited = false;
-  const size_t tok_stride = (size_t)geo.Hkv * DH;
 
   for (long long gc = g0; gc < g1;) {
     const int bg = (int)(gc / p.nchunk);
@@ -92,7 +91,7 @@ __global__ void __launch_bounds__(kDThreads) decode_attend_kernel(DecodeAttnPara
     const int w0 = max(geo.S, pos - geo.W + 1);
     const int nw = ok ? max(0, pos - w0 + 1) : 0;
     const int nsink = ok ? min(geo.S, pos + 1) : 0;
-    const size_t head_base = ((size_t)b * geo.n_cap) * tok_stride + (size_t)g * DH;
+    const size_t head_base = ((size_t)b * geo.Hkv + g) * (size_t)geo.n_cap * DH;  // the chunk-tiled cache
     const __nv_bfloat16* kbase = p.k + head_base;
     const __nv_bfloat16* krbase = p.kr + head_base;
     const __nv_bfloat16* vbase = p.v + head_base;
@@ -154,7 +153,7 @@ __global__ void __launch_bounds__(kDThreads) decode_attend_kernel(DecodeAttnPara
         for (int e = tid; e < kDChunk * PIECES; e += kDThreads) {
           const int r = e / PIECES, pc = e % PIECES;
           const bool valid = r < cnt;
-          const size_t off = (size_t)(valid ? row_token(c, r) : 0) * tok_stride + pc * 8;
+          const size_t off = tiled_offset<DH>(0, valid ? row_token(c, r) : 0, pc * 8);
           cp_async16_zfill(&sm.k[stage][r][pc * 8], ksrc + off, valid);
           cp_async16_zfill(&sm.v[stage][r][pc * 8], vbase + off, valid);
         }

@@ -112,8 +112,7 @@ __global__ void __launch_bounds__(kFThreads, 1) decode_fused_kernel(DecodeAttnPa
   const int w0 = max(geo.S, pos - geo.W + 1);
   const int nw = ok ? max(0, pos - w0 + 1) : 0;
   const int nsink = ok ? min(geo.S, pos + 1) : 0;
-  const size_t tok_stride = (size_t)geo.Hkv * DH;
-  const size_t head_base = ((size_t)b * geo.n_cap) * tok_stride + (size_t)g * DH;
+  const size_t head_base = ((size_t)b * geo.Hkv + g) * (size_t)geo.n_cap * DH;  // the chunk-tiled cache
   const __nv_bfloat16* kbase = p.k + head_base;
   const __nv_bfloat16* krbase = p.kr + head_base;
   const __nv_bfloat16* vbase = p.v + head_base;
@@ -198,7 +197,7 @@ __global__ void __launch_bounds__(kFThreads, 1) decode_fused_kernel(DecodeAttnPa
             tok = sm.blocks[key / geo.Bk] * geo.Bk + key % geo.Bk;
           }
         }
-        const size_t off = (size_t)tok * tok_stride + pc * 8;
+        const size_t off = tiled_offset<DH>(0, tok, pc * 8);
         cp_async16_zfill(st + swz<DH>(r, pc), ksrc + off, valid);
         cp_async16_zfill(st + kFChunk * DH * 2 + swz<DH>(r, pc), vbase + off, valid);
       }

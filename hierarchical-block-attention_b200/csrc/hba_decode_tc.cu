@@ -61,8 +61,9 @@ HBA_DEVICE void score_bar() { asm volatile("bar.sync 2, 224;\n" ::: "memory"); }
 // [window | sinks | routed block pairs] its K tile and its V tile.  Thread 0
 // keeps the ring full from the first instruction on, so the window tiles
 // load while the pages are scored and the top-k runs.  A page slot is freed
-// once all warps have scored it, a K slot when its S MMA completes, a V slot
-// when its PV MMA completes.
+// once all warps have scored it, a K slot when the softmax has seen its S MMA
+// complete (an arrival, not another commit for the MMA thread to issue), a V
+// slot when its PV MMA completes.
 template <int DH>
 struct DtcSmem {
   static constexpr int HALVES = DH / 64;
@@ -94,6 +95,7 @@ struct DtcSmem {
   int n_children;
   uint64_t full[NSLOT], empty[NSLOT];
   uint64_t s_full[2], p_full[2], p_free[2], cm_full[2];
+  uint64_t s_free[2];  // the 4 softmax warps have read S buffer [b] (flat: the S issuer may reuse it)
   uint64_t o_full, drain, child_ready, sel_ready, lists_ready;
   uint32_t tmem_base;
   int issued;  // ring items the producer has issued (published after each)
@@ -136,8 +138,7 @@ struct DecodeTcParams {
 
 template <int DH, int HB>
 __global__ void __launch_bounds__(kDtThreads, 1)
-    decode_tc_kernel(const __grid_constant__ CUtensorMap tm_kc, const __grid_constant__ CUtensorMap tm_kr,
-                     const __grid_constant__ CUtensorMap tm_v, DecodeTcParams P) {
+    decode_tc_kernel(DecodeTcParams P) {
   using SM = DtcSmem<DH>;
   constexpr int HALVES = SM::HALVES;
   constexpr int NSLOT = SM::NSLOT;
@@ -180,8 +181,10 @@ __global__ void __launch_bounds__(kDtThreads, 1)
   const int wlo = max(max(geo.S, pos - geo.W + 1), tok_lo);
   const int whi = min(pos, tok_hi - 1);
   const int nw = ok ? max(0, whi - wlo + 1) : 0;
+  // window chunks start on a 64-token block (the cache's tile): [wla, whi], keys before wlo masked
+  const int wla = wlo & ~63;
   const int nsink = (ok && tok_lo == 0) ? min(geo.S, pos + 1) : 0;
-  const int NCw = (nw + kDtKeys - 1) / kDtKeys;
+  const int NCw = nw > 0 ? (whi - wla) / kDtKeys + 1 : 0;
   const int NCs = nsink > 0 ? 1 : 0;
   const bool producer = warp == kDtProducer;
   const int sw = warp < kDtProducer ? warp : warp - 1;  // scoring-warp index (producer excluded)
@@ -215,6 +218,11 @@ __global__ void __launch_bounds__(kDtThreads, 1)
   const int row_bytes = row_elems * 2;
   const int PB = SM::KT / row_bytes;  // summary rows per page
   const __nv_bfloat16* summ_bg = P.summ + (size_t)bg * geo.nb_cap * row_elems;
+  // this (sequence, kv head)'s chunk-tiled K, RoPE'd K and V: [n_cap/64][dh/64][64 x 64]
+  const size_t kv_head = (size_t)bg * geo.n_cap * DH;
+  const __nv_bfloat16* k_bg = p.k + kv_head;
+  const __nv_bfloat16* kr_bg = p.kr + kv_head;
+  const __nv_bfloat16* v_bg = p.v + kv_head;
   const __nv_bfloat16* sup_bg = hier ? P.supers + (size_t)bg * geo.ns_cap * row_elems : nullptr;
   // phase-A candidates, ids id0 .. id0 + Ra - 1: flat blocks 1..bmax, or
   // supers ida..bmax/F, of them the owned ones (blocks [blo, bhi), supers
@@ -254,6 +262,7 @@ __global__ void __launch_bounds__(kDtThreads, 1)
       mbar_init(&sm.p_full[s], 128);
       mbar_init(&sm.p_free[s], 1);
       mbar_init(&sm.cm_full[s], 4);  // one arrival per softmax warp
+      mbar_init(&sm.s_free[s], 4);
     }
     mbar_init(&sm.o_full, 1);
     mbar_init(&sm.drain, 1);
@@ -293,9 +302,6 @@ __global__ void __launch_bounds__(kDtThreads, 1)
   if (producer) {
     // ---- ring producer: the items in the order described at item_of_chunk ----
     if (lane == 0) {
-      prefetch_tmap(&tm_kc);
-      prefetch_tmap(&tm_kr);
-      prefetch_tmap(&tm_v);
       int NPb = 0, R2 = 0, nsel = 0, issued = 0;
       auto issue_item = [&](int i) {
         unsigned char* dst = sm.ring[i % NSLOT];
@@ -318,27 +324,30 @@ __global__ void __launch_bounds__(kDtThreads, 1)
         } else {
           const int e = i < cp0 ? i - NPa : i - NPb - NPa;  // 2 * chunk + (V ? 1 : 0)
           const int c = e >> 1, is_v = e & 1;
-          int kind, t0, t1;
+          // the chunk's two 64-token blocks (local); a half past the keys
+          // loads a valid block again, its keys masked
+          int kind, b0, b1;
           if (c < NCw) {
             kind = 0;
-            t0 = wlo - tok_lo + c * kDtKeys;  // local row
-            t1 = t0 + 64;
+            b0 = (wla - tok_lo + c * kDtKeys) >> 6;
+            b1 = min(b0 + 1, geo.n_cap / 64 - 1);
           } else if (c < NCw + NCs) {
             kind = 1;
-            t0 = 0;
-            t1 = geo.n_cap;  // past the cache: TMA fills the unused half with zeros, no traffic
+            b0 = b1 = 0;
           } else {
             kind = 2;
             const int q = (c - NCw - NCs) * 2;
-            t0 = sm.sel_i[q] * 64;
-            t1 = (q + 1 < nsel ? sm.sel_i[q + 1] : sm.sel_i[q]) * 64;  // odd count: a valid block, masked
+            b0 = sm.sel_i[q];
+            b1 = q + 1 < nsel ? sm.sel_i[q + 1] : b0;  // odd count: a valid block, masked
           }
           mbar_arrive_expect_tx(fb, SM::KT);
-          const CUtensorMap* m = is_v ? &tm_v : (kind == 0 ? &tm_kr : &tm_kc);
+          const __nv_bfloat16* src = is_v ? v_bg : (kind == 0 ? kr_bg : k_bg);
+          // per 64-dim group one 8 KB tile per block: rows [0, 64) of the
+          // slot's group from b0, rows [64, 128) from b1
 #pragma unroll
           for (int h = 0; h < HALVES; ++h) {
-            tma_load_4d(dst + h * (kDtKeys * 128), m, h * 64, g, t0, b, fb);
-            tma_load_4d(dst + h * (kDtKeys * 128) + 64 * 128, m, h * 64, g, t1, b, fb);
+            bulk_load(dst + h * (kDtKeys * 128), src + ((size_t)b0 * HALVES + h) * 4096, 8192, fb);
+            bulk_load(dst + h * (kDtKeys * 128) + 64 * 128, src + ((size_t)b1 * HALVES + h) * 4096, 8192, fb);
           }
         }
       };
@@ -819,75 +828,113 @@ __global__ void __launch_bounds__(kDtThreads, 1)
     stamp(2);
 
     // ---- B. union softmax ----
-    if (warp == 1) {
-      if (lane == 0) {
+    if (warp == 1 || (warp == 2 && !hier)) {
+      // MMA issue.  Flat selection: warp 2 (free once the lists are merged)
+      // issues the S MMAs, up to both S buffers ahead, and warp 1 the PV MMAs,
+      // so each warp's waits overlap the other's issue (the tensor pipe takes
+      // one of these small MMAs every ~22 ns; the waits and bookkeeping around
+      // them were most of a chunk's time).  Hierarchical selection keeps warps
+      // 0 and 2 busy: warp 1 issues both, S(c) before PV(c-1).  Each loop runs
+      // on the whole warp (warp-uniform descriptors and waits); one elected
+      // lane issues each tcgen05 op.
+      const bool do_s = warp == 2 || hier, do_pv = warp == 1;
+      {
         constexpr uint32_t idesc_s = idesc_bf16(128, 16, false, false);
         constexpr uint32_t idesc_o = idesc_bf16(128, 16, true, false);
+        auto wwait = [&](uint64_t* bar, uint32_t parity) {
+          return __all_sync(0xffffffffu, mbar_wait(bar, parity, P.err));
+        };
+        auto wfull = [&](int i) { return __all_sync(0xffffffffu, wait_full(i)); };
         bool okw = true;
         int npb = 0;  // child pages ahead of chunk WA (hier: known at child_ready)
+        // dh 64: M = 128 reads a second MN group at LBO 0 (rows 64-127 of O^T duplicate 0-63, unused)
+        constexpr uint32_t lbo = DH == 128 ? kDtKeys * 128 : 0;
+        const uint64_t pdesc0 = sdesc_sw128(smem_u32(sm.pt[0][0]), 16, 1024);
+        const uint64_t pdesc1 = sdesc_sw128(smem_u32(sm.pt[1][0]), 16, 1024);
+        const uint64_t qc_desc = sdesc_sw128(smem_u32(sm.qc[0]), 16, 1024);
+        const uint64_t qr_desc = sdesc_sw128(smem_u32(sm.qr[0]), 16, 1024);
+        constexpr uint32_t qhalf = 16 * 128;  // bytes between the Q tiles' 64-dim halves
         auto pv = [&](int c) -> bool {
           const int sb = c & 1, iv = item_of_chunk(c, npb) + 1;
-          if (!mbar_wait(&sm.p_full[sb], (c >> 1) & 1, P.err)) return false;
-          if (!wait_full(iv)) return false;
+          if (!wwait(&sm.p_full[sb], (c >> 1) & 1) || !wfull(iv)) return false;
           tc_fence_after();
-          const uint32_t va = smem_u32(sm.ring[iv % NSLOT]);
-          const uint32_t pa = smem_u32(sm.pt[sb][0]);
-          // dh 64: M = 128 reads a second MN group at LBO 0 (rows 64-127 of O^T duplicate 0-63, unused)
-          const uint32_t lbo = DH == 128 ? kDtKeys * 128 : 0;
+          const uint64_t vdesc = sdesc_sw128(smem_u32(sm.ring[iv % NSLOT]), lbo, 1024);
+          if (elect_one_sync()) {
 #pragma unroll
-          for (int kk = 0; kk < kDtKeys / 16; ++kk)
-            umma_f16(tmem + 32, sdesc_sw128(va + kk * 2048, lbo, 1024),
-                     sdesc_sw128(pa + (kk >> 2) * 2048 + (kk & 3) * 32, 16, 1024), idesc_o,
-                     (c > 0 || kk > 0) ? 1u : 0u);
-          umma_commit(&sm.empty[iv % NSLOT]);
-          umma_commit(&sm.p_free[sb]);
+            for (int kk = 0; kk < kDtKeys / 16; ++kk)
+              umma_f16(tmem + 32, vdesc + (uint64_t)((kk * 2048) >> 4),
+                       (sb ? pdesc1 : pdesc0) + (uint64_t)(((kk >> 2) * 2048 + (kk & 3) * 32) >> 4), idesc_o,
+                       (c > 0 || kk > 0) ? 1u : 0u);
+            umma_commit(&sm.empty[iv % NSLOT]);  // the V tile is free once PV is done
+            umma_commit(&sm.p_free[sb]);
+          }
+          __syncwarp();
           return true;
         };
         int NC = NCk;
         bool picks_in = false;
         for (int c = 0; okw; ++c) {
           if (c == NC && !picks_in) {  // window and sinks issued: now the routed chunks
-            NC += routed_chunks();
+            NC += __shfl_sync(0xffffffffu, routed_chunks(), 0);
             picks_in = true;
           }
           if (c >= NC) break;
           if (hier && c == WA) {  // chunks from here on sit behind the child pages in the ring
-            if (!mbar_wait(&sm.child_ready, 0, P.err)) {
+            if (!wwait(&sm.child_ready, 0)) {
               okw = false;
               break;
             }
             npb = (sm.n_children + PB - 1) / PB;
           }
-          const int sb = c & 1, ik = item_of_chunk(c, npb);
-          if (!wait_full(ik)) {
-            okw = false;
-            break;
-          }
-          if (c == 0) stamp_any(8);
-          if (c == NCk - 1) stamp_any(9);
-          if (c == NCk) stamp_any(10);
-          tc_fence_after();
-          const bool window = c < NCw;
-          const uint32_t ka = smem_u32(sm.ring[ik % NSLOT]);
+          const int sb = c & 1;
+          if (do_s) {
+            const int ik = item_of_chunk(c, npb);
+            // flat: S buffer sb is free once the softmax has read S(c - 2)
+            if (!wfull(ik) || (!hier && c >= 2 && !wwait(&sm.s_free[sb], ((c - 2) >> 1) & 1))) {
+              okw = false;
+              break;
+            }
+            if (lane == 0) {
+              if (c == 0) stamp_any(8);
+              if (c == NCk - 1) stamp_any(9);
+              if (c == NCk) stamp_any(10);
+            }
+            tc_fence_after();
+            const uint64_t kdesc = sdesc_sw128(smem_u32(sm.ring[ik % NSLOT]), 16, 1024);
+            const uint64_t qdesc = c < NCw ? qr_desc : qc_desc;
+            if (elect_one_sync()) {
 #pragma unroll
-          for (int kk = 0; kk < DH / 16; ++kk) {
-            const int h = kk >> 2, ko = (kk & 3) * 32;
-            const uint32_t qa = smem_u32(window ? sm.qr[h] : sm.qc[h]);
-            umma_f16(tmem + sb * 16, sdesc_sw128(ka + h * (kDtKeys * 128) + ko, 16, 1024),
-                     sdesc_sw128(qa + ko, 16, 1024), idesc_s, kk > 0 ? 1u : 0u);
+              for (int kk = 0; kk < DH / 16; ++kk) {
+                const int h = kk >> 2, ko = (kk & 3) * 32;
+                umma_f16(tmem + sb * 16, kdesc + (uint64_t)((h * (kDtKeys * 128) + ko) >> 4),
+                         qdesc + (uint64_t)((h * qhalf + ko) >> 4), idesc_s, kk > 0 ? 1u : 0u);
+              }
+              umma_commit(&sm.s_full[sb]);  // the softmax frees the K slot once it has seen this
+            }
+            __syncwarp();
           }
-          umma_commit(&sm.s_full[sb]);
-          umma_commit(&sm.empty[ik % NSLOT]);  // K tile free once S is done
-          if (c >= 1 && !pv(c - 1)) {
-            okw = false;
-            break;
+          if (do_pv) {
+            if (hier) {
+              if (c >= 1 && !pv(c - 1)) {
+                okw = false;
+                break;
+              }
+            } else if (!pv(c)) {
+              okw = false;
+              break;
+            }
           }
         }
-        if (okw && NC >= 1) okw = pv(NC - 1);
-        stamp_any(11);
-        umma_commit(&sm.o_full);
-        umma_commit(&sm.drain);
-        mbar_wait(&sm.drain, 0, P.err);
+        if (do_pv) {
+          if (hier && okw && NC >= 1) okw = pv(NC - 1);
+          if (lane == 0) stamp_any(11);
+          if (elect_one_sync()) {
+            umma_commit(&sm.o_full);
+            umma_commit(&sm.drain);
+          }
+          __syncwarp();
+          wwait(&sm.drain, 0);
+        }
       }
     } else if (warp >= 4) {
       const int t = tid - 128;  // key row of the chunk / TMEM lane
@@ -911,12 +958,20 @@ __global__ void __launch_bounds__(kDtThreads, 1)
       bool okw = true;
       int NC = NCk;
       bool picks_in = false;
+      int npb_s = 0;  // child pages ahead of chunk WA (hier), for the ring items this warp releases
       for (int c = 0;; ++c) {
         if (c == NC && !picks_in) {
           NC += routed_chunks();
           picks_in = true;
         }
         if (c >= NC) break;
+        if (hier && c == WA) {
+          if (!__all_sync(0xffffffffu, mbar_wait(&sm.child_ready, 0, P.err))) {
+            okw = false;
+            break;
+          }
+          npb_s = (sm.n_children + PB - 1) / PB;
+        }
         const int sb = c & 1;
         // a failed wait leaves the whole warp together (the TMEM accesses below are warp-collective)
         if (!__all_sync(0xffffffffu, mbar_wait(&sm.s_full[sb], (c >> 1) & 1, P.err))) {
@@ -926,12 +981,20 @@ __global__ void __launch_bounds__(kDtThreads, 1)
         tc_fence_after();
         float s[HB];
         tmem_ld_row<HB>(tmem + sb * 16 + lane_off, s);
+        // S(c) is complete and read: its K tile's slot and (flat) its TMEM buffer are free
+        if (t == 0) mbar_arrive(&sm.empty[item_of_chunk(c, npb_s) % NSLOT]);
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&sm.s_free[sb]);
         if (c >= 2 && !__all_sync(0xffffffffu, mbar_wait(&sm.p_free[sb], ((c - 2) >> 1) & 1, P.err))) {
           okw = false;
           break;
         }
         bool valid;
-        if (c < NCw) valid = wlo + c * kDtKeys + t <= whi;
+        if (c < NCw) {
+          const int key = wla + c * kDtKeys + t;
+          valid = key >= wlo && key <= whi;
+        }
         else if (c < NCw + NCs) valid = t < nsink;
         else valid = (c - NCw - NCs) * kDtKeys + t < nsel * geo.Bk;
         if (!bounded) {
@@ -1142,66 +1205,33 @@ __global__ void __launch_bounds__(kDtThreads, 1)
 }
 
 // ---------------------------------------------------------------- host ----
-static PFN_cuTensorMapEncodeTiled_v12000 dtc_encode_fn() {
-  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
-  if (fn == nullptr) {
-    void* ptr = nullptr;
-    cudaDriverEntryPointQueryResult q;
-    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) == cudaSuccess &&
-        q == cudaDriverEntryPointSuccess)
-      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(ptr);
-  }
-  return fn;
-}
-
-static bool dtc_map(CUtensorMap* m, const void* base, int B, int n, int H, int dh) {
-  auto fn = dtc_encode_fn();
-  if (fn == nullptr) return false;
-  cuuint64_t dims[4] = {(cuuint64_t)dh, (cuuint64_t)H, (cuuint64_t)n, (cuuint64_t)B};
-  cuuint64_t strides[3] = {(cuuint64_t)dh * 2, (cuuint64_t)H * dh * 2, (cuuint64_t)n * H * dh * 2};
-  cuuint32_t box[4] = {64, 1, 64, 1};
-  cuuint32_t es[4] = {1, 1, 1, 1};
-  // a head's slice of a token row is dh*2 bytes: promote L2 fills no wider,
-  // or every routed row would also drag in its neighbour head's slice
-  const CUtensorMapL2promotion promo = dh * 2 >= 256 ? CU_TENSOR_MAP_L2_PROMOTION_L2_256B
-                                                     : CU_TENSOR_MAP_L2_PROMOTION_L2_128B;
-  return fn(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, const_cast<void*>(base), dims, strides, box, es,
-            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, promo,
-            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
-}
-
 bool decode_tc_supported(const Geom& geo, int dh, const void* k, const void* kr, const void* v, const void* summ,
                          const void* supers) {
-  // TMA tiles and 1-D bulk copies start on 16-byte boundaries
+  // 1-D bulk copies start on 16-byte boundaries
   const bool aligned = ((reinterpret_cast<uintptr_t>(k) | reinterpret_cast<uintptr_t>(kr) |
                          reinterpret_cast<uintptr_t>(v) | reinterpret_cast<uintptr_t>(summ) |
                          reinterpret_cast<uintptr_t>(geo.hier ? supers : summ)) & 15u) == 0;
-  return geo.qknorm && (dh == 64 || dh == 128) && geo.Bk == 64 && geo.m >= 1 && 128 % geo.m == 0 && geo.G <= 16 && geo.nb_cap <= kTopkMaxItems &&
-         (!geo.hier || (geo.ns_cap <= kTopkMaxItems && geo.beam * geo.F <= kTopkMaxItems)) && aligned &&
-         dtc_encode_fn() != nullptr;
+  return geo.qknorm && (dh == 64 || dh == 128) && geo.Bk == 64 && geo.n_cap % 64 == 0 && geo.m >= 1 &&
+         128 % geo.m == 0 && geo.G <= 16 && geo.nb_cap <= kTopkMaxItems &&
+         (!geo.hier || (geo.ns_cap <= kTopkMaxItems && geo.beam * geo.F <= kTopkMaxItems)) && aligned;
 }
 
 template <int DH, int HB>
-static cudaError_t launch_dtc_t(const CUtensorMap& a, const CUtensorMap& b, const CUtensorMap& c,
-                                const DecodeTcParams& P, cudaStream_t st) {
+static cudaError_t launch_dtc_t(const DecodeTcParams& P, cudaStream_t st) {
   const size_t smem = sizeof(DtcSmem<DH>) + 1024;
   static const cudaError_t attr =
       cudaFuncSetAttribute(decode_tc_kernel<DH, HB>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (attr != cudaSuccess) return attr;
-  decode_tc_kernel<DH, HB><<<P.a.geo.B * P.a.geo.Hkv, kDtThreads, smem, st>>>(a, b, c, P);
+  decode_tc_kernel<DH, HB><<<P.a.geo.B * P.a.geo.Hkv, kDtThreads, smem, st>>>(P);
   return cudaGetLastError();
 }
 
 static cudaError_t launch_dtc(DecodeTcParams P, int dh, cudaStream_t st) {
-  const DecodeAttnParams& p = P.a;
-  CUtensorMap m_kc, m_kr, m_v;
-  const Geom& geo = p.geo;
-  if (!dtc_map(&m_kc, p.k, geo.B, geo.n_cap, geo.Hkv, dh) || !dtc_map(&m_kr, p.kr, geo.B, geo.n_cap, geo.Hkv, dh) ||
-      !dtc_map(&m_v, p.v, geo.B, geo.n_cap, geo.Hkv, dh))
-    return cudaErrorInvalidValue;
+  const Geom& geo = P.a.geo;
+  if (geo.n_cap % 64 != 0) return cudaErrorInvalidValue;  // whole 64-token tiles
   // softmax head rows: 8 when the group fits, else all 16 of the MMA's N
-  if (dh == 64) return geo.G <= 8 ? launch_dtc_t<64, 8>(m_kc, m_kr, m_v, P, st) : launch_dtc_t<64, 16>(m_kc, m_kr, m_v, P, st);
-  return geo.G <= 8 ? launch_dtc_t<128, 8>(m_kc, m_kr, m_v, P, st) : launch_dtc_t<128, 16>(m_kc, m_kr, m_v, P, st);
+  if (dh == 64) return geo.G <= 8 ? launch_dtc_t<64, 8>(P, st) : launch_dtc_t<64, 16>(P, st);
+  return geo.G <= 8 ? launch_dtc_t<128, 8>(P, st) : launch_dtc_t<128, 16>(P, st);
 }
 
 

@@ -153,9 +153,10 @@ cudaError_t launch_qknorm_rope(const Geom& geo, int n, const __nv_bfloat16* k, c
 // Summaries of blocks [blk_begin, blk_end) for every sequence; if pos/t are
 // given (append), only blocks completed by tokens [pos[b], pos[b]+t) of
 // sequence b are rebuilt.
+// k_cache token-major [B, n_cap, Hkv, dh], or (tiled) the KV cache's chunk-tiled layout
 cudaError_t launch_summarize(const Geom& geo, int dh, const __nv_bfloat16* k_cache, const float* probes,
                              const float* proj, __nv_bfloat16* summ, int blk_begin, int blk_end,
-                             const int32_t* pos, int t, cudaStream_t st);
+                             const int32_t* pos, int t, cudaStream_t st, bool tiled = false);
 cudaError_t launch_supers(const Geom& geo, int dh, int nb_fixed, const __nv_bfloat16* summ,
                           __nv_bfloat16* supers, int s_begin, int s_end, const int32_t* pos, int t,
                           cudaStream_t st);

@@ -87,6 +87,24 @@ HBA_DEVICE void key_row(const __nv_bfloat16* __restrict__ ks, __nv_bfloat16* __r
   store_head_row<DH>(kr, r);
 }
 
+// A lane's PER consecutive elements (d = lane * PER ...) stored at their
+// chunk-tiled positions (contiguous: they sit in one 16-byte group).
+template <int DH>
+HBA_DEVICE void store_chunked(__nv_bfloat16* __restrict__ y, size_t row_base, int t, const float* v) {
+  constexpr int PER = DH / 32;
+  const int lane = threadIdx.x & 31;
+  __nv_bfloat16* dst = y + tiled_offset<DH>(row_base, t, lane * PER);
+  if constexpr (PER == 2) {
+    *reinterpret_cast<__nv_bfloat162*>(dst) = __floats2bfloat162_rn(v[0], v[1]);
+  } else {
+    uint2 u;
+    __nv_bfloat162* h = reinterpret_cast<__nv_bfloat162*>(&u);
+    h[0] = __floats2bfloat162_rn(v[0], v[1]);
+    h[1] = __floats2bfloat162_rn(v[2], v[3]);
+    *reinterpret_cast<uint2*>(dst) = u;
+  }
+}
+
 // Writes new tokens into the cache: k QKNorm'd (or copied when qknorm is
 // off) and its RoPE'd copy at the token's position, v copied.  One warp per
 // (batch, token, kv head).
@@ -107,45 +125,17 @@ __global__ void __launch_bounds__(256) append_kernel(Geom geo, int t, const int3
   const int b = (int)(w / ((int64_t)geo.Hkv * t));
   const int p = pos[b] + tau;
   if (p < 0 || p >= geo.n_cap) return;  // host validated; never write out of the cache
-  const int64_t dst = (((int64_t)b * geo.n_cap + p) * geo.Hkv + g) * DH;
-  key_row<DH>(k_new + w * DH, k_cache + dst, kr_cache + dst, geo.qknorm ? k_gain[g] : 1.f, geo.eps,
-              geo.qknorm != 0, cos + (size_t)p * DH, sin + (size_t)p * DH);
-  const int lane = threadIdx.x & 31;
-  for (int d = lane; d < DH / 2; d += 32)
-    reinterpret_cast<__nv_bfloat162*>(v_cache + dst)[d] = reinterpret_cast<const __nv_bfloat162*>(v_new + w * DH)[d];
-}
-
-// Element offset of (token t, dim d) of one (sequence, head) in the
-// chunk-tiled layout: per 64-token chunk, per 64-dim half, the 8 KB image a
-// 128-byte-swizzled TMA box [64 tokens x 64 dims] leaves in shared memory
-// (sw128_offset), so that one 1-D bulk copy of a chunk fills a K or V ring
-// slot in the UMMA operand layout.  row_base = first element of the
-// (sequence, head)'s chunk 0.
-template <int DH>
-HBA_DEVICE size_t chunked_offset(size_t row_base, int t, int d) {
-  constexpr int HALVES = DH / 64;
-  const int r = t & 63;
-  const int c = d & 63;
-  const uint32_t off = (uint32_t)(r * 128 + ((((c >> 3) ^ (r & 7))) << 4) + (c & 7) * 2) / 2;
-  return row_base + ((size_t)(t >> 6) * HALVES + (d >> 6)) * 4096 + off;
-}
-
-// A lane's PER consecutive elements (d = lane * PER ...) stored at their
-// chunk-tiled positions (contiguous: they sit in one 16-byte group).
-template <int DH>
-HBA_DEVICE void store_chunked(__nv_bfloat16* __restrict__ y, size_t row_base, int t, const float* v) {
+  // the cache is chunk-tiled per (sequence, kv head): [n_cap/64][dh/64][64 x 64]
+  const size_t head_base = ((size_t)b * geo.Hkv + g) * (size_t)geo.n_cap * DH;
   constexpr int PER = DH / 32;
-  const int lane = threadIdx.x & 31;
-  __nv_bfloat16* dst = y + chunked_offset<DH>(row_base, t, lane * PER);
-  if constexpr (PER == 2) {
-    *reinterpret_cast<__nv_bfloat162*>(dst) = __floats2bfloat162_rn(v[0], v[1]);
-  } else {
-    uint2 u;
-    __nv_bfloat162* h = reinterpret_cast<__nv_bfloat162*>(&u);
-    h[0] = __floats2bfloat162_rn(v[0], v[1]);
-    h[1] = __floats2bfloat162_rn(v[2], v[3]);
-    *reinterpret_cast<uint2*>(dst) = u;
-  }
+  float x[PER], r[PER], vv[PER];
+  load_head_row<DH>(k_new + w * DH, x);
+  load_head_row<DH>(v_new + w * DH, vv);
+  if (geo.qknorm) qknorm_lane<DH>(x, k_gain[g], geo.eps);
+  store_chunked<DH>(k_cache, head_base, p, x);
+  rope_lane<DH>(x, r, cos + (size_t)p * DH, sin + (size_t)p * DH);
+  store_chunked<DH>(kr_cache, head_base, p, r);
+  store_chunked<DH>(v_cache, head_base, p, vv);
 }
 
 // kc and kr for every (batch, token, kv head) of a [B, n, Hkv, dh] tensor.

@@ -36,7 +36,7 @@ __global__ void __launch_bounds__(kSumThreads, 2) summarize_kernel(Geom geo, con
                                                                    const float* __restrict__ proj,
                                                                    __nv_bfloat16* __restrict__ summ, int blk_begin,
                                                                    int blk_end, const int32_t* __restrict__ pos,
-                                                                   int t, float rsd) {
+                                                                   int t, float rsd, int tiled) {
   extern __shared__ __align__(16) float smem[];
   constexpr int KS = DH + 4;
   constexpr int CP = DH / 32;  // projection columns per thread
@@ -74,7 +74,9 @@ __global__ void __launch_bounds__(kSumThreads, 2) summarize_kernel(Geom geo, con
       __syncthreads();  // k_s / att_s free (and, first time, proj_s / probe_s written)
       for (int e = tid; e < Bk * (DH / 8); e += kSumThreads) {
         const int row = e / (DH / 8), c8 = e % (DH / 8);
-        const size_t off = (((size_t)b * geo.n_cap + (size_t)blk * Bk + row) * geo.Hkv + g) * DH + c8 * 8;
+        const size_t off =
+            tiled ? tiled_offset<DH>(((size_t)b * geo.Hkv + g) * (size_t)geo.n_cap * DH, blk * Bk + row, c8 * 8)
+                  : (((size_t)b * geo.n_cap + (size_t)blk * Bk + row) * geo.Hkv + g) * DH + c8 * 8;
         float f[8];
         unpack8(*reinterpret_cast<const uint4*>(kc + off), f);
         float4* dst = reinterpret_cast<float4*>(k_s + row * KS + c8 * 8);
@@ -203,7 +205,7 @@ static size_t summarize_smem(int dh, int m, int Bk) {
 
 cudaError_t launch_summarize(const Geom& geo, int dh, const __nv_bfloat16* k_cache, const float* probes,
                              const float* proj, __nv_bfloat16* summ, int blk_begin, int blk_end,
-                             const int32_t* pos, int t, cudaStream_t st) {
+                             const int32_t* pos, int t, cudaStream_t st, bool tiled) {
   int nblk = blk_end - blk_begin;
   if (pos != nullptr) nblk = t / geo.Bk + 2;  // upper bound on blocks completed by t tokens
   if (nblk <= 0) return cudaSuccess;
@@ -216,13 +218,13 @@ cudaError_t launch_summarize(const Geom& geo, int dh, const __nv_bfloat16* k_cac
         cudaFuncSetAttribute(summarize_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
     if ((e = attr64) != cudaSuccess) return e;
     summarize_kernel<64><<<grid, kSumThreads, smem, st>>>(geo, k_cache, probes, proj, summ, blk_begin, blk_end,
-                                                         pos, t, rsd);
+                                                         pos, t, rsd, tiled ? 1 : 0);
   } else {
     static const cudaError_t attr128 =
         cudaFuncSetAttribute(summarize_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
     if ((e = attr128) != cudaSuccess) return e;
     summarize_kernel<128><<<grid, kSumThreads, smem, st>>>(geo, k_cache, probes, proj, summ, blk_begin, blk_end,
-                                                          pos, t, rsd);
+                                                          pos, t, rsd, tiled ? 1 : 0);
   }
   return cudaGetLastError();
 }

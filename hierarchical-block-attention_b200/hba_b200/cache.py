@@ -6,10 +6,15 @@ and every block summary over the whole sequence (src/hba/attention.py:631,
 updates it incrementally, so one decode step reads only what the union
 softmax needs (~2.1K keys + the candidate summaries):
 
-* ``k``        [B, n_cap, Hkv, dh] bf16 -- QKNorm'd NoPE keys
-* ``kr``       [B, n_cap, Hkv, dh] bf16 -- the same keys RoPE'd at their positions,
-                 written once at append time and read for the window
-* ``v``        [B, n_cap, Hkv, dh] bf16
+* ``k``        QKNorm'd NoPE keys, chunk-tiled: [B, Hkv, n_cap/64, dh/64, 64, 64]
+                 bf16, per 64-token block and 64-dim group the 8 KB image a
+                 128-byte-swizzled TMA box leaves in shared memory (16-byte
+                 unit u of row r at unit u ^ (r % 8)), so the decode kernel
+                 moves a block with one 1-D bulk copy; ``tokens("k")`` gives
+                 the token-major [B, n_cap, Hkv, dh] view
+* ``kr``       the same keys RoPE'd at their positions (written once at
+                 append time, read for the window), same layout
+* ``v``        the values, same layout
 * ``summaries``[B, Hkv, n_cap/block, m, dh] bf16 -- slot summaries of complete blocks
 * ``supers``   [B, Hkv, ceil(nb/F), m, dh] bf16 -- hierarchical mode only
 * ``lens``     [B] int32 -- tokens held per sequence (ragged batches allowed)
@@ -39,7 +44,8 @@ class HBADecodeCache:
         self.hier = bool(hier)
         self.B = int(batch)
         Bk = cfg.block
-        self.n_cap = -(-int(max_len) // Bk) * Bk
+        unit = Bk * 64 // np.gcd(Bk, 64)  # whole blocks and whole 64-token cache tiles
+        self.n_cap = -(-int(max_len) // unit) * unit
         self.nb_cap = self.n_cap // Bk
         self.ns_cap = -(-self.nb_cap // cfg.fanout) if self.hier else 0
         self.device = torch.device(device)
@@ -50,7 +56,7 @@ class HBADecodeCache:
                              f"{self.pos_offset + self.n_cap}")
         dev = self.device
         self.c = c_config(cfg, self.hier)
-        self.k = torch.zeros(self.B, self.n_cap, Hkv, dh, dtype=BF16, device=dev)
+        self.k = torch.zeros(self.B, Hkv, self.n_cap // 64, dh // 64, 64, 64, dtype=BF16, device=dev)
         self.kr = torch.zeros_like(self.k)
         self.v = torch.zeros_like(self.k)
         self.summaries = torch.zeros(self.B, Hkv, self.nb_cap, m, dh, dtype=BF16, device=dev)
@@ -71,6 +77,19 @@ class HBADecodeCache:
         self.workspace[:256].zero_()  # sticky device status word (see device_status)
 
     # ---------------------------------------------------------------- state --
+
+    def tokens(self, name):
+        """The cache tensor `name` ("k", "kr" or "v") un-tiled: a token-major
+        [B, n_cap, Hkv, dh] copy (for inspection and tests)."""
+        t = getattr(self, name)
+        B, Hkv, nblk, groups, R, C = t.shape
+        x = t.reshape(B, Hkv, nblk, groups, R, 8, 8)
+        r = torch.arange(R, device=t.device)
+        u = torch.arange(8, device=t.device)
+        phys = u[None, :] ^ (r[:, None] & 7)  # where logical unit u of row r sits
+        idx = phys[None, None, None, None, :, :, None].expand(B, Hkv, nblk, groups, R, 8, 8)
+        x = torch.gather(x, 5, idx).reshape(B, Hkv, nblk, groups, R, C)
+        return x.permute(0, 2, 4, 1, 3, 5).reshape(B, nblk * R, Hkv, groups * C)
     def _refresh_scales(self):
         dh = self.cfg.head_dim
         s = [union_scale(self.cfg, dh, max(1, int(n))) for n in self.lens_host]

@@ -97,7 +97,12 @@ int hba_b200_build_supers(const hba_b200_config* cfg, int32_t batch, int32_t nb_
  * stored, and the summaries of blocks completed by the append (plus the
  * super-summaries that contain them, when `supers` is not NULL) are rebuilt.
  * k_new, v_new: [batch, t, Hkv, dh] bf16 raw; pos: [batch] int32 device;
- * k_cache, k_rope_cache, v_cache: [batch, n_cap, Hkv, dh] bf16.
+ * k_cache, k_rope_cache, v_cache: the KV cache, bf16, chunk-tiled per
+ *   (sequence, kv head): [batch, Hkv, n_cap/64, dh/64, 64, 64] -- per 64-token
+ *   block and 64-dim group the 8 KB image a 128-byte-swizzled TMA box leaves
+ *   in shared memory: element (token t, dim d) at ((t/64)*(dh/64) + d/64)*4096
+ *   + (t%64)*64 + (((d%64)/8) ^ (t%8))*8 + d%8 of the head's run, so a decode
+ *   moves a block with one 1-D bulk copy.  n_cap is a multiple of 64.
  * Has no single counterpart in the reference, which recomputes QKNorm and
  * every summary on each call (src/hba/attention.py:631,659); it produces the
  * same cache contents incrementally.
@@ -122,9 +127,10 @@ size_t hba_b200_decode_workspace_size(const hba_b200_config* cfg, int32_t batch,
  *   scales:    [batch] fp32 device, union logit scale (content scale x tau(n))
  *   q:         [batch, Hq, dh] bf16 raw query;  q_gain: [Hq], k_gain: [Hkv] fp32
  *              (the QKNorm gains; k_gain bounds the logits of the tensor-core path)
- *   k_cache, v_cache: [batch, n_cap, Hkv, dh] bf16 (keys QKNorm'd, NoPE)
- *   k_rope_cache: [batch, n_cap, Hkv, dh] bf16, the same keys RoPE'd at their
- *              positions (hba_b200_append_kv writes both); the window reads it
+ *   k_cache, v_cache: the chunk-tiled KV cache of hba_b200_append_kv (keys
+ *              QKNorm'd, NoPE); n_cap a multiple of 64
+ *   k_rope_cache: the same keys RoPE'd at their positions, same layout
+ *              (hba_b200_append_kv writes both); the window reads it
  *   summaries: [batch, Hkv, n_cap/block, m, dh] bf16
  *   supers:    [batch, Hkv, ceil(n_cap/block/F), m, dh] bf16 (hier only)
  *   cos, sin:  [n_cap, dh] fp32 RoPE tables (rope_tables layout)

@@ -92,8 +92,8 @@ def check_decode(cache, q, cfg, hier, qkn, cos, sin, rows=None, lens=None, tie_r
     for b in rows:
         n_b = int(lens[b])
         nb = n_b // cfg.block
-        kc = np32(cache.k[b:b + 1, :n_b])
-        v = np32(cache.v[b:b + 1, :n_b])
+        kc = np32(cache.tokens("k")[b:b + 1, :n_b])
+        v = np32(cache.tokens("v")[b:b + 1, :n_b])
         S0 = np32(cache.summaries[b:b + 1, :, :nb])
         S1 = np32(cache.supers[b:b + 1, :, :-(-nb // cfg.fanout)]) if hier else None
         res = orc.decode(qc[b:b + 1], kc, v, cosn, sinn, S0, S1, oracle_cfg(cfg), scale_of(cfg, n_b), None,
