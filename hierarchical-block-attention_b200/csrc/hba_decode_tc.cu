@@ -1,8 +1,8 @@
 // Decode on the 5th-generation tensor cores: one CTA per (sequence, kv head)
 // does the selection on CUDA cores and the union softmax with tcgen05 MMAs
-// whose accumulators live in TMEM, K/V tiles fed by TMA.  Used with QKNorm
-// (the logit bound below needs it); other configurations use the mma.sync
-// fused kernel.
+// whose accumulators live in TMEM, K/V tiles fed by 1-D bulk copies from the
+// chunk-tiled cache.  With QKNorm off there is no logit bound: the softmax
+// keeps the running maximum described below from the first chunk.
 //
 // The G query heads of a KV group are few (4-16), so the MMAs are swapped:
 // keys are the M dimension.  For a 128-key chunk
@@ -207,10 +207,10 @@ __global__ void __launch_bounds__(kDtThreads, 1)
             reinterpret_cast<const uint32_t*>(p.q + ((size_t)b * geo.Hq + g * G + h) * DH) + lane * (PER / 2);
 #pragma unroll
         for (int k = 0; k < PER / 2; ++k) qraw[j][k] = src[k];
-        qgain[j] = p.q_gain[g * G + h];
+        qgain[j] = geo.qknorm ? p.q_gain[g * G + h] : 1.f;
       }
     }
-    kg = P.k_gain[g];
+    kg = geo.qknorm ? P.k_gain[g] : 0.f;
   }
 
   // ---- selection geometry (known from the position alone) ----
@@ -390,7 +390,7 @@ __global__ void __launch_bounds__(kDtThreads, 1)
             v[2 * k] = t2.x;
             v[2 * k + 1] = t2.y;
           }
-          qknorm_lane<DH>(v, qgain[j], geo.eps);
+          if (geo.qknorm) qknorm_lane<DH>(v, qgain[j], geo.eps);
           const float sign = lane < 16 ? -1.f : 1.f;
 #pragma unroll
           for (int i = 0; i < PER; ++i) {
@@ -414,7 +414,8 @@ __global__ void __launch_bounds__(kDtThreads, 1)
         if (lane == 0) {
           const float kmax = sqrtf((float)DH) * kg * (1.f + 1.f / 64.f);
           const float m2 = scale * sqrtf(qn2) * kmax * kLog2e;
-          sm.m2[h] = (h < G && ok) ? m2 : 0.f;
+          // without QKNorm no bound: the running maximum from the first chunk
+          sm.m2[h] = (h < G && ok) ? (geo.qknorm ? m2 : __int_as_float(0x7f800000)) : 0.f;
         }
       }
     }
@@ -1211,7 +1212,7 @@ bool decode_tc_supported(const Geom& geo, int dh, const void* k, const void* kr,
   const bool aligned = ((reinterpret_cast<uintptr_t>(k) | reinterpret_cast<uintptr_t>(kr) |
                          reinterpret_cast<uintptr_t>(v) | reinterpret_cast<uintptr_t>(summ) |
                          reinterpret_cast<uintptr_t>(geo.hier ? supers : summ)) & 15u) == 0;
-  return geo.qknorm && (dh == 64 || dh == 128) && geo.Bk == 64 && geo.n_cap % 64 == 0 && geo.m >= 1 &&
+  return (dh == 64 || dh == 128) && geo.Bk == 64 && geo.n_cap % 64 == 0 && geo.m >= 1 &&
          128 % geo.m == 0 && geo.G <= 16 && geo.nb_cap <= kTopkMaxItems &&
          (!geo.hier || (geo.ns_cap <= kTopkMaxItems && geo.beam * geo.F <= kTopkMaxItems)) && aligned;
 }

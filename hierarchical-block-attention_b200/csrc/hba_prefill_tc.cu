@@ -525,8 +525,9 @@ __global__ void __launch_bounds__(kTcThreads, 1)
 #pragma unroll
         for (int e = 0; e < 8; ++e) qn2 = fmaf(f[e], f[e], qn2);
       }
-      const float kmax = sqrtf((float)DH) * p.k_gain[g] * (1.f + 1.f / 64.f);
-      M2 = p.scale * sqrtf(qn2) * kmax * kLog2e;
+      // without QKNorm no bound: the running maximum from the first chunk
+      M2 = geo.qknorm ? p.scale * sqrtf(qn2) * (sqrtf((float)DH) * p.k_gain[g] * (1.f + 1.f / 64.f)) * kLog2e
+                      : __int_as_float(0x7f800000);
     }
     mbar_arrive(&sm.qn_read[t]);  // the tile may be reloaded from here on
     // the row's reference maximum: its bound (fixed), or a running max that starts empty
@@ -737,7 +738,8 @@ bool prefill_tc_supported(const Geom& geo, int dh, int n, bool qknorm) {
   const int QT = 128 / G;
   // the sink block and the routed union of a tile pair (2 QT queries x k picks) fit the
   // NoPE list; its block masks (nb x 8 bytes) fit the K/V ring they overlay while the list is built
-  return qknorm && (dh == 64 || dh == 128) && geo.Bk == kTcBlock && G >= 4 && G <= 16 && QT * G >= 64 &&
+  (void)qknorm;  // without QKNorm the softmax keeps a running maximum
+  return (dh == 64 || dh == 128) && geo.Bk == kTcBlock && G >= 4 && G <= 16 && QT * G >= 64 &&
          1 + 2 * QT * geo.K <= kTcMaxEntries && (size_t)(n / geo.Bk) * 8 <= sizeof(TcSmem<64>::ring) &&
          (size_t)(n / geo.Bk) * 8 <= sizeof(TcSmem<128>::ring) && geo.W <= 1024 && encode_fn() != nullptr;
 }

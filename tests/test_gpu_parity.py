@@ -120,6 +120,10 @@ def test_decode_scale_variants(variant, path, monkeypatch):
         cfg = H.cfg_of(native_ctx=1024, n_heads=8, n_kv=2, head_dim=128)      # tau(4096) = 1 + 0.1 ln 4
     cache, wl, summ, qkn, cos, sin = H.build_cache(cfg, 2, 4096, False, seed=14)
     H.check_decode(cache, wl["q"], cfg, False, qkn, cos, sin)
+    if path == "tc":  # without QKNorm too: the tensor-core kernel (running maximum from the first chunk)
+        from hba_b200 import _lib
+        cache.attend(wl["q"])
+        assert b"decode_tc_kernel" in _lib.load().hba_b200_last_kernels()
 
 
 def test_cache_incremental_append_matches_bulk():
@@ -165,6 +169,18 @@ def test_prefill_dh128_gqa4_matches_oracle(path, monkeypatch):
     cfg = H.cfg_of(n_heads=32, n_kv=8, head_dim=128)
     rows = H.sample_rows(2048, 24, seed=2)
     H.check_prefill(cfg, 2, 2048, False, seed=22, rows=rows)
+
+
+@pytest.mark.parametrize("path", PREFILL_PATHS)
+def test_prefill_without_qknorm(path, monkeypatch):
+    # no QKNorm: no logit bound, so the tensor-core union keeps a running maximum from the first chunk
+    monkeypatch.setenv("HBA_B200_PREFILL_PATH", path)
+    cfg = H.cfg_of(qknorm=False)
+    rows = H.sample_rows(2048, 48, seed=3)
+    H.check_prefill(cfg, 1, 2048, False, seed=24, rows=rows)
+    if path == "tc":
+        from hba_b200 import _lib
+        assert b"prefill_tc_kernel" in _lib.load().hba_b200_last_kernels()
 
 
 @pytest.mark.parametrize("path", PREFILL_PATHS)
