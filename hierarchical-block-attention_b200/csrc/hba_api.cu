@@ -241,8 +241,13 @@ int decode_path(const hba_b200_config* c, const Geom& geo, size_t bh, const void
     if (strcmp(force, "fused") == 0) return fits ? kDecodeFused : kDecodeSplit;
     if (strcmp(force, "tc") == 0) return tc_ok ? kDecodeTc : kDecodeSplit;
   }
+  // the tensor-core kernel whenever it runs: at small batches too (one CTA per
+  // (sequence, kv head) took ~31 us at cfg1 geometry for B = 1, 4 and 16,
+  // the split path over all SMs 48-56 us); else the fused mma.sync kernel for
+  // enough (sequence, kv head) pairs, the split path below that
+  if (tc_ok) return kDecodeTc;
   if (!fits || (long long)bh < kFusedMinPairs) return kDecodeSplit;
-  return tc_ok ? kDecodeTc : kDecodeFused;
+  return kDecodeFused;
 }
 
 // decode split path: per-(sequence, kv head) softmax partials and merge counters

@@ -30,7 +30,7 @@ def _noalloc(cache, q, out, lse, si, ss):
 @pytest.mark.parametrize("hier", [False, True])
 def test_noalloc_decode_matches_workspace_decode_on_two_calls(hier, path, monkeypatch):
     # every decode path, forced (the library reads the variable on each call):
-    # the small batch here would otherwise always take the split path
+    # the small batch here would otherwise always take the tensor-core path
     monkeypatch.setenv("HBA_B200_DECODE_PATH", path)
     cfg = H.cfg_of(n_heads=8, n_kv=2, head_dim=128, fanout=8, beam=4) if hier else H.cfg_of()
     cache, wl, summ, qkn, cos, sin = H.build_cache(cfg, 4, 4096, hier, seed=41)
