@@ -417,3 +417,141 @@ def selection_parity(idx_a, val_a, ok_a, idx_b, val_b, ok_b, tie=1e-6, tie_rel=0
         if abs(Bs[i] - ba) > tie + tie_rel * abs(ba):
             return False, f"block {i} score {Bs[i]!r} only in second list (boundary {ba!r})"
     return True, "tie"
+
+
+# ------------------------------------------------------------ backward --------
+def rope_backward(dy, cos_rows, sin_rows):
+    """Transpose of ``apply_rope`` (attention.py:40-44): y = x*cos +
+    rot_half(x)*sin with rot_half's matrix R antisymmetric, so dx = dy*cos -
+    rot_half(dy*sin)."""
+    dy = np.asarray(dy, np.float64)
+    return dy * cos_rows - rot_half(dy * sin_rows)
+
+
+def head_rmsnorm_backward(x, gain, dy, eps=1e-6):
+    """Gradient of ``_HeadRMSNorm.forward`` (attention.py:88-94) w.r.t. its
+    input and its per-head scalar gain.  With u = x / rms, rms = sqrt(max(
+    mean(x^2), eps)): dx = (g / rms) * (dy - u * mean(dy * u)) where the mean
+    is not clamped, dx = (g / rms) * dy where it is (the clamp's gradient is
+    zero); dgain[h] = sum over every other axis of dy * u.
+    x, dy: [..., H, dh]; gain: [H].  Returns (dx, dgain) in float64."""
+    xf = np.asarray(x, np.float64)
+    dy = np.asarray(dy, np.float64)
+    ms = np.mean(xf * xf, axis=-1, keepdims=True)
+    clamped = ms <= eps
+    rms = np.sqrt(np.maximum(ms, eps))
+    u = xf / rms
+    g = np.asarray(gain, np.float64)[:, None]
+    proj = np.mean(dy * u, axis=-1, keepdims=True)
+    dx = (g / rms) * np.where(clamped, dy, dy - u * proj)
+    dgain = (dy * u).sum(axis=-1).reshape(-1, xf.shape[-2]).sum(axis=0)
+    return dx, dgain
+
+
+def union_backward_rows(pos, qc_rows, kc_g, v_g, cos, sin, sel_idx, sel_ok, S, W, Bk, scale, dout_rows,
+                        bf16=False):
+    """Gradient of the union softmax of ``union_attention_rows`` (the eval
+    body attention.py:676-711, equal to the dense / fused training paths,
+    :306-389 and :552-607) for one (batch, KV head), the selection held
+    fixed (a top-k has no gradient).  Per query row: P = softmax(scale *
+    logits) over [sinks | window | routed], dP = dout . v, dlogit = P *
+    (dP - sum(P * dP)); the NoPE parts go to q and the keys directly, the
+    window's through the transpose of RoPE at each position.
+    Returns (dqc_rows [c, G, dh], dkc_g [n, dh], dv_g [n, dh]) in float64:
+    gradients w.r.t. the QKNorm'd q and k (before RoPE) and v."""
+    rope = apply_rope_bf16 if bf16 else apply_rope
+    kc_g = np.asarray(kc_g, np.float64)
+    v_g = np.asarray(v_g, np.float64)
+    cos = np.asarray(cos, np.float64)
+    sin = np.asarray(sin, np.float64)
+    c, G, dh = qc_rows.shape
+    n = kc_g.shape[0]
+    dq = np.zeros((c, G, dh))
+    dk = np.zeros((n, dh))
+    dkr = np.zeros((n, dh))   # window keys: gradient w.r.t. the RoPE'd key, rotated back at the end
+    dv = np.zeros((n, dh))
+    for r in range(c):
+        i = int(pos[r])
+        q = np.asarray(qc_rows[r], np.float64)                      # [G, dh]
+        qr = rope(q, cos[i][None], sin[i][None])
+        do = np.asarray(dout_rows[r], np.float64)                   # [G, dh]
+        parts = []                                                  # (key rows, RoPE'd?)
+        ns_ = min(S, i + 1)
+        if ns_ > 0:
+            parts.append((np.arange(ns_), False))
+        w0 = max(S, i - W + 1)
+        if w0 <= i:
+            parts.append((np.arange(w0, i + 1), True))
+        for b, ok in zip(sel_idx[r], sel_ok[r]):
+            if ok:
+                parts.append((np.arange(int(b) * Bk, (int(b) + 1) * Bk), False))
+        keys = []
+        for rows_, rot in parts:
+            keys.append(rope(kc_g[rows_], cos[rows_], sin[rows_]) if rot else kc_g[rows_])
+        lg = np.concatenate([(qr if rot else q) @ kk.T for (rows_, rot), kk in zip(parts, keys)], axis=1) * scale
+        m = lg.max(1, keepdims=True)
+        p = np.exp(lg - m)
+        p /= p.sum(1, keepdims=True)                                # [G, keys]
+        idx = np.concatenate([rows_ for rows_, _ in parts])
+        dp = do @ v_g[idx].T
+        ds = p * (dp - (p * dp).sum(1, keepdims=True)) * scale
+        np.add.at(dv, idx, p.T @ do)
+        at = 0
+        dqr = np.zeros((G, dh))
+        for (rows_, rot), kk in zip(parts, keys):
+            blk = ds[:, at:at + len(rows_)]
+            at += len(rows_)
+            if rot:
+                dqr += blk @ kk
+                np.add.at(dkr, rows_, blk.T @ qr)
+            else:
+                dq[r] += blk @ kk
+                np.add.at(dk, rows_, blk.T @ q)
+        dq[r] += rope_backward(dqr, cos[i][None], sin[i][None])
+    dk += rope_backward(dkr, cos[:n], sin[:n])
+    return dq, dk, dv
+
+
+def eval_backward(q, k, v, cos, sin, cfg, probes, proj, q_gain, k_gain, dout, bf16=False, sel=None):
+    """Gradients of sum(out * dout) for the forward of ``eval_forward`` (the
+    union softmax of attention.py:306-389 / :552-607 / :610-713) w.r.t. q, k,
+    v and the QKNorm gains (attention.py:88-94), the block selection held
+    fixed.  ``sel`` = (idx, ok) [B, Hkv, n, kk] replaces the oracle's own
+    selection (to follow another implementation's picks).
+    Returns dict(dq, dk, dv [input shapes], dq_gain [Hq], dk_gain [Hkv], plus
+    the forward's out / lse / idx / ok)."""
+    q = np.asarray(q, np.float32)
+    k = np.asarray(k, np.float32)
+    v = np.asarray(v, np.float32)
+    B, n, Hq, dh = q.shape
+    Hkv = k.shape[2]
+    G = Hq // Hkv
+    fwd = eval_forward(q, k, v, cos, sin, cfg, probes, proj, q_gain, k_gain, bf16=bf16)
+    idx_all, ok_all = (fwd["idx"], fwd["ok"]) if sel is None else (np.asarray(sel[0]), np.asarray(sel[1]))
+    if cfg["qknorm"]:
+        qc = head_rmsnorm(q, q_gain, bf16=bf16)
+        kc = head_rmsnorm(k, k_gain, bf16=bf16)
+    else:
+        qc, kc = q, k
+    scale = fwd["scale"]
+    pos = np.arange(n)
+    dqc = np.zeros((B, n, Hq, dh))
+    dkc = np.zeros((B, n, Hkv, dh))
+    dv = np.zeros((B, n, Hkv, dh))
+    dout = np.asarray(dout, np.float64)
+    for b in range(B):
+        for g in range(Hkv):
+            dq_, dk_, dv_ = union_backward_rows(pos, qc[b, :, g * G:(g + 1) * G], kc[b, :, g], v[b, :, g], cos, sin,
+                                                idx_all[b, g], ok_all[b, g], cfg["sinks"], cfg["window"],
+                                                cfg["block"], scale, dout[b, :, g * G:(g + 1) * G], bf16=bf16)
+            dqc[b, :, g * G:(g + 1) * G] = dq_
+            dkc[b, :, g] = dk_
+            dv[b, :, g] = dv_
+    if cfg["qknorm"]:
+        dq, dqg = head_rmsnorm_backward(q, q_gain, dqc)
+        dk, dkg = head_rmsnorm_backward(k, k_gain, dkc)
+    else:
+        dq, dk = dqc, dkc
+        dqg, dkg = np.zeros(Hq), np.zeros(Hkv)
+    return dict(dq=dq, dk=dk, dv=dv, dq_gain=dqg, dk_gain=dkg, dqc=dqc, dkc=dkc, out=fwd["out"], lse=fwd["lse"],
+                idx=idx_all, ok=ok_all)

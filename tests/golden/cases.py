@@ -80,3 +80,46 @@ def cfg_dict(cfg, qknorm):
     d = dict(cfg)
     d["qknorm"] = qknorm
     return d
+
+
+# Backward cases: gradients of sum(out * dout) through the reference's dense
+# training path (attention.py:306-389), fp32 autograd.  BWD64 has the
+# tensor-core kernels' geometry (block 64, dh 64, G = 4) at a size the dense
+# path runs on a CPU in seconds.
+BWD64 = dict(n_heads=8, n_kv=2, head_dim=64, block=64, window=256, sinks=4, k_blocks=4, slots=4,
+             fanout=16, beam=4, native_ctx=32768, rope_theta=1_000_000.0, content_scale_mode="inv_d",
+             temp_c=0.1, n_cal=None)
+
+# (name, cfg, n, seed, qknorm)
+BWD_CASES = [
+    ("tiny_qk", TINY, 256, 31, True),
+    ("tiny_noqk", TINY, 256, 32, False),
+    ("g4d64_qk", BWD64, 512, 33, True),
+]
+
+
+def bwd_rows(n, seed):
+    """The query and key rows a backward fixture stores (all of a tiny case;
+    a sample, sinks and the last rows included, of a larger one)."""
+    if n <= 256:
+        a = np.arange(n, dtype=np.int64)
+        return a, a
+    return sample_rows(n, count=64, seed=seed), sample_rows(n, count=96, seed=seed + 1)
+
+
+def bwd_case_inputs(cfg, n, seed, B=1):
+    """Forward inputs as ``eval_case_inputs``, rounded to bf16 values (so a
+    bf16 device path consumes the same numbers), plus the output gradient."""
+    inp = eval_case_inputs(cfg, n, seed, B)
+    for k in ("q", "k", "v"):
+        inp[k] = _bf16_values(inp[k])
+    r = rng(seed + 500)
+    inp["dout"] = _bf16_values(randn(r, B, n, cfg["n_heads"], cfg["head_dim"]))
+    return inp
+
+
+def _bf16_values(a):
+    u = np.ascontiguousarray(a, dtype=np.float32).view(np.uint32).astype(np.uint64)
+    lsb = (u >> np.uint64(16)) & np.uint64(1)
+    return ((u + np.uint64(0x7FFF) + lsb) & np.uint64(0xFFFF0000)).astype(np.uint32).view(np.float32).reshape(
+        np.shape(a))

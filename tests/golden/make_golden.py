@@ -178,5 +178,26 @@ def main():
         out(f"eval_{name}", **arrays)
 
 
+@torch.enable_grad()
+def backward_cases():
+    """Gradients of sum(out * dout) w.r.t. q, k, v and the QKNorm gains
+    through the reference's dense training path (attention.py:306-389),
+    fp32 autograd; the selection is a top-k (no gradient)."""
+    for name, c, n, seed, qk in cases.BWD_CASES:
+        inp = cases.bwd_case_inputs(c, n, seed)
+        cfg = ref_cfg(c, qk)
+        summ, qkn = ref_modules(cfg, inp)
+        cos, sin = orc.rope_tables(n, c["head_dim"], c["rope_theta"])
+        q, k, v = (T(inp[x]).clone().requires_grad_(True) for x in ("q", "k", "v"))
+        o, _ = ref_attn.hba_attention_dense(q, k, v, T(cos), T(sin), cfg, summ, qkn)
+        (o * T(inp["dout"])).sum().backward()
+        qrows, krows = cases.bwd_rows(n, seed)
+        out(f"bwd_{name}", qrows=qrows, krows=krows, out=o.detach().numpy()[:, qrows], dq=q.grad.numpy()[:, qrows],
+            dk=k.grad.numpy()[:, krows], dv=v.grad.numpy()[:, krows],
+            dq_gain=qkn.q.gain.grad.numpy() if qk else np.zeros(c["n_heads"], np.float32),
+            dk_gain=qkn.k.gain.grad.numpy() if qk else np.zeros(c["n_kv"], np.float32))
+
+
 if __name__ == "__main__":
     main()
+    backward_cases()

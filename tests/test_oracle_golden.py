@@ -145,3 +145,24 @@ def test_oracle_matches_reference_model_layer(hier):
     assert np.abs(res["out"] - ref).max() < 1e-4
     # the gains are in the regime the fixed-maximum softmax could not hold
     assert float(np.outer(f["q_gain"], f["k_gain"]).min()) > 50
+
+
+@pytest.mark.parametrize("name,c,n,seed,qk", cases.BWD_CASES, ids=[x[0] for x in cases.BWD_CASES])
+def test_backward_matches_reference_autograd(name, c, n, seed, qk):
+    """The oracle's union-softmax backward (selection fixed) against fp32
+    autograd through the reference's dense training path
+    (attention.py:306-389): gradients of q, k, v and both QKNorm gains."""
+    g = load(f"bwd_{name}")
+    inp = cases.bwd_case_inputs(c, n, seed)
+    cfg = cases.cfg_dict(c, qk)
+    cos, sin = orc.rope_tables(n, c["head_dim"], c["rope_theta"])
+    res = orc.eval_backward(inp["q"], inp["k"], inp["v"], cos, sin, cfg, inp["probes"], inp["proj"], inp["q_gain"],
+                            inp["k_gain"], inp["dout"])
+    qr, kr = g["qrows"], g["krows"]
+    np.testing.assert_allclose(res["out"][:, qr], g["out"], rtol=1e-4, atol=1e-5)
+    for key, rows in (("dq", qr), ("dk", kr), ("dv", kr)):
+        ref = g[key]
+        err = np.abs(res[key][:, rows] - ref).max()
+        assert err <= 1e-4 * max(1.0, np.abs(ref).max()), (key, err)
+    np.testing.assert_allclose(res["dq_gain"], g["dq_gain"], rtol=1e-4, atol=1e-4)
+    np.testing.assert_allclose(res["dk_gain"], g["dk_gain"], rtol=1e-4, atol=1e-4)
