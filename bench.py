@@ -1,7 +1,7 @@
 """Benchmark of the HBA attention hot path on B200.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference]
-                    [--config cfg1|cfg3|cfg2] [--no-secondary]
+                    [--config cfg1|cfg3|cfg2|cfg2-bwd|cfg3-shard|cfg4] [--no-secondary]
 
 Headline (default): BASELINE config 1 -- one decode step (grouped-query
 scoring of every candidate block summary, flat top-16, gather of the
@@ -17,7 +17,8 @@ region: the decode kernel reads and writes the mapped host buffers directly
 (zero-copy, one graph node); `e2e.copy_variant` is the same step with an
 explicit H2D copy of q and D2H copy of out + LSE around the kernel (three
 graph nodes).  The secondary lines measure config 3 (hierarchical decode at
-128K) and config 2 (prefill at 32K), and with N > 1 ranks config 3 with every
+128K), config 2 (prefill at 32K), the backward of that prefill (cfg2-bwd:
+dq, dk, dv and the QKNorm gains' gradients), and with N > 1 ranks config 3 with every
 128K context sharded by token range over the N GPUs (one batch of 32
 sequences, strong scaling; the fused kernel exchanges the per-rank top-k
 lists and softmax partials over NVLink).  `--impl reference` times the CPU oracle port (the
@@ -50,9 +51,9 @@ def parse():
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
-    ap.add_argument("--config", default="cfg1", choices=["cfg1", "cfg2", "cfg3", "cfg3-shard", "cfg4"])
+    ap.add_argument("--config", default="cfg1", choices=["cfg1", "cfg2", "cfg2-bwd", "cfg3", "cfg3-shard", "cfg4"])
     ap.add_argument("--no-secondary", action="store_true")
-    ap.add_argument("--ncu-case", default=None, choices=["cfg1", "cfg3", "cfg2"],
+    ap.add_argument("--ncu-case", default=None, choices=["cfg1", "cfg3", "cfg2", "cfg2-bwd"],
                     help="profiling target: build this decode workload (cfg3 at batch 4) and run 3 decodes, "
                          "or (cfg2) one prefill forward; no timing, no output")
     return ap.parse_args()
@@ -272,6 +273,18 @@ def ncu_case(name, local):
     from hba_b200 import HBADecodeCache, baseline_config, synth
     from hba_b200.attention import stream_of
     dev = torch.device("cuda", local)
+    if name == "cfg2-bwd":
+        # one forward + backward of one cfg2 sequence (batch 1: ~4 GB on the device)
+        from hba_b200 import hba_attention_b200_fused
+        cfg, B, n, hier = baseline_config("cfg2")
+        summ, qkn = synth.make_weights(cfg, dev, seed=0, gains=True)
+        cos, sin = synth.rope_tables(n, cfg.head_dim, 1e6, dev)
+        wl = synth.prefill_workload(cfg, 1, n, seed=0, device=dev)
+        q, k, v = (wl[x].requires_grad_(True) for x in ("q", "k", "v"))
+        out, _ = hba_attention_b200_fused(q, k, v, cos, sin, cfg, summ, qkn)
+        out.backward(torch.ones_like(out))
+        torch.cuda.synchronize()
+        return
     cfg, B, n, hier = baseline_config(name)
     if name == "cfg2":
         from hba_b200 import hba_attention_b200
@@ -649,6 +662,155 @@ def prefill_bench(name, steps, warmup, world, rank, local, pk):
     return res
 
 
+def cpu_prefill_bwd_sample(q, k, v, cos, sin, cfg, qkn, sel, dout, n, B, rows=16):
+    """The oracle's union-softmax backward (numpy port, one thread) on a
+    bounded sample of the same workload: `rows` query positions (>= the
+    window) of one (sequence, kv head), all its query heads, with the GPU
+    forward's picks.  Projected linearly to every row of the batch (B x Hkv x
+    n rows of the same per-row work); the value is tokens/s of that projection."""
+    from oracle import hba_oracle as orc
+    try:
+        from threadpoolctl import threadpool_limits
+    except Exception:  # pragma: no cover
+        threadpool_limits = None
+    r = np.random.default_rng(1)
+    rws = np.sort(r.choice(np.arange(cfg.window, n), size=rows, replace=False))
+    G = cfg.n_heads // cfg.n_kv
+    idx = torch.as_tensor(rws, device=q.device)
+    qs = q[0, idx, :G].float().cpu().numpy()                   # [rows, G, dh], kv head 0
+    dos = dout[0, idx, :G].float().cpu().numpy()
+    ks, vs = k[0, :, 0].float().cpu().numpy(), v[0, :, 0].float().cpu().numpy()
+    cosn, sinn = cos.float().cpu().numpy(), sin.float().cpu().numpy()
+    qg, kg = qkn.q.gain.float().cpu().numpy(), qkn.k.gain.float().cpu().numpy()
+    si = sel[0, 0, idx].cpu().numpy()
+    scale = orc.union_scale(cfg.qknorm, cfg.content_scale_mode, cfg.temp_c, cfg.n_cal, cfg.native_ctx,
+                            cfg.head_dim, n)
+    ctx = threadpool_limits(limits=1) if threadpool_limits else None
+    if ctx:
+        ctx.__enter__()
+    try:
+        t0 = time.perf_counter()
+        qc = orc.head_rmsnorm(qs, qg[:G], bf16=True)
+        kc = orc.head_rmsnorm(ks[:, None], kg[:1], bf16=True)[:, 0]
+        dq, dk, dv = orc.union_backward_rows(rws, qc, kc, vs, cosn, sinn, np.maximum(si, 0), si >= 0, cfg.sinks,
+                                             cfg.window, cfg.block, scale, dos, bf16=True)
+        orc.head_rmsnorm_backward(qs, qg[:G], dq)
+        t_rows = time.perf_counter() - t0
+    finally:
+        if ctx:
+            ctx.__exit__(None, None, None)
+    t_full = B * cfg.n_kv * n * t_rows / rows
+    return dict(value=B * n / t_full, unit="prefill backward tokens/s", cores=1, kind="port",
+                sample=f"numpy oracle backward, 1 thread: {rows} query rows (all {G} heads of one kv head, positions "
+                       f">= the window) of one sequence ({t_rows:.2f} s); projected linearly to {B} x {cfg.n_kv} "
+                       f"kv heads x {n} rows",
+                measured_s=t_rows, projected_s=t_full)
+
+
+def prefill_bwd_bench(name, steps, warmup, world, rank, local, pk):
+    """The backward of the cfg2 prefill (hba_b200_prefill_backward): dq, dk,
+    dv and the QKNorm gains' gradients for a seeded output gradient, the
+    forward's outputs and picks computed once before the timed steps."""
+    from hba_b200 import baseline_config, synth
+    from hba_b200.attention import as_f32, c_config, gains, ptr, stream_of, summarizer_weights, union_scale
+    from hba_b200 import _lib
+    dev = torch.device("cuda", local)
+    cfg, B, n, hier = baseline_config(name)
+    dh, Hq, Hkv = cfg.head_dim, cfg.n_heads, cfg.n_kv
+    summ, qkn = synth.make_weights(cfg, dev, seed=0, gains=True)
+    cos, sin = synth.rope_tables(n, dh, 1e6, dev)
+    wl = synth.prefill_workload(cfg, B, n, seed=2000 + rank, device=dev)
+    q, k, v = wl["q"], wl["k"], wl["v"]
+    c = c_config(cfg, False)
+    L = _lib.load()
+    qg, kg = gains(qkn, dev)
+    probes, proj = summarizer_weights(summ, dev)
+    scale = union_scale(cfg, dh, n)
+    out = torch.empty_like(q)
+    lse = torch.empty(B, Hq, n, dtype=torch.float32, device=dev)
+    sel_i = torch.empty(B, Hkv, n, cfg.k_blocks, dtype=torch.int32, device=dev)
+    sel_s = torch.empty(B, Hkv, n, cfg.k_blocks, dtype=torch.float32, device=dev)
+    fws_bytes = L.hba_b200_prefill_workspace_size(ctypes.byref(c), B, n)
+    fws = torch.empty(fws_bytes, dtype=torch.uint8, device=dev)
+    _lib.check(L.hba_b200_prefill(ctypes.byref(c), B, n, ctypes.c_float(scale), ptr(q), ptr(k), ptr(v), ptr(cos),
+                                  ptr(sin), ptr(qg), ptr(kg), ptr(probes), ptr(proj), ptr(out), ptr(lse), ptr(sel_i),
+                                  ptr(sel_s), ptr(fws), fws_bytes, stream_of(dev)), "hba_b200_prefill")
+    del fws
+    g = torch.Generator(device="cpu").manual_seed(3000 + rank)
+    dout = torch.randn(q.shape, generator=g).to(dev, torch.bfloat16)
+    dq, dk, dv = torch.empty_like(q), torch.empty_like(k), torch.empty_like(v)
+    dqg = torch.empty(Hq, dtype=torch.float32, device=dev)
+    dkg = torch.empty(Hkv, dtype=torch.float32, device=dev)
+    ws_bytes = L.hba_b200_prefill_backward_workspace_size(ctypes.byref(c), B, n)
+    ws = torch.empty(ws_bytes, dtype=torch.uint8, device=dev)
+    flush = torch.empty(FLUSH_BYTES // 4, dtype=torch.float32, device=dev)
+
+    def call(qq, kk, vv, gg):
+        st = L.hba_b200_prefill_backward(ctypes.byref(c), B, n, ctypes.c_float(scale), ptr(qq), ptr(kk), ptr(vv),
+                                         ptr(cos), ptr(sin), ptr(qg), ptr(kg), ptr(out), ptr(lse), ptr(sel_i),
+                                         ptr(gg), ptr(dq), ptr(dk), ptr(dv), ptr(dqg), ptr(dkg), ptr(ws), ws_bytes,
+                                         stream_of(dev))
+        _lib.check(st, "hba_b200_prefill_backward")
+
+    def step():
+        call(q, k, v, dout)
+
+    times, clocks, kt = timed_steps(step, steps, warmup, flush, world, dev, local, marks=4)
+    t_ms = max_over_ranks(statistics.mean(times), world, dev)
+    kernels = _lib.load().hba_b200_last_kernels().decode().split("+")
+    status = L.hba_b200_device_status(ptr(ws), 0, stream_of(dev))
+    main_ms = kt[1]
+    keys = prefill_attended_keys(cfg, n)
+    flops = 10.0 * dh * Hq * B * keys  # 5 products of the forward's 2 per attended (row, key)
+
+    # e2e: q, k, v, dout in from pinned host memory, dq / dk / dv back, every step
+    qh, kh, vh, gh = (t.cpu().pin_memory() for t in (q, k, v, dout))
+    dqh, dkh, dvh = (torch.empty(t.shape, dtype=t.dtype).pin_memory() for t in (dq, dk, dv))
+
+    def step_e2e():
+        q.copy_(qh, non_blocking=True)
+        k.copy_(kh, non_blocking=True)
+        v.copy_(vh, non_blocking=True)
+        dout.copy_(gh, non_blocking=True)
+        call(q, k, v, dout)
+        dqh.copy_(dq, non_blocking=True)
+        dkh.copy_(dk, non_blocking=True)
+        dvh.copy_(dv, non_blocking=True)
+
+    e2e_times, _ = timed_steps(step_e2e, max(2, min(steps, 3)), 1, flush, world, dev, local)
+    e2e_ms = max_over_ranks(statistics.mean(e2e_times), world, dev)
+    torch.cuda.synchronize()
+    h2d = sum(t.numel() * t.element_size() for t in (q, k, v, dout))
+    d2h = sum(t.numel() * t.element_size() for t in (dq, dk, dv))
+    achieved = flops / (main_ms * 1e-3) / 1e12
+    res = dict(
+        metric="prefill backward tokens/s", value=B * n * world / (t_ms * 1e-3), unit="prefill backward tokens/s",
+        n_gpus=world, steps=steps, warmup=warmup, ms_per_step=t_ms, higher_is_better=True, scaling="weak",
+        vs_baseline=None, dtype="bf16",
+        data="synthetic (the cfg2 prefill workload, seeded N(0,1) output gradient, gains ~U(0.6, 1.6))",
+        config=dict(workload=f"{name}-bwd: backward of the prefill, batch {B}/rank, seq {n}, {Hq}/{Hkv} heads, "
+                             f"dh {dh}, flat top-16 (the forward's picks)",
+                    batch_per_rank=B, seq_len=n, n_heads=Hq, n_kv=Hkv, head_dim=dh,
+                    l2="flushed (256 MB write) before every timed step",
+                    timing="eager C-ABI call per step, CUDA events; kernel times between the library's event "
+                           "marks in the same steps"),
+        roofline=dict(bound="tensor", kernel="prefill_bwd_kernel", achieved=achieved, peak=pk["bf16"],
+                      unit="TFLOP/s", frac=achieved / pk["bf16"], peak_source=pk["source"],
+                      traffic=traffic_of(f"prefill_bwd_kernel_{name}"), algorithmic_flops=flops, kernel_ms=main_ms),
+        kernel_ms={"pre-pass+delta": kt[0], "prefill_bwd_kernel": kt[1], "bwd_norm_kernel x3": kt[2]},
+        e2e=dict(value=B * n * world / (e2e_ms * 1e-3), unit="prefill backward tokens/s", ms_per_step=e2e_ms,
+                 h2d_bytes_per_step=h2d, d2h_bytes_per_step=d2h,
+                 timing="per step: pinned H2D of q, k, v, dout, hba_b200_prefill_backward, pinned D2H of dq, dk, dv"),
+        gpu_launches=steps * 7,  # qknorm_rope x2, bwd_delta, prefill_bwd, bwd_norm x3
+        device_status=status, clocks=clocks,
+    )
+    if rank == 0:
+        res["cpu_baseline"] = cpu_prefill_bwd_sample(q, k, v, cos, sin, cfg, qkn, sel_i, dout, n, B)
+    del q, k, v, ws, wl, qh, kh, vh, gh, dqh, dkh, dvh, dq, dk, dv, dout
+    torch.cuda.empty_cache()
+    return res
+
+
 class _AttnTimer:
     """CUDA events around every call of the wrapped function (the HBA
     attention of a layer); .ms() sums the closed intervals."""
@@ -867,16 +1029,20 @@ def main():
         res = shard_bench("cfg3", args.steps, args.warmup, world, rank, local, pk)
     elif args.config == "cfg4":
         res = cfg4_bench(args.steps, args.warmup, world, rank, local, pk)
+    elif args.config == "cfg2-bwd":
+        res = prefill_bwd_bench("cfg2", args.steps, args.warmup, world, rank, local, pk)
     else:
         res = prefill_bench(args.config, args.steps, args.warmup, world, rank, local, pk)
     if not args.no_secondary and args.config == "cfg1":
         sec = []
-        for name in ("cfg3", "cfg2") + (("cfg3-shard",) if world > 1 else ()):
+        for name in ("cfg3", "cfg2", "cfg2-bwd") + (("cfg3-shard",) if world > 1 else ()):
             try:
                 if name == "cfg3":
                     sec.append(decode_bench(name, min(args.steps, 10), args.warmup, world, rank, local, pk))
                 elif name == "cfg3-shard":
                     sec.append(shard_bench("cfg3", min(args.steps, 10), args.warmup, world, rank, local, pk))
+                elif name == "cfg2-bwd":
+                    sec.append(prefill_bwd_bench("cfg2", min(args.steps, 3), 3, world, rank, local, pk))
                 else:
                     sec.append(prefill_bench(name, min(args.steps, 3), 3, world, rank, local, pk))
             except Exception as e:  # report, do not hide, a failing secondary

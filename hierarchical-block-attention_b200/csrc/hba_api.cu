@@ -694,6 +694,107 @@ int hba_b200_prefill_range(const hba_b200_config* cfg, int32_t batch, int32_t n,
 }
 
 
+// ---- prefill backward ----
+
+size_t hba_b200_prefill_backward_workspace_size(const hba_b200_config* cfg, int32_t batch, int32_t n) {
+  int st = HBA_B200_OK;
+  if (!config_ok(cfg, &st) || cfg->hier || batch <= 0 || n <= 0 || n % cfg->block != 0) return 0;
+  const Geom geo = make_geom(cfg, batch, n, n);
+  if (!hba::prefill_bwd_supported(geo, cfg->head_dim, n)) return 0;
+  const size_t kv = (size_t)batch * n * cfg->n_kv * cfg->head_dim;
+  const size_t qv = (size_t)batch * n * cfg->n_heads * cfg->head_dim;
+  size_t b = kAlign;                        // device status word
+  b += 4 * align_up(kv * 2);                // QKNorm'd keys; chunk-tiled QKNorm'd keys, RoPE'd keys, values
+  b += 2 * align_up(qv * 2);                // queries QKNorm'd, RoPE'd
+  b += align_up((size_t)batch * cfg->n_heads * n * 4);  // D per row
+  b += align_up(qv * 4);                    // dq (fp32)
+  b += 2 * align_up(kv * 4);                // dk, dv (fp32 accumulators)
+  return b;
+}
+
+int hba_b200_prefill_backward(const hba_b200_config* cfg, int32_t batch, int32_t n, float scale, const void* q,
+                              const void* k, const void* v, const float* cos, const float* sin, const float* q_gain,
+                              const float* k_gain, const void* out, const float* lse, const int32_t* sel_idx,
+                              const void* dout, void* dq, void* dk, void* dv, float* dq_gain, float* dk_gain,
+                              void* workspace, size_t workspace_bytes, cudaStream_t stream) {
+  int st = HBA_B200_OK;
+  if (!config_ok(cfg, &st)) return st;
+  if (batch <= 0 || n <= 0 || q == nullptr || k == nullptr || v == nullptr || cos == nullptr || sin == nullptr ||
+      out == nullptr || lse == nullptr || sel_idx == nullptr || dout == nullptr || dq == nullptr || dk == nullptr ||
+      dv == nullptr || (cfg->qknorm && (q_gain == nullptr || k_gain == nullptr)) || !std::isfinite(scale))
+    return HBA_B200_ERR_INVALID_ARGUMENT;
+  if (n % cfg->block != 0) return HBA_B200_ERR_NOT_BLOCK_MULTIPLE;
+  if (cfg->hier) return HBA_B200_ERR_UNSUPPORTED;  // the training path selects flat
+  const int dh = cfg->head_dim;
+  const Geom geo = make_geom(cfg, batch, n, n);
+  if (!hba::prefill_bwd_supported(geo, dh, n)) return HBA_B200_ERR_UNSUPPORTED;
+  const size_t need = hba_b200_prefill_backward_workspace_size(cfg, batch, n);
+  if (workspace == nullptr || workspace_bytes < need) return HBA_B200_ERR_WORKSPACE;
+  const size_t kv = (size_t)batch * n * cfg->n_kv * dh;
+  const size_t qv = (size_t)batch * n * cfg->n_heads * dh;
+  unsigned char* ws = static_cast<unsigned char*>(workspace);
+  int* dev_status = reinterpret_cast<int*>(ws);
+  ws += kAlign;
+  auto carve = [&](size_t bytes) {
+    unsigned char* p = ws;
+    ws += align_up(bytes);
+    return p;
+  };
+  auto* kc = reinterpret_cast<__nv_bfloat16*>(carve(kv * 2));
+  auto* kc_sw = reinterpret_cast<__nv_bfloat16*>(carve(kv * 2));
+  auto* kr_sw = reinterpret_cast<__nv_bfloat16*>(carve(kv * 2));
+  auto* v_sw = reinterpret_cast<__nv_bfloat16*>(carve(kv * 2));
+  auto* qcn = reinterpret_cast<__nv_bfloat16*>(carve(qv * 2));
+  auto* qrn = reinterpret_cast<__nv_bfloat16*>(carve(qv * 2));
+  auto* delta = reinterpret_cast<float*>(carve((size_t)batch * cfg->n_heads * n * 4));
+  auto* dq_acc = reinterpret_cast<float*>(carve(qv * 4));
+  auto* dk_acc = reinterpret_cast<float*>(carve(kv * 4));
+  auto* dv_acc = reinterpret_cast<float*>(carve(kv * 4));
+  const auto* kb = static_cast<const __nv_bfloat16*>(k);
+  const auto* qb = static_cast<const __nv_bfloat16*>(q);
+
+  prof_begin(stream);
+  cudaError_t e = cudaMemsetAsync(dev_status, 0, sizeof(int), stream);
+  if (e == cudaSuccess) e = cudaMemsetAsync(dk_acc, 0, kv * 4, stream);
+  if (e == cudaSuccess) e = cudaMemsetAsync(dv_acc, 0, kv * 4, stream);
+  if (e == cudaSuccess && dq_gain != nullptr) e = cudaMemsetAsync(dq_gain, 0, cfg->n_heads * sizeof(float), stream);
+  if (e == cudaSuccess && dk_gain != nullptr) e = cudaMemsetAsync(dk_gain, 0, cfg->n_kv * sizeof(float), stream);
+  // the forward's pre-pass again: the same QKNorm'd / RoPE'd operands, bit for bit
+  if (e == cudaSuccess)
+    e = hba::launch_qknorm_rope(geo, n, kb, k_gain, cos, sin, kc, nullptr, dh, stream,
+                                static_cast<const __nv_bfloat16*>(v), kc_sw, kr_sw, v_sw);
+  if (e == cudaSuccess) {
+    Geom gq = geo;
+    gq.Hkv = geo.Hq;
+    e = hba::launch_qknorm_rope(gq, n, qb, q_gain, cos, sin, qcn, qrn, dh, stream, nullptr, nullptr, nullptr,
+                                nullptr);
+  }
+  if (e == cudaSuccess)
+    e = hba::launch_bwd_delta((int64_t)batch * n * cfg->n_heads, n, cfg->n_heads, dh,
+                              static_cast<const __nv_bfloat16*>(dout), static_cast<const __nv_bfloat16*>(out), delta,
+                              stream);
+  if (e != cudaSuccess) return cuda_status(e);
+  prof_mark(stream);
+  e = hba::launch_prefill_bwd(geo, dh, n, scale, qcn, qrn, static_cast<const __nv_bfloat16*>(dout), kc_sw, kr_sw, v_sw,
+                              sel_idx, cfg->k_blocks, lse, delta, cos, sin, dq_acc, dk_acc, dv_acc, dev_status,
+                              stream);
+  if (e != cudaSuccess) return cuda_status(e);
+  prof_mark(stream);
+  e = hba::launch_bwd_norm((int64_t)batch * n * cfg->n_heads, cfg->n_heads, dh, qb, dq_acc, q_gain, cfg->eps,
+                           cfg->qknorm != 0, static_cast<__nv_bfloat16*>(dq), dq_gain, stream);
+  if (e == cudaSuccess)
+    e = hba::launch_bwd_norm((int64_t)batch * n * cfg->n_kv, cfg->n_kv, dh, kb, dk_acc, k_gain, cfg->eps,
+                             cfg->qknorm != 0, static_cast<__nv_bfloat16*>(dk), dk_gain, stream);
+  if (e == cudaSuccess)
+    e = hba::launch_bwd_norm((int64_t)batch * n * cfg->n_kv, cfg->n_kv, dh, nullptr, dv_acc, nullptr, cfg->eps,
+                             false, static_cast<__nv_bfloat16*>(dv), nullptr, stream);
+  if (e != cudaSuccess) return cuda_status(e);
+  prof_mark(stream);
+  g_last_kernels = "qknorm_rope_kernel+bwd_delta_kernel+prefill_bwd_kernel+bwd_norm_kernel";
+  return HBA_B200_OK;
+}
+
+
 // ---- KV-range sharded decode ----
 
 int hba_b200_decode_shard_select(const hba_b200_config* cfg, int32_t batch, int32_t n_cap_local, int32_t tok_lo,

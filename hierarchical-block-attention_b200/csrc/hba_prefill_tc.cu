@@ -720,8 +720,9 @@ static PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
 }
 
 // [B, n, H, dh] bf16 tensor as a 4-D map {dh, H, n, B}; a box is 64 elements
-// of dh x box_h heads x box_n tokens, 128-byte swizzle (the query tiles).
-static bool make_map(CUtensorMap* m, const void* base, int B, int n, int H, int dh, int box_h, int box_n) {
+// of dh x box_h heads x box_n tokens, 128-byte swizzle (the query tiles; the
+// backward's query and output-gradient tiles too).
+bool make_map(CUtensorMap* m, const void* base, int B, int n, int H, int dh, int box_h, int box_n) {
   auto fn = encode_fn();
   if (fn == nullptr) return false;
   cuuint64_t dims[4] = {(cuuint64_t)dh, (cuuint64_t)H, (cuuint64_t)n, (cuuint64_t)B};

@@ -5,10 +5,11 @@ Signatures and argument meaning follow the reference's
 
 * ``hba_attention_b200`` replaces ``hba_attention_eval(q, k, v, cos, sin, cfg,
   summ, qkn, cap, hier=False, equiv=False)`` (attention.py:610-713);
-* ``hba_attention_b200_fused`` replaces the forward of
-  ``hba_attention_fused`` / ``hba_attention_dense`` (attention.py:552, :306),
-  returning ``(out, aux)`` with a zero aux (inference only: the CUDA path has
-  no backward and raises if asked for one).
+* ``hba_attention_b200_fused`` replaces ``hba_attention_fused`` /
+  ``hba_attention_dense`` (attention.py:552, :306), returning ``(out, aux)``
+  with a zero aux (the summarizer's aux-KL teacher is not built); it is
+  differentiable in q, k, v and the QKNorm gains through the CUDA backward
+  (``hba_b200_prefill_backward``).
 
 ``cfg`` is any object with the reference ``HBAConfig`` field names,
 ``summ`` a module holding ``probes [Hkv, m, dh]`` and ``proj [Hkv, dh, dh]``,
@@ -100,7 +101,8 @@ def summarizer_weights(summ, device):
 
 def _no_grad_guard(*ts):
     if torch.is_grad_enabled() and any(t.requires_grad for t in ts):
-        raise NotImplementedError("hba_b200 is a forward-only (inference) path; run it under torch.no_grad()")
+        raise NotImplementedError("hba_attention_b200 is the eval path (no backward); the differentiable training "
+                                  "forward is hba_attention_b200_fused")
 
 
 # ------------------------------------------------------------- forwards ------
@@ -182,9 +184,71 @@ def _forward(q, k, v, cos, sin, cfg, summ, qkn, hier, q_lo, n_total, return_lse,
 
 
 def hba_attention_b200_fused(q, k, v, cos, sin, cfg, summ, qkn):
-    """Forward of the train-path contract ``(out, aux)`` (reference
-    hba_attention_fused attention.py:552 / hba_attention_dense :306): the same
-    union softmax; aux is a zero scalar because the summarizer's aux-KL teacher
-    is a training signal outside this inference path."""
-    out = hba_attention_b200(q, k, v, cos, sin, cfg, summ, qkn)
+    """The train-path contract ``(out, aux)`` (reference hba_attention_fused
+    attention.py:552 / hba_attention_dense :306): the same union softmax,
+    differentiable in q, k, v and the QKNorm gains ``qkn.q.gain`` /
+    ``qkn.k.gain`` (the block selection, a top-k, has none, as in the
+    reference).  aux is a zero scalar: the summarizer's aux-KL teacher
+    (attention.py:478-549) is not built."""
+    qg, kg = qkn.q.gain, qkn.k.gain
+    needs = [t.requires_grad for t in (q, k, v, qg, kg)]
+    if torch.is_grad_enabled() and any(needs):
+        out = _UnionSoftmax.apply(q, k, v, qg, kg, cos, sin, cfg, summ)
+    else:
+        out = hba_attention_b200(q, k, v, cos, sin, cfg, summ, qkn)
     return out, q.new_zeros(())
+
+
+class _Gains:
+    """A stand-in for the reference's QKNorm module holding given gain tensors."""
+
+    def __init__(self, qg, kg):
+        self.q = type("G", (), {"gain": qg})()
+        self.k = type("G", (), {"gain": kg})()
+
+
+class _UnionSoftmax(torch.autograd.Function):
+    """Forward: the prefill union softmax with its LSE and picks; backward:
+    ``hba_b200_prefill_backward`` (dq, dk, dv, dgain_q, dgain_k)."""
+
+    @staticmethod
+    def forward(ctx, q, k, v, qg, kg, cos, sin, cfg, summ):
+        out, lse, (sel_i, _) = _forward(q, k, v, cos, sin, cfg, summ, _Gains(qg, kg), False, 0, None, True, True, True)
+        ctx.cfg = cfg
+        ctx.dtypes = (q.dtype, k.dtype, v.dtype, qg.dtype, kg.dtype)
+        ctx.save_for_backward(q, k, v, qg, kg, cos, sin, out, lse, sel_i)
+        return out
+
+    @staticmethod
+    def backward(ctx, dout):
+        q, k, v, qg, kg, cos, sin, out, lse, sel_i = ctx.saved_tensors
+        cfg = ctx.cfg
+        B, n, Hq, dh = q.shape
+        Hkv = k.shape[2]
+        dev = q.device
+        with torch.cuda.device(dev):
+            qb, kb, vb = as_bf16(q), as_bf16(k), as_bf16(v)
+            ob, gb = as_bf16(out), as_bf16(dout)
+            cs, sn = as_f32(cos[:n], dev), as_f32(sin[:n], dev)
+            qgf, kgf = as_f32(qg, dev), as_f32(kg, dev)
+            c = c_config(cfg, False)
+            L = _lib.load()
+            ws_bytes = L.hba_b200_prefill_backward_workspace_size(ctypes.byref(c), B, n)
+            if ws_bytes == 0:
+                _lib.check(_lib.ERR_UNSUPPORTED, "hba_b200_prefill_backward_workspace_size")
+            ws = torch.empty(ws_bytes, dtype=torch.uint8, device=dev)
+            dq = torch.empty_like(qb)
+            dk = torch.empty_like(kb)
+            dv = torch.empty_like(vb)
+            dqg = torch.empty(Hq, dtype=torch.float32, device=dev)
+            dkg = torch.empty(Hkv, dtype=torch.float32, device=dev)
+            st = L.hba_b200_prefill_backward(ctypes.byref(c), B, n, ctypes.c_float(union_scale(cfg, dh, n)), ptr(qb),
+                                             ptr(kb), ptr(vb), ptr(cs), ptr(sn), ptr(qgf), ptr(kgf), ptr(ob),
+                                             ptr(lse), ptr(sel_i), ptr(gb), ptr(dq), ptr(dk), ptr(dv), ptr(dqg),
+                                             ptr(dkg), ptr(ws), ws_bytes, stream_of(dev))
+            _lib.check(st, "hba_b200_prefill_backward")
+            _lib.check_device(ptr(ws), stream_of(dev), "hba_b200_prefill_backward (device status)")
+        qd, kd, vd, qgd, kgd = ctx.dtypes
+        qknorm = getattr(cfg, "qknorm", False)
+        return (dq.to(qd), dk.to(kd), dv.to(vd), dqg.to(qgd) if qknorm else None, dkg.to(kgd) if qknorm else None,
+                None, None, None, None)

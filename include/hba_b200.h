@@ -238,6 +238,28 @@ int hba_b200_prefill_range(const hba_b200_config* cfg, int32_t batch, int32_t n,
                            void* workspace, size_t workspace_bytes, cudaStream_t stream);
 
 /*
+ * Backward of the prefill union softmax: the gradients that autograd takes
+ * through the reference's training attention, hba_attention_fused
+ * (src/hba/attention.py:552-607; equal to hba_attention_dense, :306-389),
+ * for the forward's block selection (a top-k: no gradient through it).
+ *   q, k, v, cos, sin, gains, scale: the forward's arguments (hba_b200_prefill)
+ *   out: [batch, n, Hq, dh] bf16 and lse: [batch, Hq, n] fp32, the forward's outputs
+ *   sel_idx: [batch, Hkv, n, k] int32, the forward's picks (-1 = none)
+ *   dout: [batch, n, Hq, dh] bf16, the gradient of out
+ * Writes dq [batch, n, Hq, dh], dk, dv [batch, n, Hkv, dh] (bf16) and, with
+ * QKNorm, dq_gain [Hq] and dk_gain [Hkv] (fp32; overwritten, not added to).
+ * Flat selection, block 64, dh 64 / 128, G = Hq / Hkv in 4 .. 16;
+ * HBA_B200_ERR_UNSUPPORTED otherwise.  Replaces the flex-attention backward
+ * (torch autograd) of the reference's training path.
+ */
+size_t hba_b200_prefill_backward_workspace_size(const hba_b200_config* cfg, int32_t batch, int32_t n);
+int hba_b200_prefill_backward(const hba_b200_config* cfg, int32_t batch, int32_t n, float scale, const void* q,
+                              const void* k, const void* v, const float* cos, const float* sin, const float* q_gain,
+                              const float* k_gain, const void* out, const float* lse, const int32_t* sel_idx,
+                              const void* dout, void* dq, void* dk, void* dv, float* dq_gain, float* dk_gain,
+                              void* workspace, size_t workspace_bytes, cudaStream_t stream);
+
+/*
  * Device status readout (no counterpart in the reference, whose torch calls
  * are synchronous).  The kernels report a failed bounded device-side wait by
  * writing 1 into a status word instead of hanging or trapping: the first 4

@@ -538,9 +538,18 @@ def eval_backward(q, k, v, cos, sin, cfg, probes, proj, q_gain, k_gain, dout, bf
     dqc = np.zeros((B, n, Hq, dh))
     dkc = np.zeros((B, n, Hkv, dh))
     dv = np.zeros((B, n, Hkv, dh))
+    out, lse = fwd["out"], fwd["lse"]
+    if sel is not None:  # the forward of the given picks
+        out, lse = np.zeros_like(out), np.zeros_like(lse)
     dout = np.asarray(dout, np.float64)
     for b in range(B):
         for g in range(Hkv):
+            if sel is not None:
+                o, ls = union_attention_rows(pos, qc[b, :, g * G:(g + 1) * G], kc[b, :, g], v[b, :, g], cos, sin,
+                                             idx_all[b, g], ok_all[b, g], cfg["sinks"], cfg["window"], cfg["block"],
+                                             scale, bf16=bf16)
+                out[b, :, g * G:(g + 1) * G] = o
+                lse[b, g * G:(g + 1) * G] = ls.T
             dq_, dk_, dv_ = union_backward_rows(pos, qc[b, :, g * G:(g + 1) * G], kc[b, :, g], v[b, :, g], cos, sin,
                                                 idx_all[b, g], ok_all[b, g], cfg["sinks"], cfg["window"],
                                                 cfg["block"], scale, dout[b, :, g * G:(g + 1) * G], bf16=bf16)
@@ -553,5 +562,5 @@ def eval_backward(q, k, v, cos, sin, cfg, probes, proj, q_gain, k_gain, dout, bf
     else:
         dq, dk = dqc, dkc
         dqg, dkg = np.zeros(Hq), np.zeros(Hkv)
-    return dict(dq=dq, dk=dk, dv=dv, dq_gain=dqg, dk_gain=dkg, dqc=dqc, dkc=dkc, out=fwd["out"], lse=fwd["lse"],
+    return dict(dq=dq, dk=dk, dv=dv, dq_gain=dqg, dk_gain=dkg, dqc=dqc, dkc=dkc, out=out, lse=lse,
                 idx=idx_all, ok=ok_all)
