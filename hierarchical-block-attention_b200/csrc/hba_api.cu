@@ -707,8 +707,8 @@ size_t hba_b200_prefill_backward_workspace_size(const hba_b200_config* cfg, int3
   b += 4 * align_up(kv * 2);                // QKNorm'd keys; chunk-tiled QKNorm'd keys, RoPE'd keys, values
   b += 2 * align_up(qv * 2);                // queries QKNorm'd, RoPE'd
   b += align_up((size_t)batch * cfg->n_heads * n * 4);  // D per row
-  b += align_up(qv * 4);                    // dq (fp32)
-  b += 2 * align_up(kv * 4);                // dk, dv (fp32 accumulators)
+  b += 2 * align_up(qv * 4);                // dq w.r.t. the QKNorm'd and the RoPE'd queries (fp32)
+  b += 3 * align_up(kv * 4);                // dk (NoPE, RoPE'd), dv (fp32 accumulators)
   return b;
 }
 
@@ -748,7 +748,9 @@ int hba_b200_prefill_backward(const hba_b200_config* cfg, int32_t batch, int32_t
   auto* qrn = reinterpret_cast<__nv_bfloat16*>(carve(qv * 2));
   auto* delta = reinterpret_cast<float*>(carve((size_t)batch * cfg->n_heads * n * 4));
   auto* dq_acc = reinterpret_cast<float*>(carve(qv * 4));
+  auto* dqr_acc = reinterpret_cast<float*>(carve(qv * 4));
   auto* dk_acc = reinterpret_cast<float*>(carve(kv * 4));
+  auto* dkr_acc = reinterpret_cast<float*>(carve(kv * 4));
   auto* dv_acc = reinterpret_cast<float*>(carve(kv * 4));
   const auto* kb = static_cast<const __nv_bfloat16*>(k);
   const auto* qb = static_cast<const __nv_bfloat16*>(q);
@@ -756,6 +758,7 @@ int hba_b200_prefill_backward(const hba_b200_config* cfg, int32_t batch, int32_t
   prof_begin(stream);
   cudaError_t e = cudaMemsetAsync(dev_status, 0, sizeof(int), stream);
   if (e == cudaSuccess) e = cudaMemsetAsync(dk_acc, 0, kv * 4, stream);
+  if (e == cudaSuccess) e = cudaMemsetAsync(dkr_acc, 0, kv * 4, stream);
   if (e == cudaSuccess) e = cudaMemsetAsync(dv_acc, 0, kv * 4, stream);
   if (e == cudaSuccess && dq_gain != nullptr) e = cudaMemsetAsync(dq_gain, 0, cfg->n_heads * sizeof(float), stream);
   if (e == cudaSuccess && dk_gain != nullptr) e = cudaMemsetAsync(dk_gain, 0, cfg->n_kv * sizeof(float), stream);
@@ -776,18 +779,18 @@ int hba_b200_prefill_backward(const hba_b200_config* cfg, int32_t batch, int32_t
   if (e != cudaSuccess) return cuda_status(e);
   prof_mark(stream);
   e = hba::launch_prefill_bwd(geo, dh, n, scale, qcn, qrn, static_cast<const __nv_bfloat16*>(dout), kc_sw, kr_sw, v_sw,
-                              sel_idx, cfg->k_blocks, lse, delta, cos, sin, dq_acc, dk_acc, dv_acc, dev_status,
-                              stream);
+                              sel_idx, cfg->k_blocks, lse, delta, dq_acc, dqr_acc, dk_acc, dkr_acc, dv_acc,
+                              dev_status, stream);
   if (e != cudaSuccess) return cuda_status(e);
   prof_mark(stream);
-  e = hba::launch_bwd_norm((int64_t)batch * n * cfg->n_heads, cfg->n_heads, dh, qb, dq_acc, q_gain, cfg->eps,
-                           cfg->qknorm != 0, static_cast<__nv_bfloat16*>(dq), dq_gain, stream);
+  e = hba::launch_bwd_norm((int64_t)batch * n * cfg->n_heads, n, cfg->n_heads, dh, qb, dq_acc, dqr_acc, cos, sin,
+                           q_gain, cfg->eps, cfg->qknorm != 0, static_cast<__nv_bfloat16*>(dq), dq_gain, stream);
   if (e == cudaSuccess)
-    e = hba::launch_bwd_norm((int64_t)batch * n * cfg->n_kv, cfg->n_kv, dh, kb, dk_acc, k_gain, cfg->eps,
-                             cfg->qknorm != 0, static_cast<__nv_bfloat16*>(dk), dk_gain, stream);
+    e = hba::launch_bwd_norm((int64_t)batch * n * cfg->n_kv, n, cfg->n_kv, dh, kb, dk_acc, dkr_acc, cos, sin, k_gain,
+                             cfg->eps, cfg->qknorm != 0, static_cast<__nv_bfloat16*>(dk), dk_gain, stream);
   if (e == cudaSuccess)
-    e = hba::launch_bwd_norm((int64_t)batch * n * cfg->n_kv, cfg->n_kv, dh, nullptr, dv_acc, nullptr, cfg->eps,
-                             false, static_cast<__nv_bfloat16*>(dv), nullptr, stream);
+    e = hba::launch_bwd_norm((int64_t)batch * n * cfg->n_kv, n, cfg->n_kv, dh, nullptr, dv_acc, nullptr, nullptr,
+                             nullptr, nullptr, cfg->eps, false, static_cast<__nv_bfloat16*>(dv), nullptr, stream);
   if (e != cudaSuccess) return cuda_status(e);
   prof_mark(stream);
   g_last_kernels = "qknorm_rope_kernel+bwd_delta_kernel+prefill_bwd_kernel+bwd_norm_kernel";

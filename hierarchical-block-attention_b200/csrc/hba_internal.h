@@ -216,19 +216,21 @@ bool prefill_bwd_supported(const Geom& geo, int dh, int n);
 // delta[b, h, t] = sum_d dout * out over rows (b, t, h) of [B, n, H, dh] bf16.
 cudaError_t launch_bwd_delta(int64_t rows, int n, int H, int dh, const __nv_bfloat16* dout, const __nv_bfloat16* out,
                              float* delta, cudaStream_t st);
-// dx (bf16) = QKNorm's backward of dy (fp32) at x, dgain[h] += sum dy * x / rms;
-// or dx = dy without QKNorm.
-cudaError_t launch_bwd_norm(int64_t rows, int H, int dh, const __nv_bfloat16* x, const float* dy, const float* gain,
-                            float eps, bool qknorm, __nv_bfloat16* dx, float* dgain, cudaStream_t st);
+// dx (bf16) = QKNorm's backward of dy + RoPE^T(dyr) (fp32; dyr may be null)
+// at x, dgain[h] += sum dy * x / rms; or that sum alone without QKNorm.
+cudaError_t launch_bwd_norm(int64_t rows, int n, int H, int dh, const __nv_bfloat16* x, const float* dy,
+                            const float* dyr, const float* cos, const float* sin, const float* gain, float eps,
+                            bool qknorm, __nv_bfloat16* dx, float* dgain, cudaStream_t st);
 // qc / qr: the pre-pass's QKNorm'd / RoPE'd queries, dout [B, n, Hq, dh] bf16;
 // kc_sw / kr_sw / v_sw chunk-tiled; sel the forward's picks [B*Hkv, n,
-// list_stride]; lse / delta [B, Hq, n]; dq_acc written, dk_acc / dv_acc
-// accumulated (zero them first), all fp32 in the q / k layouts.
+// list_stride]; lse / delta [B, Hq, n]; dq_acc / dqr_acc (w.r.t. the
+// QKNorm'd / RoPE'd queries) written, dk_acc / dkr_acc / dv_acc accumulated
+// (zero them first), all fp32 in the q / k layouts.
 cudaError_t launch_prefill_bwd(const Geom& geo, int dh, int n, float scale, const __nv_bfloat16* qc,
                                const __nv_bfloat16* qr, const __nv_bfloat16* dout, const __nv_bfloat16* kc_sw,
                                const __nv_bfloat16* kr_sw, const __nv_bfloat16* v_sw, const int32_t* sel,
-                               int list_stride, const float* lse, const float* delta, const float* cos,
-                               const float* sin, float* dq_acc, float* dk_acc, float* dv_acc, int* err,
+                               int list_stride, const float* lse, const float* delta, float* dq_acc,
+                               float* dqr_acc, float* dk_acc, float* dkr_acc, float* dv_acc, int* err,
                                cudaStream_t st);
 
 }  // namespace hba

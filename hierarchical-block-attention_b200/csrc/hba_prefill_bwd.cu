@@ -79,8 +79,7 @@ struct BwSmem {
   alignas(1024) unsigned char ring[NSLOT][KT];
   uint32_t emask[kBwMaxEntries];                        // routed blocks: bit q = query i0 + q picked it
   uint16_t eblk[kBwMaxEntries];
-  float lse2[128];                                      // per row: LSE in log2 units
-  float dd[128];                                        // per row: D
+  float2 rowc[128];                                     // per row: (LSE in log2 units, D)
   uint8_t rq[128];                                      // per row: its query in the tile (32: padding row)
   uint64_t q_ready, qc_ready;
   uint64_t full[NSLOT], empty[NSLOT];
@@ -106,25 +105,20 @@ struct PrefillBwdParams {
   const __nv_bfloat16* v;
   const float* lse;          // [B, Hq, n] natural log
   const float* delta;        // [B, Hq, n]
-  const float* cos;          // [n, DH]
-  const float* sin;
-  float* dq_acc;             // [B, n, Hq, DH]: written once per row
-  float* dk_acc;             // [B, n, Hkv, DH]: reductions (zeroed by the host)
+  // fp32 gradients in the q / k layouts: w.r.t. the QKNorm'd q (NoPE keys)
+  // and the RoPE'd q (window keys), written once per row; w.r.t. the QKNorm'd
+  // k (NoPE rows), the RoPE'd k (window rows) and v, by reductions (zeroed by
+  // the host).  The RoPE transpose and QKNorm's backward run afterwards.
+  float* dq_acc;             // [B, n, Hq, DH]
+  float* dqr_acc;
+  float* dk_acc;             // [B, n, Hkv, DH]
+  float* dkr_acc;
   float* dv_acc;
   int* err;
 };
 
 HBA_DEVICE void red_add4(float* p, float a, float b, float c, float d) {
-  asm volatile("red.global.add.v4.f32 [%0], {%1, %2, %3, %4};\n" ::"l"(p), "f"(a), "f"(b), "f"(c), "f"(d)
-               : "memory");
-}
-
-// The transpose of RoPE (rope(x) = x cos + rot_half(x) sin, rot_half(x) =
-// (-x2, x1)) for one column of the lower (hc = 0) or upper (hc = 1) half:
-// dx[d] = dy[d] cos[d] + dy[d + h] sin[d + h]  (d < h),
-// dx[d] = dy[d] cos[d] - dy[d - h] sin[d - h]  (d >= h).
-HBA_DEVICE float rope_back(float own, float other, float c_own, float s_other, int hc) {
-  return hc == 0 ? fmaf(other, s_other, own * c_own) : fmaf(-other, s_other, own * c_own);
+  asm volatile("red.global.add.v4.f32 [%0], {%1, %2, %3, %4};\n" ::"l"(p), "f"(a), "f"(b), "f"(c), "f"(d));
 }
 
 // D[b, h, t] = sum_d dout * out, one warp per row (b, t, h) of [B, n, H, DH].
@@ -154,33 +148,55 @@ __global__ void __launch_bounds__(256) bwd_delta_kernel(int64_t rows, int n, int
   }
 }
 
-// QKNorm's backward (attention.py:88-94: y = x / rms * g, rms = sqrt(max(
-// mean(x^2), eps))), one warp per row (b, t, h) of [B, n, H, DH]:
-// dx = (g / rms) (dy - u mean(dy u)) with u = x / rms (dx = (g / rms) dy
-// where the mean is clamped), dg[h] += sum_d dy u; or, without QKNorm,
+// One warp per row (b, t, h) of [B, n, H, DH]: the gradient w.r.t. the
+// QKNorm'd tensor, dy + RoPE^T(dyr) (dyr: the gradient w.r.t. its RoPE'd
+// copy at position t; rope(x) = x cos + rot_half(x) sin with rot_half(x) =
+// (-x2, x1), so RoPE^T(g)[d] = g[d] cos[d] + g[d + h] sin[d + h] for d < h
+// and g[d] cos[d] - g[d - h] sin[d - h] above, h = DH / 2), then QKNorm's
+// backward (attention.py:88-94: y = x / rms * g, rms = sqrt(max(mean(x^2),
+// eps))): dx = (g / rms) (dy - u mean(dy u)) with u = x / rms (dx = (g /
+// rms) dy where the mean is clamped), dg[h] += sum_d dy u; without QKNorm
 // dx = dy.  fp32 in, bf16 out; the gain sums go through shared memory, then
 // one atomic per head per CTA.
 template <int DH>
-__global__ void __launch_bounds__(256) bwd_norm_kernel(int64_t rows, int H, const __nv_bfloat16* __restrict__ x,
-                                                       const float* __restrict__ dy, const float* __restrict__ gain,
-                                                       float eps, int qknorm, __nv_bfloat16* __restrict__ dx,
-                                                       float* __restrict__ dgain) {
+__global__ void __launch_bounds__(256) bwd_norm_kernel(int64_t rows, int n, int H, const __nv_bfloat16* __restrict__ x,
+                                                       const float* __restrict__ dy, const float* __restrict__ dyr,
+                                                       const float* __restrict__ cos, const float* __restrict__ sin,
+                                                       const float* __restrict__ gain, float eps, int qknorm,
+                                                       __nv_bfloat16* __restrict__ dx, float* __restrict__ dgain) {
   constexpr int PER = DH / 32;
+  static_assert(PER % 2 == 0, "two columns per access");
   __shared__ float gs[kBwMaxHeads];
   for (int h = threadIdx.x; h < kBwMaxHeads; h += blockDim.x) gs[h] = 0.f;
   __syncthreads();
   const int lane = threadIdx.x & 31;
   const int64_t nwarps = (int64_t)gridDim.x * 8;
   for (int64_t w = (int64_t)blockIdx.x * 8 + threadIdx.x / 32; w < rows; w += nwarps) {
+    // lane l holds columns [l PER, l PER + PER), PER = 2 or 4: 8-byte (float2) accesses
     float d[PER], xv[PER], o[PER];
-    const float4* dp = reinterpret_cast<const float4*>(dy + w * DH + lane * PER);
+    const float2* dp = reinterpret_cast<const float2*>(dy + w * DH + lane * PER);
 #pragma unroll
-    for (int e = 0; e < PER; e += 4) {
-      const float4 f = dp[e / 4];
+    for (int e = 0; e < PER; e += 2) {
+      const float2 f = dp[e / 2];
       d[e] = f.x;
       d[e + 1] = f.y;
-      d[e + 2] = f.z;
-      d[e + 3] = f.w;
+    }
+    if (dyr != nullptr) {
+      // the RoPE partner columns (d +- DH / 2) of lane l sit in lane l ^ 16
+      const int64_t t = (w / H) % n;
+      const float2* rp = reinterpret_cast<const float2*>(dyr + w * DH + lane * PER);
+      const float2* cp = reinterpret_cast<const float2*>(cos + t * DH + lane * PER);
+      const float2* sp = reinterpret_cast<const float2*>(sin + t * DH + lane * PER);
+#pragma unroll
+      for (int e = 0; e < PER; e += 2) {
+        const float2 g2 = rp[e / 2], c2 = cp[e / 2], s2 = sp[e / 2];
+        const float gv[2] = {g2.x, g2.y}, cv[2] = {c2.x, c2.y}, sv[2] = {s2.x, s2.y};
+#pragma unroll
+        for (int j = 0; j < 2; ++j) {
+          const float og = __shfl_xor_sync(0xffffffffu, gv[j] * sv[j], 16);  // partner's g * sin
+          d[e + j] += lane < 16 ? fmaf(gv[j], cv[j], og) : fmaf(gv[j], cv[j], -og);
+        }
+      }
     }
     if (qknorm) {
 #pragma unroll
@@ -296,12 +312,10 @@ __global__ void __launch_bounds__(kBwThreads, 1)
     if (r < G * QT && qt < nq) {
       const size_t ri = ((size_t)b * geo.Hq + g * G + hh) * n + i0 + qt;
       sm.rq[r] = (uint8_t)qt;
-      sm.lse2[r] = p.lse[ri] * kLog2e;
-      sm.dd[r] = p.delta[ri];
+      sm.rowc[r] = make_float2(p.lse[ri] * kLog2e, p.delta[ri]);
     } else {
       sm.rq[r] = 32;
-      sm.lse2[r] = 0.f;
-      sm.dd[r] = 0.f;
+      sm.rowc[r] = make_float2(0.f, 0.f);
     }
   }
 
@@ -532,90 +546,82 @@ __global__ void __launch_bounds__(kBwThreads, 1)
     const int kap = lq * 32 + lane;  // key of the chunk (elementwise step, dV / dK read-outs)
     const int hk = lq >> 1;          // its half of the chunk
     const float sl2 = p.scale * kLog2e;
+    const int rows_valid = G * nq;   // rows [0, G nq) hold queries of the tile
     auto wait_all = [&](uint64_t* bar, uint32_t parity) {
       return __all_sync(0xffffffffu, mbar_wait(bar, parity, p.err));
     };
-    // read-out of a [128 x DH] fp32 accumulator with keys on the lanes:
-    // this warp's DH / 2 columns of key `kap`, rotated back (window keys),
-    // scaled, added into acc (null: the key has no valid row)
-    auto kv_out = [&](uint32_t tcol, float* acc, bool rot, int s, float mul) {
+    // read-out of a [128 x DH] fp32 accumulator with keys on the lanes: this
+    // warp's DH / 2 columns of key `kap`, scaled, added into acc (null: the
+    // key has no valid row); one TMEM wait for all of them
+    auto kv_out = [&](uint32_t tcol, float* acc, float mul) {
+      float f[HD];
 #pragma unroll
-      for (int p4 = 0; p4 < HD / 16; ++p4) {
-        float own[16], oth[16];
-        tmem_ld16(tcol + (uint32_t)(hc * HD + 16 * p4) + lane_off, own);
-        if (rot) tmem_ld16(tcol + (uint32_t)((1 - hc) * HD + 16 * p4) + lane_off, oth);
-        tmem_ld_wait();
-        if (acc != nullptr) {
-          const int d0 = hc * HD + 16 * p4;
-          if (rot) {
-            const float* cr = p.cos + (size_t)s * DH + d0;
-            const float* sr = p.sin + (size_t)s * DH + (1 - hc) * HD + 16 * p4;
+      for (int q32 = 0; q32 < HD / 32; ++q32) tmem_ld32(tcol + (uint32_t)(hc * HD + 32 * q32) + lane_off, f + 32 * q32);
+      tmem_ld_wait();
+      if (acc != nullptr) {
+        float* a = acc + hc * HD;
 #pragma unroll
-            for (int e = 0; e < 16; ++e) own[e] = rope_back(own[e], oth[e], cr[e], sr[e], hc);
-          }
-#pragma unroll
-          for (int e = 0; e < 16; e += 4)
-            red_add4(acc + d0 + e, own[e] * mul, own[e + 1] * mul, own[e + 2] * mul, own[e + 3] * mul);
-        }
+        for (int e = 0; e < HD; e += 4) red_add4(a + e, f[e] * mul, f[e + 1] * mul, f[e + 2] * mul, f[e + 3] * mul);
       }
     };
     // read-out of dQ (rows on the lanes): this warp's DH / 2 columns of row
-    // r, rotated back (window phase), scaled, stored (or added to the
-    // stored window part)
+    // r, scaled, stored to one row of dst (or zeros)
     const int r = kap;
     const int rqt = sm.rq[r];
     const bool row_ok = rqt < 32;
-    const int hq = g * G + (r % G);
-    float* dq_row = row_ok ? p.dq_acc + (((size_t)b * n + i0 + rqt) * geo.Hq + hq) * DH : nullptr;
-    auto dq_out = [&](bool rot, bool add) {
-      const int i = i0 + rqt;
+    const size_t qrow = row_ok ? (((size_t)b * n + i0 + rqt) * geo.Hq + g * G + (r % G)) * DH + hc * HD : 0;
+    auto dq_out = [&](float* dst, bool zero) {
+      float f[HD];
+      if (!zero) {
 #pragma unroll
-      for (int p4 = 0; p4 < HD / 16; ++p4) {
-        float own[16], oth[16];
-        tmem_ld16(t_dq + (uint32_t)(hc * HD + 16 * p4) + lane_off, own);
-        if (rot) tmem_ld16(t_dq + (uint32_t)((1 - hc) * HD + 16 * p4) + lane_off, oth);
+        for (int q32 = 0; q32 < HD / 32; ++q32) tmem_ld32(t_dq + (uint32_t)(hc * HD + 32 * q32) + lane_off, f + 32 * q32);
         tmem_ld_wait();
-        if (row_ok) {
-          const int d0 = hc * HD + 16 * p4;
-          if (rot) {
-            const float* cr = p.cos + (size_t)i * DH + d0;
-            const float* sr = p.sin + (size_t)i * DH + (1 - hc) * HD + 16 * p4;
+      }
+      if (row_ok) {
+        float4* d4 = reinterpret_cast<float4*>(dst + qrow);
 #pragma unroll
-            for (int e = 0; e < 16; ++e) own[e] = rope_back(own[e], oth[e], cr[e], sr[e], hc);
-          }
-          float4* dst = reinterpret_cast<float4*>(dq_row + d0);
-#pragma unroll
-          for (int e4 = 0; e4 < 4; ++e4) {
-            float4 v = make_float4(own[4 * e4] * p.scale, own[4 * e4 + 1] * p.scale, own[4 * e4 + 2] * p.scale,
-                                   own[4 * e4 + 3] * p.scale);
-            if (add) {
-              const float4 o = dst[e4];
-              v.x += o.x;
-              v.y += o.y;
-              v.z += o.z;
-              v.w += o.w;
-            }
-            dst[e4] = v;
-          }
-        }
+        for (int e = 0; e < HD; e += 4)
+          d4[e / 4] = zero ? make_float4(0.f, 0.f, 0.f, 0.f)
+                           : make_float4(f[e] * p.scale, f[e + 1] * p.scale, f[e + 2] * p.scale, f[e + 3] * p.scale);
       }
     };
     bool ok = true;
     for (int c = 0; c < NCH; ++c) {
       const Half x = half_of(c, hk);
       const int s = x.kb + (kap & (kBwBlock - 1));  // the key's token
-      // the tile's queries this key is valid for: [qlo, qhi], or the routed mask
-      int qlo = 1, qhi = 0;
-      const bool routed = x.type == kBwRouted;
-      if (x.type == kBwWindow && s >= geo.S) {
-        qlo = max(0, s - i0);
-        qhi = min(nq - 1, s + geo.W - 1 - i0);
-      } else if (x.type == kBwSink && s < geo.S) {
-        qlo = max(0, s - i0);
-        qhi = nq - 1;
+      // the rows of this warp's 64 row columns [64hc, 64hc + 64) this key is
+      // valid for, as a bit mask: window / sink keys a range of queries, a
+      // routed block the queries that picked it (G rows each)
+      unsigned long long rmask = 0ull;
+      bool key_live = false;
+      {
+        int qlo = 1, qhi = 0;
+        if (x.type == kBwWindow && s >= geo.S) {
+          qlo = max(0, s - i0);
+          qhi = min(nq - 1, s + geo.W - 1 - i0);
+        } else if (x.type == kBwSink && s < geo.S) {
+          qlo = max(0, s - i0);
+          qhi = nq - 1;
+        }
+        auto add_rows = [&](int r0, int r1) {  // rows [r0, r1) of the tile into the 64-row window
+          r0 = max(r0, 64 * hc);
+          r1 = min(min(r1, rows_valid), 64 * hc + 64);
+          if (r1 > r0) {
+            const int lo = r0 - 64 * hc, len = r1 - r0;
+            rmask |= (len >= 64 ? ~0ull : ((1ull << len) - 1ull)) << lo;
+          }
+        };
+        if (x.type == kBwRouted) {
+          key_live = x.m != 0u;
+          for (uint32_t m = x.m; m != 0u; m &= m - 1u) {
+            const int q = __ffs(m) - 1;
+            add_rows(q * G, q * G + G);
+          }
+        } else if (qlo <= qhi) {
+          key_live = true;
+          add_rows(qlo * G, qhi * G + G);
+        }
       }
-      const unsigned long long m64 = routed ? (unsigned long long)x.m : 0ull;
-      const bool key_live = routed ? x.m != 0u : qlo <= qhi;
       if (!wait_all(&sm.s_full, c & 1)) {
         ok = false;
         break;
@@ -628,17 +634,17 @@ __global__ void __launch_bounds__(kBwThreads, 1)
         tmem_ld16(t_s + (uint32_t)(64 * hc + 16 * pc) + lane_off, sv);
         tmem_ld16(t_dp + (uint32_t)(64 * hc + 16 * pc) + lane_off, dv);
         tmem_ld_wait();
+        const uint32_t bits = (uint32_t)(rmask >> (16 * pc)) & 0xffffu;
         uint32_t pk[8], dk[8];
 #pragma unroll
         for (int e = 0; e < 16; e += 2) {
           float pv[2], dsv[2];
 #pragma unroll
           for (int u = 0; u < 2; ++u) {
-            const int rr = 64 * hc + 16 * pc + e + u;
-            const int q = sm.rq[rr];
-            const bool valid = routed ? ((m64 >> q) & 1ull) != 0ull : (q >= qlo && q <= qhi);
-            pv[u] = valid ? ex2_approx(fmaf(sv[e + u], sl2, -sm.lse2[rr])) : 0.f;
-            dsv[u] = pv[u] * (dv[e + u] - sm.dd[rr]);
+            const float2 rc = sm.rowc[64 * hc + 16 * pc + e + u];
+            const bool valid = (bits >> (e + u)) & 1u;
+            pv[u] = valid ? ex2_approx(fmaf(sv[e + u], sl2, -rc.x)) : 0.f;
+            dsv[u] = pv[u] * (dv[e + u] - rc.y);
           }
           pk[e / 2] = pack_bf16x2(pv[0], pv[1]);
           dk[e / 2] = pack_bf16x2(dsv[0], dsv[1]);
@@ -653,16 +659,16 @@ __global__ void __launch_bounds__(kBwThreads, 1)
       fence_proxy_async_smem();  // dS in shared memory, for the dQ MMA
       tc_fence_before();
       mbar_arrive(&sm.p_full);
-      // dV_c and dK_c into the accumulators
-      float* dv_row = key_live ? p.dv_acc + (((size_t)b * n + s) * geo.Hkv + g) * DH : nullptr;
-      float* dk_row = key_live ? p.dk_acc + (((size_t)b * n + s) * geo.Hkv + g) * DH : nullptr;
-      const bool rot = x.type == kBwWindow;
+      // dV_c and dK_c into the accumulators (window keys: the RoPE'd keys' gradient)
+      const size_t krow = (((size_t)b * n + s) * geo.Hkv + g) * DH;
+      float* dv_row = key_live ? p.dv_acc + krow : nullptr;
+      float* dk_row = key_live ? (x.type == kBwWindow ? p.dkr_acc : p.dk_acc) + krow : nullptr;
       if (!wait_all(&sm.dv_full, c & 1)) {
         ok = false;
         break;
       }
       tc_fence_after();
-      kv_out(t_dv, dv_row, false, s, 1.f);
+      kv_out(t_dv, dv_row, 1.f);
       if (DH == 128) {
         tc_fence_before();
         mbar_arrive(&sm.tmp_free);
@@ -672,28 +678,31 @@ __global__ void __launch_bounds__(kBwThreads, 1)
         }
         tc_fence_after();
       }
-      kv_out(t_dk, dk_row, rot, s, p.scale);
+      kv_out(t_dk, dk_row, p.scale);
       tc_fence_before();
       mbar_arrive(&sm.tmp_free);
       if (c == nwc - 1 && NCH > nwc) {
-        // the window part of dQ, rotated back, before the NoPE chunks reuse the accumulator
+        // the window part of dQ (w.r.t. the RoPE'd queries), before the NoPE chunks reuse the accumulator
         if (!wait_all(&sm.dq_full, 0)) {
           ok = false;
           break;
         }
         tc_fence_after();
-        dq_out(true, false);
+        dq_out(p.dqr_acc, false);
         tc_fence_before();
         mbar_arrive(&sm.dq_free);
       }
     }
     if (ok && wait_all(&sm.fin, 0)) {
       tc_fence_after();
-      if (NCH == 0) {
-        if (row_ok)
-          for (int d = hc * HD; d < hc * HD + HD; ++d) dq_row[d] = 0.f;
+      // every row gets exactly one store into each of dq_acc (NoPE) and dqr_acc (window)
+      const bool has_w = nwc > 0, has_n = NCH > nwc;
+      if (has_n) {
+        dq_out(p.dq_acc, false);
+        if (!has_w) dq_out(p.dqr_acc, true);
       } else {
-        dq_out(NCH == nwc, NCH > nwc && nwc > 0);  // window only: rotate; NoPE after a window: add
+        dq_out(p.dqr_acc, !has_w);
+        dq_out(p.dq_acc, true);
       }
     }
   }
@@ -728,29 +737,33 @@ cudaError_t launch_bwd_delta(int64_t rows, int n, int H, int dh, const __nv_bflo
   return cudaGetLastError();
 }
 
-cudaError_t launch_bwd_norm(int64_t rows, int H, int dh, const __nv_bfloat16* x, const float* dy, const float* gain,
-                            float eps, bool qknorm, __nv_bfloat16* dx, float* dgain, cudaStream_t st) {
+cudaError_t launch_bwd_norm(int64_t rows, int n, int H, int dh, const __nv_bfloat16* x, const float* dy,
+                            const float* dyr, const float* cos, const float* sin, const float* gain, float eps,
+                            bool qknorm, __nv_bfloat16* dx, float* dgain, cudaStream_t st) {
   const int64_t blocks = std::min<int64_t>((rows + 7) / 8, 148 * 16);
   if (blocks == 0) return cudaSuccess;
-  if (H > kBwMaxHeads) return cudaErrorInvalidValue;
+  if (H > kBwMaxHeads || (dyr != nullptr && (cos == nullptr || sin == nullptr))) return cudaErrorInvalidValue;
   if (dh == 64)
-    bwd_norm_kernel<64><<<(unsigned)blocks, 256, 0, st>>>(rows, H, x, dy, gain, eps, qknorm ? 1 : 0, dx, dgain);
+    bwd_norm_kernel<64><<<(unsigned)blocks, 256, 0, st>>>(rows, n, H, x, dy, dyr, cos, sin, gain, eps, qknorm ? 1 : 0,
+                                                           dx, dgain);
   else
-    bwd_norm_kernel<128><<<(unsigned)blocks, 256, 0, st>>>(rows, H, x, dy, gain, eps, qknorm ? 1 : 0, dx, dgain);
+    bwd_norm_kernel<128><<<(unsigned)blocks, 256, 0, st>>>(rows, n, H, x, dy, dyr, cos, sin, gain, eps,
+                                                            qknorm ? 1 : 0, dx, dgain);
   return cudaGetLastError();
 }
 
 cudaError_t launch_prefill_bwd(const Geom& geo, int dh, int n, float scale, const __nv_bfloat16* qc,
                                const __nv_bfloat16* qr, const __nv_bfloat16* dout, const __nv_bfloat16* kc_sw,
                                const __nv_bfloat16* kr_sw, const __nv_bfloat16* v_sw, const int32_t* sel,
-                               int list_stride, const float* lse, const float* delta, const float* cos,
-                               const float* sin, float* dq_acc, float* dk_acc, float* dv_acc, int* err,
+                               int list_stride, const float* lse, const float* delta, float* dq_acc,
+                               float* dqr_acc, float* dk_acc, float* dkr_acc, float* dv_acc, int* err,
                                cudaStream_t st) {
   const int QT = 128 / geo.G;
   CUtensorMap m_qc, m_qr, m_do;
   if (((reinterpret_cast<uintptr_t>(kc_sw) | reinterpret_cast<uintptr_t>(kr_sw) | reinterpret_cast<uintptr_t>(v_sw) |
         reinterpret_cast<uintptr_t>(dq_acc) | reinterpret_cast<uintptr_t>(dk_acc) |
-        reinterpret_cast<uintptr_t>(dv_acc) | reinterpret_cast<uintptr_t>(cos) | reinterpret_cast<uintptr_t>(sin)) &
+        reinterpret_cast<uintptr_t>(dv_acc) | reinterpret_cast<uintptr_t>(dqr_acc) |
+        reinterpret_cast<uintptr_t>(dkr_acc)) &
        15u) != 0 ||
       !make_map(&m_qc, qc, geo.B, n, geo.Hq, dh, geo.G, QT) || !make_map(&m_qr, qr, geo.B, n, geo.Hq, dh, geo.G, QT) ||
       !make_map(&m_do, dout, geo.B, n, geo.Hq, dh, geo.G, QT))
@@ -768,10 +781,10 @@ cudaError_t launch_prefill_bwd(const Geom& geo, int dh, int n, float scale, cons
   p.v = v_sw;
   p.lse = lse;
   p.delta = delta;
-  p.cos = cos;
-  p.sin = sin;
   p.dq_acc = dq_acc;
+  p.dqr_acc = dqr_acc;
   p.dk_acc = dk_acc;
+  p.dkr_acc = dkr_acc;
   p.dv_acc = dv_acc;
   p.err = err;
   const long long grid = (long long)geo.B * geo.Hkv * p.tiles;
