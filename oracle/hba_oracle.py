@@ -449,7 +449,7 @@ def head_rmsnorm_backward(x, gain, dy, eps=1e-6):
 
 
 def union_backward_rows(pos, qc_rows, kc_g, v_g, cos, sin, sel_idx, sel_ok, S, W, Bk, scale, dout_rows,
-                        bf16=False):
+                        bf16=False, out_rows=None):
     """Gradient of the union softmax of ``union_attention_rows`` (the eval
     body attention.py:676-711, equal to the dense / fused training paths,
     :306-389 and :552-607) for one (batch, KV head), the selection held
@@ -494,7 +494,11 @@ def union_backward_rows(pos, qc_rows, kc_g, v_g, cos, sin, sel_idx, sel_ok, S, W
         p /= p.sum(1, keepdims=True)                                # [G, keys]
         idx = np.concatenate([rows_ for rows_, _ in parts])
         dp = do @ v_g[idx].T
-        ds = p * (dp - (p * dp).sum(1, keepdims=True)) * scale
+        # D = sum_keys P dP = dout . out; from the stored output when given (a
+        # bf16 path computes it from its rounded output)
+        dd = (p * dp).sum(1, keepdims=True) if out_rows is None else \
+            (do * np.asarray(out_rows[r], np.float64)).sum(1, keepdims=True)
+        ds = p * (dp - dd) * scale
         np.add.at(dv, idx, p.T @ do)
         at = 0
         dqr = np.zeros((G, dh))
@@ -512,12 +516,18 @@ def union_backward_rows(pos, qc_rows, kc_g, v_g, cos, sin, sel_idx, sel_ok, S, W
     return dq, dk, dv
 
 
-def eval_backward(q, k, v, cos, sin, cfg, probes, proj, q_gain, k_gain, dout, bf16=False, sel=None):
+def eval_backward(q, k, v, cos, sin, cfg, probes, proj, q_gain, k_gain, dout, bf16=False, sel=None,
+                  d_from_bf16_out=False):
     """Gradients of sum(out * dout) for the forward of ``eval_forward`` (the
     union softmax of attention.py:306-389 / :552-607 / :610-713) w.r.t. q, k,
     v and the QKNorm gains (attention.py:88-94), the block selection held
     fixed.  ``sel`` = (idx, ok) [B, Hkv, n, kk] replaces the oracle's own
     selection (to follow another implementation's picks).
+    ``d_from_bf16_out``: each row's D = dout . out from the forward output
+    rounded to bf16, as a bf16 path that keeps only its stored output
+    computes it (exact: sum_keys P dP).  With sharply peaked rows (trained
+    QKNorm gains) dP - D cancels on the dominant key and this rounding
+    dominates the difference between the two.
     Returns dict(dq, dk, dv [input shapes], dq_gain [Hq], dk_gain [Hkv], plus
     the forward's out / lse / idx / ok)."""
     q = np.asarray(q, np.float32)
@@ -550,9 +560,11 @@ def eval_backward(q, k, v, cos, sin, cfg, probes, proj, q_gain, k_gain, dout, bf
                                              scale, bf16=bf16)
                 out[b, :, g * G:(g + 1) * G] = o
                 lse[b, g * G:(g + 1) * G] = ls.T
+            o_rows = round_bf16(out[b, :, g * G:(g + 1) * G]) if d_from_bf16_out else None
             dq_, dk_, dv_ = union_backward_rows(pos, qc[b, :, g * G:(g + 1) * G], kc[b, :, g], v[b, :, g], cos, sin,
                                                 idx_all[b, g], ok_all[b, g], cfg["sinks"], cfg["window"],
-                                                cfg["block"], scale, dout[b, :, g * G:(g + 1) * G], bf16=bf16)
+                                                cfg["block"], scale, dout[b, :, g * G:(g + 1) * G], bf16=bf16,
+                                                out_rows=o_rows)
             dqc[b, :, g * G:(g + 1) * G] = dq_
             dkc[b, :, g] = dk_
             dv[b, :, g] = dv_
