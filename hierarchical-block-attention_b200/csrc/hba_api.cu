@@ -574,7 +574,7 @@ int hba_b200_prefill_range(const hba_b200_config* cfg, int32_t batch, int32_t n,
   // query-tiled CUDA-core kernel, =scan the per-query kernel
   const char* force_sel = getenv("HBA_B200_SELECT_PATH");
   const bool no_tc = force_sel != nullptr && (strcmp(force_sel, "scan") == 0 || strcmp(force_sel, "tile") == 0);
-  const bool tc_sel = !no_tc && hba::select_tc_supported(geo, dh, summ, qcn);
+  const bool tc_sel = !no_tc && hba::select_tc_supported(geo, dh, summ, qcn, sup);
   const bool tile_sel = !tc_sel && !(force_sel != nullptr && strcmp(force_sel, "scan") == 0) &&
                         hba::select_tile_supported(geo, dh, summ);
   const int n_lists = (tc_sel || tile_sel) ? 1 : (cfg->hier ? plan.child_splits : plan.sel_splits);
@@ -630,6 +630,26 @@ int hba_b200_prefill_range(const hba_b200_config* cfg, int32_t batch, int32_t n,
     sp.own_bhi = INT_MAX;
     sp.n_limit = geo.n_cap;
     sp.q_off = q_lo;
+    if (cfg->hier) {
+      // the super pass (top-beam supers per query), then the child pass over
+      // the block summaries, each row keeping the children of its own beam
+      Lists beam = carve_lists(ws, (size_t)batch * cfg->n_kv * n_q * cfg->beam);
+      sp.supers = sup;
+      sp.mode = hba::kSelSuper;
+      sp.list_k = cfg->beam;
+      sp.out_score = beam.score;
+      sp.out_idx = beam.idx;
+      e = hba::launch_select_tc(sp, dh, dev_status, stream);
+      if (e != cudaSuccess) return cuda_status(e);
+      prof_mark(stream);
+      sp.mode = hba::kSelChild;
+      sp.list_k = cfg->k_blocks;
+      sp.in_lists = 1;
+      sp.in_score = beam.score;
+      sp.in_idx = beam.idx;
+      sp.out_score = fin.score;
+      sp.out_idx = fin.idx;
+    }
     e = tc_sel ? hba::launch_select_tc(sp, dh, dev_status, stream) : hba::launch_select_tile(sp, dh, dev_status, stream);
     if (e != cudaSuccess) return cuda_status(e);
     prof_mark(stream);
@@ -647,8 +667,10 @@ int hba_b200_prefill_range(const hba_b200_config* cfg, int32_t batch, int32_t n,
                                g_trace_ctas, stream);
     if (e != cudaSuccess) return cuda_status(e);
     prof_mark(stream);
-    g_last_kernels = cfg->hier ? "qknorm_rope_kernel+summarize_kernel+supers_kernel+select_kernel+select_kernel+"
-                                 "prefill_tc_kernel"
+    g_last_kernels = cfg->hier ? (tc_sel ? "qknorm_rope_kernel+summarize_kernel+supers_kernel+select_tc_kernel+"
+                                           "select_tc_kernel+prefill_tc_kernel"
+                                         : "qknorm_rope_kernel+summarize_kernel+supers_kernel+select_kernel+"
+                                           "select_kernel+prefill_tc_kernel")
                                : (tc_sel ? "qknorm_rope_kernel+summarize_kernel+select_tc_kernel+prefill_tc_kernel"
                                          : (tile_sel ? "qknorm_rope_kernel+summarize_kernel+select_tile_kernel+"
                                                        "prefill_tc_kernel"
@@ -684,8 +706,10 @@ int hba_b200_prefill_range(const hba_b200_config* cfg, int32_t batch, int32_t n,
   e = hba::launch_attend(ap, dh, stream);
   if (e != cudaSuccess) return cuda_status(e);
   prof_mark(stream);
-  g_last_kernels = cfg->hier ? "qknorm_rope_kernel+summarize_kernel+supers_kernel+select_kernel+select_kernel+"
-                               "attend_kernel"
+  g_last_kernels = cfg->hier ? (tc_sel ? "qknorm_rope_kernel+summarize_kernel+supers_kernel+select_tc_kernel+"
+                                         "select_tc_kernel+attend_kernel"
+                                       : "qknorm_rope_kernel+summarize_kernel+supers_kernel+select_kernel+"
+                                         "select_kernel+attend_kernel")
                              : (tc_sel ? "qknorm_rope_kernel+summarize_kernel+select_tc_kernel+attend_kernel"
                                        : (tile_sel ? "qknorm_rope_kernel+summarize_kernel+select_tile_kernel+"
                                                      "attend_kernel"

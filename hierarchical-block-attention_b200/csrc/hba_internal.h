@@ -175,7 +175,7 @@ cudaError_t launch_select_tile(const SelParams& p, int dh, int* err, cudaStream_
 // Prefill flat selection on tcgen05 (hba_select_tc.cu): 128 queries per CTA,
 // scores as a UMMA GEMM per stage of summaries, top-k from TMEM; p.q holds the
 // QKNorm'd queries.  Writes one list of p.list_k per query.
-bool select_tc_supported(const Geom& geo, int dh, const void* summ, const void* q);
+bool select_tc_supported(const Geom& geo, int dh, const void* summ, const void* q, const void* supers);
 cudaError_t launch_select_tc(const SelParams& p, int dh, int* err, cudaStream_t st);
 // KV-range shard: the union over this shard's tokens [tok_lo, tok_lo + n_cap)
 // as unnormalised partials (O, l, m) -- m the softmax reference maximum in

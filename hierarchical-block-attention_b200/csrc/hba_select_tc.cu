@@ -1,5 +1,10 @@
-// Prefill routed-block selection, flat scan, on the 5th-generation tensor
-// cores.
+// Prefill routed-block selection on the 5th-generation tensor cores: the
+// flat scan, and the two passes of the hierarchical selection (reference
+// hier_select, src/hba/attention.py:217-246): a super pass that keeps the
+// top-beam super-summaries of each query (a super is a candidate when one of
+// its children is), then a child pass that scores the blocks exactly like
+// the flat scan (a child's score is its block score) and keeps, per query,
+// only the children of its own beam.
 //
 // One CTA per (128 consecutive query positions, sequence x kv head).  The
 // routing queries of the tile form the A operand (M = 128 rows, K = dh) and
@@ -71,11 +76,20 @@ __global__ void __launch_bounds__(kStThreads, 2)
   constexpr int BPS = kStN / MS;  // blocks per stage
   const float scale = p.qp.scale_fixed;
   const int nb = p.qp.n_fixed / geo.Bk;
+  const bool sup_mode = p.mode == kSelSuper, child_mode = p.mode == kSelChild;
+  const int F = geo.F;
   // local query i sits at position q_off + i (a query range of the sequence)
   auto bmax_of = [&](int i) { return i < nq ? min(last_candidate(p.q_off + i, geo.W, geo.Bk), nb - 1) : 0; };
-  const int bmax_tile = bmax_of(min(i0 + kStQ, nq) - 1);  // grows with i: the tile's largest
-  const int NS = bmax_tile >= 1 ? (bmax_tile + BPS - 1) / BPS : 0;
-  const int k = geo.K;
+  // items: blocks 1 .. bmax(i) (flat, child), or supers first .. bmax(i) / F,
+  // the supers with a candidate child (super 0 holds block 0 alone when F = 1)
+  const int first = sup_mode ? (F == 1 ? 1 : 0) : 1;
+  auto imax_of = [&](int i) {
+    const int bm = bmax_of(i);
+    return sup_mode ? (bm >= 1 ? bm / F : -1) : bm;
+  };
+  const int imax_tile = imax_of(min(i0 + kStQ, nq) - 1);  // grows with i: the tile's largest
+  const int NS = imax_tile >= first ? (imax_tile - first + BPS) / BPS : 0;
+  const int k = p.list_k;
 
   if (tid == 0) {
     for (int s = 0; s < 2; ++s) {
@@ -105,7 +119,7 @@ __global__ void __launch_bounds__(kStThreads, 2)
         const int sb = s & 1;
         if (s >= 2 && !mbar_wait(&sm.s_empty[sb], ((s - 2) >> 1) & 1, err)) break;
         mbar_arrive_expect_tx(&sm.s_full[sb], (uint32_t)(HALVES * kStN * 128));
-        const int row0 = (1 + s * BPS) * m;  // rows past nb_cap*m are filled with zeros (masked)
+        const int row0 = (first + s * BPS) * m;  // rows past the tensor are filled with zeros (masked)
         for (int h = 0; h < HALVES; ++h) tma_load_3d(sm.st[sb][h], &tm_s, h * 64, row0, bg, &sm.s_full[sb]);
       }
     }
@@ -162,7 +176,13 @@ __global__ void __launch_bounds__(kStThreads, 2)
       fence_proxy_async_smem();  // the tile is read by the tensor cores
       mbar_arrive(&sm.q_ready);
     }
-    const int bmax = bmax_of(i);
+    const int imax = imax_of(i);
+    // child pass: the row's beam (the super pass's list, -1 = none)
+    int par[KM];
+    const int nbeam = child_mode ? min(geo.beam, KM) : 0;
+#pragma unroll
+    for (int j = 0; j < KM; ++j)
+      par[j] = (child_mode && row_ok && j < nbeam) ? p.in_idx[((size_t)bg * nq + i) * geo.beam + j] : -1;
     float ls[KM];
     int li[KM];
 #pragma unroll
@@ -179,7 +199,7 @@ __global__ void __launch_bounds__(kStThreads, 2)
         break;
       }
       tc_fence_after();
-      const int blo = 1 + s * BPS;
+      const int blo = first + s * BPS;
 #pragma unroll 1
       for (int cb = 0; cb < kStN / 32; ++cb) {
         float v[32];
@@ -193,8 +213,16 @@ __global__ void __launch_bounds__(kStThreads, 2)
 #pragma unroll
           for (int sl = 1; sl < MS; ++sl) best = fmaxf(best, v[jb * MS + sl]);
           const float cs = best * scale;
-          // candidate and better than the list's last entry (ascending blocks: a tie never beats)
-          if (blk <= bmax && cs > ls[KM - 1]) {
+          // candidate and better than the list's last entry (ascending items: a tie never beats)
+          bool take = blk <= imax && cs > ls[KM - 1];
+          if (child_mode && take) {  // a child of the row's beam
+            const int sup = blk / F;
+            bool in = false;
+#pragma unroll
+            for (int j = 0; j < KM; ++j) in |= par[j] == sup;
+            take = in;
+          }
+          if (take) {
             // insert at the first position whose entry it beats, shifting the
             // rest down (descending j reads entry j - 1 before it moves)
 #pragma unroll
@@ -243,11 +271,15 @@ static PFN_cuTensorMapEncodeTiled_v12000 st_encode_fn() {
   return fn;
 }
 
-bool select_tc_supported(const Geom& geo, int dh, const void* summ, const void* q) {
-  // m | 32: a block's slots never straddle a 32-column TMEM load
-  return !geo.hier && (dh == 64 || dh == 128) && (geo.m == 1 || geo.m == 2 || geo.m == 4 || geo.m == 8) &&
-         geo.K >= 1 && geo.K <= 32 && (reinterpret_cast<uintptr_t>(summ) & 15u) == 0 &&
-         (reinterpret_cast<uintptr_t>(q) & 15u) == 0 && st_encode_fn() != nullptr;
+bool select_tc_supported(const Geom& geo, int dh, const void* summ, const void* q, const void* supers) {
+  // m | 32: a block's slots never straddle a 32-column TMEM load; hierarchical:
+  // the beam fits the register list, the supers are 16-byte aligned
+  return (dh == 64 || dh == 128) && (geo.m == 1 || geo.m == 2 || geo.m == 4 || geo.m == 8) && geo.K >= 1 &&
+         geo.K <= 32 && (reinterpret_cast<uintptr_t>(summ) & 15u) == 0 &&
+         (reinterpret_cast<uintptr_t>(q) & 15u) == 0 &&
+         (!geo.hier || (supers != nullptr && geo.beam >= 1 && geo.beam <= 32 && geo.F >= 1 &&
+                        (reinterpret_cast<uintptr_t>(supers) & 15u) == 0)) &&
+         st_encode_fn() != nullptr;
 }
 
 template <int DH, int KM, int MS>
@@ -276,18 +308,26 @@ cudaError_t launch_select_tc(const SelParams& p, int dh, int* err, cudaStream_t 
   auto fn = st_encode_fn();
   if (fn == nullptr) return cudaErrorInvalidValue;
   const Geom& geo = p.geo;
-  // summaries [B*Hkv, nb_cap*m, dh] bf16: box {64 dims, 128 rows, 1}, 128-byte swizzle
+  // summaries [B*Hkv, nb_cap*m, dh] (super pass: supers [B*Hkv, ns_cap*m, dh])
+  // bf16: box {64 dims, 128 rows, 1}, 128-byte swizzle
+  const bool sup = p.mode == kSelSuper;
+  const __nv_bfloat16* base = sup ? p.supers : p.summ;
+  const long long rows = (long long)(sup ? geo.ns_cap : geo.nb_cap) * geo.m;
+  if (base == nullptr || rows <= 0 || (p.mode == kSelChild && p.in_idx == nullptr)) return cudaErrorInvalidValue;
   CUtensorMap map;
-  cuuint64_t dims[3] = {(cuuint64_t)dh, (cuuint64_t)geo.nb_cap * geo.m, (cuuint64_t)geo.B * geo.Hkv};
-  cuuint64_t strides[2] = {(cuuint64_t)dh * 2, (cuuint64_t)geo.nb_cap * geo.m * dh * 2};
+  cuuint64_t dims[3] = {(cuuint64_t)dh, (cuuint64_t)rows, (cuuint64_t)geo.B * geo.Hkv};
+  cuuint64_t strides[2] = {(cuuint64_t)dh * 2, (cuuint64_t)rows * dh * 2};
   cuuint32_t box[3] = {64, (cuuint32_t)kStN, 1};
   cuuint32_t es[3] = {1, 1, 1};
-  if (fn(&map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<__nv_bfloat16*>(p.summ), dims, strides, box, es,
+  if (fn(&map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<__nv_bfloat16*>(base), dims, strides, box, es,
          CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
          CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
     return cudaErrorInvalidValue;
-  if (dh == 64) return geo.K <= 16 ? launch_st_m<64, 16>(map, p, err, st) : launch_st_m<64, 32>(map, p, err, st);
-  return geo.K <= 16 ? launch_st_m<128, 16>(map, p, err, st) : launch_st_m<128, 32>(map, p, err, st);
+  // the register list holds the output list (k or the beam) and, in the child pass, the beam
+  const int need = std::max(p.list_k, geo.hier ? geo.beam : 1);
+  if (p.list_k < 1 || need > 32) return cudaErrorInvalidValue;
+  if (dh == 64) return need <= 16 ? launch_st_m<64, 16>(map, p, err, st) : launch_st_m<64, 32>(map, p, err, st);
+  return need <= 16 ? launch_st_m<128, 16>(map, p, err, st) : launch_st_m<128, 32>(map, p, err, st);
 }
 
 }  // namespace hba

@@ -250,6 +250,37 @@ def test_prefill_selection_paths_agree_on_every_row(dh, heads, slots, n, block, 
     H.assert_picks_agree(i1, s1, i3, s3)
 
 
+@pytest.mark.parametrize("dh,heads,n,fanout,beam", [(64, (14, 2), 4096, 16, 4), (128, (32, 8), 8192, 16, 8),
+                                                     (64, (8, 2), 2048, 1, 4)])
+def test_prefill_hier_selection_tc_matches_scan(dh, heads, n, fanout, beam):
+    """Hierarchical prefill selection: the two tensor-core passes (supers, then
+    the beam's children) against the per-query CUDA-core kernels: the same
+    picks up to the 1e-6 tie rule, scores within 1e-5 (fanout 1: super 0 is
+    block 0 alone, never a candidate)."""
+    import os
+    from hba_b200 import _lib
+    cfg = H.cfg_of(n_heads=heads[0], n_kv=heads[1], head_dim=dh, fanout=fanout, beam=beam)
+    summ, qkn = synth.make_weights(cfg, "cuda", seed=33, gains=True)
+    cos, sin = synth.rope_tables(n, dh, 1e6)
+    wl = synth.prefill_workload(cfg, 2, n, seed=33)
+    res, kern = {}, {}
+    for path in ("scan", "tc"):
+        if path != "tc":
+            os.environ["HBA_B200_SELECT_PATH"] = path
+        try:
+            with torch.no_grad():
+                res[path] = hba_attention_b200(wl["q"], wl["k"], wl["v"], cos, sin, cfg, summ, qkn, hier=True,
+                                               return_lse=True, return_selection=True)
+            kern[path] = _lib.load().hba_b200_last_kernels().decode()
+        finally:
+            os.environ.pop("HBA_B200_SELECT_PATH", None)
+    assert "select_tc_kernel+select_tc_kernel" in kern["tc"] and "select_tc" not in kern["scan"]
+    (o1, l1, (i1, s1)), (o2, l2, (i2, s2)) = res["scan"], res["tc"]
+    H.assert_picks_agree(i1, s1, i2, s2)
+    if torch.equal(i1, i2):
+        assert (o1.float() - o2.float()).abs().max().item() < 2e-2
+
+
 def test_prefill_tiny_blocks_and_knobs():
     """Block 16, window 64, 2 sinks, k 4, 2 slots (the reference's test knobs)."""
     cfg = H.cfg_of(block=16, window=64, sinks=2, k_blocks=4, slots=2, fanout=4, beam=2, n_heads=4, n_kv=2)
