@@ -576,3 +576,53 @@ def eval_backward(q, k, v, cos, sin, cfg, probes, proj, q_gain, k_gain, dout, bf
         dqg, dkg = np.zeros(Hq), np.zeros(Hkv)
     return dict(dq=dq, dk=dk, dv=dv, dq_gain=dqg, dk_gain=dkg, dqc=dqc, dkc=dkc, out=out, lse=lse,
                 idx=idx_all, ok=ok_all)
+
+
+# ---------------------------------------------------------- aux-KL teacher ----
+def aux_teacher(qc, kc, cfg, scale):
+    """The summarizer's auxiliary-loss teacher (attention.py:476-490,
+    `_teacher_chunk`, as `_aux_kl_chunked` :501-529 calls it; the same
+    distribution as `hba_attention_dense`'s :364-369): per query i and KV
+    head, the mean over the group's G heads of each candidate block's share
+    of the softmax over all candidate keys (NoPE logits scale * qc . kc;
+    softmax over blockwise LSEs == softmax over keys summed per block),
+    renormalised over blocks.  qc: [B, n, Hq, dh]; kc: [B, n, Hkv, dh].
+    Returns pstar [B, Hkv, n, nb] (float64); rows with no candidate block
+    are NaN, as in the reference (its loss skips them)."""
+    qc = np.asarray(qc, np.float64)
+    kc = np.asarray(kc, np.float64)
+    B, n, Hq, dh = qc.shape
+    Hkv = kc.shape[2]
+    G = Hq // Hkv
+    Bk = cfg["block"]
+    nb = n // Bk
+    cand = route_candidates(np.arange(n), cfg["window"], nb, Bk)               # [n, nb]
+    pstar = np.zeros((B, Hkv, n, nb))
+    with np.errstate(invalid="ignore", divide="ignore"):
+        for b in range(B):
+            for g in range(Hkv):
+                s = np.einsum("ihd,jd->hij", qc[b, :, g * G:(g + 1) * G], kc[b, :, g]) * scale   # [G, n, n]
+                s = s.reshape(G, n, nb, Bk)
+                m = s.max(-1)
+                blk = m + np.log(np.exp(s - m[..., None]).sum(-1))                         # [G, n, nb]
+                blk = np.where(cand[None], blk, -np.inf)
+                mx = blk.max(-1, keepdims=True)
+                e = np.exp(blk - mx)
+                p = (e / e.sum(-1, keepdims=True)).mean(0)                                  # [n, nb]
+                pstar[b, g] = p / np.maximum(p.sum(-1, keepdims=True), 1e-9)
+    return pstar
+
+
+def aux_kl(pstar, bsc, cand):
+    """attention.py:531-537: -mean over (batch, KV head, query with a
+    candidate) of sum_blocks pstar * log_softmax(bsc) (terms with pstar = 0
+    dropped).  pstar, bsc: [B, Hkv, n, nb]; cand: [n, nb]."""
+    vq = np.asarray(cand).any(-1)
+    if not vq.any():
+        return 0.0
+    bv = np.asarray(bsc, np.float64)[:, :, vq]
+    pv = np.asarray(pstar, np.float64)[:, :, vq]
+    mx = bv.max(-1, keepdims=True)
+    logp = bv - mx - np.log(np.exp(bv - mx).sum(-1, keepdims=True))
+    term = np.where(pv > 0, pv * np.where(np.isfinite(logp), logp, 0.0), 0.0)
+    return float(-term.sum(-1).mean())

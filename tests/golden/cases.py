@@ -123,3 +123,12 @@ def _bf16_values(a):
     lsb = (u >> np.uint64(16)) & np.uint64(1)
     return ((u + np.uint64(0x7FFF) + lsb) & np.uint64(0xFFFF0000)).astype(np.uint32).view(np.float32).reshape(
         np.shape(a))
+
+
+# Aux-KL cases (teacher pstar, route_topk's block scores, the dense path's
+# aux and its summarizer gradients): (name, cfg, n, seed, qknorm)
+AUX_CASES = [
+    ("tiny_qk", TINY, 256, 41, True),
+    ("g4d64_qk", BWD64, 512, 42, True),
+    ("g4d64_noqk", BWD64, 512, 43, False),
+]

@@ -198,6 +198,38 @@ def backward_cases():
             dk_gain=qkn.k.gain.grad.numpy() if qk else np.zeros(c["n_kv"], np.float32))
 
 
+def aux_cases():
+    """The summarizer's aux-KL pieces from the reference, fp32: the teacher
+    pstar as _aux_kl_chunked computes it (attention.py:501-529, calling
+    _teacher_chunk :476-490), the block scores route_topk gives the loss
+    (:272-303), and hba_attention_dense's aux with its gradients w.r.t. the
+    summarizer's probes and proj (aux_w = 1)."""
+    for name, c, n, seed, qk in cases.AUX_CASES:
+        inp = cases.bwd_case_inputs(c, n, seed)
+        cfg = ref_cfg(c, qk)
+        cfg.aux_w = 1.0
+        summ, qkn = ref_modules(cfg, inp)
+        cos, sin = orc.rope_tables(n, c["head_dim"], c["rope_theta"])
+        q, k, v = T(inp["q"]), T(inp["k"]), T(inp["v"])
+        B, Hq, Hkv, dh, Bk = 1, c["n_heads"], c["n_kv"], c["head_dim"], c["block"]
+        G = Hq // Hkv
+        nb = n // Bk
+        with torch.no_grad():
+            qc, kc, _ = ref_attn._content_qk(q, k, cfg, qkn, n)
+            scale = (ref_attn.content_scale(cfg, dh) * ref_attn.log_len_tau(cfg, n)) if qk else dh ** -0.5
+            cand = ref_attn._route_candidates(n, c["window"], nb, Bk, "cpu")
+            qn = qc.view(B, n, Hkv, G, dh).permute(0, 2, 3, 1, 4).contiguous()
+            kt = kc.permute(0, 2, 3, 1).unsqueeze(2).contiguous()
+            pstar = ref_attn._teacher_chunk(qn, kt, cand, scale, Bk)
+            _, bsc = ref_attn.route_topk(qc, kc, cfg, summ, cand)
+        with torch.enable_grad():
+            _, aux = ref_attn.hba_attention_dense(q, k, v, T(cos), T(sin), cfg, summ, qkn)
+            aux.backward()
+        out(f"aux_{name}", pstar=pstar.numpy(), bsc=bsc.numpy(), aux=np.array(float(aux)),
+            dprobes=summ.probes.grad.numpy(), dproj=summ.proj.grad.numpy())
+
+
 if __name__ == "__main__":
     main()
     backward_cases()
+    aux_cases()

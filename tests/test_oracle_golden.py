@@ -166,3 +166,26 @@ def test_backward_matches_reference_autograd(name, c, n, seed, qk):
         assert err <= 1e-4 * max(1.0, np.abs(ref).max()), (key, err)
     np.testing.assert_allclose(res["dq_gain"], g["dq_gain"], rtol=1e-4, atol=1e-4)
     np.testing.assert_allclose(res["dk_gain"], g["dk_gain"], rtol=1e-4, atol=1e-4)
+
+
+@pytest.mark.parametrize("name,c,n,seed,qk", cases.AUX_CASES, ids=[x[0] for x in cases.AUX_CASES])
+def test_aux_teacher_and_kl_match_reference(name, c, n, seed, qk):
+    """The oracle's aux-KL teacher (pstar) and loss against the reference's
+    own (_teacher_chunk as _aux_kl_chunked calls it; hba_attention_dense's
+    aux with route_topk's block scores), fp32."""
+    g = load(f"aux_{name}")
+    inp = cases.bwd_case_inputs(c, n, seed)
+    cfg = cases.cfg_dict(c, qk)
+    dh = c["head_dim"]
+    if qk:
+        qc = orc.head_rmsnorm(inp["q"], inp["q_gain"])
+        kc = orc.head_rmsnorm(inp["k"], inp["k_gain"])
+    else:
+        qc, kc = inp["q"], inp["k"]
+    scale = orc.union_scale(qk, c["content_scale_mode"], c["temp_c"], c["n_cal"], c["native_ctx"], dh, n)
+    pstar = orc.aux_teacher(qc, kc, cfg, scale)
+    cand = orc.route_candidates(np.arange(n), c["window"], n // c["block"], c["block"])
+    rows = cand.any(-1)
+    assert rows.any()
+    np.testing.assert_allclose(pstar[:, :, rows], g["pstar"][:, :, rows], rtol=1e-4, atol=1e-6)
+    assert abs(orc.aux_kl(pstar, g["bsc"], cand) - float(g["aux"])) <= 1e-5 * max(1.0, abs(float(g["aux"])))
