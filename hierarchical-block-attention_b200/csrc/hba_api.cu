@@ -718,6 +718,68 @@ int hba_b200_prefill_range(const hba_b200_config* cfg, int32_t batch, int32_t n,
 }
 
 
+// ---- the summarizer's aux-KL teacher ----
+
+size_t hba_b200_aux_teacher_workspace_size(const hba_b200_config* cfg, int32_t batch, int32_t n) {
+  int st = HBA_B200_OK;
+  if (!config_ok(cfg, &st) || cfg->hier || batch <= 0 || n <= 0 || n % cfg->block != 0) return 0;
+  const Geom geo = make_geom(cfg, batch, n, n);
+  if (!hba::aux_teacher_supported(geo, cfg->head_dim, n)) return 0;
+  const size_t kv = (size_t)batch * n * cfg->n_kv * cfg->head_dim;
+  const size_t qv = (size_t)batch * n * cfg->n_heads * cfg->head_dim;
+  return kAlign + 3 * align_up(kv * 2) + align_up(qv * 2);  // status; keys plain, chunk-tiled, RoPE'd tiled; queries
+}
+
+int hba_b200_aux_teacher(const hba_b200_config* cfg, int32_t batch, int32_t n, float scale, const void* q,
+                         const void* k, const float* cos, const float* sin, const float* q_gain, const float* k_gain,
+                         float* pstar, void* workspace, size_t workspace_bytes, cudaStream_t stream) {
+  int st = HBA_B200_OK;
+  if (!config_ok(cfg, &st)) return st;
+  if (batch <= 0 || n <= 0 || q == nullptr || k == nullptr || cos == nullptr || sin == nullptr || pstar == nullptr ||
+      (cfg->qknorm && (q_gain == nullptr || k_gain == nullptr)) || !std::isfinite(scale))
+    return HBA_B200_ERR_INVALID_ARGUMENT;
+  if (n % cfg->block != 0) return HBA_B200_ERR_NOT_BLOCK_MULTIPLE;
+  if (cfg->hier) return HBA_B200_ERR_UNSUPPORTED;
+  const int dh = cfg->head_dim;
+  const Geom geo = make_geom(cfg, batch, n, n);
+  if (!hba::aux_teacher_supported(geo, dh, n)) return HBA_B200_ERR_UNSUPPORTED;
+  const size_t need = hba_b200_aux_teacher_workspace_size(cfg, batch, n);
+  if (workspace == nullptr || workspace_bytes < need) return HBA_B200_ERR_WORKSPACE;
+  const size_t kv = (size_t)batch * n * cfg->n_kv * dh;
+  const size_t qv = (size_t)batch * n * cfg->n_heads * dh;
+  unsigned char* ws = static_cast<unsigned char*>(workspace);
+  int* dev_status = reinterpret_cast<int*>(ws);
+  ws += kAlign;
+  auto carve = [&](size_t bytes) {
+    unsigned char* p = ws;
+    ws += align_up(bytes);
+    return p;
+  };
+  auto* kc = reinterpret_cast<__nv_bfloat16*>(carve(kv * 2));
+  auto* kc_sw = reinterpret_cast<__nv_bfloat16*>(carve(kv * 2));
+  auto* kr_sw = reinterpret_cast<__nv_bfloat16*>(carve(kv * 2));
+  auto* qcn = reinterpret_cast<__nv_bfloat16*>(carve(qv * 2));
+  const size_t nb = (size_t)n / cfg->block;
+  prof_begin(stream);
+  cudaError_t e = cudaMemsetAsync(dev_status, 0, sizeof(int), stream);
+  if (e == cudaSuccess) e = cudaMemsetAsync(pstar, 0, (size_t)batch * cfg->n_kv * n * nb * sizeof(float), stream);
+  if (e == cudaSuccess)
+    e = hba::launch_qknorm_rope(geo, n, static_cast<const __nv_bfloat16*>(k), k_gain, cos, sin, kc, nullptr, dh, stream,
+                                nullptr, kc_sw, kr_sw, nullptr);
+  const __nv_bfloat16* qsrc = static_cast<const __nv_bfloat16*>(q);
+  if (e == cudaSuccess && cfg->qknorm) {
+    e = hba::launch_qknorm(qsrc, qcn, q_gain, (int64_t)batch * n, cfg->n_heads, dh, cfg->eps, stream);
+    qsrc = qcn;
+  }
+  if (e != cudaSuccess) return cuda_status(e);
+  prof_mark(stream);
+  e = hba::launch_aux_teacher(geo, dh, n, scale, qsrc, kc_sw, pstar, dev_status, stream);
+  if (e != cudaSuccess) return cuda_status(e);
+  prof_mark(stream);
+  g_last_kernels = cfg->qknorm ? "qknorm_rope_kernel+qknorm_kernel+aux_teacher_kernel" : "qknorm_rope_kernel+aux_teacher_kernel";
+  return HBA_B200_OK;
+}
+
 // ---- prefill backward ----
 
 size_t hba_b200_prefill_backward_workspace_size(const hba_b200_config* cfg, int32_t batch, int32_t n) {

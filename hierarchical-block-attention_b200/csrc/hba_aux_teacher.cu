@@ -1,0 +1,290 @@
+// The summarizer's auxiliary-loss teacher on the 5th-generation tensor cores
+// (reference: _teacher_chunk / _aux_kl_chunked, src/hba/attention.py:476-529;
+// the same distribution as hba_attention_dense's teacher, :364-369).
+//
+// For query i of a KV head, over the NoPE logits scale * qc_h . kc of every
+// key of its candidate blocks (blocks 1 .. bmax(i), wholly before the
+// window), head h's softmax mass of block b is
+//     p_h(i, b) = sum_{keys j in b} exp(s_h(i, j) - LSE_h(i)),
+// LSE_h(i) the log-sum-exp over all candidate keys (the reference's softmax
+// over blockwise LSEs); the teacher is the mean over the group's G heads,
+// pstar(i, b) = mean_h p_h(i, b).  It sums to 1 over blocks by construction
+// (the reference's renormalisation only corrects rounding, and is not
+// repeated here); non-candidate blocks and queries with no candidate are 0.
+//
+// One CTA per (sequence, kv head, tile of QT = 128/G queries x G heads = the
+// 128 rows of the UMMA M dimension).  The tile's candidate blocks are walked
+// twice in 128-key chunks (two 64-key blocks each): S = Q K^T (M 128 rows, N
+// 128 keys, K dh) into one of two TMEM buffers, so the next chunk's MMA runs
+// while the row warps read one.
+//   pass 1: per row the running maximum and sum of 2^(s log2e - m) over its
+//           valid keys -> LSE (log2 units);
+//   pass 2: per row and block the mass 2^(s log2e - LSE), then the mean over
+//           the G rows of each query (through shared memory) -> pstar.
+// Roles (192 threads): warps 0-3 one row each per lane (TMEM lane = row);
+// warp 4 loads (the query tile by TMA, K chunks by 1-D bulk copies of the
+// pre-pass's chunk-tiled keys through a ring); warp 5 issues the MMAs and owns
+// TMEM.  Every mbarrier wait is bounded; a timeout sets *err and drains.
+#include <climits>
+#include <cudaTypedefs.h>
+
+#include "hba_common.cuh"
+#include "hba_internal.h"
+#include "hba_score.cuh"
+#include "hba_sm100.cuh"
+
+namespace hba {
+
+using namespace sm100;
+
+constexpr int kAtThreads = 192;
+constexpr int kAtLoad = 4;
+constexpr int kAtMma = 5;
+constexpr int kAtBlock = 64;
+constexpr int kAtKeys = 128;
+
+template <int DH>
+struct AtSmem {
+  static constexpr int HALVES = DH / 64;
+  static constexpr int QBYTES = HALVES * 16384;  // [128 rows x DH], swizzled per 64-dim group
+  static constexpr int GBYTES = kAtKeys * 128;   // one dim group of a K chunk
+  static constexpr int KT = HALVES * GBYTES;
+  static constexpr int NSLOT = DH == 64 ? 8 : 4;
+  alignas(1024) unsigned char q[QBYTES];
+  alignas(1024) unsigned char ring[NSLOT][KT];
+  float mass[2][2][128];  // pass 2: [chunk parity][block half][row]
+  uint64_t q_ready, full[NSLOT], empty[NSLOT], s_full[2], s_free[2], mass_full[2], drain;
+  uint32_t tmem_base;
+};
+
+static_assert(sizeof(AtSmem<128>) + 1024 <= 232448 && sizeof(AtSmem<64>) + 1024 <= 232448,
+              "teacher tile set exceeds the 227 KB of shared memory");
+
+struct AuxTeacherParams {
+  Geom geo;
+  int n;
+  float scale;
+  int QT;
+  int tiles;
+  const __nv_bfloat16* kc;  // chunk-tiled QKNorm'd (or raw) keys
+  float* pstar;             // [B, Hkv, n, nb], zeroed by the host
+  int* err;
+};
+
+template <int DH>
+__global__ void __launch_bounds__(kAtThreads, 1)
+    aux_teacher_kernel(const __grid_constant__ CUtensorMap tm_q, AuxTeacherParams p) {
+  using SM = AtSmem<DH>;
+  extern __shared__ __align__(1024) unsigned char smem_raw[];
+  SM& sm = *reinterpret_cast<SM*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  constexpr int HALVES = SM::HALVES;
+  constexpr int NSLOT = SM::NSLOT;
+  const Geom& geo = p.geo;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int G = geo.G, QT = p.QT, n = p.n;
+  const int tile = p.tiles - 1 - (int)(blockIdx.x % p.tiles);  // the latest (longest) tiles first
+  const int bg = blockIdx.x / p.tiles;
+  const int b = bg / geo.Hkv, g = bg % geo.Hkv;
+  const int i0 = tile * QT;
+  const int nq = min(QT, n - i0);
+  const int nb = n / kAtBlock;
+  auto bmax_of = [&](int i) { return min(last_candidate(i, geo.W, kAtBlock), nb - 1); };
+  const int bmaxT = bmax_of(i0 + nq - 1);      // the tile's last candidate block (0: none)
+  const int NCH = bmaxT >= 1 ? (bmaxT + 1) / 2 : 0;  // chunk c: blocks 1 + 2c, 2 + 2c
+  if (NCH == 0) return;                         // no candidate anywhere in the tile: pstar stays 0
+
+  if (tid == kAtLoad * 32) {
+    mbar_init(&sm.q_ready, 1);
+    for (int s = 0; s < NSLOT; ++s) {
+      mbar_init(&sm.full[s], 1);
+      mbar_init(&sm.empty[s], 1);
+    }
+    for (int s = 0; s < 2; ++s) {
+      mbar_init(&sm.s_full[s], 1);
+      mbar_init(&sm.s_free[s], 128);
+      mbar_init(&sm.mass_full[s], 128);
+    }
+    mbar_init(&sm.drain, 1);
+    fence_barrier_init();
+    mbar_arrive_expect_tx(&sm.q_ready, (uint32_t)(HALVES * G * QT * 128));
+    for (int h = 0; h < HALVES; ++h) tma_load_4d(sm.q + h * 16384, &tm_q, h * 64, g * G, i0, b, &sm.q_ready);
+  }
+  if (warp == kAtMma) {
+    tmem_alloc(&sm.tmem_base, 256);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = sm.tmem_base;
+  const int NIT = 2 * NCH;  // item it: chunk it % NCH, pass it / NCH
+
+  if (warp == kAtLoad) {
+    if (lane == 0) {
+      const __nv_bfloat16* kc_bg = p.kc + (size_t)bg * n * DH;
+      for (int it = 0; it < NIT; ++it) {
+        const int st = it % NSLOT;
+        if (it >= NSLOT && !mbar_wait(&sm.empty[st], ((it / NSLOT) - 1) & 1, p.err)) break;
+        const int c = it % NCH;
+        const int blk0 = 1 + 2 * c, blk1 = min(2 + 2 * c, bmaxT);  // past the last candidate: a valid block, masked
+        mbar_arrive_expect_tx(&sm.full[st], SM::KT);
+#pragma unroll
+        for (int dg = 0; dg < HALVES; ++dg) {
+          unsigned char* dst = sm.ring[st] + dg * SM::GBYTES;
+          bulk_load(dst, kc_bg + ((size_t)blk0 * HALVES + dg) * 4096, 8192, &sm.full[st]);
+          bulk_load(dst + 8192, kc_bg + ((size_t)blk1 * HALVES + dg) * 4096, 8192, &sm.full[st]);
+        }
+      }
+    }
+  } else if (warp == kAtMma) {
+    constexpr uint32_t idesc = idesc_bf16(128, kAtKeys, false, false);
+    auto wwait = [&](uint64_t* bar, uint32_t parity) {
+      return __all_sync(0xffffffffu, mbar_wait(bar, parity, p.err));
+    };
+    bool ok = wwait(&sm.q_ready, 0);
+    const uint64_t qdesc = sdesc_sw128(smem_u32(sm.q), 16, 1024);
+    for (int it = 0; ok && it < NIT; ++it) {
+      const int st = it % NSLOT, sb = it & 1;
+      if (!wwait(&sm.full[st], (it / NSLOT) & 1)) break;
+      if (it >= 2 && !wwait(&sm.s_free[sb], ((it - 2) >> 1) & 1)) break;
+      tc_fence_after();
+      const uint64_t kdesc = sdesc_sw128(smem_u32(sm.ring[st]), 16, 1024);
+      if (elect_one_sync()) {
+#pragma unroll
+        for (int kk = 0; kk < DH / 16; ++kk) {
+          const int h = kk >> 2, ko = (kk & 3) * 32;
+          umma_f16(tmem + (uint32_t)(sb * kAtKeys), qdesc + (uint64_t)((h * 16384 + ko) >> 4),
+                   kdesc + (uint64_t)((h * SM::GBYTES + ko) >> 4), idesc, kk > 0 ? 1u : 0u);
+        }
+        umma_commit(&sm.s_full[sb]);
+        umma_commit(&sm.empty[st]);
+      }
+      __syncwarp();
+    }
+    if (elect_one_sync()) umma_commit(&sm.drain);
+    __syncwarp();
+    wwait(&sm.drain, 0);
+  } else {
+    // ---------------- row warps: row r = TMEM lane ----------------
+    const int r = tid;
+    const int qt = r / G;
+    const bool row_ok = r < G * QT && qt < nq;
+    const int bmax = row_ok ? bmax_of(i0 + qt) : 0;  // the row's last candidate block (0: none)
+    const uint32_t lane_off = (uint32_t)(warp * 32) << 16;
+    const float sl2 = p.scale * kLog2e;
+    float m = neg_inf(), l = 0.f, lse2 = neg_inf();
+    bool ok = true;
+    for (int it = 0; it < NIT; ++it) {
+      const int sb = it & 1, c = it % NCH;
+      const bool pass2 = it >= NCH;
+      if (pass2 && it == NCH) lse2 = l > 0.f ? m + log2f(l) : neg_inf();
+      if (!__all_sync(0xffffffffu, mbar_wait(&sm.s_full[sb], (it >> 1) & 1, p.err))) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      float mass0 = 0.f, mass1 = 0.f;
+#pragma unroll 1
+      for (int pc = 0; pc < 4; ++pc) {  // 32 columns: half pc / 2 of the chunk
+        float v[32];
+        tmem_ld32(tmem + (uint32_t)(sb * kAtKeys + 32 * pc) + lane_off, v);
+        tmem_ld_wait();
+        const bool valid = 1 + 2 * c + (pc >> 1) <= bmax;  // the whole half is one block
+        if (!valid) continue;
+        if (!pass2) {
+          float mx = neg_inf();
+#pragma unroll
+          for (int e = 0; e < 32; ++e) mx = fmaxf(mx, v[e] * sl2);
+          const float mn = fmaxf(m, mx);
+          float sum = 0.f;
+#pragma unroll
+          for (int e = 0; e < 32; ++e) sum += ex2_approx(fmaf(v[e], sl2, -mn));
+          l = l * ex2_approx(m - mn) + sum;  // m = -inf at the first valid piece: 2^-inf = 0
+          m = mn;
+        } else {
+          float sum = 0.f;
+#pragma unroll
+          for (int e = 0; e < 32; ++e) sum += ex2_approx(fmaf(v[e], sl2, -lse2));
+          if (pc < 2)
+            mass0 += sum;
+          else
+            mass1 += sum;
+        }
+      }
+      tc_fence_before();
+      mbar_arrive(&sm.s_free[sb]);
+      if (pass2) {
+        // the mean over the G rows (heads) of each query -> pstar.  The
+        // arrays alternate by chunk parity: every row thread waits for chunk
+        // j's masses before writing chunk j + 1's, so chunk j + 2 overwrites
+        // parity j only after every thread has read chunk j.
+        const int j = c, pj = j & 1;
+        sm.mass[pj][0][r] = mass0;
+        sm.mass[pj][1][r] = mass1;
+        mbar_arrive(&sm.mass_full[pj]);
+        if (!__all_sync(0xffffffffu, mbar_wait(&sm.mass_full[pj], (j >> 1) & 1, p.err))) {
+          ok = false;
+          break;
+        }
+        for (int e = r; e < 2 * nq; e += 128) {
+          const int q_ = e >> 1, h = e & 1;
+          const int blk = 1 + 2 * c + h;
+          if (blk <= bmaxT) {
+            float s = 0.f;
+            for (int hh = 0; hh < G; ++hh) s += sm.mass[pj][h][q_ * G + hh];
+            p.pstar[((size_t)bg * n + i0 + q_) * nb + blk] = s / (float)G;
+          }
+        }
+      }
+    }
+    if (!ok && r == 0) atomicExch(p.err, 1);
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == kAtMma) tmem_dealloc(tmem, 256);
+}
+
+// ---------------------------------------------------------------- host ----
+bool make_map(CUtensorMap* m, const void* base, int B, int n, int H, int dh, int box_h, int box_n);
+
+bool aux_teacher_supported(const Geom& geo, int dh, int n) {
+  return !geo.hier && (dh == 64 || dh == 128) && geo.Bk == kAtBlock && n % kAtBlock == 0 && geo.G >= 1 &&
+         geo.G <= 16;
+}
+
+cudaError_t launch_aux_teacher(const Geom& geo, int dh, int n, float scale, const __nv_bfloat16* qc,
+                               const __nv_bfloat16* kc_sw, float* pstar, int* err, cudaStream_t st) {
+  const int QT = 128 / geo.G;
+  CUtensorMap m_q;
+  if ((reinterpret_cast<uintptr_t>(kc_sw) & 15u) != 0 || !make_map(&m_q, qc, geo.B, n, geo.Hq, dh, geo.G, QT))
+    return cudaErrorInvalidValue;
+  AuxTeacherParams p{};
+  p.geo = geo;
+  p.n = n;
+  p.scale = scale;
+  p.QT = QT;
+  p.tiles = (n + QT - 1) / QT;
+  p.kc = kc_sw;
+  p.pstar = pstar;
+  p.err = err;
+  const long long grid = (long long)geo.B * geo.Hkv * p.tiles;
+  if (grid <= 0) return cudaSuccess;
+  if (grid > INT32_MAX) return cudaErrorInvalidValue;
+  if (dh == 64) {
+    const size_t smem = sizeof(AtSmem<64>) + 1024;
+    static const cudaError_t attr =
+        cudaFuncSetAttribute(aux_teacher_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (attr != cudaSuccess) return attr;
+    aux_teacher_kernel<64><<<(unsigned)grid, kAtThreads, smem, st>>>(m_q, p);
+  } else {
+    const size_t smem = sizeof(AtSmem<128>) + 1024;
+    static const cudaError_t attr =
+        cudaFuncSetAttribute(aux_teacher_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (attr != cudaSuccess) return attr;
+    aux_teacher_kernel<128><<<(unsigned)grid, kAtThreads, smem, st>>>(m_q, p);
+  }
+  return cudaGetLastError();
+}
+
+}  // namespace hba

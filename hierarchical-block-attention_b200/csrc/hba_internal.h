@@ -211,6 +211,12 @@ cudaError_t launch_prefill_tc(const Geom& geo, int dh, int n, int q_off, float s
                               unsigned long long* trace, long long trace_rows, cudaStream_t st);
 // CTAs the decode attention grid should have for this device (all resident at once).
 int decode_attend_grid(int dh, int total_chunks);
+// The summarizer's aux-KL teacher (hba_aux_teacher.cu): qc [B, n, Hq, dh]
+// bf16 (QKNorm'd or raw queries), kc_sw the chunk-tiled keys; pstar [B, Hkv,
+// n, nb] fp32, zeroed first.
+bool aux_teacher_supported(const Geom& geo, int dh, int n);
+cudaError_t launch_aux_teacher(const Geom& geo, int dh, int n, float scale, const __nv_bfloat16* qc,
+                               const __nv_bfloat16* kc_sw, float* pstar, int* err, cudaStream_t st);
 // Backward of the prefill union softmax (hba_prefill_bwd.cu).
 bool prefill_bwd_supported(const Geom& geo, int dh, int n);
 // delta[b, h, t] = sum_d dout * out over rows (b, t, h) of [B, n, H, dh] bf16.

@@ -90,6 +90,9 @@ SIGNATURES = {
     # sel_score, workspace, workspace_bytes, stream
     "hba_b200_prefill_range": (ctypes.c_int, [_CFG, _I32, _I32, _I32, _I32, _F, _P, _P, _P, _P, _P, _P, _P, _P, _P,
                                               _P, _P, _P, _P, _P, _SZ, _P]),
+    "hba_b200_aux_teacher_workspace_size": (_SZ, [_CFG, _I32, _I32]),
+    # cfg, batch, n, scale, q, k, cos, sin, q_gain, k_gain, pstar, workspace, workspace_bytes, stream
+    "hba_b200_aux_teacher": (ctypes.c_int, [_CFG, _I32, _I32, _F, _P, _P, _P, _P, _P, _P, _P, _P, _SZ, _P]),
     "hba_b200_prefill_backward_workspace_size": (_SZ, [_CFG, _I32, _I32]),
     # cfg, batch, n, scale, q, k, v, cos, sin, q_gain, k_gain, out, lse, sel_idx, dout, dq, dk, dv, dq_gain,
     # dk_gain, workspace, workspace_bytes, stream

@@ -6,10 +6,12 @@ Signatures and argument meaning follow the reference's
 * ``hba_attention_b200`` replaces ``hba_attention_eval(q, k, v, cos, sin, cfg,
   summ, qkn, cap, hier=False, equiv=False)`` (attention.py:610-713);
 * ``hba_attention_b200_fused`` replaces ``hba_attention_fused`` /
-  ``hba_attention_dense`` (attention.py:552, :306), returning ``(out, aux)``
-  with a zero aux (the summarizer's aux-KL teacher is not built); it is
-  differentiable in q, k, v and the QKNorm gains through the CUDA backward
-  (``hba_b200_prefill_backward``).
+  ``hba_attention_dense`` (attention.py:552, :306), returning ``(out, aux)``:
+  out is differentiable in q, k, v and the QKNorm gains through the CUDA
+  backward (``hba_b200_prefill_backward``); aux is the summarizer's aux-KL
+  loss (its teacher on the tensor cores, ``hba_b200_aux_teacher``),
+  differentiable in the summarizer's probes and proj, or zero when
+  ``cfg.aux_w == 0``.
 
 ``cfg`` is any object with the reference ``HBAConfig`` field names,
 ``summ`` a module holding ``probes [Hkv, m, dh]`` and ``proj [Hkv, dh, dh]``,
@@ -188,15 +190,94 @@ def hba_attention_b200_fused(q, k, v, cos, sin, cfg, summ, qkn):
     attention.py:552 / hba_attention_dense :306): the same union softmax,
     differentiable in q, k, v and the QKNorm gains ``qkn.q.gain`` /
     ``qkn.k.gain`` (the block selection, a top-k, has none, as in the
-    reference).  aux is a zero scalar: the summarizer's aux-KL teacher
-    (attention.py:478-549) is not built."""
+    reference); aux the summarizer's aux-KL loss (``summarizer_aux_kl``), or
+    a zero scalar when ``cfg.aux_w == 0`` (the reference's stage-3 skip,
+    attention.py:604-606)."""
     qg, kg = qkn.q.gain, qkn.k.gain
     needs = [t.requires_grad for t in (q, k, v, qg, kg)]
     if torch.is_grad_enabled() and any(needs):
         out = _UnionSoftmax.apply(q, k, v, qg, kg, cos, sin, cfg, summ)
     else:
         out = hba_attention_b200(q, k, v, cos, sin, cfg, summ, qkn)
-    return out, q.new_zeros(())
+    if getattr(cfg, "aux_w", 1.0) == 0.0:
+        return out, q.new_zeros(())
+    return out, summarizer_aux_kl(q, k, cos, sin, cfg, summ, qkn)
+
+
+def route_scale(cfg, dh):
+    """The routing scores' scale (route_topk, attention.py:294): the content
+    scale without the length temperature under QKNorm, dh**-0.5 without."""
+    return content_scale(cfg, dh) if getattr(cfg, "qknorm", False) else dh ** -0.5
+
+
+def aux_teacher_b200(q, k, cos, sin, cfg, qkn):
+    """The aux-KL teacher pstar [B, Hkv, n, n / block] fp32 (reference
+    _teacher_chunk / _aux_kl_chunked, attention.py:476-529) from raw q, k:
+    per query and kv head, the group-mean of each candidate block's share of
+    the NoPE softmax over all candidate keys (tensor-core kernel,
+    ``hba_b200_aux_teacher``); 0 for non-candidate blocks and for queries
+    without candidates (the reference's NaN rows, which its loss skips)."""
+    _need_cuda(q, k)
+    B, n, Hq, dh = q.shape
+    Hkv = k.shape[2]
+    dev = q.device
+    with torch.cuda.device(dev), torch.no_grad():
+        qb, kb = as_bf16(q), as_bf16(k)
+        cs, sn = as_f32(cos[:n], dev), as_f32(sin[:n], dev)
+        qg, kg = gains(qkn, dev)
+        c = c_config(cfg, False)
+        L = _lib.load()
+        ws_bytes = L.hba_b200_aux_teacher_workspace_size(ctypes.byref(c), B, n)
+        if ws_bytes == 0:
+            _lib.check(_lib.ERR_UNSUPPORTED if n % cfg.block == 0 else _lib.ERR_NOT_BLOCK_MULTIPLE,
+                       "hba_b200_aux_teacher_workspace_size")
+        ws = torch.empty(ws_bytes, dtype=torch.uint8, device=dev)
+        pstar = torch.empty(B, Hkv, n, n // cfg.block, dtype=torch.float32, device=dev)
+        st = L.hba_b200_aux_teacher(ctypes.byref(c), B, n, ctypes.c_float(union_scale(cfg, dh, n)), ptr(qb), ptr(kb),
+                                    ptr(cs), ptr(sn), ptr(qg), ptr(kg), ptr(pstar), ptr(ws), ws_bytes, stream_of(dev))
+        _lib.check(st, "hba_b200_aux_teacher")
+        _lib.check_device(ptr(ws), stream_of(dev), "hba_b200_aux_teacher (device status)")
+    return pstar
+
+
+def summarizer_aux_kl(q, k, cos, sin, cfg, summ, qkn):
+    """The summarizer's auxiliary KL (reference _aux_kl_chunked,
+    attention.py:501-537; hba_attention_dense :364-383): -mean over (batch,
+    kv head, query with a candidate) of sum_blocks pstar * log_softmax(bsc),
+    pstar the teacher (``aux_teacher_b200``, no gradient) and bsc route_topk's
+    block scores (attention.py:294-298: the grouped QKNorm'd query against
+    the slot summaries of the QKNorm'd keys, both detached, max over slots,
+    x ``route_scale``, non-candidates -inf).  The loss reaches only the
+    summarizer's probes and proj, as in the reference; the summaries and
+    scores are evaluated in fp32 by torch (the teacher is the O(n^2) part)."""
+    B, n, Hq, dh = q.shape
+    Hkv = k.shape[2]
+    G, Bk = Hq // Hkv, cfg.block
+    nb = n // Bk
+    pstar = aux_teacher_b200(q, k, cos, sin, cfg, qkn)
+    with torch.no_grad():
+        if getattr(cfg, "qknorm", False):
+            from .ops import qknorm_b200
+            qc, kc = qknorm_b200(q, qkn.q.gain), qknorm_b200(k, qkn.k.gain)
+        else:
+            qc, kc = q.detach(), k.detach()
+        qgr = qc.float().view(B, n, Hkv, G, dh).sum(3).transpose(1, 2)           # grouped query [B, Hkv, n, dh]
+        kblk = kc.float().view(B, nb, Bk, Hkv, dh)
+    probes, proj = summ.probes.float(), summ.proj.float()
+    att = (torch.einsum("hmd,bckhd->bhcmk", probes, kblk) * dh ** -0.5).softmax(-1)
+    S = torch.einsum("bhcmd,hde->bhcme", torch.einsum("bhcmk,bckhd->bhcmd", att, kblk), proj)
+    bsc = torch.einsum("bhid,bhcmd->bhicm", qgr, S).amax(-1) * route_scale(cfg, dh)
+    i = torch.arange(n, device=q.device)[:, None]
+    blk = torch.arange(nb, device=q.device)[None, :]
+    cand = (blk >= 1) & ((blk + 1) * Bk <= i - cfg.window + 1)                      # attention.py:250-256
+    bsc = bsc.masked_fill(~cand[None, None], float("-inf"))
+    vq = cand.any(-1)
+    if not bool(vq.any()):
+        return q.new_zeros(())
+    logp = torch.log_softmax(bsc[:, :, vq], dim=-1)
+    pv = pstar[:, :, vq]
+    term = torch.where(pv > 0, pv * logp, torch.zeros_like(logp))
+    return -term.sum(-1).mean()
 
 
 class _Gains:

@@ -238,6 +238,24 @@ int hba_b200_prefill_range(const hba_b200_config* cfg, int32_t batch, int32_t n,
                            void* workspace, size_t workspace_bytes, cudaStream_t stream);
 
 /*
+ * The summarizer's auxiliary-loss teacher (reference: _teacher_chunk /
+ * _aux_kl_chunked, src/hba/attention.py:476-529): for every query position i
+ * and kv head, the mean over the group's query heads of each candidate
+ * block's share of the softmax over all candidate keys (NoPE logits scale *
+ * QKNorm(q) . QKNorm(k), candidates the blocks 1 .. wholly before the
+ * window).  pstar: [batch, Hkv, n, n / block] fp32, written whole (0 for
+ * non-candidate blocks and for queries with no candidate, where the
+ * reference's rows are NaN and its loss skips them).  scale: the union's
+ * (content scale x tau(n) under QKNorm, dh**-0.5 without).  cos / sin feed
+ * the shared key pre-pass.  Block 64, dh 64 / 128, flat configs;
+ * HBA_B200_ERR_UNSUPPORTED otherwise.  O(n^2): training only.
+ */
+size_t hba_b200_aux_teacher_workspace_size(const hba_b200_config* cfg, int32_t batch, int32_t n);
+int hba_b200_aux_teacher(const hba_b200_config* cfg, int32_t batch, int32_t n, float scale, const void* q,
+                         const void* k, const float* cos, const float* sin, const float* q_gain, const float* k_gain,
+                         float* pstar, void* workspace, size_t workspace_bytes, cudaStream_t stream);
+
+/*
  * Backward of the prefill union softmax: the gradients that autograd takes
  * through the reference's training attention, hba_attention_fused
  * (src/hba/attention.py:552-607; equal to hba_attention_dense, :306-389),

@@ -36,6 +36,7 @@ def _close(name, got, ref):
 
 
 def run_backward(cfg, B, n, seed, gains=True):
+    cfg.aux_w = 0.0  # the attention's gradients alone (the aux-KL has its own tests)
     summ, qkn = synth.make_weights(cfg, "cuda", seed=seed, gains=gains)
     cos, sin = synth.rope_tables(n, cfg.head_dim, 1e6)
     wl = synth.prefill_workload(cfg, B, n, seed=seed)
@@ -117,7 +118,7 @@ def test_backward_replays_reference_fixture():
     inp = cases.bwd_case_inputs(c, n, seed)
     cfg = H.cfg_of(**{k_: c[k_] for k_ in ("n_heads", "n_kv", "head_dim", "block", "window", "sinks", "k_blocks",
                                            "slots", "fanout", "beam", "native_ctx", "content_scale_mode", "temp_c",
-                                           "n_cal")}, qknorm=qk)
+                                           "n_cal")}, qknorm=qk, aux_w=0.0)
     dev = "cuda"
     t = lambda a, dt=torch.bfloat16: torch.from_numpy(np.ascontiguousarray(a)).to(dev, dt)  # noqa: E731
     q, k, v = (t(inp[x]).requires_grad_(True) for x in ("q", "k", "v"))
@@ -168,7 +169,7 @@ def test_backward_reference_model_layer_trained_gains():
     c = d["cfg"]
     cfg = H.cfg_of(**{k_: c[k_] for k_ in ("n_heads", "n_kv", "head_dim", "block", "window", "sinks", "k_blocks",
                                            "slots", "fanout", "beam", "native_ctx", "qknorm", "content_scale_mode",
-                                           "temp_c", "n_cal")})
+                                           "temp_c", "n_cal")}, aux_w=0.0)
     n = d["q"].shape[1]
     dev = "cuda"
     t = lambda a, dt=torch.bfloat16: torch.from_numpy(np.ascontiguousarray(a)).to(dev, dt)  # noqa: E731
