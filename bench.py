@@ -1,7 +1,7 @@
 """Benchmark of the HBA attention hot path on B200.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference]
-                    [--config cfg1|cfg3|cfg2|cfg2-bwd|cfg3-shard|cfg4] [--no-secondary]
+                    [--config cfg1|cfg3|cfg2|cfg2-bwd|cfg2-aux|cfg3-shard|cfg4] [--no-secondary]
 
 Headline (default): BASELINE config 1 -- one decode step (grouped-query
 scoring of every candidate block summary, flat top-16, gather of the
@@ -18,7 +18,8 @@ region: the decode kernel reads and writes the mapped host buffers directly
 explicit H2D copy of q and D2H copy of out + LSE around the kernel (three
 graph nodes).  The secondary lines measure config 3 (hierarchical decode at
 128K), config 2 (prefill at 32K), the backward of that prefill (cfg2-bwd:
-dq, dk, dv and the QKNorm gains' gradients), and with N > 1 ranks config 3 with every
+dq, dk, dv and the QKNorm gains' gradients), the summarizer's aux-KL teacher
+at that shape (cfg2-aux), and with N > 1 ranks config 3 with every
 128K context sharded by token range over the N GPUs (one batch of 32
 sequences, strong scaling; the fused kernel exchanges the per-rank top-k
 lists and softmax partials over NVLink).  `--impl reference` times the CPU oracle port (the
@@ -51,9 +52,9 @@ def parse():
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
-    ap.add_argument("--config", default="cfg1", choices=["cfg1", "cfg2", "cfg2-bwd", "cfg3", "cfg3-shard", "cfg4"])
+    ap.add_argument("--config", default="cfg1", choices=["cfg1", "cfg2", "cfg2-bwd", "cfg2-aux", "cfg3", "cfg3-shard", "cfg4"])
     ap.add_argument("--no-secondary", action="store_true")
-    ap.add_argument("--ncu-case", default=None, choices=["cfg1", "cfg3", "cfg2", "cfg2-bwd"],
+    ap.add_argument("--ncu-case", default=None, choices=["cfg1", "cfg3", "cfg2", "cfg2-bwd", "cfg2-aux"],
                     help="profiling target: build this decode workload (cfg3 at batch 4) and run 3 decodes, "
                          "or (cfg2) one prefill forward; no timing, no output")
     return ap.parse_args()
@@ -273,6 +274,16 @@ def ncu_case(name, local):
     from hba_b200 import HBADecodeCache, baseline_config, synth
     from hba_b200.attention import stream_of
     dev = torch.device("cuda", local)
+    if name == "cfg2-aux":
+        # one aux-KL teacher of one cfg2 sequence (batch 1: ~1 GB on the device)
+        from hba_b200.attention import aux_teacher_b200
+        cfg, B, n, hier = baseline_config("cfg2")
+        summ, qkn = synth.make_weights(cfg, dev, seed=0, gains=True)
+        cos, sin = synth.rope_tables(n, cfg.head_dim, 1e6, dev)
+        wl = synth.prefill_workload(cfg, 1, n, seed=0, device=dev)
+        aux_teacher_b200(wl["q"], wl["k"], cos, sin, cfg, qkn)
+        torch.cuda.synchronize()
+        return
     if name == "cfg2-bwd":
         # one forward + backward of one cfg2 sequence (batch 1: ~4 GB on the device)
         from hba_b200 import hba_attention_b200_fused
@@ -811,6 +822,126 @@ def prefill_bwd_bench(name, steps, warmup, world, rank, local, pk):
     return res
 
 
+def aux_candidate_keys(cfg, n):
+    """Sum over query positions of the candidate keys the aux teacher scores
+    (every key of blocks 1 .. last_candidate(i))."""
+    i = np.arange(n)
+    lim = i - cfg.window + 1
+    bmax = np.where(lim >= 2 * cfg.block, lim // cfg.block - 1, 0)
+    return float((np.minimum(bmax, n // cfg.block - 1) * cfg.block).sum())
+
+
+def aux_teacher_bench(name, steps, warmup, world, rank, local, pk):
+    """The summarizer's aux-KL teacher (hba_b200_aux_teacher) at the cfg2
+    prefill shape: pstar [B, Hkv, n, nb] from q, k (O(n^2): two passes of
+    QK^T over every query's candidate keys)."""
+    from hba_b200 import baseline_config, synth
+    from hba_b200.attention import as_f32, c_config, gains, ptr, stream_of, union_scale
+    from hba_b200 import _lib
+    dev = torch.device("cuda", local)
+    cfg, B, n, hier = baseline_config(name)
+    dh, Hq, Hkv = cfg.head_dim, cfg.n_heads, cfg.n_kv
+    nb = n // cfg.block
+    summ, qkn = synth.make_weights(cfg, dev, seed=0, gains=True)
+    cos, sin = synth.rope_tables(n, dh, 1e6, dev)
+    wl = synth.prefill_workload(cfg, B, n, seed=4000 + rank, device=dev)
+    q, k = wl["q"], wl["k"]
+    del wl
+    c = c_config(cfg, False)
+    L = _lib.load()
+    qg, kg = gains(qkn, dev)
+    scale = union_scale(cfg, dh, n)
+    pstar = torch.empty(B, Hkv, n, nb, dtype=torch.float32, device=dev)
+    ws_bytes = L.hba_b200_aux_teacher_workspace_size(ctypes.byref(c), B, n)
+    ws = torch.empty(ws_bytes, dtype=torch.uint8, device=dev)
+    flush = torch.empty(FLUSH_BYTES // 4, dtype=torch.float32, device=dev)
+
+    def call(qq, kk):
+        st = L.hba_b200_aux_teacher(ctypes.byref(c), B, n, ctypes.c_float(scale), ptr(qq), ptr(kk), ptr(cos),
+                                    ptr(sin), ptr(qg), ptr(kg), ptr(pstar), ptr(ws), ws_bytes, stream_of(dev))
+        _lib.check(st, "hba_b200_aux_teacher")
+
+    def step():
+        call(q, k)
+
+    times, clocks, kt = timed_steps(step, steps, warmup, flush, world, dev, local, marks=3)
+    t_ms = max_over_ranks(statistics.mean(times), world, dev)
+    status = L.hba_b200_device_status(ptr(ws), 0, stream_of(dev))
+    keys = aux_candidate_keys(cfg, n)
+    flops = 4.0 * dh * Hq * B * keys  # two passes of QK^T over the candidate keys
+    main_ms = kt[1]
+    achieved = flops / (main_ms * 1e-3) / 1e12
+    qh, kh = q.cpu().pin_memory(), k.cpu().pin_memory()
+    ph = torch.empty(pstar.shape, dtype=pstar.dtype).pin_memory()
+
+    def step_e2e():
+        q.copy_(qh, non_blocking=True)
+        k.copy_(kh, non_blocking=True)
+        call(q, k)
+        ph.copy_(pstar, non_blocking=True)
+
+    e2e_times, _ = timed_steps(step_e2e, 2, 1, flush, world, dev, local)
+    e2e_ms = max_over_ranks(statistics.mean(e2e_times), world, dev)
+    res = dict(
+        metric="aux-KL teacher tokens/s", value=B * n * world / (t_ms * 1e-3), unit="aux teacher tokens/s",
+        n_gpus=world, steps=steps, warmup=warmup, ms_per_step=t_ms, higher_is_better=True, scaling="weak",
+        vs_baseline=None, dtype="bf16", data="synthetic (the cfg2 prefill workload's q, k; gains ~U(0.6, 1.6))",
+        config=dict(workload=f"{name}-aux: the summarizer's aux-KL teacher, batch {B}/rank, seq {n}, {Hq}/{Hkv} "
+                             f"heads, dh {dh}", batch_per_rank=B, seq_len=n, n_heads=Hq, n_kv=Hkv, head_dim=dh,
+                    l2="flushed (256 MB write) before every timed step",
+                    timing="eager C-ABI call per step, CUDA events; kernel times between the library's event marks"),
+        roofline=dict(bound="tensor", kernel="aux_teacher_kernel", achieved=achieved, peak=pk["bf16"], unit="TFLOP/s",
+                      frac=achieved / pk["bf16"], peak_source=pk["source"], traffic=traffic_of(f"aux_teacher_kernel_{name}"),
+                      algorithmic_flops=flops, kernel_ms=main_ms),
+        kernel_ms={"pre-pass": kt[0], "aux_teacher_kernel": kt[1]},
+        e2e=dict(value=B * n * world / (e2e_ms * 1e-3), unit="aux teacher tokens/s", ms_per_step=e2e_ms,
+                 h2d_bytes_per_step=q.numel() * 2 + k.numel() * 2, d2h_bytes_per_step=pstar.numel() * 4,
+                 timing="per step: pinned H2D of q, k, hba_b200_aux_teacher, pinned D2H of pstar"),
+        gpu_launches=steps * 3, device_status=status, clocks=clocks,
+    )
+    if rank == 0:
+        res["cpu_baseline"] = cpu_aux_sample(q, k, cfg, qkn, n, B, scale)
+    del q, k, ws, pstar, qh, kh, ph
+    torch.cuda.empty_cache()
+    return res
+
+
+def cpu_aux_sample(q, k, cfg, qkn, n, B, scale, rows=8):
+    """The oracle's teacher (numpy, one thread) for `rows` query positions of
+    one (sequence, kv head) (all its heads, scoring every key), projected
+    linearly to every row of the batch."""
+    from oracle import hba_oracle as orc
+    try:
+        from threadpoolctl import threadpool_limits
+    except Exception:  # pragma: no cover
+        threadpool_limits = None
+    G = cfg.n_heads // cfg.n_kv
+    r = np.random.default_rng(2)
+    rws = np.sort(r.choice(np.arange(cfg.window + 2 * cfg.block, n), size=rows, replace=False))
+    idx = torch.as_tensor(rws, device=q.device)
+    qg, kg = qkn.q.gain.float().cpu().numpy(), qkn.k.gain.float().cpu().numpy()
+    qs = q[0, idx, :G].float().cpu().numpy()
+    ks = k[0, :, :1].float().cpu().numpy()
+    ctx = threadpool_limits(limits=1) if threadpool_limits else None
+    if ctx:
+        ctx.__enter__()
+    try:
+        t0 = time.perf_counter()
+        qc = orc.head_rmsnorm(qs, qg[:G], bf16=True)
+        kc = orc.head_rmsnorm(ks, kg[:1], bf16=True)[:, 0]
+        orc.aux_teacher_rows(rws, qc, kc, dict(block=cfg.block, window=cfg.window), scale)
+        t_rows = time.perf_counter() - t0
+    finally:
+        if ctx:
+            ctx.__exit__(None, None, None)
+    t_full = B * cfg.n_kv * n * t_rows / rows
+    return dict(value=B * n / t_full, unit="aux teacher tokens/s", cores=1, kind="port",
+                sample=f"numpy oracle teacher, 1 thread: {rows} query rows (all {G} heads of one kv head, positions "
+                       f"past the window, every key scored as the reference does) of one sequence ({t_rows:.2f} s); "
+                       f"projected linearly to {B} x {cfg.n_kv} kv heads x {n} rows",
+                measured_s=t_rows, projected_s=t_full)
+
+
 class _AttnTimer:
     """CUDA events around every call of the wrapped function (the HBA
     attention of a layer); .ms() sums the closed intervals."""
@@ -1031,11 +1162,13 @@ def main():
         res = cfg4_bench(args.steps, args.warmup, world, rank, local, pk)
     elif args.config == "cfg2-bwd":
         res = prefill_bwd_bench("cfg2", args.steps, args.warmup, world, rank, local, pk)
+    elif args.config == "cfg2-aux":
+        res = aux_teacher_bench("cfg2", args.steps, args.warmup, world, rank, local, pk)
     else:
         res = prefill_bench(args.config, args.steps, args.warmup, world, rank, local, pk)
     if not args.no_secondary and args.config == "cfg1":
         sec = []
-        for name in ("cfg3", "cfg2", "cfg2-bwd") + (("cfg3-shard",) if world > 1 else ()):
+        for name in ("cfg3", "cfg2", "cfg2-bwd", "cfg2-aux") + (("cfg3-shard",) if world > 1 else ()):
             try:
                 if name == "cfg3":
                     sec.append(decode_bench(name, min(args.steps, 10), args.warmup, world, rank, local, pk))
@@ -1043,6 +1176,8 @@ def main():
                     sec.append(shard_bench("cfg3", min(args.steps, 10), args.warmup, world, rank, local, pk))
                 elif name == "cfg2-bwd":
                     sec.append(prefill_bwd_bench("cfg2", min(args.steps, 3), 3, world, rank, local, pk))
+                elif name == "cfg2-aux":
+                    sec.append(aux_teacher_bench("cfg2", min(args.steps, 3), 3, world, rank, local, pk))
                 else:
                     sec.append(prefill_bench(name, min(args.steps, 3), 3, world, rank, local, pk))
             except Exception as e:  # report, do not hide, a failing secondary

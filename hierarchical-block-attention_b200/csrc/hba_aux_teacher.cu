@@ -21,9 +21,11 @@
 //           valid keys -> LSE (log2 units);
 //   pass 2: per row and block the mass 2^(s log2e - LSE), then the mean over
 //           the G rows of each query (through shared memory) -> pstar.
-// Roles (192 threads): warps 0-3 one row each per lane (TMEM lane = row);
-// warp 4 loads (the query tile by TMA, K chunks by 1-D bulk copies of the
-// pre-pass's chunk-tiled keys through a ring); warp 5 issues the MMAs and owns
+// Roles (320 threads): warps 0-7 the rows (TMEM lane = row), two warps per
+// lane quarter, one per 64-key block of the chunk (one warp's exponentials
+// alone are latency-bound on the MUFU); warp 8 loads (the query tile by TMA,
+// K chunks by 1-D bulk copies of the pre-pass's chunk-tiled keys through a
+// ring); warp 9 issues the MMAs and owns
 // TMEM.  Every mbarrier wait is bounded; a timeout sets *err and drains.
 #include <climits>
 #include <cudaTypedefs.h>
@@ -37,9 +39,10 @@ namespace hba {
 
 using namespace sm100;
 
-constexpr int kAtThreads = 192;
-constexpr int kAtLoad = 4;
-constexpr int kAtMma = 5;
+constexpr int kAtThreads = 320;
+constexpr int kAtRowThreads = 256;  // warps 0-7: two per TMEM lane quarter, one per 64-key block of a chunk
+constexpr int kAtLoad = 8;
+constexpr int kAtMma = 9;
 constexpr int kAtBlock = 64;
 constexpr int kAtKeys = 128;
 
@@ -53,7 +56,8 @@ struct AtSmem {
   alignas(1024) unsigned char q[QBYTES];
   alignas(1024) unsigned char ring[NSLOT][KT];
   float mass[2][2][128];  // pass 2: [chunk parity][block half][row]
-  uint64_t q_ready, full[NSLOT], empty[NSLOT], s_full[2], s_free[2], mass_full[2], drain;
+  float ml[2][2][128];    // end of pass 1: [block half][m, l][row]
+  uint64_t q_ready, full[NSLOT], empty[NSLOT], s_full[2], s_free[2], mass_full[2], ml_full, drain;
   uint32_t tmem_base;
 };
 
@@ -101,9 +105,10 @@ __global__ void __launch_bounds__(kAtThreads, 1)
     }
     for (int s = 0; s < 2; ++s) {
       mbar_init(&sm.s_full[s], 1);
-      mbar_init(&sm.s_free[s], 128);
-      mbar_init(&sm.mass_full[s], 128);
+      mbar_init(&sm.s_free[s], kAtRowThreads);
+      mbar_init(&sm.mass_full[s], kAtRowThreads);
     }
+    mbar_init(&sm.ml_full, kAtRowThreads);
     mbar_init(&sm.drain, 1);
     fence_barrier_init();
     mbar_arrive_expect_tx(&sm.q_ready, (uint32_t)(HALVES * G * QT * 128));
@@ -165,79 +170,94 @@ __global__ void __launch_bounds__(kAtThreads, 1)
     __syncwarp();
     wwait(&sm.drain, 0);
   } else {
-    // ---------------- row warps: row r = TMEM lane ----------------
-    const int r = tid;
+    // ---------------- row warps: row r = TMEM lane, warp half hb = block 1 + 2c + hb ----------------
+    const int lq = warp & 3, hb = warp >> 2;
+    const int r = lq * 32 + lane;
     const int qt = r / G;
     const bool row_ok = r < G * QT && qt < nq;
     const int bmax = row_ok ? bmax_of(i0 + qt) : 0;  // the row's last candidate block (0: none)
-    const uint32_t lane_off = (uint32_t)(warp * 32) << 16;
+    const uint32_t lane_off = (uint32_t)(lq * 32) << 16;
     const float sl2 = p.scale * kLog2e;
     float m = neg_inf(), l = 0.f, lse2 = neg_inf();
     bool ok = true;
     for (int it = 0; it < NIT; ++it) {
       const int sb = it & 1, c = it % NCH;
       const bool pass2 = it >= NCH;
-      if (pass2 && it == NCH) lse2 = l > 0.f ? m + log2f(l) : neg_inf();
+      if (pass2 && it == NCH) {
+        // the row's LSE over both halves' keys (log2 units)
+        sm.ml[hb][0][r] = m;
+        sm.ml[hb][1][r] = l;
+        mbar_arrive(&sm.ml_full);
+        if (!__all_sync(0xffffffffu, mbar_wait(&sm.ml_full, 0, p.err))) {
+          ok = false;
+          break;
+        }
+        const float m0 = sm.ml[0][0][r], l0 = sm.ml[0][1][r], m1 = sm.ml[1][0][r], l1 = sm.ml[1][1][r];
+        const float mm = fmaxf(m0, m1);
+        const float ll = (l0 > 0.f ? l0 * ex2_approx(m0 - mm) : 0.f) + (l1 > 0.f ? l1 * ex2_approx(m1 - mm) : 0.f);
+        lse2 = ll > 0.f ? mm + log2f(ll) : neg_inf();
+      }
       if (!__all_sync(0xffffffffu, mbar_wait(&sm.s_full[sb], (it >> 1) & 1, p.err))) {
         ok = false;
         break;
       }
       tc_fence_after();
-      float mass0 = 0.f, mass1 = 0.f;
-#pragma unroll 1
-      for (int pc = 0; pc < 4; ++pc) {  // 32 columns: half pc / 2 of the chunk
-        float v[32];
-        tmem_ld32(tmem + (uint32_t)(sb * kAtKeys + 32 * pc) + lane_off, v);
-        tmem_ld_wait();
-        const bool valid = 1 + 2 * c + (pc >> 1) <= bmax;  // the whole half is one block
-        if (!valid) continue;
+      float v[64];
+      tmem_ld32(tmem + (uint32_t)(sb * kAtKeys + 64 * hb) + lane_off, v);
+      tmem_ld32(tmem + (uint32_t)(sb * kAtKeys + 64 * hb + 32) + lane_off, v + 32);
+      tmem_ld_wait();
+      tc_fence_before();
+      mbar_arrive(&sm.s_free[sb]);  // the buffer may take chunk it + 2's scores
+      const bool valid = 1 + 2 * c + hb <= bmax;  // the half is one block
+      float mass = 0.f;
+      if (valid) {
         if (!pass2) {
           float mx = neg_inf();
 #pragma unroll
-          for (int e = 0; e < 32; ++e) mx = fmaxf(mx, v[e] * sl2);
-          const float mn = fmaxf(m, mx);
-          float sum = 0.f;
+          for (int e = 0; e < 64; ++e) mx = fmaxf(mx, v[e]);
+          const float mn = fmaxf(m, mx * sl2);
+          float s0 = 0.f, s1 = 0.f;
 #pragma unroll
-          for (int e = 0; e < 32; ++e) sum += ex2_approx(fmaf(v[e], sl2, -mn));
-          l = l * ex2_approx(m - mn) + sum;  // m = -inf at the first valid piece: 2^-inf = 0
+          for (int e = 0; e < 64; e += 2) {
+            s0 += ex2_approx(fmaf(v[e], sl2, -mn));
+            s1 += ex2_approx(fmaf(v[e + 1], sl2, -mn));
+          }
+          l = l * ex2_approx(m - mn) + (s0 + s1);  // m = -inf at the first valid block: 2^-inf = 0
           m = mn;
         } else {
-          float sum = 0.f;
+          float s0 = 0.f, s1 = 0.f;
 #pragma unroll
-          for (int e = 0; e < 32; ++e) sum += ex2_approx(fmaf(v[e], sl2, -lse2));
-          if (pc < 2)
-            mass0 += sum;
-          else
-            mass1 += sum;
+          for (int e = 0; e < 64; e += 2) {
+            s0 += ex2_approx(fmaf(v[e], sl2, -lse2));
+            s1 += ex2_approx(fmaf(v[e + 1], sl2, -lse2));
+          }
+          mass = s0 + s1;
         }
       }
-      tc_fence_before();
-      mbar_arrive(&sm.s_free[sb]);
       if (pass2) {
         // the mean over the G rows (heads) of each query -> pstar.  The
         // arrays alternate by chunk parity: every row thread waits for chunk
         // j's masses before writing chunk j + 1's, so chunk j + 2 overwrites
         // parity j only after every thread has read chunk j.
         const int j = c, pj = j & 1;
-        sm.mass[pj][0][r] = mass0;
-        sm.mass[pj][1][r] = mass1;
+        sm.mass[pj][hb][r] = mass;
         mbar_arrive(&sm.mass_full[pj]);
         if (!__all_sync(0xffffffffu, mbar_wait(&sm.mass_full[pj], (j >> 1) & 1, p.err))) {
           ok = false;
           break;
         }
-        for (int e = r; e < 2 * nq; e += 128) {
+        for (int e = tid; e < 2 * nq; e += kAtRowThreads) {
           const int q_ = e >> 1, h = e & 1;
           const int blk = 1 + 2 * c + h;
           if (blk <= bmaxT) {
-            float s = 0.f;
-            for (int hh = 0; hh < G; ++hh) s += sm.mass[pj][h][q_ * G + hh];
-            p.pstar[((size_t)bg * n + i0 + q_) * nb + blk] = s / (float)G;
+            float sum = 0.f;
+            for (int hh = 0; hh < G; ++hh) sum += sm.mass[pj][h][q_ * G + hh];
+            p.pstar[((size_t)bg * n + i0 + q_) * nb + blk] = sum / (float)G;
           }
         }
       }
     }
-    if (!ok && r == 0) atomicExch(p.err, 1);
+    if (!ok && tid == 0) atomicExch(p.err, 1);
   }
   tc_fence_before();
   __syncthreads();

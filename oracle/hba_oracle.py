@@ -598,19 +598,32 @@ def aux_teacher(qc, kc, cfg, scale):
     nb = n // Bk
     cand = route_candidates(np.arange(n), cfg["window"], nb, Bk)               # [n, nb]
     pstar = np.zeros((B, Hkv, n, nb))
-    with np.errstate(invalid="ignore", divide="ignore"):
-        for b in range(B):
-            for g in range(Hkv):
-                s = np.einsum("ihd,jd->hij", qc[b, :, g * G:(g + 1) * G], kc[b, :, g]) * scale   # [G, n, n]
-                s = s.reshape(G, n, nb, Bk)
-                m = s.max(-1)
-                blk = m + np.log(np.exp(s - m[..., None]).sum(-1))                         # [G, n, nb]
-                blk = np.where(cand[None], blk, -np.inf)
-                mx = blk.max(-1, keepdims=True)
-                e = np.exp(blk - mx)
-                p = (e / e.sum(-1, keepdims=True)).mean(0)                                  # [n, nb]
-                pstar[b, g] = p / np.maximum(p.sum(-1, keepdims=True), 1e-9)
+    for b in range(B):
+        for g in range(Hkv):
+            pstar[b, g] = aux_teacher_rows(np.arange(n), qc[b, :, g * G:(g + 1) * G], kc[b, :, g], cfg, scale)
     return pstar
+
+
+def aux_teacher_rows(pos, qc_rows, kc_g, cfg, scale):
+    """``aux_teacher`` for the query positions `pos` of one (batch, KV
+    head): qc_rows [c, G, dh], kc_g [n, dh] -> pstar rows [c, nb]."""
+    qc_rows = np.asarray(qc_rows, np.float64)
+    kc_g = np.asarray(kc_g, np.float64)
+    c, G, dh = qc_rows.shape
+    n = kc_g.shape[0]
+    Bk = cfg["block"]
+    nb = n // Bk
+    cand = route_candidates(pos, cfg["window"], nb, Bk)                          # [c, nb]
+    with np.errstate(invalid="ignore", divide="ignore"):
+        s = np.einsum("ihd,jd->hij", qc_rows, kc_g) * scale                      # [G, c, n]
+        s = s.reshape(G, c, nb, Bk)
+        m = s.max(-1)
+        blk = m + np.log(np.exp(s - m[..., None]).sum(-1))                       # [G, c, nb]
+        blk = np.where(cand[None], blk, -np.inf)
+        mx = blk.max(-1, keepdims=True)
+        e = np.exp(blk - mx)
+        p = (e / e.sum(-1, keepdims=True)).mean(0)                                # [c, nb]
+        return p / np.maximum(p.sum(-1, keepdims=True), 1e-9)
 
 
 def aux_kl(pstar, bsc, cand):
