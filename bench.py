@@ -868,7 +868,7 @@ def aux_teacher_bench(name, steps, warmup, world, rank, local, pk):
     t_ms = max_over_ranks(statistics.mean(times), world, dev)
     status = L.hba_b200_device_status(ptr(ws), 0, stream_of(dev))
     keys = aux_candidate_keys(cfg, n)
-    flops = 4.0 * dh * Hq * B * keys  # two passes of QK^T over the candidate keys
+    flops = 2.0 * dh * Hq * B * keys  # the reference's one QK^T over the candidate keys (the kernel runs it twice)
     main_ms = kt[1]
     achieved = flops / (main_ms * 1e-3) / 1e12
     qh, kh = q.cpu().pin_memory(), k.cpu().pin_memory()
