@@ -727,7 +727,8 @@ size_t hba_b200_aux_teacher_workspace_size(const hba_b200_config* cfg, int32_t b
   if (!hba::aux_teacher_supported(geo, cfg->head_dim, n)) return 0;
   const size_t kv = (size_t)batch * n * cfg->n_kv * cfg->head_dim;
   const size_t qv = (size_t)batch * n * cfg->n_heads * cfg->head_dim;
-  return kAlign + 3 * align_up(kv * 2) + align_up(qv * 2);  // status; keys plain, chunk-tiled, RoPE'd tiled; queries
+  // status; keys plain, chunk-tiled, RoPE'd tiled; queries; the single pass's block masses
+  return kAlign + 3 * align_up(kv * 2) + align_up(qv * 2) + align_up(hba::aux_teacher_scratch_bytes(geo, n));
 }
 
 int hba_b200_aux_teacher(const hba_b200_config* cfg, int32_t batch, int32_t n, float scale, const void* q,
@@ -759,6 +760,8 @@ int hba_b200_aux_teacher(const hba_b200_config* cfg, int32_t batch, int32_t n, f
   auto* kc_sw = reinterpret_cast<__nv_bfloat16*>(carve(kv * 2));
   auto* kr_sw = reinterpret_cast<__nv_bfloat16*>(carve(kv * 2));
   auto* qcn = reinterpret_cast<__nv_bfloat16*>(carve(qv * 2));
+  const size_t scratch_bytes = hba::aux_teacher_scratch_bytes(geo, n);
+  auto* scratch = reinterpret_cast<float*>(carve(scratch_bytes));
   const size_t nb = (size_t)n / cfg->block;
   prof_begin(stream);
   cudaError_t e = cudaMemsetAsync(dev_status, 0, sizeof(int), stream);
@@ -773,7 +776,8 @@ int hba_b200_aux_teacher(const hba_b200_config* cfg, int32_t batch, int32_t n, f
   }
   if (e != cudaSuccess) return cuda_status(e);
   prof_mark(stream);
-  e = hba::launch_aux_teacher(geo, dh, n, scale, qsrc, kc_sw, pstar, dev_status, stream);
+  e = hba::launch_aux_teacher(geo, dh, n, scale, qsrc, kc_sw, k_gain, scratch, scratch_bytes, pstar, dev_status,
+                              stream);
   if (e != cudaSuccess) return cuda_status(e);
   prof_mark(stream);
   g_last_kernels = cfg->qknorm ? "qknorm_rope_kernel+qknorm_kernel+aux_teacher_kernel" : "qknorm_rope_kernel+aux_teacher_kernel";

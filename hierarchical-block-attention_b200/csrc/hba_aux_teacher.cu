@@ -27,6 +27,7 @@
 // K chunks by 1-D bulk copies of the pre-pass's chunk-tiled keys through a
 // ring); warp 9 issues the MMAs and owns
 // TMEM.  Every mbarrier wait is bounded; a timeout sets *err and drains.
+#include <algorithm>
 #include <climits>
 #include <cudaTypedefs.h>
 
@@ -45,6 +46,7 @@ constexpr int kAtLoad = 8;
 constexpr int kAtMma = 9;
 constexpr int kAtBlock = 64;
 constexpr int kAtKeys = 128;
+constexpr size_t kAuxScratchCap = size_t(1) << 30;  // single-pass scratch: at most 1 GiB (the host slices the queries)
 
 template <int DH>
 struct AtSmem {
@@ -57,6 +59,7 @@ struct AtSmem {
   alignas(1024) unsigned char ring[NSLOT][KT];
   float mass[2][2][128];  // pass 2: [chunk parity][block half][row]
   float ml[2][2][128];    // end of pass 1: [block half][m, l][row]
+  float trow[128];        // single pass: the row's total mass
   uint64_t q_ready, full[NSLOT], empty[NSLOT], s_full[2], s_free[2], mass_full[2], ml_full, drain;
   uint32_t tmem_base;
 };
@@ -73,6 +76,12 @@ struct AuxTeacherParams {
   const __nv_bfloat16* kc;  // chunk-tiled QKNorm'd (or raw) keys
   float* pstar;             // [B, Hkv, n, nb], zeroed by the host
   int* err;
+  // queries [q0, q0 + nsl) of every sequence (a slice; the host loops)
+  int q0, nsl;
+  // single pass (QKNorm, bounded logits): k_gain bounds the keys' norms;
+  // scratch [B*Hkv, nsl, nb, G] fp32 holds each head row's block masses
+  const float* k_gain;
+  float* scratch;
 };
 
 template <int DH>
@@ -89,8 +98,8 @@ __global__ void __launch_bounds__(kAtThreads, 1)
   const int tile = p.tiles - 1 - (int)(blockIdx.x % p.tiles);  // the latest (longest) tiles first
   const int bg = blockIdx.x / p.tiles;
   const int b = bg / geo.Hkv, g = bg % geo.Hkv;
-  const int i0 = tile * QT;
-  const int nq = min(QT, n - i0);
+  const int i0 = p.q0 + tile * QT;
+  const int nq = min(QT, p.q0 + p.nsl - i0);
   const int nb = n / kAtBlock;
   auto bmax_of = [&](int i) { return min(last_candidate(i, geo.W, kAtBlock), nb - 1); };
   const int bmaxT = bmax_of(i0 + nq - 1);      // the tile's last candidate block (0: none)
@@ -122,7 +131,34 @@ __global__ void __launch_bounds__(kAtThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = sm.tmem_base;
-  const int NIT = 2 * NCH;  // item it: chunk it % NCH, pass it / NCH
+  // One pass when every row's logits are bounded (QKNorm: |s| <= scale |q|
+  // sqrt(dh) k_gain, with a 1/64 margin for the bf16 keys; the forward's
+  // bounded mode): masses 2^(s log2e - M2) never flush to zero, and each
+  // row's total normalises them at the end.  Otherwise two passes (the row
+  // LSE, then the masses).  Every thread waits for the query tile to decide.
+  const float sl2 = p.scale * kLog2e;
+  float M2 = 0.f;
+  bool unbounded = !geo.qknorm || p.scratch == nullptr;
+  if (!__all_sync(0xffffffffu, mbar_wait(&sm.q_ready, 0, p.err))) unbounded = true;
+  if (!unbounded && tid < 128) {
+    const int qt = tid / G;
+    if (tid < G * QT && qt < nq) {
+      float qn2 = 0.f;
+#pragma unroll
+      for (int d8 = 0; d8 < DH / 8; ++d8) {
+        float f[8];
+        unpack8(*reinterpret_cast<const uint4*>(sm.q + (d8 / 8) * 16384 + sw128_offset(tid, (d8 % 8) * 8)), f);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) qn2 = fmaf(f[e], f[e], qn2);
+      }
+      M2 = p.scale * sqrtf(qn2) * (sqrtf((float)DH) * p.k_gain[g] * (1.f + 1.f / 64.f)) * kLog2e;
+      unbounded = !(M2 <= kBoundedLog2);
+    }
+  }
+  const bool single = !__syncthreads_or(unbounded ? 1 : 0);
+  if (tid < 128) sm.trow[tid] = M2;  // the row's bound, read by its two row warps
+  __syncthreads();
+  const int NIT = single ? NCH : 2 * NCH;  // item it: chunk it % NCH, pass it / NCH
 
   if (warp == kAtLoad) {
     if (lane == 0) {
@@ -177,12 +213,17 @@ __global__ void __launch_bounds__(kAtThreads, 1)
     const bool row_ok = r < G * QT && qt < nq;
     const int bmax = row_ok ? bmax_of(i0 + qt) : 0;  // the row's last candidate block (0: none)
     const uint32_t lane_off = (uint32_t)(lq * 32) << 16;
-    const float sl2 = p.scale * kLog2e;
+    const float m2row = sm.trow[r];
     float m = neg_inf(), l = 0.f, lse2 = neg_inf();
+    float tot = 0.f;  // single pass: the row's mass over this warp's blocks
     bool ok = true;
+    // single pass: this row's slot in the scratch ([bg, query - q0, blk, head])
+    float* srow = single && row_ok
+                      ? p.scratch + ((size_t)bg * p.nsl + (i0 + qt - p.q0)) * nb * G + (r - qt * G)
+                      : nullptr;
     for (int it = 0; it < NIT; ++it) {
       const int sb = it & 1, c = it % NCH;
-      const bool pass2 = it >= NCH;
+      const bool pass2 = !single && it >= NCH;
       if (pass2 && it == NCH) {
         // the row's LSE over both halves' keys (log2 units)
         sm.ml[hb][0][r] = m;
@@ -210,6 +251,21 @@ __global__ void __launch_bounds__(kAtThreads, 1)
       mbar_arrive(&sm.s_free[sb]);  // the buffer may take chunk it + 2's scores
       const bool valid = 1 + 2 * c + hb <= bmax;  // the half is one block
       float mass = 0.f;
+      if (single) {
+        if (valid) {
+          float s0 = 0.f, s1 = 0.f;
+#pragma unroll
+          for (int e = 0; e < 64; e += 2) {
+            s0 += ex2_approx(fmaf(v[e], sl2, -m2row));
+            s1 += ex2_approx(fmaf(v[e + 1], sl2, -m2row));
+          }
+          mass = s0 + s1;
+          tot += mass;
+        }
+        const int blk = 1 + 2 * c + hb;
+        if (srow != nullptr && blk <= bmaxT) srow[(size_t)blk * G] = mass;
+        continue;
+      }
       if (valid) {
         if (!pass2) {
           float mx = neg_inf();
@@ -257,6 +313,27 @@ __global__ void __launch_bounds__(kAtThreads, 1)
         }
       }
     }
+    if (single && ok) {
+      // each row's total over both halves, then per (query, block) the mean
+      // over the G head rows of mass / total -> pstar
+      sm.ml[hb][1][r] = tot;
+      mbar_arrive(&sm.ml_full);
+      ok = __all_sync(0xffffffffu, mbar_wait(&sm.ml_full, 0, p.err));
+      if (ok) {
+        const float* sbase = p.scratch + ((size_t)bg * p.nsl + (i0 - p.q0)) * nb * G;
+        const int per_q = bmaxT;  // blocks 1 .. bmaxT
+        for (int e = tid; e < nq * per_q; e += kAtRowThreads) {
+          const int q_ = e / per_q, blk = 1 + e % per_q;
+          float sum = 0.f;
+          for (int hh = 0; hh < G; ++hh) {
+            const int rr = q_ * G + hh;
+            const float t = sm.ml[0][1][rr] + sm.ml[1][1][rr];
+            if (t > 0.f) sum += sbase[((size_t)q_ * nb + blk) * G + hh] / t;
+          }
+          p.pstar[((size_t)bg * n + i0 + q_) * nb + blk] = sum / (float)G;
+        }
+      }
+    }
     if (!ok && tid == 0) atomicExch(p.err, 1);
   }
   tc_fence_before();
@@ -273,8 +350,15 @@ bool aux_teacher_supported(const Geom& geo, int dh, int n) {
          geo.G <= 16;
 }
 
+size_t aux_teacher_scratch_bytes(const Geom& geo, int n) {
+  const size_t per_query = (size_t)geo.B * geo.Hq * (n / kAtBlock) * sizeof(float);
+  const size_t all = per_query * (size_t)n;
+  return std::min(all, std::max(kAuxScratchCap, per_query * (size_t)(128 / geo.G)));
+}
+
 cudaError_t launch_aux_teacher(const Geom& geo, int dh, int n, float scale, const __nv_bfloat16* qc,
-                               const __nv_bfloat16* kc_sw, float* pstar, int* err, cudaStream_t st) {
+                               const __nv_bfloat16* kc_sw, const float* k_gain, float* scratch,
+                               size_t scratch_bytes, float* pstar, int* err, cudaStream_t st) {
   const int QT = 128 / geo.G;
   CUtensorMap m_q;
   if ((reinterpret_cast<uintptr_t>(kc_sw) & 15u) != 0 || !make_map(&m_q, qc, geo.B, n, geo.Hq, dh, geo.G, QT))
@@ -284,27 +368,40 @@ cudaError_t launch_aux_teacher(const Geom& geo, int dh, int n, float scale, cons
   p.n = n;
   p.scale = scale;
   p.QT = QT;
-  p.tiles = (n + QT - 1) / QT;
   p.kc = kc_sw;
   p.pstar = pstar;
   p.err = err;
-  const long long grid = (long long)geo.B * geo.Hkv * p.tiles;
-  if (grid <= 0) return cudaSuccess;
-  if (grid > INT32_MAX) return cudaErrorInvalidValue;
-  if (dh == 64) {
-    const size_t smem = sizeof(AtSmem<64>) + 1024;
-    static const cudaError_t attr =
-        cudaFuncSetAttribute(aux_teacher_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    if (attr != cudaSuccess) return attr;
-    aux_teacher_kernel<64><<<(unsigned)grid, kAtThreads, smem, st>>>(m_q, p);
-  } else {
-    const size_t smem = sizeof(AtSmem<128>) + 1024;
-    static const cudaError_t attr =
-        cudaFuncSetAttribute(aux_teacher_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    if (attr != cudaSuccess) return attr;
-    aux_teacher_kernel<128><<<(unsigned)grid, kAtThreads, smem, st>>>(m_q, p);
+  p.k_gain = k_gain;
+  // the single pass keeps [slice queries x nb x Hq] masses: slices of whole tiles fitting the scratch
+  const size_t per_query = (size_t)geo.B * geo.Hq * (n / kAtBlock) * sizeof(float);
+  int nsl = n;
+  if (geo.qknorm && k_gain != nullptr && scratch != nullptr && scratch_bytes >= per_query * QT) {
+    nsl = (int)std::min<size_t>((size_t)n, (scratch_bytes / per_query) / QT * QT);
+    p.scratch = scratch;
   }
-  return cudaGetLastError();
+  const size_t smem = (dh == 64 ? sizeof(AtSmem<64>) : sizeof(AtSmem<128>)) + 1024;
+  static const cudaError_t attr64 =
+      cudaFuncSetAttribute(aux_teacher_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           (int)(sizeof(AtSmem<64>) + 1024));
+  static const cudaError_t attr128 =
+      cudaFuncSetAttribute(aux_teacher_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           (int)(sizeof(AtSmem<128>) + 1024));
+  if ((dh == 64 ? attr64 : attr128) != cudaSuccess) return dh == 64 ? attr64 : attr128;
+  for (int q0 = 0; q0 < n; q0 += nsl) {
+    p.q0 = q0;
+    p.nsl = std::min(nsl, n - q0);
+    p.tiles = (p.nsl + QT - 1) / QT;
+    const long long grid = (long long)geo.B * geo.Hkv * p.tiles;
+    if (grid <= 0) continue;
+    if (grid > INT32_MAX) return cudaErrorInvalidValue;
+    if (dh == 64)
+      aux_teacher_kernel<64><<<(unsigned)grid, kAtThreads, smem, st>>>(m_q, p);
+    else
+      aux_teacher_kernel<128><<<(unsigned)grid, kAtThreads, smem, st>>>(m_q, p);
+    const cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return e;
+  }
+  return cudaSuccess;
 }
 
 }  // namespace hba

@@ -215,8 +215,12 @@ int decode_attend_grid(int dh, int total_chunks);
 // bf16 (QKNorm'd or raw queries), kc_sw the chunk-tiled keys; pstar [B, Hkv,
 // n, nb] fp32, zeroed first.
 bool aux_teacher_supported(const Geom& geo, int dh, int n);
+// scratch (aux_teacher_scratch_bytes, may be null: two passes) lets rows
+// with bounded logits (QKNorm, k_gain) run in one pass.
+size_t aux_teacher_scratch_bytes(const Geom& geo, int n);
 cudaError_t launch_aux_teacher(const Geom& geo, int dh, int n, float scale, const __nv_bfloat16* qc,
-                               const __nv_bfloat16* kc_sw, float* pstar, int* err, cudaStream_t st);
+                               const __nv_bfloat16* kc_sw, const float* k_gain, float* scratch,
+                               size_t scratch_bytes, float* pstar, int* err, cudaStream_t st);
 // Backward of the prefill union softmax (hba_prefill_bwd.cu).
 bool prefill_bwd_supported(const Geom& geo, int dh, int n);
 // delta[b, h, t] = sum_d dout * out over rows (b, t, h) of [B, n, H, dh] bf16.

@@ -35,8 +35,10 @@
 //
 // Roles of prefill_bwd_kernel (320 threads):
 //   warps 0-7   gradient warps: lane quarter lq = warp & 3 of the TMEM lanes,
-//               half hc = warp >> 2 of the 128 row columns (elementwise
-//               step) or of the dh columns (read-outs)
+//               column group hc = warp >> 2 of the 128 row columns
+//               (elementwise step) or of the dh columns (read-outs)
+//               (kBwColGroups = 2; 4 groups ran no faster: the chain is not
+//               bound by the per-warp work)
 //   warp 8      loads: the query and dO tiles (TMA), K / V chunks (1-D bulk
 //               copies of the chunk-tiled pre-pass copies) through a ring
 //   warp 9      issues every tcgen05.mma (one elected lane, whole-warp loop)
@@ -56,9 +58,20 @@ namespace hba {
 
 using namespace sm100;
 
-constexpr int kBwThreads = 320;
-constexpr int kBwLoad = 8;           // load warp
-constexpr int kBwMma = 9;            // MMA warp (and TMEM owner)
+constexpr int kBwColGroups = 2;                   // gradient warps per TMEM lane quarter
+constexpr int kBwGradWarps = 4 * kBwColGroups;
+constexpr int kBwGradThreads = 32 * kBwGradWarps;
+constexpr int kBwThreads = kBwGradThreads + 64;
+constexpr int kBwLoad = kBwGradWarps;              // load warp
+constexpr int kBwMma = kBwGradWarps + 1;           // MMA warp (and TMEM owner)
+constexpr int kBwCols = 128 / kBwColGroups;        // a gradient warp's S^T / dP^T columns (rows of the tile)
+// P^T / dS^T, bf16 pairs, are written over S^T / dP^T: the 16 rows of piece
+// pc of column group cq go to the 8 columns kBwCols cq + 8 pc, inside what
+// that warp has already read; the TMEM address of MMA K-step kk (rows
+// 16 kk .. 16 kk + 15):
+__host__ __device__ constexpr uint32_t bw_packed_col(int kk) {
+  return (uint32_t)(kBwCols * (16 * kk / kBwCols) + 8 * ((16 * kk % kBwCols) / 16));
+}
 constexpr int kBwBlock = 64;         // keys per routed block = per half chunk
 constexpr int kBwKeys = 128;         // keys per chunk
 constexpr int kBwMaxEntries = 520;   // NoPE list: the sink block + the routed union of one tile (1 + QT k)
@@ -251,11 +264,16 @@ __global__ void __launch_bounds__(kBwThreads, 1)
   SM& sm = *reinterpret_cast<SM*>(base_ptr);
   constexpr int HALVES = SM::HALVES;
   constexpr int NSLOT = SM::NSLOT;
-  constexpr int HD = DH / 2;  // a gradient warp's columns in the read-outs
+  constexpr int HD = DH / kBwColGroups;  // a gradient warp's columns in the read-outs
   const Geom& geo = p.geo;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int G = geo.G, QT = p.QT, n = p.n;
-  const int tile = p.tiles - 1 - (int)(blockIdx.x % p.tiles);  // the latest (longest) tiles first
+  // the latest (longest) tiles first, one (sequence, kv head) after the
+  // other: the CTAs running together add their dK / dV into one head's
+  // accumulators (~50 MB at dh 128, 32K), which stay in L2 (interleaving the
+  // heads instead spread the reductions over all heads' accumulators: 1.6x
+  // slower at cfg2)
+  const int tile = p.tiles - 1 - (int)(blockIdx.x % p.tiles);
   const int bg = blockIdx.x / p.tiles;
   const int b = bg / geo.Hkv, g = bg % geo.Hkv;
   const int i0 = tile * QT;                 // the tile's first query
@@ -278,12 +296,12 @@ __global__ void __launch_bounds__(kBwThreads, 1)
       mbar_init(&sm.empty[s], 1);
     }
     mbar_init(&sm.s_full, 1);
-    mbar_init(&sm.p_full, 256);
+    mbar_init(&sm.p_full, kBwGradThreads);
     mbar_init(&sm.dv_full, 1);
     mbar_init(&sm.dk_full, 1);
-    mbar_init(&sm.tmp_free, 256);
+    mbar_init(&sm.tmp_free, kBwGradThreads);
     mbar_init(&sm.dq_full, 1);
-    mbar_init(&sm.dq_free, 256);
+    mbar_init(&sm.dq_free, kBwGradThreads);
     mbar_init(&sm.fin, 1);
     fence_barrier_init();
     mbar_arrive_expect_tx(&sm.q_ready, 2 * qbox_bytes);
@@ -502,7 +520,7 @@ __global__ void __launch_bounds__(kBwThreads, 1)
         // K = 16 rows (keys) = 8 packed columns per MMA; rows [64h, 64h + 64) in columns [64h, 64h + 32)
 #pragma unroll
         for (int kk = 0; kk < 8; ++kk)
-          umma_f16_ts(t_dv, t_s + (uint32_t)((kk >> 2) * 64 + (kk & 3) * 8), o_mn + (uint64_t)(kk * 2048 >> 4),
+          umma_f16_ts(t_dv, t_s + bw_packed_col(kk), o_mn + (uint64_t)(kk * 2048 >> 4),
                       idesc_kv, kk > 0 ? 1u : 0u);
 #pragma unroll
         for (int kk = 0; kk < 8; ++kk)
@@ -511,7 +529,7 @@ __global__ void __launch_bounds__(kBwThreads, 1)
         if (DH == 64) {
 #pragma unroll
           for (int kk = 0; kk < 8; ++kk)
-            umma_f16_ts(t_dk, t_dp + (uint32_t)((kk >> 2) * 64 + (kk & 3) * 8), q_mn + (uint64_t)(kk * 2048 >> 4),
+            umma_f16_ts(t_dk, t_dp + bw_packed_col(kk), q_mn + (uint64_t)(kk * 2048 >> 4),
                         idesc_kv, kk > 0 ? 1u : 0u);
         }
         umma_commit(&sm.dv_full);
@@ -525,7 +543,7 @@ __global__ void __launch_bounds__(kBwThreads, 1)
         if (elect_one_sync()) {
 #pragma unroll
           for (int kk = 0; kk < 8; ++kk)
-            umma_f16_ts(t_dk, t_dp + (uint32_t)((kk >> 2) * 64 + (kk & 3) * 8), q_mn + (uint64_t)(kk * 2048 >> 4),
+            umma_f16_ts(t_dk, t_dp + bw_packed_col(kk), q_mn + (uint64_t)(kk * 2048 >> 4),
                         idesc_kv, kk > 0 ? 1u : 0u);
           umma_commit(&sm.dk_full);
         }
@@ -541,7 +559,7 @@ __global__ void __launch_bounds__(kBwThreads, 1)
     wwait(&sm.fin, 0);
   } else {
     // ---------------- gradient warps ----------------
-    const int lq = warp & 3, hc = warp >> 2;
+    const int lq = warp & 3, hc = warp >> 2;  // lane quarter, column group
     const uint32_t lane_off = (uint32_t)(lq * 32) << 16;
     const int kap = lq * 32 + lane;  // key of the chunk (elementwise step, dV / dK read-outs)
     const int hk = lq >> 1;          // its half of the chunk
@@ -550,14 +568,22 @@ __global__ void __launch_bounds__(kBwThreads, 1)
     auto wait_all = [&](uint64_t* bar, uint32_t parity) {
       return __all_sync(0xffffffffu, mbar_wait(bar, parity, p.err));
     };
+    // HD consecutive TMEM columns of this thread's lane, one wait
+    auto ld_cols = [&](uint32_t taddr, float* f) {
+      if constexpr (HD >= 32) {
+#pragma unroll
+        for (int q32 = 0; q32 < HD / 32; ++q32) tmem_ld32(taddr + (uint32_t)(32 * q32), f + 32 * q32);
+      } else {
+        tmem_ld16(taddr, f);
+      }
+      tmem_ld_wait();
+    };
     // read-out of a [128 x DH] fp32 accumulator with keys on the lanes: this
     // warp's DH / 2 columns of key `kap`, scaled, added into acc (null: the
     // key has no valid row); one TMEM wait for all of them
     auto kv_out = [&](uint32_t tcol, float* acc, float mul) {
       float f[HD];
-#pragma unroll
-      for (int q32 = 0; q32 < HD / 32; ++q32) tmem_ld32(tcol + (uint32_t)(hc * HD + 32 * q32) + lane_off, f + 32 * q32);
-      tmem_ld_wait();
+      ld_cols(tcol + (uint32_t)(hc * HD) + lane_off, f);
       if (acc != nullptr) {
         float* a = acc + hc * HD;
 #pragma unroll
@@ -572,11 +598,7 @@ __global__ void __launch_bounds__(kBwThreads, 1)
     const size_t qrow = row_ok ? (((size_t)b * n + i0 + rqt) * geo.Hq + g * G + (r % G)) * DH + hc * HD : 0;
     auto dq_out = [&](float* dst, bool zero) {
       float f[HD];
-      if (!zero) {
-#pragma unroll
-        for (int q32 = 0; q32 < HD / 32; ++q32) tmem_ld32(t_dq + (uint32_t)(hc * HD + 32 * q32) + lane_off, f + 32 * q32);
-        tmem_ld_wait();
-      }
+      if (!zero) ld_cols(t_dq + (uint32_t)(hc * HD) + lane_off, f);
       if (row_ok) {
         float4* d4 = reinterpret_cast<float4*>(dst + qrow);
 #pragma unroll
@@ -604,10 +626,10 @@ __global__ void __launch_bounds__(kBwThreads, 1)
           qhi = nq - 1;
         }
         auto add_rows = [&](int r0, int r1) {  // rows [r0, r1) of the tile into the 64-row window
-          r0 = max(r0, 64 * hc);
-          r1 = min(min(r1, rows_valid), 64 * hc + 64);
+          r0 = max(r0, kBwCols * hc);
+          r1 = min(min(r1, rows_valid), kBwCols * hc + kBwCols);
           if (r1 > r0) {
-            const int lo = r0 - 64 * hc, len = r1 - r0;
+            const int lo = r0 - kBwCols * hc, len = r1 - r0;
             rmask |= (len >= 64 ? ~0ull : ((1ull << len) - 1ull)) << lo;
           }
         };
@@ -627,12 +649,13 @@ __global__ void __launch_bounds__(kBwThreads, 1)
         break;
       }
       tc_fence_after();
-      // S^T / dP^T columns [64hc, 64hc + 64) (rows) of this key, in pieces of 16
+      // S^T / dP^T columns [kBwCols hc, + kBwCols) (rows) of this key, in pieces of 16
 #pragma unroll 1
-      for (int pc = 0; pc < 4; ++pc) {
+      for (int pc = 0; pc < kBwCols / 16; ++pc) {
+        const int row0 = kBwCols * hc + 16 * pc;  // the piece's first row
         float sv[16], dv[16];
-        tmem_ld16(t_s + (uint32_t)(64 * hc + 16 * pc) + lane_off, sv);
-        tmem_ld16(t_dp + (uint32_t)(64 * hc + 16 * pc) + lane_off, dv);
+        tmem_ld16(t_s + (uint32_t)row0 + lane_off, sv);
+        tmem_ld16(t_dp + (uint32_t)row0 + lane_off, dv);
         tmem_ld_wait();
         const uint32_t bits = (uint32_t)(rmask >> (16 * pc)) & 0xffffu;
         uint32_t pk[8], dk[8];
@@ -641,7 +664,7 @@ __global__ void __launch_bounds__(kBwThreads, 1)
           float pv[2], dsv[2];
 #pragma unroll
           for (int u = 0; u < 2; ++u) {
-            const float2 rc = sm.rowc[64 * hc + 16 * pc + e + u];
+            const float2 rc = sm.rowc[row0 + e + u];
             const bool valid = (bits >> (e + u)) & 1u;
             pv[u] = valid ? ex2_approx(fmaf(sv[e + u], sl2, -rc.x)) : 0.f;
             dsv[u] = pv[u] * (dv[e + u] - rc.y);
@@ -649,11 +672,11 @@ __global__ void __launch_bounds__(kBwThreads, 1)
           pk[e / 2] = pack_bf16x2(pv[0], pv[1]);
           dk[e / 2] = pack_bf16x2(dsv[0], dsv[1]);
         }
-        tmem_st8_nowait(t_s + (uint32_t)(64 * hc + 8 * pc) + lane_off, pk);
-        tmem_st8_nowait(t_dp + (uint32_t)(64 * hc + 8 * pc) + lane_off, dk);
-        *reinterpret_cast<uint4*>(sm.ds[hc] + sw128_offset(kap, 16 * pc)) = make_uint4(dk[0], dk[1], dk[2], dk[3]);
-        *reinterpret_cast<uint4*>(sm.ds[hc] + sw128_offset(kap, 16 * pc + 8)) =
-            make_uint4(dk[4], dk[5], dk[6], dk[7]);
+        tmem_st8_nowait(t_s + (uint32_t)(kBwCols * hc + 8 * pc) + lane_off, pk);
+        tmem_st8_nowait(t_dp + (uint32_t)(kBwCols * hc + 8 * pc) + lane_off, dk);
+        unsigned char* dsh = sm.ds[row0 >> 6];
+        *reinterpret_cast<uint4*>(dsh + sw128_offset(kap, row0 & 63)) = make_uint4(dk[0], dk[1], dk[2], dk[3]);
+        *reinterpret_cast<uint4*>(dsh + sw128_offset(kap, (row0 & 63) + 8)) = make_uint4(dk[4], dk[5], dk[6], dk[7]);
       }
       tmem_st_wait();
       fence_proxy_async_smem();  // dS in shared memory, for the dQ MMA

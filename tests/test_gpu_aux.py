@@ -36,13 +36,17 @@ CASES = [
     ("g1_d64_qt128", dict(n_heads=2, n_kv=2, head_dim=64, window=128), 1, 512),
     ("noqk_d64", dict(n_heads=8, n_kv=2, head_dim=64, window=256, qknorm=False), 1, 1024),
     ("short_no_candidates", dict(n_heads=8, n_kv=2, head_dim=64, window=1024), 1, 512),
+    # trained-scale gains: the logits exceed the bound, the kernel takes its two passes
+    ("trained_gains_d64", dict(n_heads=8, n_kv=2, head_dim=64, window=256), 1, 1024),
 ]
 
 
 @pytest.mark.parametrize("name,kw,B,n", CASES, ids=[c[0] for c in CASES])
 def test_aux_teacher_matches_oracle(name, kw, B, n):
+    """One pass (QKNorm, bounded logits) and two passes (no QKNorm, trained
+    gains) against the oracle on every row."""
     cfg = H.cfg_of(**kw)
-    summ, qkn = synth.make_weights(cfg, "cuda", seed=70, gains=True)
+    summ, qkn = synth.make_weights(cfg, "cuda", seed=70, gains="trained" if "trained" in name else True)
     cos, sin = synth.rope_tables(n, cfg.head_dim, 1e6)
     wl = synth.prefill_workload(cfg, B, n, seed=70)
     pstar = aux_teacher_b200(wl["q"], wl["k"], cos, sin, cfg, qkn)
@@ -96,3 +100,26 @@ def test_aux_kl_replays_reference(name):
         gv, rv = H.np32(got).astype(np.float64), g[key].astype(np.float64)
         assert np.isfinite(gv).all()
         assert np.linalg.norm(gv - rv) <= 3e-2 * np.linalg.norm(rv), (key, np.linalg.norm(gv - rv), np.linalg.norm(rv))
+
+
+def test_aux_teacher_sliced_long_sequence():
+    """A 32K sequence at 32/8 heads, dh 128: the single pass's block masses
+    ([queries, blocks, heads] fp32) exceed the kernel's scratch, so the
+    queries run in slices; sampled rows on both sides of the slice boundary
+    and at the end against the oracle's rows."""
+    cfg = H.cfg_of(n_heads=32, n_kv=8, head_dim=128)
+    n = 32768
+    summ, qkn = synth.make_weights(cfg, "cuda", seed=71, gains=True)
+    cos, sin = synth.rope_tables(n, 128, 1e6)
+    wl = synth.prefill_workload(cfg, 1, n, seed=71)
+    pstar = aux_teacher_b200(wl["q"], wl["k"], cos, sin, cfg, qkn)
+    with torch.no_grad():
+        qc, kc = qknorm_b200(wl["q"], qkn.q.gain), qknorm_b200(wl["k"], qkn.k.gain)
+    torch.cuda.synchronize()
+    rows = np.array([1200, 8191, 16383, 16384, 16385, 20000, 24575, 24576, 32766, 32767])
+    G = 4
+    scale = union_scale(cfg, 128, n)
+    qcn, kcn, got = H.np32(qc), H.np32(kc), H.np32(pstar)
+    for g in (0, 7):
+        ref = orc.aux_teacher_rows(rows, qcn[0, rows, g * G:(g + 1) * G], kcn[0, :, g], H.oracle_cfg(cfg), scale)
+        np.testing.assert_allclose(got[0, g, rows], ref, rtol=1e-3, atol=1e-4)
