@@ -248,7 +248,10 @@ int hba_b200_prefill_range(const hba_b200_config* cfg, int32_t batch, int32_t n,
  * reference's rows are NaN and its loss skips them).  scale: the union's
  * (content scale x tau(n) under QKNorm, dh**-0.5 without).  cos / sin feed
  * the shared key pre-pass.  Block 64, dh 64 / 128, flat configs;
- * HBA_B200_ERR_UNSUPPORTED otherwise.  O(n^2): training only.
+ * HBA_B200_ERR_UNSUPPORTED otherwise.  O(n^2): training only.  The
+ * workspace includes up to 1 GiB for the one-pass mode's block masses
+ * (QKNorm with bounded logits); larger batches x lengths run in query
+ * slices of that size.
  */
 size_t hba_b200_aux_teacher_workspace_size(const hba_b200_config* cfg, int32_t batch, int32_t n);
 int hba_b200_aux_teacher(const hba_b200_config* cfg, int32_t batch, int32_t n, float scale, const void* q,
