@@ -245,15 +245,9 @@ def summarizer_aux_kl(q, k, cos, sin, cfg, summ, qkn):
     attention.py:501-537; hba_attention_dense :364-383): -mean over (batch,
     kv head, query with a candidate) of sum_blocks pstar * log_softmax(bsc),
     pstar the teacher (``aux_teacher_b200``, no gradient) and bsc route_topk's
-    block scores (attention.py:294-298: the grouped QKNorm'd query against
-    the slot summaries of the QKNorm'd keys, both detached, max over slots,
-    x ``route_scale``, non-candidates -inf).  The loss reaches only the
+    block scores (``route_block_scores``).  The loss reaches only the
     summarizer's probes and proj, as in the reference; the summaries and
     scores are evaluated in fp32 by torch (the teacher is the O(n^2) part)."""
-    B, n, Hq, dh = q.shape
-    Hkv = k.shape[2]
-    G, Bk = Hq // Hkv, cfg.block
-    nb = n // Bk
     pstar = aux_teacher_b200(q, k, cos, sin, cfg, qkn)
     with torch.no_grad():
         if getattr(cfg, "qknorm", False):
@@ -261,21 +255,48 @@ def summarizer_aux_kl(q, k, cos, sin, cfg, summ, qkn):
             qc, kc = qknorm_b200(q, qkn.q.gain), qknorm_b200(k, qkn.k.gain)
         else:
             qc, kc = q.detach(), k.detach()
-        qgr = qc.float().view(B, n, Hkv, G, dh).sum(3).transpose(1, 2)           # grouped query [B, Hkv, n, dh]
-        kblk = kc.float().view(B, nb, Bk, Hkv, dh)
+    return aux_kl_from_teacher(pstar, route_block_scores(qc, kc, cfg, summ), cfg)
+
+
+def route_block_scores(qc, kc, cfg, summ):
+    """route_topk's block scores (attention.py:294-298), differentiable in
+    the summarizer's probes / proj: the grouped query (summarizer.py:50-54)
+    of the QKNorm'd queries against the slot summaries (summarizer.py:34-42)
+    of the QKNorm'd keys, both detached, max over slots, x ``route_scale``,
+    non-candidate blocks (attention.py:250-256) -inf.  qc [B, n, Hq, dh], kc
+    [B, n, Hkv, dh] (any device, evaluated in fp32) -> [B, Hkv, n, nb]."""
+    B, n, Hq, dh = qc.shape
+    Hkv = kc.shape[2]
+    G, Bk = Hq // Hkv, cfg.block
+    nb = n // Bk
+    with torch.no_grad():
+        qgr = qc.detach().float().view(B, n, Hkv, G, dh).sum(3).transpose(1, 2)   # grouped query [B, Hkv, n, dh]
+        kblk = kc.detach().float().view(B, nb, Bk, Hkv, dh)
     probes, proj = summ.probes.float(), summ.proj.float()
     att = (torch.einsum("hmd,bckhd->bhcmk", probes, kblk) * dh ** -0.5).softmax(-1)
     S = torch.einsum("bhcmd,hde->bhcme", torch.einsum("bhcmk,bckhd->bhcmd", att, kblk), proj)
     bsc = torch.einsum("bhid,bhcmd->bhicm", qgr, S).amax(-1) * route_scale(cfg, dh)
-    i = torch.arange(n, device=q.device)[:, None]
-    blk = torch.arange(nb, device=q.device)[None, :]
-    cand = (blk >= 1) & ((blk + 1) * Bk <= i - cfg.window + 1)                      # attention.py:250-256
-    bsc = bsc.masked_fill(~cand[None, None], float("-inf"))
-    vq = cand.any(-1)
+    return bsc.masked_fill(~_candidates(n, cfg, qc.device)[None, None], float("-inf"))
+
+
+def _candidates(n, cfg, device):
+    """attention.py:250-256: block b is a routed candidate of query i iff
+    b >= 1 and (b + 1) * block <= i - window + 1.  -> bool [n, n / block]."""
+    i = torch.arange(n, device=device)[:, None]
+    blk = torch.arange(n // cfg.block, device=device)[None, :]
+    return (blk >= 1) & ((blk + 1) * cfg.block <= i - cfg.window + 1)
+
+
+def aux_kl_from_teacher(pstar, bsc, cfg):
+    """attention.py:531-537: -mean over (batch, kv head, query with a
+    candidate) of sum_blocks pstar * log_softmax(bsc), terms with pstar = 0
+    dropped; a zero scalar when no query has a candidate."""
+    n = bsc.shape[2]
+    vq = _candidates(n, cfg, bsc.device).any(-1)
     if not bool(vq.any()):
-        return q.new_zeros(())
+        return bsc.new_zeros(())
     logp = torch.log_softmax(bsc[:, :, vq], dim=-1)
-    pv = pstar[:, :, vq]
+    pv = pstar[:, :, vq].to(logp.dtype)
     term = torch.where(pv > 0, pv * logp, torch.zeros_like(logp))
     return -term.sum(-1).mean()
 

@@ -117,3 +117,55 @@ def test_status_maps_to_reference_style_exceptions():
         _lib.check(_lib.ERR_UNSUPPORTED, "x")
     with pytest.raises(_lib.HBAError):
         _lib.check(_lib.ERR_CUDA, "x")
+
+
+def test_backward_and_teacher_workspace_queries(lib):
+    """hba_b200_prefill_backward / hba_b200_aux_teacher: sizes for the
+    configurations their kernels take (flat, block 64, dh 64 / 128; the
+    backward also G >= 4), 0 otherwise; the teacher's one-pass scratch is
+    capped at 1 GiB whatever the batch and length."""
+    c = cfg(n_heads=8, n_kv=2, block=64)
+    ok_b = lib.hba_b200_prefill_backward_workspace_size(ctypes.byref(c), 1, 4096)
+    ok_t = lib.hba_b200_aux_teacher_workspace_size(ctypes.byref(c), 1, 4096)
+    assert ok_b > 0 and ok_t > 0
+    for bad in (cfg(n_heads=8, n_kv=2, hier=1), cfg(n_heads=8, n_kv=2, block=32)):
+        assert lib.hba_b200_prefill_backward_workspace_size(ctypes.byref(bad), 1, 4096) == 0
+        assert lib.hba_b200_aux_teacher_workspace_size(ctypes.byref(bad), 1, 4096) == 0
+    assert lib.hba_b200_prefill_backward_workspace_size(ctypes.byref(c), 1, 4000) == 0    # n % block
+    # G = 2: outside the backward's tile shape, inside the teacher's
+    g2 = cfg(n_heads=4, n_kv=2)
+    assert lib.hba_b200_prefill_backward_workspace_size(ctypes.byref(g2), 1, 4096) == 0
+    assert lib.hba_b200_aux_teacher_workspace_size(ctypes.byref(g2), 1, 4096) > 0
+    # the teacher's scratch: all queries' masses when small, at most 1 GiB beyond
+    big = cfg(n_heads=32, n_kv=8, head_dim=128)
+    n = 131072
+    kv = 4 * n * 8 * 128
+    qv = 4 * n * 32 * 128
+    base = 256 + 3 * kv * 2 + qv * 2
+    t = lib.hba_b200_aux_teacher_workspace_size(ctypes.byref(big), 4, n)
+    assert base < t <= base + (1 << 30) + 4096
+
+
+def test_backward_and_teacher_reject_bad_arguments_without_a_device(lib):
+    from hba_b200 import _lib
+    c = cfg(n_heads=8, n_kv=2)
+    P = ctypes.c_void_p
+    one = P(16)
+    z = P(0)
+    args = [one] * 16  # q k v cos sin q_gain k_gain out lse sel dout dq dk dv dq_gain dk_gain
+    st = lib.hba_b200_prefill_backward(ctypes.byref(c), 1, 100, ctypes.c_float(0.1), *args, one, 1 << 40, z)
+    assert st == _lib.ERR_NOT_BLOCK_MULTIPLE
+    st = lib.hba_b200_prefill_backward(ctypes.byref(c), 1, 128, ctypes.c_float(0.1), z, *args[1:], one, 1 << 40, z)
+    assert st == _lib.ERR_INVALID_ARGUMENT
+    st = lib.hba_b200_prefill_backward(ctypes.byref(cfg(n_heads=8, n_kv=2, hier=1)), 1, 128, ctypes.c_float(0.1),
+                                       *args, one, 1 << 40, z)
+    assert st == _lib.ERR_UNSUPPORTED
+    st = lib.hba_b200_prefill_backward(ctypes.byref(c), 1, 128, ctypes.c_float(0.1), *args, one, 16, z)
+    assert st == _lib.ERR_WORKSPACE
+    targs = [one] * 7  # q k cos sin q_gain k_gain pstar
+    st = lib.hba_b200_aux_teacher(ctypes.byref(c), 1, 100, ctypes.c_float(0.1), *targs, one, 1 << 40, z)
+    assert st == _lib.ERR_NOT_BLOCK_MULTIPLE
+    st = lib.hba_b200_aux_teacher(ctypes.byref(c), 1, 128, ctypes.c_float(0.1), *targs[:6], z, one, 1 << 40, z)
+    assert st == _lib.ERR_INVALID_ARGUMENT
+    st = lib.hba_b200_aux_teacher(ctypes.byref(c), 1, 128, ctypes.c_float(0.1), *targs, one, 16, z)
+    assert st == _lib.ERR_WORKSPACE

@@ -97,3 +97,49 @@ def test_baseline_configs():
     assert (B, n, hier, cfg.n_heads, cfg.n_kv, cfg.head_dim, cfg.beam, cfg.fanout) == (32, 131072, True, 32, 8, 128,
                                                                                       8, 16)
     assert attention.log_len_tau(cfg, n) == pytest.approx(1.138629, abs=1e-6)
+
+
+def _aux_case(name):
+    import cases
+    from hba_b200.config import HBAConfig
+    c = [x for x in cases.AUX_CASES if x[0] == name][0]
+    _, cc, n, seed, qk = c
+    inp = cases.bwd_case_inputs(cc, n, seed)
+    cfg = HBAConfig(n_heads=cc["n_heads"], n_kv=cc["n_kv"], head_dim=cc["head_dim"], block=cc["block"],
+                    window=cc["window"], sinks=cc["sinks"], k_blocks=cc["k_blocks"], slots=cc["slots"],
+                    fanout=cc["fanout"], beam=cc["beam"], native_ctx=cc["native_ctx"], qknorm=qk,
+                    content_scale_mode=cc["content_scale_mode"], temp_c=cc["temp_c"], n_cal=cc["n_cal"], aux_w=1.0)
+    return cfg, inp, n, qk
+
+
+@pytest.mark.parametrize("name", ["tiny_qk", "g4d64_qk", "g4d64_noqk"])
+def test_aux_kl_torch_part_matches_reference(name):
+    """The aux-KL's torch part (route_topk's block scores and the KL, the
+    part the summarizer's gradient flows through) on the CPU against the
+    reference's own bsc, aux and probes / proj gradients
+    (tests/golden/aux_*.npz), fed the reference's teacher pstar."""
+    import os
+    import numpy as np
+    import torch
+    from hba_b200.attention import aux_kl_from_teacher, route_block_scores
+    from oracle import hba_oracle as orc
+    cfg, inp, n, qk = _aux_case(name)
+    g = np.load(os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden", f"aux_{name}.npz"))
+    if qk:
+        qc = orc.head_rmsnorm(inp["q"], inp["q_gain"])
+        kc = orc.head_rmsnorm(inp["k"], inp["k_gain"])
+    else:
+        qc, kc = inp["q"], inp["k"]
+    probes = torch.tensor(inp["probes"], requires_grad=True)
+    proj = torch.tensor(inp["proj"], requires_grad=True)
+    summ = type("S", (), {"probes": probes, "proj": proj})()
+    bsc = route_block_scores(torch.tensor(qc), torch.tensor(kc), cfg, summ)
+    ref_bsc = g["bsc"]
+    fin = np.isfinite(ref_bsc)
+    assert (np.isfinite(bsc.detach().numpy()) == fin).all()
+    np.testing.assert_allclose(bsc.detach().numpy()[fin], ref_bsc[fin], rtol=1e-4, atol=1e-5)
+    aux = aux_kl_from_teacher(torch.tensor(np.nan_to_num(g["pstar"])), bsc, cfg)
+    assert abs(float(aux.detach()) - float(g["aux"])) <= 1e-4 * max(1.0, abs(float(g["aux"])))
+    aux.backward()
+    for key, got in (("dprobes", probes.grad), ("dproj", proj.grad)):
+        np.testing.assert_allclose(got.numpy(), g[key], rtol=1e-3, atol=1e-3 * np.abs(g[key]).max())
