@@ -269,8 +269,9 @@ int hba_b200_aux_teacher(const hba_b200_config* cfg, int32_t batch, int32_t n, f
  *   dout: [batch, n, Hq, dh] bf16, the gradient of out
  * Writes dq [batch, n, Hq, dh], dk, dv [batch, n, Hkv, dh] (bf16) and, with
  * QKNorm, dq_gain [Hq] and dk_gain [Hkv] (fp32; overwritten, not added to).
- * Flat selection, block 64, dh 64 / 128, G = Hq / Hkv in 4 .. 16;
- * HBA_B200_ERR_UNSUPPORTED otherwise.  Replaces the flex-attention backward
+ * Flat selection, block 64, dh 64 / 128, G = Hq / Hkv in 4 .. 16, and a
+ * query tile's routed union (1 + (128 / G) * k blocks) within 520 -- k <= 16
+ * at G = 4; HBA_B200_ERR_UNSUPPORTED otherwise.  Replaces the flex-attention backward
  * (torch autograd) of the reference's training path.
  */
 size_t hba_b200_prefill_backward_workspace_size(const hba_b200_config* cfg, int32_t batch, int32_t n);
